@@ -1,0 +1,419 @@
+#!/usr/bin/env python
+"""Benchmark of the B200-native Prometheus reactor (driver contract).
+
+Headline metric: fp32 SGEMM TFLOP/s at 8192^3.
+
+  * One step = one C = A*B of the workload through the reactor's device entry
+    point (oct_b200_sgemm_device_ld): the TF32 split pass plus the tcgen05
+    3xTF32 main kernel.  Inputs (U[-1,1), seeded) are resident in HBM and each
+    operand (256 MiB) is larger than the 126 MB L2, so no flush is needed.
+  * N > 1 ranks (torchrun, one per GPU): the column-parallel form of the large
+    GEMM.  Every rank holds A and its own 8192-column shard of B and writes its
+    shard of C (global N = 8192 * world): weak scaling, no data-path
+    collective (C stays column-sharded, as a column-parallel layer leaves it).
+  * `value` is whole-job TFLOP/s over the max-over-ranks device time of K steps.
+  * `e2e` is the same metric through the reference-facing host ABI
+    (prometheus_reactor_runtime_sgemm) with pinned host buffers: the host->device
+    copy of A and B and the device->host copy of C are inside the timed region.
+  * `roofline`: the main kernel's useful flops per launch / its CUDA-event time
+    on the launch stream, against the 3xTF32-adjusted tensor peak derived from
+    the measured dense bf16 peak (tf32 runs at half the bf16 rate, and each fp32
+    product costs three tf32 products): peak = bf16_tflops / 6.
+  * `cpu_baseline`: Oct's CPU SGEMM (`cpuSGEMM`, internal/prometheus/runtime.go:319-331,
+    restated in oracle/oracle.c) on all host cores, over a bounded row sample.
+
+`--impl reference` times that same CPU restatement as the reference arm (Oct's
+reactor needs Vulkan and cannot run on this machine; its Go CPU path is the
+reference implementation that exists here).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--m", type=int, default=8192)
+    p.add_argument("--n", type=int, default=8192, help="columns per rank")
+    p.add_argument("--k", type=int, default=8192)
+    p.add_argument("--variant", type=int, default=16, help="16/32 = tcgen05 stage depth, 2 = FMA control")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-secondary", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU sample")
+    return p.parse_args()
+
+
+def peaks() -> tuple[dict, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[4:8]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_sgemm_sample(m: int, n: int, k: int, seconds: float, threads: int) -> dict:
+    """Oct's cpuSGEMM restated (oracle port) on a bounded sample of output rows."""
+    from oracle import oracle as O
+    a = O.uniform_matrix(m, k, 1000).ravel()
+    b = O.uniform_matrix(k, n, 1001).ravel()
+    probe_rows = max(1, threads)
+    t0 = time.perf_counter()
+    O.cpu_sgemm_f32(a, b, m, n, k, rows=slice(0, probe_rows), threads=threads)
+    t_probe = time.perf_counter() - t0
+    rows = probe_rows * max(1, int(seconds / max(t_probe, 1e-6)))
+    rows = min(rows, m)
+    t0 = time.perf_counter()
+    O.cpu_sgemm_f32(a, b, m, n, k, rows=slice(0, rows), threads=threads)
+    t = time.perf_counter() - t0
+    return {"value": 2.0 * rows * n * k / t / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"cpuSGEMM (fp32 i-j-k, runtime.go:319-331, C restatement) on {rows} of {m} output rows of "
+                      f"{m}x{n}x{k}, {t:.1f} s on {threads} threads, extrapolated per flop",
+            "seconds": t, "rows": rows}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # the reference arm runs on rank 0 only
+    from oracle import oracle as O
+    O.build()
+    threads = O.max_threads()
+    m, n, k = args.m, args.n, args.k
+    a = O.uniform_matrix(m, k, 1000).ravel()
+    b = O.uniform_matrix(k, n, 1001).ravel()
+    # Size one step as a bounded row sample so the whole run stays within minutes.
+    t0 = time.perf_counter()
+    O.cpu_sgemm_f32(a, b, m, n, k, rows=slice(0, threads), threads=threads)
+    t_probe = time.perf_counter() - t0
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    rows = min(m, threads * max(1, int(budget / max(t_probe, 1e-6))))
+    for _ in range(args.warmup):
+        O.cpu_sgemm_f32(a, b, m, n, k, rows=slice(0, rows), threads=threads)
+    times = []
+    for s in range(args.steps):
+        r0 = (s * rows) % max(1, m - rows + 1)
+        t0 = time.perf_counter()
+        O.cpu_sgemm_f32(a, b, m, n, k, rows=slice(r0, r0 + rows), threads=threads)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = 2.0 * rows * n * k * args.steps / total / 1e12
+    sample = (f"cpuSGEMM (fp32 i-j-k, internal/prometheus/runtime.go:319-331; C restatement, Oct's Go/Vulkan "
+              f"reactor cannot run here) on {rows} of {m} rows of {m}x{n}x{k} per step, {threads} threads")
+    line = {
+        "impl": "reference", "metric": "fp32 SGEMM TFLOP/s at 8192^3", "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"sgemm {m}x{n}x{k} (row sample per step)", "m": m, "n": n, "k": k},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
+    """Reductions at BASELINE configs[2] shapes (32768 rows) and the FMA control SGEMM."""
+    from oct_b200 import reactor as R
+    out = []
+    stream = torch.cuda.current_stream()
+    rows = 32768
+    for width in (256, 2048, 4096):
+        g = torch.Generator(device="cuda").manual_seed(width)
+        x = torch.randn(rows, width, device="cuda", generator=g)
+        w = torch.rand(width, device="cuda", generator=g) + 0.5
+        y_row = torch.empty(rows, device="cuda")
+        y_full = torch.empty_like(x)
+        inv = torch.empty(rows, device="cuda")
+        for name, fn, nbytes in (
+            ("row_sum", lambda: rt.reduction_device(x, y_row, rows, width, R.OP_SUM, stream), 4 * rows * width + 4 * rows),
+            ("row_max", lambda: rt.reduction_device(x, y_row, rows, width, R.OP_MAX, stream), 4 * rows * width + 4 * rows),
+            ("softmax", lambda: rt.reduction_device(x, y_full, rows, width, R.OP_SOFTMAX, stream), 8 * rows * width),
+            ("rmsnorm", lambda: rt.rmsnorm_device(x, w, y_full, inv, rows, width, 1e-6, stream),
+             8 * rows * width + 4 * width),
+        ):
+            for _ in range(3):
+                fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            iters = 20
+            e0.record(stream)
+            for _ in range(iters):
+                fn()
+            e1.record(stream)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1) / iters
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            out.append({"kernel": name, "rows": rows, "width": width, "ms": round(ms, 5), "GB/s": round(gbs, 1),
+                        "frac_of_hbm": round(gbs / hbm_peak, 3), "bytes": nbytes})
+        st = rt.sync_status()
+        if not st.ok:
+            raise RuntimeError(f"reduction status {st}")
+        del x, y_full, y_row, inv
+    # FMA control and the 32-deep tensor-core variant at the headline shape
+    m = n = k = 8192
+    g = torch.Generator(device="cuda").manual_seed(7)
+    a = torch.rand(m, k, device="cuda", generator=g) * 2 - 1
+    b = torch.rand(k, n, device="cuda", generator=g) * 2 - 1
+    c = torch.empty(m, n, device="cuda")
+    for variant, label, iters in ((R.SGEMM_FMA, "sgemm_fma_control", 3), (R.SGEMM_TC_BK32, "sgemm_3xtf32_bk32", 5)):
+        rt.sgemm_device(a, b, c, m, n, k, variant, stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            rt.sgemm_device(a, b, c, m, n, k, variant, stream)
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        out.append({"kernel": label, "m": m, "n": n, "k": k, "ms": round(ms, 3),
+                    "TFLOP/s": round(2.0 * m * n * k / (ms * 1e-3) / 1e12, 2)})
+    rt.set_kernel_timing(False)
+    return out
+
+
+def run_ours(args) -> None:
+    import torch
+    from oct_b200 import reactor as R
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+    rt = R.Runtime()
+    m, n, k = args.m, args.n, args.k
+    stream = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    a = torch.rand(m, k, device="cuda", generator=g) * 2 - 1
+    b = torch.rand(k, n, device="cuda", generator=g) * 2 - 1
+    c = torch.empty(m, n, device="cuda")
+    flops = 2.0 * m * n * k
+
+    def step():
+        rt.sgemm_device(a, b, c, m, n, k, args.variant, stream)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    st = rt.sync_status(stream)
+    if not st.ok:
+        raise RuntimeError(f"warm-up failed: {st}")
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    rt.set_kernel_timing(True)
+    rt.read_kernel_timing()  # reset the launch count
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier()
+    ms_total = e0.elapsed_time(e1)
+    split_ms, main_ms, launches = rt.read_kernel_timing()
+    rt.set_kernel_timing(False)
+    st = rt.sync_status(stream)
+    if not st.ok:
+        raise RuntimeError(f"timed run failed: {st}")
+    t = torch.tensor([ms_total], device="cuda", dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = flops * world * args.steps / (ms_max * 1e-3) / 1e12
+
+    pk, pk_kind = peaks()
+    tensor_peak = pk["bf16_tflops"] / 6.0
+    main_per_launch_ms = main_ms / max(1, launches)
+    achieved = flops / (main_per_launch_ms * 1e-3) / 1e12
+    traffic = None
+    tpath = REPO / "profiles" / "traffic.json"
+    if tpath.exists():
+        try:
+            entry = json.loads(tpath.read_text()).get("sgemm3x_kernel_8192")
+            if entry is not None:
+                traffic = entry.get("bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    # ---- end to end through the reference-facing host ABI (pinned buffers)
+    e2e = None
+    if not args.no_e2e:
+        ha = torch.empty(m * k, dtype=torch.float32, pin_memory=True)
+        hb = torch.empty(k * n, dtype=torch.float32, pin_memory=True)
+        hc = torch.empty(m * n, dtype=torch.float32, pin_memory=True)
+        ha.copy_(a.reshape(-1).cpu())
+        hb.copy_(b.reshape(-1).cpu())
+        na, nb, nc = ha.numpy(), hb.numpy(), hc.numpy()
+        for _ in range(max(3, args.warmup // 2)):
+            _, s = rt.sgemm_with_status(m, n, k, na, nb, out=nc)
+            if not s.ok:
+                raise RuntimeError(f"e2e warm-up failed {s}")
+        barrier()
+        t0 = time.perf_counter()
+        e2e_steps = max(3, min(args.steps, 10))
+        for _ in range(e2e_steps):
+            _, s = rt.sgemm_with_status(m, n, k, na, nb, out=nc)
+            if not s.ok:
+                raise RuntimeError(f"e2e step failed {s}")
+        tt = torch.tensor([time.perf_counter() - t0], device="cuda", dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e = {"value": flops * world * e2e_steps / float(tt.item()) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": 4 * (m * k + k * n) * world, "d2h_bytes_per_step": 4 * m * n * world,
+               "steps": e2e_steps, "path": "prometheus_reactor_runtime_sgemm, pinned host buffers"}
+
+    secondary = None
+    cpu = None
+    if rank == 0 and world == 1:
+        if not args.no_secondary:
+            secondary = secondary_measurements(rt, torch, pk["hbm_gbs"])
+        if not args.no_cpu_baseline:
+            from oracle import oracle as O
+            O.build()
+            cpu = cpu_sgemm_sample(m, n, k, args.cpu_seconds, O.max_threads())
+            cpu.pop("seconds", None)
+            cpu.pop("rows", None)
+
+    if rank == 0:
+        line = {
+            "metric": "fp32 SGEMM TFLOP/s at 8192^3",
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(3, args.warmup),
+            "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic",
+            "config": {
+                "workload": f"sgemm {m}x{n}x{k} per rank (A replicated, B and C column-sharded; global N = {n}*ranks)",
+                "m": m, "n_per_rank": n, "k": k, "variant": "tcgen05 3xTF32" if args.variant in (1, 16, 32) else "fp32 FMA",
+                "stage_depth_k": args.variant if args.variant in (16, 32) else None,
+                "parallelism": f"column-parallel x{world}",
+                "l2": "no flush: every operand (256 MiB) exceeds the 126 MB L2",
+                "input": "U[-1,1) fp32, seeded per rank",
+            },
+            "roofline": {
+                "bound": "tensor",
+                "kernel": "sgemm3x_kernel (tcgen05 kind::tf32, 3 products per k-step)",
+                "achieved": achieved,
+                "peak": tensor_peak,
+                "unit": "TFLOP/s",
+                "frac": achieved / tensor_peak,
+                "traffic": traffic,
+                "peak_source": f"{pk_kind}: bf16_tflops {pk['bf16_tflops']} / 2 (tf32 rate) / 3 (products)",
+                "algorithmic_flops_per_launch": flops,
+                "main_kernel_ms_per_launch": main_per_launch_ms,
+                "split_pass_ms_per_launch": split_ms / max(1, launches),
+            },
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks.summary(),
+            "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+    rt.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,595 @@
+/*
+ * prometheus_reactor.h -- C ABI (version 1) of the B200-native Prometheus reactor.
+ *
+ * This library is a drop-in replacement for Oct's `libprometheus_reactor.so` on
+ * the fp32 dense compute path: SGEMM, row reductions (sum / max / stable
+ * softmax), RMSNorm, and the transformer-block pieces built on them.  Oct's Go
+ * host resolves these symbols with dlopen/dlsym and calls them through cgo; no
+ * Go-side change is needed.  Every declaration below names the reference
+ * declaration it replaces (paths are relative to the Oct repository root).
+ *
+ * Conventions shared by every entry point:
+ *   - Return PROM_OK / PROM_ERROR / PROM_INVALID_HANDLE / PROM_INTERNAL_ERROR.
+ *   - `out_stage` reports the pipeline stage that finished last (or failed) and
+ *     `out_detail_code` a signed detail: negative = failure class, positive =
+ *     executed-path identity.
+ *   - All host pointers are borrowed for the duration of the call only.
+ *   - No C++ exception ever crosses this boundary.
+ *   - Handles are validated against a locked registry on every call; calls on
+ *     one handle are serialised inside the library.
+ *
+ * Struct layouts are byte-compatible with the reference because the Go side
+ * passes these structs through cgo unchanged.
+ *
+ * Entry points prefixed `oct_b200_` are extensions with no counterpart in the
+ * reference.  They take DEVICE pointers and a CUDA stream, for callers whose
+ * data is already resident in HBM (benchmarks, tensor-parallel drivers).
+ */
+#ifndef OCT_B200_PROMETHEUS_REACTOR_H
+#define OCT_B200_PROMETHEUS_REACTOR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PROM_REACTOR_API __attribute__((visibility("default")))
+#else
+#define PROM_REACTOR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- versioning, status, backend (internal/prometheus/native/reactor_api.h:22-83) ---- */
+enum { PROM_REACTOR_ABI_V1 = 1u };
+
+enum {
+  PROM_OK = 0,
+  PROM_ERROR = 1,
+  PROM_INVALID_HANDLE = 2,
+  PROM_INTERNAL_ERROR = 3,
+};
+
+/* backend_type 2 is what Oct's strict `prometheus { }` path demands
+   (internal/prometheus/fft.go:50-55); this library reports it for its CUDA
+   device backend so the Go host admits it unchanged. */
+enum {
+  PROM_BACKEND_UNKNOWN = 0,
+  PROM_BACKEND_STUB = 1,
+  PROM_BACKEND_VULKAN = 2,
+  PROM_BACKEND_VULKAN_SOFTWARE = 3,
+};
+
+enum {
+  PROM_REASON_NONE = 0,
+  PROM_REASON_STUB_UNAVAILABLE = 1,
+  PROM_REASON_VULKAN_UNAVAILABLE = 2, /* reused: no usable sm_100 CUDA device */
+};
+
+enum {
+  PROM_STAGE_NONE = 0,
+  PROM_STAGE_INIT = 1,
+  PROM_STAGE_TRANSFER_IN = 2,
+  PROM_STAGE_SUBMIT = 3,
+  PROM_STAGE_TRANSFER_OUT = 4,
+  PROM_STAGE_CLEANUP = 5,
+};
+
+/* ---- async lifecycle (reactor_api.h:85-103) ---- */
+enum {
+  PROM_ASYNC_STATE_IDLE = 0,
+  PROM_ASYNC_STATE_SUBMITTED = 1,
+  PROM_ASYNC_STATE_READY = 2,
+  PROM_ASYNC_STATE_FAILED = 3,
+  PROM_ASYNC_STATE_CONSUMED = 4,
+};
+
+enum {
+  PROM_ASYNC_FAILURE_NONE = 0,
+  PROM_ASYNC_FAILURE_PRE_SUBMIT = 1,
+  PROM_ASYNC_FAILURE_OBSERVATION = 2,
+  PROM_ASYNC_FAILURE_QUERY = 3,
+  PROM_ASYNC_FAILURE_SUBMISSION = 4,
+  PROM_ASYNC_FAILURE_DEVICE_LOST = 5,
+};
+
+/* ---- host-side fault injection (reactor_api.h:132-159, 194-202) ----
+   Only the bits this library honours are listed.  Every injected failure is
+   raised on the host before or after a device call; none makes a kernel fault. */
+enum {
+  PROM_TESTCFG_FAIL_DEVICE_CREATE = 1u << 0,
+  PROM_TESTCFG_FAIL_BUFFER_ALLOC = 1u << 2,
+  PROM_TESTCFG_FAIL_UPLOAD = 1u << 3,
+  PROM_TESTCFG_FAIL_DISPATCH = 1u << 4,
+  PROM_TESTCFG_FAIL_DOWNLOAD = 1u << 5,
+  PROM_TESTCFG_FAIL_ASYNC_POLL = 1u << 15,
+  PROM_TESTCFG_FORCE_STRICT_FP32 = 1u << 17, /* selects the FP32-FMA SGEMM control */
+};
+
+enum {
+  PROM_REDUCTION_TESTCFG_FAIL_COMMAND_RECORD = 1u << 0,
+  PROM_REDUCTION_TESTCFG_FAIL_QUEUE_SUBMIT = 1u << 1,
+  PROM_REDUCTION_TESTCFG_FAIL_COMPLETION_OBSERVATION = 1u << 2,
+};
+
+/* ---- SGEMM detail codes (reactor_api.h:204-260) ---- */
+enum {
+  PROM_DETAIL_INJECTED_UPLOAD_FAILURE = -6001,
+  PROM_DETAIL_INJECTED_DISPATCH_FAILURE = -6002,
+  PROM_DETAIL_INJECTED_DOWNLOAD_FAILURE = -6003,
+  PROM_DETAIL_SIZE_OVERFLOW = -6004,
+  PROM_DETAIL_REUSE_IN_FLIGHT = -6005,
+  PROM_DETAIL_CAPABILITY_MISMATCH = -6006,
+  PROM_DETAIL_PATH_DIRECT = 6101,
+  PROM_DETAIL_ASYNC_NOT_READY = -6108,
+  PROM_DETAIL_ASYNC_NO_TASK = -6109,
+  PROM_DETAIL_ASYNC_ALREADY_CONSUMED = -6110,
+  PROM_DETAIL_ASYNC_INVALID_TASK = -6111,
+  PROM_DETAIL_ASYNC_SUBMIT_REJECTED = -6112,
+  PROM_DETAIL_ASYNC_FAILED = -6114,
+  PROM_DETAIL_ASYNC_UNCONSUMED = -6115,
+  PROM_DETAIL_INJECTED_ASYNC_POLL_FAILURE = -6116,
+  PROM_DETAIL_ASYNC_QUEUE_FULL = -6117,
+};
+
+/* RMSNorm detail codes (internal/prometheus/native/reactor_vulkan.h:1870-1888). */
+enum {
+  PROM_M46_DETAIL_INVALID_REQUEST = -7401,
+  PROM_M46_DETAIL_SHAPE = -7403,
+  PROM_M46_DETAIL_STRIDE = -7404,
+  PROM_M46_DETAIL_EPSILON = -7407,
+  PROM_M46_DETAIL_SIZE_OVERFLOW = -7409,
+  PROM_M46_DETAIL_RESOURCE = -7411,
+  PROM_M46_DETAIL_COMPLETION_UNCERTAIN = -7414,
+  PROM_M46_DETAIL_NONFINITE_INPUT = -7418,
+};
+
+/* Details with no reference counterpart (this library's device layer). */
+enum {
+  OCT_B200_DETAIL_CUDA_ERROR = -7001,        /* a CUDA runtime call failed */
+  OCT_B200_DETAIL_DEVICE_TIMEOUT = -7002,    /* a bounded in-kernel wait gave up */
+  OCT_B200_DETAIL_OUT_OF_MEMORY = -7003,     /* device allocation failed */
+  OCT_B200_DETAIL_BAD_VARIANT = -7004,       /* unknown kernel variant id */
+  OCT_B200_DETAIL_UNALIGNED = -7005,         /* device pointer not 16-byte aligned */
+};
+
+/* ---- reductions (reactor_api.h:375-581) ---- */
+enum {
+  PROM_REDUCTION_OPERATION_SUM = 1u,
+  PROM_REDUCTION_OPERATION_MAX = 2u,
+  PROM_REDUCTION_OPERATION_SOFTMAX = 3u,
+};
+
+enum {
+  PROM_REDUCTION_FINALIZATION_NONE = 0u,
+  PROM_REDUCTION_FINALIZATION_STABLE_SOFTMAX = 1u,
+};
+
+enum {
+  PROM_REDUCTION_STRATEGY_AUTO = 0u,
+  PROM_REDUCTION_STRATEGY_FUSED_SINGLE_WORKGROUP = 1u,
+  PROM_REDUCTION_STRATEGY_COMPOSED = 2u,
+  PROM_REDUCTION_STRATEGY_PACKED_SHORT_ROWS = 3u,
+};
+
+enum {
+  PROM_REDUCTION_STAGE_ROW_SUM = 1u,
+  PROM_REDUCTION_STAGE_ROW_MAX = 2u,
+  PROM_REDUCTION_STAGE_SOFTMAX_EXP_SUM = 3u,
+  PROM_REDUCTION_STAGE_SOFTMAX_NORMALIZE = 4u,
+  PROM_REDUCTION_STAGE_SOFTMAX_FUSED = 5u,
+  PROM_REDUCTION_STAGE_ROW_SUM_PACKED_SHORT = 6u,
+  PROM_REDUCTION_STAGE_SOFTMAX_PACKED_SHORT = 7u,
+};
+
+enum {
+  PROM_REDUCTION_TEMPORARY_NONE = 0u,
+  PROM_REDUCTION_TEMPORARY_PARTIALS = 1u,
+  PROM_REDUCTION_TEMPORARY_ROW_MAX = 2u,
+  PROM_REDUCTION_TEMPORARY_ROW_SUM = 3u,
+};
+
+enum {
+  PROM_REDUCTION_FLAG_FORCE_FUSED = 1u << 0u,
+  PROM_REDUCTION_FLAG_FORCE_COMPOSED = 1u << 1u,
+};
+
+enum {
+  PROM_REDUCTION_DETAIL_INVALID_REQUEST = -6801,
+  PROM_REDUCTION_DETAIL_NULL_INPUT = -6802,
+  PROM_REDUCTION_DETAIL_NULL_OUTPUT = -6803,
+  PROM_REDUCTION_DETAIL_ZERO_ROW_COUNT = -6804,
+  PROM_REDUCTION_DETAIL_ZERO_ROW_WIDTH = -6805,
+  PROM_REDUCTION_DETAIL_UNSUPPORTED_OPERATION = -6806,
+  PROM_REDUCTION_DETAIL_INVALID_FINALIZATION = -6807,
+  PROM_REDUCTION_DETAIL_SIZE_OVERFLOW = -6808,
+  PROM_REDUCTION_DETAIL_INPUT_SIZE_MISMATCH = -6809,
+  PROM_REDUCTION_DETAIL_OUTPUT_SIZE_MISMATCH = -6810,
+  PROM_REDUCTION_DETAIL_ROW_LIMIT = -6811,
+  PROM_REDUCTION_DETAIL_WIDTH_LIMIT = -6812,
+  PROM_REDUCTION_DETAIL_ELEMENT_LIMIT = -6813,
+  PROM_REDUCTION_DETAIL_NONFINITE_INPUT = -6814,
+  PROM_REDUCTION_DETAIL_UNSUPPORTED_STRATEGY = -6815,
+  PROM_REDUCTION_DETAIL_MALFORMED_PLAN = -6816,
+  PROM_REDUCTION_DETAIL_TEMPORARY_UNDERSIZED = -6817,
+  PROM_REDUCTION_DETAIL_RESOURCE_CREATE_FAILED = -6818,
+  PROM_REDUCTION_DETAIL_PIPELINE_CREATE_FAILED = -6819,
+  PROM_REDUCTION_DETAIL_COMMAND_RECORD_FAILED = -6820,
+  PROM_REDUCTION_DETAIL_QUEUE_SUBMIT_FAILED = -6821,
+  PROM_REDUCTION_DETAIL_COMPLETION_UNCERTAIN = -6822,
+  PROM_REDUCTION_DETAIL_QUERY_FAILED = -6823,
+  PROM_REDUCTION_DETAIL_READBACK_FAILED = -6824,
+  PROM_REDUCTION_DETAIL_RUNTIME_UNAVAILABLE = -6825,
+};
+
+enum {
+  PROM_SOFTMAX_DETAIL_INVALID_REQUEST = -6851,
+  PROM_SOFTMAX_DETAIL_NULL_INPUT = -6852,
+  PROM_SOFTMAX_DETAIL_NULL_OUTPUT = -6853,
+  PROM_SOFTMAX_DETAIL_COUNT_MISMATCH = -6854,
+  PROM_SOFTMAX_DETAIL_SIZE_OVERFLOW = -6855,
+  PROM_SOFTMAX_DETAIL_ROW_LIMIT = -6856,
+  PROM_SOFTMAX_DETAIL_WIDTH_LIMIT = -6857,
+  PROM_SOFTMAX_DETAIL_ELEMENT_LIMIT = -6858,
+  PROM_SOFTMAX_DETAIL_PARTIAL_ALIAS = -6859,
+  PROM_SOFTMAX_DETAIL_NONFINITE_INPUT = -6860,
+  PROM_SOFTMAX_DETAIL_RUNTIME_UNAVAILABLE = -6861,
+};
+
+/* Kernel identities reported in a plan.  The reference numbers its Vulkan
+   shaders 16-22 (reactor_api.h:480-488); the CUDA kernels here keep those ids
+   for the stage roles they fulfil so that plan replay ids stay comparable. */
+enum {
+  PROM_REDUCTION_SHADER_ROW_SUM = 16u,
+  PROM_REDUCTION_SHADER_ROW_MAX = 17u,
+  PROM_REDUCTION_SHADER_SOFTMAX_EXP_SUM = 18u,
+  PROM_REDUCTION_SHADER_SOFTMAX_NORMALIZE = 19u,
+  PROM_REDUCTION_SHADER_SOFTMAX_FUSED = 20u,
+  PROM_REDUCTION_SHADER_ROW_SUM_PACKED_SHORT = 21u,
+  PROM_REDUCTION_SHADER_SOFTMAX_PACKED_SHORT = 22u,
+};
+
+enum {
+  PROM_REDUCTION_IMPLEMENTATION_ROW_SUM = 1001u,
+  PROM_REDUCTION_IMPLEMENTATION_ROW_MAX = 1002u,
+  PROM_REDUCTION_IMPLEMENTATION_SOFTMAX_EXP_SUM = 1003u,
+  PROM_REDUCTION_IMPLEMENTATION_SOFTMAX_NORMALIZE = 1004u,
+  PROM_REDUCTION_IMPLEMENTATION_SOFTMAX_FUSED = 1005u,
+  PROM_REDUCTION_IMPLEMENTATION_ROW_SUM_PACKED_SHORT = 1006u,
+  PROM_REDUCTION_IMPLEMENTATION_SOFTMAX_PACKED_SHORT = 1007u,
+};
+
+#define PROM_REDUCTION_MAX_STAGES 8u
+/* Reference envelope (reactors/PrometheusReduction.concept:66-75).  This
+   library WIDENS it deliberately: rows up to OCT_B200_REDUCTION_MAX_ROWS and
+   totals up to OCT_B200_REDUCTION_MAX_TOTAL_ELEMENTS are admitted under the
+   same symbols; the in-envelope detail codes are unchanged. */
+#define PROM_REDUCTION_MAX_ROWS 1024u
+#define PROM_REDUCTION_MAX_ELEMENTS_PER_ROW 1048576u
+#define PROM_REDUCTION_MAX_TOTAL_ELEMENTS 16777216u
+#define PROM_REDUCTION_LOCAL_SIZE 256u
+#define PROM_REDUCTION_ELEMENTS_PER_PARTIAL 1024u
+#define PROM_REDUCTION_SINGLE_STAGE_THRESHOLD 1024u
+#define PROM_REDUCTION_FORCE_FUSED_MAX_ELEMENTS_PER_ROW 1056u
+#define PROM_REDUCTION_PACKED_SHORT_WIDTH_MAX 128u
+#define PROM_REDUCTION_PACKED_SHORT_SUM_MIN_ROWS 512u
+#define PROM_REDUCTION_PACKED_SHORT_SUM_WIDE_MIN_ROWS 1024u
+#define PROM_REDUCTION_PACKED_SHORT_ROWS_PER_GROUP 8u
+#define PROM_REDUCTION_PACKED_SHORT_LANES_PER_ROW 32u
+
+#define OCT_B200_REDUCTION_MAX_ROWS 16777216u
+#define OCT_B200_REDUCTION_MAX_TOTAL_ELEMENTS (1ull << 34)
+
+#define PROM_ROW_WISE_SOFTMAX_MAX_ROWS PROM_REDUCTION_MAX_ROWS
+#define PROM_ROW_WISE_SOFTMAX_MAX_ELEMENTS_PER_ROW PROM_REDUCTION_FORCE_FUSED_MAX_ELEMENTS_PER_ROW
+#define PROM_ROW_WISE_SOFTMAX_MAX_TOTAL_ELEMENTS PROM_REDUCTION_MAX_TOTAL_ELEMENTS
+
+/* ---- structs (layouts as reactor_api.h:509-664, 1582-1586, 1751-1779) ---- */
+typedef struct PrometheusRowWiseSoftmaxRequest {
+  uint32_t struct_size;
+  const float* input;
+  float* output;
+  uint32_t row_count;
+  uint32_t elements_per_row;
+  uint64_t input_element_count;
+  uint64_t output_element_count;
+} PrometheusRowWiseSoftmaxRequest;
+
+typedef struct PrometheusRowWiseSoftmaxResult {
+  uint32_t struct_size;
+  uint32_t stage;
+  int32_t detail_code;
+  uint32_t output_written;
+  uint32_t physical_dispatch_count;
+  uint32_t physical_submission_count;
+  uint32_t gpu_timestamp_valid;
+  uint64_t gpu_duration_ns;
+  uint64_t end_to_end_ns;
+  uint64_t first_nonfinite_index;
+} PrometheusRowWiseSoftmaxResult;
+
+typedef struct PrometheusReductionRequest {
+  uint32_t struct_size;
+  const float* input;
+  float* output;
+  uint32_t row_count;
+  uint32_t elements_per_row;
+  uint64_t input_element_count;
+  uint64_t output_element_count;
+  uint32_t operation;
+  uint32_t finalization;
+  uint32_t flags;
+} PrometheusReductionRequest;
+
+typedef struct PrometheusReductionStageDispatch {
+  uint32_t stage_role;
+  uint32_t shader_id;
+  uint32_t implementation_id;
+  uint32_t groups_x;
+  uint32_t groups_y;
+  uint32_t groups_z;
+  uint32_t input_elements_per_row;
+  uint32_t output_partials_per_row;
+  uint32_t temporary_role;
+  uint64_t temporary_bytes_written;
+} PrometheusReductionStageDispatch;
+
+typedef struct PrometheusReductionPlan {
+  uint32_t struct_size;
+  uint32_t operation;
+  uint32_t row_count;
+  uint32_t elements_per_row;
+  uint32_t strategy;
+  uint32_t local_size;
+  uint32_t elements_per_partial;
+  uint32_t partial_count;
+  uint32_t stage_count;
+  uint32_t temporary_alignment_bytes;
+  uint64_t temporary_bytes;
+  uint64_t replay_id;
+  PrometheusReductionStageDispatch stages[PROM_REDUCTION_MAX_STAGES];
+} PrometheusReductionPlan;
+
+typedef struct PrometheusReductionExecutionResult {
+  uint32_t struct_size;
+  uint32_t stage;
+  int32_t detail_code;
+  uint64_t logical_request_id;
+  uint32_t physical_slot_id;
+  uint32_t physical_slot_generation;
+  uint32_t physical_slot_recyclable;
+  uint32_t gpu_timestamp_valid;
+  uint64_t gpu_duration_ns;
+  uint64_t end_to_end_ns;
+  uint64_t first_nonfinite_index;
+  uint32_t validation_error_count_before;
+  uint32_t validation_error_count_after;
+  PrometheusReductionPlan plan;
+} PrometheusReductionExecutionResult;
+
+typedef struct PrometheusReductionBenchmarkRequest {
+  uint32_t struct_size;
+  PrometheusReductionRequest reduction;
+  uint32_t warmup_iterations;
+  uint32_t measured_iterations;
+} PrometheusReductionBenchmarkRequest;
+
+typedef struct PrometheusReductionBenchmarkResult {
+  uint32_t struct_size;
+  uint32_t completed_iterations;
+  uint32_t correctness_passed;
+  uint32_t validation_passed;
+  uint32_t device_lost;
+  uint32_t stage_count;
+  uint64_t temporary_bytes;
+  uint64_t replay_id;
+  uint64_t gpu_min_ns;
+  uint64_t gpu_median_ns;
+  uint64_t gpu_max_ns;
+  uint64_t end_to_end_min_ns;
+  uint64_t end_to_end_median_ns;
+  uint64_t end_to_end_max_ns;
+  uint32_t first_mismatch_row;
+  uint32_t first_mismatch_column;
+  float first_expected;
+  float first_actual;
+  float first_absolute_error;
+  float first_relative_error;
+  int32_t detail_code;
+} PrometheusReductionBenchmarkResult;
+
+typedef struct PrometheusCaps {
+  uint32_t available;
+  uint32_t backend_type;
+  uint32_t reason_code;
+} PrometheusCaps;
+
+typedef struct PrometheusReactorConfig {
+  uint32_t struct_size;
+  uint32_t test_flags;
+  uint32_t p15_shadow_disabled;     /* accepted, ignored: no selector shadow here */
+  uint32_t async_test_flags;
+  uint32_t batch_ring_depth;        /* accepted, ignored */
+  uint32_t reduction_test_flags;
+  uint32_t reduction_ring_depth;    /* accepted, ignored: one CUDA stream per handle */
+  const char* shader_package_root;  /* accepted, ignored: kernels are linked in */
+} PrometheusReactorConfig;
+
+typedef struct PrometheusAsyncStatus {
+  uint32_t lifecycle_state;
+  uint32_t stage;
+  int detail_code;
+  uint32_t ready;
+  uint32_t failed;
+  uint32_t consumed;
+  uint32_t outstanding_tasks;
+} PrometheusAsyncStatus;
+
+/* Gemma RMSNorm request/result (reactor_api.h:1781-1825).  The Gemma-private
+   generation/hash fields are accepted and echoed, not enforced. */
+typedef struct PrometheusGemma4E2BM1InputRmsNormRequest {
+  uint32_t struct_size;
+  const float* input;
+  const float* weight;
+  float* output;
+  float* inv_rms_output;
+  uint64_t input_element_count;
+  uint64_t weight_element_count;
+  uint64_t output_element_count;
+  uint64_t inv_rms_output_element_count;
+  uint32_t tokens;
+  uint32_t model_width;
+  uint32_t input_row_stride;
+  float epsilon;
+  uint64_t input_generation;
+  uint64_t weight_generation;
+  uint64_t exact_source_hash;
+} PrometheusGemma4E2BM1InputRmsNormRequest;
+
+typedef struct PrometheusGemma4E2BM1InputRmsNormResult {
+  uint32_t struct_size;
+  uint32_t stage;
+  int32_t detail_code;
+  uint32_t output_written;
+  uint32_t matched_input;
+  uint64_t input_hash;
+  uint64_t weight_hash;
+  uint64_t output_hash;
+  uint64_t inv_rms_hash;
+  uint32_t submit_count;
+  uint32_t final_readback_count;
+  uint32_t no_product_intermediate_readback_change;
+  uint32_t reserved0;
+  uint64_t retained_bytes;
+  uint64_t buffer_allocation_count;
+  uint64_t buffer_reuse_count;
+  uint64_t descriptor_update_count;
+  uint64_t pipeline_create_count;
+  uint64_t command_buffer_reuse_count;
+  uint64_t reduction_gpu_ns;
+  uint64_t final_reduction_gpu_ns;
+  uint64_t inv_rms_gpu_ns;
+  uint64_t apply_gpu_ns;
+  uint64_t end_to_end_ns;
+} PrometheusGemma4E2BM1InputRmsNormResult;
+
+typedef PrometheusGemma4E2BM1InputRmsNormRequest PrometheusGemma4E2BM1HeadRmsNormRequest;
+typedef PrometheusGemma4E2BM1InputRmsNormResult PrometheusGemma4E2BM1HeadRmsNormResult;
+
+/* ==== reference ABI entry points ==== */
+
+/* reactor_api.h:2557 -- always returns PROM_REACTOR_ABI_V1 (bridge.go:276-290 checks it). */
+PROM_REACTOR_API uint32_t prometheus_reactor_abi_version(void);
+/* reactor_api.h:2558 -- config may be NULL; tail fields gated by struct_size. */
+PROM_REACTOR_API int prometheus_reactor_runtime_create(void* config, void** out_handle);
+/* reactor_api.h:2559 -- requires quiescent callers. */
+PROM_REACTOR_API int prometheus_reactor_runtime_destroy(void* handle);
+/* reactor_api.h:2560 -- available=1, backend_type=2 on a usable sm_100 device. */
+PROM_REACTOR_API int prometheus_reactor_runtime_probe(void* handle, PrometheusCaps* out_caps);
+
+/* reactor_api.h:2587-2595 -- C[m x n] = A[m x k] * B[k x n], row-major fp32 host
+   buffers, C overwritten.  Sizes beyond the reference's u32 m*n*k ceiling
+   (reactor_sgemm.cpp:4171-4176) are admitted: only host/device capacity
+   limits apply.  Success reports stage TRANSFER_OUT and PROM_DETAIL_PATH_DIRECT. */
+PROM_REACTOR_API int prometheus_reactor_runtime_sgemm(void* handle, const float* a, const float* b, float* c,
+                                                      uint32_t m, uint32_t n, uint32_t k,
+                                                      uint32_t* out_stage, int* out_detail_code);
+
+/* reactor_api.h:2623-2643 -- non-blocking SGEMM.  The library owns the result
+   until consume copies it into `c` (length-checked) or abandon drops it. */
+PROM_REACTOR_API int prometheus_reactor_runtime_sgemm_submit_async(void* handle, const float* a, const float* b,
+                                                                   uint32_t m, uint32_t n, uint32_t k,
+                                                                   int* out_task_id, uint32_t* out_stage,
+                                                                   int* out_detail_code);
+PROM_REACTOR_API int prometheus_reactor_runtime_sgemm_query_async(void* handle, int task_id,
+                                                                  PrometheusAsyncStatus* out_status);
+PROM_REACTOR_API int prometheus_reactor_runtime_sgemm_consume_async(void* handle, int task_id, float* c,
+                                                                    uint32_t c_len, uint32_t* out_stage,
+                                                                    int* out_detail_code);
+PROM_REACTOR_API int prometheus_reactor_runtime_sgemm_abandon_async(void* handle, int task_id);
+
+/* reactor_api.h:2671-2672 -- host-only planner; same stage roles as the
+   reference schedule (reactors/PrometheusReduction.concept:128-164). */
+PROM_REACTOR_API int prometheus_reactor_reduction_plan(const PrometheusReductionRequest* request,
+                                                        PrometheusReductionPlan* out_plan);
+/* reactor_api.h:2673-2675 -- row SUM / MAX / stable SOFTMAX over host buffers. */
+PROM_REACTOR_API int prometheus_reactor_runtime_reduction(void* handle, const PrometheusReductionRequest* request,
+                                                          PrometheusReductionExecutionResult* out_result);
+/* reactor_api.h:2682-2685 -- forced fused softmax; rejects partial aliasing and
+   non-finite input like reactor_vulkan_fused_reduction.c:892-994. */
+PROM_REACTOR_API int prometheus_reactor_runtime_row_wise_softmax(void* handle,
+                                                                 const PrometheusRowWiseSoftmaxRequest* request,
+                                                                 PrometheusRowWiseSoftmaxResult* out_result);
+/* reactor_api.h:2686-2691 -- RMSNorm y = x / sqrt(mean(x^2) + eps) * weight per
+   token row; inv_rms_output receives the per-row scale. */
+PROM_REACTOR_API int prometheus_reactor_runtime_gemma4e2b_m1_input_rmsnorm(
+    void* handle, const PrometheusGemma4E2BM1InputRmsNormRequest* request,
+    PrometheusGemma4E2BM1InputRmsNormResult* out_result);
+/* reactor_api.h:2696-2699 -- the same primitive over [token, head, channel] rows. */
+PROM_REACTOR_API int prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm(
+    void* handle, const PrometheusGemma4E2BM1HeadRmsNormRequest* request,
+    PrometheusGemma4E2BM1HeadRmsNormResult* out_result);
+
+/* reactor_api.h:2823-2826 -- aliases kept by the reference for older drafts. */
+PROM_REACTOR_API int prometheus_runtime_create(void* config, void** out_handle);
+PROM_REACTOR_API int prometheus_runtime_destroy(void* handle);
+PROM_REACTOR_API int prometheus_runtime_probe(void* handle, PrometheusCaps* out_caps);
+
+/* ==== extensions: device-resident entry points (no reference counterpart) ==== */
+
+/* SGEMM kernel variants. */
+enum {
+  OCT_B200_SGEMM_AUTO = 0u,       /* 3xTF32 tcgen05 for large shapes, FMA for tiny ones */
+  OCT_B200_SGEMM_TC3XTF32 = 1u,   /* tcgen05/TMEM tensor cores, split-TF32 x3 */
+  OCT_B200_SGEMM_FMA = 2u,        /* plain FP32 FMA on the CUDA cores (control) */
+};
+
+/* C = A * B on device pointers (row-major, ld = k / n / n), enqueued on
+   `stream` (a cudaStream_t; NULL = the handle's stream).  Returns immediately
+   after enqueue; scratch buffers for the TF32 split live in the handle. */
+PROM_REACTOR_API int oct_b200_sgemm_device(void* handle, const float* d_a, const float* d_b, float* d_c,
+                                           uint32_t m, uint32_t n, uint32_t k, uint32_t variant,
+                                           void* stream, int* out_detail_code);
+
+/* Same as above with explicit leading dimensions (elements) for A, B and C, so
+   a caller can address a column shard of a wider matrix.  lda >= k, ldb >= n,
+   ldc >= n. */
+PROM_REACTOR_API int oct_b200_sgemm_device_ld(void* handle, const float* d_a, uint64_t lda, const float* d_b,
+                                              uint64_t ldb, float* d_c, uint64_t ldc, uint32_t m, uint32_t n,
+                                              uint32_t k, uint32_t variant, void* stream, int* out_detail_code);
+
+/* Row reductions on device pointers.  operation: PROM_REDUCTION_OPERATION_*.
+   SUM/MAX write `rows` floats, SOFTMAX writes rows*width floats. */
+PROM_REACTOR_API int oct_b200_reduction_device(void* handle, const float* d_in, float* d_out, uint32_t rows,
+                                               uint32_t width, uint32_t operation, void* stream,
+                                               int* out_detail_code);
+
+/* RMSNorm on device pointers: out[r, :] = in[r, :] * inv_rms[r] * weight[:],
+   inv_rms[r] = 1 / sqrt(mean(in[r, :]^2) + eps).  d_inv_rms may be NULL. */
+PROM_REACTOR_API int oct_b200_rmsnorm_device(void* handle, const float* d_in, const float* d_weight, float* d_out,
+                                             float* d_inv_rms, uint32_t rows, uint32_t width, float epsilon,
+                                             void* stream, int* out_detail_code);
+
+/* Waits for `stream` (NULL: only the handle's own stream), then reads and
+   clears the device status words the kernels write: returns PROM_ERROR with
+   OCT_B200_DETAIL_DEVICE_TIMEOUT if a bounded in-kernel wait gave up, or
+   PROM_REDUCTION_DETAIL_NONFINITE_INPUT if a reduction saw NaN/Inf. */
+PROM_REACTOR_API int oct_b200_sync_status(void* handle, void* stream, int* out_detail_code);
+
+/* Per-launch timing of the tensor-core SGEMM: when enabled, CUDA events are
+   recorded on the launch stream around the TF32 split pass and the main
+   kernel of every launch; read returns the summed milliseconds of the
+   launches since the last read (waiting for them) and resets the count. */
+PROM_REACTOR_API int oct_b200_set_kernel_timing(void* handle, int enable);
+PROM_REACTOR_API int oct_b200_read_kernel_timing(void* handle, double* split_ms_total, double* main_ms_total,
+                                                 uint32_t* launches);
+
+/* Library build identity, for diagnostics. */
+PROM_REACTOR_API const char* oct_b200_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OCT_B200_PROMETHEUS_REACTOR_H */

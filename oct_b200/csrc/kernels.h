@@ -1,0 +1,49 @@
+// kernels.h -- host-side launchers for the CUDA kernels, used by the C-ABI layer.
+// Every launcher enqueues on `stream` and returns a cudaError_t for the launch;
+// kernel-side wait timeouts land in the `err` device word.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace oct {
+
+// ---------------------------------------------------------------- SGEMM
+// Padded extents of the split-TF32 operand buffers for an (m, n, k) product.
+struct SplitDims {
+  uint32_t mp, np, kp;  // m rounded to the M tile, n to the N tile, k to 32
+};
+SplitDims split_dims(uint32_t m, uint32_t n, uint32_t k);
+
+// Bytes of scratch needed by sgemm_tc for (m, n, k): hi/lo copies of A and of B^T.
+uint64_t sgemm_tc_scratch_bytes(uint32_t m, uint32_t n, uint32_t k);
+
+// 3xTF32 tensor-core SGEMM.  `scratch` must hold sgemm_tc_scratch_bytes and be
+// 1024-byte aligned.  bk selects the K depth of one pipeline stage (16 or 32).
+// Optional events (may be null) are recorded on `stream` before the split
+// pass, before the main kernel and after it, for per-kernel timing.
+struct SgemmEvents {
+  cudaEvent_t split_begin = nullptr, main_begin = nullptr, main_end = nullptr;
+};
+cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
+                     uint32_t m, uint32_t n, uint32_t k, void* scratch, unsigned int* err, int bk,
+                     cudaStream_t stream, const SgemmEvents* events = nullptr);
+
+// Plain FP32-FMA SGEMM on the CUDA cores (control variant); no scratch.
+cudaError_t sgemm_fma(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
+                      uint32_t m, uint32_t n, uint32_t k, cudaStream_t stream);
+
+// ---------------------------------------------------------------- reductions
+// op: 1 = row sum, 2 = row max, 3 = stable softmax.  `nonfinite` (device
+// u64, preset to UINT64_MAX by the caller) receives the smallest flat index of
+// a NaN/Inf input element, if any.
+cudaError_t row_reduce(const float* in, float* out, uint32_t rows, uint32_t width, uint32_t op,
+                       unsigned long long* nonfinite, unsigned int* err, cudaStream_t stream);
+
+// RMSNorm: out = in * inv_rms * weight, inv_rms = 1/sqrt(mean(in^2)+eps).
+// in_stride is the element distance between consecutive input rows.
+cudaError_t rmsnorm(const float* in, uint64_t in_stride, const float* weight, float* out, float* inv_rms,
+                    uint32_t rows, uint32_t width, float eps, unsigned long long* nonfinite, unsigned int* err,
+                    cudaStream_t stream);
+
+}  // namespace oct

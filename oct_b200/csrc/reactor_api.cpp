@@ -1,0 +1,1277 @@
+// reactor_api.cpp -- the C ABI of libprometheus_reactor.so (ABI v1) over CUDA.
+//
+// This file is the drop-in boundary: the symbols, argument meanings, status /
+// stage / detail conventions and validation order of Oct's Prometheus reactor
+// (internal/prometheus/native/reactor_api.h, reactor_api.c, reactor_sgemm.cpp,
+// reactor_concept_reduction.cpp, reactor_vulkan_fused_reduction.c), with the
+// Vulkan runtime underneath replaced by one CUDA stream per handle and the
+// kernels in sgemm_tc.cu, sgemm_fma.cu and reduce.cu.
+//
+// There is no CPU fallback anywhere: a handle without a usable sm_100 device
+// reports available=0 from probe and every compute call fails with a detail
+// code.  No C++ exception crosses the boundary (each entry point catches).
+#include "../../include/prometheus_reactor.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <unordered_set>
+#include <vector>
+
+#include "kernels.h"
+
+namespace {
+
+using Clock = std::chrono::steady_clock;
+constexpr uint32_t kMagic = 0x0C7B2000u;
+constexpr int kAsyncSlots = 4;  // task capacity, as the reference (reactor_api.h:2030 tasks[4])
+
+uint64_t ns_since(Clock::time_point t0) {
+  return static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(Clock::now() - t0).count());
+}
+
+void set_status(uint32_t* stage, int* detail, uint32_t s, int d) {
+  if (stage != nullptr) *stage = s;
+  if (detail != nullptr) *detail = d;
+}
+
+// A growable device allocation.  Growth synchronises the owning stream first
+// so no kernel in flight still references the old block.
+struct DevBuf {
+  void* raw = nullptr;
+  uint64_t cap = 0;
+  void* aligned() const { return reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023)); }
+  cudaError_t ensure(uint64_t bytes, cudaStream_t s) {
+    if (bytes <= cap && raw != nullptr) return cudaSuccess;
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return e;
+    if (raw != nullptr) cudaFree(raw);
+    raw = nullptr;
+    cap = 0;
+    const uint64_t want = bytes + (bytes >> 3);  // 12.5% headroom against regrowth
+    e = cudaMalloc(&raw, want + 1024);
+    if (e != cudaSuccess) {
+      raw = nullptr;
+      (void)cudaGetLastError();
+      return e;
+    }
+    cap = want;
+    return cudaSuccess;
+  }
+  void release() {
+    if (raw != nullptr) cudaFree(raw);
+    raw = nullptr;
+    cap = 0;
+  }
+};
+
+struct AsyncTask {
+  bool active = false;
+  int id = 0;
+  uint32_t state = PROM_ASYNC_STATE_IDLE;
+  uint32_t m = 0, n = 0, k = 0;
+  int final_detail = 0;
+  uint32_t final_stage = 0;
+  cudaEvent_t done = nullptr;
+  DevBuf a, b, c;
+};
+
+struct Runtime {
+  uint32_t magic = kMagic;
+  std::mutex mu;
+  int device = 0;
+  bool available = false;
+  uint32_t reason = PROM_REASON_NONE;
+  uint32_t test_flags = 0, async_test_flags = 0, reduction_test_flags = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  DevBuf scratch;               // split-TF32 operand buffers
+  DevBuf da, db, dc;            // staging for host-pointer SGEMM
+  DevBuf rin, rout, rw, rinv;   // staging for reductions / RMSNorm
+  DevBuf words;                 // [0] kernel error bits (u32), [8] first non-finite index (u64)
+  AsyncTask tasks[kAsyncSlots];
+  int next_task_id = 1;
+  // Optional per-launch kernel timing of the tensor-core SGEMM (events on the
+  // launch stream): split pass and main kernel, summed on read.
+  bool timing = false;
+  std::vector<oct::SgemmEvents> timing_events;
+  size_t timing_used = 0;
+  uint64_t next_request_id = 1;
+
+  unsigned int* err_word() { return static_cast<unsigned int*>(words.aligned()); }
+  unsigned long long* nonfinite_word() {
+    return reinterpret_cast<unsigned long long*>(static_cast<char*>(words.aligned()) + 8);
+  }
+};
+
+std::mutex g_registry_mu;
+std::unordered_set<Runtime*>* g_registry = new std::unordered_set<Runtime*>();
+
+Runtime* lookup(void* handle) {
+  if (handle == nullptr) return nullptr;
+  std::lock_guard<std::mutex> lock(g_registry_mu);
+  Runtime* rt = static_cast<Runtime*>(handle);
+  if (g_registry->count(rt) == 0 || rt->magic != kMagic) return nullptr;
+  return rt;
+}
+
+// Resets the kernel status words on the stream (async).
+cudaError_t reset_words(Runtime* rt) {
+  cudaError_t e = cudaMemsetAsync(rt->err_word(), 0, 8, rt->stream);
+  if (e != cudaSuccess) return e;
+  return cudaMemsetAsync(rt->nonfinite_word(), 0xFF, 8, rt->stream);
+}
+
+struct Words {
+  unsigned int err = 0;
+  unsigned long long nonfinite = ~0ull;
+};
+
+cudaError_t read_words(Runtime* rt, Words* w) {
+  unsigned char host[16];
+  cudaError_t e = cudaMemcpyAsync(host, rt->words.aligned(), 16, cudaMemcpyDeviceToHost, rt->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
+  if (e != cudaSuccess) return e;
+  std::memcpy(&w->err, host, 4);
+  std::memcpy(&w->nonfinite, host + 8, 8);
+  return cudaSuccess;
+}
+
+bool checked_mul(uint64_t a, uint64_t b, uint64_t* out) {
+  if (a != 0 && b > UINT64_MAX / a) return false;
+  *out = a * b;
+  return true;
+}
+
+// ---------------------------------------------------------------- SGEMM core
+// Enqueues C = A * B for device pointers; chooses the kernel.
+int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
+                  uint32_t m, uint32_t n, uint32_t k, uint32_t variant, cudaStream_t stream) {
+  if (variant == OCT_B200_SGEMM_AUTO) {
+    // Tiny products do not fill one 128x256 tensor-core tile usefully; the
+    // FMA control is exact-tail by construction and cheaper there.
+    const double work = static_cast<double>(m) * n * k;
+    variant = (work < 4.0e6 || m < 16) ? OCT_B200_SGEMM_FMA : OCT_B200_SGEMM_TC3XTF32;
+  }
+  cudaError_t e;
+  if (variant == OCT_B200_SGEMM_FMA) {
+    e = oct::sgemm_fma(a, lda, b, ldb, c, ldc, m, n, k, stream);
+  } else if (variant == OCT_B200_SGEMM_TC3XTF32 || variant == 16u || variant == 32u) {
+    const uint64_t need = oct::sgemm_tc_scratch_bytes(m, n, k);
+    e = rt->scratch.ensure(need, stream);
+    if (e != cudaSuccess) return OCT_B200_DETAIL_OUT_OF_MEMORY;
+    const int bk = (variant == 32u) ? 32 : 16;
+    const oct::SgemmEvents* ev = nullptr;
+    if (rt->timing) {
+      if (rt->timing_used == rt->timing_events.size()) {
+        oct::SgemmEvents fresh;
+        if (cudaEventCreate(&fresh.split_begin) != cudaSuccess || cudaEventCreate(&fresh.main_begin) != cudaSuccess ||
+            cudaEventCreate(&fresh.main_end) != cudaSuccess)
+          return OCT_B200_DETAIL_CUDA_ERROR;
+        rt->timing_events.push_back(fresh);
+      }
+      ev = &rt->timing_events[rt->timing_used++];
+    }
+    e = oct::sgemm_tc(a, lda, b, ldb, c, ldc, m, n, k, rt->scratch.aligned(), rt->err_word(), bk, stream, ev);
+  } else {
+    return OCT_B200_DETAIL_BAD_VARIANT;
+  }
+  return e == cudaSuccess ? 0 : OCT_B200_DETAIL_CUDA_ERROR;
+}
+
+Runtime* create_runtime(const PrometheusReactorConfig* cfg, int* status) {
+  Runtime* rt = new (std::nothrow) Runtime();
+  if (rt == nullptr) {
+    *status = PROM_INTERNAL_ERROR;
+    return nullptr;
+  }
+  if (cfg != nullptr) {
+    const uint32_t sz = cfg->struct_size;
+    if (sz >= offsetof(PrometheusReactorConfig, test_flags) + sizeof(uint32_t)) rt->test_flags = cfg->test_flags;
+    if (sz >= offsetof(PrometheusReactorConfig, async_test_flags) + sizeof(uint32_t))
+      rt->async_test_flags = cfg->async_test_flags;
+    if (sz >= offsetof(PrometheusReactorConfig, reduction_test_flags) + sizeof(uint32_t))
+      rt->reduction_test_flags = cfg->reduction_test_flags;
+  }
+  if (rt->test_flags & PROM_TESTCFG_FAIL_DEVICE_CREATE) {
+    // Injected on the host: the handle exists but reports no device.
+    rt->reason = PROM_REASON_VULKAN_UNAVAILABLE;
+    *status = PROM_OK;
+    return rt;
+  }
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    (void)cudaGetLastError();
+    rt->reason = PROM_REASON_VULKAN_UNAVAILABLE;
+    *status = PROM_OK;
+    return rt;
+  }
+  cudaGetDevice(&rt->device);
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, rt->device) != cudaSuccess || prop.major != 10) {
+    rt->reason = PROM_REASON_VULKAN_UNAVAILABLE;
+    *status = PROM_OK;
+    return rt;
+  }
+  if (cudaStreamCreateWithFlags(&rt->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreate(&rt->ev0) != cudaSuccess || cudaEventCreate(&rt->ev1) != cudaSuccess ||
+      rt->words.ensure(16, rt->stream) != cudaSuccess) {
+    rt->reason = PROM_REASON_VULKAN_UNAVAILABLE;
+    *status = PROM_OK;
+    return rt;
+  }
+  rt->available = true;
+  *status = PROM_OK;
+  return rt;
+}
+
+void destroy_runtime(Runtime* rt) {
+  if (rt->stream != nullptr) cudaStreamSynchronize(rt->stream);
+  for (auto& ev : rt->timing_events) {
+    cudaEventSynchronize(ev.main_end);
+    cudaEventDestroy(ev.split_begin);
+    cudaEventDestroy(ev.main_begin);
+    cudaEventDestroy(ev.main_end);
+  }
+  for (auto& t : rt->tasks) {
+    if (t.done != nullptr) cudaEventDestroy(t.done);
+    t.a.release();
+    t.b.release();
+    t.c.release();
+  }
+  for (DevBuf* b : {&rt->scratch, &rt->da, &rt->db, &rt->dc, &rt->rin, &rt->rout, &rt->rw, &rt->rinv, &rt->words})
+    b->release();
+  if (rt->ev0 != nullptr) cudaEventDestroy(rt->ev0);
+  if (rt->ev1 != nullptr) cudaEventDestroy(rt->ev1);
+  if (rt->stream != nullptr) cudaStreamDestroy(rt->stream);
+  rt->magic = 0;
+  delete rt;
+}
+
+// ---------------------------------------------------------------- reductions
+struct ReductionShape {
+  uint32_t rows, width, operation, finalization, flags;
+  uint64_t input_count, output_count;
+};
+
+// Admission rules of reactors/PrometheusReduction.concept:66-88 with the row
+// and total ceilings widened (the detail codes are unchanged).
+int validate_shape(const ReductionShape& s) {
+  if (s.rows == 0) return PROM_REDUCTION_DETAIL_ZERO_ROW_COUNT;
+  if (s.width == 0) return PROM_REDUCTION_DETAIL_ZERO_ROW_WIDTH;
+  if (s.rows > OCT_B200_REDUCTION_MAX_ROWS) return PROM_REDUCTION_DETAIL_ROW_LIMIT;
+  if (s.width > PROM_REDUCTION_MAX_ELEMENTS_PER_ROW) return PROM_REDUCTION_DETAIL_WIDTH_LIMIT;
+  const uint64_t total = static_cast<uint64_t>(s.rows) * s.width;
+  if (total > OCT_B200_REDUCTION_MAX_TOTAL_ELEMENTS) return PROM_REDUCTION_DETAIL_ELEMENT_LIMIT;
+  if (s.operation != PROM_REDUCTION_OPERATION_SUM && s.operation != PROM_REDUCTION_OPERATION_MAX &&
+      s.operation != PROM_REDUCTION_OPERATION_SOFTMAX)
+    return PROM_REDUCTION_DETAIL_UNSUPPORTED_OPERATION;
+  uint64_t output = s.rows;
+  if (s.operation == PROM_REDUCTION_OPERATION_SOFTMAX) {
+    if (s.finalization != PROM_REDUCTION_FINALIZATION_STABLE_SOFTMAX) return PROM_REDUCTION_DETAIL_INVALID_FINALIZATION;
+    output = total;
+  } else if (s.finalization != PROM_REDUCTION_FINALIZATION_NONE) {
+    return PROM_REDUCTION_DETAIL_INVALID_FINALIZATION;
+  }
+  if (s.flags > 2u || (s.operation != PROM_REDUCTION_OPERATION_SOFTMAX && s.flags != 0u))
+    return PROM_REDUCTION_DETAIL_UNSUPPORTED_STRATEGY;
+  if (s.flags == PROM_REDUCTION_FLAG_FORCE_FUSED && s.width > PROM_REDUCTION_FORCE_FUSED_MAX_ELEMENTS_PER_ROW)
+    return PROM_REDUCTION_DETAIL_UNSUPPORTED_STRATEGY;
+  if (s.input_count != total) return PROM_REDUCTION_DETAIL_INPUT_SIZE_MISMATCH;
+  if (s.output_count != output) return PROM_REDUCTION_DETAIL_OUTPUT_SIZE_MISMATCH;
+  return 0;
+}
+
+ReductionShape shape_of(const PrometheusReductionRequest* r) {
+  return ReductionShape{r->row_count, r->elements_per_row, r->operation, r->finalization, r->flags,
+                        r->input_element_count, r->output_element_count};
+}
+
+uint64_t fnv_u32(uint64_t h, uint32_t v) {
+  for (uint32_t i = 0; i < 4; ++i) {
+    h ^= static_cast<uint64_t>((v >> (i * 8u)) & 0xFFu);
+    h *= 1099511628211ull;
+  }
+  return h;
+}
+
+// The logical schedule Oct's planner emits (reactors/PrometheusReduction.concept:
+// 96-164, serialised as reactor_vulkan_fused_reduction.c:101-148).  The CUDA
+// path executes every schedule as ONE fused kernel with a single HBM pass; the
+// plan is still reported so plan-level callers and replay ids stay compatible.
+void build_plan(const ReductionShape& s, PrometheusReductionPlan* p) {
+  static const uint32_t shader_of[8] = {0,
+                                        PROM_REDUCTION_SHADER_ROW_SUM,
+                                        PROM_REDUCTION_SHADER_ROW_MAX,
+                                        PROM_REDUCTION_SHADER_SOFTMAX_EXP_SUM,
+                                        PROM_REDUCTION_SHADER_SOFTMAX_NORMALIZE,
+                                        PROM_REDUCTION_SHADER_SOFTMAX_FUSED,
+                                        PROM_REDUCTION_SHADER_ROW_SUM_PACKED_SHORT,
+                                        PROM_REDUCTION_SHADER_SOFTMAX_PACKED_SHORT};
+  std::memset(p, 0, sizeof(*p));
+  p->struct_size = sizeof(*p);
+  p->operation = s.operation;
+  p->row_count = s.rows;
+  p->elements_per_row = s.width;
+  p->local_size = PROM_REDUCTION_LOCAL_SIZE;
+  p->elements_per_partial = PROM_REDUCTION_ELEMENTS_PER_PARTIAL;
+  p->temporary_alignment_bytes = sizeof(float);
+  const uint32_t partials = (s.width + PROM_REDUCTION_ELEMENTS_PER_PARTIAL - 1) / PROM_REDUCTION_ELEMENTS_PER_PARTIAL;
+  p->partial_count = partials;
+  p->strategy = PROM_REDUCTION_STRATEGY_COMPOSED;
+  const uint64_t row_bytes = static_cast<uint64_t>(s.rows) * 4u;
+  const uint64_t partial_bytes = partials > 1 ? row_bytes * partials : 0;
+
+  auto append = [&](uint32_t role, uint64_t groups, uint32_t width, uint32_t out_partials, uint32_t temp_role,
+                    uint64_t temp_bytes) {
+    PrometheusReductionStageDispatch& st = p->stages[p->stage_count++];
+    st.stage_role = role;
+    st.shader_id = shader_of[role];
+    st.implementation_id = 1000u + role;
+    st.groups_x = static_cast<uint32_t>(std::min<uint64_t>(groups, UINT32_MAX));
+    st.groups_y = 1;
+    st.groups_z = 1;
+    st.input_elements_per_row = width;
+    st.output_partials_per_row = out_partials;
+    st.temporary_role = temp_role;
+    st.temporary_bytes_written = temp_bytes;
+  };
+  // A row reduction is one partial pass plus, with >1 partial, a finishing pass.
+  auto reduce = [&](uint32_t partial_role, uint32_t final_role, uint32_t destination, uint64_t dest_bytes) {
+    uint32_t first_dest = destination;
+    uint64_t first_bytes = dest_bytes;
+    if (partials > 1) {
+      first_dest = PROM_REDUCTION_TEMPORARY_PARTIALS;
+      first_bytes = row_bytes * partials;
+    }
+    append(partial_role, static_cast<uint64_t>(s.rows) * partials, s.width, partials, first_dest, first_bytes);
+    if (partials > 1) append(final_role, s.rows, partials, 1, destination, dest_bytes);
+  };
+
+  bool packed;
+  if (s.operation == PROM_REDUCTION_OPERATION_SOFTMAX)
+    packed = s.flags == 0 && s.width <= PROM_REDUCTION_PACKED_SHORT_WIDTH_MAX;
+  else if (s.operation != PROM_REDUCTION_OPERATION_SUM)
+    packed = false;
+  else
+    packed = (s.width <= 96u && s.rows >= PROM_REDUCTION_PACKED_SHORT_SUM_MIN_ROWS) ||
+             (s.width <= PROM_REDUCTION_PACKED_SHORT_WIDTH_MAX && s.rows >= PROM_REDUCTION_PACKED_SHORT_SUM_WIDE_MIN_ROWS);
+
+  if (packed) {
+    p->strategy = PROM_REDUCTION_STRATEGY_PACKED_SHORT_ROWS;
+    append(s.operation == PROM_REDUCTION_OPERATION_SOFTMAX ? 7u : 6u,
+           (s.rows + PROM_REDUCTION_PACKED_SHORT_ROWS_PER_GROUP - 1) / PROM_REDUCTION_PACKED_SHORT_ROWS_PER_GROUP,
+           s.width, 1, 0, 0);
+  } else if (s.operation != PROM_REDUCTION_OPERATION_SOFTMAX) {
+    reduce(s.operation, s.operation, PROM_REDUCTION_TEMPORARY_NONE, 0);
+    p->temporary_bytes = partial_bytes;
+  } else if (s.flags != PROM_REDUCTION_FLAG_FORCE_COMPOSED &&
+             (s.flags == PROM_REDUCTION_FLAG_FORCE_FUSED || s.width <= PROM_REDUCTION_ELEMENTS_PER_PARTIAL)) {
+    p->strategy = PROM_REDUCTION_STRATEGY_FUSED_SINGLE_WORKGROUP;
+    append(5u, s.rows, s.width, 1, 0, 0);
+  } else {
+    reduce(2u, 2u, PROM_REDUCTION_TEMPORARY_ROW_MAX, row_bytes);
+    reduce(3u, 1u, PROM_REDUCTION_TEMPORARY_ROW_SUM, row_bytes);
+    const uint64_t total = static_cast<uint64_t>(s.rows) * s.width;
+    append(4u, (total + PROM_REDUCTION_LOCAL_SIZE - 1) / PROM_REDUCTION_LOCAL_SIZE, s.width, 1, 0, 0);
+    p->temporary_bytes = partial_bytes + 2u * row_bytes;
+  }
+
+  uint64_t h = 1469598103934665603ull;
+  h = fnv_u32(h, p->operation);
+  h = fnv_u32(h, p->row_count);
+  h = fnv_u32(h, p->elements_per_row);
+  h = fnv_u32(h, p->strategy);
+  h = fnv_u32(h, p->partial_count);
+  h = fnv_u32(h, p->stage_count);
+  for (uint32_t i = 0; i < p->stage_count; ++i) {
+    const PrometheusReductionStageDispatch& st = p->stages[i];
+    h = fnv_u32(h, st.stage_role);
+    h = fnv_u32(h, st.shader_id);
+    h = fnv_u32(h, st.implementation_id);
+    h = fnv_u32(h, st.groups_x);
+    h = fnv_u32(h, st.input_elements_per_row);
+    h = fnv_u32(h, st.output_partials_per_row);
+    h = fnv_u32(h, st.temporary_role);
+    h = fnv_u32(h, static_cast<uint32_t>(st.temporary_bytes_written));
+    h = fnv_u32(h, static_cast<uint32_t>(st.temporary_bytes_written >> 32u));
+  }
+  p->replay_id = h;
+}
+
+// Runs one reduction over host buffers; fills stage/detail/timing.
+int run_reduction_host(Runtime* rt, const float* in, float* out, uint32_t rows, uint32_t width, uint32_t op,
+                       uint32_t* stage, int32_t* detail, uint64_t* gpu_ns, uint32_t* gpu_valid,
+                       uint64_t* first_nonfinite) {
+  const uint64_t total = static_cast<uint64_t>(rows) * width;
+  const uint64_t out_count = (op == PROM_REDUCTION_OPERATION_SOFTMAX) ? total : rows;
+  if (rt->reduction_test_flags & PROM_REDUCTION_TESTCFG_FAIL_COMMAND_RECORD) {
+    *stage = PROM_STAGE_SUBMIT;
+    *detail = PROM_REDUCTION_DETAIL_COMMAND_RECORD_FAILED;
+    return PROM_ERROR;
+  }
+  if (rt->rin.ensure(total * 4, rt->stream) != cudaSuccess || rt->rout.ensure(out_count * 4, rt->stream) != cudaSuccess) {
+    *stage = PROM_STAGE_INIT;
+    *detail = PROM_REDUCTION_DETAIL_RESOURCE_CREATE_FAILED;
+    return PROM_ERROR;
+  }
+  float* din = static_cast<float*>(rt->rin.aligned());
+  float* dout = static_cast<float*>(rt->rout.aligned());
+  cudaError_t e = reset_words(rt);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(din, in, total * 4, cudaMemcpyHostToDevice, rt->stream);
+  if (e != cudaSuccess) {
+    *stage = PROM_STAGE_TRANSFER_IN;
+    *detail = PROM_REDUCTION_DETAIL_QUEUE_SUBMIT_FAILED;
+    return PROM_ERROR;
+  }
+  if (rt->reduction_test_flags & PROM_REDUCTION_TESTCFG_FAIL_QUEUE_SUBMIT) {
+    cudaStreamSynchronize(rt->stream);
+    *stage = PROM_STAGE_SUBMIT;
+    *detail = PROM_REDUCTION_DETAIL_QUEUE_SUBMIT_FAILED;
+    return PROM_ERROR;
+  }
+  cudaEventRecord(rt->ev0, rt->stream);
+  e = oct::row_reduce(din, dout, rows, width, op, rt->nonfinite_word(), rt->err_word(), rt->stream);
+  cudaEventRecord(rt->ev1, rt->stream);
+  Words w;
+  if (e != cudaSuccess || read_words(rt, &w) != cudaSuccess ||
+      (rt->reduction_test_flags & PROM_REDUCTION_TESTCFG_FAIL_COMPLETION_OBSERVATION) || w.err != 0) {
+    (void)cudaGetLastError();
+    *stage = PROM_STAGE_SUBMIT;
+    *detail = PROM_REDUCTION_DETAIL_COMPLETION_UNCERTAIN;
+    return PROM_ERROR;
+  }
+  if (w.nonfinite != ~0ull) {
+    *first_nonfinite = w.nonfinite;
+    *stage = PROM_STAGE_TRANSFER_IN;
+    *detail = PROM_REDUCTION_DETAIL_NONFINITE_INPUT;
+    return PROM_ERROR;  // output untouched: nothing was copied back
+  }
+  float ms = 0.f;
+  if (cudaEventElapsedTime(&ms, rt->ev0, rt->ev1) == cudaSuccess) {
+    *gpu_ns = static_cast<uint64_t>(static_cast<double>(ms) * 1.0e6);
+    *gpu_valid = 1;
+  }
+  e = cudaMemcpyAsync(out, dout, out_count * 4, cudaMemcpyDeviceToHost, rt->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
+  if (e != cudaSuccess) {
+    *stage = PROM_STAGE_TRANSFER_OUT;
+    *detail = PROM_REDUCTION_DETAIL_READBACK_FAILED;
+    return PROM_ERROR;
+  }
+  *stage = PROM_STAGE_NONE;
+  *detail = 0;
+  return PROM_OK;
+}
+
+bool finite_f(float v) { return std::isfinite(v); }
+
+}  // namespace
+
+namespace {
+AsyncTask* find_task(Runtime* rt, int id) {
+  for (auto& t : rt->tasks)
+    if (t.active && t.id == id) return &t;
+  return nullptr;
+}
+// Non-blocking completion check of a submitted task.
+void poll_task(Runtime* rt, AsyncTask* t) {
+  if (t->state != PROM_ASYNC_STATE_SUBMITTED) return;
+  if (rt->test_flags & PROM_TESTCFG_FAIL_ASYNC_POLL) {
+    t->state = PROM_ASYNC_STATE_FAILED;
+    t->final_detail = PROM_DETAIL_INJECTED_ASYNC_POLL_FAILURE;
+    t->final_stage = PROM_STAGE_SUBMIT;
+    return;
+  }
+  const cudaError_t q = cudaEventQuery(t->done);
+  if (q == cudaErrorNotReady) return;
+  if (q != cudaSuccess) {
+    (void)cudaGetLastError();
+    t->state = PROM_ASYNC_STATE_FAILED;
+    t->final_detail = PROM_DETAIL_ASYNC_FAILED;
+    return;
+  }
+  Words w;
+  if (read_words(rt, &w) != cudaSuccess || w.err != 0) {
+    t->state = PROM_ASYNC_STATE_FAILED;
+    t->final_detail = OCT_B200_DETAIL_DEVICE_TIMEOUT;
+    return;
+  }
+  t->state = PROM_ASYNC_STATE_READY;
+  t->final_stage = PROM_STAGE_TRANSFER_OUT;
+}
+uint32_t outstanding(Runtime* rt) {
+  uint32_t c = 0;
+  for (auto& t : rt->tasks)
+    if (t.active && t.state != PROM_ASYNC_STATE_CONSUMED) ++c;
+  return c;
+}
+}  // namespace
+
+namespace {
+// Shared body of the two Gemma RMSNorm entry points over host buffers.
+int gemma_rmsnorm(void* handle, const PrometheusGemma4E2BM1InputRmsNormRequest* r,
+                  PrometheusGemma4E2BM1InputRmsNormResult* out_result) {
+  if (out_result == nullptr) return PROM_ERROR;
+  PrometheusGemma4E2BM1InputRmsNormResult& out = *out_result;
+  const auto t0 = Clock::now();
+  std::memset(&out, 0, sizeof(out));
+  out.struct_size = sizeof(out);
+  out.stage = PROM_STAGE_INIT;
+  out.detail_code = PROM_M46_DETAIL_INVALID_REQUEST;
+  Runtime* rt = lookup(handle);
+  if (rt == nullptr) return PROM_INVALID_HANDLE;
+  if (r == nullptr || r->struct_size < sizeof(*r) || r->input == nullptr || r->weight == nullptr ||
+      r->output == nullptr)
+    return PROM_ERROR;
+  if (r->tokens == 0 || r->model_width == 0 || r->tokens > OCT_B200_REDUCTION_MAX_ROWS) {
+    out.detail_code = PROM_M46_DETAIL_SHAPE;
+    return PROM_ERROR;
+  }
+  const uint32_t stride = r->input_row_stride == 0 ? r->model_width : r->input_row_stride;
+  if (stride < r->model_width) {
+    out.detail_code = PROM_M46_DETAIL_STRIDE;
+    return PROM_ERROR;
+  }
+  if (!finite_f(r->epsilon) || r->epsilon <= 0.f) {
+    out.detail_code = PROM_M46_DETAIL_EPSILON;
+    return PROM_ERROR;
+  }
+  const uint64_t logical = static_cast<uint64_t>(r->tokens) * r->model_width;
+  const uint64_t storage = static_cast<uint64_t>(r->tokens - 1) * stride + r->model_width;
+  if (r->input_element_count < storage || r->weight_element_count != r->model_width ||
+      r->output_element_count != logical ||
+      (r->inv_rms_output != nullptr && r->inv_rms_output_element_count != r->tokens)) {
+    out.detail_code = PROM_M46_DETAIL_SHAPE;
+    return PROM_ERROR;
+  }
+  if (logical > OCT_B200_REDUCTION_MAX_TOTAL_ELEMENTS) {
+    out.detail_code = PROM_M46_DETAIL_SIZE_OVERFLOW;
+    return PROM_ERROR;
+  }
+  if (!rt->available) {
+    out.detail_code = PROM_M46_DETAIL_RESOURCE;
+    return PROM_ERROR;
+  }
+  std::lock_guard<std::mutex> lock(rt->mu);
+  if (rt->rin.ensure(storage * 4, rt->stream) != cudaSuccess || rt->rout.ensure(logical * 4, rt->stream) != cudaSuccess ||
+      rt->rw.ensure(static_cast<uint64_t>(r->model_width) * 4, rt->stream) != cudaSuccess ||
+      rt->rinv.ensure(static_cast<uint64_t>(r->tokens) * 4, rt->stream) != cudaSuccess) {
+    out.detail_code = PROM_M46_DETAIL_RESOURCE;
+    return PROM_ERROR;
+  }
+  float* din = static_cast<float*>(rt->rin.aligned());
+  float* dout = static_cast<float*>(rt->rout.aligned());
+  float* dw = static_cast<float*>(rt->rw.aligned());
+  float* dinv = static_cast<float*>(rt->rinv.aligned());
+  cudaError_t e = reset_words(rt);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(din, r->input, storage * 4, cudaMemcpyHostToDevice, rt->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(dw, r->weight, static_cast<uint64_t>(r->model_width) * 4, cudaMemcpyHostToDevice, rt->stream);
+  cudaEventRecord(rt->ev0, rt->stream);
+  if (e == cudaSuccess)
+    e = oct::rmsnorm(din, stride, dw, dout, dinv, r->tokens, r->model_width, r->epsilon, rt->nonfinite_word(),
+                     rt->err_word(), rt->stream);
+  cudaEventRecord(rt->ev1, rt->stream);
+  Words w;
+  if (e != cudaSuccess || read_words(rt, &w) != cudaSuccess || w.err != 0) {
+    (void)cudaGetLastError();
+    out.stage = PROM_STAGE_SUBMIT;
+    out.detail_code = PROM_M46_DETAIL_COMPLETION_UNCERTAIN;
+    return PROM_ERROR;
+  }
+  if (w.nonfinite != ~0ull) {
+    out.stage = PROM_STAGE_TRANSFER_IN;
+    out.detail_code = PROM_M46_DETAIL_NONFINITE_INPUT;
+    return PROM_ERROR;
+  }
+  float ms = 0.f;
+  if (cudaEventElapsedTime(&ms, rt->ev0, rt->ev1) == cudaSuccess) {
+    out.apply_gpu_ns = static_cast<uint64_t>(static_cast<double>(ms) * 1.0e6);
+  }
+  e = cudaMemcpyAsync(r->output, dout, logical * 4, cudaMemcpyDeviceToHost, rt->stream);
+  if (e == cudaSuccess && r->inv_rms_output != nullptr)
+    e = cudaMemcpyAsync(r->inv_rms_output, dinv, static_cast<uint64_t>(r->tokens) * 4, cudaMemcpyDeviceToHost,
+                        rt->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
+  if (e != cudaSuccess) {
+    out.stage = PROM_STAGE_TRANSFER_OUT;
+    out.detail_code = PROM_M46_DETAIL_COMPLETION_UNCERTAIN;
+    return PROM_ERROR;
+  }
+  out.stage = PROM_STAGE_NONE;
+  out.detail_code = 0;
+  out.output_written = 1;
+  out.matched_input = 1;
+  out.submit_count = 1;
+  out.final_readback_count = 1;
+  out.end_to_end_ns = ns_since(t0);
+  return PROM_OK;
+}
+}  // namespace
+
+// =========================================================================== ABI
+extern "C" {
+
+uint32_t prometheus_reactor_abi_version(void) { return PROM_REACTOR_ABI_V1; }
+
+int prometheus_reactor_runtime_create(void* config, void** out_handle) {
+  try {
+    if (out_handle == nullptr) return PROM_ERROR;
+    *out_handle = nullptr;
+    const PrometheusReactorConfig* cfg = static_cast<const PrometheusReactorConfig*>(config);
+    if (cfg != nullptr && cfg->struct_size < offsetof(PrometheusReactorConfig, test_flags) + sizeof(uint32_t))
+      return PROM_ERROR;
+    int status = PROM_OK;
+    Runtime* rt = create_runtime(cfg, &status);
+    if (rt == nullptr) return status;
+    {
+      std::lock_guard<std::mutex> lock(g_registry_mu);
+      g_registry->insert(rt);
+    }
+    *out_handle = rt;
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int prometheus_reactor_runtime_destroy(void* handle) {
+  try {
+    Runtime* rt = nullptr;
+    {
+      std::lock_guard<std::mutex> lock(g_registry_mu);
+      Runtime* cand = static_cast<Runtime*>(handle);
+      if (handle == nullptr || g_registry->count(cand) == 0) return PROM_INVALID_HANDLE;
+      g_registry->erase(cand);
+      rt = cand;
+    }
+    {
+      std::lock_guard<std::mutex> lock(rt->mu);  // callers must be quiescent; this only orders teardown
+    }
+    destroy_runtime(rt);
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int prometheus_reactor_runtime_probe(void* handle, PrometheusCaps* out_caps) {
+  if (out_caps == nullptr) return PROM_ERROR;
+  std::memset(out_caps, 0, sizeof(*out_caps));
+  Runtime* rt = lookup(handle);
+  if (rt == nullptr) return PROM_INVALID_HANDLE;
+  out_caps->available = rt->available ? 1u : 0u;
+  out_caps->backend_type = rt->available ? PROM_BACKEND_VULKAN : PROM_BACKEND_UNKNOWN;
+  out_caps->reason_code = rt->available ? PROM_REASON_NONE : rt->reason;
+  return PROM_OK;
+}
+
+int prometheus_runtime_create(void* config, void** out_handle) {
+  return prometheus_reactor_runtime_create(config, out_handle);
+}
+int prometheus_runtime_destroy(void* handle) { return prometheus_reactor_runtime_destroy(handle); }
+int prometheus_runtime_probe(void* handle, PrometheusCaps* out_caps) {
+  return prometheus_reactor_runtime_probe(handle, out_caps);
+}
+
+// Validation order and codes follow reactor_sgemm.cpp:4149-4176.
+int prometheus_reactor_runtime_sgemm(void* handle, const float* a, const float* b, float* c, uint32_t m, uint32_t n,
+                                     uint32_t k, uint32_t* out_stage, int* out_detail_code) {
+  try {
+    set_status(out_stage, out_detail_code, PROM_STAGE_NONE, 0);
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_INVALID_HANDLE);
+      return PROM_INVALID_HANDLE;
+    }
+    if (a == nullptr || b == nullptr || c == nullptr) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_IN, PROM_ERROR);
+      return PROM_ERROR;
+    }
+    if (m == 0 || n == 0 || k == 0) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_ERROR);
+      return PROM_ERROR;
+    }
+    if (!rt->available) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_DETAIL_CAPABILITY_MISMATCH);
+      return PROM_ERROR;
+    }
+    uint64_t a_n, b_n, c_n;
+    if (!checked_mul(m, k, &a_n) || !checked_mul(k, n, &b_n) || !checked_mul(m, n, &c_n) ||
+        a_n > (UINT64_MAX / 8) || b_n > (UINT64_MAX / 8) || c_n > (UINT64_MAX / 8)) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_IN, PROM_DETAIL_SIZE_OVERFLOW);
+      return PROM_ERROR;
+    }
+    std::lock_guard<std::mutex> lock(rt->mu);
+    set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_IN, 0);
+    if ((rt->test_flags & PROM_TESTCFG_FAIL_BUFFER_ALLOC) || rt->da.ensure(a_n * 4, rt->stream) != cudaSuccess ||
+        rt->db.ensure(b_n * 4, rt->stream) != cudaSuccess || rt->dc.ensure(c_n * 4, rt->stream) != cudaSuccess) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_IN, OCT_B200_DETAIL_OUT_OF_MEMORY);
+      return PROM_ERROR;
+    }
+    if (rt->test_flags & PROM_TESTCFG_FAIL_UPLOAD) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_IN, PROM_DETAIL_INJECTED_UPLOAD_FAILURE);
+      return PROM_ERROR;
+    }
+    float* da = static_cast<float*>(rt->da.aligned());
+    float* db = static_cast<float*>(rt->db.aligned());
+    float* dc = static_cast<float*>(rt->dc.aligned());
+    cudaError_t e = reset_words(rt);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(da, a, a_n * 4, cudaMemcpyHostToDevice, rt->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(db, b, b_n * 4, cudaMemcpyHostToDevice, rt->stream);
+    if (e != cudaSuccess) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_IN, OCT_B200_DETAIL_CUDA_ERROR);
+      return PROM_ERROR;
+    }
+    if (rt->test_flags & PROM_TESTCFG_FAIL_DISPATCH) {
+      cudaStreamSynchronize(rt->stream);
+      set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_DETAIL_INJECTED_DISPATCH_FAILURE);
+      return PROM_ERROR;
+    }
+    const uint32_t variant =
+        (rt->test_flags & PROM_TESTCFG_FORCE_STRICT_FP32) ? OCT_B200_SGEMM_FMA : OCT_B200_SGEMM_AUTO;
+    const int d = enqueue_sgemm(rt, da, k, db, n, dc, n, m, n, k, variant, rt->stream);
+    if (d != 0) {
+      cudaStreamSynchronize(rt->stream);
+      set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, d);
+      return PROM_ERROR;
+    }
+    if (rt->test_flags & PROM_TESTCFG_FAIL_DOWNLOAD) {
+      cudaStreamSynchronize(rt->stream);
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, PROM_DETAIL_INJECTED_DOWNLOAD_FAILURE);
+      return PROM_ERROR;
+    }
+    Words w;
+    if (read_words(rt, &w) != cudaSuccess) {
+      (void)cudaGetLastError();
+      set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, OCT_B200_DETAIL_CUDA_ERROR);
+      return PROM_ERROR;
+    }
+    if (w.err != 0) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, OCT_B200_DETAIL_DEVICE_TIMEOUT);
+      return PROM_ERROR;
+    }
+    e = cudaMemcpyAsync(c, dc, c_n * 4, cudaMemcpyDeviceToHost, rt->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
+    if (e != cudaSuccess) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, OCT_B200_DETAIL_CUDA_ERROR);
+      return PROM_ERROR;
+    }
+    set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, PROM_DETAIL_PATH_DIRECT);
+    return PROM_OK;
+  } catch (...) {
+    set_status(out_stage, out_detail_code, PROM_STAGE_INIT, OCT_B200_DETAIL_CUDA_ERROR);
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+// ---------------------------------------------------------------- async SGEMM
+// Lifecycle and codes follow reactor_sgemm.cpp:6298-6500: submit copies the
+// inputs into task-owned device memory and enqueues; query polls a CUDA event;
+// consume copies the result into the caller's buffer (length-checked); abandon
+// releases a finished task.  Capacity is four tasks.
+int prometheus_reactor_runtime_sgemm_submit_async(void* handle, const float* a, const float* b, uint32_t m,
+                                                  uint32_t n, uint32_t k, int* out_task_id, uint32_t* out_stage,
+                                                  int* out_detail_code) {
+  try {
+    if (out_task_id == nullptr) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_ERROR);
+      return PROM_ERROR;
+    }
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_INVALID_HANDLE);
+      return PROM_INVALID_HANDLE;
+    }
+    uint64_t a_n, b_n, c_n;
+    if (!rt->available || a == nullptr || b == nullptr || m == 0 || n == 0 || k == 0 || !checked_mul(m, k, &a_n) ||
+        !checked_mul(k, n, &b_n) || !checked_mul(m, n, &c_n) || c_n > UINT32_MAX) {
+      // c_len in consume is a uint32_t element count, so C must fit it.
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_ERROR);
+      return PROM_ERROR;
+    }
+    std::lock_guard<std::mutex> lock(rt->mu);
+    AsyncTask* task = nullptr;
+    for (auto& t : rt->tasks)
+      if (!t.active) {
+        task = &t;
+        break;
+      }
+    if (task == nullptr) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_DETAIL_ASYNC_QUEUE_FULL);
+      return PROM_ERROR;
+    }
+    if (task->done == nullptr && cudaEventCreateWithFlags(&task->done, cudaEventDisableTiming) != cudaSuccess) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_DETAIL_ASYNC_SUBMIT_REJECTED);
+      return PROM_ERROR;
+    }
+    if (task->a.ensure(a_n * 4, rt->stream) != cudaSuccess || task->b.ensure(b_n * 4, rt->stream) != cudaSuccess ||
+        task->c.ensure(c_n * 4, rt->stream) != cudaSuccess) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_IN, OCT_B200_DETAIL_OUT_OF_MEMORY);
+      return PROM_ERROR;
+    }
+    float* da = static_cast<float*>(task->a.aligned());
+    float* db = static_cast<float*>(task->b.aligned());
+    float* dc = static_cast<float*>(task->c.aligned());
+    cudaError_t e = reset_words(rt);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(da, a, a_n * 4, cudaMemcpyHostToDevice, rt->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(db, b, b_n * 4, cudaMemcpyHostToDevice, rt->stream);
+    // The caller may free a / b as soon as submit returns: wait for the copies.
+    if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
+    const uint32_t variant =
+        (rt->test_flags & PROM_TESTCFG_FORCE_STRICT_FP32) ? OCT_B200_SGEMM_FMA : OCT_B200_SGEMM_AUTO;
+    int d = (e == cudaSuccess) ? enqueue_sgemm(rt, da, k, db, n, dc, n, m, n, k, variant, rt->stream) : -1;
+    if (d == 0) e = cudaEventRecord(task->done, rt->stream);
+    if (e != cudaSuccess || d != 0) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_ERROR);
+      return PROM_ERROR;
+    }
+    task->active = true;
+    task->id = rt->next_task_id++;
+    if (rt->next_task_id <= 0) rt->next_task_id = 1;
+    task->state = PROM_ASYNC_STATE_SUBMITTED;
+    task->m = m;
+    task->n = n;
+    task->k = k;
+    task->final_detail = PROM_DETAIL_PATH_DIRECT;
+    task->final_stage = PROM_STAGE_SUBMIT;
+    *out_task_id = task->id;
+    set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, 0);
+    return PROM_OK;
+  } catch (...) {
+    set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_ERROR);
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+
+int prometheus_reactor_runtime_sgemm_query_async(void* handle, int task_id, PrometheusAsyncStatus* out_status) {
+  try {
+    if (out_status == nullptr) return PROM_ERROR;
+    std::memset(out_status, 0, sizeof(*out_status));
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    AsyncTask* t = find_task(rt, task_id);
+    if (t == nullptr) {
+      out_status->lifecycle_state = PROM_ASYNC_STATE_IDLE;
+      out_status->detail_code = PROM_DETAIL_ASYNC_NO_TASK;
+      return PROM_ERROR;
+    }
+    poll_task(rt, t);
+    out_status->lifecycle_state = t->state;
+    out_status->stage = t->final_stage == 0 ? PROM_STAGE_SUBMIT : t->final_stage;
+    out_status->detail_code = t->state == PROM_ASYNC_STATE_SUBMITTED ? PROM_DETAIL_ASYNC_NOT_READY : t->final_detail;
+    out_status->ready = t->state == PROM_ASYNC_STATE_READY;
+    out_status->failed = t->state == PROM_ASYNC_STATE_FAILED;
+    out_status->consumed = t->state == PROM_ASYNC_STATE_CONSUMED;
+    out_status->outstanding_tasks = outstanding(rt);
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int prometheus_reactor_runtime_sgemm_consume_async(void* handle, int task_id, float* c, uint32_t c_len,
+                                                   uint32_t* out_stage, int* out_detail_code) {
+  try {
+    set_status(out_stage, out_detail_code, PROM_STAGE_NONE, 0);
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_INVALID_HANDLE);
+      return PROM_INVALID_HANDLE;
+    }
+    std::lock_guard<std::mutex> lock(rt->mu);
+    AsyncTask* t = find_task(rt, task_id);
+    if (t == nullptr) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_DETAIL_ASYNC_INVALID_TASK);
+      return PROM_ERROR;
+    }
+    poll_task(rt, t);
+    if (t->state == PROM_ASYNC_STATE_SUBMITTED) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_DETAIL_ASYNC_NOT_READY);
+      return PROM_ERROR;
+    }
+    if (t->state == PROM_ASYNC_STATE_FAILED) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT,
+                 t->final_detail != 0 ? t->final_detail : PROM_DETAIL_ASYNC_FAILED);
+      return PROM_ERROR;
+    }
+    if (t->state == PROM_ASYNC_STATE_CONSUMED) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, PROM_DETAIL_ASYNC_ALREADY_CONSUMED);
+      return PROM_ERROR;
+    }
+    const uint64_t need = static_cast<uint64_t>(t->m) * t->n;
+    if (c == nullptr || c_len < need) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, PROM_ERROR);
+      return PROM_ERROR;
+    }
+    cudaError_t e = cudaMemcpyAsync(c, t->c.aligned(), need * 4, cudaMemcpyDeviceToHost, rt->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
+    if (e != cudaSuccess) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, OCT_B200_DETAIL_CUDA_ERROR);
+      return PROM_ERROR;
+    }
+    t->state = PROM_ASYNC_STATE_CONSUMED;
+    set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, t->final_detail);
+    return PROM_OK;
+  } catch (...) {
+    set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, OCT_B200_DETAIL_CUDA_ERROR);
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int prometheus_reactor_runtime_sgemm_abandon_async(void* handle, int task_id) {
+  try {
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    AsyncTask* t = find_task(rt, task_id);
+    if (t == nullptr) return PROM_ERROR;
+    poll_task(rt, t);
+    if (t->state == PROM_ASYNC_STATE_SUBMITTED) return PROM_ERROR;  // unconsumed work still in flight
+    t->active = false;
+    t->state = PROM_ASYNC_STATE_IDLE;
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+// ---------------------------------------------------------------- reductions
+int prometheus_reactor_reduction_plan(const PrometheusReductionRequest* request, PrometheusReductionPlan* out_plan) {
+  try {
+    if (out_plan == nullptr) return PROM_ERROR;
+    std::memset(out_plan, 0, sizeof(*out_plan));
+    out_plan->struct_size = sizeof(*out_plan);
+    if (request == nullptr || request->struct_size < sizeof(*request)) return PROM_ERROR;
+    if (validate_shape(shape_of(request)) != 0) return PROM_ERROR;
+    build_plan(shape_of(request), out_plan);
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+// Validation order follows reactor_concept_reduction.cpp:55-100.
+int prometheus_reactor_runtime_reduction(void* handle, const PrometheusReductionRequest* request,
+                                         PrometheusReductionExecutionResult* out_result) {
+  PrometheusReductionExecutionResult local{};
+  PrometheusReductionExecutionResult& out = out_result != nullptr ? *out_result : local;
+  try {
+    const auto t0 = Clock::now();
+    std::memset(&out, 0, sizeof(out));
+    out.struct_size = sizeof(out);
+    out.physical_slot_id = UINT32_MAX;
+    out.first_nonfinite_index = UINT64_MAX;
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) {
+      out.stage = PROM_STAGE_INIT;
+      out.detail_code = PROM_REDUCTION_DETAIL_RUNTIME_UNAVAILABLE;
+      return PROM_INVALID_HANDLE;
+    }
+    out.stage = PROM_STAGE_INIT;
+    out.detail_code = PROM_REDUCTION_DETAIL_INVALID_REQUEST;
+    if (request == nullptr || request->struct_size < sizeof(*request)) return PROM_ERROR;
+    if (request->input == nullptr) {
+      out.detail_code = PROM_REDUCTION_DETAIL_NULL_INPUT;
+      return PROM_ERROR;
+    }
+    if (request->output == nullptr) {
+      out.detail_code = PROM_REDUCTION_DETAIL_NULL_OUTPUT;
+      return PROM_ERROR;
+    }
+    const ReductionShape s = shape_of(request);
+    const int v = validate_shape(s);
+    if (v != 0) {
+      out.detail_code = v;
+      return PROM_ERROR;
+    }
+    build_plan(s, &out.plan);
+    if (!rt->available) {
+      out.detail_code = PROM_REDUCTION_DETAIL_RUNTIME_UNAVAILABLE;
+      return PROM_ERROR;
+    }
+    std::lock_guard<std::mutex> lock(rt->mu);
+    out.logical_request_id = rt->next_request_id++;
+    out.physical_slot_id = 0;
+    out.physical_slot_recyclable = 1;
+    uint32_t stage = 0;
+    int32_t detail = 0;
+    const int rc = run_reduction_host(rt, request->input, request->output, s.rows, s.width, s.operation, &stage,
+                                      &detail, &out.gpu_duration_ns, &out.gpu_timestamp_valid,
+                                      &out.first_nonfinite_index);
+    out.stage = stage;
+    out.detail_code = detail;
+    out.end_to_end_ns = ns_since(t0);
+    return rc;
+  } catch (...) {
+    out.stage = PROM_STAGE_INIT;
+    out.detail_code = PROM_REDUCTION_DETAIL_RESOURCE_CREATE_FAILED;
+    return PROM_ERROR;
+  }
+}
+
+// Validation order and codes follow reactor_vulkan_fused_reduction.c:892-994.
+// The row / total ceilings are widened to the library's reduction envelope.
+int prometheus_reactor_runtime_row_wise_softmax(void* handle, const PrometheusRowWiseSoftmaxRequest* request,
+                                                PrometheusRowWiseSoftmaxResult* out_result) {
+  PrometheusRowWiseSoftmaxResult local{};
+  PrometheusRowWiseSoftmaxResult& out = out_result != nullptr ? *out_result : local;
+  try {
+    const auto t0 = Clock::now();
+    std::memset(&out, 0, sizeof(out));
+    out.struct_size = sizeof(out);
+    out.first_nonfinite_index = UINT64_MAX;
+    auto fail = [&](uint32_t stage, int32_t detail, int rc) {
+      out.stage = stage;
+      out.detail_code = detail;
+      out.output_written = 0;
+      return rc;
+    };
+    if (request == nullptr || request->struct_size < sizeof(*request))
+      return fail(PROM_STAGE_INIT, PROM_SOFTMAX_DETAIL_INVALID_REQUEST, PROM_ERROR);
+    const uint64_t total = static_cast<uint64_t>(request->row_count) * request->elements_per_row;
+    if (request->input_element_count != total || request->output_element_count != total)
+      return fail(PROM_STAGE_INIT, PROM_SOFTMAX_DETAIL_COUNT_MISMATCH, PROM_ERROR);
+    if (total == 0) {
+      out.stage = PROM_STAGE_NONE;
+      out.detail_code = 0;
+      return PROM_OK;
+    }
+    if (request->input == nullptr) return fail(PROM_STAGE_INIT, PROM_SOFTMAX_DETAIL_NULL_INPUT, PROM_ERROR);
+    if (request->output == nullptr) return fail(PROM_STAGE_INIT, PROM_SOFTMAX_DETAIL_NULL_OUTPUT, PROM_ERROR);
+    if (request->row_count > OCT_B200_REDUCTION_MAX_ROWS)
+      return fail(PROM_STAGE_INIT, PROM_SOFTMAX_DETAIL_ROW_LIMIT, PROM_ERROR);
+    if (request->elements_per_row > PROM_ROW_WISE_SOFTMAX_MAX_ELEMENTS_PER_ROW)
+      return fail(PROM_STAGE_INIT, PROM_SOFTMAX_DETAIL_WIDTH_LIMIT, PROM_ERROR);
+    if (total > OCT_B200_REDUCTION_MAX_TOTAL_ELEMENTS)
+      return fail(PROM_STAGE_INIT, PROM_SOFTMAX_DETAIL_ELEMENT_LIMIT, PROM_ERROR);
+    {
+      const uintptr_t ib = reinterpret_cast<uintptr_t>(request->input);
+      const uintptr_t ob = reinterpret_cast<uintptr_t>(request->output);
+      const uint64_t bytes = total * sizeof(float);
+      if (ib != ob && ib < ob + bytes && ob < ib + bytes)
+        return fail(PROM_STAGE_INIT, PROM_SOFTMAX_DETAIL_PARTIAL_ALIAS, PROM_ERROR);
+    }
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return fail(PROM_STAGE_INIT, PROM_SOFTMAX_DETAIL_RUNTIME_UNAVAILABLE, PROM_INVALID_HANDLE);
+    if (!rt->available) return fail(PROM_STAGE_INIT, PROM_SOFTMAX_DETAIL_RUNTIME_UNAVAILABLE, PROM_ERROR);
+    std::lock_guard<std::mutex> lock(rt->mu);
+    uint32_t stage = 0;
+    int32_t detail = 0;
+    const int rc = run_reduction_host(rt, request->input, request->output, request->row_count,
+                                      request->elements_per_row, PROM_REDUCTION_OPERATION_SOFTMAX, &stage, &detail,
+                                      &out.gpu_duration_ns, &out.gpu_timestamp_valid, &out.first_nonfinite_index);
+    out.end_to_end_ns = ns_since(t0);
+    if (rc != PROM_OK) {
+      const int32_t d = detail == PROM_REDUCTION_DETAIL_NONFINITE_INPUT ? PROM_SOFTMAX_DETAIL_NONFINITE_INPUT : detail;
+      return fail(stage, d, rc);
+    }
+    out.stage = PROM_STAGE_NONE;
+    out.detail_code = 0;
+    out.physical_dispatch_count = 1;
+    out.physical_submission_count = 1;
+    out.output_written = 1;
+    return PROM_OK;
+  } catch (...) {
+    out.stage = PROM_STAGE_INIT;
+    out.detail_code = PROM_SOFTMAX_DETAIL_RUNTIME_UNAVAILABLE;
+    return PROM_ERROR;
+  }
+}
+
+
+int prometheus_reactor_runtime_gemma4e2b_m1_input_rmsnorm(void* handle,
+                                                          const PrometheusGemma4E2BM1InputRmsNormRequest* request,
+                                                          PrometheusGemma4E2BM1InputRmsNormResult* out_result) {
+  try {
+    return gemma_rmsnorm(handle, request, out_result);
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm(void* handle,
+                                                         const PrometheusGemma4E2BM1HeadRmsNormRequest* request,
+                                                         PrometheusGemma4E2BM1HeadRmsNormResult* out_result) {
+  try {
+    return gemma_rmsnorm(handle, request, out_result);
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+// ---------------------------------------------------------------- device extensions
+int oct_b200_sgemm_device_ld(void* handle, const float* d_a, uint64_t lda, const float* d_b, uint64_t ldb, float* d_c,
+                             uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, uint32_t variant, void* stream,
+                             int* out_detail_code) {
+  try {
+    if (out_detail_code) *out_detail_code = 0;
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    if (d_a == nullptr || d_b == nullptr || d_c == nullptr || lda < k || ldb < n || ldc < n) {
+      if (out_detail_code) *out_detail_code = PROM_ERROR;
+      return PROM_ERROR;
+    }
+    if (!rt->available) {
+      if (out_detail_code) *out_detail_code = PROM_DETAIL_CAPABILITY_MISMATCH;
+      return PROM_ERROR;
+    }
+    if (m == 0 || n == 0 || k == 0) return PROM_OK;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    cudaStream_t s = stream != nullptr ? static_cast<cudaStream_t>(stream) : rt->stream;
+    const int d = enqueue_sgemm(rt, d_a, lda, d_b, ldb, d_c, ldc, m, n, k, variant, s);
+    if (d != 0) {
+      if (out_detail_code) *out_detail_code = d;
+      return PROM_ERROR;
+    }
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int oct_b200_sgemm_device(void* handle, const float* d_a, const float* d_b, float* d_c, uint32_t m, uint32_t n,
+                          uint32_t k, uint32_t variant, void* stream, int* out_detail_code) {
+  return oct_b200_sgemm_device_ld(handle, d_a, k, d_b, n, d_c, n, m, n, k, variant, stream, out_detail_code);
+}
+
+int oct_b200_reduction_device(void* handle, const float* d_in, float* d_out, uint32_t rows, uint32_t width,
+                              uint32_t operation, void* stream, int* out_detail_code) {
+  try {
+    if (out_detail_code) *out_detail_code = 0;
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    if (d_in == nullptr || d_out == nullptr || operation < 1 || operation > 3) {
+      if (out_detail_code) *out_detail_code = PROM_REDUCTION_DETAIL_INVALID_REQUEST;
+      return PROM_ERROR;
+    }
+    if (!rt->available) {
+      if (out_detail_code) *out_detail_code = PROM_REDUCTION_DETAIL_RUNTIME_UNAVAILABLE;
+      return PROM_ERROR;
+    }
+    std::lock_guard<std::mutex> lock(rt->mu);
+    cudaStream_t s = stream != nullptr ? static_cast<cudaStream_t>(stream) : rt->stream;
+    const cudaError_t e = oct::row_reduce(d_in, d_out, rows, width, operation, rt->nonfinite_word(), rt->err_word(), s);
+    if (e != cudaSuccess) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
+      return PROM_ERROR;
+    }
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int oct_b200_rmsnorm_device(void* handle, const float* d_in, const float* d_weight, float* d_out, float* d_inv_rms,
+                            uint32_t rows, uint32_t width, float epsilon, void* stream, int* out_detail_code) {
+  try {
+    if (out_detail_code) *out_detail_code = 0;
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    if (d_in == nullptr || d_weight == nullptr || d_out == nullptr || !finite_f(epsilon) || epsilon <= 0.f) {
+      if (out_detail_code) *out_detail_code = PROM_M46_DETAIL_INVALID_REQUEST;
+      return PROM_ERROR;
+    }
+    if (!rt->available) {
+      if (out_detail_code) *out_detail_code = PROM_M46_DETAIL_RESOURCE;
+      return PROM_ERROR;
+    }
+    std::lock_guard<std::mutex> lock(rt->mu);
+    cudaStream_t s = stream != nullptr ? static_cast<cudaStream_t>(stream) : rt->stream;
+    const cudaError_t e = oct::rmsnorm(d_in, width, d_weight, d_out, d_inv_rms, rows, width, epsilon,
+                                       rt->nonfinite_word(), rt->err_word(), s);
+    if (e != cudaSuccess) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
+      return PROM_ERROR;
+    }
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int oct_b200_sync_status(void* handle, void* stream, int* out_detail_code) {
+  try {
+    if (out_detail_code) *out_detail_code = 0;
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    if (!rt->available) return PROM_ERROR;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    if (stream != nullptr && cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
+      return PROM_ERROR;
+    }
+    Words w;
+    if (read_words(rt, &w) != cudaSuccess) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
+      return PROM_ERROR;
+    }
+    if (reset_words(rt) != cudaSuccess || cudaStreamSynchronize(rt->stream) != cudaSuccess) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
+      return PROM_ERROR;
+    }
+    if (w.err != 0) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_DEVICE_TIMEOUT;
+      return PROM_ERROR;
+    }
+    if (w.nonfinite != ~0ull) {
+      if (out_detail_code) *out_detail_code = PROM_REDUCTION_DETAIL_NONFINITE_INPUT;
+      return PROM_ERROR;
+    }
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int oct_b200_set_kernel_timing(void* handle, int enable) {
+  Runtime* rt = lookup(handle);
+  if (rt == nullptr) return PROM_INVALID_HANDLE;
+  std::lock_guard<std::mutex> lock(rt->mu);
+  rt->timing = enable != 0;
+  rt->timing_used = 0;
+  return PROM_OK;
+}
+
+int oct_b200_read_kernel_timing(void* handle, double* split_ms_total, double* main_ms_total, uint32_t* launches) {
+  try {
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    double split = 0.0, main = 0.0;
+    for (size_t i = 0; i < rt->timing_used; ++i) {
+      const oct::SgemmEvents& ev = rt->timing_events[i];
+      if (cudaEventSynchronize(ev.main_end) != cudaSuccess) return PROM_ERROR;
+      float a = 0.f, b = 0.f;
+      if (cudaEventElapsedTime(&a, ev.split_begin, ev.main_begin) != cudaSuccess ||
+          cudaEventElapsedTime(&b, ev.main_begin, ev.main_end) != cudaSuccess)
+        return PROM_ERROR;
+      split += a;
+      main += b;
+    }
+    if (split_ms_total) *split_ms_total = split;
+    if (main_ms_total) *main_ms_total = main;
+    if (launches) *launches = static_cast<uint32_t>(rt->timing_used);
+    rt->timing_used = 0;
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+const char* oct_b200_build_info(void) {
+  return "oct_b200 prometheus reactor (ABI v1) sm_100a: tcgen05 3xTF32 SGEMM, FP32-FMA SGEMM, bulk-fed reductions";
+}
+
+}  // extern "C"

@@ -1,0 +1,396 @@
+// reduce.cu -- fused row reductions and RMSNorm over fp32 rows.
+//
+// Operations (Oct's reduction ABI, internal/prometheus/native/reactor_api.h:377-381):
+//   SUM      out[r] = sum_c x[r, c]
+//   MAX      out[r] = max_c x[r, c]
+//   SOFTMAX  out[r, c] = exp(x[r, c] - max_r) / sum_c exp(x[r, c] - max_r)
+// and RMSNorm  out[r, c] = x[r, c] * (1 / sqrt(mean_c x[r, c]^2 + eps)) * w[c]
+// (internal/prometheus/zimage/canonical_contract.go:91-105).
+//
+// Numerics follow the fp64 CPU reference `prom_reduction_cpu_reference`
+// (internal/prometheus/native/reactor_vulkan_fused_reduction.c:996-1036): sums
+// (of x, of exp, of x^2) accumulate in double, max is exact, the softmax
+// quotient is formed in double and rounded once.  exp itself is CUDA's fp32
+// `expf` (a few ulp), well inside the tolerance.
+//
+// Data movement: each CTA streams batches of rows HBM -> shared memory with
+// `cp.async.bulk` (the TMA engine's untiled copy) into a ring of NS slots, one
+// mbarrier per slot, so several batches are in flight while the current one is
+// reduced out of shared memory.  A row is read from HBM exactly once; softmax
+// and RMSNorm take all their passes over the shared-memory copy.
+//   W <= 1024 : a warp owns a row (8 rows per batch), warp-shuffle reductions.
+//   W <= 8192 : the whole 256-thread CTA owns a row, shuffle + shared reduction.
+// Rows whose address or width is not 16-byte granular (or wider than 8192)
+// take a plain-load fallback kernel with the same arithmetic.
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cstdint>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace oct {
+namespace {
+
+constexpr int THREADS = 256;
+constexpr uint32_t SLOT_BUDGET_BYTES = 64 * 1024;  // ring size per CTA
+constexpr uint32_t BULK_MAX_WIDTH = 8192;
+
+enum Op : int { kSum = 1, kMax = 2, kSoftmax = 3, kRms = 4 };
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Row-group reduction: TPR == 32 -> warp only; TPR == 256 -> whole CTA.
+template <int TPR>
+__device__ __forceinline__ double group_sum_d(double v, double* scratch) {
+  v = warp_sum_d(v);
+  if constexpr (TPR == 32) {
+    return v;
+  } else {
+    const int w = threadIdx.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) scratch[w] = v;
+    __syncthreads();
+    double t = 0.0;
+#pragma unroll
+    for (int i = 0; i < THREADS / 32; ++i) t += scratch[i];
+    return t;
+  }
+}
+template <int TPR>
+__device__ __forceinline__ float group_max_f(float v, float* scratch) {
+  v = warp_max_f(v);
+  if constexpr (TPR == 32) {
+    return v;
+  } else {
+    const int w = threadIdx.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) scratch[w] = v;
+    __syncthreads();
+    float t = scratch[0];
+#pragma unroll
+    for (int i = 1; i < THREADS / 32; ++i) t = fmaxf(t, scratch[i]);
+    return t;
+  }
+}
+
+__device__ __forceinline__ void note_nonfinite(float v, uint64_t flat, uint64_t& first) {
+  if (!isfinite(v) && flat < first) first = flat;
+}
+
+// Processes one row held in shared memory.  `lane` / TPR index the threads of
+// the row group; out_row points at this row's output (softmax / RMSNorm) or
+// at out[r] (sum / max).
+template <int OP, int TPR>
+__device__ __forceinline__ float process_row(float* srow, uint32_t w, uint32_t lane, uint64_t row,
+                                            float* __restrict__ out, const float* __restrict__ weight, float eps,
+                                            double* dscratch, float* fscratch, uint64_t& first_bad) {
+  const uint32_t nv = w / 4;
+  float4* v4 = reinterpret_cast<float4*>(srow);
+  if constexpr (OP == kSum) {
+    double s = 0.0;
+    for (uint32_t i = lane; i < nv; i += TPR) {
+      const float4 x = v4[i];
+      s += static_cast<double>(x.x); s += static_cast<double>(x.y);
+      s += static_cast<double>(x.z); s += static_cast<double>(x.w);
+      if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
+        note_nonfinite(x.x, row * w + 4 * i, first_bad); note_nonfinite(x.y, row * w + 4 * i + 1, first_bad);
+        note_nonfinite(x.z, row * w + 4 * i + 2, first_bad); note_nonfinite(x.w, row * w + 4 * i + 3, first_bad);
+      }
+    }
+    s = group_sum_d<TPR>(s, dscratch);
+    if (lane == 0) out[row] = static_cast<float>(s);
+    return 0.f;
+  } else if constexpr (OP == kMax) {
+    float mx = -FLT_MAX;
+    for (uint32_t i = lane; i < nv; i += TPR) {
+      const float4 x = v4[i];
+      mx = fmaxf(mx, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
+      if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
+        note_nonfinite(x.x, row * w + 4 * i, first_bad); note_nonfinite(x.y, row * w + 4 * i + 1, first_bad);
+        note_nonfinite(x.z, row * w + 4 * i + 2, first_bad); note_nonfinite(x.w, row * w + 4 * i + 3, first_bad);
+      }
+    }
+    mx = group_max_f<TPR>(mx, fscratch);
+    if (lane == 0) out[row] = mx;
+    return 0.f;
+  } else if constexpr (OP == kSoftmax) {
+    float mx = -FLT_MAX;
+    for (uint32_t i = lane; i < nv; i += TPR) {
+      const float4 x = v4[i];
+      mx = fmaxf(mx, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
+      if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
+        note_nonfinite(x.x, row * w + 4 * i, first_bad); note_nonfinite(x.y, row * w + 4 * i + 1, first_bad);
+        note_nonfinite(x.z, row * w + 4 * i + 2, first_bad); note_nonfinite(x.w, row * w + 4 * i + 3, first_bad);
+      }
+    }
+    mx = group_max_f<TPR>(mx, fscratch);
+    double s = 0.0;
+    for (uint32_t i = lane; i < nv; i += TPR) {
+      float4 x = v4[i];
+      x.x = expf(x.x - mx); x.y = expf(x.y - mx); x.z = expf(x.z - mx); x.w = expf(x.w - mx);
+      s += static_cast<double>(x.x); s += static_cast<double>(x.y);
+      s += static_cast<double>(x.z); s += static_cast<double>(x.w);
+      v4[i] = x;  // keep exp(x - max) for the normalising pass
+    }
+    s = group_sum_d<TPR>(s, dscratch);
+    const double inv = 1.0 / s;
+    float4* o4 = reinterpret_cast<float4*>(out + row * w);
+    for (uint32_t i = lane; i < nv; i += TPR) {
+      const float4 e = v4[i];
+      __stcs(o4 + i, make_float4(static_cast<float>(e.x * inv), static_cast<float>(e.y * inv),
+                                 static_cast<float>(e.z * inv), static_cast<float>(e.w * inv)));
+    }
+    return 0.f;
+  } else {  // kRms
+    double ss = 0.0;
+    for (uint32_t i = lane; i < nv; i += TPR) {
+      const float4 x = v4[i];
+      ss += static_cast<double>(x.x) * x.x; ss += static_cast<double>(x.y) * x.y;
+      ss += static_cast<double>(x.z) * x.z; ss += static_cast<double>(x.w) * x.w;
+      if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
+        note_nonfinite(x.x, row * w + 4 * i, first_bad); note_nonfinite(x.y, row * w + 4 * i + 1, first_bad);
+        note_nonfinite(x.z, row * w + 4 * i + 2, first_bad); note_nonfinite(x.w, row * w + 4 * i + 3, first_bad);
+      }
+    }
+    ss = group_sum_d<TPR>(ss, dscratch);
+    const float inv = static_cast<float>(1.0 / sqrt(ss / static_cast<double>(w) + static_cast<double>(eps)));
+    float4* o4 = reinterpret_cast<float4*>(out + row * w);
+    const float4* w4 = reinterpret_cast<const float4*>(weight);
+    for (uint32_t i = lane; i < nv; i += TPR) {
+      const float4 x = v4[i];
+      const float4 g = __ldg(w4 + i);
+      __stcs(o4 + i, make_float4(x.x * inv * g.x, x.y * inv * g.y, x.z * inv * g.z, x.w * inv * g.w));
+    }
+    return inv;
+  }
+}
+
+// Bulk-fed kernel.  TPR threads per row; rows_per_batch = THREADS / TPR.
+// Rows are `stride` floats apart; when stride == w a batch is one contiguous copy.
+template <int OP, int TPR>
+__global__ void __launch_bounds__(THREADS) row_bulk_kernel(const float* __restrict__ in, uint64_t stride,
+                                                           float* __restrict__ out, float* __restrict__ inv_rms,
+                                                           const float* __restrict__ weight, float eps,
+                                                           uint32_t rows, uint32_t w, uint32_t ns,
+                                                           unsigned long long* __restrict__ nonfinite,
+                                                           unsigned int* __restrict__ err) {
+  constexpr uint32_t RPB = THREADS / TPR;  // rows per batch
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  float* ring = reinterpret_cast<float*>(smem_raw);
+  __shared__ __align__(8) uint64_t bars[8];
+  __shared__ double dscratch[RPB][THREADS / 32];
+  __shared__ float fscratch[RPB][THREADS / 32];
+  __shared__ uint32_t abort_flag;
+
+  const uint32_t batch_floats = RPB * w;
+  const uint32_t num_batches = (rows + RPB - 1) / RPB;
+  const bool contiguous = (stride == w);
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < ns; ++s) mbar_init(&bars[s], 1);
+    abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  __syncthreads();
+
+  auto issue = [&](uint32_t batch, uint32_t slot) {
+    const uint32_t r0 = batch * RPB;
+    const uint32_t nr = min(RPB, rows - r0);
+    float* dst = ring + slot * batch_floats;
+    mbar_arrive_expect_tx(&bars[slot], nr * w * 4u);
+    if (contiguous) {
+      bulk_load(dst, in + static_cast<uint64_t>(r0) * w, nr * w * 4u, &bars[slot]);
+    } else {
+      for (uint32_t i = 0; i < nr; ++i)
+        bulk_load(dst + i * w, in + static_cast<uint64_t>(r0 + i) * stride, w * 4u, &bars[slot]);
+    }
+  };
+
+  // Prologue: fill the ring with this CTA's first `ns` batches.  Thread 0
+  // counts copies issued per slot so an aborted CTA can drain them.
+  uint32_t issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < ns; ++s) {
+      const uint32_t b = blockIdx.x + s * gridDim.x;
+      if (b >= num_batches) break;
+      issue(b, s);
+      issued[s] += 1;
+    }
+  }
+
+  uint64_t first_bad = ~0ull;
+  const uint32_t grp = threadIdx.x / TPR, lane = threadIdx.x % TPR;
+  for (uint32_t j = 0;; ++j) {
+    const uint32_t b = blockIdx.x + j * gridDim.x;
+    if (b >= num_batches) break;
+    const uint32_t slot = j % ns;
+    const bool ok = mbar_wait(&bars[slot], (j / ns) & 1u, err, kErrWaitRow);
+    if (!ok) abort_flag = 1;
+    __syncthreads();
+    if (abort_flag) break;
+    const uint32_t r = b * RPB + grp;
+    if (r < rows) {
+      float* srow = ring + slot * batch_floats + grp * w;
+      const float inv = process_row<OP, TPR>(srow, w, lane, r, out, weight, eps, dscratch[grp], fscratch[grp],
+                                             first_bad);
+      if constexpr (OP == kRms) {
+        if (lane == 0 && inv_rms != nullptr) inv_rms[r] = inv;
+      }
+    }
+    __syncthreads();  // every thread is done with this slot
+    if (threadIdx.x == 0) {
+      const uint32_t nb = blockIdx.x + (j + ns) * gridDim.x;
+      if (nb < num_batches) {
+        fence_proxy_async_smem();
+        issue(nb, slot);
+        issued[slot] += 1;
+      }
+    }
+  }
+  if (first_bad != ~0ull) atomicMin(nonfinite, static_cast<unsigned long long>(first_bad));
+  // On abort, wait (bounded) for the newest copy issued into each slot: a
+  // slot's phases complete in order, so that drains everything in flight.
+  if (abort_flag && threadIdx.x == 0) {
+    for (uint32_t s = 0; s < ns; ++s)
+      if (issued[s] > 0 && !mbar_wait(&bars[s], (issued[s] - 1) & 1u, err, kErrWaitDrain)) break;
+  }
+}
+
+// Plain-load fallback: one CTA per row, any width / alignment.  Same arithmetic.
+template <int OP>
+__global__ void __launch_bounds__(THREADS) row_plain_kernel(const float* __restrict__ in, uint64_t stride,
+                                                            float* __restrict__ out, float* __restrict__ inv_rms,
+                                                            const float* __restrict__ weight, float eps,
+                                                            uint32_t rows, uint32_t w,
+                                                            unsigned long long* __restrict__ nonfinite) {
+  __shared__ double dscr[THREADS / 32];
+  __shared__ float fscr[THREADS / 32];
+  uint64_t first_bad = ~0ull;
+  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* x = in + static_cast<uint64_t>(r) * stride;
+    if constexpr (OP == kSum) {
+      double s = 0.0;
+      for (uint32_t c = threadIdx.x; c < w; c += THREADS) {
+        const float v = __ldg(x + c);
+        s += static_cast<double>(v);
+        note_nonfinite(v, static_cast<uint64_t>(r) * w + c, first_bad);
+      }
+      s = group_sum_d<THREADS>(s, dscr);
+      if (threadIdx.x == 0) out[r] = static_cast<float>(s);
+    } else if constexpr (OP == kMax) {
+      float mx = -FLT_MAX;
+      for (uint32_t c = threadIdx.x; c < w; c += THREADS) {
+        const float v = __ldg(x + c);
+        mx = fmaxf(mx, v);
+        note_nonfinite(v, static_cast<uint64_t>(r) * w + c, first_bad);
+      }
+      mx = group_max_f<THREADS>(mx, fscr);
+      if (threadIdx.x == 0) out[r] = mx;
+    } else if constexpr (OP == kSoftmax) {
+      float mx = -FLT_MAX;
+      for (uint32_t c = threadIdx.x; c < w; c += THREADS) {
+        const float v = __ldg(x + c);
+        mx = fmaxf(mx, v);
+        note_nonfinite(v, static_cast<uint64_t>(r) * w + c, first_bad);
+      }
+      mx = group_max_f<THREADS>(mx, fscr);
+      double s = 0.0;
+      for (uint32_t c = threadIdx.x; c < w; c += THREADS) s += static_cast<double>(expf(__ldg(x + c) - mx));
+      s = group_sum_d<THREADS>(s, dscr);
+      const double inv = 1.0 / s;
+      for (uint32_t c = threadIdx.x; c < w; c += THREADS)
+        out[static_cast<uint64_t>(r) * w + c] = static_cast<float>(static_cast<double>(expf(__ldg(x + c) - mx)) * inv);
+    } else {
+      double ss = 0.0;
+      for (uint32_t c = threadIdx.x; c < w; c += THREADS) {
+        const float v = __ldg(x + c);
+        ss += static_cast<double>(v) * v;
+        note_nonfinite(v, static_cast<uint64_t>(r) * w + c, first_bad);
+      }
+      ss = group_sum_d<THREADS>(ss, dscr);
+      const float inv = static_cast<float>(1.0 / sqrt(ss / static_cast<double>(w) + static_cast<double>(eps)));
+      if (threadIdx.x == 0 && inv_rms != nullptr) inv_rms[r] = inv;
+      for (uint32_t c = threadIdx.x; c < w; c += THREADS)
+        out[static_cast<uint64_t>(r) * w + c] = __ldg(x + c) * inv * __ldg(weight + c);
+    }
+    __syncthreads();
+  }
+  if (first_bad != ~0ull) atomicMin(nonfinite, static_cast<unsigned long long>(first_bad));
+}
+
+template <int OP, int TPR>
+cudaError_t launch_bulk(const float* in, uint64_t stride, float* out, float* inv_rms, const float* weight, float eps,
+                        uint32_t rows, uint32_t w, unsigned long long* nonfinite, unsigned int* err,
+                        cudaStream_t stream) {
+  constexpr uint32_t RPB = THREADS / TPR;
+  const uint32_t batch_bytes = RPB * w * 4u;
+  uint32_t ns = SLOT_BUDGET_BYTES / batch_bytes;
+  ns = ns < 2 ? 2 : (ns > 8 ? 8 : ns);
+  const uint32_t smem = ns * batch_bytes;
+  auto kern = row_bulk_kernel<OP, TPR>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, THREADS, smem);
+  if (per_sm < 1) per_sm = 1;
+  const uint32_t batches = (rows + RPB - 1) / RPB;
+  const uint32_t grid = static_cast<uint32_t>(batches < static_cast<uint32_t>(sms * per_sm) ? batches : sms * per_sm);
+  kern<<<grid, THREADS, smem, stream>>>(in, stride, out, inv_rms, weight, eps, rows, w, ns, nonfinite, err);
+  return cudaGetLastError();
+}
+
+template <int OP>
+cudaError_t dispatch(const float* in, uint64_t stride, float* out, float* inv_rms, const float* weight, float eps,
+                     uint32_t rows, uint32_t w, unsigned long long* nonfinite, unsigned int* err,
+                     cudaStream_t stream) {
+  if (rows == 0 || w == 0) return cudaSuccess;
+  // The bulk path needs 16-byte granular rows for the copies and, for the
+  // row-wide outputs (softmax, RMSNorm), 16-byte aligned output and weight.
+  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool rowwise_out = (OP == kSoftmax || OP == kRms);
+  const bool aligned = (w % 4 == 0) && (stride % 4 == 0) && a16(in) && (!rowwise_out || a16(out)) &&
+                       (weight == nullptr || a16(weight));
+  if (aligned && w <= 1024) return launch_bulk<OP, 32>(in, stride, out, inv_rms, weight, eps, rows, w, nonfinite, err, stream);
+  if (aligned && w <= BULK_MAX_WIDTH)
+    return launch_bulk<OP, THREADS>(in, stride, out, inv_rms, weight, eps, rows, w, nonfinite, err, stream);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const uint32_t grid = rows < static_cast<uint32_t>(sms * 8) ? rows : static_cast<uint32_t>(sms * 8);
+  row_plain_kernel<OP><<<grid, THREADS, 0, stream>>>(in, stride, out, inv_rms, weight, eps, rows, w, nonfinite);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t row_reduce(const float* in, float* out, uint32_t rows, uint32_t width, uint32_t op,
+                       unsigned long long* nonfinite, unsigned int* err, cudaStream_t stream) {
+  switch (op) {
+    case 1: return dispatch<kSum>(in, width, out, nullptr, nullptr, 0.f, rows, width, nonfinite, err, stream);
+    case 2: return dispatch<kMax>(in, width, out, nullptr, nullptr, 0.f, rows, width, nonfinite, err, stream);
+    case 3: return dispatch<kSoftmax>(in, width, out, nullptr, nullptr, 0.f, rows, width, nonfinite, err, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t rmsnorm(const float* in, uint64_t in_stride, const float* weight, float* out, float* inv_rms,
+                    uint32_t rows, uint32_t width, float eps, unsigned long long* nonfinite, unsigned int* err,
+                    cudaStream_t stream) {
+  return dispatch<kRms>(in, in_stride, out, inv_rms, weight, eps, rows, width, nonfinite, err, stream);
+}
+
+}  // namespace oct

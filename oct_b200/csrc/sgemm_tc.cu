@@ -1,0 +1,377 @@
+// sgemm_tc.cu -- fp32 SGEMM on the sm_100a tensor cores with the 3xTF32 split.
+//
+// C[m x n] = A[m x k] * B[k x n], all row-major fp32, C overwritten.  This is the
+// product Oct's `prometheus_reactor_runtime_sgemm` computes
+// (internal/prometheus/native/reactor_api.h:2587-2595) and that its CPU oracle
+// `cpuSGEMM` restates (internal/prometheus/runtime.go:319-331).
+//
+// Precision: each operand x is split as x_hi = tf32(x) and x_lo = tf32(x - x_hi)
+// (round to nearest), which represents x to about 2^-22 relative.  The product
+// is accumulated in fp32 in TMEM as  A_hi*B_hi + A_hi*B_lo + A_lo*B_hi;  the
+// dropped A_lo*B_lo term is below fp32 resolution.  The result is as accurate
+// as a plain fp32 dot product (tests pin it against an fp64 oracle).
+//
+// Pipeline:
+//   1. split_rows / split_transpose write hi/lo copies of A and of B^T into
+//      a zero-padded, K-major scratch layout (M to 128, N to 256, K to 32).
+//      Padding removes every ragged edge from the main loop.
+//   2. sgemm3x_kernel: one CTA per 128x256 output tile, warp-specialised:
+//        warp 0      TMA producer: 4 tiles per stage (A_hi, A_lo, B_hi, B_lo)
+//                    into a `STAGES`-deep shared-memory ring, 64/128-B swizzle;
+//        warp 1      MMA issuer: one elected thread issues 3 tcgen05.mma
+//                    (kind::tf32, M=128, N=256, K=8) per 8-deep k step into a
+//                    128x256 fp32 accumulator in TMEM, and frees a stage with
+//                    tcgen05.commit;
+//        warps 2..5  epilogue: tcgen05.ld the accumulator lanes they own and
+//                    store C with predicated (exact-tail) vector stores.
+//   Every wait is bounded (see ptx.cuh); a timeout sets a bit in `err`.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <algorithm>
+#include <mutex>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace oct {
+namespace {
+
+constexpr uint32_t BM = 128;
+constexpr uint32_t BN = 256;
+constexpr uint32_t KPAD = 32;       // K padding granule of the split buffers
+constexpr uint32_t GROUP_M = 16;    // tile rasterisation: M tiles per group
+constexpr uint32_t TMEM_COLS = 256; // fp32 accumulator columns (= BN)
+constexpr int NUM_THREADS = 192;
+
+template <int BK>
+struct TileCfg {
+  static constexpr uint32_t SWZ = BK * 4;                 // bytes per smem row = swizzle span
+  static constexpr uint32_t A_BYTES = BM * BK * 4;
+  static constexpr uint32_t B_BYTES = BN * BK * 4;
+  static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+  static constexpr uint32_t STAGES = (BK == 16) ? 4 : 2;
+  static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+};
+
+__host__ __device__ inline uint32_t round_up(uint32_t x, uint32_t g) { return (x + g - 1) / g * g; }
+
+// ------------------------------------------------------------------ split
+// hi = tf32(v), lo = tf32(v - hi); v = 0 outside [rows, cols).
+// Each thread produces 4 consecutive padded columns of one row.
+__global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ src, uint64_t ld,
+                                                         uint32_t rows, uint32_t cols,
+                                                         float* __restrict__ hi, float* __restrict__ lo,
+                                                         uint32_t rows_p, uint32_t cols_p) {
+  const uint64_t groups_per_row = cols_p / 4;
+  const uint64_t total = static_cast<uint64_t>(rows_p) * groups_per_row;
+  const bool vec_ok = (ld % 4 == 0) && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
+  for (uint64_t g = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; g < total;
+       g += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t r = static_cast<uint32_t>(g / groups_per_row);
+    const uint32_t c = static_cast<uint32_t>(g % groups_per_row) * 4;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (r < rows) {
+      const float* p = src + r * ld + c;
+      if (vec_ok && c + 4 <= cols) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(p));
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (c + j < cols) v[j] = __ldg(p + j);
+      }
+    }
+    float h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      h[j] = to_tf32(v[j]);
+      l[j] = to_tf32(v[j] - h[j]);
+    }
+    const uint64_t o = static_cast<uint64_t>(r) * cols_p + c;
+    *reinterpret_cast<float4*>(hi + o) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(lo + o) = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// B is [k x n] row-major; writes hi/lo of B^T as [n_p x k_p] (K-major), zero padded.
+// 32x32 tiles through shared memory keep both the read and the write coalesced.
+__global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ b, uint64_t ldb,
+                                                              uint32_t k, uint32_t n,
+                                                              float* __restrict__ hi, float* __restrict__ lo,
+                                                              uint32_t kp) {
+  __shared__ float tile[32][33];
+  const uint32_t n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t kk = k0 + ty + 8 * i, nn = n0 + tx;
+    tile[ty + 8 * i][tx] = (kk < k && nn < n) ? __ldg(b + kk * ldb + nn) : 0.f;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t nn = n0 + ty + 8 * i, kk = k0 + tx;
+    const float v = tile[tx][ty + 8 * i];
+    const float h = to_tf32(v);
+    const uint64_t o = static_cast<uint64_t>(nn) * kp + kk;
+    hi[o] = h;
+    lo[o] = to_tf32(v - h);
+  }
+}
+
+// ------------------------------------------------------------------ main kernel
+template <int BK>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    sgemm3x_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+                   const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
+                   float* __restrict__ c, uint32_t m, uint32_t n, uint64_t ldc, uint32_t num_kb,
+                   uint32_t tiles_m, uint32_t tiles_n, unsigned int* __restrict__ err) {
+  using Cfg = TileCfg<BK>;
+  constexpr uint32_t S = Cfg::STAGES;
+  constexpr uint32_t IDESC = umma_idesc_tf32(BM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[S];
+  __shared__ __align__(8) uint64_t empty_bar[S];
+  __shared__ __align__(8) uint64_t accum_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ uint32_t issued_kb, consumed_kb, mma_issued, aborted;
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // Grouped rasterisation: GROUP_M tile rows sweep all tile columns together.
+  const uint32_t t = blockIdx.x;
+  const uint32_t per_group = GROUP_M * tiles_n;
+  const uint32_t first_m = (t / per_group) * GROUP_M;
+  const uint32_t group_rows = min(tiles_m - first_m, GROUP_M);
+  const uint32_t tile_m = first_m + (t % per_group) % group_rows;
+  const uint32_t tile_n = (t % per_group) / group_rows;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&accum_bar, 1);
+    issued_kb = 0;
+    consumed_kb = 0;
+    mma_issued = 0;
+    aborted = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    prefetch_tensormap(&tm_ahi);
+    prefetch_tensormap(&tm_alo);
+    prefetch_tensormap(&tm_bhi);
+    prefetch_tensormap(&tm_blo);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      const int row_a = static_cast<int>(tile_m * BM);
+      const int row_b = static_cast<int>(tile_n * BN);
+      uint32_t kb = 0;
+      for (; kb < num_kb; ++kb) {
+        const uint32_t s = kb % S;
+        if (kb >= S) {
+          if (!mbar_wait(&empty_bar[s], ((kb / S) - 1) & 1u, err, kErrWaitEmpty)) {
+            atomicExch(&aborted, 1u);
+            break;
+          }
+        }
+        if (*(volatile uint32_t*)&aborted) break;
+        uint8_t* st = smem + s * Cfg::STAGE_BYTES;
+        const int kx = static_cast<int>(kb * BK);
+        mbar_arrive_expect_tx(&full_bar[s], Cfg::STAGE_BYTES);
+        tma_load_2d(st, &tm_ahi, &full_bar[s], kx, row_a);
+        tma_load_2d(st + Cfg::A_BYTES, &tm_alo, &full_bar[s], kx, row_a);
+        tma_load_2d(st + 2 * Cfg::A_BYTES, &tm_bhi, &full_bar[s], kx, row_b);
+        tma_load_2d(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tm_blo, &full_bar[s], kx, row_b);
+      }
+      issued_kb = kb;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      uint32_t kb = 0;
+      for (; kb < num_kb; ++kb) {
+        const uint32_t s = kb % S;
+        if (!mbar_wait(&full_bar[s], (kb / S) & 1u, err, kErrWaitFull)) {
+          atomicExch(&aborted, 1u);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t base = smem_addr(smem + s * Cfg::STAGE_BYTES);
+        const uint32_t a_hi = base, a_lo = base + Cfg::A_BYTES;
+        const uint32_t b_hi = base + 2 * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
+#pragma unroll
+        for (uint32_t kk = 0; kk < BK / 8; ++kk) {
+          const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K
+          const uint64_t dah = umma_desc_kmajor(a_hi + off, Cfg::SWZ);
+          const uint64_t dal = umma_desc_kmajor(a_lo + off, Cfg::SWZ);
+          const uint64_t dbh = umma_desc_kmajor(b_hi + off, Cfg::SWZ);
+          const uint64_t dbl = umma_desc_kmajor(b_lo + off, Cfg::SWZ);
+          umma_tf32(tmem_base, dal, dbh, IDESC, (kb | kk) != 0u ? 1u : 0u);
+          umma_tf32(tmem_base, dah, dbl, IDESC, 1u);
+          umma_tf32(tmem_base, dah, dbh, IDESC, 1u);
+        }
+        umma_commit(&empty_bar[s]);
+      }
+      consumed_kb = kb;
+      mma_issued = kb;
+      umma_commit(&accum_bar);  // arrives once every MMA above has completed
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5 own TMEM lane quarters (warp % 4)
+    const uint32_t q = warp & 3u;
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&accum_bar, 0, err, kErrWaitAccum));
+    tc_fence_after();
+    if (ok && num_kb > 0) {
+      const uint32_t row = tile_m * BM + q * 32 + lane;
+      const uint32_t col0 = tile_n * BN;
+      const bool vec_ok = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0);
+#pragma unroll 1
+      for (uint32_t chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((q * 32u) << 16) + chunk * 32u, r);
+        tmem_ld_wait();
+        const uint32_t cb = col0 + chunk * 32;
+        if (row < m && cb < n) {
+          float* dst = c + static_cast<uint64_t>(row) * ldc + cb;
+          if (vec_ok && cb + 32 <= n) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (cb + j < n) dst[j] = __uint_as_float(r[j]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  // Teardown.  On an aborted run, wait (bounded) for copies and MMAs still in
+  // flight before the CTA releases its shared memory and TMEM.
+  if (aborted) {
+    if (threadIdx.x == 0) {
+      for (uint32_t kb = consumed_kb; kb < issued_kb; ++kb)
+        if (!mbar_wait(&full_bar[kb % S], (kb / S) & 1u, err, kErrWaitDrain)) break;
+    }
+    if (threadIdx.x == 32 && mma_issued > 0) mbar_wait(&accum_bar, 0, err, kErrWaitDrain);
+    __syncthreads();
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// K-major fp32 operand [rows x kp]; box = [bk x box_rows] with a bk*4-byte swizzle.
+bool make_operand_map(CUtensorMap* map, const float* base, uint32_t rows, uint32_t kp, uint32_t bk,
+                      uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {kp, rows};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kp) * sizeof(float)};
+  const cuuint32_t box[2] = {bk, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle swz = (bk == 32) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BK>
+cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
+                        uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
+                        cudaStream_t stream) {
+  using Cfg = TileCfg<BK>;
+  CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+  if (!make_operand_map(&m_ahi, ahi, d.mp, d.kp, BK, BM) || !make_operand_map(&m_alo, alo, d.mp, d.kp, BK, BM) ||
+      !make_operand_map(&m_bhi, bhi, d.np, d.kp, BK, BN) || !make_operand_map(&m_blo, blo, d.np, d.kp, BK, BN))
+    return cudaErrorInvalidValue;
+  // Set on every launch: the attribute belongs to the current device's context.
+  cudaError_t e = cudaFuncSetAttribute(sgemm3x_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(Cfg::SMEM_BYTES));
+  if (e != cudaSuccess) return e;
+  const uint32_t tiles_m = d.mp / BM, tiles_n = d.np / BN;
+  sgemm3x_kernel<BK><<<tiles_m * tiles_n, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(
+      m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, err);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+SplitDims split_dims(uint32_t m, uint32_t n, uint32_t k) {
+  return SplitDims{round_up(m, BM), round_up(n, BN), round_up(k, KPAD)};
+}
+
+uint64_t sgemm_tc_scratch_bytes(uint32_t m, uint32_t n, uint32_t k) {
+  const SplitDims d = split_dims(m, n, k);
+  return 2ull * sizeof(float) * (static_cast<uint64_t>(d.mp) * d.kp + static_cast<uint64_t>(d.np) * d.kp);
+}
+
+cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
+                     uint32_t m, uint32_t n, uint32_t k, void* scratch, unsigned int* err, int bk,
+                     cudaStream_t stream, const SgemmEvents* events) {
+  if (m == 0 || n == 0 || k == 0) return cudaSuccess;
+  if (bk != 16 && bk != 32) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(scratch) & 1023u) != 0) return cudaErrorInvalidValue;
+  const SplitDims d = split_dims(m, n, k);
+  float* ahi = static_cast<float*>(scratch);
+  float* alo = ahi + static_cast<uint64_t>(d.mp) * d.kp;
+  float* bhi = alo + static_cast<uint64_t>(d.mp) * d.kp;
+  float* blo = bhi + static_cast<uint64_t>(d.np) * d.kp;
+
+  if (events != nullptr && events->split_begin != nullptr) cudaEventRecord(events->split_begin, stream);
+  const uint64_t groups = static_cast<uint64_t>(d.mp) * (d.kp / 4);
+  const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((groups + 255) / 256, 148ull * 16));
+  split_rows_kernel<<<blocks, 256, 0, stream>>>(a, lda, m, k, ahi, alo, d.mp, d.kp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  split_transpose_kernel<<<dim3(d.np / 32, d.kp / 32), 256, 0, stream>>>(b, ldb, k, n, bhi, blo, d.kp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (events != nullptr && events->main_begin != nullptr) cudaEventRecord(events->main_begin, stream);
+  e = bk == 16 ? launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream)
+               : launch_main<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream);
+  if (events != nullptr && events->main_end != nullptr) cudaEventRecord(events->main_end, stream);
+  return e;
+}
+
+}  // namespace oct

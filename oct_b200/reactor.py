@@ -1,0 +1,583 @@
+"""Host-side binding of ``libprometheus_reactor.so``, mirroring Oct's Go bridge.
+
+Oct's Go host (internal/prometheus/bridge.go, bridge_dlopen_linux.go) finds the
+reactor library, checks ``prometheus_reactor_abi_version() == 1``, resolves the
+mandatory symbols, creates a runtime handle, probes it, and then calls
+``SGEMM`` / the async family / the Gemma entry points.  This module does the
+same through ctypes, with the same discovery order, issue codes and status
+conventions, so the parity tests read like the reference's own bridge tests.
+
+There is no CPU fallback: if the library or a usable B200 is missing, every
+constructor raises :class:`ReactorIssue`.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Optional
+
+import numpy as np
+
+EXPECTED_ABI = 1
+ENV_VAR = "OCT_PROMETHEUS_REACTOR"  # bridge.go:13
+LIB_NAME = "libprometheus_reactor.so"
+
+# ---- constants (include/prometheus_reactor.h) --------------------------------
+PROM_OK, PROM_ERROR, PROM_INVALID_HANDLE, PROM_INTERNAL_ERROR = 0, 1, 2, 3
+PROM_BACKEND_VULKAN = 2
+STAGE_NONE, STAGE_INIT, STAGE_TRANSFER_IN, STAGE_SUBMIT, STAGE_TRANSFER_OUT, STAGE_CLEANUP = range(6)
+ASYNC_IDLE, ASYNC_SUBMITTED, ASYNC_READY, ASYNC_FAILED, ASYNC_CONSUMED = range(5)
+
+TESTCFG_FAIL_DEVICE_CREATE = 1 << 0
+TESTCFG_FAIL_BUFFER_ALLOC = 1 << 2
+TESTCFG_FAIL_UPLOAD = 1 << 3
+TESTCFG_FAIL_DISPATCH = 1 << 4
+TESTCFG_FAIL_DOWNLOAD = 1 << 5
+TESTCFG_FAIL_ASYNC_POLL = 1 << 15
+TESTCFG_FORCE_STRICT_FP32 = 1 << 17
+REDUCTION_TESTCFG_FAIL_COMMAND_RECORD = 1 << 0
+REDUCTION_TESTCFG_FAIL_QUEUE_SUBMIT = 1 << 1
+REDUCTION_TESTCFG_FAIL_COMPLETION_OBSERVATION = 1 << 2
+
+DETAIL_PATH_DIRECT = 6101
+DETAIL_INJECTED_UPLOAD_FAILURE = -6001
+DETAIL_INJECTED_DISPATCH_FAILURE = -6002
+DETAIL_INJECTED_DOWNLOAD_FAILURE = -6003
+DETAIL_SIZE_OVERFLOW = -6004
+DETAIL_ASYNC_NOT_READY = -6108
+DETAIL_ASYNC_NO_TASK = -6109
+DETAIL_ASYNC_ALREADY_CONSUMED = -6110
+DETAIL_ASYNC_INVALID_TASK = -6111
+DETAIL_ASYNC_INJECTED_POLL_FAILURE = -6116
+DETAIL_ASYNC_QUEUE_FULL = -6117
+
+OP_SUM, OP_MAX, OP_SOFTMAX = 1, 2, 3
+FINALIZATION_NONE, FINALIZATION_STABLE_SOFTMAX = 0, 1
+SGEMM_AUTO, SGEMM_TC3XTF32, SGEMM_FMA = 0, 1, 2
+SGEMM_TC_BK16, SGEMM_TC_BK32 = 16, 32  # explicit tensor-core stage depths
+
+MAX_STAGES = 8
+
+
+# ---- ABI structs (byte-compatible with the C header) -------------------------
+class PrometheusCaps(C.Structure):
+    _fields_ = [("available", C.c_uint32), ("backend_type", C.c_uint32), ("reason_code", C.c_uint32)]
+
+
+class PrometheusReactorConfig(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("test_flags", C.c_uint32),
+        ("p15_shadow_disabled", C.c_uint32),
+        ("async_test_flags", C.c_uint32),
+        ("batch_ring_depth", C.c_uint32),
+        ("reduction_test_flags", C.c_uint32),
+        ("reduction_ring_depth", C.c_uint32),
+        ("shader_package_root", C.c_char_p),
+    ]
+
+
+class PrometheusAsyncStatus(C.Structure):
+    _fields_ = [
+        ("lifecycle_state", C.c_uint32),
+        ("stage", C.c_uint32),
+        ("detail_code", C.c_int),
+        ("ready", C.c_uint32),
+        ("failed", C.c_uint32),
+        ("consumed", C.c_uint32),
+        ("outstanding_tasks", C.c_uint32),
+    ]
+
+
+class PrometheusReductionRequest(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("input", C.c_void_p),
+        ("output", C.c_void_p),
+        ("row_count", C.c_uint32),
+        ("elements_per_row", C.c_uint32),
+        ("input_element_count", C.c_uint64),
+        ("output_element_count", C.c_uint64),
+        ("operation", C.c_uint32),
+        ("finalization", C.c_uint32),
+        ("flags", C.c_uint32),
+    ]
+
+
+class PrometheusReductionStageDispatch(C.Structure):
+    _fields_ = [
+        ("stage_role", C.c_uint32),
+        ("shader_id", C.c_uint32),
+        ("implementation_id", C.c_uint32),
+        ("groups_x", C.c_uint32),
+        ("groups_y", C.c_uint32),
+        ("groups_z", C.c_uint32),
+        ("input_elements_per_row", C.c_uint32),
+        ("output_partials_per_row", C.c_uint32),
+        ("temporary_role", C.c_uint32),
+        ("temporary_bytes_written", C.c_uint64),
+    ]
+
+
+class PrometheusReductionPlan(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("operation", C.c_uint32),
+        ("row_count", C.c_uint32),
+        ("elements_per_row", C.c_uint32),
+        ("strategy", C.c_uint32),
+        ("local_size", C.c_uint32),
+        ("elements_per_partial", C.c_uint32),
+        ("partial_count", C.c_uint32),
+        ("stage_count", C.c_uint32),
+        ("temporary_alignment_bytes", C.c_uint32),
+        ("temporary_bytes", C.c_uint64),
+        ("replay_id", C.c_uint64),
+        ("stages", PrometheusReductionStageDispatch * MAX_STAGES),
+    ]
+
+
+class PrometheusReductionExecutionResult(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("stage", C.c_uint32),
+        ("detail_code", C.c_int32),
+        ("logical_request_id", C.c_uint64),
+        ("physical_slot_id", C.c_uint32),
+        ("physical_slot_generation", C.c_uint32),
+        ("physical_slot_recyclable", C.c_uint32),
+        ("gpu_timestamp_valid", C.c_uint32),
+        ("gpu_duration_ns", C.c_uint64),
+        ("end_to_end_ns", C.c_uint64),
+        ("first_nonfinite_index", C.c_uint64),
+        ("validation_error_count_before", C.c_uint32),
+        ("validation_error_count_after", C.c_uint32),
+        ("plan", PrometheusReductionPlan),
+    ]
+
+
+class PrometheusRowWiseSoftmaxRequest(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("input", C.c_void_p),
+        ("output", C.c_void_p),
+        ("row_count", C.c_uint32),
+        ("elements_per_row", C.c_uint32),
+        ("input_element_count", C.c_uint64),
+        ("output_element_count", C.c_uint64),
+    ]
+
+
+class PrometheusRowWiseSoftmaxResult(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("stage", C.c_uint32),
+        ("detail_code", C.c_int32),
+        ("output_written", C.c_uint32),
+        ("physical_dispatch_count", C.c_uint32),
+        ("physical_submission_count", C.c_uint32),
+        ("gpu_timestamp_valid", C.c_uint32),
+        ("gpu_duration_ns", C.c_uint64),
+        ("end_to_end_ns", C.c_uint64),
+        ("first_nonfinite_index", C.c_uint64),
+    ]
+
+
+class PrometheusGemma4E2BM1InputRmsNormRequest(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("input", C.c_void_p),
+        ("weight", C.c_void_p),
+        ("output", C.c_void_p),
+        ("inv_rms_output", C.c_void_p),
+        ("input_element_count", C.c_uint64),
+        ("weight_element_count", C.c_uint64),
+        ("output_element_count", C.c_uint64),
+        ("inv_rms_output_element_count", C.c_uint64),
+        ("tokens", C.c_uint32),
+        ("model_width", C.c_uint32),
+        ("input_row_stride", C.c_uint32),
+        ("epsilon", C.c_float),
+        ("input_generation", C.c_uint64),
+        ("weight_generation", C.c_uint64),
+        ("exact_source_hash", C.c_uint64),
+    ]
+
+
+class PrometheusGemma4E2BM1InputRmsNormResult(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("stage", C.c_uint32),
+        ("detail_code", C.c_int32),
+        ("output_written", C.c_uint32),
+        ("matched_input", C.c_uint32),
+        ("input_hash", C.c_uint64),
+        ("weight_hash", C.c_uint64),
+        ("output_hash", C.c_uint64),
+        ("inv_rms_hash", C.c_uint64),
+        ("submit_count", C.c_uint32),
+        ("final_readback_count", C.c_uint32),
+        ("no_product_intermediate_readback_change", C.c_uint32),
+        ("reserved0", C.c_uint32),
+        ("retained_bytes", C.c_uint64),
+        ("buffer_allocation_count", C.c_uint64),
+        ("buffer_reuse_count", C.c_uint64),
+        ("descriptor_update_count", C.c_uint64),
+        ("pipeline_create_count", C.c_uint64),
+        ("command_buffer_reuse_count", C.c_uint64),
+        ("reduction_gpu_ns", C.c_uint64),
+        ("final_reduction_gpu_ns", C.c_uint64),
+        ("inv_rms_gpu_ns", C.c_uint64),
+        ("apply_gpu_ns", C.c_uint64),
+        ("end_to_end_ns", C.c_uint64),
+    ]
+
+
+# ---- signatures ---------------------------------------------------------------
+_vp, _u32, _u64, _i32p, _u32p = C.c_void_p, C.c_uint32, C.c_uint64, C.POINTER(C.c_int), C.POINTER(C.c_uint32)
+
+SIGNATURES = {
+    "prometheus_reactor_abi_version": (C.c_uint32, []),
+    "prometheus_reactor_runtime_create": (C.c_int, [_vp, C.POINTER(C.c_void_p)]),
+    "prometheus_reactor_runtime_destroy": (C.c_int, [_vp]),
+    "prometheus_reactor_runtime_probe": (C.c_int, [_vp, C.POINTER(PrometheusCaps)]),
+    "prometheus_reactor_runtime_sgemm": (C.c_int, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32p, _i32p]),
+    "prometheus_reactor_runtime_sgemm_submit_async": (
+        C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _i32p, _u32p, _i32p]),
+    "prometheus_reactor_runtime_sgemm_query_async": (C.c_int, [_vp, C.c_int, C.POINTER(PrometheusAsyncStatus)]),
+    "prometheus_reactor_runtime_sgemm_consume_async": (C.c_int, [_vp, C.c_int, _vp, _u32, _u32p, _i32p]),
+    "prometheus_reactor_runtime_sgemm_abandon_async": (C.c_int, [_vp, C.c_int]),
+    "prometheus_reactor_reduction_plan": (
+        C.c_int, [C.POINTER(PrometheusReductionRequest), C.POINTER(PrometheusReductionPlan)]),
+    "prometheus_reactor_runtime_reduction": (
+        C.c_int, [_vp, C.POINTER(PrometheusReductionRequest), C.POINTER(PrometheusReductionExecutionResult)]),
+    "prometheus_reactor_runtime_row_wise_softmax": (
+        C.c_int, [_vp, C.POINTER(PrometheusRowWiseSoftmaxRequest), C.POINTER(PrometheusRowWiseSoftmaxResult)]),
+    "prometheus_reactor_runtime_gemma4e2b_m1_input_rmsnorm": (
+        C.c_int,
+        [_vp, C.POINTER(PrometheusGemma4E2BM1InputRmsNormRequest), C.POINTER(PrometheusGemma4E2BM1InputRmsNormResult)]),
+    "prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm": (
+        C.c_int,
+        [_vp, C.POINTER(PrometheusGemma4E2BM1InputRmsNormRequest), C.POINTER(PrometheusGemma4E2BM1InputRmsNormResult)]),
+    "prometheus_runtime_create": (C.c_int, [_vp, C.POINTER(C.c_void_p)]),
+    "prometheus_runtime_destroy": (C.c_int, [_vp]),
+    "prometheus_runtime_probe": (C.c_int, [_vp, C.POINTER(PrometheusCaps)]),
+    "oct_b200_sgemm_device": (C.c_int, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp, _i32p]),
+    "oct_b200_sgemm_device_ld": (
+        C.c_int, [_vp, _vp, _u64, _vp, _u64, _vp, _u64, _u32, _u32, _u32, _u32, _vp, _i32p]),
+    "oct_b200_reduction_device": (C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _i32p]),
+    "oct_b200_rmsnorm_device": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, C.c_float, _vp, _i32p]),
+    "oct_b200_sync_status": (C.c_int, [_vp, _vp, _i32p]),
+    "oct_b200_set_kernel_timing": (C.c_int, [_vp, C.c_int]),
+    "oct_b200_read_kernel_timing": (
+        C.c_int, [_vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_uint32)]),
+    "oct_b200_build_info": (C.c_char_p, []),
+}
+
+# Symbols Go refuses to run without (bridge.go:276-340).
+MANDATORY = (
+    "prometheus_reactor_abi_version",
+    "prometheus_reactor_runtime_create",
+    "prometheus_reactor_runtime_destroy",
+    "prometheus_reactor_runtime_probe",
+    "prometheus_reactor_runtime_sgemm",
+)
+
+
+class ReactorIssue(RuntimeError):
+    """Mirror of bridge.go's ReactorIssue: a typed failure to reach the reactor."""
+
+    NOT_FOUND = "reactor_not_found"
+    LOAD_FAILED = "reactor_load_failed"
+    SYMBOL_MISSING = "symbol_missing"
+    ABI_MISMATCH = "abi_mismatch"
+    CREATE_FAILED = "runtime_create_failed"
+    PROBE_FAILED = "runtime_probe_unavailable"
+    SGEMM_FAILED = "runtime_sgemm_failed"
+
+    def __init__(self, code: str, message: str = "", *, path: str = "", symbol: str = "", stage: int = 0,
+                 detail: int = 0):
+        super().__init__(f"{code}: {message}" if message else code)
+        self.code, self.path, self.symbol, self.stage, self.detail = code, path, symbol, stage, detail
+
+
+@dataclass
+class CallStatus:
+    """reactorCallStatus in bridge.go: the native stage and detail of one call."""
+
+    rc: int
+    stage: int
+    detail: int
+
+    @property
+    def ok(self) -> bool:
+        return self.rc == PROM_OK
+
+
+def default_library_path() -> Path:
+    return Path(__file__).resolve().parent / LIB_NAME
+
+
+def candidate_paths() -> list[Path]:
+    """Discovery order of bridge.go:552-601: the env var, then the in-tree build."""
+    out = []
+    env = os.environ.get(ENV_VAR)
+    if env:
+        out.append(Path(env))
+    out.append(default_library_path())
+    return out
+
+
+def load_library(path: Optional[os.PathLike] = None) -> C.CDLL:
+    """dlopen the reactor, check the ABI, bind every known symbol's signature."""
+    paths = [Path(path)] if path is not None else candidate_paths()
+    found = next((p for p in paths if p.exists()), None)
+    if found is None:
+        raise ReactorIssue(ReactorIssue.NOT_FOUND, "no libprometheus_reactor.so (build it: python -m oct_b200.build)")
+    try:
+        lib = C.CDLL(str(found), mode=os.RTLD_NOW | os.RTLD_LOCAL)
+    except OSError as exc:
+        raise ReactorIssue(ReactorIssue.LOAD_FAILED, str(exc), path=str(found)) from exc
+    for name in MANDATORY:
+        if not hasattr(lib, name):
+            raise ReactorIssue(ReactorIssue.SYMBOL_MISSING, name, path=str(found), symbol=name)
+    for name, (res, args) in SIGNATURES.items():
+        if hasattr(lib, name):
+            fn = getattr(lib, name)
+            fn.restype, fn.argtypes = res, args
+    abi = lib.prometheus_reactor_abi_version()
+    if abi != EXPECTED_ABI:
+        raise ReactorIssue(ReactorIssue.ABI_MISMATCH, f"expected {EXPECTED_ABI}, library reports {abi}",
+                           path=str(found))
+    lib._oct_path = str(found)  # type: ignore[attr-defined]
+    return lib
+
+
+def _f32(x: np.ndarray, name: str) -> np.ndarray:
+    if not isinstance(x, np.ndarray) or x.dtype != np.float32 or not x.flags.c_contiguous:
+        raise TypeError(f"{name} must be a C-contiguous float32 numpy array")
+    return x
+
+
+def _ptr(x) -> int:
+    """Address of a numpy array or of a torch tensor's storage."""
+    if isinstance(x, np.ndarray):
+        return x.ctypes.data
+    if hasattr(x, "data_ptr"):
+        return int(x.data_ptr())
+    if x is None:
+        return 0
+    return int(x)
+
+
+class Runtime:
+    """One reactor handle: Go's nativeRuntime (bridge.go:276-520)."""
+
+    def __init__(self, lib: Optional[C.CDLL] = None, *, test_flags: int = 0, async_test_flags: int = 0,
+                 reduction_test_flags: int = 0, require_device: bool = True):
+        self.lib = lib if lib is not None else load_library()
+        cfg = PrometheusReactorConfig()
+        cfg.struct_size = C.sizeof(PrometheusReactorConfig)
+        cfg.test_flags = test_flags
+        cfg.async_test_flags = async_test_flags
+        cfg.reduction_test_flags = reduction_test_flags
+        cfg.reduction_ring_depth = 3  # what Go always passes (bridge.go:318)
+        handle = C.c_void_p()
+        rc = self.lib.prometheus_reactor_runtime_create(C.byref(cfg), C.byref(handle))
+        if rc != PROM_OK or not handle.value:
+            raise ReactorIssue(ReactorIssue.CREATE_FAILED, f"rc={rc}")
+        self.handle = handle
+        caps = PrometheusCaps()
+        rc = self.lib.prometheus_reactor_runtime_probe(self.handle, C.byref(caps))
+        self.caps = caps
+        if require_device and (rc != PROM_OK or not caps.available):
+            self.close()
+            raise ReactorIssue(ReactorIssue.PROBE_FAILED, f"rc={rc} available={caps.available} reason={caps.reason_code}")
+
+    # -- lifetime
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            self.lib.prometheus_reactor_runtime_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __enter__(self) -> "Runtime":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- SGEMM (bridge.go:410-436)
+    def sgemm_with_status(self, m: int, n: int, k: int, a: np.ndarray, b: np.ndarray,
+                          out: Optional[np.ndarray] = None) -> tuple[Optional[np.ndarray], CallStatus]:
+        _f32(a, "a")
+        _f32(b, "b")
+        if a.size != m * k or b.size != k * n:
+            return None, CallStatus(PROM_ERROR, STAGE_INIT, -2)  # "invalid matrix lengths"
+        c = out if out is not None else np.empty(m * n, dtype=np.float32)
+        _f32(c, "c")
+        stage, detail = C.c_uint32(), C.c_int()
+        rc = self.lib.prometheus_reactor_runtime_sgemm(self.handle, _ptr(a), _ptr(b), _ptr(c), m, n, k,
+                                                       C.byref(stage), C.byref(detail))
+        st = CallStatus(rc, stage.value, detail.value)
+        return (c if rc == PROM_OK else None), st
+
+    def sgemm(self, m: int, n: int, k: int, a: np.ndarray, b: np.ndarray) -> np.ndarray:
+        c, st = self.sgemm_with_status(m, n, k, a, b)
+        if not st.ok:
+            raise ReactorIssue(ReactorIssue.SGEMM_FAILED, f"stage={st.stage} detail={st.detail}", stage=st.stage,
+                               detail=st.detail)
+        return c
+
+    # -- async SGEMM (bridge.go:342-361, runtime.go:573-650)
+    def submit_async(self, m: int, n: int, k: int, a: np.ndarray, b: np.ndarray) -> tuple[int, CallStatus]:
+        _f32(a, "a")
+        _f32(b, "b")
+        task, stage, detail = C.c_int(), C.c_uint32(), C.c_int()
+        rc = self.lib.prometheus_reactor_runtime_sgemm_submit_async(self.handle, _ptr(a), _ptr(b), m, n, k,
+                                                                    C.byref(task), C.byref(stage), C.byref(detail))
+        return task.value, CallStatus(rc, stage.value, detail.value)
+
+    def query_async(self, task: int) -> tuple[int, PrometheusAsyncStatus]:
+        st = PrometheusAsyncStatus()
+        rc = self.lib.prometheus_reactor_runtime_sgemm_query_async(self.handle, task, C.byref(st))
+        return rc, st
+
+    def consume_async(self, task: int, c: np.ndarray) -> CallStatus:
+        _f32(c, "c")
+        stage, detail = C.c_uint32(), C.c_int()
+        rc = self.lib.prometheus_reactor_runtime_sgemm_consume_async(self.handle, task, _ptr(c), c.size,
+                                                                     C.byref(stage), C.byref(detail))
+        return CallStatus(rc, stage.value, detail.value)
+
+    def abandon_async(self, task: int) -> int:
+        return self.lib.prometheus_reactor_runtime_sgemm_abandon_async(self.handle, task)
+
+    # -- reductions
+    def reduction(self, x: np.ndarray, operation: int, *, flags: int = 0,
+                  out: Optional[np.ndarray] = None) -> tuple[Optional[np.ndarray], PrometheusReductionExecutionResult]:
+        _f32(x, "x")
+        rows, width = x.shape
+        n_out = x.size if operation == OP_SOFTMAX else rows
+        y = out if out is not None else np.empty(n_out, dtype=np.float32)
+        req = make_reduction_request(x, y, rows, width, operation, flags)
+        res = PrometheusReductionExecutionResult()
+        rc = self.lib.prometheus_reactor_runtime_reduction(self.handle, C.byref(req), C.byref(res))
+        return (y if rc == PROM_OK else None), res
+
+    def row_wise_softmax(self, x: np.ndarray, out: Optional[np.ndarray] = None
+                         ) -> tuple[int, Optional[np.ndarray], PrometheusRowWiseSoftmaxResult]:
+        rows, width = x.shape
+        y = out if out is not None else np.empty_like(x)
+        req = PrometheusRowWiseSoftmaxRequest()
+        req.struct_size = C.sizeof(req)
+        req.input, req.output = _ptr(x), _ptr(y)
+        req.row_count, req.elements_per_row = rows, width
+        req.input_element_count = req.output_element_count = rows * width
+        res = PrometheusRowWiseSoftmaxResult()
+        rc = self.lib.prometheus_reactor_runtime_row_wise_softmax(self.handle, C.byref(req), C.byref(res))
+        return rc, (y if rc == PROM_OK else None), res
+
+    def rmsnorm(self, x: np.ndarray, weight: np.ndarray, eps: float, *, head: bool = False
+                ) -> tuple[int, Optional[np.ndarray], Optional[np.ndarray], PrometheusGemma4E2BM1InputRmsNormResult]:
+        _f32(x, "x")
+        _f32(weight, "weight")
+        rows, width = x.shape
+        y = np.empty_like(x)
+        inv = np.empty(rows, dtype=np.float32)
+        req = PrometheusGemma4E2BM1InputRmsNormRequest()
+        req.struct_size = C.sizeof(req)
+        req.input, req.weight, req.output, req.inv_rms_output = _ptr(x), _ptr(weight), _ptr(y), _ptr(inv)
+        req.input_element_count = x.size
+        req.weight_element_count = weight.size
+        req.output_element_count = y.size
+        req.inv_rms_output_element_count = rows
+        req.tokens, req.model_width, req.input_row_stride = rows, width, width
+        req.epsilon = eps
+        req.input_generation = req.weight_generation = req.exact_source_hash = 1
+        res = PrometheusGemma4E2BM1InputRmsNormResult()
+        fn = (self.lib.prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm if head
+              else self.lib.prometheus_reactor_runtime_gemma4e2b_m1_input_rmsnorm)
+        rc = fn(self.handle, C.byref(req), C.byref(res))
+        ok = rc == PROM_OK
+        return rc, (y if ok else None), (inv if ok else None), res
+
+    # -- device-resident extensions (torch tensors or raw device addresses)
+    def sgemm_device(self, a, b, c, m: int, n: int, k: int, variant: int = SGEMM_AUTO, stream=None,
+                     lda: Optional[int] = None, ldb: Optional[int] = None, ldc: Optional[int] = None) -> None:
+        detail = C.c_int()
+        rc = self.lib.oct_b200_sgemm_device_ld(self.handle, _ptr(a), lda or k, _ptr(b), ldb or n, _ptr(c), ldc or n,
+                                               m, n, k, variant, _stream_ptr(stream), C.byref(detail))
+        if rc != PROM_OK:
+            raise ReactorIssue(ReactorIssue.SGEMM_FAILED, f"device sgemm rc={rc} detail={detail.value}",
+                               detail=detail.value)
+
+    def reduction_device(self, x, y, rows: int, width: int, operation: int, stream=None) -> None:
+        detail = C.c_int()
+        rc = self.lib.oct_b200_reduction_device(self.handle, _ptr(x), _ptr(y), rows, width, operation,
+                                                _stream_ptr(stream), C.byref(detail))
+        if rc != PROM_OK:
+            raise RuntimeError(f"device reduction rc={rc} detail={detail.value}")
+
+    def rmsnorm_device(self, x, w, y, inv, rows: int, width: int, eps: float, stream=None) -> None:
+        detail = C.c_int()
+        rc = self.lib.oct_b200_rmsnorm_device(self.handle, _ptr(x), _ptr(w), _ptr(y), _ptr(inv), rows, width, eps,
+                                              _stream_ptr(stream), C.byref(detail))
+        if rc != PROM_OK:
+            raise RuntimeError(f"device rmsnorm rc={rc} detail={detail.value}")
+
+    def sync_status(self, stream=None) -> CallStatus:
+        detail = C.c_int()
+        rc = self.lib.oct_b200_sync_status(self.handle, _stream_ptr(stream), C.byref(detail))
+        return CallStatus(rc, 0, detail.value)
+
+
+    def set_kernel_timing(self, enable: bool) -> None:
+        self.lib.oct_b200_set_kernel_timing(self.handle, 1 if enable else 0)
+
+    def read_kernel_timing(self) -> tuple[float, float, int]:
+        """(split_ms_total, main_ms_total, launches) since the last read."""
+        s, m, n = C.c_double(), C.c_double(), C.c_uint32()
+        rc = self.lib.oct_b200_read_kernel_timing(self.handle, C.byref(s), C.byref(m), C.byref(n))
+        if rc != PROM_OK:
+            raise RuntimeError(f"kernel timing read failed rc={rc}")
+        return s.value, m.value, n.value
+
+
+def _stream_ptr(stream) -> int:
+    if stream is None:
+        return 0
+    if hasattr(stream, "cuda_stream"):
+        return int(stream.cuda_stream)
+    return int(stream)
+
+
+def make_reduction_request(x, y, rows: int, width: int, operation: int, flags: int = 0
+                           ) -> PrometheusReductionRequest:
+    req = PrometheusReductionRequest()
+    req.struct_size = C.sizeof(req)
+    req.input, req.output = _ptr(x), _ptr(y)
+    req.row_count, req.elements_per_row = rows, width
+    req.input_element_count = rows * width
+    req.output_element_count = rows * width if operation == OP_SOFTMAX else rows
+    req.operation = operation
+    req.finalization = FINALIZATION_STABLE_SOFTMAX if operation == OP_SOFTMAX else FINALIZATION_NONE
+    req.flags = flags
+    return req
+
+
+def reduction_plan(lib: C.CDLL, rows: int, width: int, operation: int, flags: int = 0
+                   ) -> tuple[int, PrometheusReductionPlan]:
+    """prometheus_reactor_reduction_plan: host-only, needs no device."""
+    dummy = np.zeros(1, dtype=np.float32)
+    req = make_reduction_request(dummy, dummy, rows, width, operation, flags)
+    plan = PrometheusReductionPlan()
+    rc = lib.prometheus_reactor_reduction_plan(C.byref(req), C.byref(plan))
+    return rc, plan

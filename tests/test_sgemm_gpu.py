@@ -1,0 +1,255 @@
+"""SGEMM parity on the B200 through the C ABI, against the CPU oracle and the
+exact known answers of the reference's own test matrices.
+
+Tolerances (written here, applied to every case):
+  * Oct's own gate compareAgainstOracle (runtime.go:12-15, 339-383): an element
+    fails when BOTH |err| > 1e-4 and rel > 1e-4 versus cpuSGEMM.
+  * BASELINE's "max relative error <= 1e-5 versus an fp64 oracle", measured
+    normwise: max|C - C64| / max|C64| <= 1e-5 (elementwise relative error is
+    unbounded where cancellation drives an output to ~0, for any fp32 method).
+  * No worse than Oct's own fp32 CPU path: max|C - C64| <= 2 * max|cpuSGEMM - C64|
+    plus one ulp of the largest output.
+Inputs whose products are exact in fp32 (Marionette / M20 matrices) must come
+back bit-exact from every kernel variant.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oct_b200 import reactor as R
+from tests.golden.make_golden import GEMMA, M20, STARTER
+
+pytestmark = pytest.mark.gpu
+
+VARIANTS = [R.SGEMM_FMA, R.SGEMM_TC_BK16, R.SGEMM_TC_BK32]
+NORMWISE_TOL = 1e-5
+
+
+def device_sgemm(rt, a: np.ndarray, b: np.ndarray, m: int, n: int, k: int, variant: int) -> np.ndarray:
+    import torch
+    da = torch.from_numpy(a.reshape(m, k)).cuda()
+    db = torch.from_numpy(b.reshape(k, n)).cuda()
+    dc = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float32)
+    torch.cuda.synchronize()
+    rt.sgemm_device(da, db, dc, m, n, k, variant)
+    st = rt.sync_status()
+    assert st.ok, st
+    return dc.cpu().numpy().ravel()
+
+
+def normwise(c: np.ndarray, ref64: np.ndarray) -> float:
+    return float(np.max(np.abs(c.astype(np.float64) - ref64)) / max(np.max(np.abs(ref64)), 1e-30))
+
+
+@pytest.mark.parametrize("shape", STARTER)
+def test_starter_corpus_host_abi(runtime, oracle_mod, golden, shape):
+    """RunStarterCorpus (runtime.go:91-104) through prometheus_reactor_runtime_sgemm."""
+    o = oracle_mod
+    m, n, k = shape
+    a, b = o.deterministic_matrix(m, k), o.deterministic_matrix(k, n)
+    c, st = runtime.sgemm_with_status(m, n, k, a, b)
+    assert st.ok and st.stage == R.STAGE_TRANSFER_OUT and st.detail == R.DETAIL_PATH_DIRECT
+    assert o.compare_against_oracle(o.cpu_sgemm_f32(a, b, m, n, k), c).pass_ == 1
+    assert o.compare_against_oracle(golden[f"sgemm_starter_{m}x{n}x{k}"], c).pass_ == 1
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("shape", STARTER + M20 + [(37, 29, 13)])
+def test_exact_inputs_bit_exact(runtime, oracle_mod, golden, shape, variant):
+    o = oracle_mod
+    m, n, k = shape
+    a, b = o.marionette_matrix(m * k, 3), o.marionette_matrix(k * n, 5)
+    c = device_sgemm(runtime, a, b, m, n, k, variant)
+    want = golden[f"sgemm_m20_{m}x{n}x{k}"] if f"sgemm_m20_{m}x{n}x{k}" in golden else o.cpu_sgemm_f32(a, b, m, n, k)
+    assert np.array_equal(c, want)
+
+
+def test_marionette_async_pair(runtime, oracle_mod, golden):
+    """reactor_concept_sgemm_tests.cpp:29-87: two independent async products, inputs unmodified."""
+    o = oracle_mod
+    m, n, k = 37, 29, 13
+    a, b, other = o.marionette_matrix(m * k, 3), o.marionette_matrix(k * n, 5), o.marionette_matrix(m * k, 19)
+    a0, b0 = a.copy(), b.copy()
+    t0, s0 = runtime.submit_async(m, n, k, a, b)
+    t1, s1 = runtime.submit_async(m, n, k, other, b)
+    assert s0.ok and s1.ok and t0 != t1
+    for task, key in ((t0, "s3_s5"), (t1, "s19_s5")):
+        for _ in range(2000):  # ValidateAsyncSGEMMOnHardware polls at most 2000 times (runtime.go:620)
+            rc, qs = runtime.query_async(task)
+            assert rc == R.PROM_OK
+            if qs.lifecycle_state != R.ASYNC_SUBMITTED:
+                break
+            import time
+            time.sleep(0.001)
+        assert qs.lifecycle_state == R.ASYNC_READY and qs.ready == 1
+        c = np.empty(m * n, dtype=np.float32)
+        st = runtime.consume_async(task, c)
+        assert st.ok and st.detail == R.DETAIL_PATH_DIRECT
+        assert np.array_equal(c, golden[f"sgemm_marionette_{m}x{n}x{k}_{key}"])
+        assert runtime.consume_async(task, c).detail == R.DETAIL_ASYNC_ALREADY_CONSUMED
+        assert runtime.abandon_async(task) == R.PROM_OK
+    assert np.array_equal(a, a0) and np.array_equal(b, b0)
+    assert runtime.query_async(12345)[1].detail_code == R.DETAIL_ASYNC_NO_TASK
+    assert runtime.consume_async(12345, np.empty(1, np.float32)).detail == R.DETAIL_ASYNC_INVALID_TASK
+
+
+def test_async_queue_full_and_short_buffer(runtime, oracle_mod):
+    o = oracle_mod
+    a = o.marionette_matrix(64, 1)
+    tasks = []
+    for _ in range(4):
+        t, st = runtime.submit_async(8, 8, 8, a, a)
+        assert st.ok
+        tasks.append(t)
+    t, st = runtime.submit_async(8, 8, 8, a, a)
+    assert not st.ok and st.detail == R.DETAIL_ASYNC_QUEUE_FULL
+    short = np.empty(63, dtype=np.float32)
+    import time
+    time.sleep(0.05)
+    for t in tasks:
+        while runtime.query_async(t)[1].lifecycle_state == R.ASYNC_SUBMITTED:
+            time.sleep(0.001)
+        assert runtime.consume_async(t, short).rc == R.PROM_ERROR
+        assert runtime.consume_async(t, np.empty(64, np.float32)).ok
+        assert runtime.abandon_async(t) == R.PROM_OK
+
+
+@pytest.mark.parametrize("variant", [R.SGEMM_AUTO, *VARIANTS])
+@pytest.mark.parametrize("shape", GEMMA)
+def test_gemma_small_m_corpus(runtime, oracle_mod, golden, shape, variant):
+    """gemma4e2b_sgemm_corpus_test.go:29-100, every M of the corpus as a prefix slice."""
+    o = oracle_mod
+    m, n, k = shape
+    a, b = o.gemma_corpus_a(m * k), o.gemma_corpus_b(k * n)
+    want = golden[f"sgemm_gemma_{m}x{n}x{k}"]
+    ms = [1, 2, 7, 15, 16, 17, 31, 32, 33] if m == 33 else [m]
+    for mm in ms:
+        c = device_sgemm(runtime, a[: mm * k], b, mm, n, k, variant)
+        ref = o.cpu_sgemm_f32(a[: mm * k], b, mm, n, k)
+        assert o.compare_against_oracle(ref, c).pass_ == 1, mm
+        assert normwise(c, want[: mm * n].astype(np.float64)) <= NORMWISE_TOL
+
+
+def _check_against_fp64(o, c, a, b, m, n, k, rows=None):
+    sl = rows or slice(0, m)
+    ref64 = o.sgemm_f64(a, b, m, n, k, rows=sl)
+    cpu32 = o.cpu_sgemm_f32(a, b, m, n, k, rows=sl, threads=o.max_threads())
+    got = c.reshape(m, n)[sl].ravel()
+    nw = normwise(got, ref64)
+    err_gpu = np.max(np.abs(got.astype(np.float64) - ref64))
+    err_cpu = np.max(np.abs(cpu32.astype(np.float64) - ref64))
+    ulp = np.spacing(np.float32(np.max(np.abs(ref64))))
+    assert nw <= NORMWISE_TOL, nw
+    assert err_gpu <= 2 * err_cpu + ulp, (err_gpu, err_cpu)
+    return nw
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("shape,seed", [((512, 512, 512), 0), ((1000, 1000, 1000), 1), ((4097, 4095, 1023), 2)])
+def test_baseline_shapes_full_compare(runtime, oracle_mod, shape, seed, variant):
+    """BASELINE configs[0] and the ragged sweep's smaller shapes: every output vs fp64."""
+    o = oracle_mod
+    m, n, k = shape
+    a, b = o.uniform_matrix(m, k, seed).ravel(), o.uniform_matrix(k, n, seed + 100).ravel()
+    c = device_sgemm(runtime, a, b, m, n, k, variant)
+    if m * n * k <= 2 ** 31:
+        _check_against_fp64(o, c, a, b, m, n, k)
+    else:
+        _check_against_fp64(o, c, a, b, m, n, k, rows=slice(0, 64))
+        _check_against_fp64(o, c, a, b, m, n, k, rows=slice(m - 65, m))
+    assert o.compare_against_oracle(o.cpu_sgemm_f32(a, b, m, n, k, rows=slice(0, 16), threads=8),
+                                    c[: 16 * n]).pass_ == 1
+
+
+def _checksums(o, c64, a, b, m, n, k):
+    """Size-independent property: row sums C.1 = A(B.1) and column sums 1^T C = (1^T A) B."""
+    A = a.reshape(m, k).astype(np.float64)
+    B = b.reshape(k, n).astype(np.float64)
+    row_ref = A @ B.sum(axis=1)
+    col_ref = A.sum(axis=0) @ B
+    C = c64.reshape(m, n)
+    row_got = C.astype(np.float64).sum(axis=1)
+    col_got = C.astype(np.float64).sum(axis=0)
+    # per-sum error bound: n (or m) outputs each off by <= 1e-5 * max|C|
+    scale = np.max(np.abs(C))
+    assert np.max(np.abs(row_got - row_ref)) <= n * 1e-5 * scale
+    assert np.max(np.abs(col_got - col_ref)) <= m * 1e-5 * scale
+
+
+@pytest.mark.parametrize("variant", [R.SGEMM_TC_BK16, R.SGEMM_TC_BK32])
+@pytest.mark.parametrize("shape,seed", [((8192, 8192, 8192), 3), ((16384, 16384, 4096), 4)])
+def test_baseline_large_shapes(runtime, oracle_mod, shape, seed, variant):
+    """8192^3 and 16384^2 x 4096: sampled rows vs fp64 plus whole-matrix checksums."""
+    o = oracle_mod
+    m, n, k = shape
+    a, b = o.uniform_matrix(m, k, seed).ravel(), o.uniform_matrix(k, n, seed + 100).ravel()
+    c = device_sgemm(runtime, a, b, m, n, k, variant)
+    assert np.all(np.isfinite(c))
+    for rows in (slice(0, 32), slice(m // 2 - 16, m // 2 + 16), slice(m - 32, m)):
+        _check_against_fp64(o, c, a, b, m, n, k, rows=rows)
+    _checksums(o, c, a, b, m, n, k)
+
+
+def test_host_abi_matches_device_path(runtime, oracle_mod):
+    o = oracle_mod
+    m, n, k = 300, 517, 129
+    a, b = o.uniform_matrix(m, k, 7).ravel(), o.uniform_matrix(k, n, 8).ravel()
+    c_host, st = runtime.sgemm_with_status(m, n, k, a, b)
+    assert st.ok
+    c_dev = device_sgemm(runtime, a, b, m, n, k, R.SGEMM_AUTO)
+    assert np.array_equal(c_host, c_dev)
+
+
+def test_leading_dimensions_column_shard(runtime, oracle_mod):
+    """oct_b200_sgemm_device_ld: a column block of a wider B / C (the tensor-parallel shard)."""
+    import torch
+    o = oracle_mod
+    m, n, k = 256, 1024, 384
+    a, b = o.uniform_matrix(m, k, 9), o.uniform_matrix(k, n, 10)
+    da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    full = torch.zeros((m, n), device="cuda")
+    for variant in VARIANTS:
+        for j in range(4):
+            cols = slice(j * 256, (j + 1) * 256)
+            runtime.sgemm_device(da, db[:, cols], full[:, cols], m, 256, k, variant, ldb=n, ldc=n)
+        assert runtime.sync_status().ok
+        ref = device_sgemm(runtime, a.ravel(), b.ravel(), m, n, k, variant)
+        assert np.array_equal(full.cpu().numpy().ravel(), ref)
+
+
+@pytest.mark.parametrize("flag,stage,detail", [
+    (R.TESTCFG_FAIL_UPLOAD, R.STAGE_TRANSFER_IN, R.DETAIL_INJECTED_UPLOAD_FAILURE),
+    (R.TESTCFG_FAIL_DISPATCH, R.STAGE_SUBMIT, R.DETAIL_INJECTED_DISPATCH_FAILURE),
+    (R.TESTCFG_FAIL_DOWNLOAD, R.STAGE_TRANSFER_OUT, R.DETAIL_INJECTED_DOWNLOAD_FAILURE),
+])
+def test_host_fault_injection(lib, oracle_mod, flag, stage, detail):
+    o = oracle_mod
+    a = o.marionette_matrix(16, 1)
+    c = np.full(16, 7.0, dtype=np.float32)
+    with R.Runtime(lib, test_flags=flag) as rt:
+        out, st = rt.sgemm_with_status(4, 4, 4, a, a, out=c)
+    assert (st.rc, st.stage, st.detail) == (R.PROM_ERROR, stage, detail)
+    assert np.all(c == 7.0)  # caller output untouched on failure
+
+
+def test_async_poll_fault_injection(lib, oracle_mod):
+    a = oracle_mod.marionette_matrix(16, 1)
+    with R.Runtime(lib, test_flags=R.TESTCFG_FAIL_ASYNC_POLL) as rt:
+        t, st = rt.submit_async(4, 4, 4, a, a)
+        assert st.ok
+        rc, qs = rt.query_async(t)
+        assert qs.lifecycle_state == R.ASYNC_FAILED and qs.detail_code == R.DETAIL_ASYNC_INJECTED_POLL_FAILURE
+        assert rt.consume_async(t, np.empty(16, np.float32)).detail == R.DETAIL_ASYNC_INJECTED_POLL_FAILURE
+        assert rt.abandon_async(t) == R.PROM_OK
+
+
+def test_strict_fp32_flag_selects_fma_control(lib, oracle_mod):
+    o = oracle_mod
+    m, n, k = 200, 300, 257
+    a, b = o.uniform_matrix(m, k, 11).ravel(), o.uniform_matrix(k, n, 12).ravel()
+    with R.Runtime(lib, test_flags=R.TESTCFG_FORCE_STRICT_FP32) as rt:
+        c, st = rt.sgemm_with_status(m, n, k, a, b)
+        assert st.ok
+        ref = device_sgemm(rt, a, b, m, n, k, R.SGEMM_FMA)
+    assert np.array_equal(c, ref)
