@@ -223,7 +223,8 @@ Runtime* create_runtime(const PrometheusReactorConfig* cfg, int* status) {
   }
   if (cudaStreamCreateWithFlags(&rt->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaEventCreate(&rt->ev0) != cudaSuccess || cudaEventCreate(&rt->ev1) != cudaSuccess ||
-      rt->words.ensure(16, rt->stream) != cudaSuccess) {
+      rt->words.ensure(16, rt->stream) != cudaSuccess || reset_words(rt) != cudaSuccess ||
+      cudaStreamSynchronize(rt->stream) != cudaSuccess) {
     rt->reason = PROM_REASON_VULKAN_UNAVAILABLE;
     *status = PROM_OK;
     return rt;

@@ -18,12 +18,14 @@
 //   2. sgemm3x_kernel: one CTA per 128x256 output tile, warp-specialised:
 //        warp 0      TMA producer: 4 tiles per stage (A_hi, A_lo, B_hi, B_lo)
 //                    into a `STAGES`-deep shared-memory ring, 64/128-B swizzle;
-//        warp 1      MMA issuer: one elected thread issues 3 tcgen05.mma
-//                    (kind::tf32, M=128, N=256, K=8) per 8-deep k step into a
-//                    128x256 fp32 accumulator in TMEM, and frees a stage with
+//        warp 1      MMA issuer: one thread issues 3 tcgen05.mma (kind::tf32,
+//                    M=128, N=256, K=8) per 8-deep k step into one of two
+//                    128x256 fp32 TMEM accumulators (alternating every 64 of
+//                    K, see the accumulation note), frees a stage with
 //                    tcgen05.commit;
-//        warps 2..5  epilogue: tcgen05.ld the accumulator lanes they own and
-//                    store C with predicated (exact-tail) vector stores.
+//        warps 2..9  epilogue: drain each K chunk's accumulator from TMEM
+//                    (tcgen05.ld) into fp32 register running sums, then store C
+//                    with predicated (exact-tail) vector stores.
 //   Every wait is bounded (see ptx.cuh); a timeout sets a bit in `err`.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -42,8 +44,8 @@ constexpr uint32_t BM = 128;
 constexpr uint32_t BN = 256;
 constexpr uint32_t KPAD = 32;       // K padding granule of the split buffers
 constexpr uint32_t GROUP_M = 16;    // tile rasterisation: M tiles per group
-constexpr uint32_t TMEM_COLS = 256; // fp32 accumulator columns (= BN)
-constexpr int NUM_THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512; // two 256-column fp32 accumulators (2 x BN)
+constexpr int NUM_THREADS = 320;  // producer warp, MMA warp, 8 epilogue warps
 
 template <int BK>
 struct TileCfg {
@@ -122,6 +124,18 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __res
 }
 
 // ------------------------------------------------------------------ main kernel
+// Accumulation precision.  The tensor core adds each MMA's products into the
+// TMEM accumulator with round-toward-zero, so a single accumulator over all of
+// K collects a biased error that grows like K^1.5 (at K = 512 it is already 4x
+// the error of a plain fp32 dot product).  The kernel therefore restarts the
+// TMEM accumulation every KC elements of K and adds each chunk's partial sum
+// into an fp32 running sum in registers (round-to-nearest).  Two 256-column
+// TMEM buffers alternate so the MMA fills one chunk while the epilogue warps
+// drain the other.  With KC = 64 the result is more accurate than Oct's own
+// sequential fp32 CPU loop at every K tested (512 ... 8192).
+constexpr uint32_t KC = 64;                 // K elements per TMEM accumulation chunk
+constexpr uint32_t NUM_EPI_WARPS = 8;       // 2 per TMEM lane quarter: 128 columns each
+
 template <int BK>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     sgemm3x_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
@@ -130,17 +144,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    uint32_t tiles_m, uint32_t tiles_n, unsigned int* __restrict__ err) {
   using Cfg = TileCfg<BK>;
   constexpr uint32_t S = Cfg::STAGES;
+  constexpr uint32_t KBC = KC / BK;  // k-blocks per accumulation chunk
   constexpr uint32_t IDESC = umma_idesc_tf32(BM, BN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[S];
   __shared__ __align__(8) uint64_t empty_bar[S];
-  __shared__ __align__(8) uint64_t accum_bar;
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
-  __shared__ uint32_t issued_kb, consumed_kb, mma_issued, aborted;
+  __shared__ uint32_t issued_kb, consumed_kb, aborted;
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t num_chunks = (num_kb + KBC - 1) / KBC;
 
   // Grouped rasterisation: GROUP_M tile rows sweep all tile columns together.
   const uint32_t t = blockIdx.x;
@@ -155,10 +173,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&accum_bar, 1);
+    for (uint32_t b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], NUM_EPI_WARPS);
+    }
+    mbar_init(&drain_bar, 1);
     issued_kb = 0;
     consumed_kb = 0;
-    mma_issued = 0;
     aborted = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -206,12 +227,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // ---------------- MMA issuer
       uint32_t kb = 0;
       for (; kb < num_kb; ++kb) {
+        const uint32_t chunk = kb / KBC, in_chunk = kb % KBC;
+        const uint32_t buf = chunk & 1u;
+        if (in_chunk == 0 && chunk >= 2) {
+          // the epilogue must have drained chunk - 2 out of this buffer
+          if (!mbar_wait(&acc_empty[buf], ((chunk >> 1) - 1) & 1u, err, kErrWaitAccum)) {
+            atomicExch(&aborted, 1u);
+            break;
+          }
+          tc_fence_after();
+        }
         const uint32_t s = kb % S;
         if (!mbar_wait(&full_bar[s], (kb / S) & 1u, err, kErrWaitFull)) {
           atomicExch(&aborted, 1u);
           break;
         }
         tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
         const uint32_t base = smem_addr(smem + s * Cfg::STAGE_BYTES);
         const uint32_t a_hi = base, a_lo = base + Cfg::A_BYTES;
         const uint32_t b_hi = base + 2 * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
@@ -222,43 +254,60 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint64_t dal = umma_desc_kmajor(a_lo + off, Cfg::SWZ);
           const uint64_t dbh = umma_desc_kmajor(b_hi + off, Cfg::SWZ);
           const uint64_t dbl = umma_desc_kmajor(b_lo + off, Cfg::SWZ);
-          umma_tf32(tmem_base, dal, dbh, IDESC, (kb | kk) != 0u ? 1u : 0u);
-          umma_tf32(tmem_base, dah, dbl, IDESC, 1u);
-          umma_tf32(tmem_base, dah, dbh, IDESC, 1u);
+          umma_tf32(d_tmem, dal, dbh, IDESC, (in_chunk | kk) != 0u ? 1u : 0u);
+          umma_tf32(d_tmem, dah, dbl, IDESC, 1u);
+          umma_tf32(d_tmem, dah, dbh, IDESC, 1u);
         }
-        umma_commit(&empty_bar[s]);
+        umma_commit(&empty_bar[s]);  // frees the smem stage when these MMAs finish
+        if (in_chunk == KBC - 1 || kb == num_kb - 1) umma_commit(&acc_full[buf]);
       }
       consumed_kb = kb;
-      mma_issued = kb;
-      umma_commit(&accum_bar);  // arrives once every MMA above has completed
+      umma_commit(&drain_bar);  // arrives when every MMA issued above has completed
     }
   } else {
-    // ---------------- epilogue: warps 2..5 own TMEM lane quarters (warp % 4)
+    // ---------------- epilogue: warps 2..9; (warp % 4) owns a TMEM lane quarter,
+    // (warp - 2) / 4 selects which 128 of the 256 columns this warp sums.
     const uint32_t q = warp & 3u;
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(&accum_bar, 0, err, kErrWaitAccum));
-    tc_fence_after();
+    const uint32_t h = (warp - 2u) >> 2;
+    const uint32_t lane_addr = (q * 32u) << 16;
+    float run[128];
+#pragma unroll
+    for (int j = 0; j < 128; ++j) run[j] = 0.f;
+    bool ok = true;
+    for (uint32_t ch = 0; ch < num_chunks; ++ch) {
+      const uint32_t buf = ch & 1u;
+      ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (ch >> 1) & 1u, err, kErrWaitAccum));
+      if (!ok) {
+        if (lane == 0) atomicExch(&aborted, 1u);
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (uint32_t g = 0; g < 4; ++g) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + buf * BN + h * 128u + g * 32u, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) run[g * 32 + j] += __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
     if (ok && num_kb > 0) {
       const uint32_t row = tile_m * BM + q * 32 + lane;
-      const uint32_t col0 = tile_n * BN;
+      const uint32_t col0 = tile_n * BN + h * 128u;
       const bool vec_ok = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0);
-#pragma unroll 1
-      for (uint32_t chunk = 0; chunk < BN / 32; ++chunk) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + ((q * 32u) << 16) + chunk * 32u, r);
-        tmem_ld_wait();
-        const uint32_t cb = col0 + chunk * 32;
-        if (row < m && cb < n) {
-          float* dst = c + static_cast<uint64_t>(row) * ldc + cb;
-          if (vec_ok && cb + 32 <= n) {
+      if (row < m && col0 < n) {
+        float* dst = c + static_cast<uint64_t>(row) * ldc + col0;
+        if (vec_ok && col0 + 128 <= n) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-          } else {
+          for (int j = 0; j < 128; j += 4)
+            *reinterpret_cast<float4*>(dst + j) = make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
+        } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (cb + j < n) dst[j] = __uint_as_float(r[j]);
-          }
+          for (int j = 0; j < 128; ++j)
+            if (col0 + j < n) dst[j] = run[j];
         }
       }
     }
@@ -266,16 +315,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  // Teardown.  On an aborted run, wait (bounded) for copies and MMAs still in
-  // flight before the CTA releases its shared memory and TMEM.
-  if (aborted) {
-    if (threadIdx.x == 0) {
-      for (uint32_t kb = consumed_kb; kb < issued_kb; ++kb)
-        if (!mbar_wait(&full_bar[kb % S], (kb / S) & 1u, err, kErrWaitDrain)) break;
-    }
-    if (threadIdx.x == 32 && mma_issued > 0) mbar_wait(&accum_bar, 0, err, kErrWaitDrain);
-    __syncthreads();
+  // Teardown.  The MMA thread waits (bounded) until all its MMAs completed; an
+  // aborted CTA also waits for TMA copies still in flight before it exits.
+  if (threadIdx.x == 32) mbar_wait(&drain_bar, 0, err, kErrWaitDrain);
+  if (aborted && threadIdx.x == 0) {
+    for (uint32_t kb = consumed_kb; kb < issued_kb; ++kb)
+      if (!mbar_wait(&full_bar[kb % S], (kb / S) & 1u, err, kErrWaitDrain)) break;
   }
+  __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
