@@ -50,7 +50,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--m", type=int, default=8192)
@@ -75,7 +75,7 @@ def peaks() -> tuple[dict, str]:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms during the timed region."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -89,7 +89,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -166,7 +166,7 @@ def run_reference(args) -> None:
     O.cpu_sgemm_f32(a, b, m, n, k, rows=slice(0, threads), threads=threads)
     t_probe = time.perf_counter() - t0
     budget = 150.0 / max(1, args.steps + args.warmup)
-    rows = min(m, threads * max(1, int(budget / max(t_probe, 1e-6))))
+    rows = min(m, max(1, int(threads * budget / max(t_probe, 1e-6))))
     for _ in range(args.warmup):
         O.cpu_sgemm_f32(a, b, m, n, k, rows=slice(0, rows), threads=threads)
     times = []

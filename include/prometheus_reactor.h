@@ -546,8 +546,10 @@ enum {
 };
 
 /* C = A * B on device pointers (row-major, ld = k / n / n), enqueued on
-   `stream` (a cudaStream_t; NULL = the handle's stream).  Returns immediately
-   after enqueue; scratch buffers for the TF32 split live in the handle. */
+   `stream` (a cudaStream_t; NULL = the CUDA default stream).  Returns right
+   after the enqueue.  The TF32 split scratch lives in the handle and is shared
+   by every call on it: calls on one handle from different streams must be
+   ordered by the caller. */
 PROM_REACTOR_API int oct_b200_sgemm_device(void* handle, const float* d_a, const float* d_b, float* d_c,
                                            uint32_t m, uint32_t n, uint32_t k, uint32_t variant,
                                            void* stream, int* out_detail_code);
@@ -571,7 +573,7 @@ PROM_REACTOR_API int oct_b200_rmsnorm_device(void* handle, const float* d_in, co
                                              float* d_inv_rms, uint32_t rows, uint32_t width, float epsilon,
                                              void* stream, int* out_detail_code);
 
-/* Waits for `stream` (NULL: only the handle's own stream), then reads and
+/* Waits for `stream` (NULL: the CUDA default stream), then reads and
    clears the device status words the kernels write: returns PROM_ERROR with
    OCT_B200_DETAIL_DEVICE_TIMEOUT if a bounded in-kernel wait gave up, or
    PROM_REDUCTION_DETAIL_NONFINITE_INPUT if a reduction saw NaN/Inf. */

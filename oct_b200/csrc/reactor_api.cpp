@@ -51,7 +51,10 @@ struct DevBuf {
   void* aligned() const { return reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023)); }
   cudaError_t ensure(uint64_t bytes, cudaStream_t s) {
     if (bytes <= cap && raw != nullptr) return cudaSuccess;
-    cudaError_t e = cudaStreamSynchronize(s);
+    // Kernels on any stream may still read the old block (device entry points
+    // accept caller streams), so growth waits for the whole device.
+    (void)s;
+    cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return e;
     if (raw != nullptr) cudaFree(raw);
     raw = nullptr;
@@ -1130,7 +1133,7 @@ int oct_b200_sgemm_device_ld(void* handle, const float* d_a, uint64_t lda, const
     }
     if (m == 0 || n == 0 || k == 0) return PROM_OK;
     std::lock_guard<std::mutex> lock(rt->mu);
-    cudaStream_t s = stream != nullptr ? static_cast<cudaStream_t>(stream) : rt->stream;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);  // NULL is the CUDA default stream
     const int d = enqueue_sgemm(rt, d_a, lda, d_b, ldb, d_c, ldc, m, n, k, variant, s);
     if (d != 0) {
       if (out_detail_code) *out_detail_code = d;
@@ -1162,7 +1165,7 @@ int oct_b200_reduction_device(void* handle, const float* d_in, float* d_out, uin
       return PROM_ERROR;
     }
     std::lock_guard<std::mutex> lock(rt->mu);
-    cudaStream_t s = stream != nullptr ? static_cast<cudaStream_t>(stream) : rt->stream;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);  // NULL is the CUDA default stream
     const cudaError_t e = oct::row_reduce(d_in, d_out, rows, width, operation, rt->nonfinite_word(), rt->err_word(), s);
     if (e != cudaSuccess) {
       if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
@@ -1189,7 +1192,7 @@ int oct_b200_rmsnorm_device(void* handle, const float* d_in, const float* d_weig
       return PROM_ERROR;
     }
     std::lock_guard<std::mutex> lock(rt->mu);
-    cudaStream_t s = stream != nullptr ? static_cast<cudaStream_t>(stream) : rt->stream;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);  // NULL is the CUDA default stream
     const cudaError_t e = oct::rmsnorm(d_in, width, d_weight, d_out, d_inv_rms, rows, width, epsilon,
                                        rt->nonfinite_word(), rt->err_word(), s);
     if (e != cudaSuccess) {
@@ -1209,7 +1212,7 @@ int oct_b200_sync_status(void* handle, void* stream, int* out_detail_code) {
     if (rt == nullptr) return PROM_INVALID_HANDLE;
     if (!rt->available) return PROM_ERROR;
     std::lock_guard<std::mutex> lock(rt->mu);
-    if (stream != nullptr && cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+    if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) {
       if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
       return PROM_ERROR;
     }
