@@ -307,7 +307,11 @@ def run_ours(args) -> None:
     value = flops * world * args.steps / (ms_max * 1e-3) / 1e12
 
     pk, pk_kind = peaks()
-    tensor_peak = pk["bf16_tflops"] / 6.0
+    # The main kernel is timed inside a long continuous loop (the power cap
+    # engages), so the sustained measured peak is the denominator; the burst
+    # fraction is reported beside it.
+    tensor_peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
+    tensor_peak_burst = pk["bf16_tflops"] / 6.0
     main_per_launch_ms = main_ms / max(1, launches)
     achieved = flops / (main_per_launch_ms * 1e-3) / 1e12
     traffic = None
@@ -389,7 +393,10 @@ def run_ours(args) -> None:
                 "unit": "TFLOP/s",
                 "frac": achieved / tensor_peak,
                 "traffic": traffic,
-                "peak_source": f"{pk_kind}: bf16_tflops {pk['bf16_tflops']} / 2 (tf32 rate) / 3 (products)",
+                "peak_source": (f"{pk_kind}: bf16_tflops_sustained {pk.get('bf16_tflops_sustained')} / 2 (tf32 rate) "
+                                "/ 3 (products); kernel timed inside a continuous 100-step loop"),
+                "frac_of_burst_peak": achieved / tensor_peak_burst,
+                "burst_peak": tensor_peak_burst,
                 "algorithmic_flops_per_launch": flops,
                 "main_kernel_ms_per_launch": main_per_launch_ms,
                 "split_pass_ms_per_launch": split_ms / max(1, launches),
