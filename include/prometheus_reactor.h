@@ -152,6 +152,7 @@ enum {
   OCT_B200_DETAIL_OUT_OF_MEMORY = -7003,     /* device allocation failed */
   OCT_B200_DETAIL_BAD_VARIANT = -7004,       /* unknown kernel variant id */
   OCT_B200_DETAIL_UNALIGNED = -7005,         /* device pointer not 16-byte aligned */
+  OCT_B200_DETAIL_NOALLOC_TOO_LARGE = -7006, /* product needs more than the fixed no-alloc scratch */
 };
 
 /* ---- reductions (reactor_api.h:375-581) ---- */
@@ -578,6 +579,25 @@ PROM_REACTOR_API int oct_b200_rmsnorm_device(void* handle, const float* d_in, co
    OCT_B200_DETAIL_DEVICE_TIMEOUT if a bounded in-kernel wait gave up, or
    PROM_REDUCTION_DETAIL_NONFINITE_INPUT if a reduction saw NaN/Inf. */
 PROM_REACTOR_API int oct_b200_sync_status(void* handle, void* stream, int* out_detail_code);
+
+/* No counterpart in the reference.  C = A * B on device pointers (row-major,
+   leading dimensions lda >= k, ldb >= n, ldc >= n) with the tcgen05 3xTF32
+   kernel, for callers that cannot allocate device memory: it needs no handle
+   and calls no cudaMalloc, cudaFree or allocating library routine.  The TF32
+   split scratch and the kernel status word live in one fixed 64 MiB device
+   array that every GPU loading the library holds until the process exits.
+   Limit: 8 * (roundup(m,128) + roundup(n,256)) * roundup(k,32) bytes must fit
+   in 64 MiB (any m, n, k <= 2048 does); larger products are rejected with
+   PROM_ERROR and OCT_B200_DETAIL_NOALLOC_TOO_LARGE, and C is left untouched.
+   The first call on each device looks up the array's device address, so make
+   that first call before any stream capture.  The call waits on `stream` (NULL
+   = the CUDA default stream) until the product is done and reports an
+   in-kernel timeout as OCT_B200_DETAIL_DEVICE_TIMEOUT.  Every call shares the
+   one array, so calls whose work overlaps on the GPU (from several host
+   threads or streams) race and must be serialised by the caller. */
+PROM_REACTOR_API int oct_b200_sgemm_device_noalloc(const float* d_a, uint64_t lda, const float* d_b, uint64_t ldb,
+                                                   float* d_c, uint64_t ldc, uint32_t m, uint32_t n, uint32_t k,
+                                                   void* stream, int* out_detail_code);
 
 /* Per-launch timing of the tensor-core SGEMM: when enabled, CUDA events are
    recorded on the launch stream around the TF32 split pass and the main

@@ -34,6 +34,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "../../include/prometheus_reactor.h"
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -384,6 +385,37 @@ cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, co
 
 }  // namespace
 
+// ------------------------------------------------------------------ no-allocation variant
+// Scratch for oct_b200_sgemm_device_noalloc: some callers cannot call
+// cudaMalloc at all (for example a serving process whose fixed memory plan
+// hands all of HBM to its own pool, or code that must not trigger the device
+// synchronisation an allocation implies).  For them the TF32 split buffers and
+// the kernel status word live in this fixed array instead of in a handle.  It
+// is reserved on every GPU that loads the library, until the process exits.
+constexpr uint64_t kNoAllocSplitBytes = 64ull << 20;  // hi/lo copies of A and B^T
+constexpr uint64_t kNoAllocStatusBytes = 1024;        // status word, then padding to 1 KiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocStatusBytes + kNoAllocSplitBytes + 1024];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_base[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device.  (The array's name in host code is only a host-side stand-in.)
+cudaError_t noalloc_base(int dev, unsigned char** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_base[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_base[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = g_noalloc_base[dev];
+  return cudaSuccess;
+}
+}  // namespace
+
 SplitDims split_dims(uint32_t m, uint32_t n, uint32_t k) {
   return SplitDims{round_up(m, BM), round_up(n, BN), round_up(k, KPAD)};
 }
@@ -422,3 +454,52 @@ cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb,
 }
 
 }  // namespace oct
+
+// C = A * B on device pointers with no allocation of any kind; see the header.
+extern "C" int oct_b200_sgemm_device_noalloc(const float* d_a, uint64_t lda, const float* d_b, uint64_t ldb,
+                                             float* d_c, uint64_t ldc, uint32_t m, uint32_t n, uint32_t k,
+                                             void* stream, int* out_detail_code) {
+  using namespace oct;
+  auto fail = [&](int rc, int detail) {
+    if (out_detail_code != nullptr) *out_detail_code = detail;
+    return rc;
+  };
+  try {
+    if (out_detail_code != nullptr) *out_detail_code = 0;
+    if (d_a == nullptr || d_b == nullptr || d_c == nullptr || lda < k || ldb < n || ldc < n)
+      return fail(PROM_ERROR, PROM_ERROR);
+    if (m == 0 || n == 0 || k == 0) return PROM_OK;
+    if (sgemm_tc_scratch_bytes(m, n, k) > kNoAllocSplitBytes)
+      return fail(PROM_ERROR, OCT_B200_DETAIL_NOALLOC_TOO_LARGE);
+    int dev = 0, major = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices ||
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess || major != 10) {
+      (void)cudaGetLastError();
+      return fail(PROM_ERROR, PROM_DETAIL_CAPABILITY_MISMATCH);
+    }
+    unsigned char* base = nullptr;
+    if (noalloc_base(dev, &base) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return fail(PROM_ERROR, OCT_B200_DETAIL_CUDA_ERROR);
+    }
+    unsigned int* status = reinterpret_cast<unsigned int*>(base);
+    void* split = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(base) + kNoAllocStatusBytes + 1023) &
+                                          ~uintptr_t(1023));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // The array keeps the previous call's contents: the status word must start
+    // at zero; the split buffers (padding included) are fully rewritten.
+    cudaError_t e = cudaMemsetAsync(status, 0, sizeof(unsigned int), s);
+    if (e == cudaSuccess) e = sgemm_tc(d_a, lda, d_b, ldb, d_c, ldc, m, n, k, split, status, 16, s);
+    unsigned int host_status = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&host_status, status, sizeof(host_status), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return fail(PROM_ERROR, OCT_B200_DETAIL_CUDA_ERROR);
+    }
+    if (host_status != 0) return fail(PROM_ERROR, OCT_B200_DETAIL_DEVICE_TIMEOUT);
+    return PROM_OK;
+  } catch (...) {
+    return fail(PROM_INTERNAL_ERROR, OCT_B200_DETAIL_CUDA_ERROR);
+  }
+}

@@ -270,6 +270,8 @@ SIGNATURES = {
     "oct_b200_reduction_device": (C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _i32p]),
     "oct_b200_rmsnorm_device": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, C.c_float, _vp, _i32p]),
     "oct_b200_sync_status": (C.c_int, [_vp, _vp, _i32p]),
+    "oct_b200_sgemm_device_noalloc": (
+        C.c_int, [_vp, _u64, _vp, _u64, _vp, _u64, _u32, _u32, _u32, _vp, _i32p]),
     "oct_b200_set_kernel_timing": (C.c_int, [_vp, C.c_int]),
     "oct_b200_read_kernel_timing": (
         C.c_int, [_vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_uint32)]),
