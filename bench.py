@@ -227,6 +227,8 @@ def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
         if not st.ok:
             raise RuntimeError(f"reduction status {st}")
         del x, y_full, y_row, inv
+    # Transformer blocks at BASELINE configs[3] / configs[4] (random init, synthetic tokens)
+    out.extend(block_measurements(rt, torch, stream))
     # FMA control and the 32-deep tensor-core variant at the headline shape
     m = n = k = 8192
     g = torch.Generator(device="cuda").manual_seed(7)
@@ -246,6 +248,52 @@ def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
                     "TFLOP/s": round(2.0 * m * n * k / (ms * 1e-3) / 1e12, 2)})
     rt.set_kernel_timing(False)
     return out
+
+
+def block_measurements(rt, torch, stream, iters: int = 5) -> list[dict]:
+    """Tokens/s of one block forward at the BASELINE shapes, plus its tensor-peak fraction."""
+    from oct_b200 import reactor as R
+    from oracle import blocks as OB  # used only for the shapes and the flop count
+    pk, _ = peaks()
+    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
+    res = []
+    for name, cfg, batch in (("gemma_block", OB.gemma_config(), 4), ("dit_block", OB.dit_config(), 2)):
+        fam = R.BLOCK_GEMMA if cfg.family == OB.GEMMA else R.BLOCK_DIT
+        blk = rt.block(fam, hidden=cfg.hidden, heads=cfg.heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                       ffn=cfg.ffn, seq_len=cfg.seq_len, max_batch=batch, eps=cfg.eps, rope_base=cfg.rope_base,
+                       grid_w=cfg.grid_w, rope_frame=cfg.rope_frame)
+        g = torch.Generator(device="cuda").manual_seed(99)
+        weights = {}
+        for wname, shape in OB.weight_shapes(cfg).items():
+            t = torch.randn(*shape, device="cuda", generator=g)
+            weights[wname] = (t * 0.02 + 1.0) if len(shape) == 1 and wname != "ada_b" else (
+                t * 0.0 if wname == "ada_b" else t * 0.02)
+        blk.set_weights(weights)
+        del weights
+        T = batch * cfg.seq_len
+        x = torch.randn(T, cfg.hidden, device="cuda", generator=g)
+        y = torch.empty_like(x)
+        ts = [500.0, 250.0][:batch] if cfg.family == OB.DIT else None
+        for _ in range(2):
+            blk.forward_device(x, y, batch, ts, stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            blk.forward_device(x, y, batch, ts, stream)
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        flops = OB.flops_per_forward(cfg, batch)
+        res.append({"kernel": name, "batch": batch, "seq": cfg.seq_len, "hidden": cfg.hidden, "ms": round(ms, 3),
+                    "tokens/s": round(T / (ms * 1e-3), 1), "TFLOP/s": round(flops / (ms * 1e-3) / 1e12, 2),
+                    "frac_of_3xtf32_peak": round(flops / (ms * 1e-3) / 1e12 / peak, 3)})
+        blk.close()
+        del x, y
+        torch.cuda.empty_cache()
+    st = rt.sync_status()
+    if not st.ok:
+        raise RuntimeError(f"block status {st}")
+    return res
 
 
 def run_ours(args) -> None:

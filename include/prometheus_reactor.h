@@ -153,6 +153,11 @@ enum {
   OCT_B200_DETAIL_BAD_VARIANT = -7004,       /* unknown kernel variant id */
   OCT_B200_DETAIL_UNALIGNED = -7005,         /* device pointer not 16-byte aligned */
   OCT_B200_DETAIL_NOALLOC_TOO_LARGE = -7006, /* product needs more than the fixed no-alloc scratch */
+  OCT_B200_DETAIL_BLOCK_INVALID = -7010,     /* block configuration / slot / count rejected */
+  OCT_B200_DETAIL_BLOCK_ALLOC = -7011,       /* block weights or workspaces could not be allocated */
+  OCT_B200_DETAIL_BLOCK_NCCL = -7012,        /* tensor-parallel communicator unavailable */
+  OCT_B200_DETAIL_BLOCK_NOT_FOUND = -7013,   /* unknown block id */
+  OCT_B200_DETAIL_BLOCK_EXEC = -7014,        /* a block kernel or collective failed */
 };
 
 /* ---- reductions (reactor_api.h:375-581) ---- */
@@ -562,6 +567,17 @@ PROM_REACTOR_API int oct_b200_sgemm_device_ld(void* handle, const float* d_a, ui
                                               uint64_t ldb, float* d_c, uint64_t ldc, uint32_t m, uint32_t n,
                                               uint32_t k, uint32_t variant, void* stream, int* out_detail_code);
 
+/* Strided batch of products C_i = A_i * op(B_i) for i < batch, X_i = X + i *
+   stride_x (element strides; 0 shares an operand across the batch).  With
+   b_trans != 0, B_i is [n][k] row-major (ldb >= k) and op(B_i) = B_i^T;
+   otherwise B_i is [k][n] (ldb >= n).  The attention score (Q K^T) and
+   aggregation (P V) products of the transformer block use this. */
+PROM_REACTOR_API int oct_b200_sgemm_batched_device(void* handle, const float* d_a, uint64_t lda, uint64_t stride_a,
+                                                   const float* d_b, uint64_t ldb, uint64_t stride_b, uint32_t b_trans,
+                                                   float* d_c, uint64_t ldc, uint64_t stride_c, uint32_t batch,
+                                                   uint32_t m, uint32_t n, uint32_t k, uint32_t variant, void* stream,
+                                                   int* out_detail_code);
+
 /* Row reductions on device pointers.  operation: PROM_REDUCTION_OPERATION_*.
    SUM/MAX write `rows` floats, SOFTMAX writes rows*width floats. */
 PROM_REACTOR_API int oct_b200_reduction_device(void* handle, const float* d_in, float* d_out, uint32_t rows,
@@ -606,6 +622,71 @@ PROM_REACTOR_API int oct_b200_sgemm_device_noalloc(const float* d_a, uint64_t ld
 PROM_REACTOR_API int oct_b200_set_kernel_timing(void* handle, int enable);
 PROM_REACTOR_API int oct_b200_read_kernel_timing(void* handle, double* split_ms_total, double* main_ms_total,
                                                  uint32_t* launches);
+
+/* ---- transformer block (extension; the reference's closest counterpart is the
+   model-block lifecycle create -> upload_weights -> execute -> destroy,
+   reactor_api.h:2713-2784, which is specific to Z-Image checkpoints) ---- */
+enum { OCT_B200_BLOCK_GEMMA = 1u, OCT_B200_BLOCK_DIT = 2u };
+
+/* Weight slots.  Matrices are [in][out] row-major fp32 (canonicalLinear's
+   layout, canonical_reference.go:156-175); gains and biases are vectors.
+   Gemma: WQKV = [hidden][(heads + 2*kv_heads) * head_dim] (q heads | k | v);
+          WGU = [hidden][2*ffn] (gate | up); WO = [heads*head_dim][hidden];
+          WD = [ffn][hidden].
+   DiT:   ADA_W = [256][6*hidden] (scale_a | gate_a | scale_m | gate_m | shift_a | shift_m),
+          ADA_B = [6*hidden]; WQKV = [hidden][3*heads*128]; W13 = [hidden][2*ffn]
+          (w1 | w3); W2 = [ffn][hidden]; Q_NORM, K_NORM = [128]. */
+enum {
+  OCT_B200_GEMMA_NORM1 = 0, OCT_B200_GEMMA_WQKV = 1, OCT_B200_GEMMA_WO = 2, OCT_B200_GEMMA_NORM2 = 3,
+  OCT_B200_GEMMA_WGU = 4, OCT_B200_GEMMA_WD = 5,
+};
+enum {
+  OCT_B200_DIT_ADA_W = 0, OCT_B200_DIT_ADA_B = 1, OCT_B200_DIT_ATTN_NORM1 = 2, OCT_B200_DIT_WQKV = 3,
+  OCT_B200_DIT_Q_NORM = 4, OCT_B200_DIT_K_NORM = 5, OCT_B200_DIT_WO = 6, OCT_B200_DIT_ATTN_NORM2 = 7,
+  OCT_B200_DIT_FFN_NORM1 = 8, OCT_B200_DIT_W13 = 9, OCT_B200_DIT_W2 = 10, OCT_B200_DIT_FFN_NORM2 = 11,
+};
+
+/* heads and ffn are THIS rank's share under tensor parallelism (tp_world > 1):
+   the caller passes column shards of WQKV / WGU (W13) and row shards of WO /
+   WD (W2); the two row-parallel products are all-reduced over NCCL inside
+   the forward.  Gemma requires kv_heads == 1 (MQA; the KV head is replicated
+   on every rank).  DiT requires head_dim == 128 and rope axes (32, 48, 48). */
+typedef struct OctB200BlockConfig {
+  uint32_t struct_size;
+  uint32_t family;
+  uint32_t hidden;
+  uint32_t heads;
+  uint32_t kv_heads;
+  uint32_t head_dim;
+  uint32_t ffn;
+  uint32_t seq_len;    /* tokens per sequence (Gemma) or per image (DiT) */
+  uint32_t max_batch;  /* sequences / images per forward the workspaces are sized for */
+  float eps;           /* block RMSNorm epsilon (Gemma 1e-6, DiT 1e-5) */
+  float rope_base;     /* Gemma base (10000), DiT theta (256) */
+  uint32_t grid_w;     /* DiT: image tokens per grid row */
+  uint32_t rope_frame; /* DiT: frame coordinate of the image tokens */
+  uint32_t tp_rank;
+  uint32_t tp_world;
+  uint8_t nccl_id[128]; /* tp_world > 1: the same oct_b200_nccl_unique_id bytes on every rank */
+} OctB200BlockConfig;
+
+/* ncclGetUniqueId (NCCL is dlopen'ed; nothing links it).  Rank 0 calls this
+   and shares the 128 bytes with the other ranks. */
+PROM_REACTOR_API int oct_b200_nccl_unique_id(uint8_t* out_128_bytes);
+PROM_REACTOR_API int oct_b200_block_create(void* handle, const OctB200BlockConfig* config, uint64_t* out_block_id,
+                                           int* out_detail_code);
+PROM_REACTOR_API int oct_b200_block_set_weight(void* handle, uint64_t block_id, uint32_t slot, const float* data,
+                                               uint64_t element_count, uint32_t data_on_device);
+/* y = block(x), x and y device buffers [batch * seq_len][hidden]; timesteps
+   (DiT only) is a HOST array of `batch` floats.  Enqueued on `stream` (NULL =
+   CUDA default stream). */
+PROM_REACTOR_API int oct_b200_block_forward_device(void* handle, uint64_t block_id, const float* d_x, float* d_y,
+                                                   uint32_t batch, const float* timesteps, void* stream,
+                                                   int* out_detail_code);
+/* Same with host buffers: copies x in and y out, returns when y is written. */
+PROM_REACTOR_API int oct_b200_block_forward(void* handle, uint64_t block_id, const float* x, float* y, uint32_t batch,
+                                            const float* timesteps, int* out_detail_code);
+PROM_REACTOR_API int oct_b200_block_destroy(void* handle, uint64_t block_id);
 
 /* Library build identity, for diagnostics. */
 PROM_REACTOR_API const char* oct_b200_build_info(void);

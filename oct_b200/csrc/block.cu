@@ -1,0 +1,627 @@
+// block.cu -- the transformer block of Oct's Prometheus path, B200-first.
+//
+// Two block families, both fp32 end to end with every matrix product on the
+// tcgen05 3xTF32 tensor-core SGEMM (sgemm_tc.cu):
+//
+//  * DiT (Z-Image style), following `runCanonicalNoiseRefiner0`
+//    (internal/prometheus/zimage/canonical_reference.go:377-479): adaLN from a
+//    sinusoidal timestep embedding -> RMSNorm + modulation -> fused QKV ->
+//    per-head Q/K RMSNorm -> 3-axis interleaved RoPE -> exact bidirectional
+//    attention -> out projection -> RMSNorm -> tanh-gated residual -> FFN norm +
+//    modulation -> W1|W3 -> SiLU gate -> W2 -> RMSNorm -> gated residual.
+//    BASELINE widens the reference's 4 x hidden adaLN to 6 x hidden with shifts.
+//  * Gemma-shaped decoder: RMSNorm -> fused QKV (MQA: every query head uses KV
+//    head 0) -> half-split RoPE (`cpuGemma4e2bRope`, gemma4e2b_m1_rtx.go:834-861,
+//    without its BF16 storage rounding) -> causal attention with scale
+//    1/sqrt(head_dim) (`cpuGemma4e2bRawScores`, :863-883) -> out projection +
+//    residual -> RMSNorm -> gate|up -> GeGLU (gelu_tanh) -> down + residual.
+//
+// Data path per forward (T = batch * seq tokens, all buffers owned by the block):
+//   norms, RoPE, softmax and gated activations are one-pass fused kernels; the
+//   residual adds of the Gemma block ride in the GEMM epilogue; weights are
+//   split to TF32 hi/lo once, at upload.  Attention materialises the scores of
+//   one sequence's heads (B*H*S*S floats, 3.2 GB for the DiT config) and runs
+//   Q K^T and P V as strided-batched tensor-core products.
+//   Tensor parallel (tp_world > 1): each rank holds H/tp heads and F/tp FFN
+//   columns; the two row-parallel products (out projection, down/W2) produce
+//   partial sums that are all-reduced over NCCL on the block's stream.
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <dlfcn.h>
+#include <mutex>
+#include <vector>
+
+#include "block.h"
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace oct {
+namespace {
+
+constexpr int NT = 256;
+
+__device__ __forceinline__ double block_sum_d(double v, double* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double t = 0.0;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) t += sh[i];
+  return t;
+}
+
+__device__ __forceinline__ float block_max_f(float v, float* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = sh[0];
+#pragma unroll
+  for (int i = 1; i < NT / 32; ++i) t = fmaxf(t, sh[i]);
+  return t;
+}
+
+// Fused row norm, one CTA per row (width <= 16 * 256):
+//   y = x * inv_rms * g                              (CanonicalRMSNorm order)
+//   y = y * mul[item] + add[item]                    (optional: adaLN modulation)
+//   y = res + gate[item] * y   or   y = res + y      (optional: gated residual)
+// `item` = row / rows_per_item indexes the per-batch-item vectors (stride mod_stride).
+constexpr int NORM_VPT = 16;
+__global__ void __launch_bounds__(NT) norm_fused_kernel(const float* __restrict__ x, uint64_t ldx,
+                                                        const float* __restrict__ g, float eps,
+                                                        const float* __restrict__ mul, const float* __restrict__ add,
+                                                        const float* __restrict__ res, uint64_t ldres,
+                                                        const float* __restrict__ gate, uint64_t mod_stride,
+                                                        uint32_t rows_per_item, float* __restrict__ out,
+                                                        uint64_t ldo, uint32_t rows, uint32_t width) {
+  __shared__ double sh[NT / 32];
+  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* xr = x + r * ldx;
+    float v[NORM_VPT];
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < NORM_VPT; ++i) {
+      const uint32_t c = threadIdx.x + i * NT;
+      v[i] = c < width ? xr[c] : 0.f;
+      ss += static_cast<double>(v[i]) * v[i];
+    }
+    ss = block_sum_d(ss, sh);
+    const float inv = static_cast<float>(1.0 / sqrt(ss / static_cast<double>(width) + static_cast<double>(eps)));
+    const uint64_t mo = static_cast<uint64_t>(r / rows_per_item) * mod_stride;
+#pragma unroll
+    for (int i = 0; i < NORM_VPT; ++i) {
+      const uint32_t c = threadIdx.x + i * NT;
+      if (c >= width) continue;
+      float y = v[i] * inv * g[c];
+      if (mul != nullptr) y = y * mul[mo + c];
+      if (add != nullptr) y = y + add[mo + c];
+      if (res != nullptr) y = res[r * ldres + c] + (gate != nullptr ? gate[mo + c] * y : y);
+      out[r * ldo + c] = y;
+    }
+  }
+}
+
+// Half-split RoPE in place over `heads` heads of width hd starting at column
+// col0 of each row: pairs (i, i + hd/2), table cos/sin[pos][hd/2], pos = row % seq.
+__global__ void rope_half_kernel(float* __restrict__ buf, uint64_t ld, uint32_t col0, uint32_t heads, uint32_t hd,
+                                 const float* __restrict__ cos_t, const float* __restrict__ sin_t, uint32_t seq,
+                                 uint32_t rows) {
+  const uint32_t half = hd / 2;
+  const uint64_t total = static_cast<uint64_t>(rows) * heads * half;
+  for (uint64_t idx = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t i = static_cast<uint32_t>(idx % half);
+    const uint64_t rh = idx / half;
+    const uint32_t head = static_cast<uint32_t>(rh % heads);
+    const uint32_t row = static_cast<uint32_t>(rh / heads);
+    float* p = buf + row * ld + col0 + head * hd;
+    const uint32_t pos = row % seq;
+    const float c = cos_t[pos * half + i], s = sin_t[pos * half + i];
+    const float a = p[i], b = p[i + half];
+    p[i] = a * c - b * s;
+    p[i + half] = b * c + a * s;
+  }
+}
+
+// Per-head RMSNorm (width 128, gain g, eps) then 3-axis interleaved RoPE with
+// table cos/sin[pos][64] in place; one warp per (row, head), 4 channels a lane.
+// Covers `heads` heads starting at column col0 (Q then K are two launches).
+__global__ void qk_norm_rope3_kernel(float* __restrict__ buf, uint64_t ld, uint32_t col0, uint32_t heads,
+                                     const float* __restrict__ g, float eps, const float* __restrict__ cos_t,
+                                     const float* __restrict__ sin_t, uint32_t seq, uint32_t rows) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t warps = static_cast<uint64_t>(rows) * heads;
+  for (uint64_t wi = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; wi < warps;
+       wi += static_cast<uint64_t>(gridDim.x) * blockDim.x / 32) {
+    const uint32_t head = static_cast<uint32_t>(wi % heads);
+    const uint32_t row = static_cast<uint32_t>(wi / heads);
+    float* p = buf + row * ld + col0 + head * 128 + lane * 4;
+    float4 v = *reinterpret_cast<float4*>(p);
+    double ss = static_cast<double>(v.x) * v.x + static_cast<double>(v.y) * v.y + static_cast<double>(v.z) * v.z +
+                static_cast<double>(v.w) * v.w;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = static_cast<float>(1.0 / sqrt(ss / 128.0 + static_cast<double>(eps)));
+    const float4 gg = *reinterpret_cast<const float4*>(g + lane * 4);
+    v.x = v.x * inv * gg.x;
+    v.y = v.y * inv * gg.y;
+    v.z = v.z * inv * gg.z;
+    v.w = v.w * inv * gg.w;
+    const uint32_t pos = row % seq;
+    const uint32_t pair0 = lane * 2;  // global pair index of (v.x, v.y); (v.z, v.w) is pair0 + 1
+    const float c0 = cos_t[pos * 64 + pair0], s0 = sin_t[pos * 64 + pair0];
+    const float c1 = cos_t[pos * 64 + pair0 + 1], s1 = sin_t[pos * 64 + pair0 + 1];
+    float4 o;
+    o.x = v.x * c0 - v.y * s0;
+    o.y = v.x * s0 + v.y * c0;
+    o.z = v.z * c1 - v.w * s1;
+    o.w = v.z * s1 + v.w * c1;
+    *reinterpret_cast<float4*>(p) = o;
+  }
+}
+
+// Scaled (optionally causal) softmax of score rows in place, one CTA per row
+// (row width <= 16 * 256).  Row r is query position r % seq; causal rows keep
+// keys 0..pos and write exact zeros beyond.  exp(s - max) in fp32, the sum in
+// binary64, the quotient rounded once.
+__global__ void __launch_bounds__(NT) attn_softmax_kernel(float* __restrict__ s, uint32_t rows, uint32_t width,
+                                                          uint32_t seq, float scale, int causal) {
+  __shared__ double shd[NT / 32];
+  __shared__ float shf[NT / 32];
+  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    float* row = s + static_cast<uint64_t>(r) * width;
+    const uint32_t limit = causal ? (r % seq) + 1 : width;
+    float v[NORM_VPT];
+    float mx = -FLT_MAX;
+#pragma unroll
+    for (int i = 0; i < NORM_VPT; ++i) {
+      const uint32_t c = threadIdx.x + i * NT;
+      v[i] = (c < limit) ? row[c] * scale : -FLT_MAX;
+      mx = fmaxf(mx, v[i]);
+    }
+    mx = block_max_f(mx, shf);
+    double sum = 0.0;
+#pragma unroll
+    for (int i = 0; i < NORM_VPT; ++i) {
+      const uint32_t c = threadIdx.x + i * NT;
+      v[i] = (c < limit) ? expf(v[i] - mx) : 0.f;
+      sum += static_cast<double>(v[i]);
+    }
+    sum = block_sum_d(sum, shd);
+    const double inv = 1.0 / sum;
+#pragma unroll
+    for (int i = 0; i < NORM_VPT; ++i) {
+      const uint32_t c = threadIdx.x + i * NT;
+      if (c < width) row[c] = static_cast<float>(static_cast<double>(v[i]) * inv);
+    }
+  }
+}
+
+// act[r, c] = f(gu[r, c]) * gu[r, F + c]; f = gelu_tanh (GeGLU) or silu (SwiGLU).
+template <bool GELU>
+__global__ void gated_act_kernel(const float* __restrict__ gu, float* __restrict__ act, uint32_t rows, uint32_t f) {
+  const uint64_t total4 = static_cast<uint64_t>(rows) * (f / 4);
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total4;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t r = i / (f / 4), c = (i % (f / 4)) * 4;
+    const float4 g = *reinterpret_cast<const float4*>(gu + r * 2 * f + c);
+    const float4 u = *reinterpret_cast<const float4*>(gu + r * 2 * f + f + c);
+    float gv[4] = {g.x, g.y, g.z, g.w};
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float x = gv[j];
+      if constexpr (GELU) {
+        o[j] = 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+      } else {
+        o[j] = x / (1.f + expf(-x));
+      }
+    }
+    *reinterpret_cast<float4*>(act + r * f + c) = make_float4(o[0] * u.x, o[1] * u.y, o[2] * u.z, o[3] * u.w);
+  }
+}
+
+// 256-d sinusoidal embedding [cos | sin] of one timestep per batch item.
+__global__ void timestep_embed_kernel(const float* __restrict__ t, float* __restrict__ out, uint32_t batch) {
+  const uint32_t b = blockIdx.x, i = threadIdx.x;  // 128 threads
+  if (b >= batch || i >= 128) return;
+  const double f = exp(-log(10000.0) * static_cast<double>(i) / 128.0);
+  const double a = static_cast<double>(t[b]) * f;
+  out[b * 256 + i] = static_cast<float>(cos(a));
+  out[b * 256 + 128 + i] = static_cast<float>(sin(a));
+}
+
+// adaLN parts [scale_a, gate_a, scale_m, gate_m, shift_a, shift_m] (each d):
+// add the bias, then gate = tanh(gate) and scale = scale + 1 (canonical_reference.go:374-381).
+__global__ void ada_prep_kernel(float* __restrict__ ada, const float* __restrict__ bias, uint32_t d, uint32_t batch) {
+  const uint64_t total = static_cast<uint64_t>(batch) * 6 * d;
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t j = static_cast<uint32_t>(i % (6ull * d));
+    const uint32_t part = j / d;
+    float v = ada[i] + bias[j];
+    if (part == 1 || part == 3) v = tanhf(v);
+    if (part == 0 || part == 2) v += 1.f;
+    ada[i] = v;
+  }
+}
+
+uint32_t grid_for(uint64_t work, uint32_t per_block) {
+  const uint64_t g = (work + per_block - 1) / per_block;
+  return static_cast<uint32_t>(g < 148ull * 32 ? (g == 0 ? 1 : g) : 148ull * 32);
+}
+
+// ---------------------------------------------------------------- NCCL (dlopen)
+// The library does not link NCCL: the all-reduce symbols are resolved at the
+// first tensor-parallel block creation.
+typedef int (*NcclGetUniqueIdFn)(void* id);
+typedef int (*NcclCommInitRankFn)(void** comm, int nranks, NcclUniqueIdBytes id, int rank);
+typedef int (*NcclAllReduceFn)(const void* send, void* recv, size_t count, int dtype, int op, void* comm,
+                              cudaStream_t stream);
+typedef int (*NcclCommDestroyFn)(void* comm);
+struct Nccl {
+  bool ok = false;
+  NcclGetUniqueIdFn get_id = nullptr;
+  NcclCommInitRankFn init_rank = nullptr;
+  NcclAllReduceFn all_reduce = nullptr;
+  NcclCommDestroyFn destroy = nullptr;
+};
+Nccl& nccl() {
+  static Nccl n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h == nullptr) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (h == nullptr) return;
+    n.get_id = reinterpret_cast<NcclGetUniqueIdFn>(dlsym(h, "ncclGetUniqueId"));
+    n.init_rank = reinterpret_cast<NcclCommInitRankFn>(dlsym(h, "ncclCommInitRank"));
+    n.all_reduce = reinterpret_cast<NcclAllReduceFn>(dlsym(h, "ncclAllReduce"));
+    n.destroy = reinterpret_cast<NcclCommDestroyFn>(dlsym(h, "ncclCommDestroy"));
+    n.ok = n.get_id && n.init_rank && n.all_reduce && n.destroy;
+  });
+  return n;
+}
+constexpr int kNcclFloat32 = 7;  // ncclFloat32
+constexpr int kNcclSum = 0;      // ncclSum
+
+}  // namespace
+
+int nccl_unique_id(NcclUniqueIdBytes* out) {
+  Nccl& n = nccl();
+  if (!n.ok) return -1;
+  return n.get_id(out->bytes);
+}
+
+// ---------------------------------------------------------------- Block
+Block::~Block() {
+  cudaDeviceSynchronize();  // the caller's last stream may already be gone
+  for (void* p : allocs_) cudaFree(p);
+  if (comm_ != nullptr && nccl().ok) nccl().destroy(comm_);
+}
+
+float* Block::alloc(uint64_t floats) {
+  void* p = nullptr;
+  if (cudaMalloc(&p, floats * sizeof(float) + 1024) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return nullptr;
+  }
+  allocs_.push_back(p);
+  return reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t stream) {
+  dims_ = d;
+  stream_ = stream;
+  if (d.family != kGemma && d.family != kDit) return -1;
+  if (d.hidden == 0 || d.heads == 0 || d.head_dim == 0 || d.ffn == 0 || d.seq_len == 0 || d.max_batch == 0) return -1;
+  if (d.hidden > NORM_VPT * NT || d.seq_len > NORM_VPT * NT) return -2;  // fused row kernels' width limit
+  if (d.hidden % 4 || d.ffn % 4 || d.head_dim % 8) return -2;
+  if (d.family == kDit && (d.head_dim != 128 || d.kv_heads != d.heads || d.grid_w == 0)) return -2;
+  if (d.family == kGemma && (d.kv_heads == 0 || d.heads % d.kv_heads)) return -2;
+  const uint64_t T = static_cast<uint64_t>(d.max_batch) * d.seq_len;
+  const uint32_t qkv_cols = (d.heads + 2 * d.kv_heads) * d.head_dim;
+  const uint32_t attn_cols = d.heads * d.head_dim;
+  // weights (pre-split hi/lo for the products, raw for gains / biases)
+  auto split_alloc = [&](SplitW& w, uint32_t k, uint32_t n) {
+    w.k = k;
+    w.n = n;
+    const uint64_t e = split_b_elems(n, k);
+    w.hi = alloc(e);
+    w.lo = alloc(e);
+    return w.hi != nullptr && w.lo != nullptr;
+  };
+  bool ok = split_alloc(wqkv_, d.hidden, qkv_cols) && split_alloc(wo_, attn_cols, d.hidden) &&
+            split_alloc(wgu_, d.hidden, 2 * d.ffn) && split_alloc(wd_, d.ffn, d.hidden);
+  norm1_ = alloc(d.hidden);
+  norm2_ = alloc(d.hidden);
+  ok = ok && norm1_ && norm2_;
+  if (d.family == kDit) {
+    ada_w_ = alloc(256ull * 6 * d.hidden);
+    ada_b_ = alloc(6ull * d.hidden);
+    norm3_ = alloc(d.hidden);
+    norm4_ = alloc(d.hidden);
+    qn_ = alloc(d.head_dim);
+    kn_ = alloc(d.head_dim);
+    temb_ = alloc(256ull * d.max_batch);
+    ada_ = alloc(6ull * d.hidden * d.max_batch);
+    tsteps_ = alloc(d.max_batch);
+    ok = ok && ada_w_ && ada_b_ && norm3_ && norm4_ && qn_ && kn_ && temb_ && ada_ && tsteps_;
+  }
+  // activations and workspaces
+  hbuf_ = alloc(T * d.hidden);
+  qkv_ = alloc(T * qkv_cols);
+  scores_ = alloc(static_cast<uint64_t>(d.max_batch) * d.heads * d.seq_len * d.seq_len);
+  attn_ = alloc(T * attn_cols);
+  x1_ = alloc(T * d.hidden);
+  proj_ = alloc(T * d.hidden);
+  gu_ = alloc(T * 2ull * d.ffn);
+  act_ = alloc(T * d.ffn);
+  const uint64_t a_need = std::max({sgemm_tc_a_scratch_bytes(T, d.hidden), sgemm_tc_a_scratch_bytes(T, attn_cols),
+                                    sgemm_tc_a_scratch_bytes(T, d.ffn)});
+  const uint64_t b_need = std::max(sgemm_tc_scratch_bytes(d.seq_len, d.seq_len, d.head_dim, d.heads),
+                                   sgemm_tc_scratch_bytes(d.seq_len, d.head_dim, d.seq_len, d.heads));
+  scratch_ = alloc(std::max(a_need, b_need) / sizeof(float) + 1);
+  err_ = reinterpret_cast<unsigned int*>(alloc(4));
+  ok = ok && hbuf_ && qkv_ && scores_ && attn_ && x1_ && proj_ && gu_ && act_ && scratch_ && err_;
+  if (!ok) return -3;
+  if (cudaMemsetAsync(err_, 0, 16, stream_) != cudaSuccess) return -4;
+  if (build_rope_tables() != 0) return -4;
+  if (d.tp_world > 1) {
+    if (!nccl().ok || id == nullptr) return -5;
+    if (nccl().init_rank(&comm_, static_cast<int>(d.tp_world), *id, static_cast<int>(d.tp_rank)) != 0) {
+      comm_ = nullptr;
+      return -5;
+    }
+  }
+  return cudaStreamSynchronize(stream_) == cudaSuccess ? 0 : -4;
+}
+
+// RoPE tables, computed on the host exactly as the reference does.
+int Block::build_rope_tables() {
+  const BlockDims& d = dims_;
+  const uint32_t half = d.head_dim / 2;
+  std::vector<float> c(static_cast<size_t>(d.seq_len) * half), s(c.size());
+  if (d.family == kGemma) {
+    // inv_freq_i = base^(-2i/hd), angle = pos * inv_freq_i, evaluated in binary64.
+    for (uint32_t p = 0; p < d.seq_len; ++p)
+      for (uint32_t i = 0; i < half; ++i) {
+        const double ang = static_cast<double>(p) * std::pow(static_cast<double>(d.rope_base),
+                                                             -2.0 * static_cast<double>(i) / d.head_dim);
+        c[static_cast<size_t>(p) * half + i] = static_cast<float>(std::cos(ang));
+        s[static_cast<size_t>(p) * half + i] = static_cast<float>(std::sin(ang));
+      }
+  } else {
+    // CanonicalRopeFrequency / CanonicalRopeRotate (canonical_contract.go:66-89): fp32
+    // frequency and angle, cos/sin of the fp32 angle in binary64, rounded to fp32.
+    static const uint32_t axes[3] = {32, 48, 48};
+    for (uint32_t p = 0; p < d.seq_len; ++p) {
+      const float coord[3] = {static_cast<float>(d.rope_frame), static_cast<float>(p / d.grid_w),
+                              static_cast<float>(p % d.grid_w)};
+      uint32_t pair = 0;
+      for (int a = 0; a < 3; ++a)
+        for (uint32_t q = 0; q < axes[a] / 2; ++q, ++pair) {
+          const float freq = static_cast<float>(1.0 / std::pow(static_cast<double>(d.rope_base),
+                                                               2.0 * static_cast<double>(q) / axes[a]));
+          const float ang = coord[a] * freq;
+          c[static_cast<size_t>(p) * half + pair] = static_cast<float>(std::cos(static_cast<double>(ang)));
+          s[static_cast<size_t>(p) * half + pair] = static_cast<float>(std::sin(static_cast<double>(ang)));
+        }
+    }
+  }
+  rope_cos_ = alloc(c.size());
+  rope_sin_ = alloc(s.size());
+  if (rope_cos_ == nullptr || rope_sin_ == nullptr) return -3;
+  if (cudaMemcpy(rope_cos_, c.data(), c.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) return -4;
+  if (cudaMemcpy(rope_sin_, s.data(), s.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) return -4;
+  return 0;
+}
+
+int Block::set_weight(uint32_t slot, const float* src, uint64_t count, bool on_device) {
+  const BlockDims& d = dims_;
+  const uint32_t qkv_cols = (d.heads + 2 * d.kv_heads) * d.head_dim;
+  const uint32_t attn_cols = d.heads * d.head_dim;
+  const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  auto raw = [&](float* dst, uint64_t want) -> int {
+    if (count != want || dst == nullptr) return -1;
+    return cudaMemcpyAsync(dst, src, want * 4, kind, stream_) == cudaSuccess ? 0 : -4;
+  };
+  auto split = [&](SplitW& w, uint32_t k, uint32_t n) -> int {
+    if (count != static_cast<uint64_t>(k) * n) return -1;
+    const float* dsrc = src;
+    float* staging = nullptr;
+    if (!on_device) {
+      if (cudaMalloc(&staging, count * 4) != cudaSuccess) return -4;
+      if (cudaMemcpyAsync(staging, src, count * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess) {
+        cudaFree(staging);
+        return -4;
+      }
+      dsrc = staging;
+    }
+    cudaError_t e = sgemm_tc_split_b(dsrc, n, k, n, w.hi, w.lo, stream_);
+    if (staging != nullptr) {
+      cudaStreamSynchronize(stream_);
+      cudaFree(staging);
+    }
+    return e == cudaSuccess ? 0 : -4;
+  };
+  int rc;
+  if (d.family == kGemma) {
+    switch (slot) {
+      case kGemmaNorm1: rc = raw(norm1_, d.hidden); break;
+      case kGemmaWqkv: rc = split(wqkv_, d.hidden, qkv_cols); break;
+      case kGemmaWo: rc = split(wo_, attn_cols, d.hidden); break;
+      case kGemmaNorm2: rc = raw(norm2_, d.hidden); break;
+      case kGemmaWgu: rc = split(wgu_, d.hidden, 2 * d.ffn); break;
+      case kGemmaWd: rc = split(wd_, d.ffn, d.hidden); break;
+      default: return -1;
+    }
+  } else {
+    switch (slot) {
+      case kDitAdaW: rc = raw(ada_w_, 256ull * 6 * d.hidden); break;
+      case kDitAdaB: rc = raw(ada_b_, 6ull * d.hidden); break;
+      case kDitAttnNorm1: rc = raw(norm1_, d.hidden); break;
+      case kDitWqkv: rc = split(wqkv_, d.hidden, qkv_cols); break;
+      case kDitQNorm: rc = raw(qn_, d.head_dim); break;
+      case kDitKNorm: rc = raw(kn_, d.head_dim); break;
+      case kDitWo: rc = split(wo_, attn_cols, d.hidden); break;
+      case kDitAttnNorm2: rc = raw(norm2_, d.hidden); break;
+      case kDitFfnNorm1: rc = raw(norm3_, d.hidden); break;
+      case kDitW13: rc = split(wgu_, d.hidden, 2 * d.ffn); break;
+      case kDitW2: rc = split(wd_, d.ffn, d.hidden); break;
+      case kDitFfnNorm2: rc = raw(norm4_, d.hidden); break;
+      default: return -1;
+    }
+  }
+  if (rc != 0) return rc;
+  return cudaStreamSynchronize(stream_) == cudaSuccess ? 0 : -4;
+}
+
+cudaError_t Block::gemm(const float* a, uint64_t lda, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
+                        const float* residual, uint64_t ldr) {
+  return sgemm_tc_presplit(a, lda, w.hi, w.lo, c, ldc, m, w.n, w.k, scratch_, err_, stream_, residual, ldr);
+}
+
+cudaError_t Block::all_reduce(float* buf, uint64_t count) {
+  if (dims_.tp_world <= 1) return cudaSuccess;
+  return nccl().all_reduce(buf, buf, count, kNcclFloat32, kNcclSum, comm_, stream_) == 0 ? cudaSuccess
+                                                                                          : cudaErrorUnknown;
+}
+
+// Attention of one batch item: scores = Q K^T per head (batched), softmax, O = P V.
+cudaError_t Block::attention(uint32_t item, uint64_t ldq, uint32_t k_col, uint32_t v_col, bool shared_kv) {
+  const BlockDims& d = dims_;
+  const uint64_t S = d.seq_len, hd = d.head_dim;
+  const float* base = qkv_ + item * S * ldq;
+  float* sc = scores_ + static_cast<uint64_t>(item) * d.heads * S * S;
+  GemmBatch qk;
+  qk.count = d.heads;
+  qk.stride_a = hd;
+  qk.stride_b = shared_kv ? 0 : hd;
+  qk.stride_c = S * S;
+  qk.b_trans = true;
+  cudaError_t e = sgemm_tc(base, ldq, base + k_col, ldq, sc, S, S, S, hd, scratch_, err_, 16, stream_, nullptr, &qk);
+  if (e != cudaSuccess) return e;
+  attn_softmax_kernel<<<grid_for(d.heads * S, 1), NT, 0, stream_>>>(sc, d.heads * S, S, S,
+                                                                    1.0f / std::sqrt(static_cast<float>(hd)),
+                                                                    d.family == kGemma ? 1 : 0);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  GemmBatch pv;
+  pv.count = d.heads;
+  pv.stride_a = S * S;
+  pv.stride_b = shared_kv ? 0 : hd;
+  pv.stride_c = hd;
+  const uint64_t ldo = static_cast<uint64_t>(d.heads) * hd;
+  return sgemm_tc(sc, S, base + v_col, ldq, attn_ + item * S * ldo, ldo, S, hd, S, scratch_, err_, 16, stream_,
+                  nullptr, &pv);
+}
+
+int Block::forward(const float* x, float* y, uint32_t batch, const float* timesteps_host) {
+  const BlockDims& d = dims_;
+  if (batch == 0 || batch > d.max_batch) return -1;
+  const uint32_t T = batch * d.seq_len;
+  const uint32_t qkv_cols = (d.heads + 2 * d.kv_heads) * d.head_dim;
+  const uint32_t attn_cols = d.heads * d.head_dim;
+  const bool lead = d.tp_rank == 0;  // rank that adds the residual into row-parallel partial sums
+  cudaError_t e = cudaSuccess;
+  auto ok = [&]() { return e == cudaSuccess && (e = cudaGetLastError()) == cudaSuccess; };
+  if (d.family == kGemma) {
+    norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x, d.hidden, norm1_, d.eps, nullptr, nullptr, nullptr, 0,
+                                                          nullptr, 0, d.seq_len, hbuf_, d.hidden, T, d.hidden);
+    if (!ok()) return -4;
+    e = gemm(hbuf_, d.hidden, wqkv_, qkv_, qkv_cols, T);
+    if (!ok()) return -4;
+    const uint64_t rope_work = static_cast<uint64_t>(T) * (d.heads + d.kv_heads) * (d.head_dim / 2);
+    rope_half_kernel<<<grid_for(rope_work, NT), NT, 0, stream_>>>(qkv_, qkv_cols, 0, d.heads + d.kv_heads,
+                                                                 d.head_dim, rope_cos_, rope_sin_, d.seq_len, T);
+    if (!ok()) return -4;
+    for (uint32_t b = 0; b < batch && e == cudaSuccess; ++b)
+      e = attention(b, qkv_cols, attn_cols, attn_cols + d.kv_heads * d.head_dim, true);
+    if (!ok()) return -4;
+    e = gemm(attn_, attn_cols, wo_, x1_, d.hidden, T, lead ? x : nullptr, d.hidden);  // x1 = x + O Wo
+    if (ok()) e = all_reduce(x1_, static_cast<uint64_t>(T) * d.hidden);
+    if (!ok()) return -4;
+    norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x1_, d.hidden, norm2_, d.eps, nullptr, nullptr, nullptr, 0,
+                                                          nullptr, 0, d.seq_len, hbuf_, d.hidden, T, d.hidden);
+    if (!ok()) return -4;
+    e = gemm(hbuf_, d.hidden, wgu_, gu_, 2ull * d.ffn, T);
+    if (!ok()) return -4;
+    gated_act_kernel<true><<<grid_for(static_cast<uint64_t>(T) * d.ffn / 4, NT), NT, 0, stream_>>>(gu_, act_, T,
+                                                                                                 d.ffn);
+    if (!ok()) return -4;
+    e = gemm(act_, d.ffn, wd_, y, d.hidden, T, lead ? x1_ : nullptr, d.hidden);  // y = x1 + act Wd
+    if (ok()) e = all_reduce(y, static_cast<uint64_t>(T) * d.hidden);
+    return ok() ? 0 : -4;
+  }
+  // ---- DiT
+  if (timesteps_host == nullptr) return -1;
+  e = cudaMemcpyAsync(tsteps_, timesteps_host, batch * sizeof(float), cudaMemcpyHostToDevice, stream_);
+  if (!ok()) return -4;
+  timestep_embed_kernel<<<batch, 128, 0, stream_>>>(tsteps_, temb_, batch);
+  if (!ok()) return -4;
+  e = sgemm_fma(temb_, 256, ada_w_, 6ull * d.hidden, ada_, 6ull * d.hidden, batch, 6 * d.hidden, 256, stream_);
+  if (!ok()) return -4;
+  ada_prep_kernel<<<grid_for(6ull * d.hidden * batch, NT), NT, 0, stream_>>>(ada_, ada_b_, d.hidden, batch);
+  if (!ok()) return -4;
+  const uint64_t ms = 6ull * d.hidden;
+  float* scale_a = ada_;
+  float* gate_a = ada_ + d.hidden;
+  float* scale_m = ada_ + 2ull * d.hidden;
+  float* gate_m = ada_ + 3ull * d.hidden;
+  float* shift_a = ada_ + 4ull * d.hidden;
+  float* shift_m = ada_ + 5ull * d.hidden;
+  norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x, d.hidden, norm1_, d.eps, scale_a, shift_a, nullptr, 0,
+                                                        nullptr, ms, d.seq_len, hbuf_, d.hidden, T, d.hidden);
+  if (!ok()) return -4;
+  e = gemm(hbuf_, d.hidden, wqkv_, qkv_, qkv_cols, T);
+  if (!ok()) return -4;
+  const uint64_t qk_warps = static_cast<uint64_t>(T) * d.heads;
+  qk_norm_rope3_kernel<<<grid_for(qk_warps * 32, NT), NT, 0, stream_>>>(qkv_, qkv_cols, 0, d.heads, qn_, 1e-5f,
+                                                                       rope_cos_, rope_sin_, d.seq_len, T);
+  if (!ok()) return -4;
+  qk_norm_rope3_kernel<<<grid_for(qk_warps * 32, NT), NT, 0, stream_>>>(qkv_, qkv_cols, attn_cols, d.heads, kn_,
+                                                                       1e-5f, rope_cos_, rope_sin_, d.seq_len, T);
+  if (!ok()) return -4;
+  for (uint32_t b = 0; b < batch && e == cudaSuccess; ++b) e = attention(b, qkv_cols, attn_cols, 2 * attn_cols, false);
+  if (!ok()) return -4;
+  e = gemm(attn_, attn_cols, wo_, proj_, d.hidden, T);
+  if (ok()) e = all_reduce(proj_, static_cast<uint64_t>(T) * d.hidden);
+  if (!ok()) return -4;
+  // res = x + gate_a * RMSNorm(proj)
+  norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(proj_, d.hidden, norm2_, d.eps, nullptr, nullptr, x, d.hidden,
+                                                        gate_a, ms, d.seq_len, x1_, d.hidden, T, d.hidden);
+  if (!ok()) return -4;
+  norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x1_, d.hidden, norm3_, d.eps, scale_m, shift_m, nullptr, 0,
+                                                        nullptr, ms, d.seq_len, hbuf_, d.hidden, T, d.hidden);
+  if (!ok()) return -4;
+  e = gemm(hbuf_, d.hidden, wgu_, gu_, 2ull * d.ffn, T);
+  if (!ok()) return -4;
+  gated_act_kernel<false><<<grid_for(static_cast<uint64_t>(T) * d.ffn / 4, NT), NT, 0, stream_>>>(gu_, act_, T,
+                                                                                                d.ffn);
+  if (!ok()) return -4;
+  e = gemm(act_, d.ffn, wd_, proj_, d.hidden, T);
+  if (ok()) e = all_reduce(proj_, static_cast<uint64_t>(T) * d.hidden);
+  if (!ok()) return -4;
+  // y = res + gate_m * RMSNorm(w2 out)
+  norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(proj_, d.hidden, norm4_, d.eps, nullptr, nullptr, x1_,
+                                                        d.hidden, gate_m, ms, d.seq_len, y, d.hidden, T, d.hidden);
+  return ok() ? 0 : -4;
+}
+
+unsigned int Block::read_status() {
+  unsigned int v = 0;
+  if (cudaMemcpyAsync(&v, err_, 4, cudaMemcpyDeviceToHost, stream_) != cudaSuccess ||
+      cudaStreamSynchronize(stream_) != cudaSuccess)
+    return 0xFFFFFFFFu;
+  cudaMemsetAsync(err_, 0, 4, stream_);
+  return v;
+}
+
+}  // namespace oct

@@ -1,0 +1,84 @@
+// block.h -- the transformer block object behind the oct_b200_block_* entry points.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <vector>
+
+namespace oct {
+
+enum : uint32_t { kGemma = 1, kDit = 2 };
+
+// Weight slots (the order of the block's forward pass).
+enum : uint32_t {
+  kGemmaNorm1 = 0, kGemmaWqkv = 1, kGemmaWo = 2, kGemmaNorm2 = 3, kGemmaWgu = 4, kGemmaWd = 5,
+};
+enum : uint32_t {
+  kDitAdaW = 0, kDitAdaB = 1, kDitAttnNorm1 = 2, kDitWqkv = 3, kDitQNorm = 4, kDitKNorm = 5, kDitWo = 6,
+  kDitAttnNorm2 = 7, kDitFfnNorm1 = 8, kDitW13 = 9, kDitW2 = 10, kDitFfnNorm2 = 11,
+};
+
+struct BlockDims {
+  uint32_t family = 0;
+  uint32_t hidden = 0, heads = 0, kv_heads = 0, head_dim = 0, ffn = 0;  // heads / ffn: this rank's share
+  uint32_t seq_len = 0, max_batch = 0;
+  float eps = 1e-6f, rope_base = 10000.f;
+  uint32_t grid_w = 0, rope_frame = 0;
+  uint32_t tp_rank = 0, tp_world = 1;
+};
+
+struct NcclUniqueIdBytes {
+  char bytes[128];
+};
+
+// ncclGetUniqueId through the dlopen'ed NCCL; 0 on success.
+int nccl_unique_id(NcclUniqueIdBytes* out);
+
+class Block {
+ public:
+  Block() = default;
+  ~Block();
+  Block(const Block&) = delete;
+  Block& operator=(const Block&) = delete;
+
+  // Allocates weights and workspaces for max_batch sequences; with
+  // tp_world > 1 also joins the NCCL communicator named by `id`.
+  int init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t stream);
+  int set_weight(uint32_t slot, const float* src, uint64_t count, bool on_device);
+  // y = block(x) for `batch` sequences of seq_len tokens (x, y: [batch*seq][hidden]).
+  int forward(const float* x, float* y, uint32_t batch, const float* timesteps_host);
+  void set_stream(cudaStream_t s) { stream_ = s; }
+  cudaStream_t stream() const { return stream_; }
+  unsigned int read_status();
+  const BlockDims& dims() const { return dims_; }
+
+ private:
+  struct SplitW {
+    float* hi = nullptr;
+    float* lo = nullptr;
+    uint32_t k = 0, n = 0;
+  };
+  float* alloc(uint64_t floats);
+  int build_rope_tables();
+  cudaError_t gemm(const float* a, uint64_t lda, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
+                   const float* residual = nullptr, uint64_t ldr = 0);
+  cudaError_t attention(uint32_t item, uint64_t ldq, uint32_t k_col, uint32_t v_col, bool shared_kv);
+  cudaError_t all_reduce(float* buf, uint64_t count);
+
+  BlockDims dims_;
+  cudaStream_t stream_ = nullptr;
+  void* comm_ = nullptr;
+  std::vector<void*> allocs_;
+  SplitW wqkv_, wo_, wgu_, wd_;
+  float *norm1_ = nullptr, *norm2_ = nullptr, *norm3_ = nullptr, *norm4_ = nullptr;
+  float *qn_ = nullptr, *kn_ = nullptr, *ada_w_ = nullptr, *ada_b_ = nullptr;
+  float *temb_ = nullptr, *ada_ = nullptr, *tsteps_ = nullptr;
+  float *rope_cos_ = nullptr, *rope_sin_ = nullptr;
+  float *hbuf_ = nullptr, *qkv_ = nullptr, *scores_ = nullptr, *attn_ = nullptr, *x1_ = nullptr, *proj_ = nullptr;
+  float *gu_ = nullptr, *act_ = nullptr, *scratch_ = nullptr;
+  unsigned int* err_ = nullptr;
+};
+
+}  // namespace oct

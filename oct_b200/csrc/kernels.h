@@ -15,8 +15,18 @@ struct SplitDims {
 };
 SplitDims split_dims(uint32_t m, uint32_t n, uint32_t k);
 
-// Bytes of scratch needed by sgemm_tc for (m, n, k): hi/lo copies of A and of B^T.
-uint64_t sgemm_tc_scratch_bytes(uint32_t m, uint32_t n, uint32_t k);
+// Bytes of scratch needed by sgemm_tc for (m, n, k): hi/lo copies of A and of
+// B^T, per batch entry, times `batch`.
+uint64_t sgemm_tc_scratch_bytes(uint32_t m, uint32_t n, uint32_t k, uint32_t batch = 1);
+
+// Strided batch of independent products C_i = A_i * op(B_i), i < count, with
+// X_i = X + i * stride_x (element strides; a stride of 0 shares the operand).
+// b_trans: B is given as [n][k] row-major and op(B) = B^T (the "NT" product).
+struct GemmBatch {
+  uint32_t count = 1;
+  uint64_t stride_a = 0, stride_b = 0, stride_c = 0;
+  bool b_trans = false;
+};
 
 // 3xTF32 tensor-core SGEMM.  `scratch` must hold sgemm_tc_scratch_bytes and be
 // 1024-byte aligned.  bk selects the K depth of one pipeline stage (16 or 32).
@@ -27,11 +37,23 @@ struct SgemmEvents {
 };
 cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
                      uint32_t m, uint32_t n, uint32_t k, void* scratch, unsigned int* err, int bk,
-                     cudaStream_t stream, const SgemmEvents* events = nullptr);
+                     cudaStream_t stream, const SgemmEvents* events = nullptr, const GemmBatch* batch = nullptr);
+
+// Pre-split weights: sgemm_tc_split_b writes the hi/lo K-major layout of a
+// [k][n] operand (split_b_elems floats each); sgemm_tc_presplit then computes
+// C = R + A * B (R = residual, optional, may alias C) splitting only A into
+// a_scratch (sgemm_tc_a_scratch_bytes, 1024-byte aligned).
+uint64_t split_b_elems(uint32_t n, uint32_t k);
+cudaError_t sgemm_tc_split_b(const float* b, uint64_t ldb, uint32_t k, uint32_t n, float* bhi, float* blo,
+                             cudaStream_t stream);
+uint64_t sgemm_tc_a_scratch_bytes(uint32_t m, uint32_t k);
+cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, const float* blo, float* c,
+                              uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* a_scratch, unsigned int* err,
+                              cudaStream_t stream, const float* residual = nullptr, uint64_t ldr = 0);
 
 // Plain FP32-FMA SGEMM on the CUDA cores (control variant); no scratch.
 cudaError_t sgemm_fma(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
-                      uint32_t m, uint32_t n, uint32_t k, cudaStream_t stream);
+                      uint32_t m, uint32_t n, uint32_t k, cudaStream_t stream, const GemmBatch* batch = nullptr);
 
 // ---------------------------------------------------------------- reductions
 // op: 1 = row sum, 2 = row max, 3 = stable softmax.  `nonfinite` (device

@@ -23,9 +23,11 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <unordered_map>
 #include <unordered_set>
 #include <vector>
 
+#include "block.h"
 #include "kernels.h"
 
 namespace {
@@ -107,6 +109,9 @@ struct Runtime {
   bool timing = false;
   std::vector<oct::SgemmEvents> timing_events;
   size_t timing_used = 0;
+  // Transformer blocks created on this handle.
+  std::unordered_map<uint64_t, oct::Block*> blocks;
+  uint64_t next_block = 1;
   uint64_t next_request_id = 1;
 
   unsigned int* err_word() { return static_cast<unsigned int*>(words.aligned()); }
@@ -157,7 +162,8 @@ bool checked_mul(uint64_t a, uint64_t b, uint64_t* out) {
 // ---------------------------------------------------------------- SGEMM core
 // Enqueues C = A * B for device pointers; chooses the kernel.
 int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
-                  uint32_t m, uint32_t n, uint32_t k, uint32_t variant, cudaStream_t stream) {
+                  uint32_t m, uint32_t n, uint32_t k, uint32_t variant, cudaStream_t stream,
+                  const oct::GemmBatch* batch = nullptr) {
   if (variant == OCT_B200_SGEMM_AUTO) {
     // Tiny products do not fill one 128x256 tensor-core tile usefully; the
     // FMA control is exact-tail by construction and cheaper there.
@@ -166,9 +172,9 @@ int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uin
   }
   cudaError_t e;
   if (variant == OCT_B200_SGEMM_FMA) {
-    e = oct::sgemm_fma(a, lda, b, ldb, c, ldc, m, n, k, stream);
+    e = oct::sgemm_fma(a, lda, b, ldb, c, ldc, m, n, k, stream, batch);
   } else if (variant == OCT_B200_SGEMM_TC3XTF32 || variant == 16u || variant == 32u) {
-    const uint64_t need = oct::sgemm_tc_scratch_bytes(m, n, k);
+    const uint64_t need = oct::sgemm_tc_scratch_bytes(m, n, k, batch != nullptr ? batch->count : 1u);
     e = rt->scratch.ensure(need, stream);
     if (e != cudaSuccess) return OCT_B200_DETAIL_OUT_OF_MEMORY;
     const int bk = (variant == 32u) ? 32 : 16;
@@ -183,7 +189,7 @@ int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uin
       }
       ev = &rt->timing_events[rt->timing_used++];
     }
-    e = oct::sgemm_tc(a, lda, b, ldb, c, ldc, m, n, k, rt->scratch.aligned(), rt->err_word(), bk, stream, ev);
+    e = oct::sgemm_tc(a, lda, b, ldb, c, ldc, m, n, k, rt->scratch.aligned(), rt->err_word(), bk, stream, ev, batch);
   } else {
     return OCT_B200_DETAIL_BAD_VARIANT;
   }
@@ -239,6 +245,8 @@ Runtime* create_runtime(const PrometheusReactorConfig* cfg, int* status) {
 
 void destroy_runtime(Runtime* rt) {
   if (rt->stream != nullptr) cudaStreamSynchronize(rt->stream);
+  for (auto& kv : rt->blocks) delete kv.second;
+  rt->blocks.clear();
   for (auto& ev : rt->timing_events) {
     cudaEventSynchronize(ev.main_end);
     cudaEventDestroy(ev.split_begin);
@@ -1145,6 +1153,44 @@ int oct_b200_sgemm_device_ld(void* handle, const float* d_a, uint64_t lda, const
   }
 }
 
+int oct_b200_sgemm_batched_device(void* handle, const float* d_a, uint64_t lda, uint64_t stride_a, const float* d_b,
+                                  uint64_t ldb, uint64_t stride_b, uint32_t b_trans, float* d_c, uint64_t ldc,
+                                  uint64_t stride_c, uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
+                                  uint32_t variant, void* stream, int* out_detail_code) {
+  try {
+    if (out_detail_code) *out_detail_code = 0;
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    const uint64_t need_ldb = b_trans ? k : n;
+    if (d_a == nullptr || d_b == nullptr || d_c == nullptr || lda < k || ldb < need_ldb || ldc < n ||
+        batch > 65535u) {
+      if (out_detail_code) *out_detail_code = PROM_ERROR;
+      return PROM_ERROR;
+    }
+    if (!rt->available) {
+      if (out_detail_code) *out_detail_code = PROM_DETAIL_CAPABILITY_MISMATCH;
+      return PROM_ERROR;
+    }
+    if (m == 0 || n == 0 || k == 0 || batch == 0) return PROM_OK;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    oct::GemmBatch bt;
+    bt.count = batch;
+    bt.stride_a = stride_a;
+    bt.stride_b = stride_b;
+    bt.stride_c = stride_c;
+    bt.b_trans = b_trans != 0;
+    const int d = enqueue_sgemm(rt, d_a, lda, d_b, ldb, d_c, ldc, m, n, k, variant, static_cast<cudaStream_t>(stream),
+                                &bt);
+    if (d != 0) {
+      if (out_detail_code) *out_detail_code = d;
+      return PROM_ERROR;
+    }
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
 int oct_b200_sgemm_device(void* handle, const float* d_a, const float* d_b, float* d_c, uint32_t m, uint32_t n,
                           uint32_t k, uint32_t variant, void* stream, int* out_detail_code) {
   return oct_b200_sgemm_device_ld(handle, d_a, k, d_b, n, d_c, n, m, n, k, variant, stream, out_detail_code);
@@ -1268,6 +1314,168 @@ int oct_b200_read_kernel_timing(void* handle, double* split_ms_total, double* ma
     if (main_ms_total) *main_ms_total = main;
     if (launches) *launches = static_cast<uint32_t>(rt->timing_used);
     rt->timing_used = 0;
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int oct_b200_nccl_unique_id(uint8_t* out_128_bytes) {
+  if (out_128_bytes == nullptr) return PROM_ERROR;
+  oct::NcclUniqueIdBytes id{};
+  if (oct::nccl_unique_id(&id) != 0) return PROM_ERROR;
+  std::memcpy(out_128_bytes, id.bytes, 128);
+  return PROM_OK;
+}
+
+int oct_b200_block_create(void* handle, const OctB200BlockConfig* cfg, uint64_t* out_block_id, int* out_detail_code) {
+  auto fail = [&](int rc, int detail) {
+    if (out_detail_code) *out_detail_code = detail;
+    return rc;
+  };
+  try {
+    if (out_detail_code) *out_detail_code = 0;
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    if (cfg == nullptr || out_block_id == nullptr || cfg->struct_size < sizeof(OctB200BlockConfig))
+      return fail(PROM_ERROR, OCT_B200_DETAIL_BLOCK_INVALID);
+    if (!rt->available) return fail(PROM_ERROR, PROM_DETAIL_CAPABILITY_MISMATCH);
+    oct::BlockDims d;
+    d.family = cfg->family;
+    d.hidden = cfg->hidden;
+    d.heads = cfg->heads;
+    d.kv_heads = cfg->kv_heads;
+    d.head_dim = cfg->head_dim;
+    d.ffn = cfg->ffn;
+    d.seq_len = cfg->seq_len;
+    d.max_batch = cfg->max_batch;
+    d.eps = cfg->eps;
+    d.rope_base = cfg->rope_base;
+    d.grid_w = cfg->grid_w;
+    d.rope_frame = cfg->rope_frame;
+    d.tp_rank = cfg->tp_rank;
+    d.tp_world = cfg->tp_world == 0 ? 1 : cfg->tp_world;
+    if (d.family == oct::kGemma && d.kv_heads != 1) return fail(PROM_ERROR, OCT_B200_DETAIL_BLOCK_INVALID);
+    if (d.tp_rank >= d.tp_world) return fail(PROM_ERROR, OCT_B200_DETAIL_BLOCK_INVALID);
+    oct::NcclUniqueIdBytes id{};
+    std::memcpy(id.bytes, cfg->nccl_id, 128);
+    std::lock_guard<std::mutex> lock(rt->mu);
+    oct::Block* b = new (std::nothrow) oct::Block();
+    if (b == nullptr) return fail(PROM_ERROR, OCT_B200_DETAIL_BLOCK_ALLOC);
+    const int rc = b->init(d, &id, rt->stream);
+    if (rc != 0) {
+      delete b;
+      return fail(PROM_ERROR, rc == -3 ? OCT_B200_DETAIL_BLOCK_ALLOC
+                                       : (rc == -5 ? OCT_B200_DETAIL_BLOCK_NCCL : OCT_B200_DETAIL_BLOCK_INVALID));
+    }
+    const uint64_t id_out = rt->next_block++;
+    rt->blocks[id_out] = b;
+    *out_block_id = id_out;
+    return PROM_OK;
+  } catch (...) {
+    return fail(PROM_INTERNAL_ERROR, OCT_B200_DETAIL_BLOCK_ALLOC);
+  }
+}
+
+int oct_b200_block_set_weight(void* handle, uint64_t block_id, uint32_t slot, const float* data,
+                              uint64_t element_count, uint32_t data_on_device) {
+  try {
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    auto it = rt->blocks.find(block_id);
+    if (it == rt->blocks.end() || data == nullptr) return PROM_ERROR;
+    it->second->set_stream(rt->stream);
+    return it->second->set_weight(slot, data, element_count, data_on_device != 0) == 0 ? PROM_OK : PROM_ERROR;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int oct_b200_block_forward_device(void* handle, uint64_t block_id, const float* d_x, float* d_y, uint32_t batch,
+                                  const float* timesteps, void* stream, int* out_detail_code) {
+  try {
+    if (out_detail_code) *out_detail_code = 0;
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    auto it = rt->blocks.find(block_id);
+    if (it == rt->blocks.end()) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_BLOCK_NOT_FOUND;
+      return PROM_ERROR;
+    }
+    if (d_x == nullptr || d_y == nullptr) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_BLOCK_INVALID;
+      return PROM_ERROR;
+    }
+    oct::Block* b = it->second;
+    b->set_stream(static_cast<cudaStream_t>(stream));
+    const int rc = b->forward(d_x, d_y, batch, timesteps);
+    if (rc != 0) {
+      if (out_detail_code) *out_detail_code = rc == -1 ? OCT_B200_DETAIL_BLOCK_INVALID : OCT_B200_DETAIL_BLOCK_EXEC;
+      return PROM_ERROR;
+    }
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int oct_b200_block_forward(void* handle, uint64_t block_id, const float* x, float* y, uint32_t batch,
+                           const float* timesteps, int* out_detail_code) {
+  try {
+    if (out_detail_code) *out_detail_code = 0;
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    auto it = rt->blocks.find(block_id);
+    if (it == rt->blocks.end()) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_BLOCK_NOT_FOUND;
+      return PROM_ERROR;
+    }
+    if (x == nullptr || y == nullptr) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_BLOCK_INVALID;
+      return PROM_ERROR;
+    }
+    oct::Block* b = it->second;
+    const oct::BlockDims& d = b->dims();
+    if (batch == 0 || batch > d.max_batch) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_BLOCK_INVALID;
+      return PROM_ERROR;
+    }
+    const uint64_t bytes = static_cast<uint64_t>(batch) * d.seq_len * d.hidden * sizeof(float);
+    if (rt->rin.ensure(bytes, rt->stream) != cudaSuccess || rt->rout.ensure(bytes, rt->stream) != cudaSuccess) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_OUT_OF_MEMORY;
+      return PROM_ERROR;
+    }
+    float* dx = static_cast<float*>(rt->rin.aligned());
+    float* dy = static_cast<float*>(rt->rout.aligned());
+    b->set_stream(rt->stream);
+    cudaError_t e = cudaMemcpyAsync(dx, x, bytes, cudaMemcpyHostToDevice, rt->stream);
+    int rc = e == cudaSuccess ? b->forward(dx, dy, batch, timesteps) : -4;
+    if (rc == 0) e = cudaMemcpyAsync(y, dy, bytes, cudaMemcpyDeviceToHost, rt->stream);
+    if (rc == 0 && e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
+    if (rc == 0 && e == cudaSuccess && b->read_status() != 0) rc = -4;
+    if (rc != 0 || e != cudaSuccess) {
+      (void)cudaGetLastError();
+      if (out_detail_code) *out_detail_code = rc == -1 ? OCT_B200_DETAIL_BLOCK_INVALID : OCT_B200_DETAIL_BLOCK_EXEC;
+      return PROM_ERROR;
+    }
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int oct_b200_block_destroy(void* handle, uint64_t block_id) {
+  try {
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    auto it = rt->blocks.find(block_id);
+    if (it == rt->blocks.end()) return PROM_ERROR;
+    delete it->second;
+    rt->blocks.erase(it);
     return PROM_OK;
   } catch (...) {
     return PROM_INTERNAL_ERROR;

@@ -39,12 +39,19 @@ __device__ __forceinline__ void load4(const float* __restrict__ base, uint64_t l
   }
 }
 
+// B_TRANS: B is given as [n][k] row-major and the product is A * B^T.
+// blockIdx.z selects the batch entry (element strides stride_a/b/c).
+template <bool B_TRANS>
 __global__ void __launch_bounds__(256) sgemm_fma_kernel(const float* __restrict__ a, uint64_t lda,
                                                         const float* __restrict__ b, uint64_t ldb,
                                                         float* __restrict__ c, uint64_t ldc, uint32_t m,
-                                                        uint32_t n, uint32_t k) {
+                                                        uint32_t n, uint32_t k, uint64_t stride_a,
+                                                        uint64_t stride_b, uint64_t stride_c) {
   __shared__ __align__(16) float As[2][TK][TM + PAD];  // A slab, transposed: [k][m]
   __shared__ __align__(16) float Bs[2][TK][TN + PAD];  // B slab: [k][n]
+  a += blockIdx.z * stride_a;
+  b += blockIdx.z * stride_b;
+  c += blockIdx.z * stride_c;
 
   const uint32_t tid = threadIdx.x;
   const uint32_t tx = tid & 15, ty = tid >> 4;
@@ -52,9 +59,21 @@ __global__ void __launch_bounds__(256) sgemm_fma_kernel(const float* __restrict_
   const bool a_vec = (lda % 4 == 0) && ((reinterpret_cast<uintptr_t>(a) & 15u) == 0);
   const bool b_vec = (ldb % 4 == 0) && ((reinterpret_cast<uintptr_t>(b) & 15u) == 0);
 
-  // Loader coordinates: A -> row t/2, k offset (t%2)*4; B -> k row t/32, col (t%32)*4.
+  // Loader coordinates: A (and B^T) -> row t/2, k offset (t%2)*4; B -> k row t/32, col (t%32)*4.
   const uint32_t a_row = tid >> 1, a_k = (tid & 1) * 4;
   const uint32_t b_k = tid >> 5, b_col = (tid & 31) * 4;
+  auto load_b = [&](uint32_t k0, float (&v)[4]) {
+    if constexpr (B_TRANS) load4(b, ldb, n0 + a_row, k0 + a_k, n, k, b_vec, v);
+    else load4(b, ldb, k0 + b_k, n0 + b_col, k, n, b_vec, v);
+  };
+  auto store_b = [&](uint32_t buf, const float (&v)[4]) {
+    if constexpr (B_TRANS) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) Bs[buf][a_k + j][a_row] = v[j];
+    } else {
+      *reinterpret_cast<float4*>(&Bs[buf][b_k][b_col]) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+  };
 
   float acc[8][8];
 #pragma unroll
@@ -65,10 +84,10 @@ __global__ void __launch_bounds__(256) sgemm_fma_kernel(const float* __restrict_
   float ra[4], rb[4];
   const uint32_t num_kt = (k + TK - 1) / TK;
   load4(a, lda, m0 + a_row, a_k, m, k, a_vec, ra);
-  load4(b, ldb, b_k, n0 + b_col, k, n, b_vec, rb);
+  load_b(0, rb);
 #pragma unroll
   for (int j = 0; j < 4; ++j) As[0][a_k + j][a_row] = ra[j];
-  *reinterpret_cast<float4*>(&Bs[0][b_k][b_col]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+  store_b(0, rb);
   __syncthreads();
 
   for (uint32_t kt = 0; kt < num_kt; ++kt) {
@@ -77,7 +96,7 @@ __global__ void __launch_bounds__(256) sgemm_fma_kernel(const float* __restrict_
     if (more) {
       const uint32_t k1 = (kt + 1) * TK;
       load4(a, lda, m0 + a_row, k1 + a_k, m, k, a_vec, ra);
-      load4(b, ldb, k1 + b_k, n0 + b_col, k, n, b_vec, rb);
+      load_b(k1, rb);
     }
 #pragma unroll
     for (int kk = 0; kk < TK; ++kk) {
@@ -96,7 +115,7 @@ __global__ void __launch_bounds__(256) sgemm_fma_kernel(const float* __restrict_
       const uint32_t nxt = cur ^ 1u;
 #pragma unroll
       for (int j = 0; j < 4; ++j) As[nxt][a_k + j][a_row] = ra[j];
-      *reinterpret_cast<float4*>(&Bs[nxt][b_k][b_col]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+      store_b(nxt, rb);
     }
     __syncthreads();
   }
@@ -125,11 +144,19 @@ __global__ void __launch_bounds__(256) sgemm_fma_kernel(const float* __restrict_
 }  // namespace
 
 cudaError_t sgemm_fma(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
-                      uint32_t m, uint32_t n, uint32_t k, cudaStream_t stream) {
+                      uint32_t m, uint32_t n, uint32_t k, cudaStream_t stream, const GemmBatch* batch) {
   if (m == 0 || n == 0 || k == 0) return cudaSuccess;
-  const dim3 grid((n + TN - 1) / TN, (m + TM - 1) / TM);
-  if (grid.y > 65535u) return cudaErrorInvalidValue;
-  sgemm_fma_kernel<<<grid, 256, 0, stream>>>(a, lda, b, ldb, c, ldc, m, n, k);
+  const GemmBatch one{};
+  const GemmBatch& bt = batch != nullptr ? *batch : one;
+  if (bt.count == 0) return cudaSuccess;
+  const dim3 grid((n + TN - 1) / TN, (m + TM - 1) / TM, bt.count);
+  if (grid.y > 65535u || grid.z > 65535u) return cudaErrorInvalidValue;
+  if (bt.b_trans)
+    sgemm_fma_kernel<true><<<grid, 256, 0, stream>>>(a, lda, b, ldb, c, ldc, m, n, k, bt.stride_a, bt.stride_b,
+                                                     bt.stride_c);
+  else
+    sgemm_fma_kernel<false><<<grid, 256, 0, stream>>>(a, lda, b, ldb, c, ldc, m, n, k, bt.stride_a, bt.stride_b,
+                                                      bt.stride_c);
   return cudaGetLastError();
 }
 

@@ -63,10 +63,14 @@ __host__ __device__ inline uint32_t round_up(uint32_t x, uint32_t g) { return (x
 // ------------------------------------------------------------------ split
 // hi = tf32(v), lo = tf32(v - hi); v = 0 outside [rows, cols).
 // Each thread produces 4 consecutive padded columns of one row.
+// blockIdx.y selects the batch entry: src + y * src_stride, outputs + y * rows_p * cols_p.
 __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ src, uint64_t ld,
                                                          uint32_t rows, uint32_t cols,
                                                          float* __restrict__ hi, float* __restrict__ lo,
-                                                         uint32_t rows_p, uint32_t cols_p) {
+                                                         uint32_t rows_p, uint32_t cols_p, uint64_t src_stride) {
+  src += blockIdx.y * src_stride;
+  hi += static_cast<uint64_t>(blockIdx.y) * rows_p * cols_p;
+  lo += static_cast<uint64_t>(blockIdx.y) * rows_p * cols_p;
   const uint64_t groups_per_row = cols_p / 4;
   const uint64_t total = static_cast<uint64_t>(rows_p) * groups_per_row;
   const bool vec_ok = (ld % 4 == 0) && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
@@ -100,11 +104,15 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
 
 // B is [k x n] row-major; writes hi/lo of B^T as [n_p x k_p] (K-major), zero padded.
 // 32x32 tiles through shared memory keep both the read and the write coalesced.
+// blockIdx.z selects the batch entry: b + z * b_stride, outputs + z * np * kp.
 __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ b, uint64_t ldb,
                                                               uint32_t k, uint32_t n,
                                                               float* __restrict__ hi, float* __restrict__ lo,
-                                                              uint32_t kp) {
+                                                              uint32_t kp, uint32_t np, uint64_t b_stride) {
   __shared__ float tile[32][33];
+  b += blockIdx.z * b_stride;
+  hi += static_cast<uint64_t>(blockIdx.z) * np * kp;
+  lo += static_cast<uint64_t>(blockIdx.z) * np * kp;
   const uint32_t n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
   const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
 #pragma unroll
@@ -142,7 +150,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     sgemm3x_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                    const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
                    float* __restrict__ c, uint32_t m, uint32_t n, uint64_t ldc, uint32_t num_kb,
-                   uint32_t tiles_m, uint32_t tiles_n, unsigned int* __restrict__ err) {
+                   uint32_t tiles_m, uint32_t tiles_n, uint64_t stride_c, const float* __restrict__ residual,
+                   uint64_t ldr, unsigned int* __restrict__ err) {
   using Cfg = TileCfg<BK>;
   constexpr uint32_t S = Cfg::STAGES;
   constexpr uint32_t KBC = KC / BK;  // k-blocks per accumulation chunk
@@ -161,13 +170,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t num_chunks = (num_kb + KBC - 1) / KBC;
 
-  // Grouped rasterisation: GROUP_M tile rows sweep all tile columns together.
-  const uint32_t t = blockIdx.x;
+  // Batch entry, then grouped rasterisation inside it: GROUP_M tile rows
+  // sweep all tile columns together.  Split buffers stack the batch entries
+  // along rows (Mp and Np rows each), so a tile never straddles two entries.
+  const uint32_t tiles_per_entry = tiles_m * tiles_n;
+  const uint32_t entry = blockIdx.x / tiles_per_entry;
+  const uint32_t t = blockIdx.x % tiles_per_entry;
   const uint32_t per_group = GROUP_M * tiles_n;
   const uint32_t first_m = (t / per_group) * GROUP_M;
   const uint32_t group_rows = min(tiles_m - first_m, GROUP_M);
   const uint32_t tile_m = first_m + (t % per_group) % group_rows;
   const uint32_t tile_n = (t % per_group) / group_rows;
+  c += entry * stride_c;
+  if (residual != nullptr) residual += entry * stride_c;
 
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < S; ++s) {
@@ -201,8 +216,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
-      const int row_a = static_cast<int>(tile_m * BM);
-      const int row_b = static_cast<int>(tile_n * BN);
+      const int row_a = static_cast<int>(entry * tiles_m * BM + tile_m * BM);
+      const int row_b = static_cast<int>(entry * tiles_n * BN + tile_n * BN);
       uint32_t kb = 0;
       for (; kb < num_kb; ++kb) {
         const uint32_t s = kb % S;
@@ -298,17 +313,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (ok && num_kb > 0) {
       const uint32_t row = tile_m * BM + q * 32 + lane;
       const uint32_t col0 = tile_n * BN + h * 128u;
-      const bool vec_ok = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0);
+      const bool vec_ok = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) &&
+                          (residual == nullptr ||
+                           ((ldr % 4 == 0) && ((reinterpret_cast<uintptr_t>(residual) & 15u) == 0)));
       if (row < m && col0 < n) {
         float* dst = c + static_cast<uint64_t>(row) * ldc + col0;
+        // Optional fused residual epilogue: C = R + A * B (R may alias C).
+        const float* src = residual != nullptr ? residual + static_cast<uint64_t>(row) * ldr + col0 : nullptr;
         if (vec_ok && col0 + 128 <= n) {
 #pragma unroll
-          for (int j = 0; j < 128; j += 4)
-            *reinterpret_cast<float4*>(dst + j) = make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
+          for (int j = 0; j < 128; j += 4) {
+            float4 v = make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
+            if (src != nullptr) {
+              const float4 r4 = *reinterpret_cast<const float4*>(src + j);
+              v.x += r4.x;
+              v.y += r4.y;
+              v.z += r4.z;
+              v.w += r4.w;
+            }
+            *reinterpret_cast<float4*>(dst + j) = v;
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 128; ++j)
-            if (col0 + j < n) dst[j] = run[j];
+            if (col0 + j < n) dst[j] = src != nullptr ? src[j] + run[j] : run[j];
         }
       }
     }
@@ -367,23 +395,64 @@ bool make_operand_map(CUtensorMap* map, const float* base, uint32_t rows, uint32
 template <int BK>
 cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
                         uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, uint32_t batch, uint64_t stride_c, const float* residual = nullptr,
+                        uint64_t ldr = 0) {
   using Cfg = TileCfg<BK>;
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-  if (!make_operand_map(&m_ahi, ahi, d.mp, d.kp, BK, BM) || !make_operand_map(&m_alo, alo, d.mp, d.kp, BK, BM) ||
-      !make_operand_map(&m_bhi, bhi, d.np, d.kp, BK, BN) || !make_operand_map(&m_blo, blo, d.np, d.kp, BK, BN))
+  const uint32_t rows_a = d.mp * batch, rows_b = d.np * batch;
+  if (!make_operand_map(&m_ahi, ahi, rows_a, d.kp, BK, BM) || !make_operand_map(&m_alo, alo, rows_a, d.kp, BK, BM) ||
+      !make_operand_map(&m_bhi, bhi, rows_b, d.kp, BK, BN) || !make_operand_map(&m_blo, blo, rows_b, d.kp, BK, BN))
     return cudaErrorInvalidValue;
   // Set on every launch: the attribute belongs to the current device's context.
   cudaError_t e = cudaFuncSetAttribute(sgemm3x_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(Cfg::SMEM_BYTES));
   if (e != cudaSuccess) return e;
   const uint32_t tiles_m = d.mp / BM, tiles_n = d.np / BN;
-  sgemm3x_kernel<BK><<<tiles_m * tiles_n, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(
-      m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, err);
+  const uint64_t grid = static_cast<uint64_t>(tiles_m) * tiles_n * batch;
+  if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
+  sgemm3x_kernel<BK><<<static_cast<uint32_t>(grid), NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(
+      m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, stride_c, residual, ldr, err);
   return cudaGetLastError();
 }
 
 }  // namespace
+
+// ------------------------------------------------------------------ pre-split weights
+// A weight operand B [k][n] that many products reuse is split once into the
+// K-major hi/lo layout; later products only split their activation operand.
+uint64_t split_b_elems(uint32_t n, uint32_t k) {
+  const SplitDims d = split_dims(1, n, k);
+  return static_cast<uint64_t>(d.np) * d.kp;
+}
+
+cudaError_t sgemm_tc_split_b(const float* b, uint64_t ldb, uint32_t k, uint32_t n, float* bhi, float* blo,
+                             cudaStream_t stream) {
+  if (k == 0 || n == 0) return cudaSuccess;
+  const SplitDims d = split_dims(1, n, k);
+  split_transpose_kernel<<<dim3(d.np / 32, d.kp / 32, 1), 256, 0, stream>>>(b, ldb, k, n, bhi, blo, d.kp, d.np, 0);
+  return cudaGetLastError();
+}
+
+uint64_t sgemm_tc_a_scratch_bytes(uint32_t m, uint32_t k) {
+  const SplitDims d = split_dims(m, 1, k);
+  return 2ull * sizeof(float) * d.mp * d.kp;
+}
+
+cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, const float* blo, float* c,
+                              uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* a_scratch, unsigned int* err,
+                              cudaStream_t stream, const float* residual, uint64_t ldr) {
+  if (m == 0 || n == 0 || k == 0) return cudaSuccess;
+  if ((reinterpret_cast<uintptr_t>(a_scratch) & 1023u) != 0) return cudaErrorInvalidValue;
+  const SplitDims d = split_dims(m, n, k);
+  float* ahi = static_cast<float*>(a_scratch);
+  float* alo = ahi + static_cast<uint64_t>(d.mp) * d.kp;
+  const uint64_t groups = static_cast<uint64_t>(d.mp) * (d.kp / 4);
+  const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((groups + 255) / 256, 148ull * 16));
+  split_rows_kernel<<<dim3(blocks, 1), 256, 0, stream>>>(a, lda, m, k, ahi, alo, d.mp, d.kp, 0);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, 0, residual, ldr);
+}
 
 // ------------------------------------------------------------------ no-allocation variant
 // Scratch for oct_b200_sgemm_device_noalloc: some callers cannot call
@@ -420,35 +489,51 @@ SplitDims split_dims(uint32_t m, uint32_t n, uint32_t k) {
   return SplitDims{round_up(m, BM), round_up(n, BN), round_up(k, KPAD)};
 }
 
-uint64_t sgemm_tc_scratch_bytes(uint32_t m, uint32_t n, uint32_t k) {
+uint64_t sgemm_tc_scratch_bytes(uint32_t m, uint32_t n, uint32_t k, uint32_t batch) {
   const SplitDims d = split_dims(m, n, k);
-  return 2ull * sizeof(float) * (static_cast<uint64_t>(d.mp) * d.kp + static_cast<uint64_t>(d.np) * d.kp);
+  return 2ull * sizeof(float) * batch *
+         (static_cast<uint64_t>(d.mp) * d.kp + static_cast<uint64_t>(d.np) * d.kp);
 }
 
 cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
                      uint32_t m, uint32_t n, uint32_t k, void* scratch, unsigned int* err, int bk,
-                     cudaStream_t stream, const SgemmEvents* events) {
+                     cudaStream_t stream, const SgemmEvents* events, const GemmBatch* batch) {
   if (m == 0 || n == 0 || k == 0) return cudaSuccess;
   if (bk != 16 && bk != 32) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(scratch) & 1023u) != 0) return cudaErrorInvalidValue;
+  const GemmBatch one{};
+  const GemmBatch& bt = batch != nullptr ? *batch : one;
+  if (bt.count == 0) return cudaSuccess;
+  if (bt.count > 65535u) return cudaErrorInvalidValue;
   const SplitDims d = split_dims(m, n, k);
+  const uint64_t a_elems = static_cast<uint64_t>(d.mp) * d.kp * bt.count;
+  const uint64_t b_elems = static_cast<uint64_t>(d.np) * d.kp * bt.count;
+  if (a_elems > 0x7FFFFFFFull * 4 || b_elems > 0x7FFFFFFFull * 4) return cudaErrorInvalidValue;
   float* ahi = static_cast<float*>(scratch);
-  float* alo = ahi + static_cast<uint64_t>(d.mp) * d.kp;
-  float* bhi = alo + static_cast<uint64_t>(d.mp) * d.kp;
-  float* blo = bhi + static_cast<uint64_t>(d.np) * d.kp;
+  float* alo = ahi + a_elems;
+  float* bhi = alo + a_elems;
+  float* blo = bhi + b_elems;
 
   if (events != nullptr && events->split_begin != nullptr) cudaEventRecord(events->split_begin, stream);
   const uint64_t groups = static_cast<uint64_t>(d.mp) * (d.kp / 4);
   const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((groups + 255) / 256, 148ull * 16));
-  split_rows_kernel<<<blocks, 256, 0, stream>>>(a, lda, m, k, ahi, alo, d.mp, d.kp);
+  split_rows_kernel<<<dim3(blocks, bt.count), 256, 0, stream>>>(a, lda, m, k, ahi, alo, d.mp, d.kp, bt.stride_a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  split_transpose_kernel<<<dim3(d.np / 32, d.kp / 32), 256, 0, stream>>>(b, ldb, k, n, bhi, blo, d.kp);
+  if (bt.b_trans) {
+    // B is [n][k]: already K-major, split it like A.
+    const uint64_t bgroups = static_cast<uint64_t>(d.np) * (d.kp / 4);
+    const uint32_t bblocks = static_cast<uint32_t>(std::min<uint64_t>((bgroups + 255) / 256, 148ull * 16));
+    split_rows_kernel<<<dim3(bblocks, bt.count), 256, 0, stream>>>(b, ldb, n, k, bhi, blo, d.np, d.kp, bt.stride_b);
+  } else {
+    split_transpose_kernel<<<dim3(d.np / 32, d.kp / 32, bt.count), 256, 0, stream>>>(b, ldb, k, n, bhi, blo, d.kp,
+                                                                                     d.np, bt.stride_b);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (events != nullptr && events->main_begin != nullptr) cudaEventRecord(events->main_begin, stream);
-  e = bk == 16 ? launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream)
-               : launch_main<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream);
+  e = bk == 16 ? launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.stride_c)
+               : launch_main<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.stride_c);
   if (events != nullptr && events->main_end != nullptr) cudaEventRecord(events->main_end, stream);
   return e;
 }

@@ -235,6 +235,33 @@ class PrometheusGemma4E2BM1InputRmsNormResult(C.Structure):
     ]
 
 
+class OctB200BlockConfig(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("family", C.c_uint32),
+        ("hidden", C.c_uint32),
+        ("heads", C.c_uint32),
+        ("kv_heads", C.c_uint32),
+        ("head_dim", C.c_uint32),
+        ("ffn", C.c_uint32),
+        ("seq_len", C.c_uint32),
+        ("max_batch", C.c_uint32),
+        ("eps", C.c_float),
+        ("rope_base", C.c_float),
+        ("grid_w", C.c_uint32),
+        ("rope_frame", C.c_uint32),
+        ("tp_rank", C.c_uint32),
+        ("tp_world", C.c_uint32),
+        ("nccl_id", C.c_uint8 * 128),
+    ]
+
+
+BLOCK_GEMMA, BLOCK_DIT = 1, 2
+GEMMA_SLOTS = {"norm1": 0, "wqkv": 1, "wo": 2, "norm2": 3, "wgu": 4, "wd": 5}
+DIT_SLOTS = {"ada_w": 0, "ada_b": 1, "attn_norm1": 2, "wqkv": 3, "q_norm": 4, "k_norm": 5, "wo": 6,
+             "attn_norm2": 7, "ffn_norm1": 8, "w13": 9, "w2": 10, "ffn_norm2": 11}
+
+
 # ---- signatures ---------------------------------------------------------------
 _vp, _u32, _u64, _i32p, _u32p = C.c_void_p, C.c_uint32, C.c_uint64, C.POINTER(C.c_int), C.POINTER(C.c_uint32)
 
@@ -267,6 +294,9 @@ SIGNATURES = {
     "oct_b200_sgemm_device": (C.c_int, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp, _i32p]),
     "oct_b200_sgemm_device_ld": (
         C.c_int, [_vp, _vp, _u64, _vp, _u64, _vp, _u64, _u32, _u32, _u32, _u32, _vp, _i32p]),
+    "oct_b200_sgemm_batched_device": (
+        C.c_int, [_vp, _vp, _u64, _u64, _vp, _u64, _u64, _u32, _vp, _u64, _u64, _u32, _u32, _u32, _u32, _u32, _vp,
+                  _i32p]),
     "oct_b200_reduction_device": (C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _i32p]),
     "oct_b200_rmsnorm_device": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, C.c_float, _vp, _i32p]),
     "oct_b200_sync_status": (C.c_int, [_vp, _vp, _i32p]),
@@ -275,6 +305,12 @@ SIGNATURES = {
     "oct_b200_set_kernel_timing": (C.c_int, [_vp, C.c_int]),
     "oct_b200_read_kernel_timing": (
         C.c_int, [_vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_uint32)]),
+    "oct_b200_nccl_unique_id": (C.c_int, [_vp]),
+    "oct_b200_block_create": (C.c_int, [_vp, C.POINTER(OctB200BlockConfig), C.POINTER(C.c_uint64), _i32p]),
+    "oct_b200_block_set_weight": (C.c_int, [_vp, C.c_uint64, _u32, _vp, _u64, _u32]),
+    "oct_b200_block_forward_device": (C.c_int, [_vp, C.c_uint64, _vp, _vp, _u32, _vp, _vp, _i32p]),
+    "oct_b200_block_forward": (C.c_int, [_vp, C.c_uint64, _vp, _vp, _u32, _vp, _i32p]),
+    "oct_b200_block_destroy": (C.c_int, [_vp, C.c_uint64]),
     "oct_b200_build_info": (C.c_char_p, []),
 }
 
@@ -521,6 +557,17 @@ class Runtime:
             raise ReactorIssue(ReactorIssue.SGEMM_FAILED, f"device sgemm rc={rc} detail={detail.value}",
                                detail=detail.value)
 
+    def sgemm_batched_device(self, a, lda: int, stride_a: int, b, ldb: int, stride_b: int, b_trans: bool, c,
+                             ldc: int, stride_c: int, batch: int, m: int, n: int, k: int,
+                             variant: int = SGEMM_AUTO, stream=None) -> None:
+        detail = C.c_int()
+        rc = self.lib.oct_b200_sgemm_batched_device(self.handle, _ptr(a), lda, stride_a, _ptr(b), ldb, stride_b,
+                                                    1 if b_trans else 0, _ptr(c), ldc, stride_c, batch, m, n, k,
+                                                    variant, _stream_ptr(stream), C.byref(detail))
+        if rc != PROM_OK:
+            raise ReactorIssue(ReactorIssue.SGEMM_FAILED, f"batched sgemm rc={rc} detail={detail.value}",
+                               detail=detail.value)
+
     def reduction_device(self, x, y, rows: int, width: int, operation: int, stream=None) -> None:
         detail = C.c_int()
         rc = self.lib.oct_b200_reduction_device(self.handle, _ptr(x), _ptr(y), rows, width, operation,
@@ -551,6 +598,83 @@ class Runtime:
         if rc != PROM_OK:
             raise RuntimeError(f"kernel timing read failed rc={rc}")
         return s.value, m.value, n.value
+
+
+    # -- transformer block
+    def block(self, family: int, *, hidden: int, heads: int, kv_heads: int, head_dim: int, ffn: int, seq_len: int,
+              max_batch: int, eps: float, rope_base: float, grid_w: int = 0, rope_frame: int = 0, tp_rank: int = 0,
+              tp_world: int = 1, nccl_id: bytes = b"") -> "Block":
+        return Block(self, family, hidden=hidden, heads=heads, kv_heads=kv_heads, head_dim=head_dim, ffn=ffn,
+                     seq_len=seq_len, max_batch=max_batch, eps=eps, rope_base=rope_base, grid_w=grid_w,
+                     rope_frame=rope_frame, tp_rank=tp_rank, tp_world=tp_world, nccl_id=nccl_id)
+
+
+def nccl_unique_id(lib) -> bytes:
+    buf = (C.c_uint8 * 128)()
+    if lib.oct_b200_nccl_unique_id(C.cast(buf, C.c_void_p)) != PROM_OK:
+        raise RuntimeError("ncclGetUniqueId failed (libnccl.so.2 not loadable?)")
+    return bytes(buf)
+
+
+class Block:
+    """A transformer block on one reactor handle (oct_b200_block_*)."""
+
+    def __init__(self, rt: Runtime, family: int, **cfg):
+        self.rt, self.lib = rt, rt.lib
+        c = OctB200BlockConfig()
+        c.struct_size = C.sizeof(c)
+        c.family = family
+        for key in ("hidden", "heads", "kv_heads", "head_dim", "ffn", "seq_len", "max_batch", "grid_w", "rope_frame",
+                    "tp_rank", "tp_world"):
+            setattr(c, key, int(cfg[key]))
+        c.eps, c.rope_base = float(cfg["eps"]), float(cfg["rope_base"])
+        nid = cfg.get("nccl_id") or b""
+        for i, v in enumerate(nid[:128]):
+            c.nccl_id[i] = v
+        self.config = c
+        self.family = family
+        bid, detail = C.c_uint64(), C.c_int()
+        rc = self.lib.oct_b200_block_create(rt.handle, C.byref(c), C.byref(bid), C.byref(detail))
+        if rc != PROM_OK:
+            raise RuntimeError(f"block create rc={rc} detail={detail.value}")
+        self.id = bid.value
+
+    def set_weights(self, weights: dict) -> None:
+        slots = GEMMA_SLOTS if self.family == BLOCK_GEMMA else DIT_SLOTS
+        for name, arr in weights.items():
+            if hasattr(arr, "data_ptr"):
+                ptr, count, on_dev = arr.data_ptr(), arr.numel(), 1 if arr.is_cuda else 0
+            else:
+                arr = np.ascontiguousarray(arr, dtype=np.float32)
+                ptr, count, on_dev = arr.ctypes.data, arr.size, 0
+            rc = self.lib.oct_b200_block_set_weight(self.rt.handle, self.id, slots[name], ptr, count, on_dev)
+            if rc != PROM_OK:
+                raise RuntimeError(f"set_weight {name} rc={rc}")
+
+    def forward_device(self, x, y, batch: int, timesteps=None, stream=None) -> None:
+        ts = None if timesteps is None else np.ascontiguousarray(timesteps, dtype=np.float32)
+        detail = C.c_int()
+        rc = self.lib.oct_b200_block_forward_device(self.rt.handle, self.id, _ptr(x), _ptr(y), batch,
+                                                    None if ts is None else ts.ctypes.data, _stream_ptr(stream),
+                                                    C.byref(detail))
+        if rc != PROM_OK:
+            raise RuntimeError(f"block forward rc={rc} detail={detail.value}")
+
+    def forward(self, x: np.ndarray, batch: int, timesteps=None) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty_like(x)
+        ts = None if timesteps is None else np.ascontiguousarray(timesteps, dtype=np.float32)
+        detail = C.c_int()
+        rc = self.lib.oct_b200_block_forward(self.rt.handle, self.id, x.ctypes.data, y.ctypes.data, batch,
+                                             None if ts is None else ts.ctypes.data, C.byref(detail))
+        if rc != PROM_OK:
+            raise RuntimeError(f"block forward rc={rc} detail={detail.value}")
+        return y
+
+    def close(self) -> None:
+        if getattr(self, "id", None) is not None:
+            self.lib.oct_b200_block_destroy(self.rt.handle, self.id)
+            self.id = None
 
 
 def _stream_ptr(stream) -> int:

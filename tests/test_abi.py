@@ -277,3 +277,31 @@ def test_planner_replay_id_is_fnv1a_over_stage_words(lib):
     assert plan.replay_id == h
     # composed softmax: max partial/final, exp-sum partial/final, normalise
     assert [plan.stages[i].stage_role for i in range(plan.stage_count)] == [2, 2, 3, 1, 4]
+
+
+def test_block_create_without_device_is_rejected(lib):
+    h = _handle(lib, R.TESTCFG_FAIL_DEVICE_CREATE)
+    try:
+        cfg = R.OctB200BlockConfig()
+        cfg.struct_size = C.sizeof(cfg)
+        cfg.family, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim = 1, 512, 4, 1, 128
+        cfg.ffn, cfg.seq_len, cfg.max_batch, cfg.tp_world = 1024, 128, 1, 1
+        bid, detail = C.c_uint64(), C.c_int()
+        rc = lib.oct_b200_block_create(h, C.byref(cfg), C.byref(bid), C.byref(detail))
+        assert rc == R.PROM_ERROR and detail.value == -6006
+        cfg.struct_size = 8  # too small: rejected before anything else
+        rc = lib.oct_b200_block_create(h, C.byref(cfg), C.byref(bid), C.byref(detail))
+        assert rc == R.PROM_ERROR and detail.value == -7010
+    finally:
+        lib.prometheus_reactor_runtime_destroy(h)
+
+
+def test_block_oracle_flops_match_baseline_accounting():
+    from oracle import blocks as OB
+    g = OB.gemma_config()
+    per_token_linear = 2 * 2048 * 2560 + 2 * 2048 * 2048 + 3 * 2 * 2048 * 16384
+    attn = 1024 * 1025 / 2 * 8 * 4 * 256 * 4
+    assert OB.flops_per_forward(g, 4) == pytest.approx(4096 * per_token_linear + attn)
+    d = OB.dit_config()
+    assert OB.flops_per_forward(d, 2) == pytest.approx(8192 * (2 * 3072 * 9216 + 2 * 3072 * 3072 + 6 * 3072 * 8192)
+                                                       + 4096 ** 2 * 24 * 512 * 2)
