@@ -296,6 +296,60 @@ def block_measurements(rt, torch, stream, iters: int = 5) -> list[dict]:
     return res
 
 
+def tp_block_measurements(rt, torch, dist, rank: int, world: int, stream, iters: int = 5) -> list[dict]:
+    """Gemma / DiT blocks tensor-parallel over all ranks (NCCL inside the block): global tokens/s."""
+    from oct_b200 import reactor as R
+    from oct_b200 import tp
+    from oracle import blocks as OB  # shapes and flop counts only
+    ids = [R.nccl_unique_id(rt.lib) if rank == 0 else None]
+    dist.broadcast_object_list(ids, src=0)
+    pk, _ = peaks()
+    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
+    res = []
+    for name, cfg, batch in (("gemma_block_tp", OB.gemma_config(), 4), ("dit_block_tp", OB.dit_config(), 2)):
+        if cfg.heads % world or cfg.ffn % world:
+            continue
+        rcfg = tp.rank_config(cfg, rank, world)
+        fam = R.BLOCK_GEMMA if cfg.family == OB.GEMMA else R.BLOCK_DIT
+        blk = rt.block(fam, hidden=rcfg.hidden, heads=rcfg.heads, kv_heads=rcfg.kv_heads, head_dim=rcfg.head_dim,
+                       ffn=rcfg.ffn, seq_len=rcfg.seq_len, max_batch=batch, eps=rcfg.eps, rope_base=rcfg.rope_base,
+                       grid_w=rcfg.grid_w, rope_frame=rcfg.rope_frame, tp_rank=rank, tp_world=world,
+                       nccl_id=ids[0])
+        g = torch.Generator(device="cuda").manual_seed(99)
+        weights = {}
+        for wname, shape in OB.weight_shapes(rcfg).items():
+            t = torch.randn(*shape, device="cuda", generator=g)
+            weights[wname] = (t * 0.02 + 1.0) if len(shape) == 1 and wname != "ada_b" else (
+                t * 0.0 if wname == "ada_b" else t * 0.02)
+        blk.set_weights(weights)
+        del weights
+        T = batch * cfg.seq_len
+        x = torch.randn(T, cfg.hidden, device="cuda", generator=torch.Generator(device="cuda").manual_seed(7))
+        y = torch.empty_like(x)
+        ts = [500.0, 250.0][:batch] if cfg.family == OB.DIT else None
+        for _ in range(2):
+            blk.forward_device(x, y, batch, ts, stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            blk.forward_device(x, y, batch, ts, stream)
+        e1.record(stream)
+        e1.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / iters], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        flops = OB.flops_per_forward(cfg, batch)
+        res.append({"kernel": name, "tp": world, "batch": batch, "seq": cfg.seq_len, "ms": round(ms, 3),
+                    "tokens/s": round(T / (ms * 1e-3), 1), "TFLOP/s": round(flops / (ms * 1e-3) / 1e12, 2),
+                    "frac_of_3xtf32_peak_all_gpus": round(flops / (ms * 1e-3) / 1e12 / (peak * world), 3)})
+        blk.close()
+        del x, y
+        torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args) -> None:
     import torch
     from oct_b200 import reactor as R
@@ -401,6 +455,8 @@ def run_ours(args) -> None:
 
     secondary = None
     cpu = None
+    if world > 1 and not args.no_secondary:
+        secondary = tp_block_measurements(rt, torch, dist, rank, world, stream)
     if rank == 0 and world == 1:
         if not args.no_secondary:
             secondary = secondary_measurements(rt, torch, pk["hbm_gbs"])

@@ -174,8 +174,15 @@ def silu(x: np.ndarray) -> np.ndarray:
 
 
 # ---------------------------------------------------------------- blocks
-def gemma_forward(cfg: BlockConfig, w: dict, x: np.ndarray) -> np.ndarray:
-    """x [B*S, d] float32 -> [B*S, d] float64."""
+def _identity(a):
+    return a
+
+
+def gemma_forward(cfg: BlockConfig, w: dict, x: np.ndarray, all_reduce=_identity) -> np.ndarray:
+    """x [B*S, d] float32 -> [B*S, d] float64.
+
+    Under tensor parallelism cfg.heads / cfg.ffn are one rank's share, `w` its
+    shard, and `all_reduce` sums the two row-parallel partial products."""
     d, H, KV, hd, F, S = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.seq_len
     W = {k: v.astype(np.float64) for k, v in w.items()}
     x64 = x.astype(np.float64)
@@ -192,16 +199,16 @@ def gemma_forward(cfg: BlockConfig, w: dict, x: np.ndarray) -> np.ndarray:
         q = rope_half_split(q, pos, cfg.rope_base)
         k = rope_half_split(k, pos, cfg.rope_base)
         o = attention(q, k, v, 1.0 / math.sqrt(hd), causal=True)
-        x1 = xs + o @ W["wo"]
+        x1 = xs + all_reduce(o @ W["wo"])
         h2 = rmsnorm(x1, W["norm2"], cfg.eps)
         gu = h2 @ W["wgu"]
         act = gelu_tanh(gu[:, :F]) * gu[:, F:]
-        out[s0:s0 + S] = x1 + act @ W["wd"]
+        out[s0:s0 + S] = x1 + all_reduce(act @ W["wd"])
     return out
 
 
-def dit_forward(cfg: BlockConfig, w: dict, x: np.ndarray, timesteps) -> np.ndarray:
-    """x [B*S, d] float32, one timestep per batch item -> [B*S, d] float64."""
+def dit_forward(cfg: BlockConfig, w: dict, x: np.ndarray, timesteps, all_reduce=_identity) -> np.ndarray:
+    """x [B*S, d] float32, one timestep per batch item -> [B*S, d] float64 (TP as gemma_forward)."""
     d, H, hd, F, S = cfg.hidden, cfg.heads, cfg.head_dim, cfg.ffn, cfg.seq_len
     W = {k: v.astype(np.float64) for k, v in w.items()}
     x64 = x.astype(np.float64)
@@ -224,18 +231,20 @@ def dit_forward(cfg: BlockConfig, w: dict, x: np.ndarray, timesteps) -> np.ndarr
         q = rope_3axis(q, coords, cfg.rope_base, cfg.rope_axes)
         k = rope_3axis(k, coords, cfg.rope_base, cfg.rope_axes)
         o = attention(q, k, v, 1.0 / math.sqrt(hd), causal=False)
-        n2 = rmsnorm(o @ W["wo"], W["attn_norm2"], cfg.eps)
+        n2 = rmsnorm(all_reduce(o @ W["wo"]), W["attn_norm2"], cfg.eps)
         res = xs + gate_a * n2
         fin = rmsnorm(res, W["ffn_norm1"], cfg.eps) * scale_m + shift_m
         h13 = fin @ W["w13"]
         hidden = silu(h13[:, :F]) * h13[:, F:]
-        fo = rmsnorm(hidden @ W["w2"], W["ffn_norm2"], cfg.eps)
+        fo = rmsnorm(all_reduce(hidden @ W["w2"]), W["ffn_norm2"], cfg.eps)
         out[b * S:(b + 1) * S] = res + gate_m * fo
     return out
 
 
-def forward(cfg: BlockConfig, w: dict, x: np.ndarray, timesteps=None) -> np.ndarray:
-    return gemma_forward(cfg, w, x) if cfg.family == GEMMA else dit_forward(cfg, w, x, timesteps)
+def forward(cfg: BlockConfig, w: dict, x: np.ndarray, timesteps=None, all_reduce=_identity) -> np.ndarray:
+    if cfg.family == GEMMA:
+        return gemma_forward(cfg, w, x, all_reduce)
+    return dit_forward(cfg, w, x, timesteps, all_reduce)
 
 
 def flops_per_forward(cfg: BlockConfig, batch: int) -> float:
