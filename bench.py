@@ -337,7 +337,7 @@ def tp_block_measurements(rt, torch, dist, rank: int, world: int, stream, iters:
             blk.forward_device(x, y, batch, ts, stream)
         e1.record(stream)
         e1.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / iters], device="cuda", dtype=torch.float64)
+        t = torch.tensor([e0.elapsed_time(e1) / iters], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         flops = OB.flops_per_forward(cfg, batch)
@@ -360,8 +360,11 @@ def run_ours(args) -> None:
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
+        # Control plane only (barriers, the max-over-ranks time, the NCCL id
+        # broadcast) runs over gloo; the data-path collectives of the
+        # tensor-parallel block use the library's own NCCL communicator over NVLink.
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+        dist.init_process_group("gloo", timeout=timedelta(seconds=180))
     rt = R.Runtime()
     m, n, k = args.m, args.n, args.k
     stream = torch.cuda.current_stream()
@@ -402,7 +405,7 @@ def run_ours(args) -> None:
     st = rt.sync_status(stream)
     if not st.ok:
         raise RuntimeError(f"timed run failed: {st}")
-    t = torch.tensor([ms_total], device="cuda", dtype=torch.float64)
+    t = torch.tensor([ms_total], dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
@@ -446,7 +449,7 @@ def run_ours(args) -> None:
             _, s = rt.sgemm_with_status(m, n, k, na, nb, out=nc)
             if not s.ok:
                 raise RuntimeError(f"e2e step failed {s}")
-        tt = torch.tensor([time.perf_counter() - t0], device="cuda", dtype=torch.float64)
+        tt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64)
         if dist is not None:
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e = {"value": flops * world * e2e_steps / float(tt.item()) / 1e12, "unit": "TFLOP/s",

@@ -30,6 +30,7 @@
 #include <cfloat>
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <dlfcn.h>
 #include <mutex>
@@ -266,12 +267,14 @@ typedef int (*NcclCommInitRankFn)(void** comm, int nranks, NcclUniqueIdBytes id,
 typedef int (*NcclAllReduceFn)(const void* send, void* recv, size_t count, int dtype, int op, void* comm,
                               cudaStream_t stream);
 typedef int (*NcclCommDestroyFn)(void* comm);
+typedef const char* (*NcclGetErrorStringFn)(int result);
 struct Nccl {
   bool ok = false;
   NcclGetUniqueIdFn get_id = nullptr;
   NcclCommInitRankFn init_rank = nullptr;
   NcclAllReduceFn all_reduce = nullptr;
   NcclCommDestroyFn destroy = nullptr;
+  NcclGetErrorStringFn error_string = nullptr;
 };
 Nccl& nccl() {
   static Nccl n;
@@ -284,6 +287,7 @@ Nccl& nccl() {
     n.init_rank = reinterpret_cast<NcclCommInitRankFn>(dlsym(h, "ncclCommInitRank"));
     n.all_reduce = reinterpret_cast<NcclAllReduceFn>(dlsym(h, "ncclAllReduce"));
     n.destroy = reinterpret_cast<NcclCommDestroyFn>(dlsym(h, "ncclCommDestroy"));
+    n.error_string = reinterpret_cast<NcclGetErrorStringFn>(dlsym(h, "ncclGetErrorString"));
     n.ok = n.get_id && n.init_rank && n.all_reduce && n.destroy;
   });
   return n;
@@ -375,7 +379,10 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
   if (build_rope_tables() != 0) return -4;
   if (d.tp_world > 1) {
     if (!nccl().ok || id == nullptr) return -5;
-    if (nccl().init_rank(&comm_, static_cast<int>(d.tp_world), *id, static_cast<int>(d.tp_rank)) != 0) {
+    const int nrc = nccl().init_rank(&comm_, static_cast<int>(d.tp_world), *id, static_cast<int>(d.tp_rank));
+    if (nrc != 0) {
+      std::fprintf(stderr, "oct_b200: ncclCommInitRank(rank %u of %u) failed: %d (%s)\n", d.tp_rank, d.tp_world, nrc,
+                   nccl().error_string != nullptr ? nccl().error_string(nrc) : "?");
       comm_ = nullptr;
       return -5;
     }
