@@ -301,8 +301,6 @@ def tp_block_measurements(rt, torch, dist, rank: int, world: int, stream, iters:
     from oct_b200 import reactor as R
     from oct_b200 import tp
     from oracle import blocks as OB  # shapes and flop counts only
-    ids = [R.nccl_unique_id(rt.lib) if rank == 0 else None]
-    dist.broadcast_object_list(ids, src=0)
     pk, _ = peaks()
     peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
     res = []
@@ -311,6 +309,9 @@ def tp_block_measurements(rt, torch, dist, rank: int, world: int, stream, iters:
             continue
         rcfg = tp.rank_config(cfg, rank, world)
         fam = R.BLOCK_GEMMA if cfg.family == OB.GEMMA else R.BLOCK_DIT
+        # one NCCL unique id seeds exactly one communicator: a fresh id per block
+        ids = [R.nccl_unique_id(rt.lib) if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
         blk = rt.block(fam, hidden=rcfg.hidden, heads=rcfg.heads, kv_heads=rcfg.kv_heads, head_dim=rcfg.head_dim,
                        ffn=rcfg.ffn, seq_len=rcfg.seq_len, max_batch=batch, eps=rcfg.eps, rope_base=rcfg.rope_base,
                        grid_w=rcfg.grid_w, rope_frame=rcfg.rope_frame, tp_rank=rank, tp_world=world,

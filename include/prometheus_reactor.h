@@ -671,7 +671,8 @@ typedef struct OctB200BlockConfig {
 } OctB200BlockConfig;
 
 /* ncclGetUniqueId (NCCL is dlopen'ed; nothing links it).  Rank 0 calls this
-   and shares the 128 bytes with the other ranks. */
+   and shares the 128 bytes with the other ranks.  One id seeds exactly one
+   communicator: create a fresh id for every tensor-parallel block. */
 PROM_REACTOR_API int oct_b200_nccl_unique_id(uint8_t* out_128_bytes);
 PROM_REACTOR_API int oct_b200_block_create(void* handle, const OctB200BlockConfig* config, uint64_t* out_block_id,
                                            int* out_detail_code);
