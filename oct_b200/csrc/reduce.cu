@@ -13,13 +13,15 @@
 // quotient is formed in double and rounded once.  exp itself is CUDA's fp32
 // `expf` (a few ulp), well inside the tolerance.
 //
-// Data movement: each CTA streams batches of rows HBM -> shared memory with
-// `cp.async.bulk` (the TMA engine's untiled copy) into a ring of NS slots, one
-// mbarrier per slot, so several batches are in flight while the current one is
-// reduced out of shared memory.  A row is read from HBM exactly once; softmax
-// and RMSNorm take all their passes over the shared-memory copy.
-//   W <= 1024 : a warp owns a row (8 rows per batch), warp-shuffle reductions.
-//   W <= 8192 : the whole 256-thread CTA owns a row, shuffle + shared reduction.
+// Data movement: rows stream HBM -> shared memory with `cp.async.bulk` (the TMA
+// engine's untiled copy) into rings of slots, one mbarrier per slot, so several
+// rows are in flight while the current one is reduced out of shared memory.  A
+// row is read from HBM exactly once; softmax and RMSNorm take all their passes
+// over the shared-memory copy.
+//   W <= 2048 : per-warp pipelines -- each warp owns its rows and its ring and
+//               reduces with warp shuffles only (no CTA-wide barrier);
+//   W <= 8192 : the whole 256-thread CTA owns a row, shuffle + shared reduction
+//               (more warps per SM to hide the longer per-row arithmetic).
 // Rows whose address or width is not 16-byte granular (or wider than 8192)
 // take a plain-load fallback kernel with the same arithmetic.
 #include <cuda_runtime.h>
@@ -268,6 +270,108 @@ __global__ void __launch_bounds__(THREADS) row_bulk_kernel(const float* __restri
   }
 }
 
+// Per-warp pipelines: every warp streams its own rows HBM -> shared memory,
+// one cp.async.bulk per row into a private ring of `ns` row slots with one
+// mbarrier each, and reduces a row with warp shuffles only.  No CTA-wide
+// barrier sits on the data path, so the warps of a CTA overlap their copies
+// and their arithmetic freely.  Used for rows up to 2048 floats.
+template <int OP>
+__global__ void __launch_bounds__(THREADS) row_warp_kernel(const float* __restrict__ in, uint64_t stride,
+                                                           float* __restrict__ out, float* __restrict__ inv_rms,
+                                                           const float* __restrict__ weight, float eps,
+                                                           uint32_t rows, uint32_t w, uint32_t ns, uint32_t wpc,
+                                                           unsigned long long* __restrict__ nonfinite,
+                                                           unsigned int* __restrict__ err) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp >= wpc) return;
+  float* ring = reinterpret_cast<float*>(smem_raw) + static_cast<uint64_t>(warp) * ns * w;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + static_cast<uint64_t>(wpc) * ns * w * 4) + warp * ns;
+  if (lane == 0) {
+    for (uint32_t s = 0; s < ns; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  __syncwarp();
+  const uint32_t gw = blockIdx.x * wpc + warp, nw = gridDim.x * wpc;
+  const uint32_t row_bytes = w * 4u;
+  uint32_t issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (lane == 0) {
+    for (uint32_t s = 0; s < ns; ++s) {
+      const uint64_t r = gw + static_cast<uint64_t>(s) * nw;
+      if (r >= rows) break;
+      mbar_arrive_expect_tx(&bars[s], row_bytes);
+      bulk_load(ring + s * w, in + r * stride, row_bytes, &bars[s]);
+      issued[s] += 1;
+    }
+  }
+  uint64_t first_bad = ~0ull;
+  bool aborted = false;
+  for (uint32_t j = 0;; ++j) {
+    const uint64_t r = gw + static_cast<uint64_t>(j) * nw;
+    if (r >= rows) break;
+    const uint32_t slot = j % ns;
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars[slot], (j / ns) & 1u, err, kErrWaitRow));
+    if (!ok) {
+      aborted = true;
+      break;
+    }
+    const float inv = process_row<OP, 32>(ring + slot * w, w, lane, r, out, weight, eps, nullptr, nullptr, first_bad);
+    if constexpr (OP == kRms) {
+      if (lane == 0 && inv_rms != nullptr) inv_rms[r] = inv;
+    }
+    __syncwarp();  // every lane is done reading this slot
+    if (lane == 0) {
+      const uint64_t nr = gw + static_cast<uint64_t>(j + ns) * nw;
+      if (nr < rows) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&bars[slot], row_bytes);
+        bulk_load(ring + slot * w, in + nr * stride, row_bytes, &bars[slot]);
+        issued[slot] += 1;
+      }
+    }
+  }
+  if (first_bad != ~0ull) atomicMin(nonfinite, static_cast<unsigned long long>(first_bad));
+  if (aborted && lane == 0) {
+    // drain: a slot's phases complete in order, so its newest copy is enough
+    for (uint32_t s = 0; s < ns; ++s)
+      if (issued[s] > 0 && !mbar_wait(&bars[s], (issued[s] - 1) & 1u, err, kErrWaitDrain)) break;
+  }
+}
+
+template <int OP>
+cudaError_t launch_warp(const float* in, uint64_t stride, float* out, float* inv_rms, const float* weight, float eps,
+                        uint32_t rows, uint32_t w, unsigned long long* nonfinite, unsigned int* err,
+                        cudaStream_t stream) {
+  const uint32_t row_bytes = w * 4u;
+  uint32_t wpc, ns;
+  if (row_bytes <= 2048u) {  // short rows: 8 warps, up to 8 slots each, 64 KB ring -> 3 CTAs per SM
+    wpc = 8;
+    ns = 65536u / (wpc * row_bytes);
+    ns = ns < 2 ? 2 : (ns > 8 ? 8 : ns);
+  } else if (row_bytes <= 8192u) {  // 8 warps x 3 slots, one CTA per SM
+    wpc = 8;
+    ns = 3;
+  } else {  // up to 16 KB rows: 4 warps x 3 slots
+    wpc = 4;
+    ns = 3;
+  }
+  const uint32_t smem = wpc * ns * row_bytes + wpc * ns * 8u;
+  auto kern = row_warp_kernel<OP>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpc * 32, smem);
+  if (per_sm < 1) per_sm = 1;
+  const uint32_t need = (rows + wpc - 1) / wpc;
+  const uint32_t cap = static_cast<uint32_t>(sms * per_sm);
+  kern<<<need < cap ? need : cap, wpc * 32, smem, stream>>>(in, stride, out, inv_rms, weight, eps, rows, w, ns, wpc,
+                                                            nonfinite, err);
+  return cudaGetLastError();
+}
+
 // Plain-load fallback: one CTA per row, any width / alignment.  Same arithmetic.
 template <int OP>
 __global__ void __launch_bounds__(THREADS) row_plain_kernel(const float* __restrict__ in, uint64_t stride,
@@ -364,7 +468,7 @@ cudaError_t dispatch(const float* in, uint64_t stride, float* out, float* inv_rm
   const bool rowwise_out = (OP == kSoftmax || OP == kRms);
   const bool aligned = (w % 4 == 0) && (stride % 4 == 0) && a16(in) && (!rowwise_out || a16(out)) &&
                        (weight == nullptr || a16(weight));
-  if (aligned && w <= 1024) return launch_bulk<OP, 32>(in, stride, out, inv_rms, weight, eps, rows, w, nonfinite, err, stream);
+  if (aligned && w <= 2048) return launch_warp<OP>(in, stride, out, inv_rms, weight, eps, rows, w, nonfinite, err, stream);
   if (aligned && w <= BULK_MAX_WIDTH)
     return launch_bulk<OP, THREADS>(in, stride, out, inv_rms, weight, eps, rows, w, nonfinite, err, stream);
   int dev = 0, sms = 148;
