@@ -61,6 +61,10 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-secondary", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU sample")
+    p.add_argument("--workload", default="sgemm",
+                   choices=["sgemm", "gemma_block", "dit_block", "reductions"],
+                   help="sgemm = the driver contract line; the others run one secondary measurement "
+                        "alone (for profiling) and print it as JSON")
     return p.parse_args()
 
 
@@ -190,8 +194,8 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
-    """Reductions at BASELINE configs[2] shapes (32768 rows) and the FMA control SGEMM."""
+def reduction_measurements(rt, torch, hbm_peak: float) -> list[dict]:
+    """Row reductions and RMSNorm at BASELINE configs[2] shapes (32768 rows)."""
     from oct_b200 import reactor as R
     out = []
     stream = torch.cuda.current_stream()
@@ -227,6 +231,14 @@ def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
         if not st.ok:
             raise RuntimeError(f"reduction status {st}")
         del x, y_full, y_row, inv
+    return out
+
+
+def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
+    """Reductions, the transformer blocks, the FMA control and the 32-deep tensor-core variant."""
+    from oct_b200 import reactor as R
+    out = reduction_measurements(rt, torch, hbm_peak)
+    stream = torch.cuda.current_stream()
     # Transformer blocks at BASELINE configs[3] / configs[4] (random init, synthetic tokens)
     out.extend(block_measurements(rt, torch, stream))
     # FMA control and the 32-deep tensor-core variant at the headline shape
@@ -250,7 +262,7 @@ def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
     return out
 
 
-def block_measurements(rt, torch, stream, iters: int = 5) -> list[dict]:
+def block_measurements(rt, torch, stream, iters: int = 5, only: str | None = None) -> list[dict]:
     """Tokens/s of one block forward at the BASELINE shapes, plus its tensor-peak fraction."""
     from oct_b200 import reactor as R
     from oracle import blocks as OB  # used only for the shapes and the flop count
@@ -258,6 +270,8 @@ def block_measurements(rt, torch, stream, iters: int = 5) -> list[dict]:
     peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
     res = []
     for name, cfg, batch in (("gemma_block", OB.gemma_config(), 4), ("dit_block", OB.dit_config(), 2)):
+        if only is not None and name != only:
+            continue
         fam = R.BLOCK_GEMMA if cfg.family == OB.GEMMA else R.BLOCK_DIT
         blk = rt.block(fam, hidden=cfg.hidden, heads=cfg.heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
                        ffn=cfg.ffn, seq_len=cfg.seq_len, max_batch=batch, eps=cfg.eps, rope_base=cfg.rope_base,
@@ -522,10 +536,27 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def run_single_workload(args) -> None:
+    """One secondary measurement alone, e.g. under ncu; prints it as JSON."""
+    import torch
+    from oct_b200 import reactor as R
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    rt = R.Runtime()
+    pk, _ = peaks()
+    if args.workload == "reductions":
+        res = reduction_measurements(rt, torch, pk["hbm_gbs"])
+    else:
+        res = block_measurements(rt, torch, torch.cuda.current_stream(), iters=max(1, args.steps), only=args.workload)
+    print(json.dumps({"workload": args.workload, "results": res}), flush=True)
+    rt.close()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "sgemm":
+        run_single_workload(args)
     else:
         run_ours(args)
 
