@@ -168,16 +168,23 @@ __global__ void qk_norm_rope3_kernel(float* __restrict__ buf, uint64_t ld, uint3
   }
 }
 
-// Scaled (optionally causal) softmax of score rows in place, one CTA per row
-// (row width <= 16 * 256).  Row r is query position r % seq; causal rows keep
-// keys 0..pos and write exact zeros beyond.  exp(s - max) in fp32, the sum in
+// Scaled (optionally causal) softmax of score rows, one CTA per row (row
+// width <= 16 * 256).  Row r is query position r % seq; causal rows keep keys
+// 0..pos and write exact zeros beyond.  exp(s - max) in fp32, the sum in
 // binary64, the quotient rounded once.
-__global__ void __launch_bounds__(NT) attn_softmax_kernel(float* __restrict__ s, uint32_t rows, uint32_t width,
-                                                          uint32_t seq, float scale, int causal) {
+// The probabilities go straight into the TF32 split layout the P V product
+// reads as its A operand: row r = head h (r / seq) and query i (r % seq) goes
+// to row h * mp + i of [heads][mp][kp] hi and lo arrays; columns seq..kp-1
+// are written as zeros (rows seq..mp-1 stay zero from allocation).  This
+// replaces a separate split pass over the heads * seq * seq probabilities.
+__global__ void __launch_bounds__(NT) attn_softmax_split_kernel(const float* __restrict__ s, uint32_t rows,
+                                                                uint32_t width, uint32_t seq, float scale, int causal,
+                                                                float* __restrict__ phi, float* __restrict__ plo,
+                                                                uint32_t mp, uint32_t kp) {
   __shared__ double shd[NT / 32];
   __shared__ float shf[NT / 32];
   for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    float* row = s + static_cast<uint64_t>(r) * width;
+    const float* row = s + static_cast<uint64_t>(r) * width;
     const uint32_t limit = causal ? (r % seq) + 1 : width;
     float v[NORM_VPT];
     float mx = -FLT_MAX;
@@ -197,10 +204,20 @@ __global__ void __launch_bounds__(NT) attn_softmax_kernel(float* __restrict__ s,
     }
     sum = block_sum_d(sum, shd);
     const double inv = 1.0 / sum;
+    const uint64_t dst = (static_cast<uint64_t>(r / seq) * mp + (r % seq)) * kp;
 #pragma unroll
     for (int i = 0; i < NORM_VPT; ++i) {
       const uint32_t c = threadIdx.x + i * NT;
-      if (c < width) row[c] = static_cast<float>(static_cast<double>(v[i]) * inv);
+      if (c < width) {
+        const float p = static_cast<float>(static_cast<double>(v[i]) * inv);
+        const float h = to_tf32(p);
+        phi[dst + c] = h;
+        plo[dst + c] = to_tf32(p - h);
+      }
+    }
+    for (uint32_t c = width + threadIdx.x; c < kp; c += NT) {
+      phi[dst + c] = 0.f;
+      plo[dst + c] = 0.f;
     }
   }
 }
@@ -361,16 +378,26 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
   // activations and workspaces
   hbuf_ = alloc(T * d.hidden);
   qkv_ = alloc(T * qkv_cols);
-  scores_ = alloc(static_cast<uint64_t>(d.max_batch) * d.heads * d.seq_len * d.seq_len);
+  scores_ = alloc(static_cast<uint64_t>(d.heads) * d.seq_len * d.seq_len);  // one batch item at a time
   attn_ = alloc(T * attn_cols);
   x1_ = alloc(T * d.hidden);
   proj_ = alloc(T * d.hidden);
   gu_ = alloc(T * 2ull * d.ffn);
   act_ = alloc(T * d.ffn);
+  {
+    // P in the TF32 split layout of the P V product, one batch item at a time
+    const SplitDims pd = split_dims(d.seq_len, d.head_dim, d.seq_len);
+    p_mp_ = pd.mp;
+    p_kp_ = pd.kp;
+    const uint64_t pe = static_cast<uint64_t>(d.heads) * pd.mp * pd.kp;
+    psplit_ = alloc(2 * pe);
+    if (psplit_ == nullptr || cudaMemsetAsync(psplit_, 0, 2 * pe * sizeof(float), stream_) != cudaSuccess) return -3;
+  }
   const uint64_t a_need = std::max({sgemm_tc_a_scratch_bytes(T, d.hidden), sgemm_tc_a_scratch_bytes(T, attn_cols),
                                     sgemm_tc_a_scratch_bytes(T, d.ffn)});
+  const SplitDims vd = split_dims(1, d.head_dim, d.seq_len);  // V split of the P V product
   const uint64_t b_need = std::max(sgemm_tc_scratch_bytes(d.seq_len, d.seq_len, d.head_dim, d.heads),
-                                   sgemm_tc_scratch_bytes(d.seq_len, d.head_dim, d.seq_len, d.heads));
+                                   static_cast<uint64_t>(2ull * sizeof(float) * d.heads * vd.np * vd.kp));
   scratch_ = alloc(std::max(a_need, b_need) / sizeof(float) + 1);
   err_ = reinterpret_cast<unsigned int*>(alloc(4));
   ok = ok && hbuf_ && qkv_ && scores_ && attn_ && x1_ && proj_ && gu_ && act_ && scratch_ && err_;
@@ -506,7 +533,7 @@ cudaError_t Block::attention(uint32_t item, uint64_t ldq, uint32_t k_col, uint32
   const BlockDims& d = dims_;
   const uint64_t S = d.seq_len, hd = d.head_dim;
   const float* base = qkv_ + item * S * ldq;
-  float* sc = scores_ + static_cast<uint64_t>(item) * d.heads * S * S;
+  float* sc = scores_;
   GemmBatch qk;
   qk.count = d.heads;
   qk.stride_a = hd;
@@ -515,19 +542,19 @@ cudaError_t Block::attention(uint32_t item, uint64_t ldq, uint32_t k_col, uint32
   qk.b_trans = true;
   cudaError_t e = sgemm_tc(base, ldq, base + k_col, ldq, sc, S, S, S, hd, scratch_, err_, 16, stream_, nullptr, &qk);
   if (e != cudaSuccess) return e;
-  attn_softmax_kernel<<<grid_for(d.heads * S, 1), NT, 0, stream_>>>(sc, d.heads * S, S, S,
-                                                                    1.0f / std::sqrt(static_cast<float>(hd)),
-                                                                    d.family == kGemma ? 1 : 0);
+  const uint64_t pe = static_cast<uint64_t>(d.heads) * p_mp_ * p_kp_;
+  attn_softmax_split_kernel<<<grid_for(d.heads * S, 1), NT, 0, stream_>>>(
+      sc, d.heads * S, S, S, 1.0f / std::sqrt(static_cast<float>(hd)), d.family == kGemma ? 1 : 0, psplit_,
+      psplit_ + pe, p_mp_, p_kp_);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   GemmBatch pv;
   pv.count = d.heads;
-  pv.stride_a = S * S;
   pv.stride_b = shared_kv ? 0 : hd;
   pv.stride_c = hd;
   const uint64_t ldo = static_cast<uint64_t>(d.heads) * hd;
-  return sgemm_tc(sc, S, base + v_col, ldq, attn_ + item * S * ldo, ldo, S, hd, S, scratch_, err_, 16, stream_,
-                  nullptr, &pv);
+  return sgemm_tc_presplit_a(psplit_, psplit_ + pe, base + v_col, ldq, attn_ + item * S * ldo, ldo, S, hd, S,
+                             scratch_, err_, stream_, &pv);
 }
 
 int Block::forward(const float* x, float* y, uint32_t batch, const float* timesteps_host) {

@@ -7,6 +7,8 @@
 #include <cstdint>
 #include <vector>
 
+#include "kernels.h"
+
 namespace oct {
 
 enum : uint32_t { kGemma = 1, kDit = 2 };
@@ -78,6 +80,8 @@ class Block {
   float *rope_cos_ = nullptr, *rope_sin_ = nullptr;
   float *hbuf_ = nullptr, *qkv_ = nullptr, *scores_ = nullptr, *attn_ = nullptr, *x1_ = nullptr, *proj_ = nullptr;
   float *gu_ = nullptr, *act_ = nullptr, *scratch_ = nullptr;
+  float* psplit_ = nullptr;  // attention probabilities, TF32 hi then lo, [heads][p_mp_][p_kp_]
+  uint32_t p_mp_ = 0, p_kp_ = 0;
   unsigned int* err_ = nullptr;
 };
 

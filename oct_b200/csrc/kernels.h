@@ -51,6 +51,12 @@ cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, co
                               uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* a_scratch, unsigned int* err,
                               cudaStream_t stream, const float* residual = nullptr, uint64_t ldr = 0);
 
+// A already split by its producer (hi/lo in the [count][Mp][Kp] layout of
+// split_dims, zero padded); B is split into b_scratch.  Strided batch as GemmBatch.
+cudaError_t sgemm_tc_presplit_a(const float* ahi, const float* alo, const float* b, uint64_t ldb, float* c,
+                                uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* b_scratch, unsigned int* err,
+                                cudaStream_t stream, const GemmBatch* batch);
+
 // Plain FP32-FMA SGEMM on the CUDA cores (control variant); no scratch.
 cudaError_t sgemm_fma(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
                       uint32_t m, uint32_t n, uint32_t k, cudaStream_t stream, const GemmBatch* batch = nullptr);

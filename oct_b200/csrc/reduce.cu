@@ -137,29 +137,29 @@ __device__ __forceinline__ float process_row(float* srow, uint32_t w, uint32_t l
       }
     }
     mx = group_max_f<TPR>(mx, fscratch);
+    // exp(x - max) in fp32; each float4's four positive terms are summed in
+    // fp32 (a few ulp) and the row sum accumulates those partials in binary64.
     double s = 0.0;
     for (uint32_t i = lane; i < nv; i += TPR) {
       float4 x = v4[i];
       x.x = expf(x.x - mx); x.y = expf(x.y - mx); x.z = expf(x.z - mx); x.w = expf(x.w - mx);
-      s += static_cast<double>(x.x); s += static_cast<double>(x.y);
-      s += static_cast<double>(x.z); s += static_cast<double>(x.w);
+      s += static_cast<double>((x.x + x.y) + (x.z + x.w));
       v4[i] = x;  // keep exp(x - max) for the normalising pass
     }
     s = group_sum_d<TPR>(s, dscratch);
-    const double inv = 1.0 / s;
+    const float inv = static_cast<float>(1.0 / s);  // one rounding; the product adds one more
     float4* o4 = reinterpret_cast<float4*>(out + row * w);
     for (uint32_t i = lane; i < nv; i += TPR) {
       const float4 e = v4[i];
-      __stcs(o4 + i, make_float4(static_cast<float>(e.x * inv), static_cast<float>(e.y * inv),
-                                 static_cast<float>(e.z * inv), static_cast<float>(e.w * inv)));
+      __stcs(o4 + i, make_float4(e.x * inv, e.y * inv, e.z * inv, e.w * inv));
     }
     return 0.f;
   } else {  // kRms
     double ss = 0.0;
     for (uint32_t i = lane; i < nv; i += TPR) {
       const float4 x = v4[i];
-      ss += static_cast<double>(x.x) * x.x; ss += static_cast<double>(x.y) * x.y;
-      ss += static_cast<double>(x.z) * x.z; ss += static_cast<double>(x.w) * x.w;
+      // four non-negative squares summed in fp32, accumulated in binary64
+      ss += static_cast<double>((x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w));
       if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
         note_nonfinite(x.x, row * w + 4 * i, first_bad); note_nonfinite(x.y, row * w + 4 * i + 1, first_bad);
         note_nonfinite(x.z, row * w + 4 * i + 2, first_bad); note_nonfinite(x.w, row * w + 4 * i + 3, first_bad);
@@ -275,18 +275,22 @@ __global__ void __launch_bounds__(THREADS) row_bulk_kernel(const float* __restri
 // mbarrier each, and reduces a row with warp shuffles only.  No CTA-wide
 // barrier sits on the data path, so the warps of a CTA overlap their copies
 // and their arithmetic freely.  Used for rows up to 2048 floats.
+// A slot holds `rps` consecutive rows (one copy when rows are contiguous), so
+// short rows still move in multi-kilobyte transfers.
 template <int OP>
 __global__ void __launch_bounds__(THREADS) row_warp_kernel(const float* __restrict__ in, uint64_t stride,
                                                            float* __restrict__ out, float* __restrict__ inv_rms,
                                                            const float* __restrict__ weight, float eps,
                                                            uint32_t rows, uint32_t w, uint32_t ns, uint32_t wpc,
-                                                           unsigned long long* __restrict__ nonfinite,
+                                                           uint32_t rps, unsigned long long* __restrict__ nonfinite,
                                                            unsigned int* __restrict__ err) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp >= wpc) return;
-  float* ring = reinterpret_cast<float*>(smem_raw) + static_cast<uint64_t>(warp) * ns * w;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + static_cast<uint64_t>(wpc) * ns * w * 4) + warp * ns;
+  const uint32_t slot_floats = rps * w;
+  float* ring = reinterpret_cast<float*>(smem_raw) + static_cast<uint64_t>(warp) * ns * slot_floats;
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(smem_raw + static_cast<uint64_t>(wpc) * ns * slot_floats * 4) + warp * ns;
   if (lane == 0) {
     for (uint32_t s = 0; s < ns; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
@@ -294,39 +298,58 @@ __global__ void __launch_bounds__(THREADS) row_warp_kernel(const float* __restri
   }
   __syncwarp();
   const uint32_t gw = blockIdx.x * wpc + warp, nw = gridDim.x * wpc;
+  const uint32_t units = (rows + rps - 1) / rps;
   const uint32_t row_bytes = w * 4u;
+  const bool contiguous = (stride == w);
+  // Issue unit u (rows u*rps ...) into `slot` (lane 0 only).
+  auto issue = [&](uint32_t u, uint32_t slot) {
+    const uint32_t r0 = u * rps;
+    const uint32_t nr = min(rps, rows - r0);
+    float* dst = ring + slot * slot_floats;
+    mbar_arrive_expect_tx(&bars[slot], nr * row_bytes);
+    if (contiguous) {
+      bulk_load(dst, in + static_cast<uint64_t>(r0) * w, nr * row_bytes, &bars[slot]);
+    } else {
+      for (uint32_t i = 0; i < nr; ++i)
+        bulk_load(dst + i * w, in + static_cast<uint64_t>(r0 + i) * stride, row_bytes, &bars[slot]);
+    }
+  };
   uint32_t issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (lane == 0) {
     for (uint32_t s = 0; s < ns; ++s) {
-      const uint64_t r = gw + static_cast<uint64_t>(s) * nw;
-      if (r >= rows) break;
-      mbar_arrive_expect_tx(&bars[s], row_bytes);
-      bulk_load(ring + s * w, in + r * stride, row_bytes, &bars[s]);
+      const uint64_t u = gw + static_cast<uint64_t>(s) * nw;
+      if (u >= units) break;
+      issue(static_cast<uint32_t>(u), s);
       issued[s] += 1;
     }
   }
   uint64_t first_bad = ~0ull;
   bool aborted = false;
   for (uint32_t j = 0;; ++j) {
-    const uint64_t r = gw + static_cast<uint64_t>(j) * nw;
-    if (r >= rows) break;
+    const uint64_t u = gw + static_cast<uint64_t>(j) * nw;
+    if (u >= units) break;
     const uint32_t slot = j % ns;
     const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars[slot], (j / ns) & 1u, err, kErrWaitRow));
     if (!ok) {
       aborted = true;
       break;
     }
-    const float inv = process_row<OP, 32>(ring + slot * w, w, lane, r, out, weight, eps, nullptr, nullptr, first_bad);
-    if constexpr (OP == kRms) {
-      if (lane == 0 && inv_rms != nullptr) inv_rms[r] = inv;
+    const uint32_t r0 = static_cast<uint32_t>(u) * rps;
+    const uint32_t nr = min(rps, rows - r0);
+    for (uint32_t i = 0; i < nr; ++i) {
+      const uint64_t r = r0 + i;
+      const float inv = process_row<OP, 32>(ring + slot * slot_floats + i * w, w, lane, r, out, weight, eps, nullptr,
+                                            nullptr, first_bad);
+      if constexpr (OP == kRms) {
+        if (lane == 0 && inv_rms != nullptr) inv_rms[r] = inv;
+      }
     }
     __syncwarp();  // every lane is done reading this slot
     if (lane == 0) {
-      const uint64_t nr = gw + static_cast<uint64_t>(j + ns) * nw;
-      if (nr < rows) {
+      const uint64_t nu = gw + static_cast<uint64_t>(j + ns) * nw;
+      if (nu < units) {
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&bars[slot], row_bytes);
-        bulk_load(ring + slot * w, in + nr * stride, row_bytes, &bars[slot]);
+        issue(static_cast<uint32_t>(nu), slot);
         issued[slot] += 1;
       }
     }
@@ -344,10 +367,11 @@ cudaError_t launch_warp(const float* in, uint64_t stride, float* out, float* inv
                         uint32_t rows, uint32_t w, unsigned long long* nonfinite, unsigned int* err,
                         cudaStream_t stream) {
   const uint32_t row_bytes = w * 4u;
-  uint32_t wpc, ns;
-  if (row_bytes <= 2048u) {  // short rows: 8 warps, up to 8 slots each, 64 KB ring -> 3 CTAs per SM
+  uint32_t wpc, ns, rps = 1;
+  if (row_bytes <= 2048u) {  // short rows: 8 warps, 4 KB slots of rps rows, 64 KB ring -> 3 CTAs per SM
     wpc = 8;
-    ns = 65536u / (wpc * row_bytes);
+    rps = 4096u / row_bytes;
+    ns = 65536u / (wpc * rps * row_bytes);
     ns = ns < 2 ? 2 : (ns > 8 ? 8 : ns);
   } else if (row_bytes <= 8192u) {  // 8 warps x 3 slots, one CTA per SM
     wpc = 8;
@@ -356,7 +380,7 @@ cudaError_t launch_warp(const float* in, uint64_t stride, float* out, float* inv
     wpc = 4;
     ns = 3;
   }
-  const uint32_t smem = wpc * ns * row_bytes + wpc * ns * 8u;
+  const uint32_t smem = wpc * ns * rps * row_bytes + wpc * ns * 8u;
   auto kern = row_warp_kernel<OP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
@@ -365,10 +389,11 @@ cudaError_t launch_warp(const float* in, uint64_t stride, float* out, float* inv
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpc * 32, smem);
   if (per_sm < 1) per_sm = 1;
-  const uint32_t need = (rows + wpc - 1) / wpc;
+  const uint32_t units = (rows + rps - 1) / rps;
+  const uint32_t need = (units + wpc - 1) / wpc;
   const uint32_t cap = static_cast<uint32_t>(sms * per_sm);
   kern<<<need < cap ? need : cap, wpc * 32, smem, stream>>>(in, stride, out, inv_rms, weight, eps, rows, w, ns, wpc,
-                                                            nonfinite, err);
+                                                            rps, nonfinite, err);
   return cudaGetLastError();
 }
 

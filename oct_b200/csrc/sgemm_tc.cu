@@ -454,6 +454,35 @@ cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, co
   return launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, 0, residual, ldr);
 }
 
+// A operand already in the split layout (hi/lo, [count][Mp][Kp], zero padded),
+// written by its producer; only B is split here (into b_scratch).
+cudaError_t sgemm_tc_presplit_a(const float* ahi, const float* alo, const float* b, uint64_t ldb, float* c,
+                                uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* b_scratch, unsigned int* err,
+                                cudaStream_t stream, const GemmBatch* batch) {
+  if (m == 0 || n == 0 || k == 0) return cudaSuccess;
+  if ((reinterpret_cast<uintptr_t>(b_scratch) & 1023u) != 0) return cudaErrorInvalidValue;
+  const GemmBatch one{};
+  const GemmBatch& bt = batch != nullptr ? *batch : one;
+  if (bt.count == 0) return cudaSuccess;
+  if (bt.count > 65535u) return cudaErrorInvalidValue;
+  const SplitDims d = split_dims(m, n, k);
+  const uint64_t b_elems = static_cast<uint64_t>(d.np) * d.kp * bt.count;
+  float* bhi = static_cast<float*>(b_scratch);
+  float* blo = bhi + b_elems;
+  cudaError_t e;
+  if (bt.b_trans) {
+    const uint64_t bgroups = static_cast<uint64_t>(d.np) * (d.kp / 4);
+    const uint32_t bblocks = static_cast<uint32_t>(std::min<uint64_t>((bgroups + 255) / 256, 148ull * 16));
+    split_rows_kernel<<<dim3(bblocks, bt.count), 256, 0, stream>>>(b, ldb, n, k, bhi, blo, d.np, d.kp, bt.stride_b);
+  } else {
+    split_transpose_kernel<<<dim3(d.np / 32, d.kp / 32, bt.count), 256, 0, stream>>>(b, ldb, k, n, bhi, blo, d.kp,
+                                                                                     d.np, bt.stride_b);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.stride_c);
+}
+
 // ------------------------------------------------------------------ no-allocation variant
 // Scratch for oct_b200_sgemm_device_noalloc: some callers cannot call
 // cudaMalloc at all (for example a serving process whose fixed memory plan
