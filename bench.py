@@ -56,7 +56,8 @@ def parse_args():
     p.add_argument("--m", type=int, default=8192)
     p.add_argument("--n", type=int, default=8192, help="columns per rank")
     p.add_argument("--k", type=int, default=8192)
-    p.add_argument("--variant", type=int, default=16, help="16/32 = tcgen05 stage depth, 2 = FMA control")
+    p.add_argument("--variant", type=int, default=16,
+                   help="16/32 = tcgen05 one CTA per tile with that K stage depth, 216/232 = CTA pair, 2 = FMA")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-secondary", action="store_true")
@@ -247,7 +248,9 @@ def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
     a = torch.rand(m, k, device="cuda", generator=g) * 2 - 1
     b = torch.rand(k, n, device="cuda", generator=g) * 2 - 1
     c = torch.empty(m, n, device="cuda")
-    for variant, label, iters in ((R.SGEMM_FMA, "sgemm_fma_control", 3), (R.SGEMM_TC_BK32, "sgemm_3xtf32_bk32", 5)):
+    for variant, label, iters in ((R.SGEMM_FMA, "sgemm_fma_control", 3), (R.SGEMM_TC_BK32, "sgemm_3xtf32_bk32", 5),
+                                  (R.SGEMM_TC_PAIR16, "sgemm_3xtf32_pair16", 5),
+                                  (R.SGEMM_TC_PAIR32, "sgemm_3xtf32_pair32", 5)):
         rt.sgemm_device(a, b, c, m, n, k, variant, stream)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -501,8 +504,9 @@ def run_ours(args) -> None:
             "data": "synthetic",
             "config": {
                 "workload": f"sgemm {m}x{n}x{k} per rank (A replicated, B and C column-sharded; global N = {n}*ranks)",
-                "m": m, "n_per_rank": n, "k": k, "variant": "tcgen05 3xTF32" if args.variant in (1, 16, 32) else "fp32 FMA",
-                "stage_depth_k": args.variant if args.variant in (16, 32) else None,
+                "m": m, "n_per_rank": n, "k": k, "variant": ("tcgen05 3xTF32" + (" CTA pair" if args.variant in (216, 232) else ""))
+                if args.variant in (1, 16, 32, 216, 232) else "fp32 FMA",
+                "stage_depth_k": args.variant % 100 if args.variant in (16, 32, 216, 232) else None,
                 "parallelism": f"column-parallel x{world}",
                 "l2": "no flush: every operand (256 MiB) exceeds the 126 MB L2",
                 "input": "U[-1,1) fp32, seeded per rank",

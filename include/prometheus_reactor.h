@@ -549,6 +549,10 @@ enum {
   OCT_B200_SGEMM_AUTO = 0u,       /* 3xTF32 tcgen05 for large shapes, FMA for tiny ones */
   OCT_B200_SGEMM_TC3XTF32 = 1u,   /* tcgen05/TMEM tensor cores, split-TF32 x3 */
   OCT_B200_SGEMM_FMA = 2u,        /* plain FP32 FMA on the CUDA cores (control) */
+  OCT_B200_SGEMM_TC_BK16 = 16u,   /* tensor cores, one CTA per 128x256 tile, 16-deep K stages */
+  OCT_B200_SGEMM_TC_BK32 = 32u,   /* tensor cores, one CTA per 128x256 tile, 32-deep K stages */
+  OCT_B200_SGEMM_TC_PAIR16 = 216u, /* tensor cores, CTA pair (cta_group::2) per 256x256 tile, 16-deep */
+  OCT_B200_SGEMM_TC_PAIR32 = 232u, /* CTA pair, 32-deep K stages */
 };
 
 /* C = A * B on device pointers (row-major, ld = k / n / n), enqueued on
@@ -602,7 +606,7 @@ PROM_REACTOR_API int oct_b200_sync_status(void* handle, void* stream, int* out_d
    and calls no cudaMalloc, cudaFree or allocating library routine.  The TF32
    split scratch and the kernel status word live in one fixed 64 MiB device
    array that every GPU loading the library holds until the process exits.
-   Limit: 8 * (roundup(m,128) + roundup(n,256)) * roundup(k,32) bytes must fit
+   Limit: 8 * (roundup(m,256) + roundup(n,256)) * roundup(k,32) bytes must fit
    in 64 MiB (any m, n, k <= 2048 does); larger products are rejected with
    PROM_ERROR and OCT_B200_DETAIL_NOALLOC_TOO_LARGE, and C is left untouched.
    The first call on each device looks up the array's device address, so make

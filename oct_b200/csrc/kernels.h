@@ -28,8 +28,12 @@ struct GemmBatch {
   bool b_trans = false;
 };
 
+// Tensor-core kernel configurations: one CTA per 128 x 256 tile, or a CTA pair
+// (cta_group::2) per 256 x 256 tile; 16 or 32 K elements per pipeline stage.
+enum TcConfig : int { kTcSingle16 = 16, kTcSingle32 = 32, kTcPair16 = 216, kTcPair32 = 232 };
+
 // 3xTF32 tensor-core SGEMM.  `scratch` must hold sgemm_tc_scratch_bytes and be
-// 1024-byte aligned.  bk selects the K depth of one pipeline stage (16 or 32).
+// 1024-byte aligned.  bk is a TcConfig.
 // Optional events (may be null) are recorded on `stream` before the split
 // pass, before the main kernel and after it, for per-kernel timing.
 struct SgemmEvents {
@@ -49,13 +53,14 @@ cudaError_t sgemm_tc_split_b(const float* b, uint64_t ldb, uint32_t k, uint32_t 
 uint64_t sgemm_tc_a_scratch_bytes(uint32_t m, uint32_t k);
 cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, const float* blo, float* c,
                               uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* a_scratch, unsigned int* err,
-                              cudaStream_t stream, const float* residual = nullptr, uint64_t ldr = 0);
+                              cudaStream_t stream, const float* residual = nullptr, uint64_t ldr = 0,
+                              int cfg = kTcSingle16);
 
 // A already split by its producer (hi/lo in the [count][Mp][Kp] layout of
 // split_dims, zero padded); B is split into b_scratch.  Strided batch as GemmBatch.
 cudaError_t sgemm_tc_presplit_a(const float* ahi, const float* alo, const float* b, uint64_t ldb, float* c,
                                 uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* b_scratch, unsigned int* err,
-                                cudaStream_t stream, const GemmBatch* batch);
+                                cudaStream_t stream, const GemmBatch* batch, int cfg = kTcSingle16);
 
 // Plain FP32-FMA SGEMM on the CUDA cores (control variant); no scratch.
 cudaError_t sgemm_fma(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,

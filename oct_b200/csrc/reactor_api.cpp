@@ -173,11 +173,12 @@ int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uin
   cudaError_t e;
   if (variant == OCT_B200_SGEMM_FMA) {
     e = oct::sgemm_fma(a, lda, b, ldb, c, ldc, m, n, k, stream, batch);
-  } else if (variant == OCT_B200_SGEMM_TC3XTF32 || variant == 16u || variant == 32u) {
+  } else if (variant == OCT_B200_SGEMM_TC3XTF32 || variant == 16u || variant == 32u || variant == 216u ||
+             variant == 232u) {
     const uint64_t need = oct::sgemm_tc_scratch_bytes(m, n, k, batch != nullptr ? batch->count : 1u);
     e = rt->scratch.ensure(need, stream);
     if (e != cudaSuccess) return OCT_B200_DETAIL_OUT_OF_MEMORY;
-    const int bk = (variant == 32u) ? 32 : 16;
+    const int bk = variant == OCT_B200_SGEMM_TC3XTF32 ? oct::kTcSingle16 : static_cast<int>(variant);
     const oct::SgemmEvents* ev = nullptr;
     if (rt->timing) {
       if (rt->timing_used == rt->timing_events.size()) {

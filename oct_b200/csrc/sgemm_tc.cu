@@ -150,8 +150,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     sgemm3x_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                    const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
                    float* __restrict__ c, uint32_t m, uint32_t n, uint64_t ldc, uint32_t num_kb,
-                   uint32_t tiles_m, uint32_t tiles_n, uint64_t stride_c, const float* __restrict__ residual,
-                   uint64_t ldr, unsigned int* __restrict__ err) {
+                   uint32_t tiles_m, uint32_t tiles_n, uint32_t entry_rows_a, uint32_t entry_rows_b,
+                   uint64_t stride_c, const float* __restrict__ residual, uint64_t ldr,
+                   unsigned int* __restrict__ err) {
   using Cfg = TileCfg<BK>;
   constexpr uint32_t S = Cfg::STAGES;
   constexpr uint32_t KBC = KC / BK;  // k-blocks per accumulation chunk
@@ -216,8 +217,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
-      const int row_a = static_cast<int>(entry * tiles_m * BM + tile_m * BM);
-      const int row_b = static_cast<int>(entry * tiles_n * BN + tile_n * BN);
+      const int row_a = static_cast<int>(entry * entry_rows_a + tile_m * BM);
+      const int row_b = static_cast<int>(entry * entry_rows_b + tile_n * BN);
       uint32_t kb = 0;
       for (; kb < num_kb; ++kb) {
         const uint32_t s = kb % S;
@@ -358,6 +359,231 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------ CTA-pair kernel
+// Same product and accumulation scheme on a CTA pair (cluster of 2) that owns a
+// 256 x 256 output tile: each CTA stages its own 128 rows of A and 128 of the
+// 256 B^T rows, and the leader CTA issues tcgen05.mma.cta_group::2 (M = 256,
+// N = 256), which reads the operand halves of both CTAs.  Per CTA a stage is
+// 32 KB instead of 48 KB for the same tensor work, so six stages fit, and each
+// CTA keeps a 128 x 256 accumulator half in its own TMEM.
+//   * both CTAs' TMA loads count their bytes on the leader's `full` barrier;
+//   * the leader's commits multicast to both CTAs' `empty` / `acc_full`;
+//   * both CTAs' epilogue warps arrive on the leader's `acc_empty` (16 arrivals).
+constexpr uint32_t PAIR_BM = 256, PAIR_HALF = 128;
+
+template <int BK>
+struct PairCfg {
+  static constexpr uint32_t SWZ = BK * 4;
+  static constexpr uint32_t A_BYTES = PAIR_HALF * BK * 4;  // this CTA's 128 rows of A
+  static constexpr uint32_t B_BYTES = PAIR_HALF * BK * 4;  // this CTA's 128 rows of B^T
+  static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+  static constexpr uint32_t STAGES = (BK == 16) ? 6 : 3;
+  static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+};
+
+template <int BK>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    sgemm3x_pair_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+                        const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
+                        float* __restrict__ c, uint32_t m, uint32_t n, uint64_t ldc, uint32_t num_kb,
+                        uint32_t tiles_m, uint32_t tiles_n, uint32_t entry_rows_a, uint32_t entry_rows_b,
+                        uint64_t stride_c, const float* __restrict__ residual, uint64_t ldr,
+                        unsigned int* __restrict__ err) {
+  using Cfg = PairCfg<BK>;
+  constexpr uint32_t S = Cfg::STAGES;
+  constexpr uint32_t KBC = KC / BK;
+  constexpr uint32_t IDESC = umma_idesc_tf32(PAIR_BM, BN);
+  constexpr uint16_t PAIR_MASK = 0x3;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[S];
+  __shared__ __align__(8) uint64_t empty_bar[S];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ uint32_t aborted;
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_cta_rank();  // 0 = leader
+  const uint32_t num_chunks = (num_kb + KBC - 1) / KBC;
+
+  const uint32_t pair = blockIdx.x >> 1;
+  const uint32_t tiles_per_entry = tiles_m * tiles_n;
+  const uint32_t entry = pair / tiles_per_entry;
+  const uint32_t t = pair % tiles_per_entry;
+  const uint32_t per_group = GROUP_M * tiles_n;
+  const uint32_t first_m = (t / per_group) * GROUP_M;
+  const uint32_t group_rows = min(tiles_m - first_m, GROUP_M);
+  const uint32_t tile_m = first_m + (t % per_group) % group_rows;
+  const uint32_t tile_n = (t % per_group) / group_rows;
+  c += entry * stride_c;
+  if (residual != nullptr) residual += entry * stride_c;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (uint32_t b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * NUM_EPI_WARPS);
+    }
+    mbar_init(&drain_bar, 1);
+    aborted = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    prefetch_tensormap(&tm_ahi);
+    prefetch_tensormap(&tm_alo);
+    prefetch_tensormap(&tm_bhi);
+    prefetch_tensormap(&tm_blo);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs)
+      const int row_a = static_cast<int>(entry * entry_rows_a + tile_m * PAIR_BM + rank * PAIR_HALF);
+      const int row_b = static_cast<int>(entry * entry_rows_b + tile_n * BN + rank * PAIR_HALF);
+      for (uint32_t kb = 0; kb < num_kb; ++kb) {
+        const uint32_t s = kb % S;
+        if (kb >= S) {
+          if (!mbar_wait(&empty_bar[s], ((kb / S) - 1) & 1u, err, kErrWaitEmpty)) {
+            atomicExch(&aborted, 1u);
+            break;
+          }
+        }
+        uint8_t* st = smem + s * Cfg::STAGE_BYTES;
+        const int kx = static_cast<int>(kb * BK);
+        if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * Cfg::STAGE_BYTES);
+        tma_load_2d_pair(st, &tm_ahi, &full_bar[s], kx, row_a);
+        tma_load_2d_pair(st + Cfg::A_BYTES, &tm_alo, &full_bar[s], kx, row_a);
+        tma_load_2d_pair(st + 2 * Cfg::A_BYTES, &tm_bhi, &full_bar[s], kx, row_b);
+        tma_load_2d_pair(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tm_blo, &full_bar[s], kx, row_b);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (leader CTA only)
+      for (uint32_t kb = 0; kb < num_kb; ++kb) {
+        const uint32_t chunk = kb / KBC, in_chunk = kb % KBC;
+        const uint32_t buf = chunk & 1u;
+        if (in_chunk == 0 && chunk >= 2) {
+          if (!mbar_wait(&acc_empty[buf], ((chunk >> 1) - 1) & 1u, err, kErrWaitAccum)) {
+            atomicExch(&aborted, 1u);
+            break;
+          }
+          tc_fence_after();
+        }
+        const uint32_t s = kb % S;
+        if (!mbar_wait(&full_bar[s], (kb / S) & 1u, err, kErrWaitFull)) {
+          atomicExch(&aborted, 1u);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        const uint32_t base = smem_addr(smem + s * Cfg::STAGE_BYTES);
+        const uint32_t a_hi = base, a_lo = base + Cfg::A_BYTES;
+        const uint32_t b_hi = base + 2 * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
+#pragma unroll
+        for (uint32_t kk = 0; kk < BK / 8; ++kk) {
+          const uint32_t off = kk * 32;
+          const uint64_t dah = umma_desc_kmajor(a_hi + off, Cfg::SWZ);
+          const uint64_t dal = umma_desc_kmajor(a_lo + off, Cfg::SWZ);
+          const uint64_t dbh = umma_desc_kmajor(b_hi + off, Cfg::SWZ);
+          const uint64_t dbl = umma_desc_kmajor(b_lo + off, Cfg::SWZ);
+          umma_tf32_pair(d_tmem, dal, dbh, IDESC, (in_chunk | kk) != 0u ? 1u : 0u);
+          umma_tf32_pair(d_tmem, dah, dbl, IDESC, 1u);
+          umma_tf32_pair(d_tmem, dah, dbh, IDESC, 1u);
+        }
+        umma_commit_pair_mc(&empty_bar[s], PAIR_MASK);
+        if (in_chunk == KBC - 1 || kb == num_kb - 1) umma_commit_pair_mc(&acc_full[buf], PAIR_MASK);
+      }
+      umma_commit_pair_mc(&drain_bar, PAIR_MASK);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..9 of both CTAs, each on its own TMEM half
+    const uint32_t q = warp & 3u;
+    const uint32_t h = (warp - 2u) >> 2;
+    const uint32_t lane_addr = (q * 32u) << 16;
+    float run[128];
+#pragma unroll
+    for (int j = 0; j < 128; ++j) run[j] = 0.f;
+    bool ok = true;
+    for (uint32_t ch = 0; ch < num_chunks; ++ch) {
+      const uint32_t buf = ch & 1u;
+      ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (ch >> 1) & 1u, err, kErrWaitAccum));
+      if (!ok) {
+        if (lane == 0) atomicExch(&aborted, 1u);
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (uint32_t g = 0; g < 4; ++g) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + buf * BN + h * 128u + g * 32u, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) run[g * 32 + j] += __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(&acc_empty[buf], 0);
+    }
+    if (ok && num_kb > 0) {
+      const uint32_t row = tile_m * PAIR_BM + rank * PAIR_HALF + q * 32 + lane;
+      const uint32_t col0 = tile_n * BN + h * 128u;
+      const bool vec_ok = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) &&
+                          (residual == nullptr ||
+                           ((ldr % 4 == 0) && ((reinterpret_cast<uintptr_t>(residual) & 15u) == 0)));
+      if (row < m && col0 < n) {
+        float* dst = c + static_cast<uint64_t>(row) * ldc + col0;
+        const float* src = residual != nullptr ? residual + static_cast<uint64_t>(row) * ldr + col0 : nullptr;
+        if (vec_ok && col0 + 128 <= n) {
+#pragma unroll
+          for (int j = 0; j < 128; j += 4) {
+            float4 v = make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
+            if (src != nullptr) {
+              const float4 r4 = *reinterpret_cast<const float4*>(src + j);
+              v.x += r4.x;
+              v.y += r4.y;
+              v.z += r4.z;
+              v.w += r4.w;
+            }
+            *reinterpret_cast<float4*>(dst + j) = v;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 128; ++j)
+            if (col0 + j < n) dst[j] = src != nullptr ? src[j] + run[j] : run[j];
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  // Teardown: the leader's last commit (multicast) tells both CTAs that every
+  // pair MMA finished; then both CTAs meet before the pair frees its TMEM, so
+  // no CTA leaves while the leader's MMAs could still read its shared memory.
+  if (threadIdx.x == 32) mbar_wait(&drain_bar, 0, err, kErrWaitDrain);
+  __syncthreads();
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -407,12 +633,52 @@ cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, co
   cudaError_t e = cudaFuncSetAttribute(sgemm3x_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(Cfg::SMEM_BYTES));
   if (e != cudaSuccess) return e;
-  const uint32_t tiles_m = d.mp / BM, tiles_n = d.np / BN;
+  const uint32_t tiles_m = (m + BM - 1) / BM, tiles_n = (n + BN - 1) / BN;
   const uint64_t grid = static_cast<uint64_t>(tiles_m) * tiles_n * batch;
   if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
   sgemm3x_kernel<BK><<<static_cast<uint32_t>(grid), NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(
-      m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, stride_c, residual, ldr, err);
+      m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, d.mp, d.np, stride_c, residual, ldr,
+      err);
   return cudaGetLastError();
+}
+
+template <int BK>
+cudaError_t launch_pair(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
+                        uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
+                        cudaStream_t stream, uint32_t batch, uint64_t stride_c, const float* residual = nullptr,
+                        uint64_t ldr = 0) {
+  using Cfg = PairCfg<BK>;
+  if (d.mp % PAIR_BM != 0) return cudaErrorInvalidValue;
+  CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+  const uint32_t rows_a = d.mp * batch, rows_b = d.np * batch;
+  if (!make_operand_map(&m_ahi, ahi, rows_a, d.kp, BK, PAIR_HALF) ||
+      !make_operand_map(&m_alo, alo, rows_a, d.kp, BK, PAIR_HALF) ||
+      !make_operand_map(&m_bhi, bhi, rows_b, d.kp, BK, PAIR_HALF) ||
+      !make_operand_map(&m_blo, blo, rows_b, d.kp, BK, PAIR_HALF))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(sgemm3x_pair_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(Cfg::SMEM_BYTES));
+  if (e != cudaSuccess) return e;
+  const uint32_t tiles_m = (m + PAIR_BM - 1) / PAIR_BM, tiles_n = (n + BN - 1) / BN;
+  const uint64_t grid = 2ull * tiles_m * tiles_n * batch;
+  if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
+  sgemm3x_pair_kernel<BK><<<static_cast<uint32_t>(grid), NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(
+      m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, d.mp, d.np, stride_c, residual, ldr,
+      err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_config(int cfg, const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
+                          uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
+                          cudaStream_t stream, uint32_t batch, uint64_t stride_c, const float* residual = nullptr,
+                          uint64_t ldr = 0) {
+  switch (cfg) {
+    case kTcSingle16: return launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
+    case kTcSingle32: return launch_main<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
+    case kTcPair16: return launch_pair<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
+    case kTcPair32: return launch_pair<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace
@@ -440,7 +706,7 @@ uint64_t sgemm_tc_a_scratch_bytes(uint32_t m, uint32_t k) {
 
 cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, const float* blo, float* c,
                               uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* a_scratch, unsigned int* err,
-                              cudaStream_t stream, const float* residual, uint64_t ldr) {
+                              cudaStream_t stream, const float* residual, uint64_t ldr, int cfg) {
   if (m == 0 || n == 0 || k == 0) return cudaSuccess;
   if ((reinterpret_cast<uintptr_t>(a_scratch) & 1023u) != 0) return cudaErrorInvalidValue;
   const SplitDims d = split_dims(m, n, k);
@@ -451,14 +717,14 @@ cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, co
   split_rows_kernel<<<dim3(blocks, 1), 256, 0, stream>>>(a, lda, m, k, ahi, alo, d.mp, d.kp, 0);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, 0, residual, ldr);
+  return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, 0, residual, ldr);
 }
 
 // A operand already in the split layout (hi/lo, [count][Mp][Kp], zero padded),
 // written by its producer; only B is split here (into b_scratch).
 cudaError_t sgemm_tc_presplit_a(const float* ahi, const float* alo, const float* b, uint64_t ldb, float* c,
                                 uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* b_scratch, unsigned int* err,
-                                cudaStream_t stream, const GemmBatch* batch) {
+                                cudaStream_t stream, const GemmBatch* batch, int cfg) {
   if (m == 0 || n == 0 || k == 0) return cudaSuccess;
   if ((reinterpret_cast<uintptr_t>(b_scratch) & 1023u) != 0) return cudaErrorInvalidValue;
   const GemmBatch one{};
@@ -480,7 +746,7 @@ cudaError_t sgemm_tc_presplit_a(const float* ahi, const float* alo, const float*
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.stride_c);
+  return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.stride_c);
 }
 
 // ------------------------------------------------------------------ no-allocation variant
@@ -515,7 +781,8 @@ cudaError_t noalloc_base(int dev, unsigned char** out) {
 }  // namespace
 
 SplitDims split_dims(uint32_t m, uint32_t n, uint32_t k) {
-  return SplitDims{round_up(m, BM), round_up(n, BN), round_up(k, KPAD)};
+  // M is padded to the CTA-pair tile (256) so both kernels read one layout.
+  return SplitDims{round_up(m, PAIR_BM), round_up(n, BN), round_up(k, KPAD)};
 }
 
 uint64_t sgemm_tc_scratch_bytes(uint32_t m, uint32_t n, uint32_t k, uint32_t batch) {
@@ -528,7 +795,7 @@ cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb,
                      uint32_t m, uint32_t n, uint32_t k, void* scratch, unsigned int* err, int bk,
                      cudaStream_t stream, const SgemmEvents* events, const GemmBatch* batch) {
   if (m == 0 || n == 0 || k == 0) return cudaSuccess;
-  if (bk != 16 && bk != 32) return cudaErrorInvalidValue;
+  if (bk != kTcSingle16 && bk != kTcSingle32 && bk != kTcPair16 && bk != kTcPair32) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(scratch) & 1023u) != 0) return cudaErrorInvalidValue;
   const GemmBatch one{};
   const GemmBatch& bt = batch != nullptr ? *batch : one;
@@ -561,8 +828,7 @@ cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb,
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (events != nullptr && events->main_begin != nullptr) cudaEventRecord(events->main_begin, stream);
-  e = bk == 16 ? launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.stride_c)
-               : launch_main<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.stride_c);
+  e = launch_config(bk, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.stride_c);
   if (events != nullptr && events->main_end != nullptr) cudaEventRecord(events->main_end, stream);
   return e;
 }

@@ -22,7 +22,7 @@ from tests.golden.make_golden import GEMMA, M20, STARTER
 
 pytestmark = pytest.mark.gpu
 
-VARIANTS = [R.SGEMM_FMA, R.SGEMM_TC_BK16, R.SGEMM_TC_BK32]
+VARIANTS = [R.SGEMM_FMA, R.SGEMM_TC_BK16, R.SGEMM_TC_BK32, R.SGEMM_TC_PAIR16, R.SGEMM_TC_PAIR32]
 NORMWISE_TOL = 1e-5
 
 
@@ -177,7 +177,7 @@ def _checksums(o, c64, a, b, m, n, k):
     assert np.max(np.abs(col_got - col_ref)) <= m * 1e-5 * scale
 
 
-@pytest.mark.parametrize("variant", [R.SGEMM_TC_BK16, R.SGEMM_TC_BK32])
+@pytest.mark.parametrize("variant", [R.SGEMM_TC_BK16, R.SGEMM_TC_BK32, R.SGEMM_TC_PAIR16, R.SGEMM_TC_PAIR32])
 @pytest.mark.parametrize("shape,seed", [((8192, 8192, 8192), 3), ((16384, 16384, 4096), 4)])
 def test_baseline_large_shapes(runtime, oracle_mod, shape, seed, variant):
     """8192^3 and 16384^2 x 4096: sampled rows vs fp64 plus whole-matrix checksums."""
@@ -189,6 +189,24 @@ def test_baseline_large_shapes(runtime, oracle_mod, shape, seed, variant):
     for rows in (slice(0, 32), slice(m // 2 - 16, m // 2 + 16), slice(m - 32, m)):
         _check_against_fp64(o, c, a, b, m, n, k, rows=rows)
     _checksums(o, c, a, b, m, n, k)
+
+
+def test_variants_agree_with_batched_and_transposed_forms(runtime, oracle_mod):
+    """Strided-batch and B^T (NT) forms equal per-entry products (attention's Q K^T and P V)."""
+    import torch
+    o = oracle_mod
+    bsz, m, n, k = 3, 300, 200, 136
+    a = o.uniform_matrix(bsz * m, k, 31).reshape(bsz, m, k)
+    bt = o.uniform_matrix(bsz * n, k, 32).reshape(bsz, n, k)
+    da, dbt = torch.from_numpy(a).cuda(), torch.from_numpy(bt).cuda()
+    for variant in VARIANTS:
+        dc = torch.full((bsz, m, n), float("nan"), device="cuda")
+        runtime.sgemm_batched_device(da, k, m * k, dbt, k, n * k, True, dc, n, m * n, bsz, m, n, k, variant)
+        assert runtime.sync_status().ok
+        got = dc.cpu().numpy()
+        for i in range(bsz):
+            ref = o.sgemm_f64(np.ascontiguousarray(a[i]).ravel(), np.ascontiguousarray(bt[i].T).ravel(), m, n, k)
+            assert normwise(got[i].ravel(), ref) <= NORMWISE_TOL, (variant, i)
 
 
 def test_host_abi_matches_device_path(runtime, oracle_mod):
