@@ -368,11 +368,13 @@ cudaError_t launch_warp(const float* in, uint64_t stride, float* out, float* inv
                         cudaStream_t stream) {
   const uint32_t row_bytes = w * 4u;
   uint32_t wpc, ns, rps = 1;
-  if (row_bytes <= 2048u) {  // short rows: 8 warps, 4 KB slots of rps rows, 64 KB ring -> 3 CTAs per SM
+  if (row_bytes <= 2048u) {
+    // Short rows: 8 warps x 7 slots of 4 KB (rps rows each) = 224 KB, one CTA
+    // per SM.  148 SMs then hold ~33 MB in flight, so a 32768 x 256 input is
+    // requested in a single round trip instead of being pipelined in rounds.
     wpc = 8;
     rps = 4096u / row_bytes;
-    ns = 65536u / (wpc * rps * row_bytes);
-    ns = ns < 2 ? 2 : (ns > 8 ? 8 : ns);
+    ns = 7;
   } else if (row_bytes <= 8192u) {  // 8 warps x 3 slots, one CTA per SM
     wpc = 8;
     ns = 3;
