@@ -153,6 +153,7 @@ enum {
   OCT_B200_DETAIL_BAD_VARIANT = -7004,       /* unknown kernel variant id */
   OCT_B200_DETAIL_UNALIGNED = -7005,         /* device pointer not 16-byte aligned */
   OCT_B200_DETAIL_NOALLOC_TOO_LARGE = -7006, /* product needs more than the fixed no-alloc scratch */
+  OCT_B200_DETAIL_UNSUPPORTED_SHAPE = -7007, /* shape outside a fused kernel's envelope */
   OCT_B200_DETAIL_BLOCK_INVALID = -7010,     /* block configuration / slot / count rejected */
   OCT_B200_DETAIL_BLOCK_ALLOC = -7011,       /* block weights or workspaces could not be allocated */
   OCT_B200_DETAIL_BLOCK_NCCL = -7012,        /* tensor-parallel communicator unavailable */
@@ -593,6 +594,19 @@ PROM_REACTOR_API int oct_b200_reduction_device(void* handle, const float* d_in, 
 PROM_REACTOR_API int oct_b200_rmsnorm_device(void* handle, const float* d_in, const float* d_weight, float* d_out,
                                              float* d_inv_rms, uint32_t rows, uint32_t width, float epsilon,
                                              void* stream, int* out_detail_code);
+
+/* No counterpart in the reference's C ABI: the exact attention of the Z-Image
+   block (`canonicalAttention`, internal/prometheus/zimage/canonical_reference.go:241-289)
+   on device pointers, as one fused tcgen05 3xTF32 kernel.
+   q, k, v, out: [items * seq][heads * head_dim] row-major fp32, token-major
+   with head h in columns h*head_dim .. (the reference's
+   [(token*heads + head)*head_dim + c] layout); out = softmax(q k^T * scale) v
+   per item and head, bidirectional.  head_dim must be 128 and seq a multiple
+   of 128 (else PROM_ERROR with OCT_B200_DETAIL_UNSUPPORTED_SHAPE).  The TF32
+   split copies of q, k and v^T go to the handle's scratch. */
+PROM_REACTOR_API int oct_b200_attention_device(void* handle, const float* d_q, const float* d_k, const float* d_v,
+                                               float* d_out, uint32_t items, uint32_t seq, uint32_t heads,
+                                               uint32_t head_dim, float scale, void* stream, int* out_detail_code);
 
 /* Waits for `stream` (NULL: the CUDA default stream), then reads and
    clears the device status words the kernels write: returns PROM_ERROR with

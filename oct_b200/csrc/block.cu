@@ -31,6 +31,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <dlfcn.h>
 #include <mutex>
@@ -132,11 +133,14 @@ __global__ void rope_half_kernel(float* __restrict__ buf, uint64_t ld, uint32_t 
 }
 
 // Per-head RMSNorm (width 128, gain g, eps) then 3-axis interleaved RoPE with
-// table cos/sin[pos][64] in place; one warp per (row, head), 4 channels a lane.
+// table cos/sin[pos][64]; one warp per (row, head), 4 channels a lane.
 // Covers `heads` heads starting at column col0 (Q then K are two launches).
+// Writes in place, or, with hi != null, the TF32 hi/lo split into the
+// per-head layout of the fused attention kernel: row (item*heads + head)*seq + pos.
 __global__ void qk_norm_rope3_kernel(float* __restrict__ buf, uint64_t ld, uint32_t col0, uint32_t heads,
                                      const float* __restrict__ g, float eps, const float* __restrict__ cos_t,
-                                     const float* __restrict__ sin_t, uint32_t seq, uint32_t rows) {
+                                     const float* __restrict__ sin_t, uint32_t seq, uint32_t rows,
+                                     float* __restrict__ hi, float* __restrict__ lo) {
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t warps = static_cast<uint64_t>(rows) * heads;
   for (uint64_t wi = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; wi < warps;
@@ -164,7 +168,22 @@ __global__ void qk_norm_rope3_kernel(float* __restrict__ buf, uint64_t ld, uint3
     o.y = v.x * s0 + v.y * c0;
     o.z = v.z * c1 - v.w * s1;
     o.w = v.z * s1 + v.w * c1;
-    *reinterpret_cast<float4*>(p) = o;
+    if (hi == nullptr) {
+      *reinterpret_cast<float4*>(p) = o;
+    } else {
+      const uint64_t srow = (static_cast<uint64_t>(row / seq) * heads + head) * seq + pos;
+      float4 h, l;
+      h.x = to_tf32(o.x);
+      h.y = to_tf32(o.y);
+      h.z = to_tf32(o.z);
+      h.w = to_tf32(o.w);
+      l.x = to_tf32(o.x - h.x);
+      l.y = to_tf32(o.y - h.y);
+      l.z = to_tf32(o.z - h.z);
+      l.w = to_tf32(o.w - h.w);
+      *reinterpret_cast<float4*>(hi + srow * 128 + lane * 4) = h;
+      *reinterpret_cast<float4*>(lo + srow * 128 + lane * 4) = l;
+    }
   }
 }
 
@@ -378,13 +397,26 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
   // activations and workspaces
   hbuf_ = alloc(T * d.hidden);
   qkv_ = alloc(T * qkv_cols);
-  scores_ = alloc(static_cast<uint64_t>(d.heads) * d.seq_len * d.seq_len);  // one batch item at a time
+  fused_attn_ = d.family == kDit && flash_attention_supported(d.head_dim, d.seq_len);
+  if (const char* mode = std::getenv("OCT_B200_DIT_ATTENTION"))
+    if (std::strcmp(mode, "materialized") == 0) fused_attn_ = false;
+  if (fused_attn_) {
+    // Q, K and V^T in the TF32 hi/lo per-head layouts of the fused kernel, all batch items
+    const uint64_t e = T * attn_cols;
+    qsplit_ = alloc(2 * e);
+    ksplit_ = alloc(2 * e);
+    vtsplit_ = alloc(2 * e);
+    ok = ok && qsplit_ && ksplit_ && vtsplit_;
+  } else {
+    scores_ = alloc(static_cast<uint64_t>(d.heads) * d.seq_len * d.seq_len);  // one batch item at a time
+    ok = ok && scores_;
+  }
   attn_ = alloc(T * attn_cols);
   x1_ = alloc(T * d.hidden);
   proj_ = alloc(T * d.hidden);
   gu_ = alloc(T * 2ull * d.ffn);
   act_ = alloc(T * d.ffn);
-  {
+  if (!fused_attn_) {
     // P in the TF32 split layout of the P V product, one batch item at a time
     const SplitDims pd = split_dims(d.seq_len, d.head_dim, d.seq_len);
     p_mp_ = pd.mp;
@@ -396,11 +428,13 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
   const uint64_t a_need = std::max({sgemm_tc_a_scratch_bytes(T, d.hidden), sgemm_tc_a_scratch_bytes(T, attn_cols),
                                     sgemm_tc_a_scratch_bytes(T, d.ffn)});
   const SplitDims vd = split_dims(1, d.head_dim, d.seq_len);  // V split of the P V product
-  const uint64_t b_need = std::max(sgemm_tc_scratch_bytes(d.seq_len, d.seq_len, d.head_dim, d.heads),
-                                   static_cast<uint64_t>(2ull * sizeof(float) * d.heads * vd.np * vd.kp));
+  const uint64_t b_need =
+      fused_attn_ ? 0
+                  : std::max(sgemm_tc_scratch_bytes(d.seq_len, d.seq_len, d.head_dim, d.heads),
+                             static_cast<uint64_t>(2ull * sizeof(float) * d.heads * vd.np * vd.kp));
   scratch_ = alloc(std::max(a_need, b_need) / sizeof(float) + 1);
   err_ = reinterpret_cast<unsigned int*>(alloc(4));
-  ok = ok && hbuf_ && qkv_ && scores_ && attn_ && x1_ && proj_ && gu_ && act_ && scratch_ && err_;
+  ok = ok && hbuf_ && qkv_ && attn_ && x1_ && proj_ && gu_ && act_ && scratch_ && err_;
   if (!ok) return -3;
   if (cudaMemsetAsync(err_, 0, 16, stream_) != cudaSuccess) return -4;
   if (build_rope_tables() != 0) return -4;
@@ -617,13 +651,27 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
   e = gemm(hbuf_, d.hidden, wqkv_, qkv_, qkv_cols, T);
   if (!ok()) return -4;
   const uint64_t qk_warps = static_cast<uint64_t>(T) * d.heads;
-  qk_norm_rope3_kernel<<<grid_for(qk_warps * 32, NT), NT, 0, stream_>>>(qkv_, qkv_cols, 0, d.heads, qn_, 1e-5f,
-                                                                       rope_cos_, rope_sin_, d.seq_len, T);
+  const uint64_t se = static_cast<uint64_t>(T) * attn_cols;  // elements of one split half (this batch)
+  qk_norm_rope3_kernel<<<grid_for(qk_warps * 32, NT), NT, 0, stream_>>>(
+      qkv_, qkv_cols, 0, d.heads, qn_, 1e-5f, rope_cos_, rope_sin_, d.seq_len, T, fused_attn_ ? qsplit_ : nullptr,
+      fused_attn_ ? qsplit_ + se : nullptr);
   if (!ok()) return -4;
-  qk_norm_rope3_kernel<<<grid_for(qk_warps * 32, NT), NT, 0, stream_>>>(qkv_, qkv_cols, attn_cols, d.heads, kn_,
-                                                                       1e-5f, rope_cos_, rope_sin_, d.seq_len, T);
+  qk_norm_rope3_kernel<<<grid_for(qk_warps * 32, NT), NT, 0, stream_>>>(
+      qkv_, qkv_cols, attn_cols, d.heads, kn_, 1e-5f, rope_cos_, rope_sin_, d.seq_len, T,
+      fused_attn_ ? ksplit_ : nullptr, fused_attn_ ? ksplit_ + se : nullptr);
   if (!ok()) return -4;
-  for (uint32_t b = 0; b < batch && e == cudaSuccess; ++b) e = attention(b, qkv_cols, attn_cols, 2 * attn_cols, false);
+  if (fused_attn_) {
+    // one fused launch over every (query tile, head, batch item)
+    e = split_transpose_heads(qkv_ + 2ull * attn_cols, qkv_cols, batch, d.heads, d.seq_len, vtsplit_, vtsplit_ + se,
+                              stream_);
+    if (!ok()) return -4;
+    const AttnOperands ops{qsplit_, qsplit_ + se, ksplit_, ksplit_ + se, vtsplit_, vtsplit_ + se};
+    e = flash_attention_tf32x3(ops, attn_, attn_cols, batch, d.heads, d.seq_len,
+                               1.0f / std::sqrt(static_cast<float>(d.head_dim)), err_, stream_);
+  } else {
+    for (uint32_t b = 0; b < batch && e == cudaSuccess; ++b)
+      e = attention(b, qkv_cols, attn_cols, 2 * attn_cols, false);
+  }
   if (!ok()) return -4;
   e = gemm(attn_, attn_cols, wo_, proj_, d.hidden, T);
   if (ok()) e = all_reduce(proj_, static_cast<uint64_t>(T) * d.hidden);

@@ -55,6 +55,7 @@ class Block {
   cudaStream_t stream() const { return stream_; }
   unsigned int read_status();
   const BlockDims& dims() const { return dims_; }
+  bool fused_attention() const { return fused_attn_; }
 
  private:
   struct SplitW {
@@ -82,6 +83,9 @@ class Block {
   float *gu_ = nullptr, *act_ = nullptr, *scratch_ = nullptr;
   float* psplit_ = nullptr;  // attention probabilities, TF32 hi then lo, [heads][p_mp_][p_kp_]
   uint32_t p_mp_ = 0, p_kp_ = 0;
+  // fused attention (DiT, head_dim 128): Q, K, V^T split to TF32 hi/lo per head
+  bool fused_attn_ = false;
+  float *qsplit_ = nullptr, *ksplit_ = nullptr, *vtsplit_ = nullptr;
   unsigned int* err_ = nullptr;
 };
 

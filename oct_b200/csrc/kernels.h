@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace oct {
@@ -65,6 +66,32 @@ cudaError_t sgemm_tc_presplit_a(const float* ahi, const float* alo, const float*
 // Plain FP32-FMA SGEMM on the CUDA cores (control variant); no scratch.
 cudaError_t sgemm_fma(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
                       uint32_t m, uint32_t n, uint32_t k, cudaStream_t stream, const GemmBatch* batch = nullptr);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (null if absent).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn();
+
+// ---------------------------------------------------------------- fused attention
+// Exact bidirectional attention over heads of 128 channels, one fused
+// tensor-core kernel (attention.cu).  Operands are TF32 hi/lo splits:
+//   q/k hi, lo: [items*heads*seq][128] (row (item*heads + h)*seq + position)
+//   vt hi, lo:  [items*heads*128][seq] (V transposed per head)
+// out[(item*seq + position) * ldo + h*128 + c].  seq must be a multiple of 128.
+struct AttnOperands {
+  const float *qhi, *qlo, *khi, *klo, *vthi, *vtlo;
+};
+bool flash_attention_supported(uint32_t head_dim, uint32_t seq);
+cudaError_t flash_attention_tf32x3(const AttnOperands& in, float* out, uint64_t ldo, uint32_t items, uint32_t heads,
+                                   uint32_t seq, float scale, unsigned int* err, cudaStream_t stream);
+// V columns of `heads` heads ([items*seq][ldv], head h at columns h*128..) ->
+// the vt hi/lo layout above.
+// Q or K columns of `heads` heads ([items*seq][ldx]) -> the q/k hi/lo layout above.
+cudaError_t split_heads(const float* x, uint64_t ldx, uint32_t items, uint32_t heads, uint32_t seq, float* hi,
+                        float* lo, cudaStream_t stream);
+cudaError_t split_transpose_heads(const float* v, uint64_t ldv, uint32_t items, uint32_t heads, uint32_t seq,
+                                  float* vthi, float* vtlo, cudaStream_t stream);
 
 // ---------------------------------------------------------------- reductions
 // op: 1 = row sum, 2 = row max, 3 = stable softmax.  `nonfinite` (device

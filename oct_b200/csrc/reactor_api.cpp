@@ -159,6 +159,18 @@ bool checked_mul(uint64_t a, uint64_t b, uint64_t* out) {
   return true;
 }
 
+// The next set of per-launch timing events (created on first use); null on failure.
+const oct::SgemmEvents* next_timing_events(Runtime* rt) {
+  if (rt->timing_used == rt->timing_events.size()) {
+    oct::SgemmEvents fresh;
+    if (cudaEventCreate(&fresh.split_begin) != cudaSuccess || cudaEventCreate(&fresh.main_begin) != cudaSuccess ||
+        cudaEventCreate(&fresh.main_end) != cudaSuccess)
+      return nullptr;
+    rt->timing_events.push_back(fresh);
+  }
+  return &rt->timing_events[rt->timing_used++];
+}
+
 // ---------------------------------------------------------------- SGEMM core
 // Enqueues C = A * B for device pointers; chooses the kernel.
 int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
@@ -180,16 +192,7 @@ int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uin
     if (e != cudaSuccess) return OCT_B200_DETAIL_OUT_OF_MEMORY;
     const int bk = variant == OCT_B200_SGEMM_TC3XTF32 ? oct::kTcSingle16 : static_cast<int>(variant);
     const oct::SgemmEvents* ev = nullptr;
-    if (rt->timing) {
-      if (rt->timing_used == rt->timing_events.size()) {
-        oct::SgemmEvents fresh;
-        if (cudaEventCreate(&fresh.split_begin) != cudaSuccess || cudaEventCreate(&fresh.main_begin) != cudaSuccess ||
-            cudaEventCreate(&fresh.main_end) != cudaSuccess)
-          return OCT_B200_DETAIL_CUDA_ERROR;
-        rt->timing_events.push_back(fresh);
-      }
-      ev = &rt->timing_events[rt->timing_used++];
-    }
+    if (rt->timing && (ev = next_timing_events(rt)) == nullptr) return OCT_B200_DETAIL_CUDA_ERROR;
     e = oct::sgemm_tc(a, lda, b, ldb, c, ldc, m, n, k, rt->scratch.aligned(), rt->err_word(), bk, stream, ev, batch);
   } else {
     return OCT_B200_DETAIL_BAD_VARIANT;
@@ -1215,6 +1218,66 @@ int oct_b200_reduction_device(void* handle, const float* d_in, float* d_out, uin
     cudaStream_t s = static_cast<cudaStream_t>(stream);  // NULL is the CUDA default stream
     const cudaError_t e = oct::row_reduce(d_in, d_out, rows, width, operation, rt->nonfinite_word(), rt->err_word(), s);
     if (e != cudaSuccess) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
+      return PROM_ERROR;
+    }
+    return PROM_OK;
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+int oct_b200_attention_device(void* handle, const float* d_q, const float* d_k, const float* d_v, float* d_out,
+                              uint32_t items, uint32_t seq, uint32_t heads, uint32_t head_dim, float scale,
+                              void* stream, int* out_detail_code) {
+  try {
+    if (out_detail_code) *out_detail_code = 0;
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    if (d_q == nullptr || d_k == nullptr || d_v == nullptr || d_out == nullptr || !finite_f(scale)) {
+      if (out_detail_code) *out_detail_code = PROM_ERROR;
+      return PROM_ERROR;
+    }
+    if (items == 0 || heads == 0 || seq == 0) return PROM_OK;
+    if (!oct::flash_attention_supported(head_dim, seq) || items > 65535u || heads > 65535u) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_UNSUPPORTED_SHAPE;
+      return PROM_ERROR;
+    }
+    for (const float* p : {d_q, d_k, d_v, static_cast<const float*>(d_out)})
+      if (reinterpret_cast<uintptr_t>(p) % 16 != 0) {
+        if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_UNALIGNED;
+        return PROM_ERROR;
+      }
+    if (!rt->available) {
+      if (out_detail_code) *out_detail_code = PROM_DETAIL_CAPABILITY_MISMATCH;
+      return PROM_ERROR;
+    }
+    std::lock_guard<std::mutex> lock(rt->mu);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);  // NULL is the CUDA default stream
+    const uint64_t ld = static_cast<uint64_t>(heads) * head_dim;
+    const uint64_t e = static_cast<uint64_t>(items) * seq * ld;  // elements of one split half
+    const uint64_t half_bytes = (e * sizeof(float) + 1023) & ~uint64_t(1023);
+    if (rt->scratch.ensure(6 * half_bytes, s) != cudaSuccess) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_OUT_OF_MEMORY;
+      return PROM_ERROR;
+    }
+    auto part = [&](int i) { return reinterpret_cast<float*>(static_cast<char*>(rt->scratch.aligned()) + i * half_bytes); };
+    const oct::SgemmEvents* ev = nullptr;
+    if (rt->timing && (ev = next_timing_events(rt)) == nullptr) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
+      return PROM_ERROR;
+    }
+    cudaError_t err = ev ? cudaEventRecord(ev->split_begin, s) : cudaSuccess;
+    if (err == cudaSuccess) err = oct::split_heads(d_q, ld, items, heads, seq, part(0), part(1), s);
+    if (err == cudaSuccess) err = oct::split_heads(d_k, ld, items, heads, seq, part(2), part(3), s);
+    if (err == cudaSuccess) err = oct::split_transpose_heads(d_v, ld, items, heads, seq, part(4), part(5), s);
+    if (err == cudaSuccess && ev) err = cudaEventRecord(ev->main_begin, s);
+    if (err == cudaSuccess) {
+      const oct::AttnOperands ops{part(0), part(1), part(2), part(3), part(4), part(5)};
+      err = oct::flash_attention_tf32x3(ops, d_out, ld, items, heads, seq, scale, rt->err_word(), s);
+    }
+    if (err == cudaSuccess && ev) err = cudaEventRecord(ev->main_end, s);
+    if (err != cudaSuccess) {
       if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
       return PROM_ERROR;
     }

@@ -368,13 +368,12 @@ cudaError_t launch_warp(const float* in, uint64_t stride, float* out, float* inv
                         cudaStream_t stream) {
   const uint32_t row_bytes = w * 4u;
   uint32_t wpc, ns, rps = 1;
-  if (row_bytes <= 2048u) {
-    // Short rows: 8 warps x 7 slots of 4 KB (rps rows each) = 224 KB, one CTA
-    // per SM.  148 SMs then hold ~33 MB in flight, so a 32768 x 256 input is
-    // requested in a single round trip instead of being pipelined in rounds.
+  if (row_bytes <= 2048u) {  // short rows: 8 warps, 4 KB slots of rps rows, 64 KB ring -> 3 CTAs per SM
+    // (a deeper 224 KB ring at one CTA per SM measured slower: fewer CTAs to hide the latency)
     wpc = 8;
     rps = 4096u / row_bytes;
-    ns = 7;
+    ns = 65536u / (wpc * rps * row_bytes);
+    ns = ns < 2 ? 2 : (ns > 8 ? 8 : ns);
   } else if (row_bytes <= 8192u) {  // 8 warps x 3 slots, one CTA per SM
     wpc = 8;
     ns = 3;

@@ -300,6 +300,8 @@ SIGNATURES = {
                   _i32p]),
     "oct_b200_reduction_device": (C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _i32p]),
     "oct_b200_rmsnorm_device": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, C.c_float, _vp, _i32p]),
+    "oct_b200_attention_device": (
+        C.c_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, C.c_float, _vp, _i32p]),
     "oct_b200_sync_status": (C.c_int, [_vp, _vp, _i32p]),
     "oct_b200_sgemm_device_noalloc": (
         C.c_int, [_vp, _u64, _vp, _u64, _vp, _u64, _u32, _u32, _u32, _vp, _i32p]),
@@ -582,6 +584,17 @@ class Runtime:
                                               _stream_ptr(stream), C.byref(detail))
         if rc != PROM_OK:
             raise RuntimeError(f"device rmsnorm rc={rc} detail={detail.value}")
+
+    def attention_device(self, q, k, v, out, items: int, seq: int, heads: int, head_dim: int,
+                         scale: Optional[float] = None, stream=None) -> None:
+        """Fused exact attention; q, k, v, out: [items*seq][heads*head_dim] on the device."""
+        if scale is None:
+            scale = float(np.float32(1.0) / np.sqrt(np.float32(head_dim)))
+        detail = C.c_int()
+        rc = self.lib.oct_b200_attention_device(self.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(out), items, seq, heads,
+                                                head_dim, scale, _stream_ptr(stream), C.byref(detail))
+        if rc != PROM_OK:
+            raise RuntimeError(f"device attention rc={rc} detail={detail.value}")
 
     def sync_status(self, stream=None) -> CallStatus:
         detail = C.c_int()

@@ -24,6 +24,7 @@ CASES = {
     "dit_small": (OB.dit_config(seq_len=256, hidden=512, heads=4, ffn=1024, grid_w=16), 2),
     "gemma_baseline_dims": (OB.gemma_config(seq_len=256), 1),
     "dit_baseline_dims": (OB.dit_config(seq_len=256, grid_w=16), 1),
+    "dit_seq1024": (OB.dit_config(seq_len=1024, hidden=512, heads=4, ffn=1024, grid_w=32), 2),
 }
 
 
@@ -85,3 +86,29 @@ def test_block_is_deterministic_and_batch_independent(runtime):
         blk.close()
     assert np.array_equal(y2[cfg.seq_len:], y1)
     assert np.array_equal(y2, again)
+
+
+def test_dit_fused_and_materialized_attention_agree(runtime, monkeypatch):
+    """The DiT block's fused attention kernel and its materialised path (scores
+    in HBM, softmax kernel, two batched products) both meet the oracle bar."""
+    import torch
+    cfg, batch = CASES["dit_small"]
+    w = OB.random_weights(cfg, seed=21)
+    rng = np.random.Generator(np.random.PCG64(22))
+    x = rng.standard_normal((batch * cfg.seq_len, cfg.hidden), dtype=np.float32)
+    ts = [700.0, 100.0]
+    outs = {}
+    for mode in ("fused", "materialized"):
+        monkeypatch.setenv("OCT_B200_DIT_ATTENTION", mode)
+        blk = make_block(runtime, cfg, batch)
+        try:
+            blk.set_weights(w)
+            outs[mode] = blk.forward(x, batch, ts)
+        finally:
+            blk.close()
+        assert runtime.sync_status().ok
+    ref = OB.forward(cfg, w, x, ts)
+    for mode, y in outs.items():
+        nw, l2 = errors(y, ref)
+        print(f"dit {mode}: normwise {nw:.3e}  relL2 {l2:.3e}")
+        assert nw <= NORMWISE_TOL and l2 <= L2_TOL, (mode, nw, l2)
