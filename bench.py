@@ -63,7 +63,7 @@ def parse_args():
     p.add_argument("--no-secondary", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU sample")
     p.add_argument("--workload", default="sgemm",
-                   choices=["sgemm", "gemma_block", "dit_block", "reductions"],
+                   choices=["sgemm", "gemma_block", "dit_block", "reductions", "attention"],
                    help="sgemm = the driver contract line; the others run one secondary measurement "
                         "alone (for profiling) and print it as JSON")
     return p.parse_args()
@@ -242,6 +242,7 @@ def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
     stream = torch.cuda.current_stream()
     # Transformer blocks at BASELINE configs[3] / configs[4] (random init, synthetic tokens)
     out.extend(block_measurements(rt, torch, stream))
+    out.extend(attention_measurements(rt, torch, stream))
     # FMA control and the 32-deep tensor-core variant at the headline shape
     m = n = k = 8192
     g = torch.Generator(device="cuda").manual_seed(7)
@@ -263,6 +264,40 @@ def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
                     "TFLOP/s": round(2.0 * m * n * k / (ms * 1e-3) / 1e12, 2)})
     rt.set_kernel_timing(False)
     return out
+
+
+def attention_measurements(rt, torch, stream, iters: int = 5) -> list[dict]:
+    """The fused attention kernel alone at the DiT block's shape (2 items x 4096 tokens x 24 heads of 128)."""
+    from oracle import blocks as OB  # used only for the shape
+    pk, _ = peaks()
+    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
+    cfg, items = OB.dit_config(), 2
+    seq, heads, hd = cfg.seq_len, cfg.heads, cfg.head_dim
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q, k, v = (torch.randn(items * seq, heads * hd, device="cuda", generator=g) for _ in range(3))
+    o = torch.empty_like(q)
+    for _ in range(2):
+        rt.attention_device(q, k, v, o, items, seq, heads, hd, stream=stream)
+    rt.set_kernel_timing(True)
+    rt.read_kernel_timing()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iters):
+        rt.attention_device(q, k, v, o, items, seq, heads, hd, stream=stream)
+    e1.record(stream)
+    e1.synchronize()
+    split_ms, main_ms, launches = rt.read_kernel_timing()
+    rt.set_kernel_timing(False)
+    st = rt.sync_status()
+    if not st.ok:
+        raise RuntimeError(f"attention status {st}")
+    ms = e0.elapsed_time(e1) / iters
+    kms = main_ms / max(1, launches)
+    flops = 4.0 * items * heads * seq * seq * hd  # Q K^T and P V
+    return [{"kernel": "flash_attention_3xtf32", "items": items, "seq": seq, "heads": heads, "head_dim": hd,
+             "ms": round(ms, 3), "kernel_ms": round(kms, 3), "split_ms": round(split_ms / max(1, launches), 3),
+             "TFLOP/s": round(flops / (kms * 1e-3) / 1e12, 2),
+             "frac_of_3xtf32_peak": round(flops / (kms * 1e-3) / 1e12 / peak, 3)}]
 
 
 def block_measurements(rt, torch, stream, iters: int = 5, only: str | None = None) -> list[dict]:
@@ -549,6 +584,8 @@ def run_single_workload(args) -> None:
     pk, _ = peaks()
     if args.workload == "reductions":
         res = reduction_measurements(rt, torch, pk["hbm_gbs"])
+    elif args.workload == "attention":
+        res = attention_measurements(rt, torch, torch.cuda.current_stream(), iters=max(1, args.steps))
     else:
         res = block_measurements(rt, torch, torch.cuda.current_stream(), iters=max(1, args.steps), only=args.workload)
     print(json.dumps({"workload": args.workload, "results": res}), flush=True)

@@ -20,10 +20,13 @@
 // product (S) or 32 keys (O block); every O block is merged into fp32 running
 // sums in registers with round-to-nearest, so the result keeps fp32 accuracy.
 //
-// Warp roles (192 threads, one CTA per SM): warp 0 TMA producer (K and V^T
-// blocks through a 3-stage ring), warp 1 MMA issuer, warps 2-5 softmax and
-// merge with one query row per thread.  Every wait is bounded (ptx.cuh); on a
-// timeout the kernel records the error bit, drains its MMAs and returns.
+// Warp roles (320 threads, one CTA per SM): warp 0 TMA producer (K and V^T
+// blocks through a 3-stage ring), warp 1 MMA issuer, warps 2-5 softmax
+// (S -> P, one query row per thread), warps 6-9 correction (the fp32 output
+// sums of the same rows, merged from each P V block; they take each row's
+// rescale factor from the softmax warps through shared memory).  Every wait
+// is bounded (ptx.cuh); on a timeout the kernel records the error bit, drains
+// its MMAs and returns.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -45,7 +48,7 @@ constexpr uint32_t FA_K_BYTES = FA_BKV * FA_HD * 4;   // 16 KB: one of K hi / K 
 constexpr uint32_t FA_V_BYTES = FA_HD * FA_BKV * 4;   // 16 KB: one of V^T hi / lo
 constexpr uint32_t FA_STAGE_BYTES = 2 * FA_K_BYTES + 2 * FA_V_BYTES;
 constexpr uint32_t FA_SMEM = FA_STAGES * FA_STAGE_BYTES + 1024;
-constexpr int FA_THREADS = 192;
+constexpr int FA_THREADS = 320;
 constexpr uint32_t COL_QHI = 0, COL_QLO = 128, COL_SM = 256, COL_SC = 288, COL_PHI = 320, COL_PLO = 352,
                    COL_O = 384;
 
@@ -73,8 +76,25 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Named barrier 1 between the MMA warp and the four softmax warps.
-__device__ __forceinline__ void q_ready_barrier() { asm volatile("bar.sync 1, 160;" ::: "memory"); }
+// Named barrier 1: the MMA warp and the eight softmax / correction warps
+// (Q hi/lo are in tensor memory).
+__device__ __forceinline__ void q_ready_barrier() { asm volatile("bar.sync 1, 288;" ::: "memory"); }
+
+// True in exactly one lane of a converged warp.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// The running max of a row moves only when a key block's max exceeds it by
+// more than FA_TAU (natural-log units): probabilities then stay below e^8 in
+// fp32, and the rescale of the output sums is skipped in almost every block.
+constexpr float FA_TAU = 8.0f;
 
 __global__ void __launch_bounds__(FA_THREADS, 1)
     flash_attn_kernel(const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
@@ -87,6 +107,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t kv_full[FA_STAGES], kv_empty[FA_STAGES];
   __shared__ __align__(8) uint64_t s_full, s_empty, p_full, o_full, o_empty, drain_bar;
+  __shared__ __align__(8) uint64_t alpha_full[2], l_ready;
+  __shared__ float alpha_sh[2][FA_BQ];  // per-row rescale factor of key block j, slot (j - 1) & 1
+  __shared__ float inv_l_sh[FA_BQ];     // per-row 1 / sum of probabilities
   __shared__ uint32_t tmem_slot;
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -107,6 +130,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     mbar_init(&o_full, 1);
     mbar_init(&o_empty, 4);
     mbar_init(&drain_bar, 1);
+    mbar_init(&alpha_full[0], 4);
+    mbar_init(&alpha_full[1], 4);
+    mbar_init(&l_ready, 4);
     fence_mbar_init();
     fence_proxy_async_smem();
     prefetch_tensormap(&tm_khi);
@@ -143,65 +169,78 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    q_ready_barrier();  // Q hi/lo are in tensor memory
-    if (lane == 0) {
+    // ---------------- MMA issuer: the whole warp runs the loop converged (descriptors stay
+    // warp-uniform); one elected lane issues each tcgen05 instruction.
+    q_ready_barrier();
+    tc_fence_after();
+    auto issue_pv = [&](uint32_t jj) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(&p_full, jj & 1u, err, kErrWaitAccum))) return false;
+      if (jj >= 1 && !__all_sync(0xffffffffu, mbar_wait(&o_empty, (jj - 1) & 1u, err, kErrWaitAccum))) return false;
       tc_fence_after();
-      // ---------------- MMA issuer: S_j = Q K_j^T, then O = P_{j-1} V_{j-1}
-      auto issue_pv = [&](uint32_t jj) -> bool {
-        if (!mbar_wait(&p_full, jj & 1u, err, kErrWaitAccum)) return false;
-        if (jj >= 1 && !mbar_wait(&o_empty, (jj - 1) & 1u, err, kErrWaitAccum)) return false;
-        tc_fence_after();
-        const uint32_t st = jj % FA_STAGES;
-        const uint32_t vbase = smem_addr(smem + st * FA_STAGE_BYTES + 2 * FA_K_BYTES);
+      const uint32_t st = jj % FA_STAGES;
+      const uint32_t vbase = smem_addr(smem + st * FA_STAGE_BYTES + 2 * FA_K_BYTES);
 #pragma unroll
-        for (uint32_t kk = 0; kk < FA_BKV / 8; ++kk) {
-          const uint64_t dvh = umma_desc_kmajor(vbase + kk * 32, 128);
-          const uint64_t dvl = umma_desc_kmajor(vbase + FA_V_BYTES + kk * 32, 128);
+      for (uint32_t kk = 0; kk < FA_BKV / 8; ++kk) {
+        const uint64_t dvh = umma_desc_kmajor(vbase + kk * 32, 128);
+        const uint64_t dvl = umma_desc_kmajor(vbase + FA_V_BYTES + kk * 32, 128);
+        if (elect_one()) {
           umma_tf32_ts(tmem + COL_O, tmem + COL_PHI + kk * 8, dvl, IDESC_O, kk != 0 ? 1u : 0u);
           umma_tf32_ts(tmem + COL_O, tmem + COL_PLO + kk * 8, dvh, IDESC_O, 1u);
           umma_tf32_ts(tmem + COL_O, tmem + COL_PHI + kk * 8, dvh, IDESC_O, 1u);
         }
+        __syncwarp();
+      }
+      if (elect_one()) {
         umma_commit(&o_full);
         umma_commit(&kv_empty[st]);
-        return true;
-      };
-      bool ok = true;
-      for (uint32_t j = 0; j < nb && ok; ++j) {
-        const uint32_t st = j % FA_STAGES;
-        if (!mbar_wait(&kv_full[st], (j / FA_STAGES) & 1u, err, kErrWaitFull)) {
-          ok = false;
-          break;
-        }
-        if (j >= 1 && !mbar_wait(&s_empty, (j - 1) & 1u, err, kErrWaitAccum)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t kbase = smem_addr(smem + st * FA_STAGE_BYTES);
+      }
+      __syncwarp();
+      return true;
+    };
+    bool ok = true;
+    for (uint32_t j = 0; j < nb && ok; ++j) {
+      const uint32_t st = j % FA_STAGES;
+      if (!__all_sync(0xffffffffu, mbar_wait(&kv_full[st], (j / FA_STAGES) & 1u, err, kErrWaitFull))) {
+        ok = false;
+        break;
+      }
+      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(&s_empty, (j - 1) & 1u, err, kErrWaitAccum))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t kbase = smem_addr(smem + st * FA_STAGE_BYTES);
 #pragma unroll
-        for (uint32_t kk = 0; kk < FA_HD / 8; ++kk) {
-          const uint32_t koff = (kk >> 2) * 4096 + (kk & 3) * 32;  // box of 32 channels, 8 channels per step
-          const uint64_t dkh = umma_desc_kmajor(kbase + koff, 128);
-          const uint64_t dkl = umma_desc_kmajor(kbase + FA_K_BYTES + koff, 128);
+      for (uint32_t kk = 0; kk < FA_HD / 8; ++kk) {
+        const uint32_t koff = (kk >> 2) * 4096 + (kk & 3) * 32;  // box of 32 channels, 8 channels per step
+        const uint64_t dkh = umma_desc_kmajor(kbase + koff, 128);
+        const uint64_t dkl = umma_desc_kmajor(kbase + FA_K_BYTES + koff, 128);
+        if (elect_one()) {
           umma_tf32_ts(tmem + COL_SM, tmem + COL_QHI + kk * 8, dkh, IDESC_S, kk != 0 ? 1u : 0u);
           umma_tf32_ts(tmem + COL_SC, tmem + COL_QHI + kk * 8, dkl, IDESC_S, kk != 0 ? 1u : 0u);
           umma_tf32_ts(tmem + COL_SC, tmem + COL_QLO + kk * 8, dkh, IDESC_S, 1u);
         }
-        umma_commit(&s_full);
-        if (j >= 1) ok = issue_pv(j - 1);
+        __syncwarp();
       }
-      if (ok && nb > 0) ok = issue_pv(nb - 1);
-      umma_commit(&drain_bar);
+      if (elect_one()) umma_commit(&s_full);
+      __syncwarp();
+      if (j >= 1) ok = issue_pv(j - 1);
     }
+    if (ok && nb > 0) ok = issue_pv(nb - 1);
+    if (elect_one()) umma_commit(&drain_bar);
+    __syncwarp();
   } else {
-    // ---------------- softmax + merge: warps 2..5, thread = one query row (= TMEM lane)
-    const uint32_t quad = warp & 3u;  // a warp may only touch TMEM lanes 32 * (warp % 4) ...
+    // warps 2..5: softmax (S -> P); warps 6..9: correction (merge P V blocks into the output sums).
+    // Thread = one query row = one TMEM lane; a warp may only touch TMEM lanes 32 * (warp % 4) ...
+    const bool softmax = warp < 6;
+    const uint32_t quad = warp & 3u;
     const uint32_t row = quad * 32 + lane;
     const uint32_t lane_addr = (quad * 32u) << 16;
-    const uint64_t qrow = slab * seq + static_cast<uint64_t>(qtile) * FA_BQ + row;
-#pragma unroll 1
-    for (uint32_t part = 0; part < 2; ++part) {
-      const float* src = (part == 0 ? qhi : qlo) + qrow * FA_HD;
+    {
+      // Q hi (softmax warps) / Q lo (correction warps) -> TMEM, 32 channels at a time
+      const uint64_t qrow = slab * seq + static_cast<uint64_t>(qtile) * FA_BQ + row;
+      const float* src = (softmax ? qhi : qlo) + qrow * FA_HD;
+      const uint32_t col = softmax ? COL_QHI : COL_QLO;
 #pragma unroll 1
       for (uint32_t c0 = 0; c0 < FA_HD; c0 += 32) {
         uint32_t r[32];
@@ -213,99 +252,129 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           r[i + 2] = __float_as_uint(v.z);
           r[i + 3] = __float_as_uint(v.w);
         }
-        tmem_st_32x32b_x32(tmem + lane_addr + (part == 0 ? COL_QHI : COL_QLO) + c0, r);
-        tmem_st_wait();
+        tmem_st_32x32b_x32(tmem + lane_addr + col + c0, r);
       }
+      tmem_st_wait();
     }
     tc_fence_before();
     q_ready_barrier();
 
-    float o_run[FA_HD];
+    if (softmax) {
+      float m_run = -FLT_MAX;
+      double l_run = 0.0;
+      for (uint32_t j = 0; j < nb; ++j) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full, j & 1u, err, kErrWaitAccum))) break;
+        tc_fence_after();
+        float p[32];
+        {
+          uint32_t sm[32], sc[32];
+          tmem_ld_32x32b_x32(tmem + lane_addr + COL_SM, sm);
+          tmem_ld_32x32b_x32(tmem + lane_addr + COL_SC, sc);
+          tmem_ld_wait();
 #pragma unroll
-    for (int i = 0; i < static_cast<int>(FA_HD); ++i) o_run[i] = 0.f;
-    float m_run = -FLT_MAX;
-    double l_run = 0.0;
-    bool ok = true;
-    for (uint32_t j = 0; j < nb; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full, j & 1u, err, kErrWaitAccum));
-      if (!ok) break;
-      tc_fence_after();
-      float p[32];
-      {
-        uint32_t sm[32], sc[32];
-        tmem_ld_32x32b_x32(tmem + lane_addr + COL_SM, sm);
-        tmem_ld_32x32b_x32(tmem + lane_addr + COL_SC, sc);
-        tmem_ld_wait();
+          for (int i = 0; i < 32; ++i) p[i] = (__uint_as_float(sm[i]) + __uint_as_float(sc[i])) * scale;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty);
+        float t[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) p[i] = (__uint_as_float(sm[i]) + __uint_as_float(sc[i])) * scale;
+        for (int i = 0; i < 16; ++i) t[i] = fmaxf(p[i], p[i + 16]);
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; ++i) t[i] = fmaxf(t[i], t[i + w]);
+        const float mx = t[0];
+        const float m_new = (mx > m_run + FA_TAU) ? mx : m_run;  // the first block always moves it
+        const float alpha = (m_new == m_run) ? 1.0f : expf(m_run - m_new);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) p[i] = expf(p[i] - m_new);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t[i] = p[i] + p[i + 16];
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; ++i) t[i] += t[i + w];
+        l_run = l_run * static_cast<double>(alpha) + static_cast<double>(t[0]);
+        m_run = m_new;
+        if (j >= 1) {
+          // hand the rescale factor of this block to the correction warps, then
+          // wait until P V of the previous block has read the P buffer
+          alpha_sh[(j - 1) & 1u][row] = alpha;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&alpha_full[(j - 1) & 1u]);
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_full, (j - 1) & 1u, err, kErrWaitAccum))) break;
+          tc_fence_after();
+        }
+        {
+          uint32_t ph[32], pl[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float h = to_tf32(p[i]);
+            ph[i] = __float_as_uint(h);
+            pl[i] = __float_as_uint(to_tf32(p[i] - h));
+          }
+          tmem_st_32x32b_x32(tmem + lane_addr + COL_PHI, ph);
+          tmem_st_32x32b_x32(tmem + lane_addr + COL_PLO, pl);
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full);
       }
-      tc_fence_before();
+      inv_l_sh[row] = static_cast<float>(1.0 / l_run);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty);
-      float mx = m_run;
+      if (lane == 0) mbar_arrive(&l_ready);
+    } else {
+      float o_run[FA_HD];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) mx = fmaxf(mx, p[i]);
-      const float alpha = expf(m_run - mx);  // rescale of everything so far; 0 on the first block
-      float psum = 0.f;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        p[i] = expf(p[i] - mx);
-        psum += p[i];
-      }
-      l_run = l_run * static_cast<double>(alpha) + static_cast<double>(psum);
-      m_run = mx;
-      if (j >= 1) {
-        // o_run (relative to the previous max) += P_{j-1} V_{j-1}; then rescale to the new max
-        ok = __all_sync(0xffffffffu, mbar_wait(&o_full, (j - 1) & 1u, err, kErrWaitAccum));
+      for (int i = 0; i < static_cast<int>(FA_HD); ++i) o_run[i] = 0.f;
+      bool ok = true;
+      for (uint32_t j = 1; j < nb; ++j) {
+        // o_run (relative to the previous max) += P_{j-1} V_{j-1}, then * alpha_j
+        ok = __all_sync(0xffffffffu, mbar_wait(&alpha_full[(j - 1) & 1u], ((j - 1) >> 1) & 1u, err, kErrWaitAccum) &&
+                                         mbar_wait(&o_full, (j - 1) & 1u, err, kErrWaitAccum));
         if (!ok) break;
         tc_fence_after();
+        const float alpha = alpha_sh[(j - 1) & 1u][row];
+        const bool rescale = __any_sync(0xffffffffu, alpha != 1.0f);
 #pragma unroll
         for (uint32_t g = 0; g < FA_HD / 32; ++g) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tmem + lane_addr + COL_O + g * 32, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o_run[g * 32 + i] = (o_run[g * 32 + i] + __uint_as_float(r[i])) * alpha;
+          for (int i = 0; i < 32; ++i) o_run[g * 32 + i] += __uint_as_float(r[i]);
+          if (rescale) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o_run[g * 32 + i] *= alpha;
+          }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&o_empty);
       }
-      // P_j (hi, lo) -> TMEM; the P V product that read P_{j-1} has completed (o_full above)
-      {
-        uint32_t ph[32], pl[32];
+      if (ok && nb > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_full, (nb - 1) & 1u, err, kErrWaitAccum) &&
+                                         mbar_wait(&l_ready, 0, err, kErrWaitAccum));
+        if (ok) {
+          tc_fence_after();
+          const float inv = inv_l_sh[row];
+          float* dst = out + (static_cast<uint64_t>(item) * seq + static_cast<uint64_t>(qtile) * FA_BQ + row) * ldo +
+                       static_cast<uint64_t>(head) * FA_HD;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float h = to_tf32(p[i]);
-          ph[i] = __float_as_uint(h);
-          pl[i] = __float_as_uint(to_tf32(p[i] - h));
-        }
-        tmem_st_32x32b_x32(tmem + lane_addr + COL_PHI, ph);
-        tmem_st_32x32b_x32(tmem + lane_addr + COL_PLO, pl);
-        tmem_st_wait();
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full);
-    }
-    if (ok && nb > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&o_full, (nb - 1) & 1u, err, kErrWaitAccum));
-      if (ok) {
-        tc_fence_after();
-        const float inv = static_cast<float>(1.0 / l_run);
-        float* dst = out + (static_cast<uint64_t>(item) * seq + static_cast<uint64_t>(qtile) * FA_BQ + row) * ldo +
-                     static_cast<uint64_t>(head) * FA_HD;
+          for (uint32_t g = 0; g < FA_HD / 32; ++g) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem + lane_addr + COL_O + g * 32, r);
+            tmem_ld_wait();
 #pragma unroll
-        for (uint32_t g = 0; g < FA_HD / 32; ++g) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem + lane_addr + COL_O + g * 32, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const int c = static_cast<int>(g * 32) + i;
-            *reinterpret_cast<float4*>(dst + c) = make_float4(
-                (o_run[c] + __uint_as_float(r[i])) * inv, (o_run[c + 1] + __uint_as_float(r[i + 1])) * inv,
-                (o_run[c + 2] + __uint_as_float(r[i + 2])) * inv, (o_run[c + 3] + __uint_as_float(r[i + 3])) * inv);
+            for (int i = 0; i < 32; i += 4) {
+              const int c = static_cast<int>(g * 32) + i;
+              *reinterpret_cast<float4*>(dst + c) =
+                  make_float4((o_run[c] + __uint_as_float(r[i])) * inv, (o_run[c + 1] + __uint_as_float(r[i + 1])) * inv,
+                              (o_run[c + 2] + __uint_as_float(r[i + 2])) * inv,
+                              (o_run[c + 3] + __uint_as_float(r[i + 3])) * inv);
+            }
           }
         }
       }
