@@ -122,6 +122,7 @@ enum {
   PROM_DETAIL_REUSE_IN_FLIGHT = -6005,
   PROM_DETAIL_CAPABILITY_MISMATCH = -6006,
   PROM_DETAIL_PATH_DIRECT = 6101,
+  PROM_DETAIL_PATH_STAGED_UPLOAD_TILED = 6106,
   PROM_DETAIL_ASYNC_NOT_READY = -6108,
   PROM_DETAIL_ASYNC_NO_TASK = -6109,
   PROM_DETAIL_ASYNC_ALREADY_CONSUMED = -6110,
@@ -131,6 +132,34 @@ enum {
   PROM_DETAIL_ASYNC_UNCONSUMED = -6115,
   PROM_DETAIL_INJECTED_ASYNC_POLL_FAILURE = -6116,
   PROM_DETAIL_ASYNC_QUEUE_FULL = -6117,
+};
+
+/* SGEMM batch detail codes (reactor_api.h:282-295). */
+enum {
+  PROM_DETAIL_BATCH_PLAN_INVALID = -6602,
+  PROM_DETAIL_BATCH_EXECUTION_FAILED = -6604,
+  PROM_DETAIL_BATCH_UNSUPPORTED_OPTION = -6613,
+};
+
+/* SGEMM batch flags (reactor_api.h:1449-1451).  Bits 0..7 request a number of
+   concurrent workers (0 = 1, at most 8); bit 8 selects contiguous instead of
+   round-robin assignment of entries to workers.  Every other bit is rejected
+   with PROM_DETAIL_BATCH_UNSUPPORTED_OPTION. */
+enum {
+  PROM_BATCH_FLAG_PARTITION_CONTIGUOUS = 1u << 8,
+};
+
+/* Resident SGEMM benchmark modes and flags (reactor_api.h:1561-1580). */
+enum {
+  PROM_SGEMM_GPU_TIMING_FAILURE_NONE = 0u,
+};
+enum {
+  PROM_SGEMM_RESIDENT_MODE_PRODUCTION_SELECTOR = 0u,
+  PROM_SGEMM_RESIDENT_MODE_EXPLICIT_VARIANT = 1u,
+};
+enum {
+  PROM_SGEMM_RESIDENT_FLAG_VALIDATE_READBACK = 1u << 0,
+  PROM_SGEMM_RESIDENT_FLAG_M29_SUBMISSION_RING = 1u << 1,
 };
 
 /* RMSNorm detail codes (internal/prometheus/native/reactor_vulkan.h:1870-1888). */
@@ -406,6 +435,77 @@ typedef struct PrometheusReductionBenchmarkResult {
   int32_t detail_code;
 } PrometheusReductionBenchmarkResult;
 
+/* One independent product of a batch (reactor_api.h:1307-1314). */
+typedef struct PrometheusSgemmBatchEntry {
+  const float* a;
+  const float* b;
+  float* c;
+  uint32_t m;
+  uint32_t n;
+  uint32_t k;
+} PrometheusSgemmBatchEntry;
+
+/* Resident benchmark request / result (reactor_api.h:2034-2095), same layout. */
+typedef struct PrometheusSgemmResidentBenchmarkRequest {
+  uint32_t struct_size;
+  const float* a;
+  const float* b;
+  float* c;
+  uint32_t m;
+  uint32_t n;
+  uint32_t k;
+  uint32_t mode;
+  uint32_t requested_variant;
+  uint32_t warmup_iterations;
+  uint32_t iterations;
+  uint32_t diagnostic_batch_depth;
+  uint32_t flags;
+} PrometheusSgemmResidentBenchmarkRequest;
+
+typedef struct PrometheusSgemmResidentBenchmarkResult {
+  uint32_t struct_size;
+  uint32_t resident_mode_available;
+  uint32_t resident_mode_used;
+  uint32_t requested_variant;
+  uint32_t production_selected_variant;
+  uint32_t executed_variant;
+  uint32_t executed_compute_mode;
+  uint32_t setup_stage;
+  int32_t setup_detail_code;
+  uint32_t final_stage;
+  int32_t final_detail_code;
+  uint32_t iterations;
+  uint32_t gpu_timestamp_valid;
+  uint32_t gpu_timing_failure_reason;
+  uint64_t setup_wall_ns;
+  uint64_t upload_once_wall_ns;
+  uint64_t total_loop_wall_ns;
+  uint64_t kernel_min_ns;
+  uint64_t kernel_median_ns;
+  uint64_t kernel_p95_ns;
+  uint64_t readback_once_wall_ns;
+  uint64_t validation_wall_ns;
+  uint64_t dispatch_submit_wall_ns_median;
+  uint64_t sync_wait_wall_ns_median;
+  uint32_t diagnostic_batch_depth;
+  uint32_t queue_submissions;
+  uint32_t fence_waits;
+  uint32_t command_buffer_recordings;
+  uint32_t command_buffer_resets;
+  uint32_t descriptor_updates;
+  uint64_t query_result_wall_ns_median;
+  uint32_t configured_ring_depth;
+  uint32_t physical_slot_count;
+  uint32_t max_in_flight_depth;
+  uint64_t ring_poll_count;
+  uint64_t ring_forced_wait_count;
+  uint64_t ring_query_harvest_count;
+  uint64_t ring_full_count;
+  uint64_t ring_slot_recycle_count;
+  uint64_t ring_failure_count;
+  uint32_t ring_final_slot_state[4];
+} PrometheusSgemmResidentBenchmarkResult;
+
 typedef struct PrometheusCaps {
   uint32_t available;
   uint32_t backend_type;
@@ -505,6 +605,31 @@ PROM_REACTOR_API int prometheus_reactor_runtime_sgemm(void* handle, const float*
 
 /* reactor_api.h:2623-2643 -- non-blocking SGEMM.  The library owns the result
    until consume copies it into `c` (length-checked) or abandon drops it. */
+/* SGEMM with an explicit kernel variant (reactor_api.h:2596-2605).  The
+   reference's variant ids name its Vulkan shaders; here they name this
+   library's kernels: 0 = production selector (as prometheus_reactor_runtime_sgemm),
+   else one of OCT_B200_SGEMM_* below.  Any other id: PROM_ERROR, stage INIT,
+   OCT_B200_DETAIL_BAD_VARIANT. */
+PROM_REACTOR_API int prometheus_reactor_runtime_sgemm_benchmark_variant(void* handle, const float* a, const float* b,
+                                                                        float* c, uint32_t m, uint32_t n, uint32_t k,
+                                                                        uint32_t requested_variant,
+                                                                        uint32_t* out_stage, int* out_detail_code);
+/* Resident benchmark (reactor_api.h:2606-2609; reactor_sgemm.cpp:5629-5978):
+   A and B are uploaded once, one setup product runs, then warmup + iterations
+   products run on the resident buffers, each timed with CUDA events (kernel
+   min / median / p95 in ns).  With the M29 ring flag up to
+   diagnostic_batch_depth (1..4, default 2) products stay in flight.  With
+   VALIDATE_READBACK, C is copied to request->c once at the end. */
+PROM_REACTOR_API int prometheus_reactor_runtime_sgemm_resident_benchmark(
+    void* handle, const PrometheusSgemmResidentBenchmarkRequest* request,
+    PrometheusSgemmResidentBenchmarkResult* out_result);
+/* Independent host-buffer products (reactor_api.h:2610-2615; reactor_batch.c:244-520):
+   entries run concurrently on up to 8 CUDA streams, and every C is written,
+   in entry order, only after all entries succeeded (stage TRANSFER_OUT,
+   detail 0); on failure no caller output is touched. */
+PROM_REACTOR_API int prometheus_reactor_runtime_sgemm_batch(void* handle, const PrometheusSgemmBatchEntry* entries,
+                                                            uint32_t entry_count, uint32_t flags,
+                                                            uint32_t* out_stage, int* out_detail_code);
 PROM_REACTOR_API int prometheus_reactor_runtime_sgemm_submit_async(void* handle, const float* a, const float* b,
                                                                    uint32_t m, uint32_t n, uint32_t k,
                                                                    int* out_task_id, uint32_t* out_stage,

@@ -35,6 +35,7 @@ namespace {
 using Clock = std::chrono::steady_clock;
 constexpr uint32_t kMagic = 0x0C7B2000u;
 constexpr int kAsyncSlots = 4;  // task capacity, as the reference (reactor_api.h:2030 tasks[4])
+constexpr uint32_t kBatchWorkers = 8;  // PROM_SGEMM_BATCH_MAX_LOGICAL_WIDTH (reactor_batch.c:56)
 
 uint64_t ns_since(Clock::time_point t0) {
   return static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(Clock::now() - t0).count());
@@ -109,6 +110,10 @@ struct Runtime {
   bool timing = false;
   std::vector<oct::SgemmEvents> timing_events;
   size_t timing_used = 0;
+  // SGEMM batch workers: one stream, split scratch and A/B staging each.
+  cudaStream_t batch_streams[kBatchWorkers] = {};
+  DevBuf batch_scratch[kBatchWorkers], batch_a[kBatchWorkers], batch_b[kBatchWorkers];
+  DevBuf batch_c;  // every entry's C, until the whole batch has succeeded
   // Transformer blocks created on this handle.
   std::unordered_map<uint64_t, oct::Block*> blocks;
   uint64_t next_block = 1;
@@ -173,27 +178,40 @@ const oct::SgemmEvents* next_timing_events(Runtime* rt) {
 
 // ---------------------------------------------------------------- SGEMM core
 // Enqueues C = A * B for device pointers; chooses the kernel.
+bool known_variant(uint32_t v) {
+  return v == OCT_B200_SGEMM_AUTO || v == OCT_B200_SGEMM_TC3XTF32 || v == OCT_B200_SGEMM_FMA ||
+         v == OCT_B200_SGEMM_TC_BK16 || v == OCT_B200_SGEMM_TC_BK32 || v == OCT_B200_SGEMM_TC_PAIR16 ||
+         v == OCT_B200_SGEMM_TC_PAIR32;
+}
+
+// The kernel a variant id runs for (m, n, k): AUTO picks the FMA control for
+// tiny products (they do not fill one 128x256 tensor-core tile usefully, and the
+// control is exact-tail by construction), else the 3xTF32 tensor-core kernel.
+uint32_t resolve_variant(uint32_t variant, uint32_t m, uint32_t n, uint32_t k) {
+  if (variant != OCT_B200_SGEMM_AUTO) return variant;
+  const double work = static_cast<double>(m) * n * k;
+  return (work < 4.0e6 || m < 16) ? OCT_B200_SGEMM_FMA : OCT_B200_SGEMM_TC3XTF32;
+}
+
+// `scratch` (default: the handle's) holds the TF32 split operands; calls that
+// run concurrently on different streams need different scratch buffers.
 int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
                   uint32_t m, uint32_t n, uint32_t k, uint32_t variant, cudaStream_t stream,
-                  const oct::GemmBatch* batch = nullptr) {
-  if (variant == OCT_B200_SGEMM_AUTO) {
-    // Tiny products do not fill one 128x256 tensor-core tile usefully; the
-    // FMA control is exact-tail by construction and cheaper there.
-    const double work = static_cast<double>(m) * n * k;
-    variant = (work < 4.0e6 || m < 16) ? OCT_B200_SGEMM_FMA : OCT_B200_SGEMM_TC3XTF32;
-  }
+                  const oct::GemmBatch* batch = nullptr, DevBuf* scratch = nullptr) {
+  variant = resolve_variant(variant, m, n, k);
+  if (scratch == nullptr) scratch = &rt->scratch;
   cudaError_t e;
   if (variant == OCT_B200_SGEMM_FMA) {
     e = oct::sgemm_fma(a, lda, b, ldb, c, ldc, m, n, k, stream, batch);
   } else if (variant == OCT_B200_SGEMM_TC3XTF32 || variant == 16u || variant == 32u || variant == 216u ||
              variant == 232u) {
     const uint64_t need = oct::sgemm_tc_scratch_bytes(m, n, k, batch != nullptr ? batch->count : 1u);
-    e = rt->scratch.ensure(need, stream);
+    e = scratch->ensure(need, stream);
     if (e != cudaSuccess) return OCT_B200_DETAIL_OUT_OF_MEMORY;
     const int bk = variant == OCT_B200_SGEMM_TC3XTF32 ? oct::kTcSingle16 : static_cast<int>(variant);
     const oct::SgemmEvents* ev = nullptr;
     if (rt->timing && (ev = next_timing_events(rt)) == nullptr) return OCT_B200_DETAIL_CUDA_ERROR;
-    e = oct::sgemm_tc(a, lda, b, ldb, c, ldc, m, n, k, rt->scratch.aligned(), rt->err_word(), bk, stream, ev, batch);
+    e = oct::sgemm_tc(a, lda, b, ldb, c, ldc, m, n, k, scratch->aligned(), rt->err_word(), bk, stream, ev, batch);
   } else {
     return OCT_B200_DETAIL_BAD_VARIANT;
   }
@@ -263,8 +281,18 @@ void destroy_runtime(Runtime* rt) {
     t.b.release();
     t.c.release();
   }
-  for (DevBuf* b : {&rt->scratch, &rt->da, &rt->db, &rt->dc, &rt->rin, &rt->rout, &rt->rw, &rt->rinv, &rt->words})
+  for (DevBuf* b : {&rt->scratch, &rt->da, &rt->db, &rt->dc, &rt->rin, &rt->rout, &rt->rw, &rt->rinv, &rt->words,
+                    &rt->batch_c})
     b->release();
+  for (uint32_t w = 0; w < kBatchWorkers; ++w) {
+    if (rt->batch_streams[w] != nullptr) {
+      cudaStreamSynchronize(rt->batch_streams[w]);
+      cudaStreamDestroy(rt->batch_streams[w]);
+    }
+    rt->batch_scratch[w].release();
+    rt->batch_a[w].release();
+    rt->batch_b[w].release();
+  }
   if (rt->ev0 != nullptr) cudaEventDestroy(rt->ev0);
   if (rt->ev1 != nullptr) cudaEventDestroy(rt->ev1);
   if (rt->stream != nullptr) cudaStreamDestroy(rt->stream);
@@ -700,8 +728,11 @@ int prometheus_runtime_probe(void* handle, PrometheusCaps* out_caps) {
 }
 
 // Validation order and codes follow reactor_sgemm.cpp:4149-4176.
-int prometheus_reactor_runtime_sgemm(void* handle, const float* a, const float* b, float* c, uint32_t m, uint32_t n,
-                                     uint32_t k, uint32_t* out_stage, int* out_detail_code) {
+namespace {
+// The host-buffer SGEMM behind prometheus_reactor_runtime_sgemm and
+// ..._sgemm_benchmark_variant (`requested` = an OCT_B200_SGEMM_* id).
+int sgemm_host(void* handle, const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k,
+               uint32_t requested, uint32_t* out_stage, int* out_detail_code) {
   try {
     set_status(out_stage, out_detail_code, PROM_STAGE_NONE, 0);
     Runtime* rt = lookup(handle);
@@ -715,6 +746,10 @@ int prometheus_reactor_runtime_sgemm(void* handle, const float* a, const float* 
     }
     if (m == 0 || n == 0 || k == 0) {
       set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_ERROR);
+      return PROM_ERROR;
+    }
+    if (!known_variant(requested)) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, OCT_B200_DETAIL_BAD_VARIANT);
       return PROM_ERROR;
     }
     if (!rt->available) {
@@ -753,8 +788,7 @@ int prometheus_reactor_runtime_sgemm(void* handle, const float* a, const float* 
       set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_DETAIL_INJECTED_DISPATCH_FAILURE);
       return PROM_ERROR;
     }
-    const uint32_t variant =
-        (rt->test_flags & PROM_TESTCFG_FORCE_STRICT_FP32) ? OCT_B200_SGEMM_FMA : OCT_B200_SGEMM_AUTO;
+    const uint32_t variant = (rt->test_flags & PROM_TESTCFG_FORCE_STRICT_FP32) ? OCT_B200_SGEMM_FMA : requested;
     const int d = enqueue_sgemm(rt, da, k, db, n, dc, n, m, n, k, variant, rt->stream);
     if (d != 0) {
       cudaStreamSynchronize(rt->stream);
@@ -783,6 +817,408 @@ int prometheus_reactor_runtime_sgemm(void* handle, const float* a, const float* 
       return PROM_ERROR;
     }
     set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, PROM_DETAIL_PATH_DIRECT);
+    return PROM_OK;
+  } catch (...) {
+    set_status(out_stage, out_detail_code, PROM_STAGE_INIT, OCT_B200_DETAIL_CUDA_ERROR);
+    return PROM_INTERNAL_ERROR;
+  }
+}
+}  // namespace
+
+int prometheus_reactor_runtime_sgemm(void* handle, const float* a, const float* b, float* c, uint32_t m, uint32_t n,
+                                     uint32_t k, uint32_t* out_stage, int* out_detail_code) {
+  return sgemm_host(handle, a, b, c, m, n, k, OCT_B200_SGEMM_AUTO, out_stage, out_detail_code);
+}
+
+int prometheus_reactor_runtime_sgemm_benchmark_variant(void* handle, const float* a, const float* b, float* c,
+                                                       uint32_t m, uint32_t n, uint32_t k, uint32_t requested_variant,
+                                                       uint32_t* out_stage, int* out_detail_code) {
+  return sgemm_host(handle, a, b, c, m, n, k, requested_variant, out_stage, out_detail_code);
+}
+
+namespace {
+uint64_t wall_ns() {
+  return static_cast<uint64_t>(
+      std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now().time_since_epoch())
+          .count());
+}
+
+// Nearest-rank percentile with the index rounded up (reactor_sgemm.cpp:5357-5367).
+uint64_t percentile_ns(std::vector<uint64_t> v, uint32_t num, uint32_t den) {
+  if (v.empty() || den == 0) return 0;
+  std::sort(v.begin(), v.end());
+  const uint64_t scaled = (static_cast<uint64_t>(v.size() - 1) * num + (den - 1)) / den;
+  return v[std::min<uint64_t>(scaled, v.size() - 1)];
+}
+
+// CUDA events bracketing one resident product (or one group of them).
+struct EventPair {
+  cudaEvent_t begin = nullptr, end = nullptr;
+  bool make() { return cudaEventCreate(&begin) == cudaSuccess && cudaEventCreate(&end) == cudaSuccess; }
+  void destroy() {
+    if (begin != nullptr) cudaEventDestroy(begin);
+    if (end != nullptr) cudaEventDestroy(end);
+    begin = end = nullptr;
+  }
+  uint64_t elapsed_ns() const {
+    float ms = 0.f;
+    return cudaEventElapsedTime(&ms, begin, end) == cudaSuccess ? static_cast<uint64_t>(ms * 1.0e6) : 0;
+  }
+};
+}  // namespace
+
+// Resident benchmark (reactor_sgemm.cpp:5629-5978): validation order and result
+// fields follow the reference; the reference's Vulkan command-buffer counters
+// count CUDA enqueues and stream waits here.
+int prometheus_reactor_runtime_sgemm_resident_benchmark(void* handle,
+                                                        const PrometheusSgemmResidentBenchmarkRequest* request,
+                                                        PrometheusSgemmResidentBenchmarkResult* out) {
+  if (out == nullptr) return PROM_ERROR;
+  std::memset(out, 0, sizeof(*out));
+  out->struct_size = static_cast<uint32_t>(sizeof(*out));
+  std::vector<EventPair> evs;
+  auto cleanup = [&]() {
+    for (auto& e : evs) e.destroy();
+  };
+  try {
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) {
+      out->setup_stage = PROM_STAGE_INIT;
+      out->setup_detail_code = PROM_INVALID_HANDLE;
+      return PROM_INVALID_HANDLE;
+    }
+    out->resident_mode_available = rt->available ? 1u : 0u;
+    const PrometheusSgemmResidentBenchmarkRequest* r = request;
+    if (r == nullptr || r->a == nullptr || r->b == nullptr || r->m == 0 || r->n == 0 || r->k == 0 ||
+        ((r->flags & PROM_SGEMM_RESIDENT_FLAG_VALIDATE_READBACK) != 0 && r->c == nullptr)) {
+      out->setup_stage = PROM_STAGE_TRANSFER_IN;
+      out->setup_detail_code = PROM_ERROR;
+      return PROM_ERROR;
+    }
+    if (!rt->available) {
+      out->setup_stage = PROM_STAGE_INIT;
+      out->setup_detail_code = PROM_DETAIL_CAPABILITY_MISMATCH;
+      return PROM_ERROR;
+    }
+    const uint32_t m = r->m, n = r->n, k = r->k;
+    uint64_t a_n, b_n, c_n;
+    if (!checked_mul(m, k, &a_n) || !checked_mul(k, n, &b_n) || !checked_mul(m, n, &c_n) ||
+        a_n > (UINT64_MAX / 8) || b_n > (UINT64_MAX / 8) || c_n > (UINT64_MAX / 8)) {
+      out->setup_stage = PROM_STAGE_TRANSFER_IN;
+      out->setup_detail_code = PROM_DETAIL_SIZE_OVERFLOW;
+      return PROM_ERROR;
+    }
+    const bool explicit_variant = r->mode == PROM_SGEMM_RESIDENT_MODE_EXPLICIT_VARIANT;
+    const uint32_t requested = explicit_variant ? r->requested_variant : OCT_B200_SGEMM_AUTO;
+    if (!known_variant(requested)) {
+      out->setup_stage = PROM_STAGE_INIT;
+      out->setup_detail_code = OCT_B200_DETAIL_BAD_VARIANT;
+      return PROM_ERROR;
+    }
+    const uint32_t iterations = r->iterations == 0 ? 1u : r->iterations;
+    const uint32_t warmup = r->warmup_iterations;
+    const uint32_t depth = r->diagnostic_batch_depth == 0 ? 1u : r->diagnostic_batch_depth;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    cudaStream_t st = rt->stream;
+
+    // ---- setup: upload once, one product
+    const uint64_t t_setup0 = wall_ns();
+    if (rt->da.ensure(a_n * 4, st) != cudaSuccess || rt->db.ensure(b_n * 4, st) != cudaSuccess ||
+        rt->dc.ensure(c_n * 4, st) != cudaSuccess) {
+      out->setup_stage = PROM_STAGE_TRANSFER_IN;
+      out->setup_detail_code = OCT_B200_DETAIL_OUT_OF_MEMORY;
+      return PROM_ERROR;
+    }
+    float* da = static_cast<float*>(rt->da.aligned());
+    float* db = static_cast<float*>(rt->db.aligned());
+    float* dc = static_cast<float*>(rt->dc.aligned());
+    const uint64_t t_up0 = wall_ns();
+    cudaError_t e = reset_words(rt);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(da, r->a, a_n * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(db, r->b, b_n * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    out->upload_once_wall_ns = wall_ns() - t_up0;
+    if (e != cudaSuccess) {
+      out->setup_stage = PROM_STAGE_TRANSFER_IN;
+      out->setup_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
+      return PROM_ERROR;
+    }
+    int d = enqueue_sgemm(rt, da, k, db, n, dc, n, m, n, k, requested, st);
+    Words w;
+    if (d == 0 && (read_words(rt, &w) != cudaSuccess || w.err != 0)) d = OCT_B200_DETAIL_DEVICE_TIMEOUT;
+    out->setup_wall_ns = wall_ns() - t_setup0;
+    if (d != 0) {
+      out->setup_stage = PROM_STAGE_SUBMIT;
+      out->setup_detail_code = d;
+      return PROM_ERROR;
+    }
+    out->setup_stage = PROM_STAGE_TRANSFER_OUT;
+    out->setup_detail_code = PROM_DETAIL_PATH_DIRECT;
+    out->resident_mode_used = 1u;
+    out->requested_variant = explicit_variant ? r->requested_variant : 0u;
+    out->production_selected_variant = resolve_variant(OCT_B200_SGEMM_AUTO, m, n, k);
+    out->executed_variant = resolve_variant(requested, m, n, k);
+    out->executed_compute_mode = out->executed_variant == OCT_B200_SGEMM_FMA ? 2u : 1u;
+
+    auto fail_final = [&](uint32_t stage, int detail) {
+      cudaStreamSynchronize(st);
+      cleanup();
+      out->final_stage = stage;
+      out->final_detail_code = detail;
+      return PROM_ERROR;
+    };
+    auto product = [&]() { return enqueue_sgemm(rt, da, k, db, n, dc, n, m, n, k, requested, st); };
+    std::vector<uint64_t> kernel, submit, wait, query;
+
+    if ((r->flags & PROM_SGEMM_RESIDENT_FLAG_M29_SUBMISSION_RING) != 0) {
+      // ---- ring: up to `ring` products in flight, each bracketed by its own events
+      const uint32_t ring = r->diagnostic_batch_depth == 0 ? 2u : r->diagnostic_batch_depth;
+      if (ring < 1 || ring > 4) return fail_final(PROM_STAGE_SUBMIT, PROM_ERROR);
+      evs.resize(ring);
+      for (auto& ev : evs)
+        if (!ev.make()) return fail_final(PROM_STAGE_SUBMIT, OCT_B200_DETAIL_CUDA_ERROR);
+      uint32_t slot_busy[4] = {0, 0, 0, 0};
+      auto run_ring = [&](uint32_t count, bool record) -> int {
+        uint32_t outstanding = 0, next_slot = 0;
+        for (uint32_t i = 0; i < count; ++i) {
+          const uint32_t sl = next_slot;
+          next_slot = (next_slot + 1) % ring;
+          if (slot_busy[sl]) {  // the ring is full: harvest the oldest slot first
+            out->ring_full_count += 1;
+            out->ring_poll_count += 1;
+            if (cudaEventQuery(evs[sl].end) == cudaErrorNotReady) {
+              out->ring_forced_wait_count += 1;
+              if (cudaEventSynchronize(evs[sl].end) != cudaSuccess) return OCT_B200_DETAIL_CUDA_ERROR;
+            }
+            if (record) kernel.push_back(evs[sl].elapsed_ns());
+            out->ring_query_harvest_count += 1;
+            out->ring_slot_recycle_count += 1;
+            slot_busy[sl] = 0;
+            outstanding -= 1;
+          }
+          if (cudaEventRecord(evs[sl].begin, st) != cudaSuccess) return OCT_B200_DETAIL_CUDA_ERROR;
+          const int pd = product();
+          if (pd != 0) return pd;
+          if (cudaEventRecord(evs[sl].end, st) != cudaSuccess) return OCT_B200_DETAIL_CUDA_ERROR;
+          slot_busy[sl] = 1;
+          outstanding += 1;
+          out->max_in_flight_depth = std::max(out->max_in_flight_depth, outstanding);
+        }
+        for (uint32_t i = 0; i < ring; ++i) {  // drain in submission order
+          const uint32_t sl = (next_slot + i) % ring;
+          if (!slot_busy[sl]) continue;
+          out->ring_poll_count += 1;
+          if (cudaEventSynchronize(evs[sl].end) != cudaSuccess) return OCT_B200_DETAIL_CUDA_ERROR;
+          if (record) kernel.push_back(evs[sl].elapsed_ns());
+          out->ring_query_harvest_count += 1;
+          slot_busy[sl] = 0;
+        }
+        return 0;
+      };
+      if (warmup != 0 && (d = run_ring(warmup, false)) != 0) return fail_final(PROM_STAGE_SUBMIT, d);
+      const uint64_t t0 = wall_ns();
+      d = run_ring(iterations, true);
+      const uint64_t t1 = wall_ns();
+      if (d != 0) return fail_final(PROM_STAGE_SUBMIT, d);
+      out->iterations = iterations;
+      out->total_loop_wall_ns = t1 - t0;
+      out->diagnostic_batch_depth = ring;
+      out->queue_submissions = iterations;
+      out->fence_waits = static_cast<uint32_t>(out->ring_forced_wait_count);
+      out->command_buffer_recordings = iterations;
+      out->command_buffer_resets = iterations;
+      out->descriptor_updates = iterations;
+      out->configured_ring_depth = ring;
+      out->physical_slot_count = 4;
+      for (uint32_t i = 0; i < 4; ++i) out->ring_final_slot_state[i] = slot_busy[i];
+    } else {
+      // ---- serial: each iteration enqueues `depth` products and waits once
+      evs.resize(1);
+      if (!evs[0].make()) return fail_final(PROM_STAGE_SUBMIT, OCT_B200_DETAIL_CUDA_ERROR);
+      for (uint32_t i = 0; i < warmup; ++i) {
+        for (uint32_t j = 0; j < depth; ++j)
+          if ((d = product()) != 0) return fail_final(PROM_STAGE_SUBMIT, d);
+        if (cudaStreamSynchronize(st) != cudaSuccess) return fail_final(PROM_STAGE_SUBMIT, OCT_B200_DETAIL_CUDA_ERROR);
+      }
+      const uint64_t t0 = wall_ns();
+      for (uint32_t i = 0; i < iterations; ++i) {
+        const uint64_t s0 = wall_ns();
+        if (cudaEventRecord(evs[0].begin, st) != cudaSuccess)
+          return fail_final(PROM_STAGE_SUBMIT, OCT_B200_DETAIL_CUDA_ERROR);
+        for (uint32_t j = 0; j < depth; ++j)
+          if ((d = product()) != 0) return fail_final(PROM_STAGE_SUBMIT, d);
+        if (cudaEventRecord(evs[0].end, st) != cudaSuccess)
+          return fail_final(PROM_STAGE_SUBMIT, OCT_B200_DETAIL_CUDA_ERROR);
+        const uint64_t s1 = wall_ns();
+        if (cudaEventSynchronize(evs[0].end) != cudaSuccess)
+          return fail_final(PROM_STAGE_SUBMIT, OCT_B200_DETAIL_CUDA_ERROR);
+        const uint64_t s2 = wall_ns();
+        kernel.push_back(evs[0].elapsed_ns());
+        const uint64_t s3 = wall_ns();
+        submit.push_back(s1 - s0);
+        wait.push_back(s2 - s1);
+        query.push_back(s3 - s2);
+      }
+      const uint64_t t1 = wall_ns();
+      out->iterations = iterations * depth;
+      out->total_loop_wall_ns = t1 - t0;
+      out->dispatch_submit_wall_ns_median = percentile_ns(submit, 50, 100);
+      out->sync_wait_wall_ns_median = percentile_ns(wait, 50, 100);
+      out->query_result_wall_ns_median = percentile_ns(query, 50, 100);
+      out->diagnostic_batch_depth = depth;
+      out->queue_submissions = iterations;
+      out->fence_waits = iterations;
+      out->command_buffer_recordings = iterations;
+      out->command_buffer_resets = iterations;
+      out->descriptor_updates = iterations;
+    }
+    if (read_words(rt, &w) != cudaSuccess || w.err != 0) return fail_final(PROM_STAGE_SUBMIT, OCT_B200_DETAIL_DEVICE_TIMEOUT);
+    out->gpu_timestamp_valid = 1u;
+    for (uint64_t x : kernel)
+      if (x == 0) out->gpu_timestamp_valid = 0u;
+    if (kernel.empty()) out->gpu_timestamp_valid = 0u;
+    if (out->gpu_timestamp_valid) {
+      out->kernel_min_ns = percentile_ns(kernel, 0, 100);
+      out->kernel_median_ns = percentile_ns(kernel, 50, 100);
+      out->kernel_p95_ns = percentile_ns(kernel, 95, 100);
+      out->gpu_timing_failure_reason = PROM_SGEMM_GPU_TIMING_FAILURE_NONE;
+    }
+    if ((r->flags & PROM_SGEMM_RESIDENT_FLAG_VALIDATE_READBACK) != 0) {
+      const uint64_t t0 = wall_ns();
+      e = cudaMemcpyAsync(r->c, dc, c_n * 4, cudaMemcpyDeviceToHost, st);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+      out->readback_once_wall_ns = wall_ns() - t0;
+      out->validation_wall_ns = out->readback_once_wall_ns;
+      if (e != cudaSuccess) return fail_final(PROM_STAGE_TRANSFER_OUT, OCT_B200_DETAIL_CUDA_ERROR);
+    }
+    cleanup();
+    out->final_stage = PROM_STAGE_SUBMIT;
+    out->final_detail_code = PROM_DETAIL_PATH_STAGED_UPLOAD_TILED;
+    return PROM_OK;
+  } catch (...) {
+    cleanup();
+    out->final_stage = PROM_STAGE_CLEANUP;
+    out->final_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
+// Batch (reactor_sgemm.cpp:5984-6009; reactor_batch.c:89-180, 244-520): the
+// flag mask, plan validation (u32 element counts, as the reference's plan) and
+// ordered commit follow the reference; the execution is one CUDA stream per
+// worker with its own staging and split scratch.
+int prometheus_reactor_runtime_sgemm_batch(void* handle, const PrometheusSgemmBatchEntry* entries,
+                                           uint32_t entry_count, uint32_t flags, uint32_t* out_stage,
+                                           int* out_detail_code) {
+  try {
+    set_status(out_stage, out_detail_code, PROM_STAGE_NONE, 0);
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_INVALID_HANDLE);
+      return PROM_INVALID_HANDLE;
+    }
+    if ((flags & ~(0xFFu | PROM_BATCH_FLAG_PARTITION_CONTIGUOUS)) != 0) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_DETAIL_BATCH_UNSUPPORTED_OPTION);
+      return PROM_ERROR;
+    }
+    if (!rt->available) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_DETAIL_BATCH_EXECUTION_FAILED);
+      return PROM_ERROR;
+    }
+    if (entries == nullptr || entry_count == 0) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_ERROR);
+      return PROM_ERROR;
+    }
+    auto fits_u32 = [](uint32_t x, uint32_t y) { return static_cast<uint64_t>(x) * y <= 0xFFFFFFFFull; };
+    for (uint32_t i = 0; i < entry_count; ++i) {
+      const PrometheusSgemmBatchEntry& en = entries[i];
+      if (en.a == nullptr || en.b == nullptr || en.c == nullptr || en.m == 0 || en.n == 0 || en.k == 0 ||
+          !fits_u32(en.m, en.k) || !fits_u32(en.k, en.n) || !fits_u32(en.m, en.n)) {
+        set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_DETAIL_BATCH_PLAN_INVALID);
+        return PROM_ERROR;
+      }
+    }
+    uint32_t workers = (flags & 0xFFu) == 0 ? 1u : (flags & 0xFFu);
+    workers = std::min(workers, std::min(kBatchWorkers, entry_count));
+    const bool contiguous = (flags & PROM_BATCH_FLAG_PARTITION_CONTIGUOUS) != 0;
+    std::lock_guard<std::mutex> lock(rt->mu);
+    // every entry's C stays on the device until all entries have succeeded
+    std::vector<uint64_t> c_off(entry_count);
+    uint64_t c_total = 0;
+    for (uint32_t i = 0; i < entry_count; ++i) {
+      c_off[i] = c_total;
+      c_total += (static_cast<uint64_t>(entries[i].m) * entries[i].n * 4 + 255) & ~uint64_t(255);
+    }
+    set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_IN, 0);
+    if (rt->batch_c.ensure(c_total, rt->stream) != cudaSuccess) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_IN, OCT_B200_DETAIL_OUT_OF_MEMORY);
+      return PROM_ERROR;
+    }
+    for (uint32_t w = 0; w < workers; ++w)
+      if (rt->batch_streams[w] == nullptr &&
+          cudaStreamCreateWithFlags(&rt->batch_streams[w], cudaStreamNonBlocking) != cudaSuccess) {
+        rt->batch_streams[w] = nullptr;
+        set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_DETAIL_BATCH_EXECUTION_FAILED);
+        return PROM_ERROR;
+      }
+    if (reset_words(rt) != cudaSuccess || cudaStreamSynchronize(rt->stream) != cudaSuccess) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, PROM_DETAIL_BATCH_EXECUTION_FAILED);
+      return PROM_ERROR;
+    }
+    char* cbase = static_cast<char*>(rt->batch_c.aligned());
+    uint32_t fail_stage = PROM_STAGE_NONE;
+    int fail_detail = 0;
+    for (uint32_t i = 0; i < entry_count && fail_stage == PROM_STAGE_NONE; ++i) {
+      const PrometheusSgemmBatchEntry& en = entries[i];
+      const uint32_t w = contiguous ? static_cast<uint32_t>(static_cast<uint64_t>(i) * workers / entry_count)
+                                    : i % workers;
+      cudaStream_t s = rt->batch_streams[w];
+      const uint64_t a_n = static_cast<uint64_t>(en.m) * en.k, b_n = static_cast<uint64_t>(en.k) * en.n;
+      // a worker's staging is reused by its next entry only after this one's product (same stream)
+      if (rt->batch_a[w].ensure(a_n * 4, s) != cudaSuccess || rt->batch_b[w].ensure(b_n * 4, s) != cudaSuccess) {
+        fail_stage = PROM_STAGE_TRANSFER_IN;
+        fail_detail = OCT_B200_DETAIL_OUT_OF_MEMORY;
+        break;
+      }
+      float* da = static_cast<float*>(rt->batch_a[w].aligned());
+      float* db = static_cast<float*>(rt->batch_b[w].aligned());
+      float* dc = reinterpret_cast<float*>(cbase + c_off[i]);
+      if (cudaMemcpyAsync(da, en.a, a_n * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+          cudaMemcpyAsync(db, en.b, b_n * 4, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        fail_stage = PROM_STAGE_TRANSFER_IN;
+        fail_detail = OCT_B200_DETAIL_CUDA_ERROR;
+        break;
+      }
+      const int d = enqueue_sgemm(rt, da, en.k, db, en.n, dc, en.n, en.m, en.n, en.k, OCT_B200_SGEMM_AUTO, s, nullptr,
+                                  &rt->batch_scratch[w]);
+      if (d != 0) {
+        fail_stage = PROM_STAGE_SUBMIT;
+        fail_detail = d == OCT_B200_DETAIL_OUT_OF_MEMORY ? d : PROM_DETAIL_BATCH_EXECUTION_FAILED;
+      }
+    }
+    for (uint32_t w = 0; w < workers; ++w)  // drain every worker, failed or not
+      if (cudaStreamSynchronize(rt->batch_streams[w]) != cudaSuccess && fail_stage == PROM_STAGE_NONE) {
+        fail_stage = PROM_STAGE_SUBMIT;
+        fail_detail = PROM_DETAIL_BATCH_EXECUTION_FAILED;
+      }
+    Words wd;
+    if (fail_stage == PROM_STAGE_NONE && (read_words(rt, &wd) != cudaSuccess || wd.err != 0)) {
+      fail_stage = PROM_STAGE_SUBMIT;
+      fail_detail = OCT_B200_DETAIL_DEVICE_TIMEOUT;
+    }
+    if (fail_stage != PROM_STAGE_NONE) {
+      set_status(out_stage, out_detail_code, fail_stage, fail_detail == 0 ? PROM_ERROR : fail_detail);
+      return PROM_ERROR;
+    }
+    // ordered commit: every output, in entry order, only now
+    for (uint32_t i = 0; i < entry_count; ++i) {
+      const uint64_t c_n = static_cast<uint64_t>(entries[i].m) * entries[i].n;
+      if (cudaMemcpy(entries[i].c, cbase + c_off[i], c_n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, OCT_B200_DETAIL_CUDA_ERROR);
+        return PROM_ERROR;
+      }
+    }
+    set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, 0);
     return PROM_OK;
   } catch (...) {
     set_status(out_stage, out_detail_code, PROM_STAGE_INIT, OCT_B200_DETAIL_CUDA_ERROR);

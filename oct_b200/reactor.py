@@ -37,6 +37,12 @@ TESTCFG_FAIL_DISPATCH = 1 << 4
 TESTCFG_FAIL_DOWNLOAD = 1 << 5
 TESTCFG_FAIL_ASYNC_POLL = 1 << 15
 TESTCFG_FORCE_STRICT_FP32 = 1 << 17
+RESIDENT_MODE_PRODUCTION_SELECTOR, RESIDENT_MODE_EXPLICIT_VARIANT = 0, 1
+RESIDENT_FLAG_VALIDATE_READBACK, RESIDENT_FLAG_M29_SUBMISSION_RING = 1 << 0, 1 << 1
+BATCH_FLAG_PARTITION_CONTIGUOUS = 1 << 8
+DETAIL_BATCH_PLAN_INVALID, DETAIL_BATCH_EXECUTION_FAILED, DETAIL_BATCH_UNSUPPORTED_OPTION = -6602, -6604, -6613
+DETAIL_PATH_STAGED_UPLOAD_TILED = 6106
+DETAIL_BAD_VARIANT = -7004
 REDUCTION_TESTCFG_FAIL_COMMAND_RECORD = 1 << 0
 REDUCTION_TESTCFG_FAIL_QUEUE_SUBMIT = 1 << 1
 REDUCTION_TESTCFG_FAIL_COMPLETION_OBSERVATION = 1 << 2
@@ -78,6 +84,42 @@ class PrometheusReactorConfig(C.Structure):
         ("reduction_ring_depth", C.c_uint32),
         ("shader_package_root", C.c_char_p),
     ]
+
+
+class PrometheusSgemmBatchEntry(C.Structure):
+    """reactor_api.h:1307-1314."""
+    _fields_ = [("a", C.c_void_p), ("b", C.c_void_p), ("c", C.c_void_p), ("m", C.c_uint32), ("n", C.c_uint32),
+                ("k", C.c_uint32)]
+
+
+class PrometheusSgemmResidentBenchmarkRequest(C.Structure):
+    """reactor_api.h:2034-2050."""
+    _fields_ = [("struct_size", C.c_uint32), ("a", C.c_void_p), ("b", C.c_void_p), ("c", C.c_void_p),
+                ("m", C.c_uint32), ("n", C.c_uint32), ("k", C.c_uint32), ("mode", C.c_uint32),
+                ("requested_variant", C.c_uint32), ("warmup_iterations", C.c_uint32), ("iterations", C.c_uint32),
+                ("diagnostic_batch_depth", C.c_uint32), ("flags", C.c_uint32)]
+
+
+class PrometheusSgemmResidentBenchmarkResult(C.Structure):
+    """reactor_api.h:2052-2095."""
+    _fields_ = [(name, C.c_uint32) for name in (
+        "struct_size", "resident_mode_available", "resident_mode_used", "requested_variant",
+        "production_selected_variant", "executed_variant", "executed_compute_mode", "setup_stage")] + [
+        ("setup_detail_code", C.c_int32), ("final_stage", C.c_uint32), ("final_detail_code", C.c_int32),
+        ("iterations", C.c_uint32), ("gpu_timestamp_valid", C.c_uint32), ("gpu_timing_failure_reason", C.c_uint32)] + [
+        (name, C.c_uint64) for name in (
+            "setup_wall_ns", "upload_once_wall_ns", "total_loop_wall_ns", "kernel_min_ns", "kernel_median_ns",
+            "kernel_p95_ns", "readback_once_wall_ns", "validation_wall_ns", "dispatch_submit_wall_ns_median",
+            "sync_wait_wall_ns_median")] + [
+        (name, C.c_uint32) for name in (
+            "diagnostic_batch_depth", "queue_submissions", "fence_waits", "command_buffer_recordings",
+            "command_buffer_resets", "descriptor_updates")] + [
+        ("query_result_wall_ns_median", C.c_uint64), ("configured_ring_depth", C.c_uint32),
+        ("physical_slot_count", C.c_uint32), ("max_in_flight_depth", C.c_uint32)] + [
+        (name, C.c_uint64) for name in (
+            "ring_poll_count", "ring_forced_wait_count", "ring_query_harvest_count", "ring_full_count",
+            "ring_slot_recycle_count", "ring_failure_count")] + [
+        ("ring_final_slot_state", C.c_uint32 * 4)]
 
 
 class PrometheusAsyncStatus(C.Structure):
@@ -272,6 +314,13 @@ SIGNATURES = {
     "prometheus_reactor_runtime_destroy": (C.c_int, [_vp]),
     "prometheus_reactor_runtime_probe": (C.c_int, [_vp, C.POINTER(PrometheusCaps)]),
     "prometheus_reactor_runtime_sgemm": (C.c_int, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32p, _i32p]),
+    "prometheus_reactor_runtime_sgemm_benchmark_variant": (
+        C.c_int, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32p, _i32p]),
+    "prometheus_reactor_runtime_sgemm_resident_benchmark": (
+        C.c_int, [_vp, C.POINTER(PrometheusSgemmResidentBenchmarkRequest),
+                  C.POINTER(PrometheusSgemmResidentBenchmarkResult)]),
+    "prometheus_reactor_runtime_sgemm_batch": (
+        C.c_int, [_vp, C.POINTER(PrometheusSgemmBatchEntry), _u32, _u32, _u32p, _i32p]),
     "prometheus_reactor_runtime_sgemm_submit_async": (
         C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _i32p, _u32p, _i32p]),
     "prometheus_reactor_runtime_sgemm_query_async": (C.c_int, [_vp, C.c_int, C.POINTER(PrometheusAsyncStatus)]),
@@ -476,6 +525,54 @@ class Runtime:
             raise ReactorIssue(ReactorIssue.SGEMM_FAILED, f"stage={st.stage} detail={st.detail}", stage=st.stage,
                                detail=st.detail)
         return c
+
+    # -- explicit variant, resident benchmark, batch (reactor_api.h:2596-2615)
+    def sgemm_variant(self, m: int, n: int, k: int, a: np.ndarray, b: np.ndarray,
+                      variant: int) -> tuple[Optional[np.ndarray], CallStatus]:
+        _f32(a, "a")
+        _f32(b, "b")
+        c = np.empty(m * n, dtype=np.float32)
+        stage, detail = C.c_uint32(), C.c_int()
+        rc = self.lib.prometheus_reactor_runtime_sgemm_benchmark_variant(
+            self.handle, _ptr(a), _ptr(b), _ptr(c), m, n, k, variant, C.byref(stage), C.byref(detail))
+        st = CallStatus(rc, stage.value, detail.value)
+        return (c if rc == PROM_OK else None), st
+
+    def resident_benchmark(self, m: int, n: int, k: int, a: np.ndarray, b: np.ndarray, *, iterations: int = 5,
+                           warmup: int = 1, variant: Optional[int] = None, depth: int = 0, ring: bool = False,
+                           readback: bool = True) -> tuple[int, PrometheusSgemmResidentBenchmarkResult,
+                                                          Optional[np.ndarray]]:
+        _f32(a, "a")
+        _f32(b, "b")
+        c = np.empty(m * n, dtype=np.float32) if readback else None
+        req = PrometheusSgemmResidentBenchmarkRequest()
+        req.struct_size = C.sizeof(req)
+        req.a, req.b, req.c = _ptr(a), _ptr(b), (_ptr(c) if c is not None else None)
+        req.m, req.n, req.k = m, n, k
+        req.mode = RESIDENT_MODE_EXPLICIT_VARIANT if variant is not None else RESIDENT_MODE_PRODUCTION_SELECTOR
+        req.requested_variant = variant or 0
+        req.warmup_iterations, req.iterations, req.diagnostic_batch_depth = warmup, iterations, depth
+        req.flags = (RESIDENT_FLAG_VALIDATE_READBACK if readback else 0) | (RESIDENT_FLAG_M29_SUBMISSION_RING if ring
+                                                                            else 0)
+        res = PrometheusSgemmResidentBenchmarkResult()
+        rc = self.lib.prometheus_reactor_runtime_sgemm_resident_benchmark(self.handle, C.byref(req), C.byref(res))
+        return rc, res, c
+
+    def sgemm_batch(self, problems: list, flags: int = 0) -> tuple[Optional[list], CallStatus]:
+        """problems: [(m, n, k, a, b), ...]; returns the C of every entry, or None on failure."""
+        entries = (PrometheusSgemmBatchEntry * len(problems))()
+        outs = []
+        for e, (m, n, k, a, b) in zip(entries, problems):
+            _f32(a, "a")
+            _f32(b, "b")
+            c = np.full(m * n, np.nan, dtype=np.float32)
+            outs.append(c)
+            e.a, e.b, e.c, e.m, e.n, e.k = _ptr(a), _ptr(b), _ptr(c), m, n, k
+        stage, detail = C.c_uint32(), C.c_int()
+        rc = self.lib.prometheus_reactor_runtime_sgemm_batch(self.handle, entries, len(problems), flags,
+                                                             C.byref(stage), C.byref(detail))
+        st = CallStatus(rc, stage.value, detail.value)
+        return (outs if rc == PROM_OK else None), st
 
     # -- async SGEMM (bridge.go:342-361, runtime.go:573-650)
     def submit_async(self, m: int, n: int, k: int, a: np.ndarray, b: np.ndarray) -> tuple[int, CallStatus]:

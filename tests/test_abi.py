@@ -80,6 +80,9 @@ STRUCTS = {
     "PrometheusRowWiseSoftmaxResult": R.PrometheusRowWiseSoftmaxResult,
     "PrometheusGemma4E2BM1InputRmsNormRequest": R.PrometheusGemma4E2BM1InputRmsNormRequest,
     "PrometheusGemma4E2BM1InputRmsNormResult": R.PrometheusGemma4E2BM1InputRmsNormResult,
+    "PrometheusSgemmBatchEntry": R.PrometheusSgemmBatchEntry,
+    "PrometheusSgemmResidentBenchmarkRequest": R.PrometheusSgemmResidentBenchmarkRequest,
+    "PrometheusSgemmResidentBenchmarkResult": R.PrometheusSgemmResidentBenchmarkResult,
 }
 
 
@@ -151,6 +154,54 @@ def test_sgemm_validation_order(lib):
         rc = lib.prometheus_reactor_runtime_sgemm(h, a.ctypes.data, a.ctypes.data, a.ctypes.data, 2, 2, 2,
                                                   C.byref(st), C.byref(d))
         assert rc == R.PROM_ERROR and st.value == R.STAGE_INIT  # no device: no CPU fallback
+    finally:
+        lib.prometheus_reactor_runtime_destroy(h)
+
+
+def test_sgemm_caller_entries_validation(lib):
+    """benchmark_variant, resident benchmark and batch: the checks that precede any device work
+    (reactor_sgemm.cpp:5629-5700, 5984-6009; reactor_batch.c:244-282)."""
+    a = np.ones(4, dtype=np.float32)
+    st, d = C.c_uint32(), C.c_int()
+    h = _handle(lib, R.TESTCFG_FAIL_DEVICE_CREATE)
+    try:
+        # unknown variant id is rejected before the device check
+        rc = lib.prometheus_reactor_runtime_sgemm_benchmark_variant(h, a.ctypes.data, a.ctypes.data, a.ctypes.data,
+                                                                    2, 2, 2, 99, C.byref(st), C.byref(d))
+        assert (rc, st.value, d.value) == (R.PROM_ERROR, R.STAGE_INIT, R.DETAIL_BAD_VARIANT)
+        rc = lib.prometheus_reactor_runtime_sgemm_benchmark_variant(h, a.ctypes.data, a.ctypes.data, a.ctypes.data,
+                                                                    2, 2, 2, 2, C.byref(st), C.byref(d))
+        assert rc == R.PROM_ERROR and st.value == R.STAGE_INIT  # no device
+        # resident benchmark
+        assert lib.prometheus_reactor_runtime_sgemm_resident_benchmark(h, None, None) == R.PROM_ERROR
+        res = R.PrometheusSgemmResidentBenchmarkResult()
+        rc = lib.prometheus_reactor_runtime_sgemm_resident_benchmark(None, None, C.byref(res))
+        assert (rc, res.setup_stage, res.setup_detail_code) == (R.PROM_INVALID_HANDLE, R.STAGE_INIT,
+                                                                R.PROM_INVALID_HANDLE)
+        assert res.struct_size == C.sizeof(res)
+        rc = lib.prometheus_reactor_runtime_sgemm_resident_benchmark(h, None, C.byref(res))
+        assert (rc, res.setup_stage, res.setup_detail_code) == (R.PROM_ERROR, R.STAGE_TRANSFER_IN, R.PROM_ERROR)
+        assert res.resident_mode_available == 0
+        req = R.PrometheusSgemmResidentBenchmarkRequest()
+        req.struct_size = C.sizeof(req)
+        req.a = req.b = a.ctypes.data
+        req.m = req.n = req.k = 2
+        req.flags = R.RESIDENT_FLAG_VALIDATE_READBACK  # and c is NULL
+        rc = lib.prometheus_reactor_runtime_sgemm_resident_benchmark(h, C.byref(req), C.byref(res))
+        assert (rc, res.setup_stage, res.setup_detail_code) == (R.PROM_ERROR, R.STAGE_TRANSFER_IN, R.PROM_ERROR)
+        req.flags = 0
+        rc = lib.prometheus_reactor_runtime_sgemm_resident_benchmark(h, C.byref(req), C.byref(res))
+        assert (rc, res.setup_stage) == (R.PROM_ERROR, R.STAGE_INIT)  # no device
+        # batch: flag mask first, then the device, then the entry list
+        entries = (R.PrometheusSgemmBatchEntry * 1)()
+        entries[0].a = entries[0].b = entries[0].c = a.ctypes.data
+        entries[0].m = entries[0].n = entries[0].k = 2
+        rc = lib.prometheus_reactor_runtime_sgemm_batch(None, entries, 1, 0, C.byref(st), C.byref(d))
+        assert (rc, st.value, d.value) == (R.PROM_INVALID_HANDLE, R.STAGE_INIT, R.PROM_INVALID_HANDLE)
+        rc = lib.prometheus_reactor_runtime_sgemm_batch(h, entries, 1, 1 << 9, C.byref(st), C.byref(d))
+        assert (rc, st.value, d.value) == (R.PROM_ERROR, R.STAGE_INIT, R.DETAIL_BATCH_UNSUPPORTED_OPTION)
+        rc = lib.prometheus_reactor_runtime_sgemm_batch(h, entries, 1, 0, C.byref(st), C.byref(d))
+        assert (rc, st.value, d.value) == (R.PROM_ERROR, R.STAGE_INIT, R.DETAIL_BATCH_EXECUTION_FAILED)
     finally:
         lib.prometheus_reactor_runtime_destroy(h)
 
