@@ -302,6 +302,8 @@ typedef int (*NcclGetUniqueIdFn)(void* id);
 typedef int (*NcclCommInitRankFn)(void** comm, int nranks, NcclUniqueIdBytes id, int rank);
 typedef int (*NcclAllReduceFn)(const void* send, void* recv, size_t count, int dtype, int op, void* comm,
                               cudaStream_t stream);
+typedef int (*NcclAllGatherFn)(const void* send, void* recv, size_t count, int dtype, void* comm,
+                               cudaStream_t stream);
 typedef int (*NcclCommDestroyFn)(void* comm);
 typedef const char* (*NcclGetErrorStringFn)(int result);
 struct Nccl {
@@ -309,6 +311,7 @@ struct Nccl {
   NcclGetUniqueIdFn get_id = nullptr;
   NcclCommInitRankFn init_rank = nullptr;
   NcclAllReduceFn all_reduce = nullptr;
+  NcclAllGatherFn all_gather = nullptr;
   NcclCommDestroyFn destroy = nullptr;
   NcclGetErrorStringFn error_string = nullptr;
 };
@@ -322,14 +325,20 @@ Nccl& nccl() {
     n.get_id = reinterpret_cast<NcclGetUniqueIdFn>(dlsym(h, "ncclGetUniqueId"));
     n.init_rank = reinterpret_cast<NcclCommInitRankFn>(dlsym(h, "ncclCommInitRank"));
     n.all_reduce = reinterpret_cast<NcclAllReduceFn>(dlsym(h, "ncclAllReduce"));
+    n.all_gather = reinterpret_cast<NcclAllGatherFn>(dlsym(h, "ncclAllGather"));
     n.destroy = reinterpret_cast<NcclCommDestroyFn>(dlsym(h, "ncclCommDestroy"));
     n.error_string = reinterpret_cast<NcclGetErrorStringFn>(dlsym(h, "ncclGetErrorString"));
-    n.ok = n.get_id && n.init_rank && n.all_reduce && n.destroy;
+    n.ok = n.get_id && n.init_rank && n.all_reduce && n.all_gather && n.destroy;
   });
   return n;
 }
 constexpr int kNcclFloat32 = 7;  // ncclFloat32
 constexpr int kNcclSum = 0;      // ncclSum
+constexpr int kNcclInt8 = 0;     // ncclInt8 (bytes)
+// Cross-rank waits of the fused tensor-parallel path: generous, since ranks
+// may reach a forward at different times, but finite.
+constexpr unsigned long long kPeerWaitNs = 10ull * 1000000000ull;
+constexpr uint32_t kTpSlots = 5;  // 4 phases of a forward + the teardown barrier
 
 }  // namespace
 
@@ -341,8 +350,10 @@ int nccl_unique_id(NcclUniqueIdBytes* out) {
 
 // ---------------------------------------------------------------- Block
 Block::~Block() {
+  teardown_peers();
   cudaDeviceSynchronize();  // the caller's last stream may already be gone
   for (void* p : allocs_) cudaFree(p);
+  for (void* p : sym_raw_) cudaFree(p);
   if (comm_ != nullptr && nccl().ok) nccl().destroy(comm_);
 }
 
@@ -354,6 +365,130 @@ float* Block::alloc(uint64_t floats) {
   }
   allocs_.push_back(p);
   return reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// A whole cudaMalloc allocation (offset 0), so that a peer's IPC mapping of it
+// addresses the same bytes.
+float* Block::sym_alloc(uint64_t floats) {
+  void* p = nullptr;
+  if (cudaMalloc(&p, floats * sizeof(float)) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return nullptr;
+  }
+  sym_raw_.push_back(p);
+  return static_cast<float*>(p);
+}
+
+// Collective over the block's communicator (every rank calls it once, from
+// init): all-gathers each rank's IPC handles, device UUID and choice; opens the
+// peers' buffers.  The fused path is taken only if every rank asked for it and
+// every rank runs on a different GPU (ranks sharing a GPU would wait on one
+// another from separate launches); otherwise every rank stays on NCCL.
+int Block::setup_peers() {
+  const BlockDims& d = dims_;
+  const uint32_t w = d.tp_world, me = d.tp_rank;
+  struct Info {
+    cudaIpcMemHandle_t h[4];
+    unsigned char uuid[16];
+    uint32_t want;
+    uint32_t pad[3];
+  };
+  Info mine;
+  std::memset(&mine, 0, sizeof(mine));
+  mine.want = (rs_ != nullptr && ysym_ != nullptr && flags_ != nullptr && hbuf_ != nullptr) ? 1u : 0u;
+  int dev = 0;
+  cudaDeviceProp prop;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return -4;
+  std::memcpy(mine.uuid, prop.uuid.bytes, 16);
+  if (mine.want) {
+    void* bufs[4] = {rs_, hbuf_, ysym_, flags_};
+    for (int i = 0; i < 4; ++i)
+      if (cudaIpcGetMemHandle(&mine.h[i], bufs[i]) != cudaSuccess) {
+        (void)cudaGetLastError();
+        mine.want = 0;
+      }
+  }
+  std::vector<Info> all(w);
+  unsigned char* dbuf = nullptr;
+  if (cudaMalloc(&dbuf, sizeof(Info) * (w + 1)) != cudaSuccess) return -3;
+  cudaError_t e = cudaMemcpyAsync(dbuf + sizeof(Info) * w, &mine, sizeof(Info), cudaMemcpyHostToDevice, stream_);
+  int nrc = 0;
+  if (e == cudaSuccess)
+    nrc = nccl().all_gather(dbuf + sizeof(Info) * w, dbuf, sizeof(Info), kNcclInt8, comm_, stream_);
+  if (e == cudaSuccess && nrc == 0)
+    e = cudaMemcpyAsync(all.data(), dbuf, sizeof(Info) * w, cudaMemcpyDeviceToHost, stream_);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+  cudaFree(dbuf);
+  if (e != cudaSuccess || nrc != 0) return -5;
+  bool fused = true;
+  for (uint32_t p = 0; p < w; ++p) {
+    fused = fused && all[p].want == 1;
+    for (uint32_t q = 0; q < p; ++q)
+      if (std::memcmp(all[p].uuid, all[q].uuid, 16) == 0) fused = false;
+  }
+  if (!fused) return 0;  // NCCL all-reduce path
+  std::vector<float*> rs(w), hb(w), yb(w);
+  std::vector<uint64_t*> fl(w);
+  for (uint32_t p = 0; p < w; ++p) {
+    if (p == me) {
+      rs[p] = rs_;
+      hb[p] = hbuf_;
+      yb[p] = ysym_;
+      fl[p] = flags_;
+      continue;
+    }
+    void* ptr[4] = {nullptr, nullptr, nullptr, nullptr};
+    for (int i = 0; i < 4; ++i) {
+      if (cudaIpcOpenMemHandle(&ptr[i], all[p].h[i], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        std::fprintf(stderr, "oct_b200: cudaIpcOpenMemHandle(rank %u buffer %d) failed\n", p, i);
+        (void)cudaGetLastError();
+        return -5;
+      }
+      peer_opened_.push_back(ptr[i]);
+    }
+    rs[p] = static_cast<float*>(ptr[0]);
+    hb[p] = static_cast<float*>(ptr[1]);
+    yb[p] = static_cast<float*>(ptr[2]);
+    fl[p] = static_cast<uint64_t*>(ptr[3]);
+  }
+  void* arrays = nullptr;
+  if (cudaMalloc(&arrays, 4 * w * sizeof(void*)) != cudaSuccess) return -3;
+  allocs_.push_back(arrays);
+  rs_peers_ = static_cast<float**>(arrays);
+  h_peers_ = rs_peers_ + w;
+  y_peers_ = h_peers_ + w;
+  flag_peers_ = reinterpret_cast<uint64_t**>(y_peers_ + w);
+  e = cudaMemcpyAsync(rs_peers_, rs.data(), w * sizeof(void*), cudaMemcpyHostToDevice, stream_);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(h_peers_, hb.data(), w * sizeof(void*), cudaMemcpyHostToDevice, stream_);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(y_peers_, yb.data(), w * sizeof(void*), cudaMemcpyHostToDevice, stream_);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(flag_peers_, fl.data(), w * sizeof(void*), cudaMemcpyHostToDevice, stream_);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+  if (e != cudaSuccess) return -4;
+  fused_tp_ = true;
+  return 0;
+}
+
+// Bounded barrier on the teardown slot (no rank unmaps or frees memory a peer
+// may still write), then unmap the peers' buffers.
+void Block::teardown_peers() {
+  if (fused_tp_) {
+    // on the default stream: the caller's last stream may already be destroyed
+    cudaDeviceSynchronize();
+    const uint64_t ep = epoch_ + 1;
+    if (tp_signal(flag_peers_, kTpSlots - 1, dims_.tp_world, dims_.tp_rank, ep, nullptr) == cudaSuccess)
+      (void)tp_wait(flags_, kTpSlots - 1, dims_.tp_world, ep, err_, kPeerWaitNs, nullptr);
+    cudaDeviceSynchronize();
+    fused_tp_ = false;
+  }
+  for (void* p : peer_opened_) cudaIpcCloseMemHandle(p);
+  peer_opened_.clear();
+}
+
+// Publish this rank's stores of phase `slot`, then wait until every rank's are published.
+cudaError_t Block::tp_phase(uint32_t slot) {
+  cudaError_t e = tp_signal(flag_peers_, slot, dims_.tp_world, dims_.tp_rank, epoch_, stream_);
+  if (e == cudaSuccess) e = tp_wait(flags_, slot, dims_.tp_world, epoch_, err_, kPeerWaitNs, stream_);
+  return e;
 }
 
 int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t stream) {
@@ -395,7 +530,20 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
     ok = ok && ada_w_ && ada_b_ && norm3_ && norm4_ && qn_ && kn_ && temb_ && ada_ && tsteps_;
   }
   // activations and workspaces
-  hbuf_ = alloc(T * d.hidden);
+  // Fused tensor parallel wants hbuf_ (the all-gather target of the FFN input)
+  // in a plain cudaMalloc allocation that peers can map.
+  const char* tp_mode = std::getenv("OCT_B200_TP_COLLECTIVE");
+  const bool want_fused_tp = d.tp_world > 1 && !(tp_mode != nullptr && std::strcmp(tp_mode, "nccl") == 0);
+  hbuf_ = want_fused_tp ? sym_alloc(T * d.hidden) : alloc(T * d.hidden);
+  if (want_fused_tp) {
+    const uint64_t rpr = (T + d.tp_world - 1) / d.tp_world;  // rows per rank at max_batch
+    rs_ = sym_alloc(rpr * d.tp_world * d.hidden);
+    ysym_ = sym_alloc(T * d.hidden);
+    flags_ = reinterpret_cast<uint64_t*>(sym_alloc(2ull * kTpSlots * d.tp_world));
+    if (rs_ == nullptr || ysym_ == nullptr || flags_ == nullptr ||
+        cudaMemsetAsync(flags_, 0, 8ull * kTpSlots * d.tp_world, stream_) != cudaSuccess)
+      return -3;
+  }
   qkv_ = alloc(T * qkv_cols);
   fused_attn_ = d.family == kDit && flash_attention_supported(d.head_dim, d.seq_len);
   if (const char* mode = std::getenv("OCT_B200_DIT_ATTENTION"))
@@ -447,6 +595,8 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
       comm_ = nullptr;
       return -5;
     }
+    const int prc = setup_peers();
+    if (prc != 0) return prc;
   }
   return cudaStreamSynchronize(stream_) == cudaSuccess ? 0 : -4;
 }
@@ -552,8 +702,9 @@ int Block::set_weight(uint32_t slot, const float* src, uint64_t count, bool on_d
 }
 
 cudaError_t Block::gemm(const float* a, uint64_t lda, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
-                        const float* residual, uint64_t ldr) {
-  return sgemm_tc_presplit(a, lda, w.hi, w.lo, c, ldc, m, w.n, w.k, scratch_, err_, stream_, residual, ldr);
+                        const float* residual, uint64_t ldr, const RowScatter* scatter) {
+  return sgemm_tc_presplit(a, lda, w.hi, w.lo, c, ldc, m, w.n, w.k, scratch_, err_, stream_, residual, ldr,
+                           kTcSingle16, scatter);
 }
 
 cudaError_t Block::all_reduce(float* buf, uint64_t count) {
@@ -600,6 +751,29 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
   const bool lead = d.tp_rank == 0;  // rank that adds the residual into row-parallel partial sums
   cudaError_t e = cudaSuccess;
   auto ok = [&]() { return e == cudaSuccess && (e = cudaGetLastError()) == cudaSuccess; };
+  // Fused tensor parallel (peer memory) when every rank owns an equal row share.
+  const bool tpf = fused_tp_ && T % d.tp_world == 0;
+  const uint32_t rpr = tpf ? T / d.tp_world : 0;
+  RowScatter sc;
+  TpReduce red;
+  if (tpf) {
+    ++epoch_;  // every rank runs the same forwards, so the epochs agree
+    sc.dst = rs_peers_;
+    sc.rows_per_rank = rpr;
+    sc.src_rank = d.tp_rank;
+    sc.ld = d.hidden;
+    red.slots = rs_;
+    red.nslots = d.tp_world;
+    red.slot_stride = static_cast<uint64_t>(rpr) * d.hidden;
+    red.ld_slot = d.hidden;
+    red.rows = rpr;
+    red.row0 = d.tp_rank * rpr;
+    red.width = d.hidden;
+    red.rows_per_item = d.seq_len;
+    red.eps = d.eps;
+    red.npush = d.tp_world;
+    red.ld_push = d.hidden;
+  }
   if (d.family == kGemma) {
     norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x, d.hidden, norm1_, d.eps, nullptr, nullptr, nullptr, 0,
                                                           nullptr, 0, d.seq_len, hbuf_, d.hidden, T, d.hidden);
@@ -613,17 +787,49 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
     for (uint32_t b = 0; b < batch && e == cudaSuccess; ++b)
       e = attention(b, qkv_cols, attn_cols, attn_cols + d.kv_heads * d.head_dim, true);
     if (!ok()) return -4;
-    e = gemm(attn_, attn_cols, wo_, x1_, d.hidden, T, lead ? x : nullptr, d.hidden);  // x1 = x + O Wo
-    if (ok()) e = all_reduce(x1_, static_cast<uint64_t>(T) * d.hidden);
-    if (!ok()) return -4;
-    norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x1_, d.hidden, norm2_, d.eps, nullptr, nullptr, nullptr, 0,
-                                                          nullptr, 0, d.seq_len, hbuf_, d.hidden, T, d.hidden);
-    if (!ok()) return -4;
+    if (tpf) {
+      // partial O Wo rows -> their owners; owners: x1 = x + sum, h = RMSNorm(x1) -> every rank
+      e = gemm(attn_, attn_cols, wo_, rs_, d.hidden, T, nullptr, 0, &sc);
+      if (ok()) e = tp_phase(0);
+      if (!ok()) return -4;
+      TpReduce r = red;
+      r.res = x;
+      r.ld_res = d.hidden;
+      r.keep = x1_;
+      r.ld_keep = d.hidden;
+      r.g2 = norm2_;
+      r.push = h_peers_;
+      e = tp_reduce_rows(r, stream_);
+      if (ok()) e = tp_phase(1);
+      if (!ok()) return -4;
+    } else {
+      e = gemm(attn_, attn_cols, wo_, x1_, d.hidden, T, lead ? x : nullptr, d.hidden);  // x1 = x + O Wo
+      if (ok()) e = all_reduce(x1_, static_cast<uint64_t>(T) * d.hidden);
+      if (!ok()) return -4;
+      norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x1_, d.hidden, norm2_, d.eps, nullptr, nullptr, nullptr,
+                                                            0, nullptr, 0, d.seq_len, hbuf_, d.hidden, T, d.hidden);
+      if (!ok()) return -4;
+    }
     e = gemm(hbuf_, d.hidden, wgu_, gu_, 2ull * d.ffn, T);
     if (!ok()) return -4;
     gated_act_kernel<true><<<grid_for(static_cast<uint64_t>(T) * d.ffn / 4, NT), NT, 0, stream_>>>(gu_, act_, T,
                                                                                                  d.ffn);
     if (!ok()) return -4;
+    if (tpf) {
+      // partial act Wd rows -> owners; owners: y = x1 + sum -> every rank
+      e = gemm(act_, d.ffn, wd_, rs_, d.hidden, T, nullptr, 0, &sc);
+      if (ok()) e = tp_phase(2);
+      if (!ok()) return -4;
+      TpReduce r = red;
+      r.res = x1_;
+      r.ld_res = d.hidden;
+      r.push = y_peers_;
+      e = tp_reduce_rows(r, stream_);
+      if (ok()) e = tp_phase(3);
+      if (ok()) e = cudaMemcpyAsync(y, ysym_, static_cast<uint64_t>(T) * d.hidden * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, stream_);
+      return ok() ? 0 : -4;
+    }
     e = gemm(act_, d.ffn, wd_, y, d.hidden, T, lead ? x1_ : nullptr, d.hidden);  // y = x1 + act Wd
     if (ok()) e = all_reduce(y, static_cast<uint64_t>(T) * d.hidden);
     return ok() ? 0 : -4;
@@ -673,21 +879,62 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
       e = attention(b, qkv_cols, attn_cols, 2 * attn_cols, false);
   }
   if (!ok()) return -4;
-  e = gemm(attn_, attn_cols, wo_, proj_, d.hidden, T);
-  if (ok()) e = all_reduce(proj_, static_cast<uint64_t>(T) * d.hidden);
-  if (!ok()) return -4;
-  // res = x + gate_a * RMSNorm(proj)
-  norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(proj_, d.hidden, norm2_, d.eps, nullptr, nullptr, x, d.hidden,
-                                                        gate_a, ms, d.seq_len, x1_, d.hidden, T, d.hidden);
-  if (!ok()) return -4;
-  norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x1_, d.hidden, norm3_, d.eps, scale_m, shift_m, nullptr, 0,
-                                                        nullptr, ms, d.seq_len, hbuf_, d.hidden, T, d.hidden);
-  if (!ok()) return -4;
+  if (tpf) {
+    // partial attn Wo rows -> owners; owners: x1 = x + gate_a * RMSNorm(sum),
+    // h = RMSNorm(x1) * scale_m + shift_m -> every rank
+    e = gemm(attn_, attn_cols, wo_, rs_, d.hidden, T, nullptr, 0, &sc);
+    if (ok()) e = tp_phase(0);
+    if (!ok()) return -4;
+    TpReduce r = red;
+    r.mod_stride = ms;
+    r.g1 = norm2_;
+    r.gate1 = gate_a;
+    r.res = x;
+    r.ld_res = d.hidden;
+    r.keep = x1_;
+    r.ld_keep = d.hidden;
+    r.g2 = norm3_;
+    r.mul2 = scale_m;
+    r.add2 = shift_m;
+    r.push = h_peers_;
+    e = tp_reduce_rows(r, stream_);
+    if (ok()) e = tp_phase(1);
+    if (!ok()) return -4;
+  } else {
+    e = gemm(attn_, attn_cols, wo_, proj_, d.hidden, T);
+    if (ok()) e = all_reduce(proj_, static_cast<uint64_t>(T) * d.hidden);
+    if (!ok()) return -4;
+    // res = x + gate_a * RMSNorm(proj)
+    norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(proj_, d.hidden, norm2_, d.eps, nullptr, nullptr, x,
+                                                          d.hidden, gate_a, ms, d.seq_len, x1_, d.hidden, T, d.hidden);
+    if (!ok()) return -4;
+    norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x1_, d.hidden, norm3_, d.eps, scale_m, shift_m, nullptr, 0,
+                                                          nullptr, ms, d.seq_len, hbuf_, d.hidden, T, d.hidden);
+    if (!ok()) return -4;
+  }
   e = gemm(hbuf_, d.hidden, wgu_, gu_, 2ull * d.ffn, T);
   if (!ok()) return -4;
   gated_act_kernel<false><<<grid_for(static_cast<uint64_t>(T) * d.ffn / 4, NT), NT, 0, stream_>>>(gu_, act_, T,
                                                                                                 d.ffn);
   if (!ok()) return -4;
+  if (tpf) {
+    // partial act W2 rows -> owners; owners: y = x1 + gate_m * RMSNorm(sum) -> every rank
+    e = gemm(act_, d.ffn, wd_, rs_, d.hidden, T, nullptr, 0, &sc);
+    if (ok()) e = tp_phase(2);
+    if (!ok()) return -4;
+    TpReduce r = red;
+    r.mod_stride = ms;
+    r.g1 = norm4_;
+    r.gate1 = gate_m;
+    r.res = x1_;
+    r.ld_res = d.hidden;
+    r.push = y_peers_;
+    e = tp_reduce_rows(r, stream_);
+    if (ok()) e = tp_phase(3);
+    if (ok()) e = cudaMemcpyAsync(y, ysym_, static_cast<uint64_t>(T) * d.hidden * sizeof(float),
+                                  cudaMemcpyDeviceToDevice, stream_);
+    return ok() ? 0 : -4;
+  }
   e = gemm(act_, d.ffn, wd_, proj_, d.hidden, T);
   if (ok()) e = all_reduce(proj_, static_cast<uint64_t>(T) * d.hidden);
   if (!ok()) return -4;

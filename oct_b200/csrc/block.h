@@ -66,9 +66,15 @@ class Block {
   float* alloc(uint64_t floats);
   int build_rope_tables();
   cudaError_t gemm(const float* a, uint64_t lda, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
-                   const float* residual = nullptr, uint64_t ldr = 0);
+                   const float* residual = nullptr, uint64_t ldr = 0, const RowScatter* scatter = nullptr);
   cudaError_t attention(uint32_t item, uint64_t ldq, uint32_t k_col, uint32_t v_col, bool shared_kv);
   cudaError_t all_reduce(float* buf, uint64_t count);
+  // tensor parallel over peer memory (tp_fused.cu)
+  float* sym_alloc(uint64_t floats);
+  int setup_peers();
+  void teardown_peers();
+  cudaError_t tp_phase(uint32_t slot);  // signal this rank's stores of `slot`, wait for every rank's
+  int forward_tp_fused(const float* x, float* y, uint32_t batch);
 
   BlockDims dims_;
   cudaStream_t stream_ = nullptr;
@@ -87,6 +93,19 @@ class Block {
   bool fused_attn_ = false;
   float *qsplit_ = nullptr, *ksplit_ = nullptr, *vtsplit_ = nullptr;
   unsigned int* err_ = nullptr;
+  // Fused tensor parallel: the row-parallel products scatter their partial rows
+  // into the owner rank's `rs_` slots; owners reduce and push finished rows into
+  // every rank's `hbuf_` / `ysym_`.  Flags: [5 slots][world] u64 epochs.
+  bool fused_tp_ = false;
+  uint64_t epoch_ = 0;
+  float *rs_ = nullptr, *ysym_ = nullptr;
+  uint64_t* flags_ = nullptr;
+  std::vector<void*> sym_raw_;      // this rank's symmetric allocations
+  std::vector<void*> peer_opened_;  // peers' allocations mapped into this process
+  float** rs_peers_ = nullptr;      // device arrays of one pointer per rank
+  float** h_peers_ = nullptr;
+  float** y_peers_ = nullptr;
+  uint64_t** flag_peers_ = nullptr;
 };
 
 }  // namespace oct

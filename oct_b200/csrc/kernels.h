@@ -52,10 +52,20 @@ uint64_t split_b_elems(uint32_t n, uint32_t k);
 cudaError_t sgemm_tc_split_b(const float* b, uint64_t ldb, uint32_t k, uint32_t n, float* bhi, float* blo,
                              cudaStream_t stream);
 uint64_t sgemm_tc_a_scratch_bytes(uint32_t m, uint32_t k);
+// Row scatter epilogue (single-CTA configurations): output row r goes to rank
+// owner = r / rows_per_rank, into dst[owner] at row
+// src_rank * rows_per_rank + (r - owner * rows_per_rank), leading dimension ld.
+// `dst` is a device array of one base pointer per rank (peers' memory included).
+struct RowScatter {
+  float* const* dst = nullptr;
+  uint32_t rows_per_rank = 0;
+  uint32_t src_rank = 0;
+  uint64_t ld = 0;
+};
 cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, const float* blo, float* c,
                               uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* a_scratch, unsigned int* err,
                               cudaStream_t stream, const float* residual = nullptr, uint64_t ldr = 0,
-                              int cfg = kTcSingle16);
+                              int cfg = kTcSingle16, const RowScatter* scatter = nullptr);
 
 // A already split by its producer (hi/lo in the [count][Mp][Kp] layout of
 // split_dims, zero padded); B is split into b_scratch.  Strided batch as GemmBatch.
@@ -92,6 +102,39 @@ cudaError_t split_heads(const float* x, uint64_t ldx, uint32_t items, uint32_t h
                         float* lo, cudaStream_t stream);
 cudaError_t split_transpose_heads(const float* v, uint64_t ldv, uint32_t items, uint32_t heads, uint32_t seq,
                                   float* vthi, float* vtlo, cudaStream_t stream);
+
+// ---------------------------------------------------------------- tensor parallel over peer memory
+// (tp_fused.cu).  Flags are [slot][world] u64 epochs in each rank's memory.
+// signal: rank `src` stores `epoch` into flags_dev[k][slot][src] of every rank k
+// (release, system scope).  wait: until flags_local[slot][s] >= epoch for every
+// source s (acquire), at most budget_ns, else kErrWaitPeer in *err.
+cudaError_t tp_signal(uint64_t* const* flags_dev, uint32_t slot, uint32_t world, uint32_t src, uint64_t epoch,
+                      cudaStream_t stream);
+cudaError_t tp_wait(const uint64_t* flags_local, uint32_t slot, uint32_t world, uint64_t epoch, unsigned int* err,
+                    unsigned long long budget_ns, cudaStream_t stream);
+// Reduce the row-scatter slots of this rank's rows, then residual / norm /
+// modulation, then push the rows to every rank (see tp_fused.cu).
+struct TpReduce {
+  const float* slots = nullptr;  // [nslots][rows][ld_slot]
+  uint32_t nslots = 0;
+  uint64_t slot_stride = 0, ld_slot = 0;
+  uint32_t rows = 0, row0 = 0, width = 0, rows_per_item = 1;
+  uint64_t mod_stride = 0;
+  float eps = 1e-6f;
+  const float* g1 = nullptr;
+  const float* gate1 = nullptr;
+  const float* res = nullptr;
+  uint64_t ld_res = 0;
+  float* keep = nullptr;
+  uint64_t ld_keep = 0;
+  const float* g2 = nullptr;
+  const float* mul2 = nullptr;
+  const float* add2 = nullptr;
+  float* const* push = nullptr;  // device array of npush row-major [*][ld_push] buffers
+  uint32_t npush = 0;
+  uint64_t ld_push = 0;
+};
+cudaError_t tp_reduce_rows(const TpReduce& args, cudaStream_t stream);
 
 // ---------------------------------------------------------------- reductions
 // op: 1 = row sum, 2 = row max, 3 = stable softmax.  `nonfinite` (device

@@ -21,6 +21,7 @@ enum : unsigned int {
   kErrWaitDrain = 1u << 3,     // teardown waited too long for copies in flight
   kErrWaitRow = 1u << 4,       // reduction warp waited too long for a row
   kErrNonFinite = 1u << 5,     // reduction input held NaN/Inf
+  kErrWaitPeer = 1u << 6,      // a tensor-parallel peer's signal did not arrive in time
 };
 
 // Wall-clock budget for any single in-kernel wait.  Normal stage waits take

@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    float* __restrict__ c, uint32_t m, uint32_t n, uint64_t ldc, uint32_t num_kb,
                    uint32_t tiles_m, uint32_t tiles_n, uint32_t entry_rows_a, uint32_t entry_rows_b,
                    uint64_t stride_c, const float* __restrict__ residual, uint64_t ldr,
-                   unsigned int* __restrict__ err) {
+                   unsigned int* __restrict__ err, const RowScatter scatter) {
   using Cfg = TileCfg<BK>;
   constexpr uint32_t S = Cfg::STAGES;
   constexpr uint32_t KBC = KC / BK;  // k-blocks per accumulation chunk
@@ -319,6 +319,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                            ((ldr % 4 == 0) && ((reinterpret_cast<uintptr_t>(residual) & 15u) == 0)));
       if (row < m && col0 < n) {
         float* dst = c + static_cast<uint64_t>(row) * ldc + col0;
+        if (scatter.dst != nullptr) {
+          // Row scatter: the row's owner rank receives it in its slot for this
+          // source rank (a peer's memory over NVLink for every other owner).
+          const uint32_t owner = row / scatter.rows_per_rank;
+          const uint64_t slot_row =
+              static_cast<uint64_t>(scatter.src_rank) * scatter.rows_per_rank + (row - owner * scatter.rows_per_rank);
+          dst = scatter.dst[owner] + slot_row * scatter.ld + col0;
+        }
         // Optional fused residual epilogue: C = R + A * B (R may alias C).
         const float* src = residual != nullptr ? residual + static_cast<uint64_t>(row) * ldr + col0 : nullptr;
         if (vec_ok && col0 + 128 <= n) {
@@ -604,7 +612,7 @@ template <int BK>
 cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
                         uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
                         cudaStream_t stream, uint32_t batch, uint64_t stride_c, const float* residual = nullptr,
-                        uint64_t ldr = 0) {
+                        uint64_t ldr = 0, const RowScatter* scatter = nullptr) {
   using Cfg = TileCfg<BK>;
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
   const uint32_t rows_a = d.mp * batch, rows_b = d.np * batch;
@@ -618,9 +626,12 @@ cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, co
   const uint32_t tiles_m = (m + BM - 1) / BM, tiles_n = (n + BN - 1) / BN;
   const uint64_t grid = static_cast<uint64_t>(tiles_m) * tiles_n * batch;
   if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
+  const RowScatter sc = scatter != nullptr ? *scatter : RowScatter{};
+  if (sc.dst != nullptr && (batch != 1 || sc.rows_per_rank == 0 || sc.ld % 4 != 0 || ldc % 4 != 0))
+    return cudaErrorInvalidValue;
   sgemm3x_kernel<BK><<<static_cast<uint32_t>(grid), NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(
       m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, d.mp, d.np, stride_c, residual, ldr,
-      err);
+      err, sc);
   return cudaGetLastError();
 }
 
@@ -653,10 +664,13 @@ cudaError_t launch_pair(const float* ahi, const float* alo, const float* bhi, co
 cudaError_t launch_config(int cfg, const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
                           uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
                           cudaStream_t stream, uint32_t batch, uint64_t stride_c, const float* residual = nullptr,
-                          uint64_t ldr = 0) {
+                          uint64_t ldr = 0, const RowScatter* scatter = nullptr) {
+  // the CTA-pair kernels have no row-scatter epilogue
+  if (scatter != nullptr && scatter->dst != nullptr && cfg != kTcSingle16 && cfg != kTcSingle32)
+    return cudaErrorInvalidValue;
   switch (cfg) {
-    case kTcSingle16: return launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
-    case kTcSingle32: return launch_main<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
+    case kTcSingle16: return launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr, scatter);
+    case kTcSingle32: return launch_main<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr, scatter);
     case kTcPair16: return launch_pair<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
     case kTcPair32: return launch_pair<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
     default: return cudaErrorInvalidValue;
@@ -702,7 +716,8 @@ uint64_t sgemm_tc_a_scratch_bytes(uint32_t m, uint32_t k) {
 
 cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, const float* blo, float* c,
                               uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* a_scratch, unsigned int* err,
-                              cudaStream_t stream, const float* residual, uint64_t ldr, int cfg) {
+                              cudaStream_t stream, const float* residual, uint64_t ldr, int cfg,
+                              const RowScatter* scatter) {
   if (m == 0 || n == 0 || k == 0) return cudaSuccess;
   if ((reinterpret_cast<uintptr_t>(a_scratch) & 1023u) != 0) return cudaErrorInvalidValue;
   const SplitDims d = split_dims(m, n, k);
@@ -713,7 +728,7 @@ cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, co
   split_rows_kernel<<<dim3(blocks, 1), 256, 0, stream>>>(a, lda, m, k, ahi, alo, d.mp, d.kp, 0);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, 0, residual, ldr);
+  return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, 0, residual, ldr, scatter);
 }
 
 // A operand already in the split layout (hi/lo, [count][Mp][Kp], zero padded),
