@@ -486,9 +486,7 @@ void Block::teardown_peers() {
 
 // Publish this rank's stores of phase `slot`, then wait until every rank's are published.
 cudaError_t Block::tp_phase(uint32_t slot) {
-  cudaError_t e = tp_signal(flag_peers_, slot, dims_.tp_world, dims_.tp_rank, epoch_, stream_);
-  if (e == cudaSuccess) e = tp_wait(flags_, slot, dims_.tp_world, epoch_, err_, kPeerWaitNs, stream_);
-  return e;
+  return tp_signal_wait(flag_peers_, flags_, slot, dims_.tp_world, dims_.tp_rank, epoch_, err_, kPeerWaitNs, stream_);
 }
 
 int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t stream) {

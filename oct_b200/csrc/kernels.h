@@ -112,6 +112,10 @@ cudaError_t tp_signal(uint64_t* const* flags_dev, uint32_t slot, uint32_t world,
                       cudaStream_t stream);
 cudaError_t tp_wait(const uint64_t* flags_local, uint32_t slot, uint32_t world, uint64_t epoch, unsigned int* err,
                     unsigned long long budget_ns, cudaStream_t stream);
+// signal, then wait, in one launch
+cudaError_t tp_signal_wait(uint64_t* const* flags_dev, const uint64_t* flags_local, uint32_t slot, uint32_t world,
+                           uint32_t src, uint64_t epoch, unsigned int* err, unsigned long long budget_ns,
+                           cudaStream_t stream);
 // Reduce the row-scatter slots of this rank's rows, then residual / norm /
 // modulation, then push the rows to every rank (see tp_fused.cu).
 struct TpReduce {

@@ -311,7 +311,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
-    if (ok && num_kb > 0) {
+    if (scatter.dst != nullptr && num_kb > 0) {
+      // Row scatter: stage the 128 x 256 tile in the operand ring (idle once the
+      // last accumulator chunk arrived: every MMA and TMA copy has completed), then
+      // each warp stores whole rows as 512-byte coalesced segments -- the remote
+      // rows cross NVLink in full packets instead of 16-byte pieces.
+      constexpr uint32_t LDS = BN + 4;  // padded row stride (floats): conflict-free float4 stores
+      float* stage_tile = reinterpret_cast<float*>(smem);
+      if (ok) {
+        float* srow = stage_tile + (q * 32 + lane) * LDS + h * 128u;
+#pragma unroll
+        for (int j = 0; j < 128; j += 4)
+          *reinterpret_cast<float4*>(srow + j) = make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight epilogue warps
+      if (*(volatile uint32_t*)&aborted == 0u) {
+        const uint32_t ew = warp - 2u;
+        for (uint32_t lr = ew; lr < BM; lr += 8u) {
+          const uint32_t row = tile_m * BM + lr;
+          if (row >= m) break;
+          const uint32_t owner = row / scatter.rows_per_rank;
+          const uint64_t slot_row =
+              static_cast<uint64_t>(scatter.src_rank) * scatter.rows_per_rank + (row - owner * scatter.rows_per_rank);
+          float* drow = scatter.dst[owner] + slot_row * scatter.ld;
+          const float* srow = stage_tile + lr * LDS;
+#pragma unroll
+          for (uint32_t half = 0; half < 2; ++half) {
+            const uint32_t cl = half * 128u + lane * 4u;  // column within the tile
+            const uint32_t col = tile_n * BN + cl;
+            if (col + 4 <= n) {
+              *reinterpret_cast<float4*>(drow + col) = *reinterpret_cast<const float4*>(srow + cl);
+            } else {
+              for (uint32_t t = 0; t < 4; ++t)
+                if (col + t < n) drow[col + t] = srow[cl + t];
+            }
+          }
+        }
+      }
+    } else if (ok && num_kb > 0) {
       const uint32_t row = tile_m * BM + q * 32 + lane;
       const uint32_t col0 = tile_n * BN + h * 128u;
       const bool vec_ok = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) &&
@@ -319,14 +356,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                            ((ldr % 4 == 0) && ((reinterpret_cast<uintptr_t>(residual) & 15u) == 0)));
       if (row < m && col0 < n) {
         float* dst = c + static_cast<uint64_t>(row) * ldc + col0;
-        if (scatter.dst != nullptr) {
-          // Row scatter: the row's owner rank receives it in its slot for this
-          // source rank (a peer's memory over NVLink for every other owner).
-          const uint32_t owner = row / scatter.rows_per_rank;
-          const uint64_t slot_row =
-              static_cast<uint64_t>(scatter.src_rank) * scatter.rows_per_rank + (row - owner * scatter.rows_per_rank);
-          dst = scatter.dst[owner] + slot_row * scatter.ld + col0;
-        }
         // Optional fused residual epilogue: C = R + A * B (R may alias C).
         const float* src = residual != nullptr ? residual + static_cast<uint64_t>(row) * ldr + col0 : nullptr;
         if (vec_ok && col0 + 128 <= n) {

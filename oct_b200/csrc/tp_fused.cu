@@ -72,6 +72,30 @@ __global__ void tp_wait_kernel(const uint64_t* flags, uint32_t slot, uint32_t wo
   __syncthreads();
 }
 
+// signal + wait in one launch: lane t publishes to rank t, then waits for rank t.
+__global__ void tp_phase_kernel(uint64_t* const* flags_dev, const uint64_t* flags_local, uint32_t slot, uint32_t world,
+                                uint32_t src, uint64_t epoch, unsigned int* err, unsigned long long budget_ns) {
+  const uint32_t t = threadIdx.x;
+  if (t < world) {
+    __threadfence_system();
+    uint64_t* f = flags_dev[t] + static_cast<uint64_t>(slot) * world + src;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(epoch) : "memory");
+    const uint64_t* g = flags_local + static_cast<uint64_t>(slot) * world + t;
+    const unsigned long long start = global_timer_ns();
+    while (true) {
+      uint64_t v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(g) : "memory");
+      if (v >= epoch) break;
+      if (global_timer_ns() - start > budget_ns) {
+        atomicOr(err, kErrWaitPeer);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncwarp();
+}
+
 // One CTA per own row (global row = row0 + r):
 //   s = sum_k slots[k][r]                           (fixed order k = 0 .. nslots-1)
 //   s = rmsnorm(s) * g1                             (if g1)
@@ -161,6 +185,14 @@ cudaError_t tp_wait(const uint64_t* flags_local, uint32_t slot, uint32_t world, 
                     unsigned long long budget_ns, cudaStream_t stream) {
   if (world == 0 || world > 32) return cudaErrorInvalidValue;
   tp_wait_kernel<<<1, 32, 0, stream>>>(flags_local, slot, world, epoch, err, budget_ns);
+  return cudaGetLastError();
+}
+
+cudaError_t tp_signal_wait(uint64_t* const* flags_dev, const uint64_t* flags_local, uint32_t slot, uint32_t world,
+                           uint32_t src, uint64_t epoch, unsigned int* err, unsigned long long budget_ns,
+                           cudaStream_t stream) {
+  if (world == 0 || world > 32) return cudaErrorInvalidValue;
+  tp_phase_kernel<<<1, 32, 0, stream>>>(flags_dev, flags_local, slot, world, src, epoch, err, budget_ns);
   return cudaGetLastError();
 }
 
