@@ -110,6 +110,9 @@ struct Runtime {
   bool timing = false;
   std::vector<oct::SgemmEvents> timing_events;
   size_t timing_used = 0;
+  // Pipelined host SGEMM: upload and download streams, chunk events.
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  std::vector<cudaEvent_t> pipe_events;
   // SGEMM batch workers: one stream, split scratch and A/B staging each.
   cudaStream_t batch_streams[kBatchWorkers] = {};
   DevBuf batch_scratch[kBatchWorkers], batch_a[kBatchWorkers], batch_b[kBatchWorkers];
@@ -284,6 +287,14 @@ void destroy_runtime(Runtime* rt) {
   for (DevBuf* b : {&rt->scratch, &rt->da, &rt->db, &rt->dc, &rt->rin, &rt->rout, &rt->rw, &rt->rinv, &rt->words,
                     &rt->batch_c})
     b->release();
+  for (cudaStream_t* st : {&rt->copy_in, &rt->copy_out})
+    if (*st != nullptr) {
+      cudaStreamSynchronize(*st);
+      cudaStreamDestroy(*st);
+      *st = nullptr;
+    }
+  for (cudaEvent_t ev : rt->pipe_events) cudaEventDestroy(ev);
+  rt->pipe_events.clear();
   for (uint32_t w = 0; w < kBatchWorkers; ++w) {
     if (rt->batch_streams[w] != nullptr) {
       cudaStreamSynchronize(rt->batch_streams[w]);
@@ -729,6 +740,124 @@ int prometheus_runtime_probe(void* handle, PrometheusCaps* out_caps) {
 
 // Validation order and codes follow reactor_sgemm.cpp:4149-4176.
 namespace {
+// Host-injected failure flags that the one-shot path reports stage by stage.
+constexpr uint32_t kTestFlagsWithHostInjection =
+    PROM_TESTCFG_FAIL_BUFFER_ALLOC | PROM_TESTCFG_FAIL_UPLOAD | PROM_TESTCFG_FAIL_DISPATCH | PROM_TESTCFG_FAIL_DOWNLOAD;
+
+// Large host-buffer products: transfers and tensor work overlap inside the one
+// call.  B goes up first and is split once; A goes up in row chunks on a copy
+// stream, each chunk's product starts as soon as its rows landed, and each C
+// chunk goes down on a second copy stream as soon as it is computed.  Every C
+// element is computed exactly as in the one-shot path (same kernel, same K
+// order), so the result is bit-identical.  With pinned caller buffers all
+// three engines run concurrently; with pageable ones the host thread stages
+// one copy at a time while the GPU keeps computing.
+int sgemm_host_pipelined(Runtime* rt, const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k,
+                         float* da, float* db, float* dc, uint32_t* out_stage, int* out_detail_code) {
+  cudaStream_t cs = rt->stream;
+  if (rt->copy_in == nullptr && cudaStreamCreateWithFlags(&rt->copy_in, cudaStreamNonBlocking) != cudaSuccess) {
+    rt->copy_in = nullptr;
+    set_status(out_stage, out_detail_code, PROM_STAGE_INIT, OCT_B200_DETAIL_CUDA_ERROR);
+    return PROM_ERROR;
+  }
+  if (rt->copy_out == nullptr && cudaStreamCreateWithFlags(&rt->copy_out, cudaStreamNonBlocking) != cudaSuccess) {
+    rt->copy_out = nullptr;
+    set_status(out_stage, out_detail_code, PROM_STAGE_INIT, OCT_B200_DETAIL_CUDA_ERROR);
+    return PROM_ERROR;
+  }
+  // ~8 row chunks of at least 256 rows (the tile-pair height)
+  const uint32_t rows = std::max<uint32_t>(256u, ((m + 7u) / 8u + 255u) / 256u * 256u);
+  const uint32_t nchunks = (m + rows - 1) / rows;
+  const uint32_t nev = 2 * nchunks + 1;
+  while (rt->pipe_events.size() < nev) {
+    cudaEvent_t ev = nullptr;
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+      set_status(out_stage, out_detail_code, PROM_STAGE_INIT, OCT_B200_DETAIL_CUDA_ERROR);
+      return PROM_ERROR;
+    }
+    rt->pipe_events.push_back(ev);
+  }
+  const uint64_t b_elems = oct::split_b_elems(n, k);
+  const uint64_t b_bytes = (2 * b_elems * sizeof(float) + 1023) & ~uint64_t(1023);
+  if (rt->scratch.ensure(b_bytes + oct::sgemm_tc_a_scratch_bytes(rows, k) + 1024, cs) != cudaSuccess) {
+    set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_IN, OCT_B200_DETAIL_OUT_OF_MEMORY);
+    return PROM_ERROR;
+  }
+  float* bhi = static_cast<float*>(rt->scratch.aligned());
+  float* blo = bhi + b_elems;
+  void* a_scratch = static_cast<char*>(rt->scratch.aligned()) + b_bytes;
+  cudaEvent_t ev_b = rt->pipe_events[0];
+  auto ev_a = [&](uint32_t i) { return rt->pipe_events[1 + i]; };
+  auto ev_g = [&](uint32_t i) { return rt->pipe_events[1 + nchunks + i]; };
+  const uint64_t b_n = static_cast<uint64_t>(k) * n;
+  uint32_t fail_stage = PROM_STAGE_NONE;
+  int fail_detail = 0;
+  auto fail = [&](uint32_t stage, int detail) {
+    if (fail_stage == PROM_STAGE_NONE) {
+      fail_stage = stage;
+      fail_detail = detail;
+    }
+  };
+  cudaError_t e = reset_words(rt);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(db, b, b_n * 4, cudaMemcpyHostToDevice, rt->copy_in);
+  if (e == cudaSuccess) e = cudaEventRecord(ev_b, rt->copy_in);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, ev_b, 0);
+  if (e == cudaSuccess) e = oct::sgemm_tc_split_b(db, n, k, n, bhi, blo, cs);
+  if (e != cudaSuccess) fail(PROM_STAGE_TRANSFER_IN, OCT_B200_DETAIL_CUDA_ERROR);
+  for (uint32_t i = 0; i < nchunks && fail_stage == PROM_STAGE_NONE; ++i) {
+    const uint32_t r0 = i * rows, rc = std::min(rows, m - r0);
+    const uint64_t a_off = static_cast<uint64_t>(r0) * k, c_off = static_cast<uint64_t>(r0) * n;
+    e = cudaMemcpyAsync(da + a_off, a + a_off, static_cast<uint64_t>(rc) * k * 4, cudaMemcpyHostToDevice,
+                        rt->copy_in);
+    if (e == cudaSuccess) e = cudaEventRecord(ev_a(i), rt->copy_in);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, ev_a(i), 0);
+    if (e != cudaSuccess) {
+      fail(PROM_STAGE_TRANSFER_IN, OCT_B200_DETAIL_CUDA_ERROR);
+      break;
+    }
+    e = oct::sgemm_tc_presplit(da + a_off, k, bhi, blo, dc + c_off, n, rc, n, k, a_scratch, rt->err_word(), cs);
+    if (e == cudaSuccess) e = cudaEventRecord(ev_g(i), cs);
+    if (e != cudaSuccess) {
+      fail(PROM_STAGE_SUBMIT, OCT_B200_DETAIL_CUDA_ERROR);
+      break;
+    }
+    if (i >= 1) {  // the previous chunk's result goes down while this one computes
+      const uint32_t p0 = (i - 1) * rows, pc = std::min(rows, m - p0);
+      const uint64_t p_off = static_cast<uint64_t>(p0) * n;
+      e = cudaStreamWaitEvent(rt->copy_out, ev_g(i - 1), 0);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(c + p_off, dc + p_off, static_cast<uint64_t>(pc) * n * 4, cudaMemcpyDeviceToHost,
+                            rt->copy_out);
+      if (e != cudaSuccess) fail(PROM_STAGE_TRANSFER_OUT, OCT_B200_DETAIL_CUDA_ERROR);
+    }
+  }
+  if (fail_stage == PROM_STAGE_NONE) {
+    const uint32_t p0 = (nchunks - 1) * rows, pc = m - p0;
+    const uint64_t p_off = static_cast<uint64_t>(p0) * n;
+    e = cudaStreamWaitEvent(rt->copy_out, ev_g(nchunks - 1), 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(c + p_off, dc + p_off, static_cast<uint64_t>(pc) * n * 4, cudaMemcpyDeviceToHost,
+                          rt->copy_out);
+    if (e != cudaSuccess) fail(PROM_STAGE_TRANSFER_OUT, OCT_B200_DETAIL_CUDA_ERROR);
+  }
+  // drain every stream, failed or not
+  const cudaError_t s_in = cudaStreamSynchronize(rt->copy_in);
+  const cudaError_t s_cs = cudaStreamSynchronize(cs);
+  const cudaError_t s_out = cudaStreamSynchronize(rt->copy_out);
+  if (s_in != cudaSuccess) fail(PROM_STAGE_TRANSFER_IN, OCT_B200_DETAIL_CUDA_ERROR);
+  if (s_cs != cudaSuccess) fail(PROM_STAGE_SUBMIT, OCT_B200_DETAIL_CUDA_ERROR);
+  if (s_out != cudaSuccess) fail(PROM_STAGE_TRANSFER_OUT, OCT_B200_DETAIL_CUDA_ERROR);
+  Words w;
+  if (fail_stage == PROM_STAGE_NONE && (read_words(rt, &w) != cudaSuccess || w.err != 0))
+    fail(PROM_STAGE_SUBMIT, OCT_B200_DETAIL_DEVICE_TIMEOUT);
+  if (fail_stage != PROM_STAGE_NONE) {
+    set_status(out_stage, out_detail_code, fail_stage, fail_detail);
+    return PROM_ERROR;
+  }
+  set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, PROM_DETAIL_PATH_DIRECT);
+  return PROM_OK;
+}
+
 // The host-buffer SGEMM behind prometheus_reactor_runtime_sgemm and
 // ..._sgemm_benchmark_variant (`requested` = an OCT_B200_SGEMM_* id).
 int sgemm_host(void* handle, const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k,
@@ -776,6 +905,13 @@ int sgemm_host(void* handle, const float* a, const float* b, float* c, uint32_t 
     float* da = static_cast<float*>(rt->da.aligned());
     float* db = static_cast<float*>(rt->db.aligned());
     float* dc = static_cast<float*>(rt->dc.aligned());
+    const uint32_t variant = (rt->test_flags & PROM_TESTCFG_FORCE_STRICT_FP32) ? OCT_B200_SGEMM_FMA : requested;
+    const uint32_t exec = resolve_variant(variant, m, n, k);
+    if ((exec == OCT_B200_SGEMM_TC3XTF32 || exec == OCT_B200_SGEMM_TC_BK16) && m >= 1024 &&
+        static_cast<double>(m) * n * k >= 1.0e9 && (rt->test_flags & kTestFlagsWithHostInjection) == 0) {
+      const int pd = sgemm_host_pipelined(rt, a, b, c, m, n, k, da, db, dc, out_stage, out_detail_code);
+      return pd;
+    }
     cudaError_t e = reset_words(rt);
     if (e == cudaSuccess) e = cudaMemcpyAsync(da, a, a_n * 4, cudaMemcpyHostToDevice, rt->stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(db, b, b_n * 4, cudaMemcpyHostToDevice, rt->stream);
@@ -788,7 +924,6 @@ int sgemm_host(void* handle, const float* a, const float* b, float* c, uint32_t 
       set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_DETAIL_INJECTED_DISPATCH_FAILURE);
       return PROM_ERROR;
     }
-    const uint32_t variant = (rt->test_flags & PROM_TESTCFG_FORCE_STRICT_FP32) ? OCT_B200_SGEMM_FMA : requested;
     const int d = enqueue_sgemm(rt, da, k, db, n, dc, n, m, n, k, variant, rt->stream);
     if (d != 0) {
       cudaStreamSynchronize(rt->stream);

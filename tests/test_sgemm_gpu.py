@@ -219,6 +219,30 @@ def test_host_abi_matches_device_path(runtime, oracle_mod):
     assert np.array_equal(c_host, c_dev)
 
 
+@pytest.mark.parametrize("pinned", [False, True])
+@pytest.mark.parametrize("shape,seed", [((4097, 4095, 1023), 41), ((2048, 1024, 1024), 42), ((8192, 8192, 8192), 43)])
+def test_pipelined_host_path_matches_device_path(runtime, oracle_mod, shape, seed, pinned):
+    """Large host-buffer products upload A in row chunks, compute each chunk as it lands and
+    download C chunks while later ones compute; the result must equal the one-shot device
+    product bit for bit, from pageable and from pinned host buffers."""
+    import torch
+    o = oracle_mod
+    m, n, k = shape
+    a, b = o.uniform_matrix(m, k, seed).ravel(), o.uniform_matrix(k, n, seed + 1).ravel()
+    if pinned:
+        pa = torch.empty(a.size, dtype=torch.float32, pin_memory=True).numpy()
+        pb = torch.empty(b.size, dtype=torch.float32, pin_memory=True).numpy()
+        pc = torch.full((m * n,), float("nan"), dtype=torch.float32, pin_memory=True).numpy()
+        pa[:], pb[:] = a, b
+        c_host, st = runtime.sgemm_with_status(m, n, k, pa, pb, out=pc)
+    else:
+        c_host, st = runtime.sgemm_with_status(m, n, k, a, b)
+    assert st.ok and (st.stage, st.detail) == (R.STAGE_TRANSFER_OUT, 6101), st
+    c_dev = device_sgemm(runtime, a, b, m, n, k, R.SGEMM_AUTO)
+    assert np.array_equal(c_host, c_dev)
+    _check_against_fp64(o, c_host, a, b, m, n, k, rows=slice(m - 40, m))
+
+
 def test_leading_dimensions_column_shard(runtime, oracle_mod):
     """oct_b200_sgemm_device_ld: a column block of a wider B / C (the tensor-parallel shard)."""
     import torch
