@@ -80,17 +80,6 @@ __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.
 // (Q hi/lo are in tensor memory).
 __device__ __forceinline__ void q_ready_barrier() { asm volatile("bar.sync 1, 288;" ::: "memory"); }
 
-// True in exactly one lane of a converged warp.
-__device__ __forceinline__ bool elect_one() {
-  uint32_t pred;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "elect.sync _|p, 0xffffffff;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(pred));
-  return pred != 0;
-}
-
 // The running max of a row moves only when a key block's max exceeds it by
 // more than FA_TAU (natural-log units): probabilities then stay below e^8 in
 // fp32, and the rescale of the output sums is skipped in almost every block.

@@ -215,72 +215,79 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem_base = tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer
-      const int row_a = static_cast<int>(entry * entry_rows_a + tile_m * BM);
-      const int row_b = static_cast<int>(entry * entry_rows_b + tile_n * BN);
-      uint32_t kb = 0;
-      for (; kb < num_kb; ++kb) {
-        const uint32_t s = kb % S;
-        if (kb >= S) {
-          if (!mbar_wait(&empty_bar[s], ((kb / S) - 1) & 1u, err, kErrWaitEmpty)) {
-            atomicExch(&aborted, 1u);
-            break;
-          }
+    // ---------------- TMA producer: the warp runs the loop converged, one elected lane issues
+    const int row_a = static_cast<int>(entry * entry_rows_a + tile_m * BM);
+    const int row_b = static_cast<int>(entry * entry_rows_b + tile_n * BN);
+    uint32_t kb = 0;
+    for (; kb < num_kb; ++kb) {
+      const uint32_t s = kb % S;
+      if (kb >= S) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&empty_bar[s], ((kb / S) - 1) & 1u, err, kErrWaitEmpty))) {
+          if (lane == 0) atomicExch(&aborted, 1u);
+          break;
         }
-        if (*(volatile uint32_t*)&aborted) break;
-        uint8_t* st = smem + s * Cfg::STAGE_BYTES;
-        const int kx = static_cast<int>(kb * BK);
+      }
+      if (__any_sync(0xffffffffu, *(volatile uint32_t*)&aborted != 0u)) break;
+      uint8_t* st = smem + s * Cfg::STAGE_BYTES;
+      const int kx = static_cast<int>(kb * BK);
+      if (elect_one()) {
         mbar_arrive_expect_tx(&full_bar[s], Cfg::STAGE_BYTES);
         tma_load_2d(st, &tm_ahi, &full_bar[s], kx, row_a);
         tma_load_2d(st + Cfg::A_BYTES, &tm_alo, &full_bar[s], kx, row_a);
         tma_load_2d(st + 2 * Cfg::A_BYTES, &tm_bhi, &full_bar[s], kx, row_b);
         tma_load_2d(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tm_blo, &full_bar[s], kx, row_b);
       }
-      issued_kb = kb;
+      __syncwarp();
     }
+    if (lane == 0) issued_kb = kb;
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer
-      uint32_t kb = 0;
-      for (; kb < num_kb; ++kb) {
-        const uint32_t chunk = kb / KBC, in_chunk = kb % KBC;
-        const uint32_t buf = chunk & 1u;
-        if (in_chunk == 0 && chunk >= 2) {
-          // the epilogue must have drained chunk - 2 out of this buffer
-          if (!mbar_wait(&acc_empty[buf], ((chunk >> 1) - 1) & 1u, err, kErrWaitAccum)) {
-            atomicExch(&aborted, 1u);
-            break;
-          }
-          tc_fence_after();
-        }
-        const uint32_t s = kb % S;
-        if (!mbar_wait(&full_bar[s], (kb / S) & 1u, err, kErrWaitFull)) {
-          atomicExch(&aborted, 1u);
+    // ---------------- MMA issuer: converged warp (descriptors stay warp-uniform), one
+    // elected lane issues each tcgen05 instruction
+    uint32_t kb = 0;
+    for (; kb < num_kb; ++kb) {
+      const uint32_t chunk = kb / KBC, in_chunk = kb % KBC;
+      const uint32_t buf = chunk & 1u;
+      if (in_chunk == 0 && chunk >= 2) {
+        // the epilogue must have drained chunk - 2 out of this buffer
+        if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], ((chunk >> 1) - 1) & 1u, err, kErrWaitAccum))) {
+          if (lane == 0) atomicExch(&aborted, 1u);
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
-        const uint32_t base = smem_addr(smem + s * Cfg::STAGE_BYTES);
-        const uint32_t a_hi = base, a_lo = base + Cfg::A_BYTES;
-        const uint32_t b_hi = base + 2 * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
+      }
+      const uint32_t s = kb % S;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[s], (kb / S) & 1u, err, kErrWaitFull))) {
+        if (lane == 0) atomicExch(&aborted, 1u);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * BN;
+      const uint32_t base = smem_addr(smem + s * Cfg::STAGE_BYTES);
+      const uint32_t a_hi = base, a_lo = base + Cfg::A_BYTES;
+      const uint32_t b_hi = base + 2 * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
 #pragma unroll
-        for (uint32_t kk = 0; kk < BK / 8; ++kk) {
-          const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K
-          const uint64_t dah = umma_desc_kmajor(a_hi + off, Cfg::SWZ);
-          const uint64_t dal = umma_desc_kmajor(a_lo + off, Cfg::SWZ);
-          const uint64_t dbh = umma_desc_kmajor(b_hi + off, Cfg::SWZ);
-          const uint64_t dbl = umma_desc_kmajor(b_lo + off, Cfg::SWZ);
+      for (uint32_t kk = 0; kk < BK / 8; ++kk) {
+        const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K
+        const uint64_t dah = umma_desc_kmajor(a_hi + off, Cfg::SWZ);
+        const uint64_t dal = umma_desc_kmajor(a_lo + off, Cfg::SWZ);
+        const uint64_t dbh = umma_desc_kmajor(b_hi + off, Cfg::SWZ);
+        const uint64_t dbl = umma_desc_kmajor(b_lo + off, Cfg::SWZ);
+        if (elect_one()) {
           umma_tf32(d_tmem, dal, dbh, IDESC, (in_chunk | kk) != 0u ? 1u : 0u);
           umma_tf32(d_tmem, dah, dbl, IDESC, 1u);
           umma_tf32(d_tmem, dah, dbh, IDESC, 1u);
         }
+        __syncwarp();
+      }
+      if (elect_one()) {
         umma_commit(&empty_bar[s]);  // frees the smem stage when these MMAs finish
         if (in_chunk == KBC - 1 || kb == num_kb - 1) umma_commit(&acc_full[buf]);
       }
-      consumed_kb = kb;
-      umma_commit(&drain_bar);  // arrives when every MMA issued above has completed
+      __syncwarp();
     }
+    if (lane == 0) consumed_kb = kb;
+    if (elect_one()) umma_commit(&drain_bar);  // arrives when every MMA issued above has completed
+    __syncwarp();
   } else {
     // ---------------- epilogue: warps 2..9; (warp % 4) owns a TMEM lane quarter,
     // (warp - 2) / 4 selects which 128 of the 256 columns this warp sums.
