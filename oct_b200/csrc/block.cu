@@ -19,9 +19,10 @@
 // Data path per forward (T = batch * seq tokens, all buffers owned by the block):
 //   norms, RoPE, softmax and gated activations are one-pass fused kernels; the
 //   residual adds of the Gemma block ride in the GEMM epilogue; weights are
-//   split to TF32 hi/lo once, at upload.  Attention materialises the scores of
-//   one sequence's heads (B*H*S*S floats, 3.2 GB for the DiT config) and runs
-//   Q K^T and P V as strided-batched tensor-core products.
+//   split to TF32 hi/lo once, at upload.  DiT attention is one fused kernel
+//   (attention.cu); the Gemma (causal, head 256) attention materialises the
+//   scores of every (item, head) and runs Q K^T and P V as strided-batched
+//   tensor-core products.
 //   Tensor parallel (tp_world > 1): each rank holds H/tp heads and F/tp FFN
 //   columns; the two row-parallel products (out projection, down/W2) produce
 //   partial sums that are all-reduced over NCCL on the block's stream.
@@ -554,7 +555,7 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
     vtsplit_ = alloc(2 * e);
     ok = ok && qsplit_ && ksplit_ && vtsplit_;
   } else {
-    scores_ = alloc(static_cast<uint64_t>(d.heads) * d.seq_len * d.seq_len);  // one batch item at a time
+    scores_ = alloc(static_cast<uint64_t>(d.max_batch) * d.heads * d.seq_len * d.seq_len);
     ok = ok && scores_;
   }
   attn_ = alloc(T * attn_cols);
@@ -567,7 +568,7 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
     const SplitDims pd = split_dims(d.seq_len, d.head_dim, d.seq_len);
     p_mp_ = pd.mp;
     p_kp_ = pd.kp;
-    const uint64_t pe = static_cast<uint64_t>(d.heads) * pd.mp * pd.kp;
+    const uint64_t pe = static_cast<uint64_t>(d.max_batch) * d.heads * pd.mp * pd.kp;
     psplit_ = alloc(2 * pe);
     if (psplit_ == nullptr || cudaMemsetAsync(psplit_, 0, 2 * pe * sizeof(float), stream_) != cudaSuccess) return -3;
   }
@@ -576,8 +577,8 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
   const SplitDims vd = split_dims(1, d.head_dim, d.seq_len);  // V split of the P V product
   const uint64_t b_need =
       fused_attn_ ? 0
-                  : std::max(sgemm_tc_scratch_bytes(d.seq_len, d.seq_len, d.head_dim, d.heads),
-                             static_cast<uint64_t>(2ull * sizeof(float) * d.heads * vd.np * vd.kp));
+                  : std::max(sgemm_tc_scratch_bytes(d.seq_len, d.seq_len, d.head_dim, d.max_batch * d.heads),
+                             static_cast<uint64_t>(2ull * sizeof(float) * d.max_batch * d.heads * vd.np * vd.kp));
   scratch_ = alloc(std::max(a_need, b_need) / sizeof(float) + 1);
   err_ = reinterpret_cast<unsigned int*>(alloc(4));
   ok = ok && hbuf_ && qkv_ && attn_ && x1_ && proj_ && gu_ && act_ && scratch_ && err_;
@@ -712,32 +713,44 @@ cudaError_t Block::all_reduce(float* buf, uint64_t count) {
 }
 
 // Attention of one batch item: scores = Q K^T per head (batched), softmax, O = P V.
-cudaError_t Block::attention(uint32_t item, uint64_t ldq, uint32_t k_col, uint32_t v_col, bool shared_kv) {
+// Materialised attention of every batch item at once: scores = Q K^T for each
+// (item, head) entry as one strided-batched product, one softmax launch over all
+// score rows, O = P V as one batched product.  Entry e = item * heads + head:
+// operands step by head inside an item (stride) and by item (outer).
+cudaError_t Block::attention(uint32_t batch, uint64_t ldq, uint32_t k_col, uint32_t v_col, bool shared_kv) {
   const BlockDims& d = dims_;
   const uint64_t S = d.seq_len, hd = d.head_dim;
-  const float* base = qkv_ + item * S * ldq;
-  float* sc = scores_;
+  const uint32_t entries = batch * d.heads;
   GemmBatch qk;
-  qk.count = d.heads;
+  qk.count = entries;
+  qk.inner = d.heads;
   qk.stride_a = hd;
+  qk.outer_a = S * ldq;
   qk.stride_b = shared_kv ? 0 : hd;
+  qk.outer_b = S * ldq;
   qk.stride_c = S * S;
+  qk.outer_c = static_cast<uint64_t>(d.heads) * S * S;
   qk.b_trans = true;
-  cudaError_t e = sgemm_tc(base, ldq, base + k_col, ldq, sc, S, S, S, hd, scratch_, err_, 16, stream_, nullptr, &qk);
+  cudaError_t e = sgemm_tc(qkv_, ldq, qkv_ + k_col, ldq, scores_, S, S, S, hd, scratch_, err_, 16, stream_, nullptr,
+                           &qk);
   if (e != cudaSuccess) return e;
-  const uint64_t pe = static_cast<uint64_t>(d.heads) * p_mp_ * p_kp_;
-  attn_softmax_split_kernel<<<grid_for(d.heads * S, 1), NT, 0, stream_>>>(
-      sc, d.heads * S, S, S, 1.0f / std::sqrt(static_cast<float>(hd)), d.family == kGemma ? 1 : 0, psplit_,
-      psplit_ + pe, p_mp_, p_kp_);
+  const uint64_t pe = static_cast<uint64_t>(d.max_batch) * d.heads * p_mp_ * p_kp_;  // one of P hi / P lo
+  const uint64_t rows = static_cast<uint64_t>(entries) * S;
+  attn_softmax_split_kernel<<<grid_for(rows, 1), NT, 0, stream_>>>(
+      scores_, static_cast<uint32_t>(rows), S, S, 1.0f / std::sqrt(static_cast<float>(hd)),
+      d.family == kGemma ? 1 : 0, psplit_, psplit_ + pe, p_mp_, p_kp_);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   GemmBatch pv;
-  pv.count = d.heads;
+  pv.count = entries;
+  pv.inner = d.heads;
   pv.stride_b = shared_kv ? 0 : hd;
-  pv.stride_c = hd;
+  pv.outer_b = S * ldq;
   const uint64_t ldo = static_cast<uint64_t>(d.heads) * hd;
-  return sgemm_tc_presplit_a(psplit_, psplit_ + pe, base + v_col, ldq, attn_ + item * S * ldo, ldo, S, hd, S,
-                             scratch_, err_, stream_, &pv);
+  pv.stride_c = hd;
+  pv.outer_c = S * ldo;
+  return sgemm_tc_presplit_a(psplit_, psplit_ + pe, qkv_ + v_col, ldq, attn_, ldo, S, hd, S, scratch_, err_, stream_,
+                             &pv);
 }
 
 int Block::forward(const float* x, float* y, uint32_t batch, const float* timesteps_host) {
@@ -782,8 +795,7 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
     rope_half_kernel<<<grid_for(rope_work, NT), NT, 0, stream_>>>(qkv_, qkv_cols, 0, d.heads + d.kv_heads,
                                                                  d.head_dim, rope_cos_, rope_sin_, d.seq_len, T);
     if (!ok()) return -4;
-    for (uint32_t b = 0; b < batch && e == cudaSuccess; ++b)
-      e = attention(b, qkv_cols, attn_cols, attn_cols + d.kv_heads * d.head_dim, true);
+    e = attention(batch, qkv_cols, attn_cols, attn_cols + d.kv_heads * d.head_dim, true);
     if (!ok()) return -4;
     if (tpf) {
       // partial O Wo rows -> their owners; owners: x1 = x + sum, h = RMSNorm(x1) -> every rank
@@ -873,8 +885,7 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
     e = flash_attention_tf32x3(ops, attn_, attn_cols, batch, d.heads, d.seq_len,
                                1.0f / std::sqrt(static_cast<float>(d.head_dim)), err_, stream_);
   } else {
-    for (uint32_t b = 0; b < batch && e == cudaSuccess; ++b)
-      e = attention(b, qkv_cols, attn_cols, 2 * attn_cols, false);
+    e = attention(batch, qkv_cols, attn_cols, 2 * attn_cols, false);
   }
   if (!ok()) return -4;
   if (tpf) {

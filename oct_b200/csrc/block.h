@@ -67,7 +67,7 @@ class Block {
   int build_rope_tables();
   cudaError_t gemm(const float* a, uint64_t lda, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
                    const float* residual = nullptr, uint64_t ldr = 0, const RowScatter* scatter = nullptr);
-  cudaError_t attention(uint32_t item, uint64_t ldq, uint32_t k_col, uint32_t v_col, bool shared_kv);
+  cudaError_t attention(uint32_t batch, uint64_t ldq, uint32_t k_col, uint32_t v_col, bool shared_kv);
   cudaError_t all_reduce(float* buf, uint64_t count);
   // tensor parallel over peer memory (tp_fused.cu)
   float* sym_alloc(uint64_t floats);
@@ -87,7 +87,7 @@ class Block {
   float *rope_cos_ = nullptr, *rope_sin_ = nullptr;
   float *hbuf_ = nullptr, *qkv_ = nullptr, *scores_ = nullptr, *attn_ = nullptr, *x1_ = nullptr, *proj_ = nullptr;
   float *gu_ = nullptr, *act_ = nullptr, *scratch_ = nullptr;
-  float* psplit_ = nullptr;  // attention probabilities, TF32 hi then lo, [heads][p_mp_][p_kp_]
+  float* psplit_ = nullptr;  // attention probabilities, TF32 hi then lo, [max_batch*heads][p_mp_][p_kp_]
   uint32_t p_mp_ = 0, p_kp_ = 0;
   // fused attention (DiT, head_dim 128): Q, K, V^T split to TF32 hi/lo per head
   bool fused_attn_ = false;

@@ -23,10 +23,28 @@ uint64_t sgemm_tc_scratch_bytes(uint32_t m, uint32_t n, uint32_t k, uint32_t bat
 // Strided batch of independent products C_i = A_i * op(B_i), i < count, with
 // X_i = X + i * stride_x (element strides; a stride of 0 shares the operand).
 // b_trans: B is given as [n][k] row-major and op(B) = B^T (the "NT" product).
+// Element offset of batch entry e: e * stride, or, with inner > 0, a two-level
+// index (e / inner) * outer + (e % inner) * stride (e.g. entry = item * heads + head).
+struct EntryStride {
+  uint64_t stride = 0;
+  uint32_t inner = 0;
+  uint64_t outer = 0;
+  __host__ __device__ uint64_t at(uint32_t e) const {
+    return inner != 0 ? static_cast<uint64_t>(e / inner) * outer + static_cast<uint64_t>(e % inner) * stride
+                      : static_cast<uint64_t>(e) * stride;
+  }
+};
+
 struct GemmBatch {
   uint32_t count = 1;
   uint64_t stride_a = 0, stride_b = 0, stride_c = 0;
   bool b_trans = false;
+  // optional second level: entry e = (e / inner, e % inner); outer_* step the first index
+  uint32_t inner = 0;
+  uint64_t outer_a = 0, outer_b = 0, outer_c = 0;
+  EntryStride sa() const { return EntryStride{stride_a, inner, outer_a}; }
+  EntryStride sb() const { return EntryStride{stride_b, inner, outer_b}; }
+  EntryStride sc() const { return EntryStride{stride_c, inner, outer_c}; }
 };
 
 // Tensor-core kernel configurations: one CTA per 128 x 256 tile, or a CTA pair

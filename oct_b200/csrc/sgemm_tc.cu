@@ -63,12 +63,12 @@ __host__ __device__ inline uint32_t round_up(uint32_t x, uint32_t g) { return (x
 // ------------------------------------------------------------------ split
 // hi = tf32(v), lo = tf32(v - hi); v = 0 outside [rows, cols).
 // Each thread produces 4 consecutive padded columns of one row.
-// blockIdx.y selects the batch entry: src + y * src_stride, outputs + y * rows_p * cols_p.
+// blockIdx.y selects the batch entry: src + src_stride.at(y), outputs + y * rows_p * cols_p.
 __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ src, uint64_t ld,
                                                          uint32_t rows, uint32_t cols,
                                                          float* __restrict__ hi, float* __restrict__ lo,
-                                                         uint32_t rows_p, uint32_t cols_p, uint64_t src_stride) {
-  src += blockIdx.y * src_stride;
+                                                         uint32_t rows_p, uint32_t cols_p, EntryStride src_stride) {
+  src += src_stride.at(blockIdx.y);
   hi += static_cast<uint64_t>(blockIdx.y) * rows_p * cols_p;
   lo += static_cast<uint64_t>(blockIdx.y) * rows_p * cols_p;
   const uint64_t groups_per_row = cols_p / 4;
@@ -104,13 +104,13 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
 
 // B is [k x n] row-major; writes hi/lo of B^T as [n_p x k_p] (K-major), zero padded.
 // 32x32 tiles through shared memory keep both the read and the write coalesced.
-// blockIdx.z selects the batch entry: b + z * b_stride, outputs + z * np * kp.
+// blockIdx.z selects the batch entry: b + b_stride.at(z), outputs + z * np * kp.
 __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ b, uint64_t ldb,
                                                               uint32_t k, uint32_t n,
                                                               float* __restrict__ hi, float* __restrict__ lo,
-                                                              uint32_t kp, uint32_t np, uint64_t b_stride) {
+                                                              uint32_t kp, uint32_t np, EntryStride b_stride) {
   __shared__ float tile[32][33];
-  b += blockIdx.z * b_stride;
+  b += b_stride.at(blockIdx.z);
   hi += static_cast<uint64_t>(blockIdx.z) * np * kp;
   lo += static_cast<uint64_t>(blockIdx.z) * np * kp;
   const uint32_t n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
                    float* __restrict__ c, uint32_t m, uint32_t n, uint64_t ldc, uint32_t num_kb,
                    uint32_t tiles_m, uint32_t tiles_n, uint32_t entry_rows_a, uint32_t entry_rows_b,
-                   uint64_t stride_c, const float* __restrict__ residual, uint64_t ldr,
+                   EntryStride stride_c, const float* __restrict__ residual, uint64_t ldr,
                    unsigned int* __restrict__ err, const RowScatter scatter) {
   using Cfg = TileCfg<BK>;
   constexpr uint32_t S = Cfg::STAGES;
@@ -182,8 +182,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t group_rows = min(tiles_m - first_m, GROUP_M);
   const uint32_t tile_m = first_m + (t % per_group) % group_rows;
   const uint32_t tile_n = (t % per_group) / group_rows;
-  c += entry * stride_c;
-  if (residual != nullptr) residual += entry * stride_c;
+  c += stride_c.at(entry);
+  if (residual != nullptr) residual += stride_c.at(entry);
 
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < S; ++s) {
@@ -431,7 +431,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                         const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
                         float* __restrict__ c, uint32_t m, uint32_t n, uint64_t ldc, uint32_t num_kb,
                         uint32_t tiles_m, uint32_t tiles_n, uint32_t entry_rows_a, uint32_t entry_rows_b,
-                        uint64_t stride_c, const float* __restrict__ residual, uint64_t ldr,
+                        EntryStride stride_c, const float* __restrict__ residual, uint64_t ldr,
                         unsigned int* __restrict__ err) {
   using Cfg = PairCfg<BK>;
   constexpr uint32_t S = Cfg::STAGES;
@@ -462,8 +462,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const uint32_t group_rows = min(tiles_m - first_m, GROUP_M);
   const uint32_t tile_m = first_m + (t % per_group) % group_rows;
   const uint32_t tile_n = (t % per_group) / group_rows;
-  c += entry * stride_c;
-  if (residual != nullptr) residual += entry * stride_c;
+  c += stride_c.at(entry);
+  if (residual != nullptr) residual += stride_c.at(entry);
 
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < S; ++s) {
@@ -647,7 +647,7 @@ bool make_operand_map(CUtensorMap* map, const float* base, uint32_t rows, uint32
 template <int BK>
 cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
                         uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
-                        cudaStream_t stream, uint32_t batch, uint64_t stride_c, const float* residual = nullptr,
+                        cudaStream_t stream, uint32_t batch, EntryStride stride_c, const float* residual = nullptr,
                         uint64_t ldr = 0, const RowScatter* scatter = nullptr) {
   using Cfg = TileCfg<BK>;
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
@@ -674,7 +674,7 @@ cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, co
 template <int BK>
 cudaError_t launch_pair(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
                         uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
-                        cudaStream_t stream, uint32_t batch, uint64_t stride_c, const float* residual = nullptr,
+                        cudaStream_t stream, uint32_t batch, EntryStride stride_c, const float* residual = nullptr,
                         uint64_t ldr = 0) {
   using Cfg = PairCfg<BK>;
   if (d.mp % PAIR_BM != 0) return cudaErrorInvalidValue;
@@ -699,7 +699,7 @@ cudaError_t launch_pair(const float* ahi, const float* alo, const float* bhi, co
 
 cudaError_t launch_config(int cfg, const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
                           uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
-                          cudaStream_t stream, uint32_t batch, uint64_t stride_c, const float* residual = nullptr,
+                          cudaStream_t stream, uint32_t batch, EntryStride stride_c, const float* residual = nullptr,
                           uint64_t ldr = 0, const RowScatter* scatter = nullptr) {
   // the CTA-pair kernels have no row-scatter epilogue
   if (scatter != nullptr && scatter->dst != nullptr && cfg != kTcSingle16 && cfg != kTcSingle32)
@@ -741,7 +741,7 @@ cudaError_t sgemm_tc_split_b(const float* b, uint64_t ldb, uint32_t k, uint32_t 
                              cudaStream_t stream) {
   if (k == 0 || n == 0) return cudaSuccess;
   const SplitDims d = split_dims(1, n, k);
-  split_transpose_kernel<<<dim3(d.np / 32, d.kp / 32, 1), 256, 0, stream>>>(b, ldb, k, n, bhi, blo, d.kp, d.np, 0);
+  split_transpose_kernel<<<dim3(d.np / 32, d.kp / 32, 1), 256, 0, stream>>>(b, ldb, k, n, bhi, blo, d.kp, d.np, EntryStride{});
   return cudaGetLastError();
 }
 
@@ -761,10 +761,10 @@ cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, co
   float* alo = ahi + static_cast<uint64_t>(d.mp) * d.kp;
   const uint64_t groups = static_cast<uint64_t>(d.mp) * (d.kp / 4);
   const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((groups + 255) / 256, 148ull * 16));
-  split_rows_kernel<<<dim3(blocks, 1), 256, 0, stream>>>(a, lda, m, k, ahi, alo, d.mp, d.kp, 0);
+  split_rows_kernel<<<dim3(blocks, 1), 256, 0, stream>>>(a, lda, m, k, ahi, alo, d.mp, d.kp, EntryStride{});
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, 0, residual, ldr, scatter);
+  return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, EntryStride{}, residual, ldr, scatter);
 }
 
 // A operand already in the split layout (hi/lo, [count][Mp][Kp], zero padded),
@@ -786,14 +786,14 @@ cudaError_t sgemm_tc_presplit_a(const float* ahi, const float* alo, const float*
   if (bt.b_trans) {
     const uint64_t bgroups = static_cast<uint64_t>(d.np) * (d.kp / 4);
     const uint32_t bblocks = static_cast<uint32_t>(std::min<uint64_t>((bgroups + 255) / 256, 148ull * 16));
-    split_rows_kernel<<<dim3(bblocks, bt.count), 256, 0, stream>>>(b, ldb, n, k, bhi, blo, d.np, d.kp, bt.stride_b);
+    split_rows_kernel<<<dim3(bblocks, bt.count), 256, 0, stream>>>(b, ldb, n, k, bhi, blo, d.np, d.kp, bt.sb());
   } else {
     split_transpose_kernel<<<dim3(d.np / 32, d.kp / 32, bt.count), 256, 0, stream>>>(b, ldb, k, n, bhi, blo, d.kp,
-                                                                                     d.np, bt.stride_b);
+                                                                                     d.np, bt.sb());
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.stride_c);
+  return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.sc());
 }
 
 // ------------------------------------------------------------------ no-allocation variant
@@ -860,22 +860,22 @@ cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb,
   if (events != nullptr && events->split_begin != nullptr) cudaEventRecord(events->split_begin, stream);
   const uint64_t groups = static_cast<uint64_t>(d.mp) * (d.kp / 4);
   const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((groups + 255) / 256, 148ull * 16));
-  split_rows_kernel<<<dim3(blocks, bt.count), 256, 0, stream>>>(a, lda, m, k, ahi, alo, d.mp, d.kp, bt.stride_a);
+  split_rows_kernel<<<dim3(blocks, bt.count), 256, 0, stream>>>(a, lda, m, k, ahi, alo, d.mp, d.kp, bt.sa());
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (bt.b_trans) {
     // B is [n][k]: already K-major, split it like A.
     const uint64_t bgroups = static_cast<uint64_t>(d.np) * (d.kp / 4);
     const uint32_t bblocks = static_cast<uint32_t>(std::min<uint64_t>((bgroups + 255) / 256, 148ull * 16));
-    split_rows_kernel<<<dim3(bblocks, bt.count), 256, 0, stream>>>(b, ldb, n, k, bhi, blo, d.np, d.kp, bt.stride_b);
+    split_rows_kernel<<<dim3(bblocks, bt.count), 256, 0, stream>>>(b, ldb, n, k, bhi, blo, d.np, d.kp, bt.sb());
   } else {
     split_transpose_kernel<<<dim3(d.np / 32, d.kp / 32, bt.count), 256, 0, stream>>>(b, ldb, k, n, bhi, blo, d.kp,
-                                                                                     d.np, bt.stride_b);
+                                                                                     d.np, bt.sb());
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (events != nullptr && events->main_begin != nullptr) cudaEventRecord(events->main_begin, stream);
-  e = launch_config(bk, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.stride_c);
+  e = launch_config(bk, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, bt.count, bt.sc());
   if (events != nullptr && events->main_end != nullptr) cudaEventRecord(events->main_end, stream);
   return e;
 }
