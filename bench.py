@@ -243,6 +243,27 @@ def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
     # Transformer blocks at BASELINE configs[3] / configs[4] (random init, synthetic tokens)
     out.extend(block_measurements(rt, torch, stream))
     out.extend(attention_measurements(rt, torch, stream))
+    # small-M products (Gemma per-token shapes): HBM-bound on B
+    for (m, n, k) in ((1, 16384, 2048), (8, 16384, 2048), (16, 8192, 4096)):  # B = 134 MB > L2
+        g = torch.Generator(device="cuda").manual_seed(11)
+        a = torch.rand(m, k, device="cuda", generator=g) * 2 - 1
+        b = torch.rand(k, n, device="cuda", generator=g) * 2 - 1
+        c = torch.empty(m, n, device="cuda")
+        for _ in range(3):
+            rt.sgemm_device(a, b, c, m, n, k, R.SGEMM_AUTO, stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        iters = 20
+        e0.record(stream)
+        for _ in range(iters):
+            rt.sgemm_device(a, b, c, m, n, k, R.SGEMM_AUTO, stream)
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        nbytes = 4 * (k * n + m * k + m * n)
+        out.append({"kernel": "sgemm_smallm", "m": m, "n": n, "k": k, "ms": round(ms, 4),
+                    "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1), "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 /
+                                                                                       hbm_peak, 3),
+                    "bytes": nbytes, "l2": "B larger than L2, no flush"})
     # FMA control and the 32-deep tensor-core variant at the headline shape
     m = n = k = 8192
     g = torch.Generator(device="cuda").manual_seed(7)

@@ -672,9 +672,10 @@ PROM_REACTOR_API int prometheus_runtime_probe(void* handle, PrometheusCaps* out_
 
 /* SGEMM kernel variants. */
 enum {
-  OCT_B200_SGEMM_AUTO = 0u,       /* 3xTF32 tcgen05 for large shapes, FMA for tiny ones */
+  OCT_B200_SGEMM_AUTO = 0u,       /* small-M kernel for m <= 16, else 3xTF32 tcgen05; FMA for tiny products */
   OCT_B200_SGEMM_TC3XTF32 = 1u,   /* tcgen05/TMEM tensor cores, split-TF32 x3 */
   OCT_B200_SGEMM_FMA = 2u,        /* plain FP32 FMA on the CUDA cores (control) */
+  OCT_B200_SGEMM_SMALLM = 3u,     /* m <= 16: HBM-bound CUDA-core kernel, split-K, ordered reduction */
   OCT_B200_SGEMM_TC_BK16 = 16u,   /* tensor cores, one CTA per 128x256 tile, 16-deep K stages */
   OCT_B200_SGEMM_TC_BK32 = 32u,   /* tensor cores, one CTA per 128x256 tile, 32-deep K stages */
   OCT_B200_SGEMM_TC_PAIR16 = 216u, /* tensor cores, CTA pair (cta_group::2) per 256x256 tile, 16-deep */

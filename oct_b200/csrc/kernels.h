@@ -158,6 +158,14 @@ struct TpReduce {
 };
 cudaError_t tp_reduce_rows(const TpReduce& args, cudaStream_t stream);
 
+// Small-M fp32 SGEMM (1 <= m <= 16): HBM-bound on B, CUDA-core FMA, split-K with
+// an ordered reduction of the partials (sgemm_smallm.cu).  `scratch` must hold
+// sgemm_smallm_scratch_bytes (may be 0 bytes: then it may be null).
+bool sgemm_smallm_supported(uint32_t m);
+uint64_t sgemm_smallm_scratch_bytes(uint32_t m, uint32_t n, uint32_t k);
+cudaError_t sgemm_smallm(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
+                         uint32_t m, uint32_t n, uint32_t k, void* scratch, cudaStream_t stream);
+
 // ---------------------------------------------------------------- reductions
 // op: 1 = row sum, 2 = row max, 3 = stable softmax.  `nonfinite` (device
 // u64, preset to UINT64_MAX by the caller) receives the smallest flat index of

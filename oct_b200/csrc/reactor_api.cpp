@@ -183,17 +183,20 @@ const oct::SgemmEvents* next_timing_events(Runtime* rt) {
 // Enqueues C = A * B for device pointers; chooses the kernel.
 bool known_variant(uint32_t v) {
   return v == OCT_B200_SGEMM_AUTO || v == OCT_B200_SGEMM_TC3XTF32 || v == OCT_B200_SGEMM_FMA ||
+         v == OCT_B200_SGEMM_SMALLM ||
          v == OCT_B200_SGEMM_TC_BK16 || v == OCT_B200_SGEMM_TC_BK32 || v == OCT_B200_SGEMM_TC_PAIR16 ||
          v == OCT_B200_SGEMM_TC_PAIR32;
 }
 
-// The kernel a variant id runs for (m, n, k): AUTO picks the FMA control for
-// tiny products (they do not fill one 128x256 tensor-core tile usefully, and the
-// control is exact-tail by construction), else the 3xTF32 tensor-core kernel.
+// The kernel a variant id runs for (m, n, k): AUTO picks the small-M kernel for
+// m <= 16 (the product reads B once from HBM and has almost no arithmetic per
+// byte), the FMA control for other tiny products (they do not fill one 128x256
+// tensor-core tile usefully), else the 3xTF32 tensor-core kernel.
 uint32_t resolve_variant(uint32_t variant, uint32_t m, uint32_t n, uint32_t k) {
   if (variant != OCT_B200_SGEMM_AUTO) return variant;
+  if (oct::sgemm_smallm_supported(m)) return OCT_B200_SGEMM_SMALLM;
   const double work = static_cast<double>(m) * n * k;
-  return (work < 4.0e6 || m < 16) ? OCT_B200_SGEMM_FMA : OCT_B200_SGEMM_TC3XTF32;
+  return work < 4.0e6 ? OCT_B200_SGEMM_FMA : OCT_B200_SGEMM_TC3XTF32;
 }
 
 // `scratch` (default: the handle's) holds the TF32 split operands; calls that
@@ -203,8 +206,15 @@ int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uin
                   const oct::GemmBatch* batch = nullptr, DevBuf* scratch = nullptr) {
   variant = resolve_variant(variant, m, n, k);
   if (scratch == nullptr) scratch = &rt->scratch;
+  // the small-M kernel has no batched form: strided batches take the FMA control
+  if (variant == OCT_B200_SGEMM_SMALLM && batch != nullptr && batch->count > 1) variant = OCT_B200_SGEMM_FMA;
   cudaError_t e;
-  if (variant == OCT_B200_SGEMM_FMA) {
+  if (variant == OCT_B200_SGEMM_SMALLM) {
+    if (!oct::sgemm_smallm_supported(m)) return OCT_B200_DETAIL_UNSUPPORTED_SHAPE;
+    const uint64_t need = oct::sgemm_smallm_scratch_bytes(m, n, k);
+    if (need != 0 && scratch->ensure(need, stream) != cudaSuccess) return OCT_B200_DETAIL_OUT_OF_MEMORY;
+    e = oct::sgemm_smallm(a, lda, b, ldb, c, ldc, m, n, k, need != 0 ? scratch->aligned() : nullptr, stream);
+  } else if (variant == OCT_B200_SGEMM_FMA) {
     e = oct::sgemm_fma(a, lda, b, ldb, c, ldc, m, n, k, stream, batch);
   } else if (variant == OCT_B200_SGEMM_TC3XTF32 || variant == 16u || variant == 32u || variant == 216u ||
              variant == 232u) {
@@ -1093,7 +1103,8 @@ int prometheus_reactor_runtime_sgemm_resident_benchmark(void* handle,
     out->requested_variant = explicit_variant ? r->requested_variant : 0u;
     out->production_selected_variant = resolve_variant(OCT_B200_SGEMM_AUTO, m, n, k);
     out->executed_variant = resolve_variant(requested, m, n, k);
-    out->executed_compute_mode = out->executed_variant == OCT_B200_SGEMM_FMA ? 2u : 1u;
+    out->executed_compute_mode =
+        (out->executed_variant == OCT_B200_SGEMM_FMA || out->executed_variant == OCT_B200_SGEMM_SMALLM) ? 2u : 1u;
 
     auto fail_final = [&](uint32_t stage, int detail) {
       cudaStreamSynchronize(st);

@@ -61,7 +61,7 @@ DETAIL_ASYNC_QUEUE_FULL = -6117
 
 OP_SUM, OP_MAX, OP_SOFTMAX = 1, 2, 3
 FINALIZATION_NONE, FINALIZATION_STABLE_SOFTMAX = 0, 1
-SGEMM_AUTO, SGEMM_TC3XTF32, SGEMM_FMA = 0, 1, 2
+SGEMM_AUTO, SGEMM_TC3XTF32, SGEMM_FMA, SGEMM_SMALLM = 0, 1, 2, 3
 SGEMM_TC_BK16, SGEMM_TC_BK32 = 16, 32  # explicit tensor-core stage depths, one CTA per tile
 SGEMM_TC_PAIR16, SGEMM_TC_PAIR32 = 216, 232  # CTA-pair (cta_group::2) 256x256 tiles
 

@@ -131,6 +131,34 @@ def test_gemma_small_m_corpus(runtime, oracle_mod, golden, shape, variant):
         assert normwise(c, want[: mm * n].astype(np.float64)) <= NORMWISE_TOL
 
 
+@pytest.mark.parametrize("shape", [(1, 256, 1536), (2, 256, 1536), (7, 256, 1536), (15, 256, 1536),
+                                   (16, 256, 1536), (15, 2048, 1536), (16, 16384, 2048), (1, 16384, 2048),
+                                   (9, 1001, 777), (3, 5, 7), (16, 3, 40000)])
+def test_small_m_kernel(runtime, oracle_mod, golden, shape):
+    """The small-M kernel (m <= 16, split-K with an ordered reduction): the reference's small-M
+    corpus shapes (gemma4e2b_sgemm_corpus_test.go:44-59), Gemma per-token shapes, ragged and
+    deep-K ones; AUTO takes it for m <= 16; repeat calls are bit-identical."""
+    o = oracle_mod
+    m, n, k = shape
+    a, b = o.uniform_matrix(m, k, m + n).ravel(), o.uniform_matrix(k, n, k).ravel()
+    c = device_sgemm(runtime, a, b, m, n, k, R.SGEMM_SMALLM)
+    _check_against_fp64(o, c, a, b, m, n, k)
+    assert np.array_equal(c, device_sgemm(runtime, a, b, m, n, k, R.SGEMM_AUTO))
+    assert np.array_equal(c, device_sgemm(runtime, a, b, m, n, k, R.SGEMM_SMALLM))
+    if (m, n, k) == (15, 256, 1536):  # the corpus inputs and their golden answer
+        ga, gb = o.gemma_corpus_a(15 * 1536), o.gemma_corpus_b(1536 * 256)
+        c = device_sgemm(runtime, ga, gb, 15, 256, 1536, R.SGEMM_SMALLM)
+        assert o.compare_against_oracle(o.cpu_sgemm_f32(ga, gb, 15, 256, 1536), c).pass_ == 1
+
+
+def test_small_m_kernel_rejects_larger_m(runtime):
+    import torch
+    x = torch.zeros((17, 8), device="cuda")
+    with pytest.raises(R.ReactorIssue, match="detail=-7007"):
+        runtime.sgemm_device(x, torch.zeros((8, 8), device="cuda"), torch.zeros((17, 8), device="cuda"), 17, 8, 8,
+                             R.SGEMM_SMALLM)
+
+
 def _check_against_fp64(o, c, a, b, m, n, k, rows=None):
     sl = rows or slice(0, m)
     ref64 = o.sgemm_f64(a, b, m, n, k, rows=sl)
