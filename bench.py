@@ -370,58 +370,77 @@ def block_measurements(rt, torch, stream, iters: int = 5, only: str | None = Non
 
 
 def tp_block_measurements(rt, torch, dist, rank: int, world: int, stream, iters: int = 5) -> list[dict]:
-    """Gemma / DiT blocks tensor-parallel over all ranks (NCCL inside the block): global tokens/s."""
+    """Gemma / DiT blocks over all ranks, global tokens/s: pure tensor parallel (tp = world), and
+    tensor parallel within groups of ranks plus data parallel across the groups (each group runs
+    its share of the batch) when the batch divides."""
+    from oracle import blocks as OB  # shapes and flop counts only
+    res = []
+    for name, cfg, batch in (("gemma_block", OB.gemma_config(), 4), ("dit_block", OB.dit_config(), 2)):
+        layouts = [world]
+        dp = max(d for d in range(1, world + 1) if world % d == 0 and batch % d == 0 and world // d >= 2)
+        if dp > 1:
+            layouts.append(world // dp)
+        for tp_size in layouts:
+            r = _block_group_measure(rt, torch, dist, rank, world, stream, iters, name, cfg, batch, tp_size)
+            if r is not None:
+                res.append(r)
+    return res
+
+
+def _block_group_measure(rt, torch, dist, rank, world, stream, iters, name, cfg, batch, tp_size):
     from oct_b200 import reactor as R
     from oct_b200 import tp
-    from oracle import blocks as OB  # shapes and flop counts only
+    from oracle import blocks as OB
+    if cfg.heads % tp_size or cfg.ffn % tp_size:
+        return None
     pk, _ = peaks()
     peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
-    res = []
-    for name, cfg, batch in (("gemma_block_tp", OB.gemma_config(), 4), ("dit_block_tp", OB.dit_config(), 2)):
-        if cfg.heads % world or cfg.ffn % world:
-            continue
-        rcfg = tp.rank_config(cfg, rank, world)
-        fam = R.BLOCK_GEMMA if cfg.family == OB.GEMMA else R.BLOCK_DIT
-        # one NCCL unique id seeds exactly one communicator: a fresh id per block
-        ids = [R.nccl_unique_id(rt.lib) if rank == 0 else None]
-        dist.broadcast_object_list(ids, src=0)
-        blk = rt.block(fam, hidden=rcfg.hidden, heads=rcfg.heads, kv_heads=rcfg.kv_heads, head_dim=rcfg.head_dim,
-                       ffn=rcfg.ffn, seq_len=rcfg.seq_len, max_batch=batch, eps=rcfg.eps, rope_base=rcfg.rope_base,
-                       grid_w=rcfg.grid_w, rope_frame=rcfg.rope_frame, tp_rank=rank, tp_world=world,
-                       nccl_id=ids[0])
-        g = torch.Generator(device="cuda").manual_seed(99)
-        weights = {}
-        for wname, shape in OB.weight_shapes(rcfg).items():
-            t = torch.randn(*shape, device="cuda", generator=g)
-            weights[wname] = (t * 0.02 + 1.0) if len(shape) == 1 and wname != "ada_b" else (
-                t * 0.0 if wname == "ada_b" else t * 0.02)
-        blk.set_weights(weights)
-        del weights
-        T = batch * cfg.seq_len
-        x = torch.randn(T, cfg.hidden, device="cuda", generator=torch.Generator(device="cuda").manual_seed(7))
-        y = torch.empty_like(x)
-        ts = [500.0, 250.0][:batch] if cfg.family == OB.DIT else None
-        for _ in range(2):
-            blk.forward_device(x, y, batch, ts, stream)
-        torch.cuda.synchronize()
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(iters):
-            blk.forward_device(x, y, batch, ts, stream)
-        e1.record(stream)
-        e1.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / iters], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        flops = OB.flops_per_forward(cfg, batch)
-        res.append({"kernel": name, "tp": world, "batch": batch, "seq": cfg.seq_len, "ms": round(ms, 3),
-                    "tokens/s": round(T / (ms * 1e-3), 1), "TFLOP/s": round(flops / (ms * 1e-3) / 1e12, 2),
-                    "frac_of_3xtf32_peak_all_gpus": round(flops / (ms * 1e-3) / 1e12 / (peak * world), 3)})
-        blk.close()
-        del x, y
-        torch.cuda.empty_cache()
-    return res
+    dp = world // tp_size
+    group, tp_rank = rank // tp_size, rank % tp_size
+    local_batch = batch // dp
+    rcfg = tp.rank_config(cfg, tp_rank, tp_size)
+    fam = R.BLOCK_GEMMA if cfg.family == OB.GEMMA else R.BLOCK_DIT
+    # one NCCL unique id seeds exactly one communicator: a fresh id per group and block
+    ids = [[R.nccl_unique_id(rt.lib) for _ in range(dp)] if rank == 0 else None]
+    dist.broadcast_object_list(ids, src=0)
+    blk = rt.block(fam, hidden=rcfg.hidden, heads=rcfg.heads, kv_heads=rcfg.kv_heads, head_dim=rcfg.head_dim,
+                   ffn=rcfg.ffn, seq_len=rcfg.seq_len, max_batch=local_batch, eps=rcfg.eps, rope_base=rcfg.rope_base,
+                   grid_w=rcfg.grid_w, rope_frame=rcfg.rope_frame, tp_rank=tp_rank, tp_world=tp_size,
+                   nccl_id=ids[0][group] if tp_size > 1 else b"")
+    g = torch.Generator(device="cuda").manual_seed(99)
+    weights = {}
+    for wname, shape in OB.weight_shapes(rcfg).items():
+        t = torch.randn(*shape, device="cuda", generator=g)
+        weights[wname] = (t * 0.02 + 1.0) if len(shape) == 1 and wname != "ada_b" else (
+            t * 0.0 if wname == "ada_b" else t * 0.02)
+    blk.set_weights(weights)
+    del weights
+    T_local = local_batch * cfg.seq_len
+    x = torch.randn(T_local, cfg.hidden, device="cuda", generator=torch.Generator(device="cuda").manual_seed(7 + group))
+    y = torch.empty_like(x)
+    ts = ([500.0, 250.0][group * local_batch:(group + 1) * local_batch] if cfg.family == OB.DIT else None)
+    for _ in range(2):
+        blk.forward_device(x, y, local_batch, ts, stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iters):
+        blk.forward_device(x, y, local_batch, ts, stream)
+    e1.record(stream)
+    e1.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / iters], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    T = batch * cfg.seq_len
+    flops = OB.flops_per_forward(cfg, batch)
+    label = f"{name}_tp{tp_size}" if dp == 1 else f"{name}_tp{tp_size}_dp{dp}"
+    blk.close()
+    del x, y
+    torch.cuda.empty_cache()
+    return {"kernel": label, "tp": tp_size, "dp": dp, "batch": batch, "seq": cfg.seq_len, "ms": round(ms, 3),
+            "tokens/s": round(T / (ms * 1e-3), 1), "TFLOP/s": round(flops / (ms * 1e-3) / 1e12, 2),
+            "frac_of_3xtf32_peak_all_gpus": round(flops / (ms * 1e-3) / 1e12 / (peak * world), 3)}
 
 
 def run_ours(args) -> None:
