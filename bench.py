@@ -63,7 +63,7 @@ def parse_args():
     p.add_argument("--no-secondary", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU sample")
     p.add_argument("--workload", default="sgemm",
-                   choices=["sgemm", "gemma_block", "dit_block", "reductions", "attention"],
+                   choices=["sgemm", "gemma_block", "dit_block", "reductions", "attention", "smallm"],
                    help="sgemm = the driver contract line; the others run one secondary measurement "
                         "alone (for profiling) and print it as JSON")
     return p.parse_args()
@@ -235,15 +235,10 @@ def reduction_measurements(rt, torch, hbm_peak: float) -> list[dict]:
     return out
 
 
-def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
-    """Reductions, the transformer blocks, the FMA control and the 32-deep tensor-core variant."""
+def smallm_measurements(rt, torch, stream, hbm_peak: float) -> list[dict]:
+    """Small-M products (Gemma per-token shapes): HBM-bound on B; B = 134 MB > L2, no flush needed."""
     from oct_b200 import reactor as R
-    out = reduction_measurements(rt, torch, hbm_peak)
-    stream = torch.cuda.current_stream()
-    # Transformer blocks at BASELINE configs[3] / configs[4] (random init, synthetic tokens)
-    out.extend(block_measurements(rt, torch, stream))
-    out.extend(attention_measurements(rt, torch, stream))
-    # small-M products (Gemma per-token shapes): HBM-bound on B
+    out = []
     for (m, n, k) in ((1, 16384, 2048), (8, 16384, 2048), (16, 8192, 4096)):  # B = 134 MB > L2
         g = torch.Generator(device="cuda").manual_seed(11)
         a = torch.rand(m, k, device="cuda", generator=g) * 2 - 1
@@ -264,6 +259,18 @@ def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
                     "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1), "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 /
                                                                                        hbm_peak, 3),
                     "bytes": nbytes, "l2": "B larger than L2, no flush"})
+    return out
+
+
+def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
+    """Reductions, the transformer blocks, the FMA control and the 32-deep tensor-core variant."""
+    from oct_b200 import reactor as R
+    out = reduction_measurements(rt, torch, hbm_peak)
+    stream = torch.cuda.current_stream()
+    # Transformer blocks at BASELINE configs[3] / configs[4] (random init, synthetic tokens)
+    out.extend(block_measurements(rt, torch, stream))
+    out.extend(attention_measurements(rt, torch, stream))
+    out.extend(smallm_measurements(rt, torch, stream, hbm_peak))
     # FMA control and the 32-deep tensor-core variant at the headline shape
     m = n = k = 8192
     g = torch.Generator(device="cuda").manual_seed(7)
@@ -510,7 +517,8 @@ def run_ours(args) -> None:
     # fraction is reported beside it.
     tensor_peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
     tensor_peak_burst = pk["bf16_tflops"] / 6.0
-    main_per_launch_ms = main_ms / max(1, launches)
+    # The FMA control records no per-kernel events: its whole step is the kernel.
+    main_per_launch_ms = main_ms / launches if launches > 0 and main_ms > 0 else ms_max / args.steps
     achieved = flops / (main_per_launch_ms * 1e-3) / 1e12
     traffic = None
     tpath = REPO / "profiles" / "traffic.json"
@@ -604,7 +612,7 @@ def run_ours(args) -> None:
             },
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": (1 if args.variant == 2 else 3) * args.steps,  # FMA: one kernel; TC: 2 splits + main
             "clocks": clocks.summary(),
             "secondary": secondary,
         }
@@ -624,6 +632,8 @@ def run_single_workload(args) -> None:
     pk, _ = peaks()
     if args.workload == "reductions":
         res = reduction_measurements(rt, torch, pk["hbm_gbs"])
+    elif args.workload == "smallm":
+        res = smallm_measurements(rt, torch, torch.cuda.current_stream(), pk["hbm_gbs"])
     elif args.workload == "attention":
         res = attention_measurements(rt, torch, torch.cuda.current_stream(), iters=max(1, args.steps))
     else:
