@@ -100,17 +100,19 @@ __device__ __forceinline__ float process_row(float* srow, uint32_t w, uint32_t l
   const uint32_t nv = w / 4;
   float4* v4 = reinterpret_cast<float4*>(srow);
   if constexpr (OP == kSum) {
-    double s = 0.0;
+    // four independent binary64 chains (one per float4 lane), joined at the end:
+    // the same exact sums as one chain wherever binary64 holds the sum exactly
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
     for (uint32_t i = lane; i < nv; i += TPR) {
       const float4 x = v4[i];
-      s += static_cast<double>(x.x); s += static_cast<double>(x.y);
-      s += static_cast<double>(x.z); s += static_cast<double>(x.w);
+      s0 += static_cast<double>(x.x); s1 += static_cast<double>(x.y);
+      s2 += static_cast<double>(x.z); s3 += static_cast<double>(x.w);
       if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
         note_nonfinite(x.x, row * w + 4 * i, first_bad); note_nonfinite(x.y, row * w + 4 * i + 1, first_bad);
         note_nonfinite(x.z, row * w + 4 * i + 2, first_bad); note_nonfinite(x.w, row * w + 4 * i + 3, first_bad);
       }
     }
-    s = group_sum_d<TPR>(s, dscratch);
+    const double s = group_sum_d<TPR>((s0 + s1) + (s2 + s3), dscratch);
     if (lane == 0) out[row] = static_cast<float>(s);
     return 0.f;
   } else if constexpr (OP == kMax) {
