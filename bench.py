@@ -376,6 +376,46 @@ def block_measurements(rt, torch, stream, iters: int = 5, only: str | None = Non
     return res
 
 
+def sharded_sgemm_measurements(rt, torch, dist, rank: int, world: int, stream, iters: int = 5) -> list[dict]:
+    """BASELINE configs[1]'s two largest products at a fixed global size, column-sharded: each rank
+    holds A and N / world columns of B and C (C stays sharded); time = max over ranks."""
+    from oct_b200 import reactor as R
+    res = []
+    pk, _ = peaks()
+    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
+    for (m, n, k) in ((8192, 8192, 8192), (16384, 16384, 4096)):
+        if n % (world * 256):
+            continue
+        nr = n // world
+        g = torch.Generator(device="cuda").manual_seed(17 + rank)
+        a = torch.rand(m, k, device="cuda", generator=g) * 2 - 1
+        b = torch.rand(k, nr, device="cuda", generator=g) * 2 - 1
+        c = torch.empty(m, nr, device="cuda")
+        for _ in range(2):
+            rt.sgemm_device(a, b, c, m, nr, k, R.SGEMM_AUTO, stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            rt.sgemm_device(a, b, c, m, nr, k, R.SGEMM_AUTO, stream)
+        e1.record(stream)
+        e1.synchronize()
+        st = rt.sync_status(stream)
+        if not st.ok:
+            raise RuntimeError(f"sharded sgemm failed: {st}")
+        t = torch.tensor([e0.elapsed_time(e1) / iters], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+        res.append({"kernel": f"sgemm_{m}x{n}x{k}_colshard", "ranks": world, "n_per_rank": nr, "ms": round(ms, 3),
+                    "TFLOP/s": round(tf, 2), "frac_of_3xtf32_peak_all_gpus": round(tf / (peak * world), 3),
+                    "scaling": "strong (fixed global product)"})
+        del a, b, c
+        torch.cuda.empty_cache()
+    return res
+
+
 def tp_block_measurements(rt, torch, dist, rank: int, world: int, stream, iters: int = 5) -> list[dict]:
     """Gemma / DiT blocks over all ranks, global tokens/s: pure tensor parallel (tp = world), and
     tensor parallel within groups of ranks plus data parallel across the groups (each group runs
@@ -560,7 +600,8 @@ def run_ours(args) -> None:
     secondary = None
     cpu = None
     if world > 1 and not args.no_secondary:
-        secondary = tp_block_measurements(rt, torch, dist, rank, world, stream)
+        secondary = sharded_sgemm_measurements(rt, torch, dist, rank, world, stream)
+        secondary += tp_block_measurements(rt, torch, dist, rank, world, stream)
     if rank == 0 and world == 1:
         if not args.no_secondary:
             secondary = secondary_measurements(rt, torch, pk["hbm_gbs"])

@@ -734,6 +734,13 @@ PROM_REACTOR_API int oct_b200_attention_device(void* handle, const float* d_q, c
                                                float* d_out, uint32_t items, uint32_t seq, uint32_t heads,
                                                uint32_t head_dim, float scale, void* stream, int* out_detail_code);
 
+/* Test-only, no reference counterpart: runs the tensor-parallel peer-wait
+   kernel against a flag that nothing sets, with a wall-clock budget of
+   budget_ns (1 ms .. 1 s).  The wait must give up, record its error bit and
+   return: PROM_ERROR with OCT_B200_DETAIL_DEVICE_TIMEOUT, the handle still
+   usable.  Failure detection is exercised without faulting or hanging a GPU. */
+PROM_REACTOR_API int oct_b200_selftest_wait_timeout(void* handle, uint64_t budget_ns, int* out_detail_code);
+
 /* Waits for `stream` (NULL: the CUDA default stream), then reads and
    clears the device status words the kernels write: returns PROM_ERROR with
    OCT_B200_DETAIL_DEVICE_TIMEOUT if a bounded in-kernel wait gave up, or

@@ -1869,6 +1869,46 @@ int oct_b200_attention_device(void* handle, const float* d_q, const float* d_k, 
   }
 }
 
+int oct_b200_selftest_wait_timeout(void* handle, uint64_t budget_ns, int* out_detail_code) {
+  try {
+    if (out_detail_code) *out_detail_code = 0;
+    Runtime* rt = lookup(handle);
+    if (rt == nullptr) return PROM_INVALID_HANDLE;
+    if (budget_ns < 1000000ull || budget_ns > 1000000000ull) {
+      if (out_detail_code) *out_detail_code = PROM_ERROR;
+      return PROM_ERROR;
+    }
+    if (!rt->available) {
+      if (out_detail_code) *out_detail_code = PROM_DETAIL_CAPABILITY_MISMATCH;
+      return PROM_ERROR;
+    }
+    std::lock_guard<std::mutex> lock(rt->mu);
+    DevBuf flag;  // one u64 epoch that no rank ever sets
+    cudaError_t e = flag.ensure(64, rt->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(flag.aligned(), 0, 8, rt->stream);
+    if (e == cudaSuccess) e = reset_words(rt);
+    if (e == cudaSuccess)
+      e = oct::tp_wait(static_cast<const uint64_t*>(flag.aligned()), 0, 1, 1, rt->err_word(), budget_ns, rt->stream);
+    Words w;
+    if (e == cudaSuccess) e = read_words(rt, &w);
+    // the observed bit is reported here and cleared: the handle carries no stale status
+    if (e == cudaSuccess) e = reset_words(rt);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
+    flag.release();
+    if (e != cudaSuccess) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_CUDA_ERROR;
+      return PROM_ERROR;
+    }
+    if (w.err != 0) {
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_DEVICE_TIMEOUT;
+      return PROM_ERROR;
+    }
+    return PROM_OK;  // the wait did not give up: the self-test failed to observe a timeout
+  } catch (...) {
+    return PROM_INTERNAL_ERROR;
+  }
+}
+
 int oct_b200_rmsnorm_device(void* handle, const float* d_in, const float* d_weight, float* d_out, float* d_inv_rms,
                             uint32_t rows, uint32_t width, float epsilon, void* stream, int* out_detail_code) {
   try {

@@ -43,6 +43,7 @@ BATCH_FLAG_PARTITION_CONTIGUOUS = 1 << 8
 DETAIL_BATCH_PLAN_INVALID, DETAIL_BATCH_EXECUTION_FAILED, DETAIL_BATCH_UNSUPPORTED_OPTION = -6602, -6604, -6613
 DETAIL_PATH_STAGED_UPLOAD_TILED = 6106
 DETAIL_BAD_VARIANT = -7004
+DETAIL_DEVICE_TIMEOUT = -7002  # a bounded in-kernel wait gave up
 REDUCTION_TESTCFG_FAIL_COMMAND_RECORD = 1 << 0
 REDUCTION_TESTCFG_FAIL_QUEUE_SUBMIT = 1 << 1
 REDUCTION_TESTCFG_FAIL_COMPLETION_OBSERVATION = 1 << 2
@@ -351,6 +352,7 @@ SIGNATURES = {
     "oct_b200_rmsnorm_device": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, C.c_float, _vp, _i32p]),
     "oct_b200_attention_device": (
         C.c_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, C.c_float, _vp, _i32p]),
+    "oct_b200_selftest_wait_timeout": (C.c_int, [_vp, _u64, _i32p]),
     "oct_b200_sync_status": (C.c_int, [_vp, _vp, _i32p]),
     "oct_b200_sgemm_device_noalloc": (
         C.c_int, [_vp, _u64, _vp, _u64, _vp, _u64, _u32, _u32, _u32, _vp, _i32p]),
@@ -692,6 +694,12 @@ class Runtime:
                                                 head_dim, scale, _stream_ptr(stream), C.byref(detail))
         if rc != PROM_OK:
             raise RuntimeError(f"device attention rc={rc} detail={detail.value}")
+
+    def selftest_wait_timeout(self, budget_ns: int) -> CallStatus:
+        """Test-only: a bounded in-kernel wait on a flag nothing sets must report a timeout."""
+        detail = C.c_int()
+        rc = self.lib.oct_b200_selftest_wait_timeout(self.handle, budget_ns, C.byref(detail))
+        return CallStatus(rc, 0, detail.value)
 
     def sync_status(self, stream=None) -> CallStatus:
         detail = C.c_int()
