@@ -89,7 +89,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     flash_attn_kernel(const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
                       const __grid_constant__ CUtensorMap tm_vhi, const __grid_constant__ CUtensorMap tm_vlo,
                       const float* __restrict__ qhi, const float* __restrict__ qlo, float* __restrict__ out,
-                      uint64_t ldo, uint32_t heads, uint32_t seq, float scale, unsigned int* __restrict__ err) {
+                      uint64_t ldo, uint32_t heads, uint32_t seq, float scale, unsigned int* __restrict__ err,
+                      float* __restrict__ out_lo) {
   constexpr uint32_t IDESC_S = umma_idesc_tf32(FA_BQ, FA_BKV);
   constexpr uint32_t IDESC_O = umma_idesc_tf32(FA_BQ, FA_HD);
   extern __shared__ uint8_t smem_raw[];
@@ -349,8 +350,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         if (ok) {
           tc_fence_after();
           const float inv = inv_l_sh[row];
-          float* dst = out + (static_cast<uint64_t>(item) * seq + static_cast<uint64_t>(qtile) * FA_BQ + row) * ldo +
-                       static_cast<uint64_t>(head) * FA_HD;
+          const uint64_t o = (static_cast<uint64_t>(item) * seq + static_cast<uint64_t>(qtile) * FA_BQ + row) * ldo +
+                             static_cast<uint64_t>(head) * FA_HD;
+          float* dst = out + o;
+          float* dst_lo = out_lo != nullptr ? out_lo + o : nullptr;  // TF32 split for the next product
 #pragma unroll
           for (uint32_t g = 0; g < FA_HD / 32; ++g) {
             uint32_t r[32];
@@ -359,10 +362,17 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
               const int c = static_cast<int>(g * 32) + i;
-              *reinterpret_cast<float4*>(dst + c) =
-                  make_float4((o_run[c] + __uint_as_float(r[i])) * inv, (o_run[c + 1] + __uint_as_float(r[i + 1])) * inv,
-                              (o_run[c + 2] + __uint_as_float(r[i + 2])) * inv,
-                              (o_run[c + 3] + __uint_as_float(r[i + 3])) * inv);
+              float4 v = make_float4((o_run[c] + __uint_as_float(r[i])) * inv,
+                                     (o_run[c + 1] + __uint_as_float(r[i + 1])) * inv,
+                                     (o_run[c + 2] + __uint_as_float(r[i + 2])) * inv,
+                                     (o_run[c + 3] + __uint_as_float(r[i + 3])) * inv);
+              if (dst_lo != nullptr) {
+                const float4 h = make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
+                *reinterpret_cast<float4*>(dst_lo + c) =
+                    make_float4(to_tf32(v.x - h.x), to_tf32(v.y - h.y), to_tf32(v.z - h.z), to_tf32(v.w - h.w));
+                v = h;
+              }
+              *reinterpret_cast<float4*>(dst + c) = v;
             }
           }
         }
@@ -467,7 +477,7 @@ cudaError_t split_heads(const float* x, uint64_t ldx, uint32_t items, uint32_t h
 }
 
 cudaError_t flash_attention_tf32x3(const AttnOperands& in, float* out, uint64_t ldo, uint32_t items, uint32_t heads,
-                                   uint32_t seq, float scale, unsigned int* err, cudaStream_t stream) {
+                                   uint32_t seq, float scale, unsigned int* err, cudaStream_t stream, float* out_lo) {
   if (!flash_attention_supported(FA_HD, seq) || items == 0 || heads == 0) return cudaErrorInvalidValue;
   const uint64_t slabs = static_cast<uint64_t>(items) * heads;
   if (slabs * seq > 0x7FFFFFFFull) return cudaErrorInvalidValue;  // TMA row coordinates are int32
@@ -482,7 +492,7 @@ cudaError_t flash_attention_tf32x3(const AttnOperands& in, float* out, uint64_t 
   if (e != cudaSuccess) return e;
   const dim3 grid(seq / FA_BQ, heads, items);
   flash_attn_kernel<<<grid, FA_THREADS, FA_SMEM, stream>>>(m_khi, m_klo, m_vhi, m_vlo, in.qhi, in.qlo, out, ldo, heads,
-                                                           seq, scale, err);
+                                                           seq, scale, err, out_lo);
   return cudaGetLastError();
 }
 

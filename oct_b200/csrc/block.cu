@@ -36,6 +36,7 @@
 #include <cstring>
 #include <dlfcn.h>
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "block.h"
@@ -76,6 +77,7 @@ __device__ __forceinline__ float block_max_f(float v, float* sh) {
 //   y = y * mul[item] + add[item]                    (optional: adaLN modulation)
 //   y = res + gate[item] * y   or   y = res + y      (optional: gated residual)
 // `item` = row / rows_per_item indexes the per-batch-item vectors (stride mod_stride).
+// With out_lo != null the result is written as its TF32 split (hi to out, lo to out_lo).
 constexpr int NORM_VPT = 16;
 __global__ void __launch_bounds__(NT) norm_fused_kernel(const float* __restrict__ x, uint64_t ldx,
                                                         const float* __restrict__ g, float eps,
@@ -83,7 +85,8 @@ __global__ void __launch_bounds__(NT) norm_fused_kernel(const float* __restrict_
                                                         const float* __restrict__ res, uint64_t ldres,
                                                         const float* __restrict__ gate, uint64_t mod_stride,
                                                         uint32_t rows_per_item, float* __restrict__ out,
-                                                        uint64_t ldo, uint32_t rows, uint32_t width) {
+                                                        uint64_t ldo, uint32_t rows, uint32_t width,
+                                                        float* __restrict__ out_lo) {
   __shared__ double sh[NT / 32];
   for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* xr = x + r * ldx;
@@ -106,6 +109,11 @@ __global__ void __launch_bounds__(NT) norm_fused_kernel(const float* __restrict_
       if (mul != nullptr) y = y * mul[mo + c];
       if (add != nullptr) y = y + add[mo + c];
       if (res != nullptr) y = res[r * ldres + c] + (gate != nullptr ? gate[mo + c] * y : y);
+      if (out_lo != nullptr) {  // write the TF32 split the next product reads as its A operand
+        const float h = to_tf32(y);
+        out_lo[r * ldo + c] = to_tf32(y - h);
+        y = h;
+      }
       out[r * ldo + c] = y;
     }
   }
@@ -243,8 +251,10 @@ __global__ void __launch_bounds__(NT) attn_softmax_split_kernel(const float* __r
 }
 
 // act[r, c] = f(gu[r, c]) * gu[r, F + c]; f = gelu_tanh (GeGLU) or silu (SwiGLU).
+// With act_lo != null the product is written as its TF32 split (hi to act, lo to act_lo).
 template <bool GELU>
-__global__ void gated_act_kernel(const float* __restrict__ gu, float* __restrict__ act, uint32_t rows, uint32_t f) {
+__global__ void gated_act_kernel(const float* __restrict__ gu, float* __restrict__ act, uint32_t rows, uint32_t f,
+                                 float* __restrict__ act_lo) {
   const uint64_t total4 = static_cast<uint64_t>(rows) * (f / 4);
   for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total4;
        i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
@@ -262,7 +272,14 @@ __global__ void gated_act_kernel(const float* __restrict__ gu, float* __restrict
         o[j] = x / (1.f + expf(-x));
       }
     }
-    *reinterpret_cast<float4*>(act + r * f + c) = make_float4(o[0] * u.x, o[1] * u.y, o[2] * u.z, o[3] * u.w);
+    float4 v = make_float4(o[0] * u.x, o[1] * u.y, o[2] * u.z, o[3] * u.w);
+    if (act_lo != nullptr) {
+      const float4 h = make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
+      *reinterpret_cast<float4*>(act_lo + r * f + c) =
+          make_float4(to_tf32(v.x - h.x), to_tf32(v.y - h.y), to_tf32(v.z - h.z), to_tf32(v.w - h.w));
+      v = h;
+    }
+    *reinterpret_cast<float4*>(act + r * f + c) = v;
   }
 }
 
@@ -533,7 +550,19 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
   // in a plain cudaMalloc allocation that peers can map.
   const char* tp_mode = std::getenv("OCT_B200_TP_COLLECTIVE");
   const bool want_fused_tp = d.tp_world > 1 && !(tp_mode != nullptr && std::strcmp(tp_mode, "nccl") == 0);
-  hbuf_ = want_fused_tp ? sym_alloc(T * d.hidden) : alloc(T * d.hidden);
+  // Without the peer-memory path, the producers of the products' A operands (norms,
+  // gated activation, fused attention) write them straight in the TF32 split layout:
+  // hi into hbuf_ / act_ / attn_, lo into hlo_ / actlo_ / attnlo_, rows padded to the
+  // 256-row tile (the tensor maps read Mp rows), K a multiple of 32.
+  split_producers_ = !want_fused_tp && d.hidden % 32 == 0 && d.ffn % 32 == 0 && attn_cols % 32 == 0;
+  const uint64_t TP_rows = split_producers_ ? (T + 255) / 256 * 256 : T;
+  hbuf_ = want_fused_tp ? sym_alloc(T * d.hidden) : alloc(TP_rows * d.hidden);
+  if (split_producers_) {
+    hlo_ = alloc(TP_rows * d.hidden);
+    actlo_ = alloc(TP_rows * d.ffn);
+    attnlo_ = alloc(TP_rows * attn_cols);
+    ok = ok && hlo_ && actlo_ && attnlo_;
+  }
   if (want_fused_tp) {
     const uint64_t rpr = (T + d.tp_world - 1) / d.tp_world;  // rows per rank at max_batch
     rs_ = sym_alloc(rpr * d.tp_world * d.hidden);
@@ -558,11 +587,11 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
     scores_ = alloc(static_cast<uint64_t>(d.max_batch) * d.heads * d.seq_len * d.seq_len);
     ok = ok && scores_;
   }
-  attn_ = alloc(T * attn_cols);
+  attn_ = alloc(TP_rows * attn_cols);
   x1_ = alloc(T * d.hidden);
   proj_ = alloc(T * d.hidden);
   gu_ = alloc(T * 2ull * d.ffn);
-  act_ = alloc(T * d.ffn);
+  act_ = alloc(TP_rows * d.ffn);
   if (!fused_attn_) {
     // P in the TF32 split layout of the P V product, one batch item at a time
     const SplitDims pd = split_dims(d.seq_len, d.head_dim, d.seq_len);
@@ -584,6 +613,13 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
   ok = ok && hbuf_ && qkv_ && attn_ && x1_ && proj_ && gu_ && act_ && scratch_ && err_;
   if (!ok) return -3;
   if (cudaMemsetAsync(err_, 0, 16, stream_) != cudaSuccess) return -4;
+  if (split_producers_) {  // padding rows of the split operands start (and stay) zero
+    const uint64_t rows = (T + 255) / 256 * 256;
+    const std::pair<float*, uint64_t> bufs[] = {{hbuf_, d.hidden}, {hlo_, d.hidden}, {act_, d.ffn},
+                                                {actlo_, d.ffn},   {attn_, attn_cols}, {attnlo_, attn_cols}};
+    for (const auto& b : bufs)
+      if (cudaMemsetAsync(b.first, 0, rows * b.second * sizeof(float), stream_) != cudaSuccess) return -4;
+  }
   if (build_rope_tables() != 0) return -4;
   if (d.tp_world > 1) {
     if (!nccl().ok || id == nullptr) return -5;
@@ -706,6 +742,11 @@ cudaError_t Block::gemm(const float* a, uint64_t lda, const SplitW& w, float* c,
                            kTcSingle16, scatter);
 }
 
+cudaError_t Block::gemm_ab(const float* ahi, const float* alo, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
+                           const float* residual, uint64_t ldr) {
+  return sgemm_tc_presplit_ab(ahi, alo, w.hi, w.lo, c, ldc, m, w.n, w.k, err_, stream_, residual, ldr);
+}
+
 cudaError_t Block::all_reduce(float* buf, uint64_t count) {
   if (dims_.tp_world <= 1) return cudaSuccess;
   return nccl().all_reduce(buf, buf, count, kNcclFloat32, kNcclSum, comm_, stream_) == 0 ? cudaSuccess
@@ -765,6 +806,8 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
   // Fused tensor parallel (peer memory) when every rank owns an equal row share.
   const bool tpf = fused_tp_ && T % d.tp_world == 0;
   const uint32_t rpr = tpf ? T / d.tp_world : 0;
+  // producers write the products' A operands already split (hi in the fp32 buffer, lo beside it)
+  const bool sp = split_producers_ && !tpf;
   RowScatter sc;
   TpReduce red;
   if (tpf) {
@@ -787,9 +830,10 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
   }
   if (d.family == kGemma) {
     norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x, d.hidden, norm1_, d.eps, nullptr, nullptr, nullptr, 0,
-                                                          nullptr, 0, d.seq_len, hbuf_, d.hidden, T, d.hidden);
+                                                          nullptr, 0, d.seq_len, hbuf_, d.hidden, T, d.hidden,
+                                                          sp ? hlo_ : nullptr);
     if (!ok()) return -4;
-    e = gemm(hbuf_, d.hidden, wqkv_, qkv_, qkv_cols, T);
+    e = sp ? gemm_ab(hbuf_, hlo_, wqkv_, qkv_, qkv_cols, T) : gemm(hbuf_, d.hidden, wqkv_, qkv_, qkv_cols, T);
     if (!ok()) return -4;
     const uint64_t rope_work = static_cast<uint64_t>(T) * (d.heads + d.kv_heads) * (d.head_dim / 2);
     rope_half_kernel<<<grid_for(rope_work, NT), NT, 0, stream_>>>(qkv_, qkv_cols, 0, d.heads + d.kv_heads,
@@ -817,13 +861,14 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
       if (ok()) e = all_reduce(x1_, static_cast<uint64_t>(T) * d.hidden);
       if (!ok()) return -4;
       norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x1_, d.hidden, norm2_, d.eps, nullptr, nullptr, nullptr,
-                                                            0, nullptr, 0, d.seq_len, hbuf_, d.hidden, T, d.hidden);
+                                                            0, nullptr, 0, d.seq_len, hbuf_, d.hidden, T, d.hidden,
+                                                            sp ? hlo_ : nullptr);
       if (!ok()) return -4;
     }
-    e = gemm(hbuf_, d.hidden, wgu_, gu_, 2ull * d.ffn, T);
+    e = sp ? gemm_ab(hbuf_, hlo_, wgu_, gu_, 2ull * d.ffn, T) : gemm(hbuf_, d.hidden, wgu_, gu_, 2ull * d.ffn, T);
     if (!ok()) return -4;
-    gated_act_kernel<true><<<grid_for(static_cast<uint64_t>(T) * d.ffn / 4, NT), NT, 0, stream_>>>(gu_, act_, T,
-                                                                                                 d.ffn);
+    gated_act_kernel<true><<<grid_for(static_cast<uint64_t>(T) * d.ffn / 4, NT), NT, 0, stream_>>>(
+        gu_, act_, T, d.ffn, sp ? actlo_ : nullptr);
     if (!ok()) return -4;
     if (tpf) {
       // partial act Wd rows -> owners; owners: y = x1 + sum -> every rank
@@ -840,7 +885,8 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
                                     cudaMemcpyDeviceToDevice, stream_);
       return ok() ? 0 : -4;
     }
-    e = gemm(act_, d.ffn, wd_, y, d.hidden, T, lead ? x1_ : nullptr, d.hidden);  // y = x1 + act Wd
+    e = sp ? gemm_ab(act_, actlo_, wd_, y, d.hidden, T, lead ? x1_ : nullptr, d.hidden)  // y = x1 + act Wd
+           : gemm(act_, d.ffn, wd_, y, d.hidden, T, lead ? x1_ : nullptr, d.hidden);
     if (ok()) e = all_reduce(y, static_cast<uint64_t>(T) * d.hidden);
     return ok() ? 0 : -4;
   }
@@ -862,9 +908,10 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
   float* shift_a = ada_ + 4ull * d.hidden;
   float* shift_m = ada_ + 5ull * d.hidden;
   norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x, d.hidden, norm1_, d.eps, scale_a, shift_a, nullptr, 0,
-                                                        nullptr, ms, d.seq_len, hbuf_, d.hidden, T, d.hidden);
+                                                        nullptr, ms, d.seq_len, hbuf_, d.hidden, T, d.hidden,
+                                                        sp ? hlo_ : nullptr);
   if (!ok()) return -4;
-  e = gemm(hbuf_, d.hidden, wqkv_, qkv_, qkv_cols, T);
+  e = sp ? gemm_ab(hbuf_, hlo_, wqkv_, qkv_, qkv_cols, T) : gemm(hbuf_, d.hidden, wqkv_, qkv_, qkv_cols, T);
   if (!ok()) return -4;
   const uint64_t qk_warps = static_cast<uint64_t>(T) * d.heads;
   const uint64_t se = static_cast<uint64_t>(T) * attn_cols;  // elements of one split half (this batch)
@@ -883,7 +930,8 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
     if (!ok()) return -4;
     const AttnOperands ops{qsplit_, qsplit_ + se, ksplit_, ksplit_ + se, vtsplit_, vtsplit_ + se};
     e = flash_attention_tf32x3(ops, attn_, attn_cols, batch, d.heads, d.seq_len,
-                               1.0f / std::sqrt(static_cast<float>(d.head_dim)), err_, stream_);
+                               1.0f / std::sqrt(static_cast<float>(d.head_dim)), err_, stream_,
+                               sp ? attnlo_ : nullptr);
   } else {
     e = attention(batch, qkv_cols, attn_cols, 2 * attn_cols, false);
   }
@@ -910,21 +958,23 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
     if (ok()) e = tp_phase(1);
     if (!ok()) return -4;
   } else {
-    e = gemm(attn_, attn_cols, wo_, proj_, d.hidden, T);
+    e = (sp && fused_attn_) ? gemm_ab(attn_, attnlo_, wo_, proj_, d.hidden, T)
+                            : gemm(attn_, attn_cols, wo_, proj_, d.hidden, T);
     if (ok()) e = all_reduce(proj_, static_cast<uint64_t>(T) * d.hidden);
     if (!ok()) return -4;
     // res = x + gate_a * RMSNorm(proj)
     norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(proj_, d.hidden, norm2_, d.eps, nullptr, nullptr, x,
-                                                          d.hidden, gate_a, ms, d.seq_len, x1_, d.hidden, T, d.hidden);
+                                                          d.hidden, gate_a, ms, d.seq_len, x1_, d.hidden, T, d.hidden, nullptr);
     if (!ok()) return -4;
     norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x1_, d.hidden, norm3_, d.eps, scale_m, shift_m, nullptr, 0,
-                                                          nullptr, ms, d.seq_len, hbuf_, d.hidden, T, d.hidden);
+                                                          nullptr, ms, d.seq_len, hbuf_, d.hidden, T, d.hidden,
+                                                          sp ? hlo_ : nullptr);
     if (!ok()) return -4;
   }
-  e = gemm(hbuf_, d.hidden, wgu_, gu_, 2ull * d.ffn, T);
+  e = sp ? gemm_ab(hbuf_, hlo_, wgu_, gu_, 2ull * d.ffn, T) : gemm(hbuf_, d.hidden, wgu_, gu_, 2ull * d.ffn, T);
   if (!ok()) return -4;
-  gated_act_kernel<false><<<grid_for(static_cast<uint64_t>(T) * d.ffn / 4, NT), NT, 0, stream_>>>(gu_, act_, T,
-                                                                                                d.ffn);
+  gated_act_kernel<false><<<grid_for(static_cast<uint64_t>(T) * d.ffn / 4, NT), NT, 0, stream_>>>(
+      gu_, act_, T, d.ffn, sp ? actlo_ : nullptr);
   if (!ok()) return -4;
   if (tpf) {
     // partial act W2 rows -> owners; owners: y = x1 + gate_m * RMSNorm(sum) -> every rank
@@ -944,12 +994,12 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
                                   cudaMemcpyDeviceToDevice, stream_);
     return ok() ? 0 : -4;
   }
-  e = gemm(act_, d.ffn, wd_, proj_, d.hidden, T);
+  e = sp ? gemm_ab(act_, actlo_, wd_, proj_, d.hidden, T) : gemm(act_, d.ffn, wd_, proj_, d.hidden, T);
   if (ok()) e = all_reduce(proj_, static_cast<uint64_t>(T) * d.hidden);
   if (!ok()) return -4;
   // y = res + gate_m * RMSNorm(w2 out)
   norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(proj_, d.hidden, norm4_, d.eps, nullptr, nullptr, x1_,
-                                                        d.hidden, gate_m, ms, d.seq_len, y, d.hidden, T, d.hidden);
+                                                        d.hidden, gate_m, ms, d.seq_len, y, d.hidden, T, d.hidden, nullptr);
   return ok() ? 0 : -4;
 }
 

@@ -67,6 +67,9 @@ class Block {
   int build_rope_tables();
   cudaError_t gemm(const float* a, uint64_t lda, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
                    const float* residual = nullptr, uint64_t ldr = 0, const RowScatter* scatter = nullptr);
+  // C = R + A * W with A already split by its producer (hi, lo rows of length w.k)
+  cudaError_t gemm_ab(const float* ahi, const float* alo, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
+                      const float* residual = nullptr, uint64_t ldr = 0);
   cudaError_t attention(uint32_t batch, uint64_t ldq, uint32_t k_col, uint32_t v_col, bool shared_kv);
   cudaError_t all_reduce(float* buf, uint64_t count);
   // tensor parallel over peer memory (tp_fused.cu)
@@ -89,6 +92,9 @@ class Block {
   float *gu_ = nullptr, *act_ = nullptr, *scratch_ = nullptr;
   float* psplit_ = nullptr;  // attention probabilities, TF32 hi then lo, [max_batch*heads][p_mp_][p_kp_]
   uint32_t p_mp_ = 0, p_kp_ = 0;
+  // producers write the products' A operands pre-split (hi in hbuf_ / act_ / attn_)
+  bool split_producers_ = false;
+  float *hlo_ = nullptr, *actlo_ = nullptr, *attnlo_ = nullptr;
   // fused attention (DiT, head_dim 128): Q, K, V^T split to TF32 hi/lo per head
   bool fused_attn_ = false;
   float *qsplit_ = nullptr, *ksplit_ = nullptr, *vtsplit_ = nullptr;

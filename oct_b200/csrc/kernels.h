@@ -85,6 +85,13 @@ cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, co
                               cudaStream_t stream, const float* residual = nullptr, uint64_t ldr = 0,
                               int cfg = kTcSingle16, const RowScatter* scatter = nullptr);
 
+// A and B both already split: A hi/lo rows of length Kp (split_dims), written by
+// the kernel that produced A; C = R + A * B as in sgemm_tc_presplit.
+cudaError_t sgemm_tc_presplit_ab(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
+                                 uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, unsigned int* err,
+                                 cudaStream_t stream, const float* residual = nullptr, uint64_t ldr = 0,
+                                 int cfg = kTcSingle16);
+
 // A already split by its producer (hi/lo in the [count][Mp][Kp] layout of
 // split_dims, zero padded); B is split into b_scratch.  Strided batch as GemmBatch.
 cudaError_t sgemm_tc_presplit_a(const float* ahi, const float* alo, const float* b, uint64_t ldb, float* c,
@@ -111,8 +118,10 @@ struct AttnOperands {
   const float *qhi, *qlo, *khi, *klo, *vthi, *vtlo;
 };
 bool flash_attention_supported(uint32_t head_dim, uint32_t seq);
+// With out_lo != null the output is written as its TF32 split: hi to out, lo to out_lo.
 cudaError_t flash_attention_tf32x3(const AttnOperands& in, float* out, uint64_t ldo, uint32_t items, uint32_t heads,
-                                   uint32_t seq, float scale, unsigned int* err, cudaStream_t stream);
+                                   uint32_t seq, float scale, unsigned int* err, cudaStream_t stream,
+                                   float* out_lo = nullptr);
 // V columns of `heads` heads ([items*seq][ldv], head h at columns h*128..) ->
 // the vt hi/lo layout above.
 // Q or K columns of `heads` heads ([items*seq][ldx]) -> the q/k hi/lo layout above.

@@ -767,6 +767,16 @@ cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, co
   return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, EntryStride{}, residual, ldr, scatter);
 }
 
+// Both operands already split: A hi/lo in the [Mp][Kp] layout of split_dims
+// (written by its producer), B as from sgemm_tc_split_b.
+cudaError_t sgemm_tc_presplit_ab(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
+                                 uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, unsigned int* err,
+                                 cudaStream_t stream, const float* residual, uint64_t ldr, int cfg) {
+  if (m == 0 || n == 0 || k == 0) return cudaSuccess;
+  const SplitDims d = split_dims(m, n, k);
+  return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, EntryStride{}, residual, ldr);
+}
+
 // A operand already in the split layout (hi/lo, [count][Mp][Kp], zero padded),
 // written by its producer; only B is split here (into b_scratch).
 cudaError_t sgemm_tc_presplit_a(const float* ahi, const float* alo, const float* b, uint64_t ldb, float* c,
