@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200-native Prometheus reactor (driver contract).
 
-Headline metric (BASELINE.json): fp32 SGEMM TFLOP/s at 8192^3.
+Headline metric: fp32 SGEMM TFLOP/s at 8192^3.
 
   * One step = one C = A*B of the workload through the reactor's device entry
     point (oct_b200_sgemm_device_ld): the TF32 split pass plus the tcgen05
@@ -196,7 +196,7 @@ def run_reference(args) -> None:
 
 
 def reduction_measurements(rt, torch, hbm_peak: float) -> list[dict]:
-    """Row reductions and RMSNorm at BASELINE configs[2] shapes (32768 rows)."""
+    """Row reductions and RMSNorm at the benchmark shapes (32768 rows x 256 / 2048 / 4096)."""
     from oct_b200 import reactor as R
     out = []
     stream = torch.cuda.current_stream()
@@ -267,7 +267,7 @@ def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
     from oct_b200 import reactor as R
     out = reduction_measurements(rt, torch, hbm_peak)
     stream = torch.cuda.current_stream()
-    # Transformer blocks at BASELINE configs[3] / configs[4] (random init, synthetic tokens)
+    # Transformer blocks at the benchmark shapes (random init, synthetic tokens)
     out.extend(block_measurements(rt, torch, stream))
     out.extend(attention_measurements(rt, torch, stream))
     out.extend(smallm_measurements(rt, torch, stream, hbm_peak))
@@ -329,7 +329,7 @@ def attention_measurements(rt, torch, stream, iters: int = 5) -> list[dict]:
 
 
 def block_measurements(rt, torch, stream, iters: int = 5, only: str | None = None) -> list[dict]:
-    """Tokens/s of one block forward at the BASELINE shapes, plus its tensor-peak fraction."""
+    """Tokens/s of one block forward at the benchmark shapes, plus its tensor-peak fraction."""
     from oct_b200 import reactor as R
     from oracle import blocks as OB  # used only for the shapes and the flop count
     pk, _ = peaks()
@@ -377,7 +377,7 @@ def block_measurements(rt, torch, stream, iters: int = 5, only: str | None = Non
 
 
 def sharded_sgemm_measurements(rt, torch, dist, rank: int, world: int, stream, iters: int = 5) -> list[dict]:
-    """BASELINE configs[1]'s two largest products at a fixed global size, column-sharded: each rank
+    """The ragged sweep's two largest products at a fixed global size, column-sharded: each rank
     holds A and N / world columns of B and C (C stays sharded); time = max over ranks."""
     from oct_b200 import reactor as R
     res = []

@@ -9,7 +9,7 @@
 //    per-head Q/K RMSNorm -> 3-axis interleaved RoPE -> exact bidirectional
 //    attention -> out projection -> RMSNorm -> tanh-gated residual -> FFN norm +
 //    modulation -> W1|W3 -> SiLU gate -> W2 -> RMSNorm -> gated residual.
-//    BASELINE widens the reference's 4 x hidden adaLN to 6 x hidden with shifts.
+//    The adaLN here is 6 x hidden (adds two shifts) where the reference has 4 x hidden.
 //  * Gemma-shaped decoder: RMSNorm -> fused QKV (MQA: every query head uses KV
 //    head 0) -> half-split RoPE (`cpuGemma4e2bRope`, gemma4e2b_m1_rtx.go:834-861,
 //    without its BF16 storage rounding) -> causal attention with scale

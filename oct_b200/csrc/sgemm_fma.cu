@@ -4,7 +4,7 @@
 // row-major fp32 with leading dimensions, C overwritten.  Each output is one
 // fp32 fused-multiply-add chain over k in ascending order -- the order of Oct's
 // CPU oracle `cpuSGEMM` (internal/prometheus/runtime.go:319-331) -- so it is
-// the plain-fp32 control against which the 3xTF32 path is judged.
+// the plain-fp32 control the 3xTF32 path is compared with.
 //
 // Tiling: 128x128 output tile per 256-thread CTA, 8x8 outputs per thread held
 // in registers, K staged 8 deep through double-buffered shared memory with a

@@ -3,7 +3,7 @@
 Only tests/ and bench.py's CPU leg use this module, as the checker; the product
 (libprometheus_reactor.so) never calls it.  It restates, step by step, the
 reference's CPU block code in numpy float64 so every output of the CUDA block
-can be compared against it (BASELINE tolerance: <= 1e-4 per block output).
+can be compared against it (tolerance: <= 1e-4 relative per block output).
 
 DiT block: `runCanonicalNoiseRefiner0` (internal/prometheus/zimage/canonical_reference.go:377-479)
   adaLN linear -> tanh(gates), scales + 1            (:358-381)
@@ -16,7 +16,7 @@ DiT block: `runCanonicalNoiseRefiner0` (internal/prometheus/zimage/canonical_ref
   exact softmax attention, scale 1/sqrt(head_dim) (`canonicalAttention`, :241-289)
   out projection -> RMSNorm -> gated residual (`canonicalAddGate`, :201-210)
   FFN norm -> modulation -> w1, w3 -> silu(w1)*w3 (:455-458) -> w2 -> RMSNorm -> gated residual.
-  BASELINE extensions (unpinned by the reference, which has 4 x hidden and no
+  Extensions of the benchmark configs (unpinned by the reference, which has 4 x hidden and no
   shift): a 6 x hidden adaLN whose extra parts are additive shifts applied after
   each modulation, and a 256-d sinusoidal timestep embedding [cos | sin] with
   frequencies exp(-ln(10000) i / 128) computed here instead of read from a file.
@@ -62,13 +62,13 @@ class BlockConfig:
 
 def gemma_config(seq_len: int = 1024, hidden: int = 2048, heads: int = 8, head_dim: int = 256, ffn: int = 16384,
                  kv_heads: int = 1) -> BlockConfig:
-    """Gemma-2B-shaped decoder block."""
+    """The benchmark's Gemma-2B-shaped decoder block (4 x 1024 tokens, hidden 2048, 8 x 256 MQA, GeGLU 16384)."""
     return BlockConfig(GEMMA, hidden, heads, kv_heads, head_dim, ffn, seq_len, eps=1e-6, rope_base=10000.0)
 
 
 def dit_config(seq_len: int = 4096, hidden: int = 3072, heads: int = 24, head_dim: int = 128, ffn: int = 8192,
                grid_w: int = 64, rope_frame: int = 33) -> BlockConfig:
-    """Z-Image-style DiT block (64 x 64 latent patches)."""
+    """The benchmark's Z-Image-style DiT block (2 x 4096 tokens = 64 x 64 latent patches, hidden 3072)."""
     return BlockConfig(DIT, hidden, heads, heads, head_dim, ffn, seq_len, eps=1e-5, rope_base=256.0,
                        grid_w=grid_w, rope_frame=rope_frame)
 
@@ -90,7 +90,7 @@ def weight_shapes(cfg: BlockConfig) -> dict[str, tuple]:
 
 
 def random_weights(cfg: BlockConfig, seed: int) -> dict[str, np.ndarray]:
-    """BASELINE init: linear weights N(0, 0.02); norm gains 1 + N(0, 0.02); adaLN bias 0."""
+    """Benchmark init: linear weights N(0, 0.02); norm gains 1 + N(0, 0.02); adaLN bias 0."""
     rng = np.random.Generator(np.random.PCG64(seed))
     out = {}
     for name, shape in weight_shapes(cfg).items():

@@ -206,12 +206,12 @@ def reduction_input(rows: int, width: int, distribution: str = "deterministic", 
 
 
 def uniform_matrix(rows: int, cols: int, seed: int) -> np.ndarray:
-    """Seeded U[-1, 1) fp32 matrix (PCG64): the BASELINE SGEMM input distribution."""
+    """Seeded U[-1, 1) fp32 matrix (PCG64): the SGEMM benchmark input distribution."""
     rng = np.random.Generator(np.random.PCG64(seed))
     return (rng.random((rows, cols), dtype=np.float32) * np.float32(2.0) - np.float32(1.0)).astype(np.float32)
 
 
 def normal_matrix(rows: int, cols: int, seed: int) -> np.ndarray:
-    """Seeded N(0, 1) fp32 matrix (PCG64): the BASELINE reduction input distribution."""
+    """Seeded N(0, 1) fp32 matrix (PCG64): the reduction benchmark input distribution."""
     rng = np.random.Generator(np.random.PCG64(seed))
     return rng.standard_normal((rows, cols), dtype=np.float32)

@@ -1,9 +1,9 @@
 """Transformer-block parity on the B200 against the binary64 oracle (oracle/blocks.py).
 
-Tolerance (BASELINE: <= 1e-4 per block output), written here:
+Tolerance (<= 1e-4 per block output), written here:
   normwise relative error max|y - y64| / max|y64| <= 1e-4 for every block output,
   and relative L2 error ||y - y64|| / ||y64|| <= 1e-5.
-Cases: reduced dims, then the BASELINE hidden / head / FFN dims with shorter
+Cases: reduced dims, then the benchmark hidden / head / FFN dims with shorter
 sequences (the oracle runs in seconds); both through the device and the host
 entry points.
 """

@@ -2,7 +2,7 @@
 
 Gates (written here): the reference comparator prom_reduction_compare
 (reactor_vulkan_fused_reduction.c:1038-1114, restated in the oracle), plus
-BASELINE's max relative error <= 1e-5 versus the fp64 oracle, elementwise with
+max relative error <= 1e-5 versus the fp64 oracle, elementwise with
 the comparator's floor (|ref| < 1e-20 -> denominator 1).  SUM accumulates in
 binary64 on the device and MAX is exact, so both also match the known answers
 bit for bit.
@@ -55,7 +55,7 @@ def test_row_counts(runtime, oracle_mod, golden, rows):
 @pytest.mark.parametrize("width", [256, 2048, 4096])
 @pytest.mark.parametrize("op", [R.OP_SUM, R.OP_MAX, R.OP_SOFTMAX])
 def test_baseline_shapes(runtime, oracle_mod, width, op):
-    """32768 rows x {256, 2048, 4096}, N(0,1) seeded."""
+    """Benchmark shapes: 32768 rows x {256, 2048, 4096}, N(0,1) seeded."""
     o = oracle_mod
     rows = 32768
     x = o.normal_matrix(rows, width, seed=width)
@@ -138,7 +138,7 @@ def test_rmsnorm_known_answers(runtime, oracle_mod, golden, w):
 
 @pytest.mark.parametrize("width", [256, 2048, 4096, 33])
 def test_rmsnorm_baseline(runtime, oracle_mod, width):
-    """BASELINE configs[2] RMSNorm: eps 1e-6, gamma ~ U[0.5, 1.5)."""
+    """Benchmark RMSNorm: 32768 rows, eps 1e-6, gamma ~ U[0.5, 1.5)."""
     o = oracle_mod
     rows = 32768 if width != 33 else 100
     x = o.normal_matrix(rows, width, seed=width + 1)

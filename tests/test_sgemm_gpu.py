@@ -4,7 +4,7 @@ exact known answers of the reference's own test matrices.
 Tolerances (written here, applied to every case):
   * Oct's own gate compareAgainstOracle (runtime.go:12-15, 339-383): an element
     fails when BOTH |err| > 1e-4 and rel > 1e-4 versus cpuSGEMM.
-  * BASELINE's "max relative error <= 1e-5 versus an fp64 oracle", measured
+  * "max relative error <= 1e-5 versus an fp64 oracle", measured
     normwise: max|C - C64| / max|C64| <= 1e-5 (elementwise relative error is
     unbounded where cancellation drives an output to ~0, for any fp32 method).
   * No worse than Oct's own fp32 CPU path: max|C - C64| <= 2 * max|cpuSGEMM - C64|
@@ -176,7 +176,7 @@ def _check_against_fp64(o, c, a, b, m, n, k, rows=None):
 @pytest.mark.parametrize("variant", VARIANTS)
 @pytest.mark.parametrize("shape,seed", [((512, 512, 512), 0), ((1000, 1000, 1000), 1), ((4097, 4095, 1023), 2)])
 def test_baseline_shapes_full_compare(runtime, oracle_mod, shape, seed, variant):
-    """BASELINE configs[0] and the ragged sweep's smaller shapes: every output vs fp64."""
+    """512^3 and the ragged sweep's smaller shapes: every output vs fp64."""
     o = oracle_mod
     m, n, k = shape
     a, b = o.uniform_matrix(m, k, seed).ravel(), o.uniform_matrix(k, n, seed + 100).ravel()
