@@ -172,8 +172,11 @@ cudaError_t tp_reduce_rows(const TpReduce& args, cudaStream_t stream);
 // sgemm_smallm_scratch_bytes (may be 0 bytes: then it may be null).
 bool sgemm_smallm_supported(uint32_t m);
 uint64_t sgemm_smallm_scratch_bytes(uint32_t m, uint32_t n, uint32_t k);
+// With `err` (the kernel status word) and B rows copyable in 16-byte units, the
+// bulk-copy-fed variant runs; otherwise the register-streaming one.
 cudaError_t sgemm_smallm(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
-                         uint32_t m, uint32_t n, uint32_t k, void* scratch, cudaStream_t stream);
+                         uint32_t m, uint32_t n, uint32_t k, void* scratch, cudaStream_t stream,
+                         unsigned int* err = nullptr);
 
 // ---------------------------------------------------------------- reductions
 // op: 1 = row sum, 2 = row max, 3 = stable softmax.  `nonfinite` (device

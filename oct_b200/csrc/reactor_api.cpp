@@ -213,7 +213,8 @@ int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uin
     if (!oct::sgemm_smallm_supported(m)) return OCT_B200_DETAIL_UNSUPPORTED_SHAPE;
     const uint64_t need = oct::sgemm_smallm_scratch_bytes(m, n, k);
     if (need != 0 && scratch->ensure(need, stream) != cudaSuccess) return OCT_B200_DETAIL_OUT_OF_MEMORY;
-    e = oct::sgemm_smallm(a, lda, b, ldb, c, ldc, m, n, k, need != 0 ? scratch->aligned() : nullptr, stream);
+    e = oct::sgemm_smallm(a, lda, b, ldb, c, ldc, m, n, k, need != 0 ? scratch->aligned() : nullptr, stream,
+                          rt->err_word());
   } else if (variant == OCT_B200_SGEMM_FMA) {
     e = oct::sgemm_fma(a, lda, b, ldb, c, ldc, m, n, k, stream, batch);
   } else if (variant == OCT_B200_SGEMM_TC3XTF32 || variant == 16u || variant == 32u || variant == 216u ||

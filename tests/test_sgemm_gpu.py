@@ -133,11 +133,14 @@ def test_gemma_small_m_corpus(runtime, oracle_mod, golden, shape, variant):
 
 @pytest.mark.parametrize("shape", [(1, 256, 1536), (2, 256, 1536), (7, 256, 1536), (15, 256, 1536),
                                    (16, 256, 1536), (15, 2048, 1536), (16, 16384, 2048), (1, 16384, 2048),
-                                   (9, 1001, 777), (3, 5, 7), (16, 3, 40000)])
+                                   (9, 1001, 777), (3, 5, 7), (16, 3, 40000), (8, 16384, 2048),
+                                   (5, 1004, 777), (16, 12, 40000), (4, 2052, 3)])
 def test_small_m_kernel(runtime, oracle_mod, golden, shape):
     """The small-M kernel (m <= 16, split-K with an ordered reduction): the reference's small-M
     corpus shapes (gemma4e2b_sgemm_corpus_test.go:44-59), Gemma per-token shapes, ragged and
-    deep-K ones; AUTO takes it for m <= 16; repeat calls are bit-identical."""
+    deep-K ones; AUTO takes it for m <= 16; repeat calls are bit-identical.  n a multiple of 4
+    takes the bulk-copy-fed kernel (ragged column tiles and K ranges included), other n the
+    register-streaming one."""
     o = oracle_mod
     m, n, k = shape
     a, b = o.uniform_matrix(m, k, m + n).ravel(), o.uniform_matrix(k, n, k).ravel()
