@@ -201,37 +201,45 @@ def reduction_measurements(rt, torch, hbm_peak: float) -> list[dict]:
     out = []
     stream = torch.cuda.current_stream()
     rows = 32768
+    l2_bytes = 126 * 2 ** 20
     for width in (256, 2048, 4096):
         g = torch.Generator(device="cuda").manual_seed(width)
-        x = torch.randn(rows, width, device="cuda", generator=g)
+        # back-to-back launches rotate over enough inputs that each one was evicted from L2
+        # (126 MB) by the launches before it: 12 x 33.5 MB at W = 256, 2 at the larger widths
+        nbuf = max(2, -(-3 * l2_bytes // (4 * rows * width)))
+        xs = [torch.randn(rows, width, device="cuda", generator=g) for _ in range(nbuf)]
         w = torch.rand(width, device="cuda", generator=g) + 0.5
         y_row = torch.empty(rows, device="cuda")
-        y_full = torch.empty_like(x)
+        y_full = torch.empty_like(xs[0])
         inv = torch.empty(rows, device="cuda")
         for name, fn, nbytes in (
-            ("row_sum", lambda: rt.reduction_device(x, y_row, rows, width, R.OP_SUM, stream), 4 * rows * width + 4 * rows),
-            ("row_max", lambda: rt.reduction_device(x, y_row, rows, width, R.OP_MAX, stream), 4 * rows * width + 4 * rows),
-            ("softmax", lambda: rt.reduction_device(x, y_full, rows, width, R.OP_SOFTMAX, stream), 8 * rows * width),
-            ("rmsnorm", lambda: rt.rmsnorm_device(x, w, y_full, inv, rows, width, 1e-6, stream),
+            ("row_sum", lambda x: rt.reduction_device(x, y_row, rows, width, R.OP_SUM, stream),
+             4 * rows * width + 4 * rows),
+            ("row_max", lambda x: rt.reduction_device(x, y_row, rows, width, R.OP_MAX, stream),
+             4 * rows * width + 4 * rows),
+            ("softmax", lambda x: rt.reduction_device(x, y_full, rows, width, R.OP_SOFTMAX, stream),
+             8 * rows * width),
+            ("rmsnorm", lambda x: rt.rmsnorm_device(x, w, y_full, inv, rows, width, 1e-6, stream),
              8 * rows * width + 4 * width),
         ):
-            for _ in range(3):
-                fn()
+            for i in range(max(3, nbuf)):
+                fn(xs[i % nbuf])
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            iters = 20
+            iters = 24
             e0.record(stream)
-            for _ in range(iters):
-                fn()
+            for i in range(iters):
+                fn(xs[i % nbuf])
             e1.record(stream)
             e1.synchronize()
             ms = e0.elapsed_time(e1) / iters
             gbs = nbytes / (ms * 1e-3) / 1e9
             out.append({"kernel": name, "rows": rows, "width": width, "ms": round(ms, 5), "GB/s": round(gbs, 1),
-                        "frac_of_hbm": round(gbs / hbm_peak, 3), "bytes": nbytes})
+                        "frac_of_hbm": round(gbs / hbm_peak, 3), "bytes": nbytes,
+                        "l2": f"inputs rotate over {nbuf} buffers ({nbuf * 4 * rows * width / 1e6:.0f} MB)"})
         st = rt.sync_status()
         if not st.ok:
             raise RuntimeError(f"reduction status {st}")
-        del x, y_full, y_row, inv
+        del xs, y_full, y_row, inv
     return out
 
 

@@ -163,7 +163,10 @@ uint32_t smallm_splits(uint32_t m, uint32_t n, uint32_t k) {
 // per stage, five stages in flight), so the loads run ahead of the FMAs, and all
 // m <= 16 rows live in one CTA (no row groups re-reading B from L2).  The CTA's
 // two halves (warps 0-3, 4-7) take rows 0-3 and 4-7 of each stage, each thread
-// four columns; the halves' sums meet in shared memory at the end.  A's rows
+// four columns; the halves' sums meet in shared memory at the end.  Warps never
+// wait for one another inside the K loop: a slot's full barrier (the copies)
+// and empty barrier (one arrival per warp) order it, and thread 0 refills a
+// slot once all eight warps have released it.  A's rows
 // for the CTA's K range are staged once in shared memory and read as float4
 // (four k values per load).  Split-K with the same ordered reduction.
 constexpr int BK_THREADS = 256;
@@ -179,8 +182,10 @@ __global__ void __launch_bounds__(BK_THREADS, 2) sgemm_smallm_bulk_kernel(
   extern __shared__ __align__(128) uint8_t smem_raw[];
   float* ring = reinterpret_cast<float*>(smem_raw);  // [stage][BK_SR][SM_COLS]
   float* as = ring + BK_STAGES * BK_SR * SM_COLS;    // [MR][BK_KMAX]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(as + MR * BK_KMAX);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(as + MR * BK_KMAX);  // full[BK_STAGES], empty[BK_STAGES]
+  uint64_t* empty = bars + BK_STAGES;
   __shared__ bool last_cta;
+  __shared__ int abort_flag;
   const uint32_t tid = threadIdx.x, half = tid / SM_THREADS, lane4 = tid % SM_THREADS;
   const uint32_t col0 = blockIdx.x * SM_COLS;
   const uint32_t cols = min(static_cast<uint32_t>(SM_COLS), n - col0);
@@ -190,7 +195,11 @@ __global__ void __launch_bounds__(BK_THREADS, 2) sgemm_smallm_bulk_kernel(
   const uint32_t stages_total = (kn + BK_SR - 1) / BK_SR;
   const uint32_t col = col0 + lane4 * 4;
   if (tid == 0) {
-    for (int s = 0; s < BK_STAGES; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < BK_STAGES; ++s) {
+      mbar_init(&bars[s], 1);
+      mbar_init(&empty[s], BK_THREADS / 32);
+    }
+    abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
   }
@@ -203,12 +212,22 @@ __global__ void __launch_bounds__(BK_THREADS, 2) sgemm_smallm_bulk_kernel(
     for (uint32_t i = 0; i < nr; ++i)
       bulk_load(dst + i * SM_COLS, b + static_cast<uint64_t>(r0 + i) * ldb + col0, cols * 4u, &bars[slot]);
   };
+  uint32_t issued = min(stages_total, static_cast<uint32_t>(BK_STAGES));  // thread 0's count
   if (tid == 0)
-    for (uint32_t st = 0; st < stages_total && st < static_cast<uint32_t>(BK_STAGES); ++st) issue(st);
-  // A rows of this CTA's K range -> shared memory (zero past m / kn), while the first copies fly
-  for (uint32_t i = tid; i < MR * BK_KMAX; i += BK_THREADS) {
-    const uint32_t r = i / BK_KMAX, kk = i % BK_KMAX;
-    as[i] = (r < m && kk < kn) ? a[static_cast<uint64_t>(r) * lda + k0 + kk] : 0.f;
+    for (uint32_t st = 0; st < issued; ++st) issue(st);
+  // A rows of this CTA's K range -> shared memory (zero past m / kn), while the
+  // first copies fly; all of a thread's loads are issued before the first store
+  static_assert(BK_KMAX % BK_THREADS == 0, "A staging assumes whole rows per pass");
+  {
+    constexpr int kPer = MR * BK_KMAX / BK_THREADS;
+    float v[kPer];
+#pragma unroll
+    for (int it = 0; it < kPer; ++it) {
+      const uint32_t i = tid + it * BK_THREADS, r = i / BK_KMAX, kk = i % BK_KMAX;
+      v[it] = (r < m && kk < kn) ? __ldg(&a[static_cast<uint64_t>(r) * lda + k0 + kk]) : 0.f;
+    }
+#pragma unroll
+    for (int it = 0; it < kPer; ++it) as[tid + it * BK_THREADS] = v[it];
   }
   __syncthreads();
   float acc[MR][4];
@@ -217,12 +236,12 @@ __global__ void __launch_bounds__(BK_THREADS, 2) sgemm_smallm_bulk_kernel(
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
   bool ok = true;
-  uint32_t failed_at = stages_total;
   for (uint32_t st = 0; st < stages_total; ++st) {
     const uint32_t slot = st % BK_STAGES;
-    ok = __syncthreads_and(mbar_wait(&bars[slot], (st / BK_STAGES) & 1u, err, kErrWaitRow)) != 0;
-    if (!ok) {
-      failed_at = st;
+    ok = __all_sync(0xffffffffu, ok && mbar_wait(&bars[slot], (st / BK_STAGES) & 1u, err, kErrWaitRow));
+    if (!ok || *reinterpret_cast<volatile int*>(&abort_flag) != 0) {
+      ok = false;
+      *reinterpret_cast<volatile int*>(&abort_flag) = 1;
       break;
     }
     const uint32_t nr = min(static_cast<uint32_t>(BK_SR), kn - st * BK_SR);
@@ -261,17 +280,23 @@ __global__ void __launch_bounds__(BK_THREADS, 2) sgemm_smallm_bulk_kernel(
         }
       }
     }
-    __syncthreads();  // every thread is done with this slot
+    __syncwarp();
+    if ((tid & 31u) == 0) mbar_arrive(&empty[slot]);  // this warp is done with the slot
     if (tid == 0 && st + BK_STAGES < stages_total) {
-      fence_proxy_async_smem();
-      issue(st + BK_STAGES);
+      // refill once every warp has released the slot (bounded wait)
+      if (mbar_wait(&empty[slot], (st / BK_STAGES) & 1u, err, kErrWaitEmpty)) {
+        fence_proxy_async_smem();
+        issue(st + BK_STAGES);
+        issued = st + BK_STAGES + 1;
+      } else {
+        ok = false;
+      }
     }
   }
-  if (!ok) {
-    // drain: stages [0, failed_at + BK_STAGES) were issued; a slot's phases
-    // complete in order, so waiting (bounded) for its newest copy is enough
+  if (!__syncthreads_and(ok)) {
+    // drain: stages [0, issued) were issued; a slot's phases complete in
+    // order, so waiting (bounded) for its newest copy is enough
     if (tid == 0) {
-      const uint32_t issued = min(stages_total, failed_at + BK_STAGES);
       for (uint32_t s = 0; s < static_cast<uint32_t>(BK_STAGES) && s < issued; ++s) {
         const uint32_t count = (issued - s + BK_STAGES - 1) / BK_STAGES;
         if (!mbar_wait(&bars[s], (count - 1) & 1u, err, kErrWaitDrain)) break;
@@ -358,13 +383,13 @@ bool smallm_bulk_ok(const float* b, uint64_t ldb, uint32_t n) {
 
 template <int MR>
 constexpr uint32_t smallm_bulk_smem() {
-  return (BK_STAGES * BK_SR * SM_COLS + MR * BK_KMAX) * 4u + BK_STAGES * 8u;
+  return (BK_STAGES * BK_SR * SM_COLS + MR * BK_KMAX) * 4u + 2u * BK_STAGES * 8u;
 }
 
 // resident CTAs per SM by shared memory (228 KB per SM, 1 KB reserved per CTA)
 constexpr uint32_t smallm_bulk_per_sm(uint32_t m) {
   const uint32_t mr = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : m <= 8 ? 8 : 16;
-  const uint32_t smem = (BK_STAGES * BK_SR * SM_COLS + mr * BK_KMAX) * 4u + BK_STAGES * 8u + 1024u;
+  const uint32_t smem = (BK_STAGES * BK_SR * SM_COLS + mr * BK_KMAX) * 4u + 2u * BK_STAGES * 8u + 1024u;
   return 233472u / smem;
 }
 
