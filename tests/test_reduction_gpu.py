@@ -71,6 +71,23 @@ def test_baseline_shapes(runtime, oracle_mod, width, op):
         assert np.array_equal(y, ref)
 
 
+@pytest.mark.parametrize("rows,width", [(30001, 256), (40000, 128), (32768, 512)])
+@pytest.mark.parametrize("op", [R.OP_SUM, R.OP_MAX, R.OP_SOFTMAX])
+def test_tall_short_rows(runtime, oracle_mod, rows, width, op):
+    """Tall matrices of short rows whose row count leaves the last ring slot ragged, and
+    rows too many for every warp to hold all of its rows in the ring at once."""
+    o = oracle_mod
+    x = o.normal_matrix(rows, width, seed=rows + width)
+    y, res = runtime.reduction(x, op)
+    assert y is not None, res.detail_code
+    _, ref = o.reduction_cpu_reference(x, op, threads=o.max_threads())
+    assert o.reduction_compare(rows, width, op, ref, y)[0] == 0
+    if op == R.OP_SOFTMAX:
+        assert rel_err(y, ref) <= REL_TOL
+    else:
+        assert np.array_equal(y, ref)
+
+
 @pytest.mark.parametrize("width", [7, 33, 1057, 9000])
 def test_unaligned_and_wide_rows_use_same_arithmetic(runtime, oracle_mod, width):
     o = oracle_mod
