@@ -90,6 +90,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Waits until the grids this one depends on (the previous kernel in the stream,
+// when this one was launched with programmatic stream serialization) have
+// completed and their memory operations are visible; a no-op otherwise.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the next kernel in the stream be scheduled before this grid exits (it
+// still waits in griddep_wait for this grid to complete).
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 // 2-D tiled load of one box into shared memory, completing on `bar`.
 // The innermost coordinate x is in elements; x * sizeof(elem) must be a

@@ -39,6 +39,25 @@ constexpr int THREADS = 256;
 constexpr uint32_t SLOT_BUDGET_BYTES = 64 * 1024;  // ring size per CTA
 constexpr uint32_t BULK_MAX_WIDTH = 8192;
 
+// Launches a one-wave ring kernel with programmatic stream serialization: it may
+// be scheduled while the previous kernel in the stream drains, and it waits
+// (griddep_wait) for that kernel to complete before touching global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, uint32_t smem, cudaStream_t stream,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 enum Op : int { kSum = 1, kMax = 2, kSoftmax = 3, kRms = 4 };
 
 __device__ __forceinline__ double warp_sum_d(double v) {
@@ -208,6 +227,11 @@ __global__ void __launch_bounds__(THREADS) row_bulk_kernel(const float* __restri
     fence_proxy_async_smem();
   }
   __syncthreads();
+  // The rows (and the output) may belong to the previous kernel in the stream:
+  // wait for it to complete before the first global access.  The grid is one
+  // wave, so the next reduction's CTAs may be scheduled as these exit.
+  griddep_wait();
+  griddep_launch_dependents();
 
   auto issue = [&](uint32_t batch, uint32_t slot) {
     const uint32_t r0 = batch * RPB;
@@ -299,6 +323,8 @@ __global__ void __launch_bounds__(THREADS) row_warp_kernel(const float* __restri
     fence_proxy_async_smem();
   }
   __syncwarp();
+  griddep_wait();  // as in row_bulk_kernel: the previous kernel completes first
+  griddep_launch_dependents();
   const uint32_t gw = blockIdx.x * wpc + warp, nw = gridDim.x * wpc;
   const uint32_t units = (rows + rps - 1) / rps;
   const uint32_t row_bytes = w * 4u;
@@ -395,9 +421,8 @@ cudaError_t launch_warp(const float* in, uint64_t stride, float* out, float* inv
   const uint32_t units = (rows + rps - 1) / rps;
   const uint32_t need = (units + wpc - 1) / wpc;
   const uint32_t cap = static_cast<uint32_t>(sms * per_sm);
-  kern<<<need < cap ? need : cap, wpc * 32, smem, stream>>>(in, stride, out, inv_rms, weight, eps, rows, w, ns, wpc,
-                                                            rps, nonfinite, err);
-  return cudaGetLastError();
+  return launch_dependent(kern, dim3(need < cap ? need : cap), dim3(wpc * 32), smem, stream, in, stride, out, inv_rms,
+                          weight, eps, rows, w, ns, wpc, rps, nonfinite, err);
 }
 
 // Plain-load fallback: one CTA per row, any width / alignment.  Same arithmetic.
@@ -481,8 +506,8 @@ cudaError_t launch_bulk(const float* in, uint64_t stride, float* out, float* inv
   if (per_sm < 1) per_sm = 1;
   const uint32_t batches = (rows + RPB - 1) / RPB;
   const uint32_t grid = static_cast<uint32_t>(batches < static_cast<uint32_t>(sms * per_sm) ? batches : sms * per_sm);
-  kern<<<grid, THREADS, smem, stream>>>(in, stride, out, inv_rms, weight, eps, rows, w, ns, nonfinite, err);
-  return cudaGetLastError();
+  return launch_dependent(kern, dim3(grid), dim3(THREADS), smem, stream, in, stride, out, inv_rms, weight, eps, rows,
+                          w, ns, nonfinite, err);
 }
 
 template <int OP>
