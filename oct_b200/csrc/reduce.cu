@@ -228,10 +228,10 @@ __global__ void __launch_bounds__(THREADS) row_bulk_kernel(const float* __restri
   }
   __syncthreads();
   // The rows (and the output) may belong to the previous kernel in the stream:
-  // wait for it to complete before the first global access.  The grid is one
-  // wave, so the next reduction's CTAs may be scheduled as these exit.
+  // wait for it to complete before the first global access.  No early trigger:
+  // work after this kernel is released at its completion, as without the
+  // launch attribute.
   griddep_wait();
-  griddep_launch_dependents();
 
   auto issue = [&](uint32_t batch, uint32_t slot) {
     const uint32_t r0 = batch * RPB;
@@ -324,7 +324,6 @@ __global__ void __launch_bounds__(THREADS) row_warp_kernel(const float* __restri
   }
   __syncwarp();
   griddep_wait();  // as in row_bulk_kernel: the previous kernel completes first
-  griddep_launch_dependents();
   const uint32_t gw = blockIdx.x * wpc + warp, nw = gridDim.x * wpc;
   const uint32_t units = (rows + rps - 1) / rps;
   const uint32_t row_bytes = w * 4u;

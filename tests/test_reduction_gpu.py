@@ -169,6 +169,27 @@ def test_rmsnorm_baseline(runtime, oracle_mod, width):
     assert rel_err(y, ref32) <= 1e-4  # the fp32 canonical formula differs by its own rounding only
 
 
+def test_device_output_read_right_after_the_call(runtime, oracle_mod):
+    """A long device-path launch whose output is copied back right after the status read: the
+    copy must see every row (outputs start as NaN)."""
+    import torch
+    o = oracle_mod
+    x = o.normal_matrix(32768, 4096, seed=9)
+    dx = torch.from_numpy(x).cuda()
+    w = torch.ones(4096, device="cuda")
+    for _ in range(2):
+        yr = torch.full_like(dx, float("nan"))
+        inv = torch.full((32768,), float("nan"), device="cuda")
+        ys = torch.full((32768,), float("nan"), device="cuda")
+        torch.cuda.synchronize()
+        runtime.reduction_device(dx, ys, 32768, 4096, R.OP_SUM)
+        runtime.rmsnorm_device(dx, w, yr, inv, 32768, 4096, 1e-6)
+        assert runtime.sync_status().ok
+        y = yr.cpu().numpy()
+        assert not np.isnan(y).any() and not np.isnan(inv.cpu().numpy()).any()
+        assert np.array_equal(ys.cpu().numpy(), o.reduction_cpu_reference(x, R.OP_SUM, o.max_threads())[1])
+
+
 def test_device_entry_points(runtime, oracle_mod):
     import torch
     o = oracle_mod
