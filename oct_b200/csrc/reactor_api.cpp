@@ -206,8 +206,9 @@ int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uin
                   const oct::GemmBatch* batch = nullptr, DevBuf* scratch = nullptr) {
   variant = resolve_variant(variant, m, n, k);
   if (scratch == nullptr) scratch = &rt->scratch;
-  // the small-M kernel has no batched form: strided batches take the FMA control
-  if (variant == OCT_B200_SGEMM_SMALLM && batch != nullptr && batch->count > 1) variant = OCT_B200_SGEMM_FMA;
+  // the small-M kernel has no batched or B^T form: those take the FMA control
+  if (variant == OCT_B200_SGEMM_SMALLM && batch != nullptr && (batch->count > 1 || batch->b_trans))
+    variant = OCT_B200_SGEMM_FMA;
   cudaError_t e;
   if (variant == OCT_B200_SGEMM_SMALLM) {
     if (!oct::sgemm_smallm_supported(m)) return OCT_B200_DETAIL_UNSUPPORTED_SHAPE;

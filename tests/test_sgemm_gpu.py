@@ -240,6 +240,26 @@ def test_variants_agree_with_batched_and_transposed_forms(runtime, oracle_mod):
             assert normwise(got[i].ravel(), ref) <= NORMWISE_TOL, (variant, i)
 
 
+@pytest.mark.parametrize("bsz,m", [(1, 8), (2, 1), (1, 16)])
+def test_small_m_batched_and_transposed_forms(runtime, oracle_mod, bsz, m):
+    """m <= 16 through the strided-batch entry with B^T: AUTO and the small-M id fall back to a
+    kernel that reads B^T (the small-M kernel has neither form), one entry included."""
+    import torch
+    o = oracle_mod
+    n, k = 264, 136
+    a = o.uniform_matrix(bsz * m, k, 41).reshape(bsz, m, k)
+    bt = o.uniform_matrix(bsz * n, k, 42).reshape(bsz, n, k)
+    da, dbt = torch.from_numpy(a).cuda(), torch.from_numpy(bt).cuda()
+    for variant in (R.SGEMM_AUTO, R.SGEMM_SMALLM):
+        dc = torch.full((bsz, m, n), float("nan"), device="cuda")
+        runtime.sgemm_batched_device(da, k, m * k, dbt, k, n * k, True, dc, n, m * n, bsz, m, n, k, variant)
+        assert runtime.sync_status().ok
+        got = dc.cpu().numpy()
+        for i in range(bsz):
+            ref = o.sgemm_f64(np.ascontiguousarray(a[i]).ravel(), np.ascontiguousarray(bt[i].T).ravel(), m, n, k)
+            assert normwise(got[i].ravel(), ref) <= NORMWISE_TOL, (variant, i)
+
+
 def test_host_abi_matches_device_path(runtime, oracle_mod):
     o = oracle_mod
     m, n, k = 300, 517, 129
