@@ -17,8 +17,9 @@ Headline metric: fp32 SGEMM TFLOP/s at 8192^3.
     copy of A and B and the device->host copy of C are inside the timed region.
   * `roofline`: the main kernel's useful flops per launch / its CUDA-event time
     on the launch stream, against the 3xTF32-adjusted tensor peak derived from
-    the measured dense bf16 peak (tf32 runs at half the bf16 rate, and each fp32
-    product costs three tf32 products): peak = bf16_tflops / 6.
+    the measured burst dense bf16 peak (tf32 runs at half the bf16 rate, and each
+    fp32 product costs three tf32 products): peak = bf16_tflops / 6, scaled by the
+    run's median SM clock over the maximum when the part ran below it.
   * `cpu_baseline`: Oct's CPU SGEMM (`cpuSGEMM`, internal/prometheus/runtime.go:319-331,
     restated in oracle/oracle.c) on all host cores, over a bounded row sample.
 
@@ -79,15 +80,45 @@ def peaks() -> tuple[dict, str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
+def nvidia_smi_selector(props) -> str:
+    """The `nvidia-smi -i` argument naming the GPU behind a CUDA device.
+
+    nvidia-smi ignores CUDA_VISIBLE_DEVICES and numbers every GPU of the node, so
+    the CUDA ordinal would name another GPU whenever the visible set is a subset
+    (a lease of GPU 3 is CUDA device 0).  The device's UUID names it on both sides."""
+    uuid = str(getattr(props, "uuid", "") or "")
+    if not uuid:
+        raise ValueError("device properties carry no UUID")
+    return uuid if uuid.startswith(("GPU-", "MIG-")) else f"GPU-{uuid}"
+
+
+def tensor_roofline_peak(pk: dict, pk_kind: str, clock_rec: dict) -> tuple[float, str]:
+    """The 3xTF32-adjusted tensor peak a kernel timed in this run is held against.
+
+    The measured burst cuBLAS bf16 figure / 2 (tf32 runs at half the bf16 rate) / 3
+    (products per fp32 MAC).  The burst figure is taken at the maximum SM clock; when
+    this run's clock record shows the part below it (the 1 kW power cap), the peak is
+    scaled by the median SM clock under load over the maximum, and the note says so."""
+    burst = pk["bf16_tflops"] / 6.0
+    note = f"{pk_kind}: bf16_tflops {pk['bf16_tflops']} (burst) / 2 (tf32 rate) / 3 (products)"
+    sm, smax = clock_rec.get("sm_mhz"), clock_rec.get("sm_max_mhz") or pk.get("sm_max_mhz")
+    if sm and smax and sm < 0.98 * smax:
+        ratio = sm / smax
+        return burst * ratio, note + f", scaled by the median SM clock {sm:.0f} / max {smax:.0f} MHz = {ratio:.3f}"
+    return burst, note + (f", part at its maximum clock (median {sm:.0f} MHz)" if sm else ", no clock record")
+
+
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 50 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms during the timed region.
+
+    `gpu` is an nvidia-smi selector (a UUID from nvidia_smi_selector), never a CUDA ordinal."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, gpu: str):
+        self.gpu = gpu
         self.proc = None
         self.lines: list[str] = []
 
@@ -131,9 +162,9 @@ class ClockSampler:
                 if flag.lower().startswith("active"):
                     reasons.add(name)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "gpu": self.gpu}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "gpu": self.gpu}
 
 
 def cpu_sgemm_sample(m: int, n: int, k: int, seconds: float, threads: int) -> dict:
@@ -306,7 +337,7 @@ def attention_measurements(rt, torch, stream, iters: int = 5) -> list[dict]:
     """The fused attention kernel alone at the DiT block's shape (2 items x 4096 tokens x 24 heads of 128)."""
     from oracle import blocks as OB  # used only for the shape
     pk, _ = peaks()
-    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
+    peak = pk["bf16_tflops"] / 6.0  # burst 3xTF32-adjusted peak
     cfg, items = OB.dit_config(), 2
     seq, heads, hd = cfg.seq_len, cfg.heads, cfg.head_dim
     g = torch.Generator(device="cuda").manual_seed(5)
@@ -341,7 +372,7 @@ def block_measurements(rt, torch, stream, iters: int = 5, only: str | None = Non
     from oct_b200 import reactor as R
     from oracle import blocks as OB  # used only for the shapes and the flop count
     pk, _ = peaks()
-    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
+    peak = pk["bf16_tflops"] / 6.0  # burst 3xTF32-adjusted peak
     res = []
     for name, cfg, batch in (("gemma_block", OB.gemma_config(), 4), ("dit_block", OB.dit_config(), 2)):
         if only is not None and name != only:
@@ -390,7 +421,7 @@ def sharded_sgemm_measurements(rt, torch, dist, rank: int, world: int, stream, i
     from oct_b200 import reactor as R
     res = []
     pk, _ = peaks()
-    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
+    peak = pk["bf16_tflops"] / 6.0  # burst 3xTF32-adjusted peak
     for (m, n, k) in ((8192, 8192, 8192), (16384, 16384, 4096)):
         if n % (world * 256):
             continue
@@ -449,7 +480,7 @@ def _block_group_measure(rt, torch, dist, rank, world, stream, iters, name, cfg,
     if cfg.heads % tp_size or cfg.ffn % tp_size:
         return None
     pk, _ = peaks()
-    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
+    peak = pk["bf16_tflops"] / 6.0  # burst 3xTF32-adjusted peak
     dp = world // tp_size
     group, tp_rank = rank // tp_size, rank % tp_size
     local_batch = batch // dp
@@ -541,7 +572,7 @@ def run_ours(args) -> None:
     rt.read_kernel_timing()  # reset the launch count
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
-    with ClockSampler(local) as clocks:
+    with ClockSampler(nvidia_smi_selector(torch.cuda.get_device_properties(local))) as clocks:
         e0.record(stream)
         for _ in range(args.steps):
             step()
@@ -560,11 +591,10 @@ def run_ours(args) -> None:
     value = flops * world * args.steps / (ms_max * 1e-3) / 1e12
 
     pk, pk_kind = peaks()
-    # The main kernel is timed inside a long continuous loop (the power cap
-    # engages), so the sustained measured peak is the denominator; the burst
-    # fraction is reported beside it.
-    tensor_peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
+    clock_rec = clocks.summary()
+    tensor_peak, peak_note = tensor_roofline_peak(pk, pk_kind, clock_rec)
     tensor_peak_burst = pk["bf16_tflops"] / 6.0
+    tensor_peak_sustained = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6.0
     # The FMA control records no per-kernel events: its whole step is the kernel.
     main_per_launch_ms = main_ms / launches if launches > 0 and main_ms > 0 else ms_max / args.steps
     achieved = flops / (main_per_launch_ms * 1e-3) / 1e12
@@ -651,10 +681,11 @@ def run_ours(args) -> None:
                 "unit": "TFLOP/s",
                 "frac": achieved / tensor_peak,
                 "traffic": traffic,
-                "peak_source": (f"{pk_kind}: bf16_tflops_sustained {pk.get('bf16_tflops_sustained')} / 2 (tf32 rate) "
-                                "/ 3 (products); kernel timed inside a continuous 100-step loop"),
+                "peak_source": peak_note,
                 "frac_of_burst_peak": achieved / tensor_peak_burst,
                 "burst_peak": tensor_peak_burst,
+                "frac_of_sustained_peak": achieved / tensor_peak_sustained,
+                "sustained_peak": tensor_peak_sustained,
                 "algorithmic_flops_per_launch": flops,
                 "main_kernel_ms_per_launch": main_per_launch_ms,
                 "split_pass_ms_per_launch": split_ms / max(1, launches),
@@ -662,7 +693,7 @@ def run_ours(args) -> None:
             "e2e": e2e,
             "cpu_baseline": cpu,
             "gpu_launches": (1 if args.variant == 2 else 3) * args.steps,  # FMA: one kernel; TC: 2 splits + main
-            "clocks": clocks.summary(),
+            "clocks": clock_rec,
             "secondary": secondary,
         }
         print(json.dumps(line), flush=True)

@@ -183,6 +183,7 @@ enum {
   OCT_B200_DETAIL_UNALIGNED = -7005,         /* device pointer not 16-byte aligned */
   OCT_B200_DETAIL_NOALLOC_TOO_LARGE = -7006, /* product needs more than the fixed no-alloc scratch */
   OCT_B200_DETAIL_UNSUPPORTED_SHAPE = -7007, /* shape outside a fused kernel's envelope */
+  OCT_B200_DETAIL_INVALID_ARGUMENT = -7008,  /* null pointer, short leading dimension or out-of-range argument */
   OCT_B200_DETAIL_BLOCK_INVALID = -7010,     /* block configuration / slot / count rejected */
   OCT_B200_DETAIL_BLOCK_ALLOC = -7011,       /* block weights or workspaces could not be allocated */
   OCT_B200_DETAIL_BLOCK_NCCL = -7012,        /* tensor-parallel communicator unavailable */
@@ -757,7 +758,12 @@ PROM_REACTOR_API int oct_b200_sync_status(void* handle, void* stream, int* out_d
    in 64 MiB (any m, n, k <= 2048 does); larger products are rejected with
    PROM_ERROR and OCT_B200_DETAIL_NOALLOC_TOO_LARGE, and C is left untouched.
    The first call on each device looks up the array's device address, so make
-   that first call before any stream capture.  The call waits on `stream` (NULL
+   that first call before any stream capture.  The address is looked up in,
+   and cached for, the device's primary context (the one the CUDA runtime
+   uses); a process that resets the device (cudaDeviceReset) or drives the
+   GPU through another context must not call this entry point afterwards.
+   Null pointers or short leading dimensions fail with
+   OCT_B200_DETAIL_INVALID_ARGUMENT.  The call waits on `stream` (NULL
    = the CUDA default stream) until the product is done and reports an
    in-kernel timeout as OCT_B200_DETAIL_DEVICE_TIMEOUT.  Every call shares the
    one array, so calls whose work overlaps on the GPU (from several host

@@ -1720,7 +1720,7 @@ int oct_b200_sgemm_device_ld(void* handle, const float* d_a, uint64_t lda, const
     Runtime* rt = lookup(handle);
     if (rt == nullptr) return PROM_INVALID_HANDLE;
     if (d_a == nullptr || d_b == nullptr || d_c == nullptr || lda < k || ldb < n || ldc < n) {
-      if (out_detail_code) *out_detail_code = PROM_ERROR;
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_INVALID_ARGUMENT;
       return PROM_ERROR;
     }
     if (!rt->available) {
@@ -1752,7 +1752,7 @@ int oct_b200_sgemm_batched_device(void* handle, const float* d_a, uint64_t lda, 
     const uint64_t need_ldb = b_trans ? k : n;
     if (d_a == nullptr || d_b == nullptr || d_c == nullptr || lda < k || ldb < need_ldb || ldc < n ||
         batch > 65535u) {
-      if (out_detail_code) *out_detail_code = PROM_ERROR;
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_INVALID_ARGUMENT;
       return PROM_ERROR;
     }
     if (!rt->available) {
@@ -1819,7 +1819,7 @@ int oct_b200_attention_device(void* handle, const float* d_q, const float* d_k, 
     Runtime* rt = lookup(handle);
     if (rt == nullptr) return PROM_INVALID_HANDLE;
     if (d_q == nullptr || d_k == nullptr || d_v == nullptr || d_out == nullptr || !finite_f(scale)) {
-      if (out_detail_code) *out_detail_code = PROM_ERROR;
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_INVALID_ARGUMENT;
       return PROM_ERROR;
     }
     if (items == 0 || heads == 0 || seq == 0) return PROM_OK;
@@ -1877,7 +1877,7 @@ int oct_b200_selftest_wait_timeout(void* handle, uint64_t budget_ns, int* out_de
     Runtime* rt = lookup(handle);
     if (rt == nullptr) return PROM_INVALID_HANDLE;
     if (budget_ns < 1000000ull || budget_ns > 1000000000ull) {
-      if (out_detail_code) *out_detail_code = PROM_ERROR;
+      if (out_detail_code) *out_detail_code = OCT_B200_DETAIL_INVALID_ARGUMENT;
       return PROM_ERROR;
     }
     if (!rt->available) {

@@ -824,6 +824,9 @@ unsigned char* g_noalloc_base[kMaxDevices] = {};
 
 // Device address of g_noalloc_scratch on the current device, looked up once
 // per device.  (The array's name in host code is only a host-side stand-in.)
+// The address belongs to the device's primary context, the one the CUDA
+// runtime API uses; after a cudaDeviceReset the cached value would be stale,
+// which the header documents as a limit of this entry point.
 cudaError_t noalloc_base(int dev, unsigned char** out) {
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (g_noalloc_base[dev] == nullptr) {
@@ -904,7 +907,7 @@ extern "C" int oct_b200_sgemm_device_noalloc(const float* d_a, uint64_t lda, con
   try {
     if (out_detail_code != nullptr) *out_detail_code = 0;
     if (d_a == nullptr || d_b == nullptr || d_c == nullptr || lda < k || ldb < n || ldc < n)
-      return fail(PROM_ERROR, PROM_ERROR);
+      return fail(PROM_ERROR, OCT_B200_DETAIL_INVALID_ARGUMENT);
     if (m == 0 || n == 0 || k == 0) return PROM_OK;
     if (sgemm_tc_scratch_bytes(m, n, k) > kNoAllocSplitBytes)
       return fail(PROM_ERROR, OCT_B200_DETAIL_NOALLOC_TOO_LARGE);

@@ -44,6 +44,8 @@ DETAIL_BATCH_PLAN_INVALID, DETAIL_BATCH_EXECUTION_FAILED, DETAIL_BATCH_UNSUPPORT
 DETAIL_PATH_STAGED_UPLOAD_TILED = 6106
 DETAIL_BAD_VARIANT = -7004
 DETAIL_DEVICE_TIMEOUT = -7002  # a bounded in-kernel wait gave up
+DETAIL_NOALLOC_TOO_LARGE = -7006  # product needs more than the no-alloc entry's fixed scratch
+DETAIL_INVALID_ARGUMENT = -7008  # null pointer, short leading dimension or out-of-range argument
 REDUCTION_TESTCFG_FAIL_COMMAND_RECORD = 1 << 0
 REDUCTION_TESTCFG_FAIL_QUEUE_SUBMIT = 1 << 1
 REDUCTION_TESTCFG_FAIL_COMPLETION_OBSERVATION = 1 << 2

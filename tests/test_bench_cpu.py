@@ -15,7 +15,7 @@ CONTRACT_KEYS = ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per
 
 def _sampler(lines):
     import bench
-    cs = bench.ClockSampler(0)
+    cs = bench.ClockSampler("GPU-00000000-0000-0000-0000-000000000000")
     cs.lines = list(lines)
     return cs.summary()
 
@@ -40,7 +40,28 @@ def test_clock_summary_reports_every_slowdown_reason():
 
 
 def test_clock_summary_without_samples():
-    assert _sampler([]) == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+    assert _sampler([]) == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                            "gpu": "GPU-00000000-0000-0000-0000-000000000000"}
+
+
+class _Props:
+    def __init__(self, uuid):
+        self.uuid = uuid
+
+
+def test_clock_sampler_names_the_gpu_by_uuid_not_by_cuda_ordinal(monkeypatch):
+    """Under CUDA_VISIBLE_DEVICES=3 the process's CUDA device 0 is the node's GPU 3;
+    nvidia-smi numbers GPUs node-wide, so the sampler must select by UUID."""
+    import bench
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "3")
+    sel = bench.nvidia_smi_selector(_Props("6f1d2a3b-1111-2222-3333-444455556666"))
+    assert sel == "GPU-6f1d2a3b-1111-2222-3333-444455556666"
+    assert bench.nvidia_smi_selector(_Props("GPU-abc")) == "GPU-abc"  # already prefixed
+    cs = bench.ClockSampler(sel)
+    assert cs.gpu == sel and cs.summary()["gpu"] == sel
+    import pytest
+    with pytest.raises(ValueError):
+        bench.nvidia_smi_selector(_Props(""))
 
 
 def _reference_arm(extra_env=None):
@@ -68,3 +89,14 @@ def test_reference_arm_runs_on_rank_zero_only():
     out = _reference_arm({"RANK": "1"})
     assert out.returncode == 0, out.stderr
     assert out.stdout.strip() == ""
+
+
+def test_roofline_peak_is_the_burst_peak_scaled_by_the_clock_record():
+    import bench
+    pk = {"bf16_tflops": 1642.6, "bf16_tflops_sustained": 1377.5, "sm_max_mhz": 1965.0}
+    peak, note = bench.tensor_roofline_peak(pk, "measured", {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0})
+    assert abs(peak - 1642.6 / 6) < 1e-9 and "maximum clock" in note
+    peak, note = bench.tensor_roofline_peak(pk, "measured", {"sm_mhz": 1572.0, "sm_max_mhz": 1965.0})
+    assert abs(peak - 1642.6 / 6 * 0.8) < 1e-9 and "scaled" in note
+    peak, _ = bench.tensor_roofline_peak(pk, "measured", {"sm_mhz": None, "sm_max_mhz": None})
+    assert abs(peak - 1642.6 / 6) < 1e-9
