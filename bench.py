@@ -385,8 +385,7 @@ def block_measurements(rt, torch, stream, iters: int = 5, only: str | None = Non
         weights = {}
         for wname, shape in OB.weight_shapes(cfg).items():
             t = torch.randn(*shape, device="cuda", generator=g)
-            weights[wname] = (t * 0.02 + 1.0) if len(shape) == 1 and wname != "ada_b" else (
-                t * 0.0 if wname == "ada_b" else t * 0.02)
+            weights[wname] = (t * 0.02 + 1.0) if len(shape) == 1 and wname != "ada_b" else t * 0.02
         blk.set_weights(weights)
         del weights
         T = batch * cfg.seq_len
@@ -497,8 +496,7 @@ def _block_group_measure(rt, torch, dist, rank, world, stream, iters, name, cfg,
     weights = {}
     for wname, shape in OB.weight_shapes(rcfg).items():
         t = torch.randn(*shape, device="cuda", generator=g)
-        weights[wname] = (t * 0.02 + 1.0) if len(shape) == 1 and wname != "ada_b" else (
-            t * 0.0 if wname == "ada_b" else t * 0.02)
+        weights[wname] = (t * 0.02 + 1.0) if len(shape) == 1 and wname != "ada_b" else t * 0.02
     blk.set_weights(weights)
     del weights
     T_local = local_batch * cfg.seq_len

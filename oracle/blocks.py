@@ -90,12 +90,15 @@ def weight_shapes(cfg: BlockConfig) -> dict[str, tuple]:
 
 
 def random_weights(cfg: BlockConfig, seed: int) -> dict[str, np.ndarray]:
-    """Benchmark init: linear weights N(0, 0.02); norm gains 1 + N(0, 0.02); adaLN bias 0."""
+    """Benchmark init: linear weights and the adaLN bias N(0, 0.02); norm gains 1 + N(0, 0.02).
+
+    The non-zero adaLN bias exercises `canonicalLinear`'s bias term
+    (canonical_reference.go:163-164)."""
     rng = np.random.Generator(np.random.PCG64(seed))
     out = {}
     for name, shape in weight_shapes(cfg).items():
         if name == "ada_b":
-            out[name] = np.zeros(shape, dtype=np.float32)
+            out[name] = (0.02 * rng.standard_normal(shape)).astype(np.float32)
         elif len(shape) == 1:
             out[name] = (1.0 + 0.02 * rng.standard_normal(shape)).astype(np.float32)
         else:

@@ -333,10 +333,13 @@ ORACLE_API int oracle_reduction_compare(int64_t rows, int64_t width, int op, con
 
 /* ---------------------------------------------------------------- RMSNorm */
 
-/* CanonicalRMSNorm (internal/prometheus/zimage/canonical_contract.go:91-105)
-   and cpuHeadRMSNorm (internal/prometheus/gemma4e2b_m1_rtx.go:811-832), per
-   row: fp32 left-to-right sum of squares, scale = float32(1/sqrt(float64(
-   sum/W + eps))), out = x * scale * weight (fp32, left to right). */
+/* cpuHeadRMSNorm (internal/prometheus/gemma4e2b_m1_rtx.go:811-832) and
+   CanonicalRMSNorm (internal/prometheus/zimage/canonical_contract.go:91-105),
+   per row: fp32 left-to-right sum of squares, m = sum/W + eps in fp32, then
+     head form (form 0):      scale = float32(1.0 / sqrt(float64(m)))
+     canonical form (form 1): scale = float32(1) / float32(sqrt(float64(m)))
+   (the canonical form rounds the square root to fp32 and divides in fp32),
+   and out = x * scale * weight in fp32, left to right. */
 typedef struct {
   int64_t width, stride;
   const float* in;
@@ -347,6 +350,7 @@ typedef struct {
   float* inv;
   double* out64;
   double* inv64;
+  int form;
 } rms_ctx;
 
 static void rms_f32_range(void* p, int64_t begin, int64_t end) {
@@ -356,15 +360,16 @@ static void rms_f32_range(void* p, int64_t begin, int64_t end) {
     const float* x = q->in + r * q->stride;
     float sum = 0.0f;
     for (int64_t c = 0; c < width; ++c) sum += x[c] * x[c];
-    const float scale = (float)(1.0 / sqrt((double)(sum / (float)width + q->eps)));
+    const float m = sum / (float)width + q->eps;
+    const float scale = q->form == 1 ? 1.0f / (float)sqrt((double)m) : (float)(1.0 / sqrt((double)m));
     if (q->inv != NULL) q->inv[r] = scale;
     for (int64_t c = 0; c < width; ++c) q->out[r * width + c] = x[c] * scale * q->weight[c];
   }
 }
 
 ORACLE_API void oracle_rmsnorm_f32(int64_t rows, int64_t width, int64_t stride, const float* in, const float* weight,
-                                   float eps, float* out, float* inv_rms, int threads) {
-  rms_ctx q = {width, stride, in, weight, eps, 0.0, out, inv_rms, NULL, NULL};
+                                   float eps, float* out, float* inv_rms, int threads, int form) {
+  rms_ctx q = {width, stride, in, weight, eps, 0.0, out, inv_rms, NULL, NULL, form};
   parallel_rows(threads, 0, rows, rms_f32_range, &q);
 }
 
@@ -384,7 +389,7 @@ static void rms_f64_range(void* p, int64_t begin, int64_t end) {
 
 ORACLE_API void oracle_rmsnorm_f64(int64_t rows, int64_t width, int64_t stride, const float* in, const float* weight,
                                    double eps, double* out, double* inv_rms, int threads) {
-  rms_ctx q = {width, stride, in, weight, 0.0f, eps, NULL, NULL, out, inv_rms};
+  rms_ctx q = {width, stride, in, weight, 0.0f, eps, NULL, NULL, out, inv_rms, 0};
   parallel_rows(threads, 0, rows, rms_f64_range, &q);
 }
 

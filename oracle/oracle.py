@@ -55,7 +55,7 @@ def lib() -> C.CDLL:
         L.oracle_reduction_cpu_reference.restype = i32
         L.oracle_reduction_compare.argtypes = [i64, i64, i32, vp, vp, C.POINTER(Mismatch)]
         L.oracle_reduction_compare.restype = i32
-        L.oracle_rmsnorm_f32.argtypes = [i64, i64, i64, vp, vp, C.c_float, vp, vp, i32]
+        L.oracle_rmsnorm_f32.argtypes = [i64, i64, i64, vp, vp, C.c_float, vp, vp, i32, i32]
         L.oracle_rmsnorm_f64.argtypes = [i64, i64, i64, vp, vp, C.c_double, vp, vp, i32]
         L.oracle_max_threads.restype = i32
         _lib = L
@@ -132,11 +132,16 @@ def find_nonfinite(x: np.ndarray) -> int:
     return int(lib().oracle_find_nonfinite(_p(np.ascontiguousarray(x, dtype=np.float32)), x.size))
 
 
-def rmsnorm_f32(x: np.ndarray, w: np.ndarray, eps: float, threads: int = 1) -> tuple[np.ndarray, np.ndarray]:
+def rmsnorm_f32(x: np.ndarray, w: np.ndarray, eps: float, threads: int = 1, form: str = "head"
+                ) -> tuple[np.ndarray, np.ndarray]:
+    """fp32 RMSNorm as Oct's CPU code evaluates it: form "head" is cpuHeadRMSNorm
+    (gemma4e2b_m1_rtx.go:811-832, Gemma), "canonical" is CanonicalRMSNorm
+    (zimage/canonical_contract.go:91-105, the Z-Image / DiT path)."""
     rows, width = x.shape
     out = np.empty_like(x)
     inv = np.empty(rows, dtype=np.float32)
-    lib().oracle_rmsnorm_f32(rows, width, width, _p(x), _p(w), eps, _p(out), _p(inv), threads)
+    lib().oracle_rmsnorm_f32(rows, width, width, _p(x), _p(w), eps, _p(out), _p(inv), threads,
+                             {"head": 0, "canonical": 1}[form])
     return out, inv
 
 

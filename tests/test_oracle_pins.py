@@ -139,3 +139,31 @@ def test_multithreaded_oracle_matches_serial(oracle_mod):
     x = o.normal_matrix(40, 300, 3)
     for op in (1, 2, 3):
         assert np.array_equal(o.reduction_cpu_reference(x, op, 1)[1], o.reduction_cpu_reference(x, op, 4)[1])
+
+
+def _go_rmsnorm_f32(x, w, eps, canonical):
+    """Direct numpy float32 transcription of the two Go loops, for pinning the C oracle."""
+    out = np.empty_like(x)
+    for r in range(x.shape[0]):
+        acc = np.float32(0.0)
+        for v in x[r]:
+            acc = np.float32(acc + np.float32(v * v))
+        m = np.float32(acc / np.float32(x.shape[1])) + np.float32(eps)
+        m = np.float32(m)
+        if canonical:
+            scale = np.float32(np.float32(1.0) / np.float32(np.sqrt(np.float64(m))))
+        else:
+            scale = np.float32(1.0 / np.sqrt(np.float64(m)))
+        out[r] = (x[r] * scale).astype(np.float32) * w
+    return out
+
+
+@pytest.mark.parametrize("form", ["head", "canonical"])
+def test_rmsnorm_fp32_forms_follow_the_go_loops_bit_for_bit(oracle_mod, form):
+    """cpuHeadRMSNorm rounds 1/sqrt once from binary64; CanonicalRMSNorm rounds the square
+    root to fp32 and divides in fp32.  The C oracle reproduces each exactly."""
+    o = oracle_mod
+    x = o.normal_matrix(24, 300, 41)
+    w = (o.uniform_matrix(1, 300, 42).ravel() + np.float32(1.0)).astype(np.float32)
+    got, _ = o.rmsnorm_f32(x, w, 1e-5, form=form)
+    assert np.array_equal(got, _go_rmsnorm_f32(x, w, 1e-5, form == "canonical"))
