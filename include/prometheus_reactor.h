@@ -162,15 +162,19 @@ enum {
   PROM_SGEMM_RESIDENT_FLAG_M29_SUBMISSION_RING = 1u << 1,
 };
 
-/* RMSNorm detail codes (internal/prometheus/native/reactor_vulkan.h:1870-1888). */
+/* RMSNorm / RoPE / score detail codes (internal/prometheus/native/reactor_vulkan.h:1870-1888). */
 enum {
   PROM_M46_DETAIL_INVALID_REQUEST = -7401,
   PROM_M46_DETAIL_SHAPE = -7403,
   PROM_M46_DETAIL_STRIDE = -7404,
+  PROM_M46_DETAIL_STALE_WEIGHT_GENERATION = -7406,
   PROM_M46_DETAIL_EPSILON = -7407,
   PROM_M46_DETAIL_SIZE_OVERFLOW = -7409,
   PROM_M46_DETAIL_RESOURCE = -7411,
+  PROM_M46_DETAIL_COMMAND = -7412,
+  PROM_M46_DETAIL_SUBMIT = -7413,
   PROM_M46_DETAIL_COMPLETION_UNCERTAIN = -7414,
+  PROM_M46_DETAIL_READBACK = -7416,
   PROM_M46_DETAIL_NONFINITE_INPUT = -7418,
 };
 
@@ -534,8 +538,9 @@ typedef struct PrometheusAsyncStatus {
   uint32_t outstanding_tasks;
 } PrometheusAsyncStatus;
 
-/* Gemma RMSNorm request/result (reactor_api.h:1781-1825).  The Gemma-private
-   generation/hash fields are accepted and echoed, not enforced. */
+/* Gemma RMSNorm request/result (reactor_api.h:1781-1825).  Generations and the
+   source hash must be non-zero; the weight generation must exceed the one the
+   handle last committed (the reference's stale-weight rule). */
 typedef struct PrometheusGemma4E2BM1InputRmsNormRequest {
   uint32_t struct_size;
   const float* input;
@@ -584,6 +589,165 @@ typedef struct PrometheusGemma4E2BM1InputRmsNormResult {
 
 typedef PrometheusGemma4E2BM1InputRmsNormRequest PrometheusGemma4E2BM1HeadRmsNormRequest;
 typedef PrometheusGemma4E2BM1InputRmsNormResult PrometheusGemma4E2BM1HeadRmsNormResult;
+
+/* Half-split RoPE request/result (reactor_api.h:1835-1871): source and output
+   [token][head][component], tables [token][component]; the operation rounds
+   its products and sums through BF16 as the reference's storage graph does. */
+typedef struct PrometheusGemma4E2BM1RopeRequest {
+  uint32_t struct_size;
+  const float* source;
+  const float* cosine;
+  const float* sine;
+  float* output;
+  uint64_t source_element_count;
+  uint64_t cosine_element_count;
+  uint64_t sine_element_count;
+  uint64_t output_element_count;
+  uint32_t tokens;
+  uint32_t heads;
+  uint32_t head_width;
+  uint32_t reserved0;
+  uint64_t source_generation;
+  uint64_t table_generation;
+} PrometheusGemma4E2BM1RopeRequest;
+
+typedef struct PrometheusGemma4E2BM1RopeResult {
+  uint32_t struct_size;
+  uint32_t stage;
+  int32_t detail_code;
+  uint32_t output_written;
+  uint32_t dispatch_count;
+  uint64_t source_hash;
+  uint64_t cosine_hash;
+  uint64_t sine_hash;
+  uint64_t output_hash;
+  uint64_t buffer_allocation_count;
+  uint64_t buffer_reuse_count;
+  uint64_t descriptor_update_count;
+  uint64_t pipeline_create_count;
+  uint64_t command_buffer_reuse_count;
+} PrometheusGemma4E2BM1RopeResult;
+
+/* Head RMSNorm followed by RoPE with nothing read back in between
+   (reactor_api.h:1873-1922).  `output` may be NULL (output_element_count 0):
+   the positioned rows then stay on the device only. */
+typedef struct PrometheusGemma4E2BM1HeadRmsNormRopeRequest {
+  uint32_t struct_size;
+  const float* input;
+  const float* weight;
+  const float* cosine;
+  const float* sine;
+  float* output;
+  uint64_t input_element_count;
+  uint64_t weight_element_count;
+  uint64_t cosine_element_count;
+  uint64_t sine_element_count;
+  uint64_t output_element_count;
+  uint32_t tokens;
+  uint32_t heads;
+  uint32_t head_width;
+  uint32_t reserved0;
+  float epsilon;
+  uint64_t input_generation;
+  uint64_t weight_generation;
+  uint64_t table_generation;
+  uint64_t exact_source_hash;
+} PrometheusGemma4E2BM1HeadRmsNormRopeRequest;
+
+typedef struct PrometheusGemma4E2BM1HeadRmsNormRopeResult {
+  uint32_t struct_size;
+  uint32_t stage;
+  int32_t detail_code;
+  uint32_t output_written;
+  uint32_t dispatch_count;
+  uint32_t resident_source_bound;
+  uint32_t normalized_readback_count;
+  uint64_t source_byte_offset;
+  uint64_t source_byte_range;
+  uint64_t destination_byte_offset;
+  uint64_t destination_byte_range;
+  uint64_t input_hash;
+  uint64_t weight_hash;
+  uint64_t output_hash;
+  uint64_t buffer_allocation_count;
+  uint64_t buffer_reuse_count;
+  uint64_t descriptor_update_count;
+  uint64_t pipeline_create_count;
+  uint64_t command_buffer_reuse_count;
+  uint64_t observed_weight_generation;
+  uint64_t requested_weight_generation;
+} PrometheusGemma4E2BM1HeadRmsNormRopeResult;
+
+/* Raw pre-mask attention scores (reactor_api.h:1924-1985): Q and K each go
+   through head RMSNorm -> RoPE on the device, then
+   scores[head][query][key] = q . k * scale, every query head reading KV head 0. */
+typedef struct PrometheusGemma4E2BM1AttentionScoresRequest {
+  uint32_t struct_size;
+  const float* query_input;
+  const float* key_input;
+  const float* query_weight;
+  const float* key_weight;
+  const float* cosine;
+  const float* sine;
+  float* scores;
+  uint64_t query_input_element_count;
+  uint64_t key_input_element_count;
+  uint64_t query_weight_element_count;
+  uint64_t key_weight_element_count;
+  uint64_t cosine_element_count;
+  uint64_t sine_element_count;
+  uint64_t score_element_count;
+  uint32_t tokens;
+  uint32_t query_heads;
+  uint32_t key_heads;
+  uint32_t head_width;
+  float epsilon;
+  float scale;
+  uint32_t preparation_order; /* 0: Q then K; 1: K then Q */
+  uint64_t query_input_generation;
+  uint64_t key_input_generation;
+  uint64_t query_weight_generation;
+  uint64_t key_weight_generation;
+  uint64_t table_generation;
+  uint64_t query_exact_source_hash;
+  uint64_t key_exact_source_hash;
+} PrometheusGemma4E2BM1AttentionScoresRequest;
+
+typedef struct PrometheusGemma4E2BM1AttentionScoresResult {
+  uint32_t struct_size;
+  uint32_t stage;
+  int32_t detail_code;
+  uint32_t score_written;
+  uint32_t positional_dispatch_count;
+  uint32_t score_dispatch_count;
+  uint32_t score_readback_count;
+  uint32_t host_detour_count;
+  uint32_t query_slot_id;
+  uint32_t query_slot_generation;
+  uint32_t key_slot_id;
+  uint32_t key_slot_generation;
+  uint32_t score_slot_id;
+  uint32_t score_slot_generation;
+  uint64_t query_byte_range;
+  uint64_t key_byte_range;
+  uint64_t score_byte_range;
+  uint64_t score_hash;
+  uint64_t buffer_allocation_count;
+  uint64_t buffer_reuse_count;
+  uint64_t descriptor_update_count;
+  uint64_t pipeline_create_count;
+  uint64_t observed_weight_generation;
+  uint64_t requested_weight_generation;
+} PrometheusGemma4E2BM1AttentionScoresResult;
+
+/* Envelope of the Gemma M1 entry points.  The reference admits only the M1
+   geometry (15 tokens, 8 or 1 heads of 256, internal/prometheus/native/
+   reactor_api.c:370-395, 404-441, 507-547; reactor_concept_rmsnorm.cpp:157-212);
+   this library widens the ceilings below and keeps the same detail codes for
+   requests inside the reference's envelope. */
+#define OCT_B200_M1_MAX_TOKENS 65536u
+#define OCT_B200_M1_MAX_HEADS 64u
+#define OCT_B200_M1_MAX_HEAD_WIDTH 1024u
 
 /* ==== reference ABI entry points ==== */
 
@@ -659,10 +823,30 @@ PROM_REACTOR_API int prometheus_reactor_runtime_row_wise_softmax(void* handle,
 PROM_REACTOR_API int prometheus_reactor_runtime_gemma4e2b_m1_input_rmsnorm(
     void* handle, const PrometheusGemma4E2BM1InputRmsNormRequest* request,
     PrometheusGemma4E2BM1InputRmsNormResult* out_result);
-/* reactor_api.h:2696-2699 -- the same primitive over [token, head, channel] rows. */
+/* reactor_api.h:2692-2695 -- the same RMSNorm with its output rounded to BF16
+   (the Q/K/V projections' activation storage boundary, reactor_api.c:362-368). */
+PROM_REACTOR_API int prometheus_reactor_runtime_gemma4e2b_m1_projection_activation_rmsnorm(
+    void* handle, const PrometheusGemma4E2BM1InputRmsNormRequest* request,
+    PrometheusGemma4E2BM1InputRmsNormResult* out_result);
+/* reactor_api.h:2696-2699 -- the same primitive over [token, head, channel] rows,
+   input and output rounded to BF16, epsilon 1e-6, row stride = width
+   (reactor_api.c:370-395; the reference's 120-row / 256-wide ceilings are widened). */
 PROM_REACTOR_API int prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm(
     void* handle, const PrometheusGemma4E2BM1HeadRmsNormRequest* request,
     PrometheusGemma4E2BM1HeadRmsNormResult* out_result);
+/* reactor_api.h:2700-2703 -- half-split RoPE with BF16 products and sums
+   (cpuGemma4e2bRope, gemma4e2b_m1_rtx.go:834-861). */
+PROM_REACTOR_API int prometheus_reactor_runtime_gemma4e2b_m1_rope(
+    void* handle, const PrometheusGemma4E2BM1RopeRequest* request, PrometheusGemma4E2BM1RopeResult* out_result);
+/* reactor_api.h:2704-2707 -- head RMSNorm then RoPE in one device pass (reactor_api.c:404-505). */
+PROM_REACTOR_API int prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm_rope(
+    void* handle, const PrometheusGemma4E2BM1HeadRmsNormRopeRequest* request,
+    PrometheusGemma4E2BM1HeadRmsNormRopeResult* out_result);
+/* reactor_api.h:2708-2711 -- both positional preparations, then the raw scores
+   (reactor_api.c:507-586; cpuGemma4e2bRawScores, gemma4e2b_m1_rtx.go:863-883). */
+PROM_REACTOR_API int prometheus_reactor_runtime_gemma4e2b_m1_attention_scores(
+    void* handle, const PrometheusGemma4E2BM1AttentionScoresRequest* request,
+    PrometheusGemma4E2BM1AttentionScoresResult* out_result);
 
 /* reactor_api.h:2823-2826 -- aliases kept by the reference for older drafts. */
 PROM_REACTOR_API int prometheus_runtime_create(void* config, void** out_handle);

@@ -191,4 +191,26 @@ cudaError_t rmsnorm(const float* in, uint64_t in_stride, const float* weight, fl
                     uint32_t rows, uint32_t width, float eps, unsigned long long* nonfinite, unsigned int* err,
                     cudaStream_t stream);
 
+// ---------------------------------------------------------------- Gemma M1 boundary (gemma_m1.cu)
+// BF16 storage rounding as the reference's M1 entry points apply it; inputs
+// must already be checked finite.  Head widths are even and <= kM1MaxHeadWidth.
+constexpr uint32_t kM1MaxHeadWidth = 1024;
+// y = round_out((round_in(x) * inv) * w) per row, inv = float(1/sqrt(sum x^2 / width + eps))
+// with the sum of squares in binary64.
+cudaError_t m1_rmsnorm_bf16(const float* in, uint64_t stride, const float* w, float* out, float* inv_rms,
+                            uint32_t rows, uint32_t width, float eps, bool round_in, bool round_out,
+                            cudaStream_t stream);
+// Half-split RoPE of [tokens][heads][head_width] with [tokens][head_width] tables
+// (only each row's first head_width / 2 entries are read), BF16 products and sums.
+cudaError_t m1_rope_bf16(const float* src, const float* cos_table, const float* sin_table, float* out,
+                         uint32_t tokens, uint32_t heads, uint32_t head_width, cudaStream_t stream);
+// The BF16 head RMSNorm of every (token, head) row followed by the RoPE above.
+cudaError_t m1_head_rmsnorm_rope(const float* in, const float* w, const float* cos_table, const float* sin_table,
+                                 float* out, uint32_t tokens, uint32_t heads, uint32_t head_width, float eps,
+                                 cudaStream_t stream);
+// scores[h][i][j] = float(sum_d q[i][h][d] k[j][d] * scale) in binary64; k is [tokens][head_width]
+// (one KV head shared by every query head).
+cudaError_t m1_raw_scores(const float* q, const float* k, float* scores, uint32_t tokens, uint32_t query_heads,
+                          uint32_t head_width, float scale, cudaStream_t stream);
+
 }  // namespace oct

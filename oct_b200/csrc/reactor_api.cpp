@@ -29,104 +29,10 @@
 
 #include "block.h"
 #include "kernels.h"
+#include "runtime.h"
 
-namespace {
-
-using Clock = std::chrono::steady_clock;
-constexpr uint32_t kMagic = 0x0C7B2000u;
-constexpr int kAsyncSlots = 4;  // task capacity, as the reference (reactor_api.h:2030 tasks[4])
-constexpr uint32_t kBatchWorkers = 8;  // PROM_SGEMM_BATCH_MAX_LOGICAL_WIDTH (reactor_batch.c:56)
-
-uint64_t ns_since(Clock::time_point t0) {
-  return static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(Clock::now() - t0).count());
-}
-
-void set_status(uint32_t* stage, int* detail, uint32_t s, int d) {
-  if (stage != nullptr) *stage = s;
-  if (detail != nullptr) *detail = d;
-}
-
-// A growable device allocation.  Growth synchronises the owning stream first
-// so no kernel in flight still references the old block.
-struct DevBuf {
-  void* raw = nullptr;
-  uint64_t cap = 0;
-  void* aligned() const { return reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023)); }
-  cudaError_t ensure(uint64_t bytes, cudaStream_t s) {
-    if (bytes <= cap && raw != nullptr) return cudaSuccess;
-    // Kernels on any stream may still read the old block (device entry points
-    // accept caller streams), so growth waits for the whole device.
-    (void)s;
-    cudaError_t e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) return e;
-    if (raw != nullptr) cudaFree(raw);
-    raw = nullptr;
-    cap = 0;
-    const uint64_t want = bytes + (bytes >> 3);  // 12.5% headroom against regrowth
-    e = cudaMalloc(&raw, want + 1024);
-    if (e != cudaSuccess) {
-      raw = nullptr;
-      (void)cudaGetLastError();
-      return e;
-    }
-    cap = want;
-    return cudaSuccess;
-  }
-  void release() {
-    if (raw != nullptr) cudaFree(raw);
-    raw = nullptr;
-    cap = 0;
-  }
-};
-
-struct AsyncTask {
-  bool active = false;
-  int id = 0;
-  uint32_t state = PROM_ASYNC_STATE_IDLE;
-  uint32_t m = 0, n = 0, k = 0;
-  int final_detail = 0;
-  uint32_t final_stage = 0;
-  cudaEvent_t done = nullptr;
-  DevBuf a, b, c;
-};
-
-struct Runtime {
-  uint32_t magic = kMagic;
-  std::mutex mu;
-  int device = 0;
-  bool available = false;
-  uint32_t reason = PROM_REASON_NONE;
-  uint32_t test_flags = 0, async_test_flags = 0, reduction_test_flags = 0;
-  cudaStream_t stream = nullptr;
-  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-  DevBuf scratch;               // split-TF32 operand buffers
-  DevBuf da, db, dc;            // staging for host-pointer SGEMM
-  DevBuf rin, rout, rw, rinv;   // staging for reductions / RMSNorm
-  DevBuf words;                 // [0] kernel error bits (u32), [8] first non-finite index (u64)
-  AsyncTask tasks[kAsyncSlots];
-  int next_task_id = 1;
-  // Optional per-launch kernel timing of the tensor-core SGEMM (events on the
-  // launch stream): split pass and main kernel, summed on read.
-  bool timing = false;
-  std::vector<oct::SgemmEvents> timing_events;
-  size_t timing_used = 0;
-  // Pipelined host SGEMM: upload and download streams, chunk events.
-  cudaStream_t copy_in = nullptr, copy_out = nullptr;
-  std::vector<cudaEvent_t> pipe_events;
-  // SGEMM batch workers: one stream, split scratch and A/B staging each.
-  cudaStream_t batch_streams[kBatchWorkers] = {};
-  DevBuf batch_scratch[kBatchWorkers], batch_a[kBatchWorkers], batch_b[kBatchWorkers];
-  DevBuf batch_c;  // every entry's C, until the whole batch has succeeded
-  // Transformer blocks created on this handle.
-  std::unordered_map<uint64_t, oct::Block*> blocks;
-  uint64_t next_block = 1;
-  uint64_t next_request_id = 1;
-
-  unsigned int* err_word() { return static_cast<unsigned int*>(words.aligned()); }
-  unsigned long long* nonfinite_word() {
-    return reinterpret_cast<unsigned long long*>(static_cast<char*>(words.aligned()) + 8);
-  }
-};
+namespace oct {
+namespace rt {
 
 std::mutex g_registry_mu;
 std::unordered_set<Runtime*>* g_registry = new std::unordered_set<Runtime*>();
@@ -139,33 +45,23 @@ Runtime* lookup(void* handle) {
   return rt;
 }
 
-// Resets the kernel status words on the stream (async).
-cudaError_t reset_words(Runtime* rt) {
-  cudaError_t e = cudaMemsetAsync(rt->err_word(), 0, 8, rt->stream);
-  if (e != cudaSuccess) return e;
-  return cudaMemsetAsync(rt->nonfinite_word(), 0xFF, 8, rt->stream);
+void register_runtime(Runtime* rt) {
+  std::lock_guard<std::mutex> lock(g_registry_mu);
+  g_registry->insert(rt);
 }
 
-struct Words {
-  unsigned int err = 0;
-  unsigned long long nonfinite = ~0ull;
-};
-
-cudaError_t read_words(Runtime* rt, Words* w) {
-  unsigned char host[16];
-  cudaError_t e = cudaMemcpyAsync(host, rt->words.aligned(), 16, cudaMemcpyDeviceToHost, rt->stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
-  if (e != cudaSuccess) return e;
-  std::memcpy(&w->err, host, 4);
-  std::memcpy(&w->nonfinite, host + 8, 8);
-  return cudaSuccess;
+void unregister_runtime(Runtime* rt) {
+  std::lock_guard<std::mutex> lock(g_registry_mu);
+  g_registry->erase(rt);
 }
 
-bool checked_mul(uint64_t a, uint64_t b, uint64_t* out) {
-  if (a != 0 && b > UINT64_MAX / a) return false;
-  *out = a * b;
-  return true;
-}
+}  // namespace rt
+}  // namespace oct
+
+namespace {
+
+using namespace oct::rt;
+
 
 // The next set of per-launch timing events (created on first use); null on failure.
 const oct::SgemmEvents* next_timing_events(Runtime* rt) {
@@ -199,11 +95,13 @@ uint32_t resolve_variant(uint32_t variant, uint32_t m, uint32_t n, uint32_t k) {
   return work < 4.0e6 ? OCT_B200_SGEMM_FMA : OCT_B200_SGEMM_TC3XTF32;
 }
 
+}  // namespace
+
 // `scratch` (default: the handle's) holds the TF32 split operands; calls that
 // run concurrently on different streams need different scratch buffers.
-int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
-                  uint32_t m, uint32_t n, uint32_t k, uint32_t variant, cudaStream_t stream,
-                  const oct::GemmBatch* batch = nullptr, DevBuf* scratch = nullptr) {
+int oct::rt::enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c,
+                           uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, uint32_t variant, cudaStream_t stream,
+                           const oct::GemmBatch* batch, DevBuf* scratch) {
   variant = resolve_variant(variant, m, n, k);
   if (scratch == nullptr) scratch = &rt->scratch;
   // the small-M kernel has no batched or B^T form: those take the FMA control
@@ -232,6 +130,8 @@ int enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uin
   }
   return e == cudaSuccess ? 0 : OCT_B200_DETAIL_CUDA_ERROR;
 }
+
+namespace {
 
 Runtime* create_runtime(const PrometheusReactorConfig* cfg, int* status) {
   Runtime* rt = new (std::nothrow) Runtime();
@@ -297,7 +197,7 @@ void destroy_runtime(Runtime* rt) {
     t.c.release();
   }
   for (DevBuf* b : {&rt->scratch, &rt->da, &rt->db, &rt->dc, &rt->rin, &rt->rout, &rt->rw, &rt->rinv, &rt->words,
-                    &rt->batch_c})
+                    &rt->batch_c, &rt->m1_cos, &rt->m1_sin, &rt->m1_q, &rt->m1_k, &rt->m1_scores})
     b->release();
   for (cudaStream_t* st : {&rt->copy_in, &rt->copy_out})
     if (*st != nullptr) {
@@ -583,107 +483,6 @@ uint32_t outstanding(Runtime* rt) {
 }
 }  // namespace
 
-namespace {
-// Shared body of the two Gemma RMSNorm entry points over host buffers.
-int gemma_rmsnorm(void* handle, const PrometheusGemma4E2BM1InputRmsNormRequest* r,
-                  PrometheusGemma4E2BM1InputRmsNormResult* out_result) {
-  if (out_result == nullptr) return PROM_ERROR;
-  PrometheusGemma4E2BM1InputRmsNormResult& out = *out_result;
-  const auto t0 = Clock::now();
-  std::memset(&out, 0, sizeof(out));
-  out.struct_size = sizeof(out);
-  out.stage = PROM_STAGE_INIT;
-  out.detail_code = PROM_M46_DETAIL_INVALID_REQUEST;
-  Runtime* rt = lookup(handle);
-  if (rt == nullptr) return PROM_INVALID_HANDLE;
-  if (r == nullptr || r->struct_size < sizeof(*r) || r->input == nullptr || r->weight == nullptr ||
-      r->output == nullptr)
-    return PROM_ERROR;
-  if (r->tokens == 0 || r->model_width == 0 || r->tokens > OCT_B200_REDUCTION_MAX_ROWS) {
-    out.detail_code = PROM_M46_DETAIL_SHAPE;
-    return PROM_ERROR;
-  }
-  const uint32_t stride = r->input_row_stride == 0 ? r->model_width : r->input_row_stride;
-  if (stride < r->model_width) {
-    out.detail_code = PROM_M46_DETAIL_STRIDE;
-    return PROM_ERROR;
-  }
-  if (!finite_f(r->epsilon) || r->epsilon <= 0.f) {
-    out.detail_code = PROM_M46_DETAIL_EPSILON;
-    return PROM_ERROR;
-  }
-  const uint64_t logical = static_cast<uint64_t>(r->tokens) * r->model_width;
-  const uint64_t storage = static_cast<uint64_t>(r->tokens - 1) * stride + r->model_width;
-  if (r->input_element_count < storage || r->weight_element_count != r->model_width ||
-      r->output_element_count != logical ||
-      (r->inv_rms_output != nullptr && r->inv_rms_output_element_count != r->tokens)) {
-    out.detail_code = PROM_M46_DETAIL_SHAPE;
-    return PROM_ERROR;
-  }
-  if (logical > OCT_B200_REDUCTION_MAX_TOTAL_ELEMENTS) {
-    out.detail_code = PROM_M46_DETAIL_SIZE_OVERFLOW;
-    return PROM_ERROR;
-  }
-  if (!rt->available) {
-    out.detail_code = PROM_M46_DETAIL_RESOURCE;
-    return PROM_ERROR;
-  }
-  std::lock_guard<std::mutex> lock(rt->mu);
-  if (rt->rin.ensure(storage * 4, rt->stream) != cudaSuccess || rt->rout.ensure(logical * 4, rt->stream) != cudaSuccess ||
-      rt->rw.ensure(static_cast<uint64_t>(r->model_width) * 4, rt->stream) != cudaSuccess ||
-      rt->rinv.ensure(static_cast<uint64_t>(r->tokens) * 4, rt->stream) != cudaSuccess) {
-    out.detail_code = PROM_M46_DETAIL_RESOURCE;
-    return PROM_ERROR;
-  }
-  float* din = static_cast<float*>(rt->rin.aligned());
-  float* dout = static_cast<float*>(rt->rout.aligned());
-  float* dw = static_cast<float*>(rt->rw.aligned());
-  float* dinv = static_cast<float*>(rt->rinv.aligned());
-  cudaError_t e = reset_words(rt);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(din, r->input, storage * 4, cudaMemcpyHostToDevice, rt->stream);
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(dw, r->weight, static_cast<uint64_t>(r->model_width) * 4, cudaMemcpyHostToDevice, rt->stream);
-  cudaEventRecord(rt->ev0, rt->stream);
-  if (e == cudaSuccess)
-    e = oct::rmsnorm(din, stride, dw, dout, dinv, r->tokens, r->model_width, r->epsilon, rt->nonfinite_word(),
-                     rt->err_word(), rt->stream);
-  cudaEventRecord(rt->ev1, rt->stream);
-  Words w;
-  if (e != cudaSuccess || read_words(rt, &w) != cudaSuccess || w.err != 0) {
-    (void)cudaGetLastError();
-    out.stage = PROM_STAGE_SUBMIT;
-    out.detail_code = PROM_M46_DETAIL_COMPLETION_UNCERTAIN;
-    return PROM_ERROR;
-  }
-  if (w.nonfinite != ~0ull) {
-    out.stage = PROM_STAGE_TRANSFER_IN;
-    out.detail_code = PROM_M46_DETAIL_NONFINITE_INPUT;
-    return PROM_ERROR;
-  }
-  float ms = 0.f;
-  if (cudaEventElapsedTime(&ms, rt->ev0, rt->ev1) == cudaSuccess) {
-    out.apply_gpu_ns = static_cast<uint64_t>(static_cast<double>(ms) * 1.0e6);
-  }
-  e = cudaMemcpyAsync(r->output, dout, logical * 4, cudaMemcpyDeviceToHost, rt->stream);
-  if (e == cudaSuccess && r->inv_rms_output != nullptr)
-    e = cudaMemcpyAsync(r->inv_rms_output, dinv, static_cast<uint64_t>(r->tokens) * 4, cudaMemcpyDeviceToHost,
-                        rt->stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
-  if (e != cudaSuccess) {
-    out.stage = PROM_STAGE_TRANSFER_OUT;
-    out.detail_code = PROM_M46_DETAIL_COMPLETION_UNCERTAIN;
-    return PROM_ERROR;
-  }
-  out.stage = PROM_STAGE_NONE;
-  out.detail_code = 0;
-  out.output_written = 1;
-  out.matched_input = 1;
-  out.submit_count = 1;
-  out.final_readback_count = 1;
-  out.end_to_end_ns = ns_since(t0);
-  return PROM_OK;
-}
-}  // namespace
 
 // =========================================================================== ABI
 extern "C" {
@@ -1690,26 +1489,6 @@ int prometheus_reactor_runtime_row_wise_softmax(void* handle, const PrometheusRo
   }
 }
 
-
-int prometheus_reactor_runtime_gemma4e2b_m1_input_rmsnorm(void* handle,
-                                                          const PrometheusGemma4E2BM1InputRmsNormRequest* request,
-                                                          PrometheusGemma4E2BM1InputRmsNormResult* out_result) {
-  try {
-    return gemma_rmsnorm(handle, request, out_result);
-  } catch (...) {
-    return PROM_INTERNAL_ERROR;
-  }
-}
-
-int prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm(void* handle,
-                                                         const PrometheusGemma4E2BM1HeadRmsNormRequest* request,
-                                                         PrometheusGemma4E2BM1HeadRmsNormResult* out_result) {
-  try {
-    return gemma_rmsnorm(handle, request, out_result);
-  } catch (...) {
-    return PROM_INTERNAL_ERROR;
-  }
-}
 
 // ---------------------------------------------------------------- device extensions
 int oct_b200_sgemm_device_ld(void* handle, const float* d_a, uint64_t lda, const float* d_b, uint64_t ldb, float* d_c,

@@ -46,6 +46,8 @@ DETAIL_BAD_VARIANT = -7004
 DETAIL_DEVICE_TIMEOUT = -7002  # a bounded in-kernel wait gave up
 DETAIL_NOALLOC_TOO_LARGE = -7006  # product needs more than the no-alloc entry's fixed scratch
 DETAIL_INVALID_ARGUMENT = -7008  # null pointer, short leading dimension or out-of-range argument
+M46_INVALID_REQUEST, M46_STALE_WEIGHT_GENERATION, M46_RESOURCE = -7401, -7406, -7411
+M46_COMPLETION_UNCERTAIN, M46_READBACK, M46_NONFINITE_INPUT = -7414, -7416, -7418
 REDUCTION_TESTCFG_FAIL_COMMAND_RECORD = 1 << 0
 REDUCTION_TESTCFG_FAIL_QUEUE_SUBMIT = 1 << 1
 REDUCTION_TESTCFG_FAIL_COMPLETION_OBSERVATION = 1 << 2
@@ -281,6 +283,91 @@ class PrometheusGemma4E2BM1InputRmsNormResult(C.Structure):
     ]
 
 
+class PrometheusGemma4E2BM1RopeRequest(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("source", C.c_void_p), ("cosine", C.c_void_p), ("sine", C.c_void_p), ("output", C.c_void_p),
+        ("source_element_count", C.c_uint64), ("cosine_element_count", C.c_uint64),
+        ("sine_element_count", C.c_uint64), ("output_element_count", C.c_uint64),
+        ("tokens", C.c_uint32), ("heads", C.c_uint32), ("head_width", C.c_uint32), ("reserved0", C.c_uint32),
+        ("source_generation", C.c_uint64), ("table_generation", C.c_uint64),
+    ]
+
+
+class PrometheusGemma4E2BM1RopeResult(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32), ("stage", C.c_uint32), ("detail_code", C.c_int32),
+        ("output_written", C.c_uint32), ("dispatch_count", C.c_uint32),
+        ("source_hash", C.c_uint64), ("cosine_hash", C.c_uint64), ("sine_hash", C.c_uint64),
+        ("output_hash", C.c_uint64), ("buffer_allocation_count", C.c_uint64), ("buffer_reuse_count", C.c_uint64),
+        ("descriptor_update_count", C.c_uint64), ("pipeline_create_count", C.c_uint64),
+        ("command_buffer_reuse_count", C.c_uint64),
+    ]
+
+
+class PrometheusGemma4E2BM1HeadRmsNormRopeRequest(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("input", C.c_void_p), ("weight", C.c_void_p), ("cosine", C.c_void_p), ("sine", C.c_void_p),
+        ("output", C.c_void_p),
+        ("input_element_count", C.c_uint64), ("weight_element_count", C.c_uint64),
+        ("cosine_element_count", C.c_uint64), ("sine_element_count", C.c_uint64),
+        ("output_element_count", C.c_uint64),
+        ("tokens", C.c_uint32), ("heads", C.c_uint32), ("head_width", C.c_uint32), ("reserved0", C.c_uint32),
+        ("epsilon", C.c_float),
+        ("input_generation", C.c_uint64), ("weight_generation", C.c_uint64), ("table_generation", C.c_uint64),
+        ("exact_source_hash", C.c_uint64),
+    ]
+
+
+class PrometheusGemma4E2BM1HeadRmsNormRopeResult(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32), ("stage", C.c_uint32), ("detail_code", C.c_int32),
+        ("output_written", C.c_uint32), ("dispatch_count", C.c_uint32), ("resident_source_bound", C.c_uint32),
+        ("normalized_readback_count", C.c_uint32),
+        ("source_byte_offset", C.c_uint64), ("source_byte_range", C.c_uint64),
+        ("destination_byte_offset", C.c_uint64), ("destination_byte_range", C.c_uint64),
+        ("input_hash", C.c_uint64), ("weight_hash", C.c_uint64), ("output_hash", C.c_uint64),
+        ("buffer_allocation_count", C.c_uint64), ("buffer_reuse_count", C.c_uint64),
+        ("descriptor_update_count", C.c_uint64), ("pipeline_create_count", C.c_uint64),
+        ("command_buffer_reuse_count", C.c_uint64),
+        ("observed_weight_generation", C.c_uint64), ("requested_weight_generation", C.c_uint64),
+    ]
+
+
+class PrometheusGemma4E2BM1AttentionScoresRequest(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("query_input", C.c_void_p), ("key_input", C.c_void_p), ("query_weight", C.c_void_p),
+        ("key_weight", C.c_void_p), ("cosine", C.c_void_p), ("sine", C.c_void_p), ("scores", C.c_void_p),
+        ("query_input_element_count", C.c_uint64), ("key_input_element_count", C.c_uint64),
+        ("query_weight_element_count", C.c_uint64), ("key_weight_element_count", C.c_uint64),
+        ("cosine_element_count", C.c_uint64), ("sine_element_count", C.c_uint64),
+        ("score_element_count", C.c_uint64),
+        ("tokens", C.c_uint32), ("query_heads", C.c_uint32), ("key_heads", C.c_uint32), ("head_width", C.c_uint32),
+        ("epsilon", C.c_float), ("scale", C.c_float), ("preparation_order", C.c_uint32),
+        ("query_input_generation", C.c_uint64), ("key_input_generation", C.c_uint64),
+        ("query_weight_generation", C.c_uint64), ("key_weight_generation", C.c_uint64),
+        ("table_generation", C.c_uint64), ("query_exact_source_hash", C.c_uint64),
+        ("key_exact_source_hash", C.c_uint64),
+    ]
+
+
+class PrometheusGemma4E2BM1AttentionScoresResult(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32), ("stage", C.c_uint32), ("detail_code", C.c_int32),
+        ("score_written", C.c_uint32), ("positional_dispatch_count", C.c_uint32),
+        ("score_dispatch_count", C.c_uint32), ("score_readback_count", C.c_uint32),
+        ("host_detour_count", C.c_uint32), ("query_slot_id", C.c_uint32), ("query_slot_generation", C.c_uint32),
+        ("key_slot_id", C.c_uint32), ("key_slot_generation", C.c_uint32), ("score_slot_id", C.c_uint32),
+        ("score_slot_generation", C.c_uint32),
+        ("query_byte_range", C.c_uint64), ("key_byte_range", C.c_uint64), ("score_byte_range", C.c_uint64),
+        ("score_hash", C.c_uint64), ("buffer_allocation_count", C.c_uint64), ("buffer_reuse_count", C.c_uint64),
+        ("descriptor_update_count", C.c_uint64), ("pipeline_create_count", C.c_uint64),
+        ("observed_weight_generation", C.c_uint64), ("requested_weight_generation", C.c_uint64),
+    ]
+
+
 class OctB200BlockConfig(C.Structure):
     _fields_ = [
         ("struct_size", C.c_uint32),
@@ -341,6 +428,17 @@ SIGNATURES = {
     "prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm": (
         C.c_int,
         [_vp, C.POINTER(PrometheusGemma4E2BM1InputRmsNormRequest), C.POINTER(PrometheusGemma4E2BM1InputRmsNormResult)]),
+    "prometheus_reactor_runtime_gemma4e2b_m1_projection_activation_rmsnorm": (
+        C.c_int,
+        [_vp, C.POINTER(PrometheusGemma4E2BM1InputRmsNormRequest), C.POINTER(PrometheusGemma4E2BM1InputRmsNormResult)]),
+    "prometheus_reactor_runtime_gemma4e2b_m1_rope": (
+        C.c_int, [_vp, C.POINTER(PrometheusGemma4E2BM1RopeRequest), C.POINTER(PrometheusGemma4E2BM1RopeResult)]),
+    "prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm_rope": (
+        C.c_int, [_vp, C.POINTER(PrometheusGemma4E2BM1HeadRmsNormRopeRequest),
+                  C.POINTER(PrometheusGemma4E2BM1HeadRmsNormRopeResult)]),
+    "prometheus_reactor_runtime_gemma4e2b_m1_attention_scores": (
+        C.c_int, [_vp, C.POINTER(PrometheusGemma4E2BM1AttentionScoresRequest),
+                  C.POINTER(PrometheusGemma4E2BM1AttentionScoresResult)]),
     "prometheus_runtime_create": (C.c_int, [_vp, C.POINTER(C.c_void_p)]),
     "prometheus_runtime_destroy": (C.c_int, [_vp]),
     "prometheus_runtime_probe": (C.c_int, [_vp, C.POINTER(PrometheusCaps)]),
@@ -627,12 +725,31 @@ class Runtime:
         rc = self.lib.prometheus_reactor_runtime_row_wise_softmax(self.handle, C.byref(req), C.byref(res))
         return rc, (y if rc == PROM_OK else None), res
 
-    def rmsnorm(self, x: np.ndarray, weight: np.ndarray, eps: float, *, head: bool = False
+    def next_weight_generation(self) -> int:
+        """A fresh weight generation for this handle: the M1 entries require each weight
+        preparation to carry a generation above the last one committed (as Go's lane does,
+        gemma4e2b_m1_rtx.go:268-545)."""
+        self._generation = getattr(self, "_generation", 0) + 1
+        return self._generation
+
+    def rmsnorm(self, x: np.ndarray, weight: np.ndarray, eps: float, *, head: bool = False,
+                mode: str = "input", stride: Optional[int] = None, width: Optional[int] = None,
+                rows: Optional[int] = None
                 ) -> tuple[int, Optional[np.ndarray], Optional[np.ndarray], PrometheusGemma4E2BM1InputRmsNormResult]:
+        """The M46 RMSNorm family over host rows: mode "input" (fp32), "projection" (BF16
+        output), "head" (BF16 input and output; also selected by head=True).  x may be 1-D
+        with explicit rows / width / stride (row stride >= width), else [rows, width]."""
         _f32(x, "x")
         _f32(weight, "weight")
-        rows, width = x.shape
-        y = np.empty_like(x)
+        if head:
+            mode = "head"
+        if x.ndim == 2 and rows is None:
+            rows, width = x.shape
+            stride = width
+        width = width or weight.size
+        stride = stride or width
+        rows = rows if rows is not None else x.size // stride
+        y = np.empty((rows, width), dtype=np.float32)
         inv = np.empty(rows, dtype=np.float32)
         req = PrometheusGemma4E2BM1InputRmsNormRequest()
         req.struct_size = C.sizeof(req)
@@ -641,15 +758,86 @@ class Runtime:
         req.weight_element_count = weight.size
         req.output_element_count = y.size
         req.inv_rms_output_element_count = rows
-        req.tokens, req.model_width, req.input_row_stride = rows, width, width
+        req.tokens, req.model_width, req.input_row_stride = rows, width, stride
         req.epsilon = eps
-        req.input_generation = req.weight_generation = req.exact_source_hash = 1
+        req.input_generation = req.exact_source_hash = 1
+        req.weight_generation = self.next_weight_generation()
         res = PrometheusGemma4E2BM1InputRmsNormResult()
-        fn = (self.lib.prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm if head
-              else self.lib.prometheus_reactor_runtime_gemma4e2b_m1_input_rmsnorm)
+        fn = {"input": self.lib.prometheus_reactor_runtime_gemma4e2b_m1_input_rmsnorm,
+              "projection": self.lib.prometheus_reactor_runtime_gemma4e2b_m1_projection_activation_rmsnorm,
+              "head": self.lib.prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm}[mode]
         rc = fn(self.handle, C.byref(req), C.byref(res))
         ok = rc == PROM_OK
         return rc, (y if ok else None), (inv if ok else None), res
+
+    # -- Gemma M1 positional / score boundary (bridge.go:493-515)
+    def gemma_rope(self, source: np.ndarray, cosine: np.ndarray, sine: np.ndarray, tokens: int, heads: int,
+                   head_width: int, out: Optional[np.ndarray] = None
+                   ) -> tuple[int, np.ndarray, PrometheusGemma4E2BM1RopeResult]:
+        for t, nm in ((source, "source"), (cosine, "cosine"), (sine, "sine")):
+            _f32(t, nm)
+        y = np.empty(source.size, dtype=np.float32) if out is None else out
+        req = PrometheusGemma4E2BM1RopeRequest()
+        req.struct_size = C.sizeof(req)
+        req.source, req.cosine, req.sine, req.output = _ptr(source), _ptr(cosine), _ptr(sine), _ptr(y)
+        req.source_element_count, req.cosine_element_count = source.size, cosine.size
+        req.sine_element_count, req.output_element_count = sine.size, y.size
+        req.tokens, req.heads, req.head_width = tokens, heads, head_width
+        req.source_generation = req.table_generation = 1
+        res = PrometheusGemma4E2BM1RopeResult()
+        rc = self.lib.prometheus_reactor_runtime_gemma4e2b_m1_rope(self.handle, C.byref(req), C.byref(res))
+        return rc, y, res
+
+    def gemma_head_rmsnorm_rope(self, x: np.ndarray, weight: np.ndarray, cosine: np.ndarray, sine: np.ndarray,
+                                tokens: int, heads: int, head_width: int, eps: float = 1e-6,
+                                read_back: bool = True, weight_generation: Optional[int] = None
+                                ) -> tuple[int, Optional[np.ndarray], PrometheusGemma4E2BM1HeadRmsNormRopeResult]:
+        for t, nm in ((x, "x"), (weight, "weight"), (cosine, "cosine"), (sine, "sine")):
+            _f32(t, nm)
+        y = np.empty(x.size, dtype=np.float32) if read_back else None
+        req = PrometheusGemma4E2BM1HeadRmsNormRopeRequest()
+        req.struct_size = C.sizeof(req)
+        req.input, req.weight, req.cosine, req.sine = _ptr(x), _ptr(weight), _ptr(cosine), _ptr(sine)
+        req.output = _ptr(y) if y is not None else None
+        req.input_element_count, req.weight_element_count = x.size, weight.size
+        req.cosine_element_count, req.sine_element_count = cosine.size, sine.size
+        req.output_element_count = y.size if y is not None else 0
+        req.tokens, req.heads, req.head_width, req.epsilon = tokens, heads, head_width, eps
+        req.input_generation = req.table_generation = req.exact_source_hash = 1
+        req.weight_generation = weight_generation or self.next_weight_generation()
+        res = PrometheusGemma4E2BM1HeadRmsNormRopeResult()
+        rc = self.lib.prometheus_reactor_runtime_gemma4e2b_m1_head_rmsnorm_rope(self.handle, C.byref(req),
+                                                                                C.byref(res))
+        return rc, (y if rc == PROM_OK else None), res
+
+    def gemma_attention_scores(self, q: np.ndarray, k: np.ndarray, q_weight: np.ndarray, k_weight: np.ndarray,
+                               cosine: np.ndarray, sine: np.ndarray, tokens: int, query_heads: int,
+                               head_width: int, scale: float, order: int = 0, eps: float = 1e-6,
+                               out: Optional[np.ndarray] = None
+                               ) -> tuple[int, np.ndarray, PrometheusGemma4E2BM1AttentionScoresResult]:
+        for t, nm in ((q, "q"), (k, "k"), (q_weight, "q_weight"), (k_weight, "k_weight"), (cosine, "cosine"),
+                      (sine, "sine")):
+            _f32(t, nm)
+        s = np.empty(query_heads * tokens * tokens, dtype=np.float32) if out is None else out
+        req = PrometheusGemma4E2BM1AttentionScoresRequest()
+        req.struct_size = C.sizeof(req)
+        req.query_input, req.key_input = _ptr(q), _ptr(k)
+        req.query_weight, req.key_weight = _ptr(q_weight), _ptr(k_weight)
+        req.cosine, req.sine, req.scores = _ptr(cosine), _ptr(sine), _ptr(s)
+        req.query_input_element_count, req.key_input_element_count = q.size, k.size
+        req.query_weight_element_count, req.key_weight_element_count = q_weight.size, k_weight.size
+        req.cosine_element_count, req.sine_element_count, req.score_element_count = cosine.size, sine.size, s.size
+        req.tokens, req.query_heads, req.key_heads, req.head_width = tokens, query_heads, 1, head_width
+        req.epsilon, req.scale, req.preparation_order = eps, scale, order
+        req.query_input_generation, req.key_input_generation, req.table_generation = 1, 2, 1
+        first, second = self.next_weight_generation(), self.next_weight_generation()
+        # weights are prepared in preparation order, each with a fresh generation
+        req.query_weight_generation, req.key_weight_generation = (first, second) if order == 0 else (second, first)
+        req.query_exact_source_hash, req.key_exact_source_hash = 11, 12
+        res = PrometheusGemma4E2BM1AttentionScoresResult()
+        rc = self.lib.prometheus_reactor_runtime_gemma4e2b_m1_attention_scores(self.handle, C.byref(req),
+                                                                               C.byref(res))
+        return rc, s, res
 
     # -- device-resident extensions (torch tensors or raw device addresses)
     def sgemm_device(self, a, b, c, m: int, n: int, k: int, variant: int = SGEMM_AUTO, stream=None,

@@ -393,6 +393,95 @@ ORACLE_API void oracle_rmsnorm_f64(int64_t rows, int64_t width, int64_t stride, 
   parallel_rows(threads, 0, rows, rms_f64_range, &q);
 }
 
+/* ---------------------------------------------------------------- Gemma M1 BF16 boundary */
+
+/* float32ToBF16 then bf16ToFloat32 (internal/prometheus/gemma4e2b_m1_rtx.go:1005-1014):
+   round to nearest even on the fp32 bit pattern, re-expanded to fp32. */
+static float bf16_round(float v) {
+  uint32_t b;
+  memcpy(&b, &v, 4);
+  b += 0x7fffu + ((b >> 16) & 1u);
+  b &= 0xffff0000u;
+  float r;
+  memcpy(&r, &b, 4);
+  return r;
+}
+
+ORACLE_API void oracle_bf16_round(int64_t n, const float* in, float* out) {
+  for (int64_t i = 0; i < n; ++i) out[i] = bf16_round(in[i]);
+}
+
+/* The reference's own RMSNorm oracle with optional BF16 rounding of input and
+   output (internal/prometheus/native/Marionette/reactor_concept_rmsnorm_tests.cpp:17-35,
+   the arithmetic of the M46 family, reactor_api.c:250-395): binary64 sum of
+   squares, inv = float(1 / sqrt(sum / width + eps)) in binary64, value =
+   (x * inv) * weight in fp32, then the optional output rounding. */
+ORACLE_API void oracle_m1_rmsnorm(int64_t rows, int64_t width, int64_t stride, const float* in, const float* weight,
+                                  float eps, int round_in, int round_out, float* out, float* inv_rms) {
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* x = in + r * stride;
+    double sum = 0.0;
+    for (int64_t c = 0; c < width; ++c) {
+      const double v = round_in ? bf16_round(x[c]) : x[c];
+      sum += v * v;
+    }
+    const float inv = (float)(1.0 / sqrt(sum / (double)width + (double)eps));
+    if (inv_rms != NULL) inv_rms[r] = inv;
+    for (int64_t c = 0; c < width; ++c) {
+      const float v = round_in ? bf16_round(x[c]) : x[c];
+      const float t = v * inv * weight[c];
+      out[r * width + c] = round_out ? bf16_round(t) : t;
+    }
+  }
+}
+
+/* cpuGemma4e2bRope (internal/prometheus/gemma4e2b_m1_rtx.go:834-861): for row
+   (token, head) and component c, f = c mod hw/2, mate = the other half's c;
+   first = bf16(x[c] * cos[token][f]), second = bf16(x[mate] * sin[token][f]),
+   out = bf16(first - second) for the first half, bf16(first + second) for the
+   second.  Tables are [token][hw]; only their first hw/2 entries are read. */
+ORACLE_API void oracle_m1_rope(int64_t tokens, int64_t heads, int64_t hw, const float* src, const float* cos_t,
+                               const float* sin_t, float* out) {
+  const int64_t half = hw / 2;
+  for (int64_t t = 0; t < tokens; ++t)
+    for (int64_t h = 0; h < heads; ++h) {
+      const int64_t base = (t * heads + h) * hw;
+      for (int64_t c = 0; c < hw; ++c) {
+        const int64_t f = c % half;
+        const int64_t mate = c >= half ? base + f : base + f + half;
+        const float first = bf16_round(src[base + c] * cos_t[t * hw + f]);
+        const float second = bf16_round(src[mate] * sin_t[t * hw + f]);
+        out[base + c] = bf16_round(c >= half ? first + second : first - second);
+      }
+    }
+}
+
+/* Raw pre-mask scores from positioned Q [tokens][qheads][hw] and K [tokens][hw]
+   (every query head reads KV head 0, cpuGemma4e2bRawScores,
+   gemma4e2b_m1_rtx.go:863-883), out [qheads][tokens][tokens].  form 0 is the
+   reference test's independent chain: binary64 dot, times scale, rounded once
+   (Marionette/reactor_concept_rmsnorm_tests.cpp:157-162); form 1 is the Go
+   loop itself: fp32 accumulation left to right, then * scale in fp32. */
+ORACLE_API void oracle_m1_scores(int64_t tokens, int64_t qheads, int64_t hw, const float* q, const float* k,
+                                 double scale, int form, float* out) {
+  for (int64_t h = 0; h < qheads; ++h)
+    for (int64_t i = 0; i < tokens; ++i)
+      for (int64_t j = 0; j < tokens; ++j) {
+        const float* qr = q + (i * qheads + h) * hw;
+        const float* kr = k + j * hw;
+        float* dst = out + (h * tokens + i) * tokens + j;
+        if (form == 1) {
+          float acc = 0.0f;
+          for (int64_t d = 0; d < hw; ++d) acc += qr[d] * kr[d];
+          *dst = acc * (float)scale;
+        } else {
+          double acc = 0.0;
+          for (int64_t d = 0; d < hw; ++d) acc += (double)qr[d] * (double)kr[d];
+          *dst = (float)(acc * scale);
+        }
+      }
+}
+
 ORACLE_API int oracle_max_threads(void) {
   const long n = sysconf(_SC_NPROCESSORS_ONLN);
   return n > 0 ? (int)n : 1;

@@ -57,6 +57,10 @@ def lib() -> C.CDLL:
         L.oracle_reduction_compare.restype = i32
         L.oracle_rmsnorm_f32.argtypes = [i64, i64, i64, vp, vp, C.c_float, vp, vp, i32, i32]
         L.oracle_rmsnorm_f64.argtypes = [i64, i64, i64, vp, vp, C.c_double, vp, vp, i32]
+        L.oracle_bf16_round.argtypes = [i64, vp, vp]
+        L.oracle_m1_rmsnorm.argtypes = [i64, i64, i64, vp, vp, C.c_float, i32, i32, vp, vp]
+        L.oracle_m1_rope.argtypes = [i64, i64, i64, vp, vp, vp, vp]
+        L.oracle_m1_scores.argtypes = [i64, i64, i64, vp, vp, C.c_double, i32, vp]
         L.oracle_max_threads.restype = i32
         _lib = L
     return _lib
@@ -220,3 +224,55 @@ def normal_matrix(rows: int, cols: int, seed: int) -> np.ndarray:
     """Seeded N(0, 1) fp32 matrix (PCG64): the reduction benchmark input distribution."""
     rng = np.random.Generator(np.random.PCG64(seed))
     return rng.standard_normal((rows, cols), dtype=np.float32)
+
+
+# ------------------------------------------------------------------ Gemma M1 BF16 boundary
+def _f32c(x) -> np.ndarray:
+    return np.ascontiguousarray(x, dtype=np.float32)
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """float32ToBF16 then bf16ToFloat32 (gemma4e2b_m1_rtx.go:1005-1014)."""
+    x = _f32c(x)
+    out = np.empty_like(x)
+    lib().oracle_bf16_round(x.size, _p(x), _p(out))
+    return out
+
+
+def m1_rmsnorm(x: np.ndarray, w: np.ndarray, eps: float, round_in: bool, round_out: bool,
+               stride: int | None = None, rows: int | None = None, width: int | None = None
+               ) -> tuple[np.ndarray, np.ndarray]:
+    """The M46 RMSNorm family's arithmetic (reference oracle, reactor_concept_rmsnorm_tests.cpp:17-35)."""
+    x, w = _f32c(x), _f32c(w)
+    width = width or w.size
+    stride = stride or width
+    rows = rows if rows is not None else x.size // stride
+    out = np.empty(rows * width, dtype=np.float32)
+    inv = np.empty(rows, dtype=np.float32)
+    lib().oracle_m1_rmsnorm(rows, width, stride, _p(x), _p(w), eps, int(round_in), int(round_out), _p(out), _p(inv))
+    return out, inv
+
+
+def m1_rope(src: np.ndarray, cos: np.ndarray, sin: np.ndarray, tokens: int, heads: int, hw: int) -> np.ndarray:
+    """cpuGemma4e2bRope (gemma4e2b_m1_rtx.go:834-861)."""
+    src, cos, sin = _f32c(src), _f32c(cos), _f32c(sin)
+    out = np.empty(tokens * heads * hw, dtype=np.float32)
+    lib().oracle_m1_rope(tokens, heads, hw, _p(src), _p(cos), _p(sin), _p(out))
+    return out
+
+
+def m1_head_rmsnorm_rope(x, w, cos, sin, tokens: int, heads: int, hw: int, eps: float = 1e-6) -> np.ndarray:
+    """BF16 head RMSNorm then RoPE (reactor_api.c:404-505; the test oracle `positional`,
+    reactor_concept_rmsnorm_tests.cpp:59-70)."""
+    normed, _ = m1_rmsnorm(x, w, eps, True, True, stride=hw, rows=tokens * heads, width=hw)
+    return m1_rope(normed, cos, sin, tokens, heads, hw)
+
+
+def m1_scores(q: np.ndarray, k: np.ndarray, tokens: int, qheads: int, hw: int, scale: float,
+              form: str = "f64") -> np.ndarray:
+    """Raw scores [qheads][tokens][tokens]; form "f64" is the reference test's binary64 chain,
+    "go" is cpuGemma4e2bRawScores' fp32 loop (gemma4e2b_m1_rtx.go:863-883)."""
+    q, k = _f32c(q), _f32c(k)
+    out = np.empty(qheads * tokens * tokens, dtype=np.float32)
+    lib().oracle_m1_scores(tokens, qheads, hw, _p(q), _p(k), float(scale), {"f64": 0, "go": 1}[form], _p(out))
+    return out

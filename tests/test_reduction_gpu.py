@@ -160,13 +160,20 @@ def test_rmsnorm_baseline(runtime, oracle_mod, width):
     rows = 32768 if width != 33 else 100
     x = o.normal_matrix(rows, width, seed=width + 1)
     wt = (o.uniform_matrix(1, width, seed=width + 2).ravel() * np.float32(0.5) + np.float32(1.0)).astype(np.float32)
-    rc, y, inv, res = runtime.rmsnorm(x, wt, 1e-6, head=(width == 256))
+    rc, y, inv, res = runtime.rmsnorm(x, wt, 1e-6)
     assert rc == R.PROM_OK, res.detail_code
     ref64, inv64 = o.rmsnorm_f64(x, wt, 1e-6)
     assert rel_err(y, ref64) <= REL_TOL
     assert rel_err(inv, inv64) <= REL_TOL
-    ref32, _ = o.rmsnorm_f32(x, wt, 1e-6, threads=o.max_threads())
-    assert rel_err(y, ref32) <= 1e-4  # the fp32 canonical formula differs by its own rounding only
+    for form in ("head", "canonical"):  # Gemma's and Z-Image's fp32 CPU forms
+        ref32, _ = o.rmsnorm_f32(x, wt, 1e-6, threads=o.max_threads(), form=form)
+        assert rel_err(y, ref32) <= 1e-4  # each fp32 CPU formula differs by its own rounding only
+    if width == 256:
+        # the head entry rounds its input and output through BF16 (reactor_api.c:370-395)
+        rc, yh, invh, res = runtime.rmsnorm(x, wt, 1e-6, mode="head")
+        assert rc == R.PROM_OK, res.detail_code
+        want, want_inv = o.m1_rmsnorm(x, wt, 1e-6, True, True)
+        assert np.array_equal(yh.ravel(), want) and np.array_equal(invh, want_inv)
 
 
 def test_device_output_read_right_after_the_call(runtime, oracle_mod):
