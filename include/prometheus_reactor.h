@@ -524,7 +524,7 @@ typedef struct PrometheusReactorConfig {
   uint32_t async_test_flags;
   uint32_t batch_ring_depth;        /* accepted, ignored */
   uint32_t reduction_test_flags;
-  uint32_t reduction_ring_depth;    /* accepted, ignored: one CUDA stream per handle */
+  uint32_t reduction_ring_depth;    /* reported by reduction diagnostics; one CUDA stream per handle */
   const char* shader_package_root;  /* accepted, ignored: kernels are linked in */
 } PrometheusReactorConfig;
 
@@ -740,6 +740,93 @@ typedef struct PrometheusGemma4E2BM1AttentionScoresResult {
   uint64_t requested_weight_generation;
 } PrometheusGemma4E2BM1AttentionScoresResult;
 
+/* Reduction diagnostics (reactor_api.h:600-633): counters of the handle's
+   reduction executor.  CUDA meaning: one "physical slot" per handle (the
+   handle's stream), a "queue submit" is one enqueued launch sequence. */
+typedef struct PrometheusReductionDiagnostics {
+  uint32_t struct_size;
+  uint32_t initialized;
+  uint32_t production_enabled;
+  uint32_t experimental_enabled;
+  uint32_t configured_ring_depth;
+  uint32_t physical_slot_count;
+  uint32_t acquire_cursor;
+  uint32_t outstanding_slots;
+  uint32_t quarantined_slots;
+  uint64_t next_logical_request_id;
+  uint64_t total_requests;
+  uint64_t successful_requests;
+  uint64_t logical_failure_count;
+  uint64_t physical_recycle_count;
+  uint64_t quarantine_count;
+  uint64_t reap_count;
+  uint64_t pipeline_create_count;
+  uint64_t descriptor_update_count;
+  uint64_t command_record_count;
+  uint64_t queue_submit_count;
+  uint64_t buffer_allocation_count;
+  uint64_t buffer_reuse_count;
+  uint64_t temporary_capacity_bytes;
+  uint64_t last_replay_id;
+  uint64_t last_gpu_duration_ns;
+  uint64_t last_end_to_end_ns;
+  uint32_t last_stage_count;
+  uint32_t last_physical_slot_id;
+  uint32_t last_physical_slot_generation;
+  int32_t last_detail_code;
+  uint32_t validation_enabled;
+  uint32_t validation_error_count;
+} PrometheusReductionDiagnostics;
+
+/* Async SGEMM diagnostics (reactor_api.h:1987-2032).  One physical slot per
+   task; quarantine and deferred feedback do not exist on CUDA and stay 0. */
+typedef struct PrometheusSgemmAsyncTaskDiagnostics {
+  int32_t task_id;
+  uint32_t generation;
+  uint32_t lifecycle_state;
+  uint32_t physical_slot_id;
+  uint32_t physical_slot_generation;
+  uint64_t submission_sequence;
+  uint32_t timing_valid;
+  uint64_t gpu_duration_ns;
+  uint32_t feedback_pending;
+  uint32_t feedback_committed;
+  int32_t failure_detail;
+  uint32_t failure_class;
+  uint32_t abandoned;
+  uint32_t physical_slot_state;
+  uint32_t quarantined;
+  uint32_t physical_completion_confirmed;
+  uint32_t reap_pending;
+  uint32_t reap_completed;
+} PrometheusSgemmAsyncTaskDiagnostics;
+
+typedef struct PrometheusSgemmAsyncDiagnostics {
+  uint32_t task_capacity;
+  uint32_t active_task_count;
+  uint32_t submitted_count;
+  uint32_t ready_count;
+  uint32_t failed_count;
+  uint32_t consumed_count;
+  uint32_t abandoned_count;
+  uint64_t queue_full_count;
+  uint64_t stale_id_rejection_count;
+  uint32_t max_in_flight;
+  uint32_t feedback_pending_count;
+  uint64_t feedback_committed_count;
+  uint64_t feedback_skipped_count;
+  uint64_t next_feedback_sequence;
+  uint32_t quarantined_slot_count;
+  uint64_t quarantine_event_count;
+  uint64_t reap_poll_count;
+  uint64_t reap_success_count;
+  uint64_t reap_wait_count;
+  uint64_t reap_failure_count;
+  uint32_t max_quarantine_depth;
+  uint32_t runtime_unsafe_to_reuse;
+  PrometheusSgemmAsyncTaskDiagnostics tasks[4];
+} PrometheusSgemmAsyncDiagnostics;
+
 /* Envelope of the Gemma M1 entry points.  The reference admits only the M1
    geometry (15 tokens, 8 or 1 heads of 256, internal/prometheus/native/
    reactor_api.c:370-395, 404-441, 507-547; reactor_concept_rmsnorm.cpp:157-212);
@@ -805,6 +892,9 @@ PROM_REACTOR_API int prometheus_reactor_runtime_sgemm_consume_async(void* handle
                                                                     uint32_t c_len, uint32_t* out_stage,
                                                                     int* out_detail_code);
 PROM_REACTOR_API int prometheus_reactor_runtime_sgemm_abandon_async(void* handle, int task_id);
+/* reactor_api.h:2635-2636 -- task table and lifecycle counters of the async SGEMM queue. */
+PROM_REACTOR_API int prometheus_reactor_runtime_sgemm_async_diagnostics(void* handle,
+                                                                         PrometheusSgemmAsyncDiagnostics* out_diag);
 
 /* reactor_api.h:2671-2672 -- host-only planner; same stage roles as the
    reference schedule (reactors/PrometheusReduction.concept:128-164). */
@@ -813,6 +903,16 @@ PROM_REACTOR_API int prometheus_reactor_reduction_plan(const PrometheusReduction
 /* reactor_api.h:2673-2675 -- row SUM / MAX / stable SOFTMAX over host buffers. */
 PROM_REACTOR_API int prometheus_reactor_runtime_reduction(void* handle, const PrometheusReductionRequest* request,
                                                           PrometheusReductionExecutionResult* out_result);
+/* reactor_api.h:2676-2677 -- counters of the handle's reduction executor. */
+PROM_REACTOR_API int prometheus_reactor_runtime_reduction_diagnostics(void* handle,
+                                                                      PrometheusReductionDiagnostics* out_diag);
+/* reactor_api.h:2678-2681 -- warm-up and measured executions of one reduction
+   request, then a correctness check of the last output (reactor_vulkan_fused_
+   reduction.c:1122-1206).  The check runs on the device: an independent
+   recomputation and the reference comparator's tolerances. */
+PROM_REACTOR_API int prometheus_reactor_runtime_reduction_benchmark(void* handle,
+                                                                    const PrometheusReductionBenchmarkRequest* request,
+                                                                    PrometheusReductionBenchmarkResult* out_result);
 /* reactor_api.h:2682-2685 -- forced fused softmax; rejects partial aliasing and
    non-finite input like reactor_vulkan_fused_reduction.c:892-994. */
 PROM_REACTOR_API int prometheus_reactor_runtime_row_wise_softmax(void* handle,

@@ -191,6 +191,14 @@ cudaError_t rmsnorm(const float* in, uint64_t in_stride, const float* weight, fl
                     uint32_t rows, uint32_t width, float eps, unsigned long long* nonfinite, unsigned int* err,
                     cudaStream_t stream);
 
+// Correctness check of a reduction's output on the device: `expected` (row count,
+// or rows * width for softmax, floats) receives an independent recomputation and
+// `first_bad` (preset to UINT64_MAX) the smallest failing flat index under the
+// reference comparator's tolerances; softmax row-sum failures are reported as
+// rows * width + row.
+cudaError_t reduction_self_check(const float* in, const float* actual, float* expected, uint32_t rows,
+                                 uint32_t width, uint32_t op, unsigned long long* first_bad, cudaStream_t stream);
+
 // ---------------------------------------------------------------- Gemma M1 boundary (gemma_m1.cu)
 // BF16 storage rounding as the reference's M1 entry points apply it; inputs
 // must already be checked finite.  Head widths are even and <= kM1MaxHeadWidth.

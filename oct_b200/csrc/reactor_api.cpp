@@ -146,6 +146,8 @@ Runtime* create_runtime(const PrometheusReactorConfig* cfg, int* status) {
       rt->async_test_flags = cfg->async_test_flags;
     if (sz >= offsetof(PrometheusReactorConfig, reduction_test_flags) + sizeof(uint32_t))
       rt->reduction_test_flags = cfg->reduction_test_flags;
+    if (sz >= offsetof(PrometheusReactorConfig, reduction_ring_depth) + sizeof(uint32_t))
+      rt->red_stats.ring_depth = cfg->reduction_ring_depth;
   }
   if (rt->test_flags & PROM_TESTCFG_FAIL_DEVICE_CREATE) {
     // Injected on the host: the handle exists but reports no device.
@@ -191,6 +193,7 @@ void destroy_runtime(Runtime* rt) {
     cudaEventDestroy(ev.main_end);
   }
   for (auto& t : rt->tasks) {
+    if (t.begin != nullptr) cudaEventDestroy(t.begin);
     if (t.done != nullptr) cudaEventDestroy(t.done);
     t.a.release();
     t.b.release();
@@ -375,6 +378,25 @@ void build_plan(const ReductionShape& s, PrometheusReductionPlan* p) {
 }
 
 // Runs one reduction over host buffers; fills stage/detail/timing.
+// Records one executed reduction request in the handle's counters.
+void note_reduction(Runtime* rt, int rc, int32_t detail, uint32_t stage_count, uint64_t replay, uint64_t gpu_ns,
+                    uint64_t e2e_ns) {
+  ReductionStats& st = rt->red_stats;
+  st.initialized = true;
+  ++st.total;
+  ++st.slot_generation;
+  if (rc == PROM_OK) {
+    ++st.success;
+  } else {
+    ++st.failures;
+  }
+  st.last_detail = detail;
+  st.last_stage_count = stage_count;
+  st.last_replay = replay;
+  st.last_gpu_ns = gpu_ns;
+  st.last_e2e_ns = e2e_ns;
+}
+
 int run_reduction_host(Runtime* rt, const float* in, float* out, uint32_t rows, uint32_t width, uint32_t op,
                        uint32_t* stage, int32_t* detail, uint64_t* gpu_ns, uint32_t* gpu_valid,
                        uint64_t* first_nonfinite) {
@@ -384,6 +406,13 @@ int run_reduction_host(Runtime* rt, const float* in, float* out, uint32_t rows, 
     *stage = PROM_STAGE_SUBMIT;
     *detail = PROM_REDUCTION_DETAIL_COMMAND_RECORD_FAILED;
     return PROM_ERROR;
+  }
+  ++rt->red_stats.command_records;
+  {
+    const bool grow_in = rt->rin.raw == nullptr || total * 4 > rt->rin.cap;
+    const bool grow_out = rt->rout.raw == nullptr || out_count * 4 > rt->rout.cap;
+    rt->red_stats.allocations += static_cast<uint64_t>(grow_in) + static_cast<uint64_t>(grow_out);
+    rt->red_stats.reuses += static_cast<uint64_t>(!grow_in) + static_cast<uint64_t>(!grow_out);
   }
   if (rt->rin.ensure(total * 4, rt->stream) != cudaSuccess || rt->rout.ensure(out_count * 4, rt->stream) != cudaSuccess) {
     *stage = PROM_STAGE_INIT;
@@ -407,6 +436,7 @@ int run_reduction_host(Runtime* rt, const float* in, float* out, uint32_t rows, 
   }
   cudaEventRecord(rt->ev0, rt->stream);
   e = oct::row_reduce(din, dout, rows, width, op, rt->nonfinite_word(), rt->err_word(), rt->stream);
+  if (e == cudaSuccess) ++rt->red_stats.submits;
   cudaEventRecord(rt->ev1, rt->stream);
   Words w;
   if (e != cudaSuccess || read_words(rt, &w) != cudaSuccess ||
@@ -452,28 +482,39 @@ AsyncTask* find_task(Runtime* rt, int id) {
 // Non-blocking completion check of a submitted task.
 void poll_task(Runtime* rt, AsyncTask* t) {
   if (t->state != PROM_ASYNC_STATE_SUBMITTED) return;
+  ++rt->async_stats.polls;
   if (rt->test_flags & PROM_TESTCFG_FAIL_ASYNC_POLL) {
     t->state = PROM_ASYNC_STATE_FAILED;
     t->final_detail = PROM_DETAIL_INJECTED_ASYNC_POLL_FAILURE;
     t->final_stage = PROM_STAGE_SUBMIT;
+    ++rt->async_stats.failed;
     return;
   }
   const cudaError_t q = cudaEventQuery(t->done);
   if (q == cudaErrorNotReady) return;
+  ++rt->async_stats.reaped;
   if (q != cudaSuccess) {
     (void)cudaGetLastError();
     t->state = PROM_ASYNC_STATE_FAILED;
     t->final_detail = PROM_DETAIL_ASYNC_FAILED;
+    ++rt->async_stats.failed;
     return;
   }
   Words w;
   if (read_words(rt, &w) != cudaSuccess || w.err != 0) {
     t->state = PROM_ASYNC_STATE_FAILED;
     t->final_detail = OCT_B200_DETAIL_DEVICE_TIMEOUT;
+    ++rt->async_stats.failed;
     return;
+  }
+  float ms = 0.f;
+  if (t->begin != nullptr && cudaEventElapsedTime(&ms, t->begin, t->done) == cudaSuccess) {
+    t->timed = true;
+    t->gpu_ns = static_cast<uint64_t>(static_cast<double>(ms) * 1.0e6);
   }
   t->state = PROM_ASYNC_STATE_READY;
   t->final_stage = PROM_STAGE_TRANSFER_OUT;
+  ++rt->async_stats.ready;
 }
 uint32_t outstanding(Runtime* rt) {
   uint32_t c = 0;
@@ -1206,10 +1247,12 @@ int prometheus_reactor_runtime_sgemm_submit_async(void* handle, const float* a, 
         break;
       }
     if (task == nullptr) {
+      ++rt->async_stats.queue_full;
       set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_DETAIL_ASYNC_QUEUE_FULL);
       return PROM_ERROR;
     }
-    if (task->done == nullptr && cudaEventCreateWithFlags(&task->done, cudaEventDisableTiming) != cudaSuccess) {
+    if ((task->begin == nullptr && cudaEventCreate(&task->begin) != cudaSuccess) ||
+        (task->done == nullptr && cudaEventCreate(&task->done) != cudaSuccess)) {
       set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_DETAIL_ASYNC_SUBMIT_REJECTED);
       return PROM_ERROR;
     }
@@ -1228,6 +1271,7 @@ int prometheus_reactor_runtime_sgemm_submit_async(void* handle, const float* a, 
     if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
     const uint32_t variant =
         (rt->test_flags & PROM_TESTCFG_FORCE_STRICT_FP32) ? OCT_B200_SGEMM_FMA : OCT_B200_SGEMM_AUTO;
+    if (e == cudaSuccess) e = cudaEventRecord(task->begin, rt->stream);
     int d = (e == cudaSuccess) ? enqueue_sgemm(rt, da, k, db, n, dc, n, m, n, k, variant, rt->stream) : -1;
     if (d == 0) e = cudaEventRecord(task->done, rt->stream);
     if (e != cudaSuccess || d != 0) {
@@ -1243,6 +1287,18 @@ int prometheus_reactor_runtime_sgemm_submit_async(void* handle, const float* a, 
     task->k = k;
     task->final_detail = PROM_DETAIL_PATH_DIRECT;
     task->final_stage = PROM_STAGE_SUBMIT;
+    task->generation += 1;
+    task->sequence = ++rt->async_stats.sequence;
+    task->abandoned = false;
+    task->timed = false;
+    task->gpu_ns = 0;
+    ++rt->async_stats.submitted;
+    {
+      uint32_t in_flight = 0;
+      for (auto& t : rt->tasks)
+        if (t.active && t.state == PROM_ASYNC_STATE_SUBMITTED) ++in_flight;
+      rt->async_stats.max_in_flight = std::max(rt->async_stats.max_in_flight, in_flight);
+    }
     *out_task_id = task->id;
     set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, 0);
     return PROM_OK;
@@ -1292,6 +1348,7 @@ int prometheus_reactor_runtime_sgemm_consume_async(void* handle, int task_id, fl
     std::lock_guard<std::mutex> lock(rt->mu);
     AsyncTask* t = find_task(rt, task_id);
     if (t == nullptr) {
+      ++rt->async_stats.stale_ids;
       set_status(out_stage, out_detail_code, PROM_STAGE_SUBMIT, PROM_DETAIL_ASYNC_INVALID_TASK);
       return PROM_ERROR;
     }
@@ -1321,6 +1378,7 @@ int prometheus_reactor_runtime_sgemm_consume_async(void* handle, int task_id, fl
       return PROM_ERROR;
     }
     t->state = PROM_ASYNC_STATE_CONSUMED;
+    ++rt->async_stats.consumed;
     set_status(out_stage, out_detail_code, PROM_STAGE_TRANSFER_OUT, t->final_detail);
     return PROM_OK;
   } catch (...) {
@@ -1335,9 +1393,14 @@ int prometheus_reactor_runtime_sgemm_abandon_async(void* handle, int task_id) {
     if (rt == nullptr) return PROM_INVALID_HANDLE;
     std::lock_guard<std::mutex> lock(rt->mu);
     AsyncTask* t = find_task(rt, task_id);
-    if (t == nullptr) return PROM_ERROR;
+    if (t == nullptr) {
+      ++rt->async_stats.stale_ids;
+      return PROM_ERROR;
+    }
     poll_task(rt, t);
     if (t->state == PROM_ASYNC_STATE_SUBMITTED) return PROM_ERROR;  // unconsumed work still in flight
+    if (t->state != PROM_ASYNC_STATE_CONSUMED) ++rt->async_stats.abandoned;
+    t->abandoned = t->state != PROM_ASYNC_STATE_CONSUMED;
     t->active = false;
     t->state = PROM_ASYNC_STATE_IDLE;
     return PROM_OK;
@@ -1412,6 +1475,8 @@ int prometheus_reactor_runtime_reduction(void* handle, const PrometheusReduction
     out.stage = stage;
     out.detail_code = detail;
     out.end_to_end_ns = ns_since(t0);
+    out.physical_slot_generation = rt->red_stats.slot_generation;
+    note_reduction(rt, rc, detail, out.plan.stage_count, out.plan.replay_id, out.gpu_duration_ns, out.end_to_end_ns);
     return rc;
   } catch (...) {
     out.stage = PROM_STAGE_INIT;
@@ -1472,6 +1537,7 @@ int prometheus_reactor_runtime_row_wise_softmax(void* handle, const PrometheusRo
                                       request->elements_per_row, PROM_REDUCTION_OPERATION_SOFTMAX, &stage, &detail,
                                       &out.gpu_duration_ns, &out.gpu_timestamp_valid, &out.first_nonfinite_index);
     out.end_to_end_ns = ns_since(t0);
+    note_reduction(rt, rc, detail, 1, 0, out.gpu_duration_ns, out.end_to_end_ns);
     if (rc != PROM_OK) {
       const int32_t d = detail == PROM_REDUCTION_DETAIL_NONFINITE_INPUT ? PROM_SOFTMAX_DETAIL_NONFINITE_INPUT : detail;
       return fail(stage, d, rc);

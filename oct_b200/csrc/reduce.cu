@@ -27,6 +27,7 @@
 #include <cuda_runtime.h>
 
 #include <cfloat>
+#include <algorithm>
 #include <cstdint>
 
 #include "kernels.h"
@@ -547,6 +548,87 @@ cudaError_t rmsnorm(const float* in, uint64_t in_stride, const float* weight, fl
                     uint32_t rows, uint32_t width, float eps, unsigned long long* nonfinite, unsigned int* err,
                     cudaStream_t stream) {
   return dispatch<kRms>(in, in_stride, out, inv_rms, weight, eps, rows, width, nonfinite, err, stream);
+}
+
+// ---------------------------------------------------------------- self-check
+// The reduction benchmark entry's correctness check (reactor_vulkan_fused_reduction.c:
+// 1122-1206 checks its output against prom_reduction_cpu_reference with
+// prom_reduction_compare, :996-1114).  Here both halves run on the device: an
+// independent plain kernel, one thread per row walking it in order, recomputes
+// the expected values (SUM in binary64, MAX exact, SOFTMAX with binary64 exp and
+// denominator), and a compare kernel applies the comparator's tolerances and
+// records the smallest failing flat index (softmax row-sum failures are encoded
+// after the element range).
+namespace {
+
+__global__ void check_expected_kernel(const float* __restrict__ in, float* __restrict__ expected, uint32_t rows,
+                                      uint32_t width, uint32_t op) {
+  for (uint64_t r = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; r < rows;
+       r += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const float* v = in + r * width;
+    if (op == kSum) {
+      double acc = 0.0;
+      for (uint32_t c = 0; c < width; ++c) acc += static_cast<double>(v[c]);
+      expected[r] = static_cast<float>(acc);
+    } else {
+      float mx = v[0];
+      for (uint32_t c = 1; c < width; ++c) mx = v[c] > mx ? v[c] : mx;
+      if (op == kMax) {
+        expected[r] = mx;
+      } else {
+        double den = 0.0;
+        for (uint32_t c = 0; c < width; ++c) den += exp(static_cast<double>(v[c]) - mx);
+        for (uint32_t c = 0; c < width; ++c)
+          expected[r * width + c] = static_cast<float>(exp(static_cast<double>(v[c]) - mx) / den);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float rel_floor(float expected, float actual) {
+  float den = fabsf(expected);
+  if (den < 1.0e-20f) den = 1.0f;
+  return fabsf(actual - expected) / den;
+}
+
+__global__ void check_compare_kernel(const float* __restrict__ expected, const float* __restrict__ actual,
+                                     uint32_t rows, uint32_t width, uint32_t op,
+                                     unsigned long long* __restrict__ first_bad) {
+  const uint64_t count = op == kSoftmax ? static_cast<uint64_t>(rows) * width : rows;
+  const float atol = op == kSoftmax ? 2.0e-5f : (op == kMax ? 0.0f : 2.0e-5f * static_cast<float>(width));
+  const float rtol = op == kSoftmax ? 2.0e-4f : (op == kMax ? 0.0f : 2.0e-5f);
+  const uint64_t step = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  const uint64_t t0 = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+  for (uint64_t i = t0; i < count; i += step) {
+    const float a = actual[i], e = expected[i];
+    if (!isfinite(a) || (fabsf(a - e) > atol && rel_floor(e, a) > rtol)) atomicMin(first_bad, i);
+  }
+  if (op == kSoftmax) {
+    for (uint64_t r = t0; r < rows; r += step) {
+      double s = 0.0;
+      bool ok = true;
+      for (uint32_t c = 0; c < width; ++c) {
+        const float v = actual[r * width + c];
+        if (!isfinite(v) || v < -2.0e-7f) ok = false;
+        s += v;
+      }
+      if (!ok || fabs(s - 1.0) > 3.0e-4) atomicMin(first_bad, count + r);
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t reduction_self_check(const float* in, const float* actual, float* expected, uint32_t rows,
+                                 uint32_t width, uint32_t op, unsigned long long* first_bad, cudaStream_t stream) {
+  if (rows == 0 || width == 0) return cudaSuccess;
+  if (op != kSum && op != kMax && op != kSoftmax) return cudaErrorInvalidValue;
+  const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>((rows + 127) / 128, 148ull * 8));
+  check_expected_kernel<<<grid, 128, 0, stream>>>(in, expected, rows, width, op);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  check_compare_kernel<<<148 * 8, 256, 0, stream>>>(expected, actual, rows, width, op, first_bad);
+  return cudaGetLastError();
 }
 
 }  // namespace oct

@@ -72,8 +72,32 @@ struct AsyncTask {
   uint32_t m = 0, n = 0, k = 0;
   int final_detail = 0;
   uint32_t final_stage = 0;
-  cudaEvent_t done = nullptr;
+  cudaEvent_t begin = nullptr, done = nullptr;  // bracket the task's work on the handle's stream
   DevBuf a, b, c;
+  // diagnostics (prometheus_reactor_runtime_sgemm_async_diagnostics)
+  uint32_t generation = 0;       // submissions through this slot
+  uint64_t sequence = 0;         // handle-wide submission sequence number
+  bool abandoned = false;
+  bool timed = false;
+  uint64_t gpu_ns = 0;
+};
+
+// Lifecycle counters of the async queue.
+struct AsyncStats {
+  uint64_t submitted = 0, ready = 0, failed = 0, consumed = 0, abandoned = 0;
+  uint64_t queue_full = 0, stale_ids = 0, polls = 0, reaped = 0, sequence = 0;
+  uint32_t max_in_flight = 0;
+};
+
+// Counters of the reduction executor (prometheus_reactor_runtime_reduction_diagnostics).
+struct ReductionStats {
+  bool initialized = false;
+  uint32_t ring_depth = 0;  // as configured (Go passes 3); one CUDA stream serves every request
+  uint64_t total = 0, success = 0, failures = 0, command_records = 0, submits = 0;
+  uint64_t allocations = 0, reuses = 0;
+  uint64_t last_replay = 0, last_gpu_ns = 0, last_e2e_ns = 0;
+  uint32_t last_stage_count = 0, slot_generation = 0;
+  int32_t last_detail = 0;
 };
 
 struct Runtime {
@@ -91,6 +115,8 @@ struct Runtime {
   DevBuf words;                 // [0] kernel error bits (u32), [8] first non-finite index (u64)
   AsyncTask tasks[kAsyncSlots];
   int next_task_id = 1;
+  AsyncStats async_stats;
+  ReductionStats red_stats;
   // Optional per-launch kernel timing of the tensor-core SGEMM (events on the
   // launch stream): split pass and main kernel, summed on read.
   bool timing = false;

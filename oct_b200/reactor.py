@@ -283,6 +283,60 @@ class PrometheusGemma4E2BM1InputRmsNormResult(C.Structure):
     ]
 
 
+class PrometheusReductionDiagnostics(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in (
+        "struct_size", "initialized", "production_enabled", "experimental_enabled", "configured_ring_depth",
+        "physical_slot_count", "acquire_cursor", "outstanding_slots", "quarantined_slots")] + [
+        (n, C.c_uint64) for n in (
+            "next_logical_request_id", "total_requests", "successful_requests", "logical_failure_count",
+            "physical_recycle_count", "quarantine_count", "reap_count", "pipeline_create_count",
+            "descriptor_update_count", "command_record_count", "queue_submit_count", "buffer_allocation_count",
+            "buffer_reuse_count", "temporary_capacity_bytes", "last_replay_id", "last_gpu_duration_ns",
+            "last_end_to_end_ns")] + [
+        ("last_stage_count", C.c_uint32), ("last_physical_slot_id", C.c_uint32),
+        ("last_physical_slot_generation", C.c_uint32), ("last_detail_code", C.c_int32),
+        ("validation_enabled", C.c_uint32), ("validation_error_count", C.c_uint32)]
+
+
+class PrometheusReductionBenchmarkRequest(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("reduction", PrometheusReductionRequest),
+                ("warmup_iterations", C.c_uint32), ("measured_iterations", C.c_uint32)]
+
+
+class PrometheusReductionBenchmarkResult(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in (
+        "struct_size", "completed_iterations", "correctness_passed", "validation_passed", "device_lost",
+        "stage_count")] + [(n, C.c_uint64) for n in (
+            "temporary_bytes", "replay_id", "gpu_min_ns", "gpu_median_ns", "gpu_max_ns", "end_to_end_min_ns",
+            "end_to_end_median_ns", "end_to_end_max_ns")] + [
+        ("first_mismatch_row", C.c_uint32), ("first_mismatch_column", C.c_uint32), ("first_expected", C.c_float),
+        ("first_actual", C.c_float), ("first_absolute_error", C.c_float), ("first_relative_error", C.c_float),
+        ("detail_code", C.c_int32)]
+
+
+class PrometheusSgemmAsyncTaskDiagnostics(C.Structure):
+    _fields_ = [("task_id", C.c_int32), ("generation", C.c_uint32), ("lifecycle_state", C.c_uint32),
+                ("physical_slot_id", C.c_uint32), ("physical_slot_generation", C.c_uint32),
+                ("submission_sequence", C.c_uint64), ("timing_valid", C.c_uint32), ("gpu_duration_ns", C.c_uint64),
+                ("feedback_pending", C.c_uint32), ("feedback_committed", C.c_uint32), ("failure_detail", C.c_int32),
+                ("failure_class", C.c_uint32), ("abandoned", C.c_uint32), ("physical_slot_state", C.c_uint32),
+                ("quarantined", C.c_uint32), ("physical_completion_confirmed", C.c_uint32),
+                ("reap_pending", C.c_uint32), ("reap_completed", C.c_uint32)]
+
+
+class PrometheusSgemmAsyncDiagnostics(C.Structure):
+    _fields_ = [("task_capacity", C.c_uint32), ("active_task_count", C.c_uint32), ("submitted_count", C.c_uint32),
+                ("ready_count", C.c_uint32), ("failed_count", C.c_uint32), ("consumed_count", C.c_uint32),
+                ("abandoned_count", C.c_uint32), ("queue_full_count", C.c_uint64),
+                ("stale_id_rejection_count", C.c_uint64), ("max_in_flight", C.c_uint32),
+                ("feedback_pending_count", C.c_uint32), ("feedback_committed_count", C.c_uint64),
+                ("feedback_skipped_count", C.c_uint64), ("next_feedback_sequence", C.c_uint64),
+                ("quarantined_slot_count", C.c_uint32), ("quarantine_event_count", C.c_uint64),
+                ("reap_poll_count", C.c_uint64), ("reap_success_count", C.c_uint64), ("reap_wait_count", C.c_uint64),
+                ("reap_failure_count", C.c_uint64), ("max_quarantine_depth", C.c_uint32),
+                ("runtime_unsafe_to_reuse", C.c_uint32), ("tasks", PrometheusSgemmAsyncTaskDiagnostics * 4)]
+
+
 class PrometheusGemma4E2BM1RopeRequest(C.Structure):
     _fields_ = [
         ("struct_size", C.c_uint32),
@@ -420,6 +474,12 @@ SIGNATURES = {
         C.c_int, [C.POINTER(PrometheusReductionRequest), C.POINTER(PrometheusReductionPlan)]),
     "prometheus_reactor_runtime_reduction": (
         C.c_int, [_vp, C.POINTER(PrometheusReductionRequest), C.POINTER(PrometheusReductionExecutionResult)]),
+    "prometheus_reactor_runtime_reduction_diagnostics": (
+        C.c_int, [_vp, C.POINTER(PrometheusReductionDiagnostics)]),
+    "prometheus_reactor_runtime_reduction_benchmark": (
+        C.c_int, [_vp, C.POINTER(PrometheusReductionBenchmarkRequest), C.POINTER(PrometheusReductionBenchmarkResult)]),
+    "prometheus_reactor_runtime_sgemm_async_diagnostics": (
+        C.c_int, [_vp, C.POINTER(PrometheusSgemmAsyncDiagnostics)]),
     "prometheus_reactor_runtime_row_wise_softmax": (
         C.c_int, [_vp, C.POINTER(PrometheusRowWiseSoftmaxRequest), C.POINTER(PrometheusRowWiseSoftmaxResult)]),
     "prometheus_reactor_runtime_gemma4e2b_m1_input_rmsnorm": (

@@ -83,6 +83,17 @@ STRUCTS = {
     "PrometheusSgemmBatchEntry": R.PrometheusSgemmBatchEntry,
     "PrometheusSgemmResidentBenchmarkRequest": R.PrometheusSgemmResidentBenchmarkRequest,
     "PrometheusSgemmResidentBenchmarkResult": R.PrometheusSgemmResidentBenchmarkResult,
+    "PrometheusGemma4E2BM1RopeRequest": R.PrometheusGemma4E2BM1RopeRequest,
+    "PrometheusGemma4E2BM1RopeResult": R.PrometheusGemma4E2BM1RopeResult,
+    "PrometheusGemma4E2BM1HeadRmsNormRopeRequest": R.PrometheusGemma4E2BM1HeadRmsNormRopeRequest,
+    "PrometheusGemma4E2BM1HeadRmsNormRopeResult": R.PrometheusGemma4E2BM1HeadRmsNormRopeResult,
+    "PrometheusGemma4E2BM1AttentionScoresRequest": R.PrometheusGemma4E2BM1AttentionScoresRequest,
+    "PrometheusGemma4E2BM1AttentionScoresResult": R.PrometheusGemma4E2BM1AttentionScoresResult,
+    "PrometheusReductionDiagnostics": R.PrometheusReductionDiagnostics,
+    "PrometheusReductionBenchmarkRequest": R.PrometheusReductionBenchmarkRequest,
+    "PrometheusReductionBenchmarkResult": R.PrometheusReductionBenchmarkResult,
+    "PrometheusSgemmAsyncTaskDiagnostics": R.PrometheusSgemmAsyncTaskDiagnostics,
+    "PrometheusSgemmAsyncDiagnostics": R.PrometheusSgemmAsyncDiagnostics,
 }
 
 
@@ -104,6 +115,24 @@ def test_struct_layouts_match_the_c_header(tmp_path):
         assert int(got[cname]) == C.sizeof(py), cname
         for fname, *_ in py._fields_:
             assert int(got[f"{cname}.{fname}"]) == getattr(py, fname).offset, f"{cname}.{fname}"
+
+
+def test_struct_layouts_match_the_reference_header():
+    """Every struct this header shares with the reference's reactor_api.h has the
+    reference's field names, offsets and size (fixture: tests/golden/make_layouts.py,
+    measured by gcc on the reference header itself)."""
+    import json
+    import sys
+    sys.path.insert(0, str(REPO / "tests" / "golden"))
+    import make_layouts as ML
+    fixture = json.loads((REPO / "tests" / "golden" / "reference_layouts.json").read_text())["structs"]
+    ours = ML.parse_structs(HEADER.read_text())
+    assert len(fixture) >= 25
+    for name, ref in fixture.items():
+        assert name in ours, name
+        assert ours[name] == [f for f, _ in ref["fields"]], name
+    got = ML.measure(HEADER, {name: ours[name] for name in fixture})
+    assert got == fixture
 
 
 # ---- handle semantics without a device ------------------------------------------
@@ -356,3 +385,37 @@ def test_block_oracle_flops_match_baseline_accounting():
     d = OB.dit_config()
     assert OB.flops_per_forward(d, 2) == pytest.approx(8192 * (2 * 3072 * 9216 + 2 * 3072 * 3072 + 6 * 3072 * 8192)
                                                        + 4096 ** 2 * 24 * 512 * 2)
+
+
+def test_diagnostics_entries_without_a_device(lib):
+    """reactor_concept_reduction.cpp:96-110, reactor_sgemm.cpp:6371-6412,
+    reactor_vulkan_fused_reduction.c:1122-1145: null outputs, handles, request checks."""
+    assert lib.prometheus_reactor_runtime_reduction_diagnostics(None, None) == R.PROM_ERROR
+    d = R.PrometheusReductionDiagnostics()
+    assert lib.prometheus_reactor_runtime_reduction_diagnostics(None, C.byref(d)) == R.PROM_INVALID_HANDLE
+    a = R.PrometheusSgemmAsyncDiagnostics()
+    assert lib.prometheus_reactor_runtime_sgemm_async_diagnostics(None, C.byref(a)) == R.PROM_INVALID_HANDLE
+    cfg = R.PrometheusReactorConfig()
+    cfg.struct_size = C.sizeof(cfg)
+    cfg.test_flags = R.TESTCFG_FAIL_DEVICE_CREATE
+    cfg.reduction_ring_depth = 3
+    h = C.c_void_p()
+    assert lib.prometheus_reactor_runtime_create(C.byref(cfg), C.byref(h)) == R.PROM_OK
+    try:
+        assert lib.prometheus_reactor_runtime_reduction_diagnostics(h, C.byref(d)) == R.PROM_OK
+        assert (d.struct_size, d.initialized, d.configured_ring_depth, d.total_requests) == (C.sizeof(d), 0, 3, 0)
+        assert lib.prometheus_reactor_runtime_sgemm_async_diagnostics(h, C.byref(a)) == R.PROM_OK
+        assert (a.task_capacity, a.active_task_count, a.queue_full_count) == (4, 0, 0)
+        x = np.ones(8, np.float32)
+        y = np.empty(2, np.float32)
+        req = R.PrometheusReductionBenchmarkRequest()
+        req.struct_size = C.sizeof(req)
+        req.reduction = R.make_reduction_request(x, y, 2, 4, R.OP_SUM)
+        res = R.PrometheusReductionBenchmarkResult()
+        assert lib.prometheus_reactor_runtime_reduction_benchmark(h, C.byref(req), C.byref(res)) == R.PROM_ERROR
+        assert res.detail_code == -6801 and res.first_mismatch_row == 0xFFFFFFFF  # no measured iterations
+        req.measured_iterations = 3
+        assert lib.prometheus_reactor_runtime_reduction_benchmark(h, C.byref(req), C.byref(res)) == R.PROM_ERROR
+        assert res.detail_code == -6825 and res.completed_iterations == 0  # the device is unavailable
+    finally:
+        lib.prometheus_reactor_runtime_destroy(h)
