@@ -308,6 +308,17 @@ __global__ void ada_prep_kernel(float* __restrict__ ada, const float* __restrict
   }
 }
 
+// The unmodulated block (a context refiner): scales 1, gates 1, shifts 0, so the
+// fused norm / residual kernels compute norm(x) and x + y exactly.
+__global__ void ada_identity_kernel(float* __restrict__ ada, uint32_t d, uint32_t batch) {
+  const uint64_t total = static_cast<uint64_t>(batch) * 6 * d;
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t part = static_cast<uint32_t>(i % (6ull * d)) / d;
+    ada[i] = part < 4 ? 1.f : 0.f;
+  }
+}
+
 uint32_t grid_for(uint64_t work, uint32_t per_block) {
   const uint64_t g = (work + per_block - 1) / per_block;
   return static_cast<uint32_t>(g < 148ull * 32 ? (g == 0 ? 1 : g) : 148ull * 32);
@@ -655,8 +666,12 @@ int Block::build_rope_tables() {
     // frequency and angle, cos/sin of the fp32 angle in binary64, rounded to fp32.
     static const uint32_t axes[3] = {32, 48, 48};
     for (uint32_t p = 0; p < d.seq_len; ++p) {
-      const float coord[3] = {static_cast<float>(d.rope_frame), static_cast<float>(p / d.grid_w),
-                              static_cast<float>(p % d.grid_w)};
+      // image tokens: (frame, row, column) of a grid_w-wide grid
+      // (CanonicalImageTokenCoordinate, canonical_contract.go:53-64); caption / context
+      // tokens: (first frame + p, 0, 0) (contextRope, context_refiner_reference.go:151-174)
+      const float coord[3] = {static_cast<float>(d.rope_text ? d.rope_frame + p : d.rope_frame),
+                              d.rope_text ? 0.f : static_cast<float>(p / d.grid_w),
+                              d.rope_text ? 0.f : static_cast<float>(p % d.grid_w)};
       uint32_t pair = 0;
       for (int a = 0; a < 3; ++a)
         for (uint32_t q = 0; q < axes[a] / 2; ++q, ++pair) {
@@ -794,7 +809,8 @@ cudaError_t Block::attention(uint32_t batch, uint64_t ldq, uint32_t k_col, uint3
                              &pv);
 }
 
-int Block::forward(const float* x, float* y, uint32_t batch, const float* timesteps_host) {
+int Block::forward(const float* x, float* y, uint32_t batch, const float* timesteps_host,
+                   const float* temb_device) {
   const BlockDims& d = dims_;
   if (batch == 0 || batch > d.max_batch) return -1;
   const uint32_t T = batch * d.seq_len;
@@ -891,15 +907,25 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
     return ok() ? 0 : -4;
   }
   // ---- DiT
-  if (timesteps_host == nullptr) return -1;
-  e = cudaMemcpyAsync(tsteps_, timesteps_host, batch * sizeof(float), cudaMemcpyHostToDevice, stream_);
-  if (!ok()) return -4;
-  timestep_embed_kernel<<<batch, 128, 0, stream_>>>(tsteps_, temb_, batch);
-  if (!ok()) return -4;
-  e = sgemm_fma(temb_, 256, ada_w_, 6ull * d.hidden, ada_, 6ull * d.hidden, batch, 6 * d.hidden, 256, stream_);
-  if (!ok()) return -4;
-  ada_prep_kernel<<<grid_for(6ull * d.hidden * batch, NT), NT, 0, stream_>>>(ada_, ada_b_, d.hidden, batch);
-  if (!ok()) return -4;
+  if (d.unmodulated) {
+    ada_identity_kernel<<<grid_for(6ull * d.hidden * batch, NT), NT, 0, stream_>>>(ada_, d.hidden, batch);
+    if (!ok()) return -4;
+  } else {
+    if (temb_device != nullptr) {
+      e = cudaMemcpyAsync(temb_, temb_device, 256ull * batch * sizeof(float), cudaMemcpyDeviceToDevice, stream_);
+      if (!ok()) return -4;
+    } else {
+      if (timesteps_host == nullptr) return -1;
+      e = cudaMemcpyAsync(tsteps_, timesteps_host, batch * sizeof(float), cudaMemcpyHostToDevice, stream_);
+      if (!ok()) return -4;
+      timestep_embed_kernel<<<batch, 128, 0, stream_>>>(tsteps_, temb_, batch);
+      if (!ok()) return -4;
+    }
+    e = sgemm_fma(temb_, 256, ada_w_, 6ull * d.hidden, ada_, 6ull * d.hidden, batch, 6 * d.hidden, 256, stream_);
+    if (!ok()) return -4;
+    ada_prep_kernel<<<grid_for(6ull * d.hidden * batch, NT), NT, 0, stream_>>>(ada_, ada_b_, d.hidden, batch);
+    if (!ok()) return -4;
+  }
   const uint64_t ms = 6ull * d.hidden;
   float* scale_a = ada_;
   float* gate_a = ada_ + d.hidden;

@@ -29,6 +29,10 @@ struct BlockDims {
   float eps = 1e-6f, rope_base = 10000.f;
   uint32_t grid_w = 0, rope_frame = 0;
   uint32_t tp_rank = 0, tp_world = 1;
+  // DiT variants of the Z-Image executors: rope_text places token p at
+  // (rope_frame + p, 0, 0) (caption / context tokens) instead of the image grid;
+  // unmodulated runs the block with scale 1, gate 1 and no shift (no adaLN).
+  uint32_t rope_text = 0, unmodulated = 0;
 };
 
 struct NcclUniqueIdBytes {
@@ -50,7 +54,10 @@ class Block {
   int init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t stream);
   int set_weight(uint32_t slot, const float* src, uint64_t count, bool on_device);
   // y = block(x) for `batch` sequences of seq_len tokens (x, y: [batch*seq][hidden]).
-  int forward(const float* x, float* y, uint32_t batch, const float* timesteps_host);
+  // DiT: one timestep per item (host array, embedded sinusoidally on the device),
+  // or, with temb_device, the items' 256-d embeddings already on the device.
+  int forward(const float* x, float* y, uint32_t batch, const float* timesteps_host,
+              const float* temb_device = nullptr);
   void set_stream(cudaStream_t s) { stream_ = s; }
   cudaStream_t stream() const { return stream_; }
   unsigned int read_status();

@@ -35,4 +35,4 @@ def test_peer_wait_gives_up_and_reports_timeout(runtime):
 
 def test_wait_budget_is_validated(runtime):
     st = runtime.selftest_wait_timeout(10)
-    assert st.rc == R.PROM_ERROR and st.detail == R.PROM_ERROR
+    assert st.rc == R.PROM_ERROR and st.detail == R.DETAIL_INVALID_ARGUMENT
