@@ -948,6 +948,362 @@ PROM_REACTOR_API int prometheus_reactor_runtime_gemma4e2b_m1_attention_scores(
     void* handle, const PrometheusGemma4E2BM1AttentionScoresRequest* request,
     PrometheusGemma4E2BM1AttentionScoresResult* out_result);
 
+/* ==== Z-Image model-block executors (reactor_api.h:666-1250, 2713-2784) ====
+   One closed model block per handle, as in the reference (one model_block
+   state per runtime, reactor_vulkan_model_block.c:1603-1780):
+     family 0, shader 23        the resident identity proof: output = input;
+     noise refiner (family 1)   Z-Image Turbo noise_refiner.{0,1}: BF16 image
+                                tokens [1024][3840] and a BF16 256-d timestep
+                                embedding in, the FP32 block output resident;
+     context refiner (family 2) context_refiner.{0,1}: FP32 caption tokens
+                                [32][3840], unmodulated, output resident.
+   Weights are uploaded as the reference's cache payloads: IEEE binary16, linear
+   weights row-major [in][out], in the cache manifest's lexical order (the byte
+   counts below).  The block runs on the library's DiT block (tcgen05 3xTF32
+   products, fused attention, fused norm / modulation / gated residuals); the
+   FP16 weights are widened exactly to fp32 and held pre-split for the tensor
+   cores, so a block holds about four times the declared weight bytes on the
+   device.  The staged M1B / M1C / M1D audit executes, static audits, the
+   30-layer main transformer and compiled-model sessions are not provided. */
+#define PROM_MODEL_BLOCK_MAX_WEIGHTS 13u
+#define PROM_MODEL_BLOCK_MAX_STEPS 7u
+#define PROM_MODEL_BLOCK_MAX_AUDIT_POINTS 1u
+#define PROM_MODEL_BLOCK_M1B_PIPELINE_COUNT 6u
+#define PROM_MODEL_BLOCK_MAIN_STAGE_COUNT 13u
+
+enum {
+  PROM_MODEL_BLOCK_STEP_BIND_PIPELINE = 1u,
+  PROM_MODEL_BLOCK_STEP_BIND_RESOURCES = 2u,
+  PROM_MODEL_BLOCK_STEP_PUSH_CONSTANTS = 3u,
+  PROM_MODEL_BLOCK_STEP_DISPATCH = 4u,
+  PROM_MODEL_BLOCK_STEP_BARRIER = 5u,
+  PROM_MODEL_BLOCK_STEP_AUDIT_COPY = 6u,
+  PROM_MODEL_BLOCK_STEP_OUTPUT_COPY = 7u,
+};
+
+enum {
+  PROM_MODEL_BLOCK_DETAIL_INVALID_REQUEST = -6901,
+  PROM_MODEL_BLOCK_DETAIL_NOT_FOUND = -6902,
+  PROM_MODEL_BLOCK_DETAIL_ALREADY_CREATED = -6903,
+  PROM_MODEL_BLOCK_DETAIL_WEIGHT_MISMATCH = -6904,
+  PROM_MODEL_BLOCK_DETAIL_RESOURCE_CREATE_FAILED = -6905,
+  PROM_MODEL_BLOCK_DETAIL_PIPELINE_CREATE_FAILED = -6906,
+  PROM_MODEL_BLOCK_DETAIL_UPLOAD_FAILED = -6907,
+  PROM_MODEL_BLOCK_DETAIL_COMMAND_RECORD_FAILED = -6908,
+  PROM_MODEL_BLOCK_DETAIL_QUEUE_SUBMIT_FAILED = -6909,
+  PROM_MODEL_BLOCK_DETAIL_COMPLETION_UNCERTAIN = -6910,
+  PROM_MODEL_BLOCK_DETAIL_AUDIT_FAILED = -6911,
+  PROM_MODEL_BLOCK_DETAIL_STALE_OUTPUT = -6912,
+  PROM_MODEL_BLOCK_DETAIL_INGRESS_PIPELINE_CREATE_FAILED = -6913,
+  PROM_MODEL_BLOCK_DETAIL_INGRESS_DISPATCH_FAILED = -6914,
+  PROM_MODEL_BLOCK_DETAIL_INGRESS_AUDIT_MISMATCH = -6915,
+  PROM_MODEL_BLOCK_DETAIL_INGRESS_INPUT_SIZE_MISMATCH = -6916,
+  PROM_MODEL_BLOCK_DETAIL_INGRESS_TIMESTEP_SIZE_MISMATCH = -6917,
+  PROM_MODEL_BLOCK_DETAIL_M1C_SOFTMAX_INVALID = -6918,
+  PROM_MODEL_BLOCK_DETAIL_M1D_NONFINITE = -6919,
+  PROM_MODEL_BLOCK_DETAIL_PARAMETER_SET_MISMATCH = -6920,
+  PROM_MODEL_BLOCK_DETAIL_REBIND_FAILED = -6921,
+  PROM_MODEL_BLOCK_DETAIL_DESCRIPTOR_UPDATE_FAILED = -6922,
+};
+
+enum {
+  PROM_NOISE_REFINER_FAMILY_Z_IMAGE_TURBO = 1u,
+  PROM_NOISE_REFINER_PARAMETER_SET_0 = 1u,
+  PROM_NOISE_REFINER_PARAMETER_SET_1 = 2u,
+  PROM_CONTEXT_REFINER_FAMILY_Z_IMAGE_TURBO = 2u,
+  PROM_CONTEXT_REFINER_PARAMETER_SET_0 = 1u,
+  PROM_CONTEXT_REFINER_PARAMETER_SET_1 = 2u,
+  PROM_MAIN_TRANSFORMER_FAMILY_Z_IMAGE_TURBO = 3u,
+  PROM_MAIN_TRANSFORMER_PARAMETER_SET_0 = 1u,
+};
+
+enum {
+  PROM_NOISE_REFINER_BINDING_BOUND = 1u,
+  PROM_NOISE_REFINER_BINDING_VALIDATING = 2u,
+  PROM_NOISE_REFINER_BINDING_UPLOADING = 3u,
+  PROM_NOISE_REFINER_BINDING_UPDATING_DESCRIPTORS = 4u,
+  PROM_NOISE_REFINER_BINDING_READY_TO_COMMIT = 5u,
+  PROM_NOISE_REFINER_BINDING_COMMITTED = 6u,
+  PROM_NOISE_REFINER_BINDING_FAILED_BEFORE_COMMIT = 7u,
+  PROM_NOISE_REFINER_BINDING_COMPLETION_UNCERTAIN = 8u,
+  PROM_NOISE_REFINER_BINDING_QUARANTINED = 9u,
+};
+
+enum {
+  PROM_NOISE_REFINER_AUDIT_NONE = 0u,
+  PROM_NOISE_REFINER_AUDIT_M1B = 1u,
+  PROM_NOISE_REFINER_AUDIT_M1C = 2u,
+  PROM_NOISE_REFINER_AUDIT_M1D = 3u,
+};
+
+/* The Z-Image Turbo model lock's identities the closed families are checked
+   against (internal/prometheus/models/zimage-turbo/resolved_descriptor.h:5-15,
+   resolved_audit_schedule.h:6). */
+#define OCT_B200_ZIMAGE_TURBO_LOCK_ID 0x71ef202b4e34b562ull
+#define OCT_B200_ZIMAGE_NOISE_REFINER0_AGGREGATE 0xa1ba526898a2a752ull
+#define OCT_B200_ZIMAGE_NOISE_REFINER1_AGGREGATE 0x80c0cd75f44cc434ull
+#define OCT_B200_ZIMAGE_CONTEXT_REFINER0_AGGREGATE 0xc08b908a921a80e1ull
+#define OCT_B200_ZIMAGE_CONTEXT_REFINER1_AGGREGATE 0x30268c3b0d7a6fafull
+#define OCT_B200_ZIMAGE_CONTEXT_MEMORY_PLAN_BYTES 536870912ull
+#define OCT_B200_ZIMAGE_AUDIT_ARENA_BYTES 47186176u
+
+typedef struct PrometheusModelBlockWeightDeclaration {
+  uint64_t content_identity;
+  uint64_t layout_identity;
+  uint64_t byte_count;
+} PrometheusModelBlockWeightDeclaration;
+
+typedef struct PrometheusModelBlockCreateRequest {
+  uint32_t struct_size;
+  uint32_t assembly_family;
+  uint32_t parameter_set;
+  uint64_t parameter_set_aggregate_identity;
+  uint64_t model_contract_identity;
+  uint64_t weight_identity;
+  uint64_t shader_portfolio_identity;
+  uint64_t precision_policy_identity;
+  uint64_t capability_route_identity;
+  uint64_t memory_ceiling_bytes;
+  uint64_t external_input_bytes;
+  uint64_t external_output_bytes;
+  uint64_t audit_bytes;
+  uint32_t shader_id;
+  uint32_t weight_count;
+  PrometheusModelBlockWeightDeclaration weights[PROM_MODEL_BLOCK_MAX_WEIGHTS];
+  uint32_t step_count;
+  uint32_t steps[PROM_MODEL_BLOCK_MAX_STEPS];
+} PrometheusModelBlockCreateRequest;
+
+typedef struct PrometheusModelBlockWeightUpload {
+  uint32_t binding_index;
+  const void* bytes;
+  uint64_t byte_count;
+  uint64_t content_identity;
+  uint64_t layout_identity;
+} PrometheusModelBlockWeightUpload;
+
+typedef struct PrometheusNoiseRefinerRebindRequest {
+  uint32_t struct_size;
+  uint32_t model_local_block_id;
+  uint64_t lock_identity;
+  uint32_t upload_count;
+  const PrometheusModelBlockWeightUpload* uploads;
+} PrometheusNoiseRefinerRebindRequest;
+
+typedef struct PrometheusContextRefinerCreateRequest {
+  uint32_t struct_size;
+  uint32_t model_local_block_id;
+  uint64_t lock_identity;
+  uint32_t upload_count;
+  const PrometheusModelBlockWeightUpload* uploads;
+} PrometheusContextRefinerCreateRequest;
+
+typedef PrometheusContextRefinerCreateRequest PrometheusContextRefinerRebindRequest;
+
+typedef struct PrometheusModelBlockExecuteRequest {
+  uint32_t struct_size;
+  const float* input;
+  float* output;
+  uint64_t element_count;
+  uint64_t input_identity;
+  uint32_t audit_enabled;
+  float* audit_output;
+  uint64_t audit_element_capacity;
+} PrometheusModelBlockExecuteRequest;
+
+typedef struct PrometheusNoiseRefiner0ExecuteRequest {
+  uint32_t struct_size;
+  const void* model_input_bf16;
+  const void* timestep_bf16;
+  uint64_t model_input_bytes;
+  uint64_t timestep_bytes;
+  uint64_t input_identity;
+  uint64_t timestep_identity;
+  uint64_t output_identity;
+  uint32_t audit_enabled;
+} PrometheusNoiseRefiner0ExecuteRequest;
+
+typedef PrometheusNoiseRefiner0ExecuteRequest PrometheusNoiseRefiner1ExecuteRequest;
+
+typedef struct PrometheusNoiseRefinerResidentExecuteRequest {
+  uint32_t struct_size;
+  uint64_t input_generation;
+  uint64_t output_identity;
+  uint32_t audit_enabled;
+  uint32_t audit_family;
+  uint32_t audit_stage;
+  float* audit_output;
+  uint64_t audit_element_capacity;
+} PrometheusNoiseRefinerResidentExecuteRequest;
+
+typedef struct PrometheusContextRefiner0ExecuteRequest {
+  uint32_t struct_size;
+  const float* context_input;
+  uint64_t context_input_bytes;
+  uint64_t input_identity;
+  uint64_t output_identity;
+  uint32_t audit_enabled;
+} PrometheusContextRefiner0ExecuteRequest;
+
+typedef struct PrometheusContextRefinerResidentExecuteRequest {
+  uint32_t struct_size;
+  uint64_t input_generation;
+  uint64_t output_identity;
+  uint32_t audit_enabled;
+} PrometheusContextRefinerResidentExecuteRequest;
+
+typedef struct PrometheusNoiseRefinerFinalAuditRequest {
+  uint32_t struct_size;
+  uint64_t required_output_generation;
+  uint64_t output_identity;
+  float* output;
+  uint64_t output_element_capacity;
+} PrometheusNoiseRefinerFinalAuditRequest;
+
+typedef PrometheusNoiseRefinerFinalAuditRequest PrometheusContextRefinerFinalAuditRequest;
+
+/* Evidence of the model block (reactor_api.h:1105-1183).  CUDA meaning of the
+   counters: a "pipeline" is a kernel the block launches, a "queue submit" one
+   enqueued forward; the vk_* counters stay 0. */
+typedef struct PrometheusModelBlockEvidence {
+  uint32_t struct_size;
+  int32_t detail_code;
+  uint32_t created;
+  uint32_t weights_uploaded;
+  uint32_t quarantined;
+  uint32_t output_valid;
+  uint32_t audit_valid;
+  uint32_t fixed_step_count;
+  uint32_t weight_count;
+  uint64_t persistent_bytes;
+  uint64_t reusable_bytes;
+  uint64_t audit_bytes;
+  uint64_t external_bytes;
+  uint64_t total_committed_bytes;
+  uint64_t peak_plan_bytes;
+  uint64_t cold_buffer_allocation_count;
+  uint64_t warm_buffer_allocation_count;
+  uint64_t pipeline_create_count;
+  uint64_t descriptor_set_count;
+  uint64_t weight_upload_count;
+  uint64_t execution_count;
+  uint64_t last_execution_ns;
+  uint64_t execution_plan_identity;
+  uint64_t replay_identity;
+  uint32_t assembly_family;
+  uint32_t parameter_set;
+  uint32_t binding_state;
+  uint32_t active_weight_window;
+  uint64_t parameter_set_aggregate_identity;
+  uint64_t binding_generation;
+  uint64_t output_generation;
+  uint64_t descriptor_generation;
+  uint64_t m1b_boundary_gpu_ns[PROM_MODEL_BLOCK_M1B_PIPELINE_COUNT];
+  uint64_t gpu_total_begin_tick;
+  uint64_t gpu_total_end_tick;
+  uint64_t gpu_total_ns;
+  uint64_t gpu_compute_begin_tick;
+  uint64_t gpu_compute_end_tick;
+  uint64_t gpu_compute_ns;
+  uint64_t gpu_ingress_transfer_ns;
+  uint64_t gpu_joint_copy_ns;
+  uint64_t gpu_readback_ns;
+  uint64_t main_stage_gpu_begin_tick[PROM_MODEL_BLOCK_MAIN_STAGE_COUNT];
+  uint64_t main_stage_gpu_end_tick[PROM_MODEL_BLOCK_MAIN_STAGE_COUNT];
+  uint64_t main_stage_gpu_ns[PROM_MODEL_BLOCK_MAIN_STAGE_COUNT];
+  uint64_t last_active_target_validation_ns;
+  uint64_t last_command_reset_ns;
+  uint64_t last_command_begin_ns;
+  uint64_t last_command_record_ns;
+  uint64_t last_command_end_ns;
+  uint64_t last_queue_submit_ns;
+  uint64_t last_fence_wait_ns;
+  uint64_t last_descriptor_update_ns;
+  uint64_t last_staging_memcpy_ns;
+  uint64_t last_output_readback_ns;
+  uint64_t vk_create_buffer_count;
+  uint64_t vk_destroy_buffer_count;
+  uint64_t vk_allocate_memory_count;
+  uint64_t vk_free_memory_count;
+  uint64_t vk_create_shader_module_count;
+  uint64_t vk_destroy_shader_module_count;
+  uint64_t vk_create_compute_pipelines_count;
+  uint64_t vk_allocate_descriptor_sets_count;
+  uint64_t vk_update_descriptor_sets_count;
+  uint64_t vk_create_command_pool_count;
+  uint64_t vk_allocate_command_buffers_count;
+  uint64_t vk_reset_command_buffer_count;
+  uint64_t vk_queue_submit_count;
+  uint64_t vk_fence_wait_count;
+  uint64_t vk_timeline_wait_count;
+  uint64_t vk_map_memory_count;
+  uint64_t vk_unmap_memory_count;
+  uint64_t vk_flush_count;
+  uint64_t vk_invalidate_count;
+  uint64_t m6a_activation_pack_gpu_ns;
+  uint64_t m6a_cooperative_execute_gpu_ns;
+  uint64_t m6a_w3_segment_repack_gpu_ns;
+} PrometheusModelBlockEvidence;
+
+/* reactor_api.h:2713-2715 -- create the handle's one model block
+   (validation: reactor_vulkan_model_block.c:393-477). */
+PROM_REACTOR_API int prometheus_reactor_runtime_model_block_create(
+    void* handle, const PrometheusModelBlockCreateRequest* request, uint64_t* out_block_id,
+    PrometheusModelBlockEvidence* out_evidence);
+/* reactor_api.h:2716-2718 -- the declared weights, once, in binding order (:1781-1829). */
+PROM_REACTOR_API int prometheus_reactor_runtime_model_block_upload_weights(
+    void* handle, uint64_t block_id, const PrometheusModelBlockWeightUpload* uploads, uint32_t upload_count,
+    PrometheusModelBlockEvidence* out_evidence);
+/* reactor_api.h:2719-2721 -- the family-0 resident identity block: output = input,
+   audit = the first audit elements (:1884-1953; resident_identity.sdslv). */
+PROM_REACTOR_API int prometheus_reactor_runtime_model_block_execute(
+    void* handle, uint64_t block_id, const PrometheusModelBlockExecuteRequest* request,
+    PrometheusModelBlockEvidence* out_evidence);
+/* reactor_api.h:2731-2736 -- noise_refiner.0 / .1 from external BF16 ingress;
+   the FP32 output stays resident (:2204-2303; runCanonicalNoiseRefiner0,
+   canonical_reference.go:315-480).  audit_enabled must be 0. */
+PROM_REACTOR_API int prometheus_reactor_runtime_noise_refiner0_execute(
+    void* handle, uint64_t block_id, const PrometheusNoiseRefiner0ExecuteRequest* request,
+    PrometheusModelBlockEvidence* out_evidence);
+PROM_REACTOR_API int prometheus_reactor_runtime_noise_refiner1_execute(
+    void* handle, uint64_t block_id, const PrometheusNoiseRefiner1ExecuteRequest* request,
+    PrometheusModelBlockEvidence* out_evidence);
+/* reactor_api.h:2737-2739 -- replace block 0's weights with block 1's (:1831-1882). */
+PROM_REACTOR_API int prometheus_reactor_runtime_noise_refiner_rebind(
+    void* handle, uint64_t block_id, const PrometheusNoiseRefinerRebindRequest* request,
+    PrometheusModelBlockEvidence* out_evidence);
+/* reactor_api.h:2740-2742 -- noise_refiner.1 on the resident predecessor output
+   (:3274-3396).  Only audit_enabled = 0 is provided. */
+PROM_REACTOR_API int prometheus_reactor_runtime_noise_refiner_execute_resident(
+    void* handle, uint64_t block_id, const PrometheusNoiseRefinerResidentExecuteRequest* request,
+    PrometheusModelBlockEvidence* out_evidence);
+/* reactor_api.h:2746-2748 -- read back the resident final output (:3402-3459). */
+PROM_REACTOR_API int prometheus_reactor_runtime_noise_refiner_audit_final(
+    void* handle, uint64_t block_id, const PrometheusNoiseRefinerFinalAuditRequest* request,
+    PrometheusModelBlockEvidence* out_evidence);
+/* reactor_api.h:2749-2763 -- the context refiner family: create (+ upload), rebind
+   to block 1, execute on FP32 ingress or on the resident output, read back
+   (reactor_vulkan_model_block.c:2305-2367, 2464-2669). */
+PROM_REACTOR_API int prometheus_reactor_runtime_context_refiner_create(
+    void* handle, const PrometheusContextRefinerCreateRequest* request, uint64_t* out_block_id,
+    PrometheusModelBlockEvidence* out_evidence);
+PROM_REACTOR_API int prometheus_reactor_runtime_context_refiner_rebind(
+    void* handle, uint64_t block_id, const PrometheusContextRefinerRebindRequest* request,
+    PrometheusModelBlockEvidence* out_evidence);
+PROM_REACTOR_API int prometheus_reactor_runtime_context_refiner0_execute(
+    void* handle, uint64_t block_id, const PrometheusContextRefiner0ExecuteRequest* request,
+    PrometheusModelBlockEvidence* out_evidence);
+PROM_REACTOR_API int prometheus_reactor_runtime_context_refiner_execute_resident(
+    void* handle, uint64_t block_id, const PrometheusContextRefinerResidentExecuteRequest* request,
+    PrometheusModelBlockEvidence* out_evidence);
+PROM_REACTOR_API int prometheus_reactor_runtime_context_refiner_audit_final(
+    void* handle, uint64_t block_id, const PrometheusContextRefinerFinalAuditRequest* request,
+    PrometheusModelBlockEvidence* out_evidence);
+/* reactor_api.h:2776-2779 -- evidence and teardown (:3503-3522). */
+PROM_REACTOR_API int prometheus_reactor_runtime_model_block_get_evidence(void* handle, uint64_t block_id,
+                                                                         PrometheusModelBlockEvidence* out_evidence);
+PROM_REACTOR_API int prometheus_reactor_runtime_model_block_destroy(void* handle, uint64_t block_id);
+
 /* reactor_api.h:2823-2826 -- aliases kept by the reference for older drafts. */
 PROM_REACTOR_API int prometheus_runtime_create(void* config, void** out_handle);
 PROM_REACTOR_API int prometheus_runtime_destroy(void* handle);

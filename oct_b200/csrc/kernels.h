@@ -199,6 +199,14 @@ cudaError_t rmsnorm(const float* in, uint64_t in_stride, const float* weight, fl
 cudaError_t reduction_self_check(const float* in, const float* actual, float* expected, uint32_t rows,
                                  uint32_t width, uint32_t op, unsigned long long* first_bad, cudaStream_t stream);
 
+// ---------------------------------------------------------------- Z-Image ingress (zimage.cu)
+// BF16 values (the high half of a binary32) and binary16 values widened exactly
+// to fp32; widen_f16 writes a [rows][cols] source at column col0 of a dst with
+// leading dimension ld.
+cudaError_t widen_bf16(const void* src, float* dst, uint64_t n, cudaStream_t stream);
+cudaError_t widen_f16(const void* src, uint32_t rows, uint32_t cols, float* dst, uint64_t ld, uint32_t col0,
+                      cudaStream_t stream);
+
 // ---------------------------------------------------------------- Gemma M1 boundary (gemma_m1.cu)
 // BF16 storage rounding as the reference's M1 entry points apply it; inputs
 // must already be checked finite.  Head widths are even and <= kM1MaxHeadWidth.

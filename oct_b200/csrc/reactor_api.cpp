@@ -186,6 +186,7 @@ void destroy_runtime(Runtime* rt) {
   if (rt->stream != nullptr) cudaStreamSynchronize(rt->stream);
   for (auto& kv : rt->blocks) delete kv.second;
   rt->blocks.clear();
+  destroy_model_block(rt);
   for (auto& ev : rt->timing_events) {
     cudaEventSynchronize(ev.main_end);
     cudaEventDestroy(ev.split_begin);

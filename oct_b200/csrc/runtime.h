@@ -140,6 +140,9 @@ struct Runtime {
   uint64_t m46_allocations = 0;   // staging (re)allocations made by the RMSNorm entries
   DevBuf m1_cos, m1_sin, m1_q, m1_k, m1_scores;
   uint32_t m1_slot_generation[3] = {0, 0, 0};  // writes of the Q, K and score slots
+  // The handle's one Z-Image model block (zimage_api.cpp), or null.
+  struct ModelBlockState* model_block = nullptr;
+  uint64_t next_model_block_id = 1;
 
   unsigned int* err_word() { return static_cast<unsigned int*>(words.aligned()); }
   unsigned long long* nonfinite_word() {
@@ -147,6 +150,10 @@ struct Runtime {
   }
 };
 
+
+struct ModelBlockState;
+// Releases the handle's model block (zimage_api.cpp); the handle's stream is idle.
+void destroy_model_block(Runtime* rt);
 
 // The live handle behind `handle`, or null when it is not one (locked registry).
 Runtime* lookup(void* handle);

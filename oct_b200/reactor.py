@@ -422,6 +422,108 @@ class PrometheusGemma4E2BM1AttentionScoresResult(C.Structure):
     ]
 
 
+MODEL_BLOCK_MAX_WEIGHTS, MODEL_BLOCK_MAX_STEPS = 13, 7
+NOISE_REFINER_FAMILY, CONTEXT_REFINER_FAMILY = 1, 2
+ZIMAGE_LOCK_ID = 0x71ef202b4e34b562
+ZIMAGE_NOISE_AGGREGATES = (0xa1ba526898a2a752, 0x80c0cd75f44cc434)
+ZIMAGE_AUDIT_ARENA_BYTES = 47186176
+MB_INVALID_REQUEST, MB_NOT_FOUND, MB_ALREADY_CREATED, MB_WEIGHT_MISMATCH = -6901, -6902, -6903, -6904
+MB_RESOURCE_CREATE_FAILED, MB_AUDIT_FAILED, MB_STALE_OUTPUT = -6905, -6911, -6912
+MB_PARAMETER_SET_MISMATCH, MB_REBIND_FAILED = -6920, -6921
+
+
+class PrometheusModelBlockWeightDeclaration(C.Structure):
+    _fields_ = [("content_identity", C.c_uint64), ("layout_identity", C.c_uint64), ("byte_count", C.c_uint64)]
+
+
+class PrometheusModelBlockCreateRequest(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("assembly_family", C.c_uint32), ("parameter_set", C.c_uint32)] + [
+        (n, C.c_uint64) for n in ("parameter_set_aggregate_identity", "model_contract_identity", "weight_identity",
+                                  "shader_portfolio_identity", "precision_policy_identity",
+                                  "capability_route_identity", "memory_ceiling_bytes", "external_input_bytes",
+                                  "external_output_bytes", "audit_bytes")] + [
+        ("shader_id", C.c_uint32), ("weight_count", C.c_uint32),
+        ("weights", PrometheusModelBlockWeightDeclaration * MODEL_BLOCK_MAX_WEIGHTS),
+        ("step_count", C.c_uint32), ("steps", C.c_uint32 * MODEL_BLOCK_MAX_STEPS)]
+
+
+class PrometheusModelBlockWeightUpload(C.Structure):
+    _fields_ = [("binding_index", C.c_uint32), ("bytes", C.c_void_p), ("byte_count", C.c_uint64),
+                ("content_identity", C.c_uint64), ("layout_identity", C.c_uint64)]
+
+
+class PrometheusNoiseRefinerRebindRequest(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("model_local_block_id", C.c_uint32), ("lock_identity", C.c_uint64),
+                ("upload_count", C.c_uint32), ("uploads", C.POINTER(PrometheusModelBlockWeightUpload))]
+
+
+PrometheusContextRefinerCreateRequest = PrometheusNoiseRefinerRebindRequest  # same layout (reactor_api.h:842-848)
+
+
+class PrometheusModelBlockExecuteRequest(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("input", C.c_void_p), ("output", C.c_void_p),
+                ("element_count", C.c_uint64), ("input_identity", C.c_uint64), ("audit_enabled", C.c_uint32),
+                ("audit_output", C.c_void_p), ("audit_element_capacity", C.c_uint64)]
+
+
+class PrometheusNoiseRefiner0ExecuteRequest(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("model_input_bf16", C.c_void_p), ("timestep_bf16", C.c_void_p),
+                ("model_input_bytes", C.c_uint64), ("timestep_bytes", C.c_uint64), ("input_identity", C.c_uint64),
+                ("timestep_identity", C.c_uint64), ("output_identity", C.c_uint64), ("audit_enabled", C.c_uint32)]
+
+
+class PrometheusNoiseRefinerResidentExecuteRequest(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("input_generation", C.c_uint64), ("output_identity", C.c_uint64),
+                ("audit_enabled", C.c_uint32), ("audit_family", C.c_uint32), ("audit_stage", C.c_uint32),
+                ("audit_output", C.c_void_p), ("audit_element_capacity", C.c_uint64)]
+
+
+class PrometheusContextRefiner0ExecuteRequest(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("context_input", C.c_void_p), ("context_input_bytes", C.c_uint64),
+                ("input_identity", C.c_uint64), ("output_identity", C.c_uint64), ("audit_enabled", C.c_uint32)]
+
+
+class PrometheusContextRefinerResidentExecuteRequest(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("input_generation", C.c_uint64), ("output_identity", C.c_uint64),
+                ("audit_enabled", C.c_uint32)]
+
+
+class PrometheusNoiseRefinerFinalAuditRequest(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("required_output_generation", C.c_uint64),
+                ("output_identity", C.c_uint64), ("output", C.c_void_p), ("output_element_capacity", C.c_uint64)]
+
+
+class PrometheusModelBlockEvidence(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("struct_size",)] + [("detail_code", C.c_int32)] + [
+        (n, C.c_uint32) for n in ("created", "weights_uploaded", "quarantined", "output_valid", "audit_valid",
+                                  "fixed_step_count", "weight_count")] + [
+        (n, C.c_uint64) for n in ("persistent_bytes", "reusable_bytes", "audit_bytes", "external_bytes",
+                                  "total_committed_bytes", "peak_plan_bytes", "cold_buffer_allocation_count",
+                                  "warm_buffer_allocation_count", "pipeline_create_count", "descriptor_set_count",
+                                  "weight_upload_count", "execution_count", "last_execution_ns",
+                                  "execution_plan_identity", "replay_identity")] + [
+        (n, C.c_uint32) for n in ("assembly_family", "parameter_set", "binding_state", "active_weight_window")] + [
+        (n, C.c_uint64) for n in ("parameter_set_aggregate_identity", "binding_generation", "output_generation",
+                                  "descriptor_generation")] + [
+        ("m1b_boundary_gpu_ns", C.c_uint64 * 6)] + [
+        (n, C.c_uint64) for n in ("gpu_total_begin_tick", "gpu_total_end_tick", "gpu_total_ns",
+                                  "gpu_compute_begin_tick", "gpu_compute_end_tick", "gpu_compute_ns",
+                                  "gpu_ingress_transfer_ns", "gpu_joint_copy_ns", "gpu_readback_ns")] + [
+        ("main_stage_gpu_begin_tick", C.c_uint64 * 13), ("main_stage_gpu_end_tick", C.c_uint64 * 13),
+        ("main_stage_gpu_ns", C.c_uint64 * 13)] + [
+        (n, C.c_uint64) for n in (
+            "last_active_target_validation_ns", "last_command_reset_ns", "last_command_begin_ns",
+            "last_command_record_ns", "last_command_end_ns", "last_queue_submit_ns", "last_fence_wait_ns",
+            "last_descriptor_update_ns", "last_staging_memcpy_ns", "last_output_readback_ns",
+            "vk_create_buffer_count", "vk_destroy_buffer_count", "vk_allocate_memory_count", "vk_free_memory_count",
+            "vk_create_shader_module_count", "vk_destroy_shader_module_count", "vk_create_compute_pipelines_count",
+            "vk_allocate_descriptor_sets_count", "vk_update_descriptor_sets_count", "vk_create_command_pool_count",
+            "vk_allocate_command_buffers_count", "vk_reset_command_buffer_count", "vk_queue_submit_count",
+            "vk_fence_wait_count", "vk_timeline_wait_count", "vk_map_memory_count", "vk_unmap_memory_count",
+            "vk_flush_count", "vk_invalidate_count", "m6a_activation_pack_gpu_ns", "m6a_cooperative_execute_gpu_ns",
+            "m6a_w3_segment_repack_gpu_ns")]
+
+
 class OctB200BlockConfig(C.Structure):
     _fields_ = [
         ("struct_size", C.c_uint32),
@@ -499,6 +601,34 @@ SIGNATURES = {
     "prometheus_reactor_runtime_gemma4e2b_m1_attention_scores": (
         C.c_int, [_vp, C.POINTER(PrometheusGemma4E2BM1AttentionScoresRequest),
                   C.POINTER(PrometheusGemma4E2BM1AttentionScoresResult)]),
+    "prometheus_reactor_runtime_model_block_create": (
+        C.c_int, [_vp, C.POINTER(PrometheusModelBlockCreateRequest), C.POINTER(C.c_uint64), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_model_block_upload_weights": (
+        C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusModelBlockWeightUpload), _u32, C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_model_block_execute": (
+        C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusModelBlockExecuteRequest), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_noise_refiner0_execute": (
+        C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusNoiseRefiner0ExecuteRequest), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_noise_refiner1_execute": (
+        C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusNoiseRefiner0ExecuteRequest), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_noise_refiner_rebind": (
+        C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusNoiseRefinerRebindRequest), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_noise_refiner_execute_resident": (
+        C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusNoiseRefinerResidentExecuteRequest), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_noise_refiner_audit_final": (
+        C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusNoiseRefinerFinalAuditRequest), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_context_refiner_create": (
+        C.c_int, [_vp, C.POINTER(PrometheusContextRefinerCreateRequest), C.POINTER(C.c_uint64), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_context_refiner_rebind": (
+        C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusContextRefinerCreateRequest), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_context_refiner0_execute": (
+        C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusContextRefiner0ExecuteRequest), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_context_refiner_execute_resident": (
+        C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusContextRefinerResidentExecuteRequest), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_context_refiner_audit_final": (
+        C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusNoiseRefinerFinalAuditRequest), C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_model_block_get_evidence": (C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusModelBlockEvidence)]),
+    "prometheus_reactor_runtime_model_block_destroy": (C.c_int, [_vp, C.c_uint64]),
     "prometheus_runtime_create": (C.c_int, [_vp, C.POINTER(C.c_void_p)]),
     "prometheus_runtime_destroy": (C.c_int, [_vp]),
     "prometheus_runtime_probe": (C.c_int, [_vp, C.POINTER(PrometheusCaps)]),
@@ -1076,3 +1206,141 @@ def reduction_plan(lib: C.CDLL, rows: int, width: int, operation: int, flags: in
     plan = PrometheusReductionPlan()
     rc = lib.prometheus_reactor_reduction_plan(C.byref(req), C.byref(plan))
     return rc, plan
+
+
+# ---- Z-Image model-block executors (reactor_api.h:2713-2784) --------------------------------
+def weight_uploads(payloads: list) -> tuple:
+    """PrometheusModelBlockWeightUpload[] for binary16 payloads in binding order; the
+    identities are FNV-1a of each payload's bytes and shape (any non-zero values serve)."""
+    arr = (PrometheusModelBlockWeightUpload * len(payloads))()
+    for i, p in enumerate(payloads):
+        p = np.ascontiguousarray(p)
+        arr[i].binding_index = i
+        arr[i].bytes = p.ctypes.data
+        arr[i].byte_count = p.nbytes
+        arr[i].content_identity = _fnv64(p.tobytes()[:4096]) ^ (i + 1)
+        arr[i].layout_identity = _fnv64(repr(p.shape).encode()) | 1
+    return arr
+
+
+def _fnv64(data: bytes) -> int:
+    h = 1469598103934665603
+    for b in data:
+        h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return h or 1
+
+
+class ModelBlock:
+    """The handle's one Z-Image model block, driven the way Go's compiled-model
+    adapter drives the reference (create -> upload -> execute -> audit / rebind)."""
+
+    def __init__(self, rt: "Runtime"):
+        self.rt = rt
+        self.lib = rt.lib
+        self.id = 0
+        self.evidence = PrometheusModelBlockEvidence()
+
+    def create_noise_refiner(self, payloads: list, parameter_set: int = 1,
+                             memory_ceiling: int = 1 << 31) -> tuple[int, PrometheusModelBlockEvidence]:
+        req = PrometheusModelBlockCreateRequest()
+        req.struct_size = C.sizeof(req)
+        req.assembly_family, req.parameter_set = NOISE_REFINER_FAMILY, parameter_set
+        req.parameter_set_aggregate_identity = ZIMAGE_NOISE_AGGREGATES[parameter_set - 1]
+        req.model_contract_identity = req.weight_identity = ZIMAGE_LOCK_ID
+        req.shader_portfolio_identity = req.precision_policy_identity = req.capability_route_identity = ZIMAGE_LOCK_ID
+        req.memory_ceiling_bytes = memory_ceiling
+        req.external_input_bytes = 2 * 1024 * 3840
+        req.audit_bytes = ZIMAGE_AUDIT_ARENA_BYTES
+        req.shader_id = 24
+        req.weight_count = len(payloads)
+        ups = weight_uploads(payloads)
+        for i in range(len(payloads)):
+            req.weights[i].content_identity = ups[i].content_identity
+            req.weights[i].layout_identity = ups[i].layout_identity
+            req.weights[i].byte_count = ups[i].byte_count
+        req.step_count = MODEL_BLOCK_MAX_STEPS
+        for i in range(MODEL_BLOCK_MAX_STEPS):
+            req.steps[i] = i + 1
+        bid = C.c_uint64()
+        rc = self.lib.prometheus_reactor_runtime_model_block_create(self.rt.handle, C.byref(req), C.byref(bid),
+                                                                    C.byref(self.evidence))
+        if rc != PROM_OK:
+            return rc, self.evidence
+        self.id = bid.value
+        rc = self.lib.prometheus_reactor_runtime_model_block_upload_weights(self.rt.handle, self.id, ups, len(ups),
+                                                                            C.byref(self.evidence))
+        return rc, self.evidence
+
+    def create_context_refiner(self, payloads: list) -> tuple[int, PrometheusModelBlockEvidence]:
+        ups = weight_uploads(payloads)
+        req = PrometheusContextRefinerCreateRequest()
+        req.struct_size = C.sizeof(req)
+        req.model_local_block_id, req.lock_identity = 0, ZIMAGE_LOCK_ID
+        req.upload_count, req.uploads = len(ups), ups
+        bid = C.c_uint64()
+        rc = self.lib.prometheus_reactor_runtime_context_refiner_create(self.rt.handle, C.byref(req), C.byref(bid),
+                                                                        C.byref(self.evidence))
+        self.id = bid.value
+        return rc, self.evidence
+
+    def rebind(self, payloads: list, context: bool = False) -> tuple[int, PrometheusModelBlockEvidence]:
+        ups = weight_uploads(payloads)
+        req = PrometheusNoiseRefinerRebindRequest()
+        req.struct_size = C.sizeof(req)
+        req.model_local_block_id, req.lock_identity = 1, ZIMAGE_LOCK_ID
+        req.upload_count, req.uploads = len(ups), ups
+        fn = (self.lib.prometheus_reactor_runtime_context_refiner_rebind if context
+              else self.lib.prometheus_reactor_runtime_noise_refiner_rebind)
+        rc = fn(self.rt.handle, self.id, C.byref(req), C.byref(self.evidence))
+        return rc, self.evidence
+
+    def noise_execute(self, image_bf16: np.ndarray, timestep_bf16: np.ndarray, block: int = 0
+                      ) -> tuple[int, PrometheusModelBlockEvidence]:
+        req = PrometheusNoiseRefiner0ExecuteRequest()
+        req.struct_size = C.sizeof(req)
+        req.model_input_bf16, req.timestep_bf16 = image_bf16.ctypes.data, timestep_bf16.ctypes.data
+        req.model_input_bytes, req.timestep_bytes = image_bf16.nbytes, timestep_bf16.nbytes
+        req.input_identity = req.timestep_identity = req.output_identity = 7
+        fn = (self.lib.prometheus_reactor_runtime_noise_refiner1_execute if block == 1
+              else self.lib.prometheus_reactor_runtime_noise_refiner0_execute)
+        rc = fn(self.rt.handle, self.id, C.byref(req), C.byref(self.evidence))
+        return rc, self.evidence
+
+    def context_execute(self, x: np.ndarray) -> tuple[int, PrometheusModelBlockEvidence]:
+        req = PrometheusContextRefiner0ExecuteRequest()
+        req.struct_size = C.sizeof(req)
+        req.context_input, req.context_input_bytes = x.ctypes.data, x.nbytes
+        req.input_identity = req.output_identity = 9
+        rc = self.lib.prometheus_reactor_runtime_context_refiner0_execute(self.rt.handle, self.id, C.byref(req),
+                                                                          C.byref(self.evidence))
+        return rc, self.evidence
+
+    def execute_resident(self, input_generation: int, context: bool = False
+                         ) -> tuple[int, PrometheusModelBlockEvidence]:
+        if context:
+            req = PrometheusContextRefinerResidentExecuteRequest()
+            fn = self.lib.prometheus_reactor_runtime_context_refiner_execute_resident
+        else:
+            req = PrometheusNoiseRefinerResidentExecuteRequest()
+            fn = self.lib.prometheus_reactor_runtime_noise_refiner_execute_resident
+        req.struct_size = C.sizeof(req)
+        req.input_generation, req.output_identity = input_generation, 11
+        rc = fn(self.rt.handle, self.id, C.byref(req), C.byref(self.evidence))
+        return rc, self.evidence
+
+    def audit_final(self, tokens: int, generation: int, context: bool = False
+                    ) -> tuple[int, Optional[np.ndarray], PrometheusModelBlockEvidence]:
+        out = np.empty((tokens, 3840), dtype=np.float32)
+        req = PrometheusNoiseRefinerFinalAuditRequest()
+        req.struct_size = C.sizeof(req)
+        req.required_output_generation, req.output_identity = generation, 13
+        req.output, req.output_element_capacity = out.ctypes.data, out.size
+        fn = (self.lib.prometheus_reactor_runtime_context_refiner_audit_final if context
+              else self.lib.prometheus_reactor_runtime_noise_refiner_audit_final)
+        rc = fn(self.rt.handle, self.id, C.byref(req), C.byref(self.evidence))
+        return rc, (out if rc == PROM_OK else None), self.evidence
+
+    def destroy(self) -> int:
+        rc = self.lib.prometheus_reactor_runtime_model_block_destroy(self.rt.handle, self.id)
+        self.id = 0
+        return rc

@@ -258,3 +258,85 @@ def flops_per_forward(cfg: BlockConfig, batch: int) -> float:
     pairs = S * (S + 1) / 2 if cfg.family == GEMMA else float(S * S)
     attn = batch * H * pairs * 4.0 * hd
     return linear + attn
+
+
+# ---------------------------------------------------------------- Z-Image model-block executors
+ZIMAGE_NOISE_NAMES = ("adaLN_modulation.0.bias", "adaLN_modulation.0.weight", "attention.k_norm.weight",
+                      "attention.out.weight", "attention.q_norm.weight", "attention.qkv.weight",
+                      "attention_norm1.weight", "attention_norm2.weight", "feed_forward.w1.weight",
+                      "feed_forward.w2.weight", "feed_forward.w3.weight", "ffn_norm1.weight", "ffn_norm2.weight")
+ZIMAGE_CONTEXT_NAMES = ZIMAGE_NOISE_NAMES[2:]
+
+
+def zimage_weight_shapes(context: bool = False, width: int = 3840, heads: int = 30, head_dim: int = 128,
+                         ffn: int = 10240) -> dict[str, tuple]:
+    """The cache manifest's tensors in lexical order, linear weights [in][out]
+    (canonicalLoadWeights, zimage/canonical_reference.go:51-80; reactor_vulkan_model_block.c:160-183)."""
+    shapes = {"adaLN_modulation.0.bias": (4 * width,), "adaLN_modulation.0.weight": (256, 4 * width),
+              "attention.k_norm.weight": (head_dim,), "attention.out.weight": (width, width),
+              "attention.q_norm.weight": (head_dim,), "attention.qkv.weight": (width, 3 * width),
+              "attention_norm1.weight": (width,), "attention_norm2.weight": (width,),
+              "feed_forward.w1.weight": (width, ffn), "feed_forward.w2.weight": (ffn, width),
+              "feed_forward.w3.weight": (width, ffn), "ffn_norm1.weight": (width,), "ffn_norm2.weight": (width,)}
+    names = ZIMAGE_CONTEXT_NAMES if context else ZIMAGE_NOISE_NAMES
+    return {n: shapes[n] for n in names}
+
+
+def zimage_random_weights_f16(seed: int, context: bool = False) -> dict[str, np.ndarray]:
+    """Random binary16 payloads: linear weights and the adaLN N(0, 0.02), gains 1 + N(0, 0.02)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    out = {}
+    for name, shape in zimage_weight_shapes(context).items():
+        if len(shape) == 1 and not name.startswith("adaLN"):
+            v = 1.0 + 0.02 * rng.standard_normal(shape)
+        else:
+            v = 0.02 * rng.standard_normal(shape)
+        out[name] = v.astype(np.float16)
+    return out
+
+
+def bf16_values(x: np.ndarray) -> np.ndarray:
+    """fp32 -> BF16 (round to nearest even) -> fp32, and the raw 16-bit payload."""
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    b = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    return (b.astype(np.uint32) << 16).view(np.float32), b
+
+
+def _canonical_rope_rows(x: np.ndarray, coords: np.ndarray, theta: float = 256.0) -> np.ndarray:
+    return rope_3axis(x, coords, theta, (32, 48, 48))
+
+
+def zimage_refiner_forward(w16: dict, x: np.ndarray, temb: np.ndarray | None, tokens: int, context: bool,
+                           width: int = 3840, heads: int = 30, head_dim: int = 128, ffn: int = 10240) -> np.ndarray:
+    """One Z-Image refiner block in binary64 from binary16 weights.
+
+    Noise refiner: runCanonicalNoiseRefiner0 (zimage/canonical_reference.go:315-480): adaLN
+    256 -> 4 x width with bias, gates tanh, scales + 1, no shift; image tokens on the 32-wide
+    grid at frame 33 (canonical_contract.go:44-64).  Context refiner: runCanonicalContextRefiner
+    (zimage/context_refiner_reference.go:229-299): the same block unmodulated, token t at
+    (t + 1, 0, 0) (:151-174).  Both: RMSNorm eps 1e-5, sandwich norms, SwiGLU, residuals."""
+    W = {k: v.astype(np.float64) for k, v in w16.items()}
+    xs = x.astype(np.float64).reshape(tokens, width)
+    eps = float(np.float32(1e-5))
+    if context:
+        scale_a = scale_m = gate_a = gate_m = 1.0
+        coords = np.stack([np.arange(tokens) + 1, np.zeros(tokens), np.zeros(tokens)], axis=1)
+    else:
+        ada = temb.astype(np.float64) @ W["adaLN_modulation.0.weight"] + W["adaLN_modulation.0.bias"]
+        scale_a, gate_a, scale_m, gate_m = (ada[i * width:(i + 1) * width] for i in range(4))
+        gate_a, gate_m = np.tanh(gate_a), np.tanh(gate_m)
+        scale_a, scale_m = scale_a + 1.0, scale_m + 1.0
+        tok = np.arange(tokens)
+        coords = np.stack([np.full(tokens, 33), tok // 32, tok % 32], axis=1)
+    mod = rmsnorm(xs, W["attention_norm1.weight"], eps) * scale_a
+    qkv = mod @ W["attention.qkv.weight"]
+    q = qkv[:, :width].reshape(tokens, heads, head_dim)
+    k = qkv[:, width:2 * width].reshape(tokens, heads, head_dim)
+    v = qkv[:, 2 * width:].reshape(tokens, heads, head_dim)
+    q = _canonical_rope_rows(rmsnorm(q, W["attention.q_norm.weight"], eps), coords)
+    k = _canonical_rope_rows(rmsnorm(k, W["attention.k_norm.weight"], eps), coords)
+    o = attention(q, k, v, 1.0 / math.sqrt(head_dim), causal=False)
+    res = xs + gate_a * rmsnorm(o @ W["attention.out.weight"], W["attention_norm2.weight"], eps)
+    fin = rmsnorm(res, W["ffn_norm1.weight"], eps) * scale_m
+    hidden = silu(fin @ W["feed_forward.w1.weight"]) * (fin @ W["feed_forward.w3.weight"])
+    return res + gate_m * rmsnorm(hidden @ W["feed_forward.w2.weight"], W["ffn_norm2.weight"], eps)

@@ -94,6 +94,18 @@ STRUCTS = {
     "PrometheusReductionBenchmarkResult": R.PrometheusReductionBenchmarkResult,
     "PrometheusSgemmAsyncTaskDiagnostics": R.PrometheusSgemmAsyncTaskDiagnostics,
     "PrometheusSgemmAsyncDiagnostics": R.PrometheusSgemmAsyncDiagnostics,
+    "PrometheusModelBlockWeightDeclaration": R.PrometheusModelBlockWeightDeclaration,
+    "PrometheusModelBlockCreateRequest": R.PrometheusModelBlockCreateRequest,
+    "PrometheusModelBlockWeightUpload": R.PrometheusModelBlockWeightUpload,
+    "PrometheusNoiseRefinerRebindRequest": R.PrometheusNoiseRefinerRebindRequest,
+    "PrometheusContextRefinerCreateRequest": R.PrometheusContextRefinerCreateRequest,
+    "PrometheusModelBlockExecuteRequest": R.PrometheusModelBlockExecuteRequest,
+    "PrometheusNoiseRefiner0ExecuteRequest": R.PrometheusNoiseRefiner0ExecuteRequest,
+    "PrometheusNoiseRefinerResidentExecuteRequest": R.PrometheusNoiseRefinerResidentExecuteRequest,
+    "PrometheusContextRefiner0ExecuteRequest": R.PrometheusContextRefiner0ExecuteRequest,
+    "PrometheusContextRefinerResidentExecuteRequest": R.PrometheusContextRefinerResidentExecuteRequest,
+    "PrometheusNoiseRefinerFinalAuditRequest": R.PrometheusNoiseRefinerFinalAuditRequest,
+    "PrometheusModelBlockEvidence": R.PrometheusModelBlockEvidence,
 }
 
 
@@ -127,7 +139,7 @@ def test_struct_layouts_match_the_reference_header():
     import make_layouts as ML
     fixture = json.loads((REPO / "tests" / "golden" / "reference_layouts.json").read_text())["structs"]
     ours = ML.parse_structs(HEADER.read_text())
-    assert len(fixture) >= 25
+    assert len(fixture) >= 37
     for name, ref in fixture.items():
         assert name in ours, name
         assert ours[name] == [f for f, _ in ref["fields"]], name
