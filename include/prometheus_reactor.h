@@ -948,6 +948,145 @@ PROM_REACTOR_API int prometheus_reactor_runtime_gemma4e2b_m1_attention_scores(
     void* handle, const PrometheusGemma4E2BM1AttentionScoresRequest* request,
     PrometheusGemma4E2BM1AttentionScoresResult* out_result);
 
+/* ==== FFT (reactor_api.h:327-380, 1251-1305, 2654-2669) ====
+   Radix-2 decimation-in-time complex transforms of N = 2^k <= 2^20 points.
+   fft64 (the entry Go's FFT engine binds, internal/prometheus/fft.go:21-44):
+   one forward unnormalised transform of interleaved binary64 (re, im) pairs;
+   twiddles are computed in binary64 on the host, as the reference does
+   (reactor_concept_fft.cpp:51-58), and the butterflies run the reference's
+   arithmetic exactly (shaders/sdslv/production/fft/radix2_fp64.sdslv).
+   fft: batches of interleaved fp32 pairs, stride_elements apart (0 = N),
+   forward or inverse, optionally normalised by 1/N; fp32 twiddles from the
+   per-pass angle (radix2_butterfly.sdslv).  Only each batch's N outputs are
+   written; the caller's elements between batches are left untouched. */
+typedef struct PrometheusComplex32 {
+  float real;
+  float imag;
+} PrometheusComplex32;
+
+enum {
+  PROM_FFT_FLAG_FORWARD = 1u << 0,
+  PROM_FFT_FLAG_INVERSE = 1u << 1,
+  PROM_FFT_FLAG_INVERSE_NORMALIZE = 1u << 2,
+  PROM_FFT_FLAG_BENCHMARK_ALLOW_NON_PRODUCTION_PATH = 1u << 3,
+};
+
+enum {
+  PROM_FFT_PATH_NONE = 0,
+  PROM_FFT_PATH_UNAVAILABLE = 1,
+  PROM_FFT_PATH_CPU_ORACLE_RESERVED = 2,
+  PROM_FFT_PATH_VULKAN_RADIX2_RESERVED = 3, /* the radix-2 device route (here: CUDA) */
+};
+
+enum {
+  PROM_FFT_PATH_STATUS_UNAVAILABLE = 0,
+  PROM_FFT_PATH_STATUS_REGISTERED = 1,
+  PROM_FFT_PATH_STATUS_BENCHMARK_ENABLED = 2,
+  PROM_FFT_PATH_STATUS_PRODUCTION_ENABLED = 3,
+};
+
+enum {
+  PROM_FFT_BENCHMARK_VARIANT_NONE = 0,
+  PROM_FFT_BENCHMARK_VARIANT_RADIX2 = 2,
+};
+
+enum {
+  PROM_FFT_DETAIL_UNAVAILABLE = -6701,
+  PROM_FFT_DETAIL_INVALID_REQUEST = -6702,
+  PROM_FFT_DETAIL_NULL_INPUT = -6703,
+  PROM_FFT_DETAIL_NULL_OUTPUT = -6704,
+  PROM_FFT_DETAIL_ZERO_ELEMENT_COUNT = -6705,
+  PROM_FFT_DETAIL_NON_POWER_OF_TWO = -6706,
+  PROM_FFT_DETAIL_INVALID_DIRECTION_FLAGS = -6707,
+  PROM_FFT_DETAIL_INVALID_STRIDE = -6708,
+  PROM_FFT_DETAIL_SIZE_OVERFLOW = -6709,
+  PROM_FFT_DETAIL_ZERO_BATCH_COUNT = -6710,
+  PROM_FFT_DETAIL_INVERSE_NORMALIZE_REQUIRES_INVERSE = -6711,
+  PROM_FFT_DETAIL_VULKAN_UNAVAILABLE = -6712, /* no usable device */
+  PROM_FFT_DETAIL_UNSUPPORTED_SIZE = -6713,
+  PROM_FFT_DETAIL_ALLOCATION_FAILED = -6714,
+  PROM_FFT_DETAIL_UPLOAD_FAILED = -6715,
+  PROM_FFT_DETAIL_DISPATCH_FAILED = -6716,
+  PROM_FFT_DETAIL_READBACK_FAILED = -6717,
+  PROM_FFT_DETAIL_SHADER_UNAVAILABLE = -6718,
+  PROM_FFT_DETAIL_PLAN_DISPATCH_DISAGREEMENT = -6719,
+  PROM_FFT_DETAIL_FLOAT64_UNAVAILABLE = -6720,
+};
+
+typedef struct PrometheusFftRequest {
+  uint32_t struct_size;
+  const PrometheusComplex32* input;
+  PrometheusComplex32* output;
+  uint32_t element_count;
+  uint32_t batch_count;
+  uint32_t stride_elements;
+  uint32_t flags;
+} PrometheusFftRequest;
+
+typedef struct PrometheusFftDiagnostics {
+  uint32_t struct_size;
+  uint32_t api_declared;
+  uint32_t capability_reported;
+  uint32_t production_enabled;
+  uint32_t benchmark_enabled;
+  uint32_t last_element_count;
+  uint32_t last_batch_count;
+  uint32_t last_stride_elements;
+  uint32_t last_effective_stride_elements;
+  uint32_t last_flags;
+  uint32_t last_direction;
+  uint32_t last_validation_status;
+  int32_t last_failure_detail;
+  uint32_t requested_path_id;
+  uint32_t executed_path_id;
+  uint32_t requested_radix;
+  uint32_t executed_radix;
+  uint32_t fallback_reason;
+  uint32_t plan_pass_count;
+  uint32_t ping_pong_swap_count;
+  uint32_t final_output_role;
+  uint64_t ping_arena_reuse_count;
+  uint64_t ping_arena_grow_count;
+  uint64_t pong_arena_reuse_count;
+  uint64_t pong_arena_grow_count;
+  uint64_t twiddle_arena_reuse_count;
+  uint64_t twiddle_arena_grow_count;
+  uint32_t selector_cache_valid;
+  uint32_t plan_valid;
+  uint32_t plan_element_count;
+  uint32_t plan_log2_element_count;
+  uint32_t plan_first_span;
+  uint32_t plan_last_span;
+  uint32_t plan_radix_mask;
+  uint32_t plan_bit_reversal_required;
+  uint32_t plan_first_source_role;
+  uint32_t plan_first_destination_role;
+  uint32_t plan_direction;
+  uint32_t plan_twiddle_mode;
+  uint64_t selector_cache_reuse_count;
+  uint64_t selector_cache_recompute_count;
+  uint64_t selector_cache_invalidation_count;
+  uint64_t selector_cache_last_dependency_mask;
+} PrometheusFftDiagnostics;
+
+/* reactor_api.h:2652-2654 -- forward unnormalised binary64 FFT of `count`
+   interleaved pairs (reactor_concept_fft.cpp:107-116). */
+PROM_REACTOR_API int prometheus_reactor_runtime_fft64(void* handle, const double* input, double* output,
+                                                      uint32_t count, uint32_t* stage, int* detail);
+/* reactor_api.h:2655-2658 -- batched fp32 FFT; validation order of
+   reactor_vulkan_fft.c:59-86, plan bookkeeping of :88-114. */
+PROM_REACTOR_API int prometheus_reactor_runtime_fft(void* handle, const PrometheusFftRequest* request,
+                                                    uint32_t* out_stage, int* out_detail_code);
+/* reactor_api.h:2659-2663 -- the radix-2 variant (2) only. */
+PROM_REACTOR_API int prometheus_reactor_runtime_fft_benchmark_variant(void* handle,
+                                                                      const PrometheusFftRequest* request,
+                                                                      uint32_t requested_variant, uint32_t* out_stage,
+                                                                      int* out_detail_code);
+/* reactor_api.h:2664-2669 -- the handle's FFT diagnostics (sized: copy out_size bytes). */
+PROM_REACTOR_API int prometheus_reactor_runtime_fft_diagnostics(void* handle, PrometheusFftDiagnostics* out_diag);
+PROM_REACTOR_API int prometheus_reactor_runtime_fft_diagnostics_sized(void* handle, PrometheusFftDiagnostics* out_diag,
+                                                                      uint32_t out_size);
+
 /* ==== Z-Image model-block executors (reactor_api.h:666-1250, 2713-2784) ====
    One closed model block per handle, as in the reference (one model_block
    state per runtime, reactor_vulkan_model_block.c:1603-1780):

@@ -207,6 +207,18 @@ cudaError_t widen_bf16(const void* src, float* dst, uint64_t n, cudaStream_t str
 cudaError_t widen_f16(const void* src, uint32_t rows, uint32_t cols, float* dst, uint64_t ld, uint32_t col0,
                       cudaStream_t stream);
 
+// ---------------------------------------------------------------- FFT (fft.cu)
+// Radix-2 decimation-in-time complex transforms of n = 2^k <= kFftMaxElements
+// points, interleaved (re, im) pairs; `in` and `out` must not overlap.
+// fft64: forward, one transform, binary64, host twiddle table of n doubles
+// (cos, sin of -2 pi i / n for i < n / 2).  fft32: `batch` transforms
+// stride_elements apart, twiddles computed per pass in fp32; inverse uses +2 pi,
+// normalize divides the inverse by n.
+constexpr uint32_t kFftMaxElements = 1u << 20;
+cudaError_t fft64(const double* in, double* out, uint32_t n, const double* twiddles, cudaStream_t stream);
+cudaError_t fft32(const float* in, float* out, uint32_t n, uint32_t batch, uint64_t stride_elements, bool inverse,
+                  bool normalize, cudaStream_t stream);
+
 // ---------------------------------------------------------------- Gemma M1 boundary (gemma_m1.cu)
 // BF16 storage rounding as the reference's M1 entry points apply it; inputs
 // must already be checked finite.  Head widths are even and <= kM1MaxHeadWidth.

@@ -201,7 +201,8 @@ void destroy_runtime(Runtime* rt) {
     t.c.release();
   }
   for (DevBuf* b : {&rt->scratch, &rt->da, &rt->db, &rt->dc, &rt->rin, &rt->rout, &rt->rw, &rt->rinv, &rt->words,
-                    &rt->batch_c, &rt->m1_cos, &rt->m1_sin, &rt->m1_q, &rt->m1_k, &rt->m1_scores})
+                    &rt->batch_c, &rt->m1_cos, &rt->m1_sin, &rt->m1_q, &rt->m1_k, &rt->m1_scores, &rt->fft_in,
+                    &rt->fft_out, &rt->fft_tw})
     b->release();
   for (cudaStream_t* st : {&rt->copy_in, &rt->copy_out})
     if (*st != nullptr) {

@@ -140,6 +140,13 @@ struct Runtime {
   uint64_t m46_allocations = 0;   // staging (re)allocations made by the RMSNorm entries
   DevBuf m1_cos, m1_sin, m1_q, m1_k, m1_scores;
   uint32_t m1_slot_generation[3] = {0, 0, 0};  // writes of the Q, K and score slots
+  // FFT (fft_api.cpp): device staging, the binary64 twiddle table of the last
+  // size, and the diagnostics record of the last request.
+  DevBuf fft_in, fft_out, fft_tw;
+  uint32_t fft_tw_count = 0;
+  uint64_t fft_grow[3] = {0, 0, 0}, fft_reuse[3] = {0, 0, 0};  // ping (in), pong (out), twiddles
+  PrometheusFftDiagnostics fft_diag = {};
+  bool fft_diag_init = false;
   // The handle's one Z-Image model block (zimage_api.cpp), or null.
   struct ModelBlockState* model_block = nullptr;
   uint64_t next_model_block_id = 1;
