@@ -432,6 +432,35 @@ MB_RESOURCE_CREATE_FAILED, MB_AUDIT_FAILED, MB_STALE_OUTPUT = -6905, -6911, -691
 MB_PARAMETER_SET_MISMATCH, MB_REBIND_FAILED = -6920, -6921
 
 
+FFT_FLAG_FORWARD, FFT_FLAG_INVERSE, FFT_FLAG_INVERSE_NORMALIZE = 1, 2, 4
+FFT_PATH_UNAVAILABLE, FFT_PATH_RADIX2 = 1, 3
+
+
+class PrometheusFftRequest(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("input", C.c_void_p), ("output", C.c_void_p),
+                ("element_count", C.c_uint32), ("batch_count", C.c_uint32), ("stride_elements", C.c_uint32),
+                ("flags", C.c_uint32)]
+
+
+class PrometheusFftDiagnostics(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in (
+        "struct_size", "api_declared", "capability_reported", "production_enabled", "benchmark_enabled",
+        "last_element_count", "last_batch_count", "last_stride_elements", "last_effective_stride_elements",
+        "last_flags", "last_direction", "last_validation_status")] + [("last_failure_detail", C.c_int32)] + [
+        (n, C.c_uint32) for n in ("requested_path_id", "executed_path_id", "requested_radix", "executed_radix",
+                                  "fallback_reason", "plan_pass_count", "ping_pong_swap_count",
+                                  "final_output_role")] + [
+        (n, C.c_uint64) for n in ("ping_arena_reuse_count", "ping_arena_grow_count", "pong_arena_reuse_count",
+                                  "pong_arena_grow_count", "twiddle_arena_reuse_count",
+                                  "twiddle_arena_grow_count")] + [
+        (n, C.c_uint32) for n in ("selector_cache_valid", "plan_valid", "plan_element_count",
+                                  "plan_log2_element_count", "plan_first_span", "plan_last_span", "plan_radix_mask",
+                                  "plan_bit_reversal_required", "plan_first_source_role",
+                                  "plan_first_destination_role", "plan_direction", "plan_twiddle_mode")] + [
+        (n, C.c_uint64) for n in ("selector_cache_reuse_count", "selector_cache_recompute_count",
+                                  "selector_cache_invalidation_count", "selector_cache_last_dependency_mask")]
+
+
 class PrometheusModelBlockWeightDeclaration(C.Structure):
     _fields_ = [("content_identity", C.c_uint64), ("layout_identity", C.c_uint64), ("byte_count", C.c_uint64)]
 
@@ -629,6 +658,13 @@ SIGNATURES = {
         C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusNoiseRefinerFinalAuditRequest), C.POINTER(PrometheusModelBlockEvidence)]),
     "prometheus_reactor_runtime_model_block_get_evidence": (C.c_int, [_vp, C.c_uint64, C.POINTER(PrometheusModelBlockEvidence)]),
     "prometheus_reactor_runtime_model_block_destroy": (C.c_int, [_vp, C.c_uint64]),
+    "prometheus_reactor_runtime_fft64": (C.c_int, [_vp, _vp, _vp, _u32, _u32p, _i32p]),
+    "prometheus_reactor_runtime_fft": (C.c_int, [_vp, C.POINTER(PrometheusFftRequest), _u32p, _i32p]),
+    "prometheus_reactor_runtime_fft_benchmark_variant": (
+        C.c_int, [_vp, C.POINTER(PrometheusFftRequest), _u32, _u32p, _i32p]),
+    "prometheus_reactor_runtime_fft_diagnostics": (C.c_int, [_vp, C.POINTER(PrometheusFftDiagnostics)]),
+    "prometheus_reactor_runtime_fft_diagnostics_sized": (
+        C.c_int, [_vp, C.POINTER(PrometheusFftDiagnostics), _u32]),
     "prometheus_runtime_create": (C.c_int, [_vp, C.POINTER(C.c_void_p)]),
     "prometheus_runtime_destroy": (C.c_int, [_vp]),
     "prometheus_runtime_probe": (C.c_int, [_vp, C.POINTER(PrometheusCaps)]),
@@ -1028,6 +1064,36 @@ class Runtime:
         rc = self.lib.prometheus_reactor_runtime_gemma4e2b_m1_attention_scores(self.handle, C.byref(req),
                                                                                C.byref(res))
         return rc, s, res
+
+    # -- FFT (fft.go:21-44 binds fft64; the batched fp32 entry is native-only)
+    def fft64(self, x: np.ndarray, out: Optional[np.ndarray] = None) -> tuple[Optional[np.ndarray], CallStatus]:
+        """Forward unnormalised binary64 FFT of a complex128 vector (Go's fftBackend.Transform)."""
+        x = np.ascontiguousarray(x, dtype=np.complex128)
+        y = np.empty_like(x) if out is None else out
+        st, d = C.c_uint32(), C.c_int()
+        rc = self.lib.prometheus_reactor_runtime_fft64(self.handle, x.ctypes.data, y.ctypes.data, x.size,
+                                                        C.byref(st), C.byref(d))
+        return (y if rc == PROM_OK else None), CallStatus(rc, st.value, d.value)
+
+    def fft(self, x: np.ndarray, n: int, batch: int = 1, stride: int = 0, flags: int = 0,
+            out: Optional[np.ndarray] = None) -> tuple[np.ndarray, CallStatus]:
+        """Batched fp32 FFT of complex64 data laid out `stride` (0: n) elements per batch item."""
+        x = np.ascontiguousarray(x, dtype=np.complex64)
+        y = np.zeros_like(x) if out is None else out
+        req = PrometheusFftRequest()
+        req.struct_size = C.sizeof(req)
+        req.input, req.output = x.ctypes.data, y.ctypes.data
+        req.element_count, req.batch_count, req.stride_elements, req.flags = n, batch, stride, flags
+        st, d = C.c_uint32(), C.c_int()
+        rc = self.lib.prometheus_reactor_runtime_fft(self.handle, C.byref(req), C.byref(st), C.byref(d))
+        return y, CallStatus(rc, st.value, d.value)
+
+    def fft_diagnostics(self) -> PrometheusFftDiagnostics:
+        diag = PrometheusFftDiagnostics()
+        rc = self.lib.prometheus_reactor_runtime_fft_diagnostics(self.handle, C.byref(diag))
+        if rc != PROM_OK:
+            raise RuntimeError(f"fft diagnostics rc={rc}")
+        return diag
 
     # -- device-resident extensions (torch tensors or raw device addresses)
     def sgemm_device(self, a, b, c, m: int, n: int, k: int, variant: int = SGEMM_AUTO, stream=None,

@@ -21,6 +21,7 @@
 #include <math.h>
 #include <stddef.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <pthread.h>
 #include <string.h>
 #include <unistd.h>
@@ -480,6 +481,118 @@ ORACLE_API void oracle_m1_scores(int64_t tokens, int64_t qheads, int64_t hw, con
           *dst = (float)(acc * scale);
         }
       }
+}
+
+/* ---------------------------------------------------------------- FFT */
+
+/* The reference's binary64 FFT (prometheus_reactor_runtime_fft64): twiddles
+   computed on the host in binary64, table[2i] = cos(-2 pi i / n),
+   table[2i+1] = sin(..) for i < n/2 (internal/prometheus/native/
+   reactor_concept_fft.cpp:51-58); one bit-reversal pass and log2(n) radix-2
+   butterfly passes through ping-pong buffers, each output formed as
+   a +- (wr br - wi bi, wr bi + wi br) with the twiddle lower * (n / span)
+   (shaders/sdslv/production/fft/radix2_fp64.sdslv).  `twiddles` receives the n-double table. */
+ORACLE_API void oracle_fft64(int64_t n, const double* in, double* out, double* twiddles) {
+  const double pi = 3.14159265358979323846264338327950288;
+  double* tw = twiddles; /* n doubles */
+  for (int64_t i = 0; i < n / 2; ++i) {
+    const double angle = -2.0 * pi * (double)i / (double)n;
+    tw[2 * i] = cos(angle);
+    tw[2 * i + 1] = sin(angle);
+  }
+  int bits = 0;
+  while ((1ll << bits) < n) ++bits;
+  double* src = (double*)malloc(sizeof(double) * 2 * (size_t)n);
+  double* dst = (double*)malloc(sizeof(double) * 2 * (size_t)n);
+  if (src == NULL || dst == NULL) {
+    free(src);
+    free(dst);
+    return;
+  }
+  for (int64_t i = 0; i < n; ++i) {
+    int64_t r = 0, v = i;
+    for (int k = 0; k < bits; ++k) {
+      r = (r << 1) | (v & 1);
+      v >>= 1;
+    }
+    src[2 * r] = in[2 * i];
+    src[2 * r + 1] = in[2 * i + 1];
+  }
+  for (int64_t half = 1; half < n; half *= 2) {
+    const int64_t span = 2 * half;
+    for (int64_t index = 0; index < n; ++index) {
+      const int64_t lane = index % span, lower = lane % half;
+      const int64_t base = index - lane + lower, other = base + half;
+      const int64_t t = lower * (n / span);
+      const double wr = tw[2 * t], wi = tw[2 * t + 1];
+      const double ar = src[2 * base], ai = src[2 * base + 1], br = src[2 * other], bi = src[2 * other + 1];
+      const double tr = wr * br - wi * bi, ti = wr * bi + wi * br;
+      dst[2 * index] = lane < half ? ar + tr : ar - tr;
+      dst[2 * index + 1] = lane < half ? ai + ti : ai - ti;
+    }
+    double* sw = src;
+    src = dst;
+    dst = sw;
+  }
+  for (int64_t i = 0; i < 2 * n; ++i) out[i] = src[i];
+  free(src);
+  free(dst);
+}
+
+/* The fp32 transform of prometheus_reactor_runtime_fft with the shader's per-pass
+   angle sign * 2 pi * lower / span in fp32 and libm cosf / sinf for its native
+   cos / sin (radix2_butterfly.sdslv); inverse normalisation divides by n in
+   the last pass.  `batch` transforms `stride` complex elements apart. */
+ORACLE_API void oracle_fft32(int64_t n, int64_t batch, int64_t stride, int inverse, int normalize, const float* in,
+                             float* out) {
+  int bits = 0;
+  while ((1ll << bits) < n) ++bits;
+  float* src = (float*)malloc(sizeof(float) * 2 * (size_t)n);
+  float* dst = (float*)malloc(sizeof(float) * 2 * (size_t)n);
+  if (src == NULL || dst == NULL) {
+    free(src);
+    free(dst);
+    return;
+  }
+  for (int64_t bt = 0; bt < batch; ++bt) {
+    const float* x = in + 2 * bt * stride;
+    for (int64_t i = 0; i < n; ++i) {
+      int64_t r = 0, v = i;
+      for (int k = 0; k < bits; ++k) {
+        r = (r << 1) | (v & 1);
+        v >>= 1;
+      }
+      src[2 * r] = x[2 * i];
+      src[2 * r + 1] = x[2 * i + 1];
+    }
+    for (int64_t half = 1; half < n; half *= 2) {
+      const int64_t span = 2 * half;
+      const int last = normalize && span == n;
+      for (int64_t index = 0; index < n; ++index) {
+        const int64_t lane = index % span, lower = lane % half;
+        const int64_t base = index - lane + lower, other = base + half;
+        const float sign = inverse ? 1.0f : -1.0f;
+        const float angle = sign * 6.28318530717958647692f * (float)lower / (float)span;
+        const float wr = cosf(angle), wi = sinf(angle);
+        const float br = src[2 * other], bi = src[2 * other + 1];
+        const float tr = wr * br - wi * bi, ti = wr * bi + wi * br;
+        float re = lane < half ? src[2 * base] + tr : src[2 * base] - tr;
+        float im = lane < half ? src[2 * base + 1] + ti : src[2 * base + 1] - ti;
+        if (last) {
+          re = re / (float)n;
+          im = im / (float)n;
+        }
+        dst[2 * index] = re;
+        dst[2 * index + 1] = im;
+      }
+      float* sw = src;
+      src = dst;
+      dst = sw;
+    }
+    for (int64_t i = 0; i < 2 * n; ++i) out[2 * bt * stride + i] = src[i];
+  }
+  free(src);
+  free(dst);
 }
 
 ORACLE_API int oracle_max_threads(void) {

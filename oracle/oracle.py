@@ -61,6 +61,8 @@ def lib() -> C.CDLL:
         L.oracle_m1_rmsnorm.argtypes = [i64, i64, i64, vp, vp, C.c_float, i32, i32, vp, vp]
         L.oracle_m1_rope.argtypes = [i64, i64, i64, vp, vp, vp, vp]
         L.oracle_m1_scores.argtypes = [i64, i64, i64, vp, vp, C.c_double, i32, vp]
+        L.oracle_fft64.argtypes = [i64, vp, vp, vp]
+        L.oracle_fft32.argtypes = [i64, i64, i64, i32, i32, vp, vp]
         L.oracle_max_threads.restype = i32
         _lib = L
     return _lib
@@ -275,4 +277,27 @@ def m1_scores(q: np.ndarray, k: np.ndarray, tokens: int, qheads: int, hw: int, s
     q, k = _f32c(q), _f32c(k)
     out = np.empty(qheads * tokens * tokens, dtype=np.float32)
     lib().oracle_m1_scores(tokens, qheads, hw, _p(q), _p(k), float(scale), {"f64": 0, "go": 1}[form], _p(out))
+    return out
+
+
+# ------------------------------------------------------------------ FFT
+def fft64(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """The reference's binary64 radix-2 network on complex128 input (oracle.c
+    oracle_fft64); returns (spectrum, the n-double twiddle table)."""
+    x = np.ascontiguousarray(x, dtype=np.complex128)
+    n = x.size
+    out = np.empty(n, dtype=np.complex128)
+    tw = np.empty(max(n, 2), dtype=np.float64)
+    lib().oracle_fft64(n, _p(x), _p(out), _p(tw))
+    return out, tw
+
+
+def fft32(x: np.ndarray, n: int, batch: int = 1, stride: int | None = None, inverse: bool = False,
+          normalize: bool = False) -> np.ndarray:
+    """The fp32 radix-2 network (oracle.c oracle_fft32) on complex64 input laid out
+    `stride` elements per batch item."""
+    stride = stride or n
+    x = np.ascontiguousarray(x, dtype=np.complex64)
+    out = np.zeros_like(x)
+    lib().oracle_fft32(n, batch, stride, int(inverse), int(normalize), _p(x), _p(out))
     return out
