@@ -3,9 +3,11 @@
 Tolerance (<= 1e-4 per block output), written here:
   normwise relative error max|y - y64| / max|y64| <= 1e-4 for every block output,
   and relative L2 error ||y - y64|| / ||y64|| <= 1e-5.
-Cases: reduced dims, then the benchmark hidden / head / FFN dims with shorter
-sequences (the oracle runs in seconds); both through the device and the host
-entry points.
+Cases: reduced dims, the benchmark hidden / head / FFN dims with shorter
+sequences, and the two benchmark configurations end to end (Gemma 4 x 1024 at
+hidden 2048, DiT 2 x 4096 at hidden 3072; the oracle takes tens of seconds);
+both through the device and the host entry points.  Weights include a
+non-zero adaLN bias.
 """
 from __future__ import annotations
 
@@ -25,6 +27,9 @@ CASES = {
     "gemma_baseline_dims": (OB.gemma_config(seq_len=256), 1),
     "dit_baseline_dims": (OB.dit_config(seq_len=256, grid_w=16), 1),
     "dit_seq1024": (OB.dit_config(seq_len=1024, hidden=512, heads=4, ffn=1024, grid_w=32), 2),
+    # the benchmark configurations themselves
+    "gemma_baseline_config": (OB.gemma_config(), 4),
+    "dit_baseline_config": (OB.dit_config(), 2),
 }
 
 
