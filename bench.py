@@ -415,41 +415,74 @@ def block_measurements(rt, torch, stream, iters: int = 5, only: str | None = Non
 
 
 def sharded_sgemm_measurements(rt, torch, dist, rank: int, world: int, stream, iters: int = 5) -> list[dict]:
-    """The ragged sweep's two largest products at a fixed global size, column-sharded: each rank
-    holds A and N / world columns of B and C (C stays sharded); time = max over ranks."""
+    """The column-parallel SGEMM with the gather (oct_b200_sgemm_tp_device): the ragged
+    sweep's two largest products at a FIXED global size (strong scaling).  Every rank holds
+    the same A and N / world columns of B and ends with all of C; time = max over ranks.
+    Each collective is timed; rank 0 also times the one-GPU product of the full size for
+    the strong-scaling efficiency t1 / (world * tN).  Before timing, every rank's gathered
+    C is compared with its own one-GPU product of the full size."""
     from oct_b200 import reactor as R
+    from oct_b200 import tp
     res = []
     pk, _ = peaks()
     peak = pk["bf16_tflops"] / 6.0  # burst 3xTF32-adjusted peak
     for (m, n, k) in ((8192, 8192, 8192), (16384, 16384, 4096)):
-        if n % (world * 256):
+        if n % (4 * world):
             continue
-        nr = n // world
-        g = torch.Generator(device="cuda").manual_seed(17 + rank)
+        g = torch.Generator(device="cuda").manual_seed(17)  # the same A and B on every rank
         a = torch.rand(m, k, device="cuda", generator=g) * 2 - 1
-        b = torch.rand(k, nr, device="cuda", generator=g) * 2 - 1
-        c = torch.empty(m, nr, device="cuda")
+        b = torch.rand(k, n, device="cuda", generator=g) * 2 - 1
+        b_shard = tp.shard_columns(b, rank, world)
+        # one-GPU reference product of the full size (every rank: parity; rank 0: t1)
+        c1 = torch.empty(m, n, device="cuda")
         for _ in range(2):
-            rt.sgemm_device(a, b, c, m, nr, k, R.SGEMM_AUTO, stream)
-        torch.cuda.synchronize()
-        dist.barrier()
+            rt.sgemm_device(a, b, c1, m, n, k, R.SGEMM_TC_BK16, stream)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(iters):
-            rt.sgemm_device(a, b, c, m, nr, k, R.SGEMM_AUTO, stream)
+            rt.sgemm_device(a, b, c1, m, n, k, R.SGEMM_TC_BK16, stream)
         e1.record(stream)
         e1.synchronize()
-        st = rt.sync_status(stream)
-        if not st.ok:
-            raise RuntimeError(f"sharded sgemm failed: {st}")
-        t = torch.tensor([e0.elapsed_time(e1) / iters], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
-        res.append({"kernel": f"sgemm_{m}x{n}x{k}_colshard", "ranks": world, "n_per_rank": nr, "ms": round(ms, 3),
-                    "TFLOP/s": round(tf, 2), "frac_of_3xtf32_peak_all_gpus": round(tf / (peak * world), 3),
-                    "scaling": "strong (fixed global product)"})
-        del a, b, c
+        t1 = torch.tensor([e0.elapsed_time(e1) / iters], dtype=torch.float64)
+        dist.broadcast(t1, src=0)
+        del b
+        for collective, cname in ((R.TP_COLLECTIVE_PEER, "peer_stores"), (R.TP_COLLECTIVE_NCCL, "nccl_allgather")):
+            ids = [R.nccl_unique_id(rt.lib) if rank == 0 else None]
+            dist.broadcast_object_list(ids, src=0)
+            t = rt.tp_sgemm(rank, world, max_m=m, max_n=n, nccl_id=ids[0], collective=collective)
+            c = torch.full((m, n), float("nan"), device="cuda")
+            t.run_device(a, b_shard, c, m, n, k, stream)
+            if t.sync(stream) != 0:
+                raise RuntimeError(f"tp sgemm {cname} failed")
+            err = float((c - c1).abs().max() / c1.abs().max())
+            te = torch.tensor([err], dtype=torch.float64)
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+            del c
+            for _ in range(2):
+                t.run_device(a, b_shard, None, m, n, k, stream)
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0.record(stream)
+            for _ in range(iters):
+                t.run_device(a, b_shard, None, m, n, k, stream)
+            e1.record(stream)
+            e1.synchronize()
+            if t.sync(stream) != 0:
+                raise RuntimeError(f"tp sgemm {cname} failed")
+            tt = torch.tensor([e0.elapsed_time(e1) / iters], dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t.close()
+            ms, ms1 = float(tt.item()), float(t1.item())
+            tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+            parity = {"vs_1gpu_normwise": float(te.item()), "ok": bool(te.item() <= 1e-6)}
+            if not parity["ok"]:
+                raise RuntimeError(f"tp sgemm {cname} parity failed: {parity}")
+            res.append({"kernel": f"sgemm_tp_{m}x{n}x{k}", "collective": cname, "ranks": world,
+                        "n_per_rank": n // world, "ms": round(ms, 3), "ms_1gpu": round(ms1, 3),
+                        "TFLOP/s": round(tf, 2), "frac_of_3xtf32_peak_all_gpus": round(tf / (peak * world), 3),
+                        "strong_scaling_efficiency": round(ms1 / (world * ms), 3),
+                        "scaling": "strong (fixed global product, C gathered on every rank)", "parity": parity})
+        del a, b_shard, c1
         torch.cuda.empty_cache()
     return res
 
@@ -492,13 +525,16 @@ def _block_group_measure(rt, torch, dist, rank, world, stream, iters, name, cfg,
                    ffn=rcfg.ffn, seq_len=rcfg.seq_len, max_batch=local_batch, eps=rcfg.eps, rope_base=rcfg.rope_base,
                    grid_w=rcfg.grid_w, rope_frame=rcfg.rope_frame, tp_rank=tp_rank, tp_world=tp_size,
                    nccl_id=ids[0][group] if tp_size > 1 else b"")
+    # one full weight set (same seed on every rank), sharded for this rank
     g = torch.Generator(device="cuda").manual_seed(99)
-    weights = {}
-    for wname, shape in OB.weight_shapes(rcfg).items():
+    full = {}
+    for wname, shape in OB.weight_shapes(cfg).items():
         t = torch.randn(*shape, device="cuda", generator=g)
-        weights[wname] = (t * 0.02 + 1.0) if len(shape) == 1 and wname != "ada_b" else t * 0.02
-    blk.set_weights(weights)
-    del weights
+        full[wname] = (t * 0.02 + 1.0) if len(shape) == 1 and wname != "ada_b" else t * 0.02
+    shard = (tp.shard_weights(cfg.family, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, full, tp_rank,
+                              tp_size) if tp_size > 1 else full)
+    blk.set_weights(shard)
+    del shard
     T_local = local_batch * cfg.seq_len
     x = torch.randn(T_local, cfg.hidden, device="cuda", generator=torch.Generator(device="cuda").manual_seed(7 + group))
     y = torch.empty_like(x)
@@ -520,11 +556,66 @@ def _block_group_measure(rt, torch, dist, rank, world, stream, iters, name, cfg,
     flops = OB.flops_per_forward(cfg, batch)
     label = f"{name}_tp{tp_size}" if dp == 1 else f"{name}_tp{tp_size}_dp{dp}"
     blk.close()
-    del x, y
+    # parity of this layout at the benchmark configuration: each group's leader runs the
+    # same items through one GPU with the full weights (outside the timed region)
+    err = 0.0
+    if tp_rank == 0:
+        one = rt.block(fam, hidden=cfg.hidden, heads=cfg.heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                       ffn=cfg.ffn, seq_len=cfg.seq_len, max_batch=local_batch, eps=cfg.eps, rope_base=cfg.rope_base,
+                       grid_w=cfg.grid_w, rope_frame=cfg.rope_frame)
+        one.set_weights(full)
+        y1 = torch.empty_like(x)
+        one.forward_device(x, y1, local_batch, ts, stream)
+        torch.cuda.synchronize()
+        one.close()
+        err = float((y - y1).abs().max() / y1.abs().max())
+        del y1
+    te = torch.tensor([err], dtype=torch.float64)
+    dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    small = _tp_small_parity(rt, torch, dist, rank, world, cfg.family, tp_size)
+    parity = {"vs_1gpu_normwise": float(te.item()), "oracle_small_normwise": small,
+              "ok": bool(te.item() <= 1e-4 and small <= 1e-4)}
+    if not parity["ok"]:
+        raise RuntimeError(f"tensor-parallel parity failed for {label}: {parity}")
+    del x, y, full
     torch.cuda.empty_cache()
     return {"kernel": label, "tp": tp_size, "dp": dp, "batch": batch, "seq": cfg.seq_len, "ms": round(ms, 3),
             "tokens/s": round(T / (ms * 1e-3), 1), "TFLOP/s": round(flops / (ms * 1e-3) / 1e12, 2),
-            "frac_of_3xtf32_peak_all_gpus": round(flops / (ms * 1e-3) / 1e12 / (peak * world), 3)}
+            "frac_of_3xtf32_peak_all_gpus": round(flops / (ms * 1e-3) / 1e12 / (peak * world), 3),
+            "parity": parity}
+
+
+def _tp_small_parity(rt, torch, dist, rank, world, family, tp_size) -> float:
+    """One tensor-parallel layout at a small configuration against the binary64 oracle
+    (oracle/blocks.py, the checker): max normwise error over every rank."""
+    from oct_b200 import reactor as R
+    from oct_b200 import tp
+    from oracle import blocks as OB
+    dp = world // tp_size
+    group, tp_rank = rank // tp_size, rank % tp_size
+    if family == OB.GEMMA:
+        cfg, ts = OB.gemma_config(seq_len=128, hidden=1024, heads=8, head_dim=128, ffn=2048), None
+    else:
+        cfg, ts = OB.dit_config(seq_len=256, hidden=1024, heads=8, ffn=2048, grid_w=16), [300.0 + 50.0 * group]
+    w = OB.random_weights(cfg, seed=41)
+    x = np.random.default_rng(42 + group).standard_normal((cfg.seq_len, cfg.hidden)).astype(np.float32)
+    ids = [[R.nccl_unique_id(rt.lib) for _ in range(dp)] if rank == 0 else None]
+    dist.broadcast_object_list(ids, src=0)
+    shard = (tp.shard_weights(cfg.family, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, w, tp_rank,
+                              tp_size) if tp_size > 1 else w)
+    rcfg = tp.rank_config(cfg, tp_rank, tp_size)
+    fam = R.BLOCK_GEMMA if family == OB.GEMMA else R.BLOCK_DIT
+    blk = rt.block(fam, hidden=rcfg.hidden, heads=rcfg.heads, kv_heads=rcfg.kv_heads, head_dim=rcfg.head_dim,
+                   ffn=rcfg.ffn, seq_len=rcfg.seq_len, max_batch=1, eps=rcfg.eps, rope_base=rcfg.rope_base,
+                   grid_w=rcfg.grid_w, rope_frame=rcfg.rope_frame, tp_rank=tp_rank, tp_world=tp_size,
+                   nccl_id=ids[0][group] if tp_size > 1 else b"")
+    blk.set_weights(shard)
+    y = blk.forward(x, 1, ts)
+    blk.close()
+    ref = OB.forward(cfg, w, x, ts)
+    t = torch.tensor([float(np.max(np.abs(y - ref)) / np.max(np.abs(ref)))], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 def run_ours(args) -> None:
@@ -663,11 +754,13 @@ def run_ours(args) -> None:
             "dtype": "f32",
             "data": "synthetic",
             "config": {
-                "workload": f"sgemm {m}x{n}x{k} per rank (A replicated, B and C column-sharded; global N = {n}*ranks)",
+                "workload": (f"sgemm {m}x{n}x{k} per rank: independent products, A and B seeded per rank, no data "
+                             "exchange (weak scaling); the column-parallel product with replicated A and the "
+                             "gathered C is the sgemm_tp secondary lines (strong scaling)"),
                 "m": m, "n_per_rank": n, "k": k, "variant": ("tcgen05 3xTF32" + (" CTA pair" if args.variant in (216, 232) else ""))
                 if args.variant in (1, 16, 32, 216, 232) else "fp32 FMA",
                 "stage_depth_k": args.variant % 100 if args.variant in (16, 32, 216, 232) else None,
-                "parallelism": f"column-parallel x{world}",
+                "parallelism": f"independent replicas x{world}",
                 "l2": "no flush: every operand (256 MiB) exceeds the 126 MB L2",
                 "input": "U[-1,1) fp32, seeded per rank",
             },

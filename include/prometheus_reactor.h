@@ -193,6 +193,11 @@ enum {
   OCT_B200_DETAIL_BLOCK_NCCL = -7012,        /* tensor-parallel communicator unavailable */
   OCT_B200_DETAIL_BLOCK_NOT_FOUND = -7013,   /* unknown block id */
   OCT_B200_DETAIL_BLOCK_EXEC = -7014,        /* a block kernel or collective failed */
+  OCT_B200_DETAIL_TP_INVALID = -7020,        /* tensor-parallel SGEMM configuration or call rejected */
+  OCT_B200_DETAIL_TP_ALLOC = -7021,          /* its output / exchange buffers could not be allocated */
+  OCT_B200_DETAIL_TP_NCCL = -7022,           /* communicator or peer-memory setup failed */
+  OCT_B200_DETAIL_TP_NOT_FOUND = -7023,      /* unknown tensor-parallel SGEMM id */
+  OCT_B200_DETAIL_TP_EXEC = -7024,           /* a kernel, copy or collective of the call failed */
 };
 
 /* ---- reductions (reactor_api.h:375-581) ---- */
@@ -1624,6 +1629,54 @@ PROM_REACTOR_API int oct_b200_block_forward_device(void* handle, uint64_t block_
 PROM_REACTOR_API int oct_b200_block_forward(void* handle, uint64_t block_id, const float* x, float* y, uint32_t batch,
                                             const float* timesteps, int* out_detail_code);
 PROM_REACTOR_API int oct_b200_block_destroy(void* handle, uint64_t block_id);
+
+/* ---- column-parallel SGEMM over tensor-parallel ranks (extension: the
+   reference drives one device per handle, prometheus_reactor_runtime_sgemm,
+   reactor_api.h:2587-2595; this is its multi-GPU form, one process per GPU).
+   C = A * B for A [m][k] (the same on every rank) and B [k][n] column-sharded:
+   rank r passes B[:, r*n/world .. (r+1)*n/world) as d_b_shard ([k][n/world],
+   leading dimension ldb).  Every rank receives all of C [m][n], row-major.
+   Every rank makes the same calls in the same order with the same m, n, k;
+   n must be a multiple of 4 * world, m <= max_m, n <= max_n.
+   Collective AUTO takes the peer-store path when every rank runs on its own
+   GPU: the GEMM epilogue stores each finished tile into every rank's output
+   buffer over NVLink (no TMA or bulk copy reads or writes peer memory), then a
+   bounded flag wait publishes completion.  NCCL: the GEMM writes this rank's
+   slab, ncclAllGather fills the rest, a repack kernel makes row-major C. ---- */
+enum {
+  OCT_B200_TP_COLLECTIVE_AUTO = 0u, /* peer stores when possible, else NCCL */
+  OCT_B200_TP_COLLECTIVE_PEER = 1u, /* peer stores; creation fails when not possible */
+  OCT_B200_TP_COLLECTIVE_NCCL = 2u, /* NCCL all-gather + repack */
+};
+typedef struct OctB200TpSgemmConfig {
+  uint32_t struct_size;
+  uint32_t rank;
+  uint32_t world;
+  uint32_t max_m;      /* largest m of any call */
+  uint32_t max_n;      /* largest full n of any call (multiple of 4 * world) */
+  uint32_t collective; /* OCT_B200_TP_COLLECTIVE_* */
+  uint8_t nccl_id[128]; /* world > 1: the same oct_b200_nccl_unique_id bytes on every rank */
+} OctB200TpSgemmConfig;
+/* Collective: every rank calls it with the same world, max_m, max_n, id. */
+PROM_REACTOR_API int oct_b200_tp_sgemm_create(void* handle, const OctB200TpSgemmConfig* config, uint64_t* out_id,
+                                              int* out_detail_code);
+/* Enqueue one product on `stream` (NULL = CUDA default stream).  d_c
+   (optional, leading dimension ldc >= n) receives C; *out_result (optional)
+   receives the library's own copy of C (leading dimension n), valid until this
+   rank's next call on the same id (reads must finish, or be ordered on
+   `stream`, before that call).  At least one of d_c, out_result is given. */
+PROM_REACTOR_API int oct_b200_sgemm_tp_device(void* handle, uint64_t id, const float* d_a, uint64_t lda,
+                                              const float* d_b_shard, uint64_t ldb, float* d_c, uint64_t ldc,
+                                              uint32_t m, uint32_t n, uint32_t k, void* stream, float** out_result,
+                                              int* out_detail_code);
+/* Waits for `stream`; PROM_ERROR with OCT_B200_DETAIL_DEVICE_TIMEOUT when a
+   bounded wait of an earlier call gave up (a peer never signalled). */
+PROM_REACTOR_API int oct_b200_tp_sgemm_sync(void* handle, uint64_t id, void* stream, int* out_detail_code);
+/* The collective the object took: OCT_B200_TP_COLLECTIVE_PEER or _NCCL (AUTO for world 1). */
+PROM_REACTOR_API int oct_b200_tp_sgemm_collective(void* handle, uint64_t id, uint32_t* out_collective);
+/* Collective: every rank destroys its object (a bounded barrier keeps peers'
+   buffers mapped until no rank can still write them). */
+PROM_REACTOR_API int oct_b200_tp_sgemm_destroy(void* handle, uint64_t id);
 
 /* Library build identity, for diagnostics. */
 PROM_REACTOR_API const char* oct_b200_build_info(void);

@@ -324,46 +324,30 @@ uint32_t grid_for(uint64_t work, uint32_t per_block) {
   return static_cast<uint32_t>(g < 148ull * 32 ? (g == 0 ? 1 : g) : 148ull * 32);
 }
 
+}  // namespace
+
 // ---------------------------------------------------------------- NCCL (dlopen)
-// The library does not link NCCL: the all-reduce symbols are resolved at the
-// first tensor-parallel block creation.
-typedef int (*NcclGetUniqueIdFn)(void* id);
-typedef int (*NcclCommInitRankFn)(void** comm, int nranks, NcclUniqueIdBytes id, int rank);
-typedef int (*NcclAllReduceFn)(const void* send, void* recv, size_t count, int dtype, int op, void* comm,
-                              cudaStream_t stream);
-typedef int (*NcclAllGatherFn)(const void* send, void* recv, size_t count, int dtype, void* comm,
-                               cudaStream_t stream);
-typedef int (*NcclCommDestroyFn)(void* comm);
-typedef const char* (*NcclGetErrorStringFn)(int result);
-struct Nccl {
-  bool ok = false;
-  NcclGetUniqueIdFn get_id = nullptr;
-  NcclCommInitRankFn init_rank = nullptr;
-  NcclAllReduceFn all_reduce = nullptr;
-  NcclAllGatherFn all_gather = nullptr;
-  NcclCommDestroyFn destroy = nullptr;
-  NcclGetErrorStringFn error_string = nullptr;
-};
-Nccl& nccl() {
-  static Nccl n;
+// The library does not link NCCL: the collective symbols are resolved at the
+// first tensor-parallel object creation.
+NcclApi& nccl() {
+  static NcclApi n;
   static std::once_flag once;
   std::call_once(once, [] {
     void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
     if (h == nullptr) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
     if (h == nullptr) return;
-    n.get_id = reinterpret_cast<NcclGetUniqueIdFn>(dlsym(h, "ncclGetUniqueId"));
-    n.init_rank = reinterpret_cast<NcclCommInitRankFn>(dlsym(h, "ncclCommInitRank"));
-    n.all_reduce = reinterpret_cast<NcclAllReduceFn>(dlsym(h, "ncclAllReduce"));
-    n.all_gather = reinterpret_cast<NcclAllGatherFn>(dlsym(h, "ncclAllGather"));
-    n.destroy = reinterpret_cast<NcclCommDestroyFn>(dlsym(h, "ncclCommDestroy"));
-    n.error_string = reinterpret_cast<NcclGetErrorStringFn>(dlsym(h, "ncclGetErrorString"));
+    n.get_id = reinterpret_cast<NcclApi::GetUniqueIdFn>(dlsym(h, "ncclGetUniqueId"));
+    n.init_rank = reinterpret_cast<NcclApi::CommInitRankFn>(dlsym(h, "ncclCommInitRank"));
+    n.all_reduce = reinterpret_cast<NcclApi::AllReduceFn>(dlsym(h, "ncclAllReduce"));
+    n.all_gather = reinterpret_cast<NcclApi::AllGatherFn>(dlsym(h, "ncclAllGather"));
+    n.destroy = reinterpret_cast<NcclApi::CommDestroyFn>(dlsym(h, "ncclCommDestroy"));
+    n.error_string = reinterpret_cast<NcclApi::GetErrorStringFn>(dlsym(h, "ncclGetErrorString"));
     n.ok = n.get_id && n.init_rank && n.all_reduce && n.all_gather && n.destroy;
   });
   return n;
 }
-constexpr int kNcclFloat32 = 7;  // ncclFloat32
-constexpr int kNcclSum = 0;      // ncclSum
-constexpr int kNcclInt8 = 0;     // ncclInt8 (bytes)
+
+namespace {
 // Cross-rank waits of the fused tensor-parallel path: generous, since ranks
 // may reach a forward at different times, but finite.
 constexpr unsigned long long kPeerWaitNs = 10ull * 1000000000ull;
@@ -372,7 +356,7 @@ constexpr uint32_t kTpSlots = 5;  // 4 phases of a forward + the teardown barrie
 }  // namespace
 
 int nccl_unique_id(NcclUniqueIdBytes* out) {
-  Nccl& n = nccl();
+  NcclApi& n = nccl();
   if (!n.ok) return -1;
   return n.get_id(out->bytes);
 }

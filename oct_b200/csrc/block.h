@@ -42,6 +42,29 @@ struct NcclUniqueIdBytes {
 // ncclGetUniqueId through the dlopen'ed NCCL; 0 on success.
 int nccl_unique_id(NcclUniqueIdBytes* out);
 
+// The NCCL entry points the library uses, resolved once by dlopen (ok is false
+// when no NCCL library can be loaded).
+struct NcclApi {
+  typedef int (*GetUniqueIdFn)(void* id);
+  typedef int (*CommInitRankFn)(void** comm, int nranks, NcclUniqueIdBytes id, int rank);
+  typedef int (*AllReduceFn)(const void* send, void* recv, size_t count, int dtype, int op, void* comm,
+                             cudaStream_t stream);
+  typedef int (*AllGatherFn)(const void* send, void* recv, size_t count, int dtype, void* comm, cudaStream_t stream);
+  typedef int (*CommDestroyFn)(void* comm);
+  typedef const char* (*GetErrorStringFn)(int result);
+  bool ok = false;
+  GetUniqueIdFn get_id = nullptr;
+  CommInitRankFn init_rank = nullptr;
+  AllReduceFn all_reduce = nullptr;
+  AllGatherFn all_gather = nullptr;
+  CommDestroyFn destroy = nullptr;
+  GetErrorStringFn error_string = nullptr;
+};
+NcclApi& nccl();
+constexpr int kNcclFloat32 = 7;  // ncclFloat32
+constexpr int kNcclSum = 0;      // ncclSum
+constexpr int kNcclInt8 = 0;     // ncclInt8 (bytes)
+
 class Block {
  public:
   Block() = default;

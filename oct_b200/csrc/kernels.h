@@ -74,11 +74,16 @@ uint64_t sgemm_tc_a_scratch_bytes(uint32_t m, uint32_t k);
 // owner = r / rows_per_rank, into dst[owner] at row
 // src_rank * rows_per_rank + (r - owner * rows_per_rank), leading dimension ld.
 // `dst` is a device array of one base pointer per rank (peers' memory included).
+// Broadcast form (bcast = world > 0; rows_per_rank unused): every output row r
+// goes to every rank k, into dst[k] at row r, columns col_offset.. -- the
+// column-parallel product's all-gather done by the epilogue's stores.
 struct RowScatter {
   float* const* dst = nullptr;
   uint32_t rows_per_rank = 0;
   uint32_t src_rank = 0;
   uint64_t ld = 0;
+  uint32_t bcast = 0;
+  uint64_t col_offset = 0;
 };
 cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, const float* blo, float* c,
                               uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* a_scratch, unsigned int* err,

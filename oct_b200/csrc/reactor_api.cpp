@@ -186,6 +186,8 @@ void destroy_runtime(Runtime* rt) {
   if (rt->stream != nullptr) cudaStreamSynchronize(rt->stream);
   for (auto& kv : rt->blocks) delete kv.second;
   rt->blocks.clear();
+  for (auto& kv : rt->tp_sgemms) delete kv.second;
+  rt->tp_sgemms.clear();
   destroy_model_block(rt);
   for (auto& ev : rt->timing_events) {
     cudaEventSynchronize(ev.main_end);

@@ -14,6 +14,7 @@
 #include "../../include/prometheus_reactor.h"
 #include "block.h"
 #include "kernels.h"
+#include "tp_sgemm.h"
 
 namespace oct {
 namespace rt {
@@ -132,6 +133,9 @@ struct Runtime {
   // Transformer blocks created on this handle.
   std::unordered_map<uint64_t, oct::Block*> blocks;
   uint64_t next_block = 1;
+  // Column-parallel SGEMM objects (tp_sgemm_api.cpp).
+  std::unordered_map<uint64_t, oct::TpSgemm*> tp_sgemms;
+  uint64_t next_tp_sgemm = 1;
   uint64_t next_request_id = 1;
   // Gemma M1 boundary (gemma_m1_api.cpp): the generation of the handle's one
   // committed RMSNorm weight, and device staging for the positional tables and

@@ -332,7 +332,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           *reinterpret_cast<float4*>(srow + j) = make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
       }
       asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight epilogue warps
-      if (*(volatile uint32_t*)&aborted == 0u) {
+      if (*(volatile uint32_t*)&aborted == 0u && scatter.bcast > 0u) {
+        // Broadcast: each row to every rank, the peers first and this rank last,
+        // each warp starting at a different peer so the links fill evenly.
+        const uint32_t ew = warp - 2u;
+        for (uint32_t lr = ew; lr < BM; lr += 8u) {
+          const uint32_t row = tile_m * BM + lr;
+          if (row >= m) break;
+          const float* srow = stage_tile + lr * LDS;
+          for (uint32_t i = 1; i <= scatter.bcast; ++i) {
+            const uint32_t rk = (scatter.src_rank + (i == scatter.bcast ? 0u : 1u + (i - 1u + ew) % (scatter.bcast - 1u))) %
+                                scatter.bcast;
+            float* drow = scatter.dst[rk] + static_cast<uint64_t>(row) * scatter.ld + scatter.col_offset;
+#pragma unroll
+            for (uint32_t half = 0; half < 2; ++half) {
+              const uint32_t cl = half * 128u + lane * 4u;
+              const uint32_t col = tile_n * BN + cl;
+              if (col + 4 <= n) {
+                *reinterpret_cast<float4*>(drow + col) = *reinterpret_cast<const float4*>(srow + cl);
+              } else {
+                for (uint32_t t = 0; t < 4; ++t)
+                  if (col + t < n) drow[col + t] = srow[cl + t];
+              }
+            }
+          }
+        }
+      } else if (*(volatile uint32_t*)&aborted == 0u) {
         const uint32_t ew = warp - 2u;
         for (uint32_t lr = ew; lr < BM; lr += 8u) {
           const uint32_t row = tile_m * BM + lr;
@@ -663,7 +688,8 @@ cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, co
   const uint64_t grid = static_cast<uint64_t>(tiles_m) * tiles_n * batch;
   if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
   const RowScatter sc = scatter != nullptr ? *scatter : RowScatter{};
-  if (sc.dst != nullptr && (batch != 1 || sc.rows_per_rank == 0 || sc.ld % 4 != 0 || ldc % 4 != 0))
+  if (sc.dst != nullptr && (batch != 1 || (sc.rows_per_rank == 0 && sc.bcast == 0) || sc.ld % 4 != 0 ||
+                            ldc % 4 != 0 || sc.col_offset % 4 != 0 || (sc.bcast > 0 && sc.src_rank >= sc.bcast)))
     return cudaErrorInvalidValue;
   sgemm3x_kernel<BK><<<static_cast<uint32_t>(grid), NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(
       m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, d.mp, d.np, stride_c, residual, ldr,

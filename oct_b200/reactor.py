@@ -575,6 +575,23 @@ class OctB200BlockConfig(C.Structure):
 
 
 BLOCK_GEMMA, BLOCK_DIT = 1, 2
+
+
+class OctB200TpSgemmConfig(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_uint32),
+        ("rank", C.c_uint32),
+        ("world", C.c_uint32),
+        ("max_m", C.c_uint32),
+        ("max_n", C.c_uint32),
+        ("collective", C.c_uint32),
+        ("nccl_id", C.c_uint8 * 128),
+    ]
+
+
+TP_COLLECTIVE_AUTO, TP_COLLECTIVE_PEER, TP_COLLECTIVE_NCCL = 0, 1, 2
+DETAIL_TP_INVALID, DETAIL_TP_ALLOC, DETAIL_TP_NCCL, DETAIL_TP_NOT_FOUND, DETAIL_TP_EXEC = (
+    -7020, -7021, -7022, -7023, -7024)
 GEMMA_SLOTS = {"norm1": 0, "wqkv": 1, "wo": 2, "norm2": 3, "wgu": 4, "wd": 5}
 DIT_SLOTS = {"ada_w": 0, "ada_b": 1, "attn_norm1": 2, "wqkv": 3, "q_norm": 4, "k_norm": 5, "wo": 6,
              "attn_norm2": 7, "ffn_norm1": 8, "w13": 9, "w2": 10, "ffn_norm2": 11}
@@ -687,6 +704,12 @@ SIGNATURES = {
         C.c_int, [_vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_uint32)]),
     "oct_b200_nccl_unique_id": (C.c_int, [_vp]),
     "oct_b200_block_create": (C.c_int, [_vp, C.POINTER(OctB200BlockConfig), C.POINTER(C.c_uint64), _i32p]),
+    "oct_b200_tp_sgemm_create": (C.c_int, [_vp, C.POINTER(OctB200TpSgemmConfig), C.POINTER(C.c_uint64), _i32p]),
+    "oct_b200_sgemm_tp_device": (C.c_int, [_vp, C.c_uint64, _vp, _u64, _vp, _u64, _vp, _u64, _u32, _u32, _u32, _vp,
+                                           C.POINTER(C.c_void_p), _i32p]),
+    "oct_b200_tp_sgemm_sync": (C.c_int, [_vp, C.c_uint64, _vp, _i32p]),
+    "oct_b200_tp_sgemm_collective": (C.c_int, [_vp, C.c_uint64, C.POINTER(C.c_uint32)]),
+    "oct_b200_tp_sgemm_destroy": (C.c_int, [_vp, C.c_uint64]),
     "oct_b200_block_set_weight": (C.c_int, [_vp, C.c_uint64, _u32, _vp, _u64, _u32]),
     "oct_b200_block_forward_device": (C.c_int, [_vp, C.c_uint64, _vp, _vp, _u32, _vp, _vp, _i32p]),
     "oct_b200_block_forward": (C.c_int, [_vp, C.c_uint64, _vp, _vp, _u32, _vp, _i32p]),
@@ -1174,6 +1197,11 @@ class Runtime:
                      rope_frame=rope_frame, tp_rank=tp_rank, tp_world=tp_world, nccl_id=nccl_id)
 
 
+    def tp_sgemm(self, rank: int, world: int, max_m: int, max_n: int, nccl_id: bytes = b"",
+                 collective: int = 0) -> "TpSgemm":
+        return TpSgemm(self, rank, world, max_m, max_n, nccl_id, collective)
+
+
 def nccl_unique_id(lib) -> bytes:
     buf = (C.c_uint8 * 128)()
     if lib.oct_b200_nccl_unique_id(C.cast(buf, C.c_void_p)) != PROM_OK:
@@ -1239,6 +1267,55 @@ class Block:
     def close(self) -> None:
         if getattr(self, "id", None) is not None:
             self.lib.oct_b200_block_destroy(self.rt.handle, self.id)
+            self.id = None
+
+
+class TpSgemm:
+    """Column-parallel SGEMM over tensor-parallel ranks (oct_b200_tp_sgemm_*): every
+    rank passes the same A and its column shard of B (oct_b200.tp.shard_columns) and
+    receives all of C."""
+
+    def __init__(self, rt: Runtime, rank: int, world: int, max_m: int, max_n: int, nccl_id: bytes = b"",
+                 collective: int = TP_COLLECTIVE_AUTO):
+        self.rt, self.lib = rt, rt.lib
+        c = OctB200TpSgemmConfig()
+        c.struct_size = C.sizeof(c)
+        c.rank, c.world, c.max_m, c.max_n, c.collective = rank, world, max_m, max_n, collective
+        for i, v in enumerate((nccl_id or b"")[:128]):
+            c.nccl_id[i] = v
+        tid, detail = C.c_uint64(), C.c_int()
+        rc = self.lib.oct_b200_tp_sgemm_create(rt.handle, C.byref(c), C.byref(tid), C.byref(detail))
+        if rc != PROM_OK:
+            raise RuntimeError(f"tp sgemm create rc={rc} detail={detail.value}")
+        self.id, self.rank, self.world = tid.value, rank, world
+
+    @property
+    def collective(self) -> int:
+        out = C.c_uint32()
+        if self.lib.oct_b200_tp_sgemm_collective(self.rt.handle, self.id, C.byref(out)) != PROM_OK:
+            raise RuntimeError("tp sgemm collective query failed")
+        return out.value
+
+    def run_device(self, a, b_shard, c, m: int, n: int, k: int, stream=None, lda: int = 0, ldb: int = 0,
+                   ldc: int = 0) -> int:
+        """Enqueue C = A * B; returns the device address of the library's copy of C (ld n)."""
+        res, detail = C.c_void_p(), C.c_int()
+        rc = self.lib.oct_b200_sgemm_tp_device(self.rt.handle, self.id, _ptr(a), lda or k, _ptr(b_shard),
+                                               ldb or n // self.world, None if c is None else _ptr(c), ldc or n, m,
+                                               n, k, _stream_ptr(stream), C.byref(res), C.byref(detail))
+        if rc != PROM_OK:
+            raise RuntimeError(f"tp sgemm rc={rc} detail={detail.value}")
+        return res.value or 0
+
+    def sync(self, stream=None) -> int:
+        """Waits for the stream; 0 or the detail code of a failed earlier call."""
+        detail = C.c_int()
+        rc = self.lib.oct_b200_tp_sgemm_sync(self.rt.handle, self.id, _stream_ptr(stream), C.byref(detail))
+        return 0 if rc == PROM_OK else (detail.value or rc)
+
+    def close(self) -> None:
+        if getattr(self, "id", None) is not None:
+            self.lib.oct_b200_tp_sgemm_destroy(self.rt.handle, self.id)
             self.id = None
 
 

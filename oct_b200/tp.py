@@ -70,3 +70,31 @@ def shard_weights(family: int, hidden: int, heads: int, kv_heads: int, head_dim:
     out[gu_name] = _cat_cols([gu[:, f0:f1], gu[:, ffn + f0:ffn + f1]])
     out[down_name] = _rows(weights[down_name], f0, f1)
     return out
+
+
+# ---------------------------------------------------------------- column-parallel SGEMM
+def check_columns(n: int, world: int) -> int:
+    """Columns per rank of the column-parallel SGEMM (oct_b200_sgemm_tp_device): n must
+    be a multiple of 4 * world (whole 16-byte granules per rank)."""
+    if world < 1 or n <= 0 or n % (4 * world):
+        raise ValueError(f"n ({n}) must be a positive multiple of 4 * world ({4 * world})")
+    return n // world
+
+
+def shard_columns(b, rank: int, world: int):
+    """This rank's column block B[:, r n/w .. (r+1) n/w) of a [k][n] operand, contiguous."""
+    nr = check_columns(b.shape[1], world)
+    part = b[:, rank * nr:(rank + 1) * nr]
+    return part.contiguous() if hasattr(part, "contiguous") else part.copy()
+
+
+def gather_columns(slabs):
+    """Row-major C from the gathered slabs [world][m][n/w] -- what the library's
+    repack kernel does after the all-gather: C[i, r n/w + j] = slabs[r][i][j]."""
+    if hasattr(slabs, "dim"):  # torch [w][m][nr]
+        w, m, nr = slabs.shape
+        return slabs.permute(1, 0, 2).reshape(m, w * nr).contiguous()
+    import numpy as np
+    slabs = np.asarray(slabs)
+    w, m, nr = slabs.shape
+    return np.ascontiguousarray(slabs.transpose(1, 0, 2).reshape(m, w * nr))

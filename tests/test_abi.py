@@ -106,6 +106,8 @@ STRUCTS = {
     "PrometheusContextRefinerResidentExecuteRequest": R.PrometheusContextRefinerResidentExecuteRequest,
     "PrometheusNoiseRefinerFinalAuditRequest": R.PrometheusNoiseRefinerFinalAuditRequest,
     "PrometheusModelBlockEvidence": R.PrometheusModelBlockEvidence,
+    "OctB200BlockConfig": R.OctB200BlockConfig,
+    "OctB200TpSgemmConfig": R.OctB200TpSgemmConfig,
 }
 
 
@@ -384,6 +386,26 @@ def test_block_create_without_device_is_rejected(lib):
         cfg.struct_size = 8  # too small: rejected before anything else
         rc = lib.oct_b200_block_create(h, C.byref(cfg), C.byref(bid), C.byref(detail))
         assert rc == R.PROM_ERROR and detail.value == -7010
+    finally:
+        lib.prometheus_reactor_runtime_destroy(h)
+
+
+def test_tp_sgemm_create_is_validated_on_the_host(lib):
+    """Configuration checks run before any device or NCCL work."""
+    h = _handle(lib, R.TESTCFG_FAIL_DEVICE_CREATE)
+    try:
+        cfg = R.OctB200TpSgemmConfig()
+        cfg.struct_size = 8  # too small
+        tid, detail = C.c_uint64(), C.c_int()
+        rc = lib.oct_b200_tp_sgemm_create(h, C.byref(cfg), C.byref(tid), C.byref(detail))
+        assert rc == R.PROM_ERROR and detail.value == R.DETAIL_TP_INVALID
+        cfg.struct_size = C.sizeof(cfg)
+        cfg.rank, cfg.world, cfg.max_m, cfg.max_n = 0, 2, 64, 64
+        rc = lib.oct_b200_tp_sgemm_create(h, C.byref(cfg), C.byref(tid), C.byref(detail))
+        assert rc == R.PROM_ERROR and detail.value == -6006  # handle without a device
+        rc = lib.oct_b200_sgemm_tp_device(h, 1, None, 0, None, 0, None, 0, 1, 8, 1, None, None, C.byref(detail))
+        assert rc == R.PROM_ERROR and detail.value == R.DETAIL_TP_NOT_FOUND
+        assert lib.oct_b200_tp_sgemm_destroy(h, 1) == R.PROM_ERROR
     finally:
         lib.prometheus_reactor_runtime_destroy(h)
 

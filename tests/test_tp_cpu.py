@@ -80,3 +80,57 @@ def test_shard_shapes_and_divisibility():
     assert np.array_equal(s["wqkv"][:, 32:], w["wqkv"][:, 128:])  # replicated MQA K|V
     with pytest.raises(ValueError):
         tp.shard_weights(cfg.family, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, w, 0, 3)
+
+
+def _sgemm_rank_main(rank: int, world: int, port: int, queue) -> None:
+    """Column-parallel SGEMM host logic: shard B by columns, multiply locally with the
+    oracle (binary64 accumulation), all-gather the slabs [w][m][n/w] over gloo and
+    repack them to row-major C, as oct_b200_sgemm_tp_device does on the GPUs."""
+    import torch
+    import torch.distributed as dist
+    from oct_b200 import tp
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        m, n, k = 37, 48, 29  # ragged m and k; n a multiple of 4 * world
+        rng = np.random.default_rng(8)
+        a = rng.uniform(-1, 1, (m, k)).astype(np.float32)  # replicated
+        b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+        part = tp.shard_columns(b, rank, world)
+        slab = torch.from_numpy(a.astype(np.float64) @ part.astype(np.float64))
+        slabs = [torch.empty_like(slab) for _ in range(world)]
+        dist.all_gather(slabs, slab)
+        c = tp.gather_columns(torch.stack(slabs)).numpy()
+        full = a.astype(np.float64) @ b.astype(np.float64)
+        queue.put((rank, bool(np.array_equal(c, full)), part.shape))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_column_parallel_sgemm_layout_world2():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sgemm_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = dict((r, (ok, shape)) for r, ok, shape in (q.get(timeout=5) for _ in range(2)))
+    assert all(ok for ok, _ in res.values()), res
+    assert all(shape == (29, 24) for _, shape in res.values())
+
+
+def test_column_shard_helpers():
+    from oct_b200 import tp
+    b = np.arange(6 * 32, dtype=np.float32).reshape(6, 32)
+    parts = [tp.shard_columns(b, r, 4) for r in range(4)]
+    assert all(p.shape == (6, 8) and p.flags.c_contiguous for p in parts)
+    assert np.array_equal(tp.gather_columns(np.stack(parts)), b)
+    with pytest.raises(ValueError):
+        tp.shard_columns(b, 0, 3)  # 32 is not a multiple of 12
+    with pytest.raises(ValueError):
+        tp.check_columns(40, 4)
