@@ -58,7 +58,8 @@ def parse_args():
     p.add_argument("--n", type=int, default=8192, help="columns per rank")
     p.add_argument("--k", type=int, default=8192)
     p.add_argument("--variant", type=int, default=16,
-                   help="16/32 = tcgen05 one CTA per tile with that K stage depth, 216/232 = CTA pair, 2 = FMA")
+                   help="16/32 = tcgen05 one CTA per tile with that K stage depth, 216/232 = CTA pair, "
+                        "316/332 = CTA pair with the TF32 split inside the kernel, 2 = FMA")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-secondary", action="store_true")
@@ -187,6 +188,118 @@ def cpu_sgemm_sample(m: int, n: int, k: int, seconds: float, threads: int) -> di
             "seconds": t, "rows": rows}
 
 
+def cpu_baseline_table(threads: int, budget_s: float = 2.0) -> list[dict]:
+    """The reference's CPU paths, restated in C / numpy (oracle/, the checker), each timed
+    with one thread and with all host threads: cpuSGEMM (runtime.go:319-331) and the fp64
+    `@` __octMatMulMM (emit_go_runtime.go:168-200) on output-row samples of 8192^3 sized to
+    ~budget_s; prom_reduction_cpu_reference (reactor_vulkan_fused_reduction.c:996-1114) for
+    sum / max / softmax and CanonicalRMSNorm (canonical_contract.go:91-105) over all of
+    32768 x {256, 2048, 4096}; the binary64 block pipelines (oracle/blocks.py) at a reduced
+    token count."""
+    import numpy as np
+    from oracle import oracle as O
+    from oracle import blocks as OB
+    out = []
+
+    def timed(fn):
+        t0 = time.perf_counter()
+        fn()
+        return time.perf_counter() - t0
+
+    m = n = k = 8192
+    a = O.uniform_matrix(m, k, 1000).ravel()
+    b = O.uniform_matrix(k, n, 1001).ravel()
+    for th in (1, threads):
+        probe = timed(lambda: O.cpu_sgemm_f32(a, b, m, n, k, rows=slice(0, th), threads=th))
+        rows = min(m, th * max(1, int(budget_s / max(probe, 1e-6))))
+        t = timed(lambda: O.cpu_sgemm_f32(a, b, m, n, k, rows=slice(0, rows), threads=th))
+        out.append({"path": "cpuSGEMM fp32 (runtime.go:319-331)", "kind": "port (C restatement)", "cores": th,
+                    "shape": f"{m}x{n}x{k}", "sample_rows": rows, "TFLOP/s": 2.0 * rows * n * k / t / 1e12})
+    a64, b64 = a.astype(np.float64), b.astype(np.float64)
+    probe = timed(lambda: O.oct_matmul_f64(a64, b64, m, n, k, rows=slice(0, 1)))
+    rows = min(m, max(1, int(budget_s / max(probe, 1e-6))))
+    t = timed(lambda: O.oct_matmul_f64(a64, b64, m, n, k, rows=slice(0, rows)))
+    out.append({"path": "Oct `@` __octMatMulMM[float64] (emit_go_runtime.go:168-200)", "kind": "port (C restatement)",
+                "cores": 1, "shape": f"{m}x{n}x{k}", "sample_rows": rows, "TFLOP/s": 2.0 * rows * n * k / t / 1e12})
+    del a, b, a64, b64
+    # Row reductions and RMSNorm over all 32768 rows of the reference tests' deterministic
+    # input, GB/s of algorithmic bytes
+    for width in (256, 2048, 4096):
+        x = O.reduction_input(32768, width)
+        w = (np.random.default_rng(width + 1).random(width) + 0.5).astype(np.float32)
+        r = x.shape[0]
+        for th in (1, threads):
+            for name, op in (("sum", 1), ("max", 2), ("softmax", 3), ("rmsnorm", 0)):
+                if op == 0:
+                    t = timed(lambda: O.rmsnorm_f32(x, w, 1e-5, threads=th, form="canonical"))
+                    nbytes = 8 * r * width
+                    path = "CanonicalRMSNorm (canonical_contract.go:91-105)"
+                else:
+                    t = timed(lambda: O.reduction_cpu_reference(x, op, threads=th))
+                    nbytes = (8 if op == 3 else 4) * r * width + (0 if op == 3 else 4 * r)
+                    path = f"prom_reduction_cpu_reference {name} (reactor_vulkan_fused_reduction.c)"
+                out.append({"path": path, "kind": "port (C restatement)", "cores": th,
+                            "shape": f"{r}x{width}", "GB/s": nbytes / t / 1e9, "rows/s": r / t})
+        del x
+    # Block pipelines in binary64 at a reduced token count (numpy BLAS on every host thread)
+    for name, cfg, ts in (("gemma_block", OB.gemma_config(seq_len=128), None),
+                          ("dit_block", OB.dit_config(seq_len=256, grid_w=16), [500.0])):
+        wts = OB.random_weights(cfg, seed=3)
+        xb = np.random.default_rng(4).standard_normal((cfg.seq_len, cfg.hidden)).astype(np.float32)
+        t = timed(lambda: OB.forward(cfg, wts, xb, ts))
+        out.append({"path": f"{name} pipeline, binary64 numpy restatement (oracle/blocks.py)",
+                    "kind": "port (numpy, BLAS threads)", "cores": threads,
+                    "shape": f"1 x {cfg.seq_len} tokens at the benchmark hidden / head / FFN dims",
+                    "tokens/s": cfg.seq_len / t,
+                    "note": "reduced token count: attention is a smaller share than at the benchmark length"})
+    for r in out:
+        for key in ("TFLOP/s", "GB/s", "rows/s", "tokens/s"):
+            if key in r:
+                r[key] = round(r[key], 6 if key == "TFLOP/s" else 2)
+    return out
+
+
+def ragged_sgemm_measurements(rt, torch, stream) -> list[dict]:
+    """The reference's smaller SGEMM configurations (512^3, 1000^3 and the ragged
+    4097 x 4095 x 1023) on the device (the auto-selected kernel) and end to end through
+    prometheus_reactor_runtime_sgemm with host buffers (copies included)."""
+    import numpy as np
+    from oct_b200 import reactor as R
+    out = []
+    for (m, n, k) in ((512, 512, 512), (1000, 1000, 1000), (4097, 4095, 1023)):
+        g = torch.Generator(device="cuda").manual_seed(m + n)
+        a = torch.rand(m, k, device="cuda", generator=g) * 2 - 1
+        b = torch.rand(k, n, device="cuda", generator=g) * 2 - 1
+        c = torch.empty(m, n, device="cuda")
+        iters = 50
+        for _ in range(5):
+            rt.sgemm_device(a, b, c, m, n, k, R.SGEMM_AUTO, stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            rt.sgemm_device(a, b, c, m, n, k, R.SGEMM_AUTO, stream)
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        ha, hb = a.cpu().numpy().ravel(), b.cpu().numpy().ravel()
+        hc = np.empty(m * n, dtype=np.float32)
+        for _ in range(3):
+            rt.sgemm_with_status(m, n, k, ha, hb, out=hc)
+        t0 = time.perf_counter()
+        for _ in range(10):
+            _, st = rt.sgemm_with_status(m, n, k, ha, hb, out=hc)
+        e2e_ms = (time.perf_counter() - t0) * 100.0
+        if not st.ok:
+            raise RuntimeError(f"sgemm {m}x{n}x{k} failed: {st}")
+        flops = 2.0 * m * n * k
+        out.append({"kernel": f"sgemm_{m}x{n}x{k}", "variant": "auto", "ms": round(ms, 4),
+                    "TFLOP/s": round(flops / (ms * 1e-3) / 1e12, 2), "e2e_ms": round(e2e_ms, 4),
+                    "e2e_TFLOP/s": round(flops / (e2e_ms * 1e-3) / 1e12, 3),
+                    "e2e_path": "prometheus_reactor_runtime_sgemm, pageable host buffers"})
+        del a, b, c
+    return out
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -310,15 +423,19 @@ def secondary_measurements(rt, torch, hbm_peak: float) -> list[dict]:
     out.extend(block_measurements(rt, torch, stream))
     out.extend(attention_measurements(rt, torch, stream))
     out.extend(smallm_measurements(rt, torch, stream, hbm_peak))
+    out.extend(ragged_sgemm_measurements(rt, torch, stream))
     # FMA control and the 32-deep tensor-core variant at the headline shape
     m = n = k = 8192
     g = torch.Generator(device="cuda").manual_seed(7)
     a = torch.rand(m, k, device="cuda", generator=g) * 2 - 1
     b = torch.rand(k, n, device="cuda", generator=g) * 2 - 1
     c = torch.empty(m, n, device="cuda")
-    for variant, label, iters in ((R.SGEMM_FMA, "sgemm_fma_control", 3), (R.SGEMM_TC_BK32, "sgemm_3xtf32_bk32", 5),
+    for variant, label, iters in ((R.SGEMM_FMA, "sgemm_fma_control", 3), (R.SGEMM_TC_BK16, "sgemm_3xtf32_bk16", 5),
+                                  (R.SGEMM_TC_BK32, "sgemm_3xtf32_bk32", 5),
                                   (R.SGEMM_TC_PAIR16, "sgemm_3xtf32_pair16", 5),
-                                  (R.SGEMM_TC_PAIR32, "sgemm_3xtf32_pair32", 5)):
+                                  (R.SGEMM_TC_PAIR32, "sgemm_3xtf32_pair32", 5),
+                                  (R.SGEMM_TC_INSM16, "sgemm_3xtf32_insm16", 5),
+                                  (R.SGEMM_TC_INSM32, "sgemm_3xtf32_insm32", 5)):
         rt.sgemm_device(a, b, c, m, n, k, variant, stream)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -738,6 +855,7 @@ def run_ours(args) -> None:
             cpu = cpu_sgemm_sample(m, n, k, args.cpu_seconds, O.max_threads())
             cpu.pop("seconds", None)
             cpu.pop("rows", None)
+            cpu["reference_paths"] = cpu_baseline_table(O.max_threads())
 
     if rank == 0:
         line = {
@@ -757,16 +875,20 @@ def run_ours(args) -> None:
                 "workload": (f"sgemm {m}x{n}x{k} per rank: independent products, A and B seeded per rank, no data "
                              "exchange (weak scaling); the column-parallel product with replicated A and the "
                              "gathered C is the sgemm_tp secondary lines (strong scaling)"),
-                "m": m, "n_per_rank": n, "k": k, "variant": ("tcgen05 3xTF32" + (" CTA pair" if args.variant in (216, 232) else ""))
-                if args.variant in (1, 16, 32, 216, 232) else "fp32 FMA",
-                "stage_depth_k": args.variant % 100 if args.variant in (16, 32, 216, 232) else None,
+                "m": m, "n_per_rank": n, "k": k,
+                "variant": ("tcgen05 3xTF32" + (" CTA pair" if args.variant in (216, 232, 316, 332) else "")
+                            + (", TF32 split inside the kernel" if args.variant in (316, 332) else ", split pass"))
+                if args.variant in (1, 16, 32, 216, 232, 316, 332) else "fp32 FMA",
+                "stage_depth_k": args.variant % 100 if args.variant in (16, 32, 216, 232, 316, 332) else None,
                 "parallelism": f"independent replicas x{world}",
                 "l2": "no flush: every operand (256 MiB) exceeds the 126 MB L2",
                 "input": "U[-1,1) fp32, seeded per rank",
             },
             "roofline": {
                 "bound": "tensor",
-                "kernel": "sgemm3x_kernel (tcgen05 kind::tf32, 3 products per k-step)",
+                "kernel": ("sgemm3x_insm_kernel" if args.variant in (316, 332) else
+                           "sgemm3x_pair_kernel" if args.variant in (216, 232) else "sgemm3x_kernel")
+                          + " (tcgen05 kind::tf32, 3 products per k-step)",
                 "achieved": achieved,
                 "peak": tensor_peak,
                 "unit": "TFLOP/s",
@@ -783,7 +905,8 @@ def run_ours(args) -> None:
             },
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "gpu_launches": (1 if args.variant == 2 else 3) * args.steps,  # FMA: one kernel; TC: 2 splits + main
+            # FMA and the in-kernel split: one kernel per step; the others: 2 split passes + main
+            "gpu_launches": (1 if args.variant in (2, 316, 332) else 3) * args.steps,
             "clocks": clock_rec,
             "secondary": secondary,
         }

@@ -1465,6 +1465,10 @@ enum {
   OCT_B200_SGEMM_TC_BK32 = 32u,   /* tensor cores, one CTA per 128x256 tile, 32-deep K stages */
   OCT_B200_SGEMM_TC_PAIR16 = 216u, /* tensor cores, CTA pair (cta_group::2) per 256x256 tile, 16-deep */
   OCT_B200_SGEMM_TC_PAIR32 = 232u, /* CTA pair, 32-deep K stages */
+  OCT_B200_SGEMM_TC_INSM16 = 316u, /* CTA pair, TF32 split inside the kernel from A and B in place (no split
+                                      pass); needs 16-byte aligned A / B and lda, ldb multiples of 4, else
+                                      runs as OCT_B200_SGEMM_TC_PAIR16 */
+  OCT_B200_SGEMM_TC_INSM32 = 332u, /* the same with 32-deep K stages (else as OCT_B200_SGEMM_TC_PAIR32) */
 };
 
 /* C = A * B on device pointers (row-major, ld = k / n / n), enqueued on

@@ -49,7 +49,10 @@ struct GemmBatch {
 
 // Tensor-core kernel configurations: one CTA per 128 x 256 tile, or a CTA pair
 // (cta_group::2) per 256 x 256 tile; 16 or 32 K elements per pipeline stage.
-enum TcConfig : int { kTcSingle16 = 16, kTcSingle32 = 32, kTcPair16 = 216, kTcPair32 = 232 };
+enum TcConfig : int {
+  kTcSingle16 = 16, kTcSingle32 = 32, kTcPair16 = 216, kTcPair32 = 232,
+  kTcInsm16 = 316, kTcInsm32 = 332,  // CTA pair, TF32 split inside the kernel (no split pass)
+};
 
 // 3xTF32 tensor-core SGEMM.  `scratch` must hold sgemm_tc_scratch_bytes and be
 // 1024-byte aligned.  bk is a TcConfig.
@@ -61,6 +64,14 @@ struct SgemmEvents {
 cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
                      uint32_t m, uint32_t n, uint32_t k, void* scratch, unsigned int* err, int bk,
                      cudaStream_t stream, const SgemmEvents* events = nullptr, const GemmBatch* batch = nullptr);
+// The in-SM split kernel reads A and B in place with TMA: single products whose
+// bases are 16-byte aligned and whose leading dimensions are multiples of 4.
+// It needs no scratch; C = R + A * B when `residual` is given.
+bool sgemm_insm_eligible(const float* a, uint64_t lda, const float* b, uint64_t ldb, uint32_t m, uint32_t n,
+                         uint32_t k, const GemmBatch* batch);
+cudaError_t sgemm_tc_insm(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
+                          uint32_t m, uint32_t n, uint32_t k, unsigned int* err, int bk, cudaStream_t stream,
+                          const SgemmEvents* events = nullptr, const float* residual = nullptr, uint64_t ldr = 0);
 
 // Pre-split weights: sgemm_tc_split_b writes the hi/lo K-major layout of a
 // [k][n] operand (split_b_elems floats each); sgemm_tc_presplit then computes

@@ -90,6 +90,54 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// As mbar_wait, with cluster-scope acquire: for barriers that CTAs of the cluster
+// arrive on remotely after writing shared memory the waiter's consumers read.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, unsigned int* err,
+                                                  unsigned int err_bit) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long start = global_timer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((++spins & 255u) == 0u) {
+      if (global_timer_ns() - start > kWaitBudgetNs) {
+        atomicOr(err, err_bit);
+        return false;
+      }
+    }
+  }
+}
+
+// Named barrier over `count` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// Named barrier that also returns the AND of every participant's `pred`, so a
+// group of warps takes one decision together.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // Waits until the grids this one depends on (the previous kernel in the stream,
 // when this one was launched with programmatic stream serialization) have

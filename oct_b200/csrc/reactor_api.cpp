@@ -81,7 +81,7 @@ bool known_variant(uint32_t v) {
   return v == OCT_B200_SGEMM_AUTO || v == OCT_B200_SGEMM_TC3XTF32 || v == OCT_B200_SGEMM_FMA ||
          v == OCT_B200_SGEMM_SMALLM ||
          v == OCT_B200_SGEMM_TC_BK16 || v == OCT_B200_SGEMM_TC_BK32 || v == OCT_B200_SGEMM_TC_PAIR16 ||
-         v == OCT_B200_SGEMM_TC_PAIR32;
+         v == OCT_B200_SGEMM_TC_PAIR32 || v == OCT_B200_SGEMM_TC_INSM16 || v == OCT_B200_SGEMM_TC_INSM32;
 }
 
 // The kernel a variant id runs for (m, n, k): AUTO picks the small-M kernel for
@@ -116,15 +116,22 @@ int oct::rt::enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const floa
                           rt->err_word());
   } else if (variant == OCT_B200_SGEMM_FMA) {
     e = oct::sgemm_fma(a, lda, b, ldb, c, ldc, m, n, k, stream, batch);
-  } else if (variant == OCT_B200_SGEMM_TC3XTF32 || variant == 16u || variant == 32u || variant == 216u ||
-             variant == 232u) {
-    const uint64_t need = oct::sgemm_tc_scratch_bytes(m, n, k, batch != nullptr ? batch->count : 1u);
-    e = scratch->ensure(need, stream);
-    if (e != cudaSuccess) return OCT_B200_DETAIL_OUT_OF_MEMORY;
+  } else if (variant == OCT_B200_SGEMM_TC3XTF32 || variant == OCT_B200_SGEMM_TC_BK16 ||
+             variant == OCT_B200_SGEMM_TC_BK32 || variant == OCT_B200_SGEMM_TC_PAIR16 ||
+             variant == OCT_B200_SGEMM_TC_PAIR32 || variant == OCT_B200_SGEMM_TC_INSM16 ||
+             variant == OCT_B200_SGEMM_TC_INSM32) {
     const int bk = variant == OCT_B200_SGEMM_TC3XTF32 ? oct::kTcSingle16 : static_cast<int>(variant);
+    const bool insm = (bk == oct::kTcInsm16 || bk == oct::kTcInsm32) &&
+                      oct::sgemm_insm_eligible(a, lda, b, ldb, m, n, k, batch);
+    if (!insm) {  // the in-SM split kernel needs no split scratch
+      const uint64_t need = oct::sgemm_tc_scratch_bytes(m, n, k, batch != nullptr ? batch->count : 1u);
+      e = scratch->ensure(need, stream);
+      if (e != cudaSuccess) return OCT_B200_DETAIL_OUT_OF_MEMORY;
+    }
     const oct::SgemmEvents* ev = nullptr;
     if (rt->timing && (ev = next_timing_events(rt)) == nullptr) return OCT_B200_DETAIL_CUDA_ERROR;
-    e = oct::sgemm_tc(a, lda, b, ldb, c, ldc, m, n, k, scratch->aligned(), rt->err_word(), bk, stream, ev, batch);
+    e = oct::sgemm_tc(a, lda, b, ldb, c, ldc, m, n, k, insm ? nullptr : scratch->aligned(), rt->err_word(), bk,
+                      stream, ev, batch);
   } else {
     return OCT_B200_DETAIL_BAD_VARIANT;
   }

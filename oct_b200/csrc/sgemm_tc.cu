@@ -653,6 +653,314 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------ in-SM split, CTA pair
+// The CTA-pair product with the TF32 split done inside the kernel, so no split
+// pass runs and HBM carries each operand once, in fp32, straight from the
+// caller's row-major A and B:
+//   * each CTA's TMA loads its raw A rows [128][BK] (K-major, swizzled as the
+//     MMA reads them) into the stage's A_hi slot, and its raw B rows
+//     [BK][128] (B is N-major) unswizzled into the B_lo slot, counting the
+//     bytes on the CTA's own `raw_full` barrier; the TMA zero-fills every
+//     element past m, n or k, so ragged edges need no padding;
+//   * two converter warps per CTA split A in place (A_hi <- tf32(a),
+//     A_lo <- tf32(a - A_hi), elementwise: both slots share one layout) and
+//     transpose B into the K-major swizzled B_hi / B_lo slots (all of the
+//     stage's B is read into registers first, then written over the staging
+//     copy), make the writes visible to the tensor core (fence.proxy.async)
+//     and arrive on the leader's `full` barrier;
+//   * the leader issues the same three tcgen05.mma.cta_group::2 per 8-deep k
+//     step as sgemm3x_pair_kernel; accumulation and epilogue are unchanged.
+// 12 warps: producer, MMA issuer, two converters, eight epilogue warps.
+constexpr int INSM_THREADS = 384;
+constexpr uint32_t INSM_CONV_WARPS = 2;
+constexpr uint32_t INSM_EPI_WARP0 = 4;
+
+template <int BK>
+struct InsmCfg {
+  static constexpr uint32_t SWZ = BK * 4;
+  static constexpr uint32_t A_BYTES = PAIR_HALF * BK * 4;
+  static constexpr uint32_t B_BYTES = PAIR_HALF * BK * 4;
+  static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+  static constexpr uint32_t STAGES = (BK == 16) ? 6 : 3;
+  static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+};
+
+// Byte offset of the 16-byte granule `g` of K-major row `r` in a tile whose
+// rows are `swz` bytes long, under the TMA / UMMA swizzle of that span
+// (granule index XOR the row bits above the span: 64 B: (r / 2) % 4, 128 B: r % 8).
+template <uint32_t SWZ>
+__device__ __forceinline__ uint32_t swizzled_offset(uint32_t r, uint32_t g) {
+  if constexpr (SWZ == 128u) {
+    return r * 128u + ((g ^ (r & 7u)) << 4);
+  } else {
+    return r * 64u + ((g ^ ((r >> 1) & 3u)) << 4);
+  }
+}
+
+template <int BK>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
+    sgemm3x_insm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                        float* __restrict__ c, uint32_t m, uint32_t n, uint64_t ldc, uint32_t num_kb,
+                        uint32_t tiles_m, uint32_t tiles_n, const float* __restrict__ residual, uint64_t ldr,
+                        unsigned int* __restrict__ err) {
+  using Cfg = InsmCfg<BK>;
+  constexpr uint32_t S = Cfg::STAGES;
+  constexpr uint32_t KBC = KC / BK;
+  constexpr uint32_t IDESC = umma_idesc_tf32(PAIR_BM, BN);
+  constexpr uint16_t PAIR_MASK = 0x3;
+  constexpr uint32_t CONV_THREADS = INSM_CONV_WARPS * 32;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t raw_full[S];
+  __shared__ __align__(8) uint64_t full_bar[S];
+  __shared__ __align__(8) uint64_t empty_bar[S];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ uint32_t aborted;
+  __shared__ uint32_t issued_kb;
+  __shared__ uint32_t converted_kb[INSM_CONV_WARPS];
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_cta_rank();  // 0 = leader
+  const uint32_t num_chunks = (num_kb + KBC - 1) / KBC;
+
+  const uint32_t t = blockIdx.x >> 1;
+  const uint32_t per_group = GROUP_M * tiles_n;
+  const uint32_t first_m = (t / per_group) * GROUP_M;
+  const uint32_t group_rows = min(tiles_m - first_m, GROUP_M);
+  const uint32_t tile_m = first_m + (t % per_group) % group_rows;
+  const uint32_t tile_n = (t % per_group) / group_rows;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < S; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&full_bar[s], 2 * INSM_CONV_WARPS);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (uint32_t b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * NUM_EPI_WARPS);
+    }
+    mbar_init(&drain_bar, 1);
+    aborted = 0;
+    issued_kb = 0;
+    for (uint32_t w = 0; w < INSM_CONV_WARPS; ++w) converted_kb[w] = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    prefetch_tensormap(&tm_a);
+    prefetch_tensormap(&tm_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (each CTA, its own barrier)
+      const int row_a = static_cast<int>(tile_m * PAIR_BM + rank * PAIR_HALF);
+      const int col_b = static_cast<int>(tile_n * BN + rank * PAIR_HALF);
+      for (uint32_t kb = 0; kb < num_kb; ++kb) {
+        const uint32_t s = kb % S;
+        if (kb >= S) {
+          if (!mbar_wait(&empty_bar[s], ((kb / S) - 1) & 1u, err, kErrWaitEmpty)) {
+            atomicExch(&aborted, 1u);
+            break;
+          }
+        }
+        if (*(volatile uint32_t*)&aborted != 0u) break;
+        uint8_t* st = smem + s * Cfg::STAGE_BYTES;
+        const int kx = static_cast<int>(kb * BK);
+        mbar_arrive_expect_tx(&raw_full[s], Cfg::A_BYTES + Cfg::B_BYTES);
+        tma_load_2d(st, &tm_a, &raw_full[s], kx, row_a);
+        tma_load_2d(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tm_b, &raw_full[s], col_b, kx);
+        *(volatile uint32_t*)&issued_kb = kb + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (leader CTA only)
+      for (uint32_t kb = 0; kb < num_kb; ++kb) {
+        const uint32_t chunk = kb / KBC, in_chunk = kb % KBC;
+        const uint32_t buf = chunk & 1u;
+        if (in_chunk == 0 && chunk >= 2) {
+          if (!mbar_wait(&acc_empty[buf], ((chunk >> 1) - 1) & 1u, err, kErrWaitAccum)) {
+            atomicExch(&aborted, 1u);
+            break;
+          }
+          tc_fence_after();
+        }
+        const uint32_t s = kb % S;
+        if (!mbar_wait_cluster(&full_bar[s], (kb / S) & 1u, err, kErrWaitFull)) {
+          atomicExch(&aborted, 1u);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        const uint32_t base = smem_addr(smem + s * Cfg::STAGE_BYTES);
+        const uint32_t a_hi = base, a_lo = base + Cfg::A_BYTES;
+        const uint32_t b_hi = base + 2 * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
+#pragma unroll
+        for (uint32_t kk = 0; kk < BK / 8; ++kk) {
+          const uint32_t off = kk * 32;
+          const uint64_t dah = umma_desc_kmajor(a_hi + off, Cfg::SWZ);
+          const uint64_t dal = umma_desc_kmajor(a_lo + off, Cfg::SWZ);
+          const uint64_t dbh = umma_desc_kmajor(b_hi + off, Cfg::SWZ);
+          const uint64_t dbl = umma_desc_kmajor(b_lo + off, Cfg::SWZ);
+          umma_tf32_pair(d_tmem, dal, dbh, IDESC, (in_chunk | kk) != 0u ? 1u : 0u);
+          umma_tf32_pair(d_tmem, dah, dbl, IDESC, 1u);
+          umma_tf32_pair(d_tmem, dah, dbh, IDESC, 1u);
+        }
+        umma_commit_pair_mc(&empty_bar[s], PAIR_MASK);
+        if (in_chunk == KBC - 1 || kb == num_kb - 1) umma_commit_pair_mc(&acc_full[buf], PAIR_MASK);
+      }
+      umma_commit_pair_mc(&drain_bar, PAIR_MASK);
+    }
+  } else if (warp < INSM_EPI_WARP0) {
+    // ---------------- converters (each CTA): split A in place, transpose + split B
+    const uint32_t ct = threadIdx.x - 64u;  // 0 .. CONV_THREADS - 1
+    const uint32_t cw = warp - 2u;
+    constexpr uint32_t COLS = PAIR_HALF / CONV_THREADS;  // B columns (rows of B^T) per thread
+    for (uint32_t kb = 0; kb < num_kb; ++kb) {
+      const uint32_t s = kb % S;
+      const bool mine = mbar_wait(&raw_full[s], (kb / S) & 1u, err, kErrWaitFull) &&
+                        *(volatile uint32_t*)&aborted == 0u;
+      // both converter warps continue or stop together (they meet at a barrier below)
+      if (!named_bar_and(2, CONV_THREADS, mine)) {
+        if (lane == 0) atomicExch(&aborted, 1u);
+        break;
+      }
+      uint8_t* st = smem + s * Cfg::STAGE_BYTES;
+      float4* ahi = reinterpret_cast<float4*>(st);
+      float4* alo = reinterpret_cast<float4*>(st + Cfg::A_BYTES);
+#pragma unroll 4
+      for (uint32_t i = ct; i < Cfg::A_BYTES / 16; i += CONV_THREADS) {
+        const float4 v = ahi[i];
+        float4 h, l;
+        h.x = to_tf32(v.x); h.y = to_tf32(v.y); h.z = to_tf32(v.z); h.w = to_tf32(v.w);
+        l.x = to_tf32(v.x - h.x); l.y = to_tf32(v.y - h.y); l.z = to_tf32(v.z - h.z); l.w = to_tf32(v.w - h.w);
+        ahi[i] = h;
+        alo[i] = l;
+      }
+      uint8_t* bhi = st + 2 * Cfg::A_BYTES;
+      uint8_t* blo = bhi + Cfg::B_BYTES;
+      const float* stage_b = reinterpret_cast<const float*>(blo);  // raw B [BK][128]
+      float v[COLS][BK];
+#pragma unroll
+      for (uint32_t cc = 0; cc < COLS; ++cc)
+#pragma unroll
+        for (uint32_t kk = 0; kk < BK; ++kk) v[cc][kk] = stage_b[kk * PAIR_HALF + ct + cc * CONV_THREADS];
+      named_bar_sync(3, CONV_THREADS);  // every converter has read the staging copy
+#pragma unroll
+      for (uint32_t cc = 0; cc < COLS; ++cc) {
+        const uint32_t r = ct + cc * CONV_THREADS;  // row of B^T (column of B)
+#pragma unroll
+        for (uint32_t g = 0; g < BK / 4; ++g) {
+          float4 h, l;
+          h.x = to_tf32(v[cc][4 * g + 0]); h.y = to_tf32(v[cc][4 * g + 1]);
+          h.z = to_tf32(v[cc][4 * g + 2]); h.w = to_tf32(v[cc][4 * g + 3]);
+          l.x = to_tf32(v[cc][4 * g + 0] - h.x); l.y = to_tf32(v[cc][4 * g + 1] - h.y);
+          l.z = to_tf32(v[cc][4 * g + 2] - h.z); l.w = to_tf32(v[cc][4 * g + 3] - h.w);
+          const uint32_t off = swizzled_offset<Cfg::SWZ>(r, g);
+          *reinterpret_cast<float4*>(bhi + off) = h;
+          *reinterpret_cast<float4*>(blo + off) = l;
+        }
+      }
+      fence_proxy_async_smem();  // the generic-proxy writes, visible to the tensor core
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_cluster(&full_bar[s], 0);
+        *(volatile uint32_t*)&converted_kb[cw] = kb + 1;
+      }
+    }
+  } else {
+    // ---------------- epilogue: warps 4..11 of both CTAs, each on its own TMEM half
+    const uint32_t q = warp & 3u;
+    const uint32_t h = (warp - INSM_EPI_WARP0) >> 2;
+    const uint32_t lane_addr = (q * 32u) << 16;
+    float run[128];
+#pragma unroll
+    for (int j = 0; j < 128; ++j) run[j] = 0.f;
+    bool ok = true;
+    for (uint32_t ch = 0; ch < num_chunks; ++ch) {
+      const uint32_t buf = ch & 1u;
+      ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (ch >> 1) & 1u, err, kErrWaitAccum));
+      if (!ok) {
+        if (lane == 0) atomicExch(&aborted, 1u);
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (uint32_t g = 0; g < 4; ++g) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + buf * BN + h * 128u + g * 32u, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) run[g * 32 + j] += __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(&acc_empty[buf], 0);
+    }
+    if (ok && num_kb > 0) {
+      const uint32_t row = tile_m * PAIR_BM + rank * PAIR_HALF + q * 32 + lane;
+      const uint32_t col0 = tile_n * BN + h * 128u;
+      const bool vec_ok = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) &&
+                          (residual == nullptr ||
+                           ((ldr % 4 == 0) && ((reinterpret_cast<uintptr_t>(residual) & 15u) == 0)));
+      if (row < m && col0 < n) {
+        float* dst = c + static_cast<uint64_t>(row) * ldc + col0;
+        const float* src = residual != nullptr ? residual + static_cast<uint64_t>(row) * ldr + col0 : nullptr;
+        if (vec_ok && col0 + 128 <= n) {
+#pragma unroll
+          for (int j = 0; j < 128; j += 4) {
+            float4 o = make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
+            if (src != nullptr) {
+              const float4 r4 = *reinterpret_cast<const float4*>(src + j);
+              o.x += r4.x;
+              o.y += r4.y;
+              o.z += r4.z;
+              o.w += r4.w;
+            }
+            *reinterpret_cast<float4*>(dst + j) = o;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 128; ++j)
+            if (col0 + j < n) dst[j] = src != nullptr ? src[j] + run[j] : run[j];
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  // Teardown.  The leader's last commit (multicast) tells both CTAs that every
+  // pair MMA finished.  A CTA that aborted first waits (bounded) for its own
+  // TMA copies still in flight: those the converters never consumed.
+  if (threadIdx.x == 32) mbar_wait(&drain_bar, 0, err, kErrWaitDrain);
+  if (aborted && threadIdx.x == 0) {
+    uint32_t done = converted_kb[0];
+    for (uint32_t w = 1; w < INSM_CONV_WARPS; ++w) done = min(done, converted_kb[w]);
+    for (uint32_t kb = done; kb < issued_kb; ++kb)
+      if (!mbar_wait(&raw_full[kb % S], (kb / S) & 1u, err, kErrWaitDrain)) break;
+  }
+  __syncthreads();
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while the leader's MMAs could still read its shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 // K-major fp32 operand [rows x kp]; box = [bk x box_rows] with a bk*4-byte swizzle.
 bool make_operand_map(CUtensorMap* map, const float* base, uint32_t rows, uint32_t kp, uint32_t bk,
@@ -694,6 +1002,45 @@ cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, co
   sgemm3x_kernel<BK><<<static_cast<uint32_t>(grid), NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(
       m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, d.mp, d.np, stride_c, residual, ldr,
       err, sc);
+  return cudaGetLastError();
+}
+
+// Row-major fp32 matrix [rows][ld] read in place by TMA: box = [box_x x box_y]
+// (x innermost), `swz`-byte swizzle (0 = none).  Elements past cols / rows read as 0.
+bool make_inplace_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, uint64_t ld,
+                      uint32_t box_x, uint32_t box_y, uint32_t swz) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * 4};
+  const cuuint32_t box[2] = {box_x, box_y};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = swz == 128u  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swz == 64u ? CU_TENSOR_MAP_SWIZZLE_64B
+                                             : CU_TENSOR_MAP_SWIZZLE_NONE;
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BK>
+cudaError_t launch_insm(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
+                        uint32_t m, uint32_t n, uint32_t k, unsigned int* err, cudaStream_t stream,
+                        const float* residual, uint64_t ldr) {
+  using Cfg = InsmCfg<BK>;
+  CUtensorMap m_a, m_b;
+  if (!make_inplace_map(&m_a, a, k, m, lda, BK, PAIR_HALF, Cfg::SWZ) ||
+      !make_inplace_map(&m_b, b, n, k, ldb, PAIR_HALF, BK, 0))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(sgemm3x_insm_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(Cfg::SMEM_BYTES));
+  if (e != cudaSuccess) return e;
+  const uint32_t tiles_m = (m + PAIR_BM - 1) / PAIR_BM, tiles_n = (n + BN - 1) / BN;
+  const uint64_t grid = 2ull * tiles_m * tiles_n;
+  if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
+  const uint32_t num_kb = (k + BK - 1) / BK;
+  sgemm3x_insm_kernel<BK><<<static_cast<uint32_t>(grid), INSM_THREADS, Cfg::SMEM_BYTES, stream>>>(
+      m_a, m_b, c, m, n, ldc, num_kb, tiles_m, tiles_n, residual, ldr, err);
   return cudaGetLastError();
 }
 
@@ -877,10 +1224,36 @@ uint64_t sgemm_tc_scratch_bytes(uint32_t m, uint32_t n, uint32_t k, uint32_t bat
          (static_cast<uint64_t>(d.mp) * d.kp + static_cast<uint64_t>(d.np) * d.kp);
 }
 
+bool sgemm_insm_eligible(const float* a, uint64_t lda, const float* b, uint64_t ldb, uint32_t m, uint32_t n,
+                         uint32_t k, const GemmBatch* batch) {
+  if (batch != nullptr && (batch->count > 1 || batch->b_trans)) return false;
+  return m > 0 && n > 0 && k > 0 && lda % 4 == 0 && ldb % 4 == 0 &&
+         (reinterpret_cast<uintptr_t>(a) & 15u) == 0 && (reinterpret_cast<uintptr_t>(b) & 15u) == 0 &&
+         lda < (1ull << 37) && ldb < (1ull << 37);
+}
+
+cudaError_t sgemm_tc_insm(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
+                          uint32_t m, uint32_t n, uint32_t k, unsigned int* err, int bk, cudaStream_t stream,
+                          const SgemmEvents* events, const float* residual, uint64_t ldr) {
+  if (m == 0 || n == 0 || k == 0) return cudaSuccess;
+  if (!sgemm_insm_eligible(a, lda, b, ldb, m, n, k, nullptr)) return cudaErrorInvalidValue;
+  if (events != nullptr && events->split_begin != nullptr) cudaEventRecord(events->split_begin, stream);
+  if (events != nullptr && events->main_begin != nullptr) cudaEventRecord(events->main_begin, stream);
+  const cudaError_t e = bk == kTcInsm32 ? launch_insm<32>(a, lda, b, ldb, c, ldc, m, n, k, err, stream, residual, ldr)
+                                        : launch_insm<16>(a, lda, b, ldb, c, ldc, m, n, k, err, stream, residual, ldr);
+  if (events != nullptr && events->main_end != nullptr) cudaEventRecord(events->main_end, stream);
+  return e;
+}
+
 cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
                      uint32_t m, uint32_t n, uint32_t k, void* scratch, unsigned int* err, int bk,
                      cudaStream_t stream, const SgemmEvents* events, const GemmBatch* batch) {
   if (m == 0 || n == 0 || k == 0) return cudaSuccess;
+  if (bk == kTcInsm16 || bk == kTcInsm32) {
+    if (sgemm_insm_eligible(a, lda, b, ldb, m, n, k, batch))
+      return sgemm_tc_insm(a, lda, b, ldb, c, ldc, m, n, k, err, bk, stream, events);
+    bk = bk == kTcInsm32 ? kTcPair32 : kTcPair16;  // operands TMA cannot read in place: split pass
+  }
   if (bk != kTcSingle16 && bk != kTcSingle32 && bk != kTcPair16 && bk != kTcPair32) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(scratch) & 1023u) != 0) return cudaErrorInvalidValue;
   const GemmBatch one{};

@@ -69,6 +69,7 @@ FINALIZATION_NONE, FINALIZATION_STABLE_SOFTMAX = 0, 1
 SGEMM_AUTO, SGEMM_TC3XTF32, SGEMM_FMA, SGEMM_SMALLM = 0, 1, 2, 3
 SGEMM_TC_BK16, SGEMM_TC_BK32 = 16, 32  # explicit tensor-core stage depths, one CTA per tile
 SGEMM_TC_PAIR16, SGEMM_TC_PAIR32 = 216, 232  # CTA-pair (cta_group::2) 256x256 tiles
+SGEMM_TC_INSM16, SGEMM_TC_INSM32 = 316, 332  # CTA pair, TF32 split inside the kernel (no split pass)
 
 MAX_STAGES = 8
 

@@ -22,7 +22,8 @@ from tests.golden.make_golden import GEMMA, M20, STARTER
 
 pytestmark = pytest.mark.gpu
 
-VARIANTS = [R.SGEMM_FMA, R.SGEMM_TC_BK16, R.SGEMM_TC_BK32, R.SGEMM_TC_PAIR16, R.SGEMM_TC_PAIR32]
+VARIANTS = [R.SGEMM_FMA, R.SGEMM_TC_BK16, R.SGEMM_TC_BK32, R.SGEMM_TC_PAIR16, R.SGEMM_TC_PAIR32, R.SGEMM_TC_INSM16,
+            R.SGEMM_TC_INSM32]
 NORMWISE_TOL = 1e-5
 
 
@@ -208,7 +209,8 @@ def _checksums(o, c64, a, b, m, n, k):
     assert np.max(np.abs(col_got - col_ref)) <= m * 1e-5 * scale
 
 
-@pytest.mark.parametrize("variant", [R.SGEMM_TC_BK16, R.SGEMM_TC_BK32, R.SGEMM_TC_PAIR16, R.SGEMM_TC_PAIR32])
+@pytest.mark.parametrize("variant", [R.SGEMM_TC_BK16, R.SGEMM_TC_BK32, R.SGEMM_TC_PAIR16, R.SGEMM_TC_PAIR32,
+                                     R.SGEMM_TC_INSM16, R.SGEMM_TC_INSM32])
 @pytest.mark.parametrize("shape,seed", [((8192, 8192, 8192), 3), ((16384, 16384, 4096), 4)])
 def test_baseline_large_shapes(runtime, oracle_mod, shape, seed, variant):
     """8192^3 and 16384^2 x 4096: sampled rows vs fp64 plus whole-matrix checksums."""
@@ -220,6 +222,38 @@ def test_baseline_large_shapes(runtime, oracle_mod, shape, seed, variant):
     for rows in (slice(0, 32), slice(m // 2 - 16, m // 2 + 16), slice(m - 32, m)):
         _check_against_fp64(o, c, a, b, m, n, k, rows=rows)
     _checksums(o, c, a, b, m, n, k)
+
+
+@pytest.mark.parametrize("insm,pair", [(R.SGEMM_TC_INSM16, R.SGEMM_TC_PAIR16), (R.SGEMM_TC_INSM32, R.SGEMM_TC_PAIR32)])
+@pytest.mark.parametrize("shape", [(17, 31, 23), (37, 29, 13), (255, 257, 33), (300, 517, 129), (1000, 1000, 1000),
+                                   (4097, 4095, 1023)])
+def test_in_kernel_split_reads_ragged_operands_in_place(runtime, oracle_mod, shape, insm, pair):
+    """The in-SM split kernel reads A and B where they lie (leading dimensions padded to a
+    multiple of 4 floats, so TMA may read them); the TMA's zero fill past m, n and k replaces
+    the split pass's padding.  The split itself is the split pass's (round to nearest tf32,
+    then the remainder), so the result equals the split-pass CTA-pair kernel bit for bit;
+    columns of C past n stay untouched."""
+    import torch
+    o = oracle_mod
+    m, n, k = shape
+    lda, ldb, ldc = (k + 3) // 4 * 4 + 4, (n + 3) // 4 * 4, n + 3
+    a, b = o.uniform_matrix(m, k, m + 1).ravel(), o.uniform_matrix(k, n, n + 2).ravel()
+    da = torch.zeros((m, lda), device="cuda")
+    db = torch.zeros((k, ldb), device="cuda")
+    da[:, :k] = torch.from_numpy(a.reshape(m, k)).cuda()
+    db[:, :n] = torch.from_numpy(b.reshape(k, n)).cuda()
+    da[:, k:] = float("nan")  # never read: the TMA box stops at k
+    outs = {}
+    for v in (insm, pair):
+        dc = torch.full((m, ldc), -3.0, device="cuda")
+        runtime.sgemm_device(da, db, dc, m, n, k, v, lda=lda, ldb=ldb, ldc=ldc)
+        assert runtime.sync_status().ok
+        outs[v] = dc.cpu().numpy()
+    got = outs[insm]
+    assert np.all(got[:, n:] == -3.0)
+    assert np.array_equal(got[:, :n], outs[pair][:, :n])
+    _check_against_fp64(o, np.ascontiguousarray(got[:, :n]).ravel(), a, b, m, n, k,
+                        rows=slice(0, min(m, 64)))
 
 
 def test_variants_agree_with_batched_and_transposed_forms(runtime, oracle_mod):
