@@ -659,29 +659,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 // caller's row-major A and B:
 //   * each CTA's TMA loads its raw A rows [128][BK] (K-major, swizzled as the
 //     MMA reads them) into the stage's A_hi slot, and its raw B rows
-//     [BK][128] (B is N-major) unswizzled into the B_lo slot, counting the
-//     bytes on the CTA's own `raw_full` barrier; the TMA zero-fills every
+//     [BK][128] (B is N-major) unswizzled into the stage's B_raw slot, counting
+//     the bytes on the CTA's own `raw_full` barrier; the TMA zero-fills every
 //     element past m, n or k, so ragged edges need no padding;
-//   * two converter warps per CTA split A in place (A_hi <- tf32(a),
+//   * six converter warps per CTA split A in place (A_hi <- tf32(a),
 //     A_lo <- tf32(a - A_hi), elementwise: both slots share one layout) and
-//     transpose B into the K-major swizzled B_hi / B_lo slots (all of the
-//     stage's B is read into registers first, then written over the staging
-//     copy), make the writes visible to the tensor core (fence.proxy.async)
-//     and arrive on the leader's `full` barrier;
+//     transpose B from B_raw into the K-major swizzled B_hi / B_lo slots, each
+//     warp on its own share of 16-byte granules, make their writes visible to
+//     the tensor core (fence.proxy.async) and arrive on the leader's `full`
+//     barrier;
 //   * the leader issues the same three tcgen05.mma.cta_group::2 per 8-deep k
 //     step as sgemm3x_pair_kernel; accumulation and epilogue are unchanged.
-// 12 warps: producer, MMA issuer, two converters, eight epilogue warps.
-constexpr int INSM_THREADS = 384;
-constexpr uint32_t INSM_CONV_WARPS = 2;
-constexpr uint32_t INSM_EPI_WARP0 = 4;
+// 16 warps: producer, MMA issuer, six converters, eight epilogue warps.  The
+// epilogue's fp32 running sums need ~170 registers a thread, the other roles
+// few: warpgroups 0-1 give registers back (setmaxnreg.dec) and 2-3 take them
+// (setmaxnreg.inc).  The launcher checks that the launch's register budget
+// covers the split, so the increase can always be granted.
+constexpr int INSM_THREADS = 512;
+constexpr uint32_t INSM_CONV_WARP0 = 2;
+constexpr uint32_t INSM_CONV_WARPS = 6;
+constexpr uint32_t INSM_EPI_WARP0 = 8;
+constexpr uint32_t INSM_REGS_LOW = 64;    // warpgroups 0-1: producer, MMA, converters
+constexpr uint32_t INSM_REGS_HIGH = 184;  // warpgroups 2-3: epilogue
+static_assert(2 * 128 * INSM_REGS_LOW + 2 * 128 * INSM_REGS_HIGH <= 65536, "register split exceeds the SM file");
 
 template <int BK>
 struct InsmCfg {
   static constexpr uint32_t SWZ = BK * 4;
   static constexpr uint32_t A_BYTES = PAIR_HALF * BK * 4;
   static constexpr uint32_t B_BYTES = PAIR_HALF * BK * 4;
-  static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-  static constexpr uint32_t STAGES = (BK == 16) ? 6 : 3;
+  static constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 3 * B_BYTES;  // A hi, A lo, B hi, B lo, B raw
+  static constexpr uint32_t STAGES = (BK == 16) ? 5 : 2;
   static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
 };
 
@@ -695,6 +703,15 @@ __device__ __forceinline__ uint32_t swizzled_offset(uint32_t r, uint32_t g) {
   } else {
     return r * 64u + ((g ^ ((r >> 1) & 3u)) << 4);
   }
+}
+
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 template <int BK>
@@ -761,8 +778,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
   cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
-
-  if (warp == 0) {
+  // Register split: the same setmaxnreg instruction in every warp of a warpgroup,
+  // before the warps branch into their roles.
+  if (warp < INSM_EPI_WARP0) {
+   setmaxnreg_dec<INSM_REGS_LOW>();
+   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer (each CTA, its own barrier)
       const int row_a = static_cast<int>(tile_m * PAIR_BM + rank * PAIR_HALF);
@@ -780,7 +800,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
         const int kx = static_cast<int>(kb * BK);
         mbar_arrive_expect_tx(&raw_full[s], Cfg::A_BYTES + Cfg::B_BYTES);
         tma_load_2d(st, &tm_a, &raw_full[s], kx, row_a);
-        tma_load_2d(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tm_b, &raw_full[s], col_b, kx);
+        tma_load_2d(st + 2 * Cfg::A_BYTES + 2 * Cfg::B_BYTES, &tm_b, &raw_full[s], col_b, kx);
         *(volatile uint32_t*)&issued_kb = kb + 1;
       }
     }
@@ -823,52 +843,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
       }
       umma_commit_pair_mc(&drain_bar, PAIR_MASK);
     }
-  } else if (warp < INSM_EPI_WARP0) {
+  } else {
     // ---------------- converters (each CTA): split A in place, transpose + split B
-    const uint32_t ct = threadIdx.x - 64u;  // 0 .. CONV_THREADS - 1
-    const uint32_t cw = warp - 2u;
-    constexpr uint32_t COLS = PAIR_HALF / CONV_THREADS;  // B columns (rows of B^T) per thread
+    const uint32_t ct = threadIdx.x - INSM_CONV_WARP0 * 32u;  // 0 .. CONV_THREADS - 1
+    const uint32_t cw = warp - INSM_CONV_WARP0;
+    constexpr uint32_t A_ITEMS = Cfg::A_BYTES / 16;          // float4 granules of A
+    constexpr uint32_t B_ITEMS = PAIR_HALF * (BK / 4);       // granules of B^T: (row n, k group g)
     for (uint32_t kb = 0; kb < num_kb; ++kb) {
       const uint32_t s = kb % S;
-      const bool mine = mbar_wait(&raw_full[s], (kb / S) & 1u, err, kErrWaitFull) &&
-                        *(volatile uint32_t*)&aborted == 0u;
-      // both converter warps continue or stop together (they meet at a barrier below)
-      if (!named_bar_and(2, CONV_THREADS, mine)) {
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&raw_full[s], (kb / S) & 1u, err, kErrWaitFull));
+      if (!ok || *(volatile uint32_t*)&aborted != 0u) {
         if (lane == 0) atomicExch(&aborted, 1u);
         break;
       }
       uint8_t* st = smem + s * Cfg::STAGE_BYTES;
       float4* ahi = reinterpret_cast<float4*>(st);
       float4* alo = reinterpret_cast<float4*>(st + Cfg::A_BYTES);
-#pragma unroll 4
-      for (uint32_t i = ct; i < Cfg::A_BYTES / 16; i += CONV_THREADS) {
-        const float4 v = ahi[i];
+      uint8_t* bhi = st + 2 * Cfg::A_BYTES;
+      uint8_t* blo = bhi + Cfg::B_BYTES;
+      const float* braw = reinterpret_cast<const float*>(blo + Cfg::B_BYTES);  // [BK][128]
+      for (uint32_t i = ct; i < A_ITEMS + B_ITEMS; i += CONV_THREADS) {
+        float4 v;
+        if (i < A_ITEMS) {
+          v = ahi[i];
+        } else {
+          const uint32_t j = i - A_ITEMS, r = j & (PAIR_HALF - 1), g = j / PAIR_HALF;
+          const float* src = braw + (4u * g) * PAIR_HALF + r;
+          v = make_float4(src[0], src[PAIR_HALF], src[2 * PAIR_HALF], src[3 * PAIR_HALF]);
+        }
         float4 h, l;
         h.x = to_tf32(v.x); h.y = to_tf32(v.y); h.z = to_tf32(v.z); h.w = to_tf32(v.w);
         l.x = to_tf32(v.x - h.x); l.y = to_tf32(v.y - h.y); l.z = to_tf32(v.z - h.z); l.w = to_tf32(v.w - h.w);
-        ahi[i] = h;
-        alo[i] = l;
-      }
-      uint8_t* bhi = st + 2 * Cfg::A_BYTES;
-      uint8_t* blo = bhi + Cfg::B_BYTES;
-      const float* stage_b = reinterpret_cast<const float*>(blo);  // raw B [BK][128]
-      float v[COLS][BK];
-#pragma unroll
-      for (uint32_t cc = 0; cc < COLS; ++cc)
-#pragma unroll
-        for (uint32_t kk = 0; kk < BK; ++kk) v[cc][kk] = stage_b[kk * PAIR_HALF + ct + cc * CONV_THREADS];
-      named_bar_sync(3, CONV_THREADS);  // every converter has read the staging copy
-#pragma unroll
-      for (uint32_t cc = 0; cc < COLS; ++cc) {
-        const uint32_t r = ct + cc * CONV_THREADS;  // row of B^T (column of B)
-#pragma unroll
-        for (uint32_t g = 0; g < BK / 4; ++g) {
-          float4 h, l;
-          h.x = to_tf32(v[cc][4 * g + 0]); h.y = to_tf32(v[cc][4 * g + 1]);
-          h.z = to_tf32(v[cc][4 * g + 2]); h.w = to_tf32(v[cc][4 * g + 3]);
-          l.x = to_tf32(v[cc][4 * g + 0] - h.x); l.y = to_tf32(v[cc][4 * g + 1] - h.y);
-          l.z = to_tf32(v[cc][4 * g + 2] - h.z); l.w = to_tf32(v[cc][4 * g + 3] - h.w);
-          const uint32_t off = swizzled_offset<Cfg::SWZ>(r, g);
+        if (i < A_ITEMS) {
+          ahi[i] = h;
+          alo[i] = l;
+        } else {
+          const uint32_t j = i - A_ITEMS;
+          const uint32_t off = swizzled_offset<Cfg::SWZ>(j & (PAIR_HALF - 1), j / PAIR_HALF);
           *reinterpret_cast<float4*>(bhi + off) = h;
           *reinterpret_cast<float4*>(blo + off) = l;
         }
@@ -880,8 +891,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
         *(volatile uint32_t*)&converted_kb[cw] = kb + 1;
       }
     }
+  }
   } else {
-    // ---------------- epilogue: warps 4..11 of both CTAs, each on its own TMEM half
+    setmaxnreg_inc<INSM_REGS_HIGH>();
+    // ---------------- epilogue: warps 8..15 of both CTAs, each on its own TMEM half
     const uint32_t q = warp & 3u;
     const uint32_t h = (warp - INSM_EPI_WARP0) >> 2;
     const uint32_t lane_addr = (q * 32u) << 16;
@@ -1023,6 +1036,20 @@ bool make_inplace_map(CUtensorMap* map, const float* base, uint64_t cols, uint64
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// setmaxnreg.inc waits until the registers it asks for are free in the block's
+// launch allocation (threads x registers per thread at launch): the kernel runs
+// only when that allocation covers the whole split.
+template <int BK>
+bool insm_register_split_fits() {
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, sgemm3x_insm_kernel<BK>) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return static_cast<uint64_t>(fa.numRegs) * INSM_THREADS >=
+         2ull * 128 * INSM_REGS_LOW + 2ull * 128 * INSM_REGS_HIGH;
+}
+
 template <int BK>
 cudaError_t launch_insm(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
                         uint32_t m, uint32_t n, uint32_t k, unsigned int* err, cudaStream_t stream,
@@ -1035,6 +1062,7 @@ cudaError_t launch_insm(const float* a, uint64_t lda, const float* b, uint64_t l
   cudaError_t e = cudaFuncSetAttribute(sgemm3x_insm_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(Cfg::SMEM_BYTES));
   if (e != cudaSuccess) return e;
+  if (!insm_register_split_fits<BK>()) return cudaErrorInvalidConfiguration;
   const uint32_t tiles_m = (m + PAIR_BM - 1) / PAIR_BM, tiles_n = (n + BN - 1) / BN;
   const uint64_t grid = 2ull * tiles_m * tiles_n;
   if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
@@ -1227,7 +1255,8 @@ uint64_t sgemm_tc_scratch_bytes(uint32_t m, uint32_t n, uint32_t k, uint32_t bat
 bool sgemm_insm_eligible(const float* a, uint64_t lda, const float* b, uint64_t ldb, uint32_t m, uint32_t n,
                          uint32_t k, const GemmBatch* batch) {
   if (batch != nullptr && (batch->count > 1 || batch->b_trans)) return false;
-  return m > 0 && n > 0 && k > 0 && lda % 4 == 0 && ldb % 4 == 0 &&
+  static const bool regs_ok = insm_register_split_fits<16>() && insm_register_split_fits<32>();
+  return regs_ok && m > 0 && n > 0 && k > 0 && lda % 4 == 0 && ldb % 4 == 0 &&
          (reinterpret_cast<uintptr_t>(a) & 15u) == 0 && (reinterpret_cast<uintptr_t>(b) & 15u) == 0 &&
          lda < (1ull << 37) && ldb < (1ull << 37);
 }
