@@ -662,12 +662,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 //     [BK][128] (B is N-major) unswizzled into the stage's B_raw slot, counting
 //     the bytes on the CTA's own `raw_full` barrier; the TMA zero-fills every
 //     element past m, n or k, so ragged edges need no padding;
-//   * six converter warps per CTA split A in place (A_hi <- tf32(a),
-//     A_lo <- tf32(a - A_hi), elementwise: both slots share one layout) and
-//     transpose B from B_raw into the K-major swizzled B_hi / B_lo slots, each
-//     warp on its own share of 16-byte granules, make their writes visible to
-//     the tensor core (fence.proxy.async) and arrive on the leader's `full`
-//     barrier;
+//   * six converter warps per CTA, each owning whole stages in turn, split A
+//     in place (A_hi <- tf32(a), A_lo <- tf32(a - A_hi), elementwise: both
+//     slots share one layout) and transpose B from B_raw into the K-major
+//     swizzled B_hi / B_lo slots, make the writes visible to the tensor core
+//     (fence.proxy.async) and arrive on the leader's `full` barrier;
 //   * the leader issues the same three tcgen05.mma.cta_group::2 per 8-deep k
 //     step as sgemm3x_pair_kernel; accumulation and epilogue are unchanged.
 // 16 warps: producer, MMA issuer, six converters, eight epilogue warps.  The
@@ -679,8 +678,8 @@ constexpr int INSM_THREADS = 512;
 constexpr uint32_t INSM_CONV_WARP0 = 2;
 constexpr uint32_t INSM_CONV_WARPS = 6;
 constexpr uint32_t INSM_EPI_WARP0 = 8;
-constexpr uint32_t INSM_REGS_LOW = 64;    // warpgroups 0-1: producer, MMA, converters
-constexpr uint32_t INSM_REGS_HIGH = 184;  // warpgroups 2-3: epilogue
+constexpr uint32_t INSM_REGS_LOW = 80;    // warpgroups 0-1: producer, MMA, converters
+constexpr uint32_t INSM_REGS_HIGH = 168;  // warpgroups 2-3: epilogue
 static_assert(2 * 128 * INSM_REGS_LOW + 2 * 128 * INSM_REGS_HIGH <= 65536, "register split exceeds the SM file");
 
 template <int BK>
@@ -725,7 +724,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
   constexpr uint32_t KBC = KC / BK;
   constexpr uint32_t IDESC = umma_idesc_tf32(PAIR_BM, BN);
   constexpr uint16_t PAIR_MASK = 0x3;
-  constexpr uint32_t CONV_THREADS = INSM_CONV_WARPS * 32;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -754,7 +752,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < S; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&full_bar[s], 2 * INSM_CONV_WARPS);
+      mbar_init(&full_bar[s], 2);  // one converter warp in each CTA
       mbar_init(&empty_bar[s], 1);
     }
     for (uint32_t b = 0; b < 2; ++b) {
@@ -764,7 +762,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
     mbar_init(&drain_bar, 1);
     aborted = 0;
     issued_kb = 0;
-    for (uint32_t w = 0; w < INSM_CONV_WARPS; ++w) converted_kb[w] = 0;
+    for (uint32_t w = 0; w < INSM_CONV_WARPS; ++w) converted_kb[w] = w;  // each warp's next stage
     fence_mbar_init();
     fence_proxy_async_smem();
     prefetch_tensormap(&tm_a);
@@ -844,12 +842,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
       umma_commit_pair_mc(&drain_bar, PAIR_MASK);
     }
   } else {
-    // ---------------- converters (each CTA): split A in place, transpose + split B
-    const uint32_t ct = threadIdx.x - INSM_CONV_WARP0 * 32u;  // 0 .. CONV_THREADS - 1
+    // ---------------- converters (each CTA): split A in place, transpose + split B.
+    // Converter warp w takes whole stages kb = w, w + 6, ...: several stages
+    // convert at once, and each warp's proxy fence covers a whole stage.
     const uint32_t cw = warp - INSM_CONV_WARP0;
     constexpr uint32_t A_ITEMS = Cfg::A_BYTES / 16;          // float4 granules of A
     constexpr uint32_t B_ITEMS = PAIR_HALF * (BK / 4);       // granules of B^T: (row n, k group g)
-    for (uint32_t kb = 0; kb < num_kb; ++kb) {
+    for (uint32_t kb = cw; kb < num_kb; kb += INSM_CONV_WARPS) {
       const uint32_t s = kb % S;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&raw_full[s], (kb / S) & 1u, err, kErrWaitFull));
       if (!ok || *(volatile uint32_t*)&aborted != 0u) {
@@ -862,33 +861,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
       uint8_t* bhi = st + 2 * Cfg::A_BYTES;
       uint8_t* blo = bhi + Cfg::B_BYTES;
       const float* braw = reinterpret_cast<const float*>(blo + Cfg::B_BYTES);  // [BK][128]
-      for (uint32_t i = ct; i < A_ITEMS + B_ITEMS; i += CONV_THREADS) {
-        float4 v;
-        if (i < A_ITEMS) {
-          v = ahi[i];
-        } else {
-          const uint32_t j = i - A_ITEMS, r = j & (PAIR_HALF - 1), g = j / PAIR_HALF;
-          const float* src = braw + (4u * g) * PAIR_HALF + r;
-          v = make_float4(src[0], src[PAIR_HALF], src[2 * PAIR_HALF], src[3 * PAIR_HALF]);
-        }
+#pragma unroll 4
+      for (uint32_t i = lane; i < A_ITEMS; i += 32) {
+        const float4 v = ahi[i];
         float4 h, l;
         h.x = to_tf32(v.x); h.y = to_tf32(v.y); h.z = to_tf32(v.z); h.w = to_tf32(v.w);
         l.x = to_tf32(v.x - h.x); l.y = to_tf32(v.y - h.y); l.z = to_tf32(v.z - h.z); l.w = to_tf32(v.w - h.w);
-        if (i < A_ITEMS) {
-          ahi[i] = h;
-          alo[i] = l;
-        } else {
-          const uint32_t j = i - A_ITEMS;
-          const uint32_t off = swizzled_offset<Cfg::SWZ>(j & (PAIR_HALF - 1), j / PAIR_HALF);
-          *reinterpret_cast<float4*>(bhi + off) = h;
-          *reinterpret_cast<float4*>(blo + off) = l;
-        }
+        ahi[i] = h;
+        alo[i] = l;
+      }
+#pragma unroll 4
+      for (uint32_t j = lane; j < B_ITEMS; j += 32) {
+        const uint32_t r = j & (PAIR_HALF - 1), g = j / PAIR_HALF;
+        const float* src = braw + (4u * g) * PAIR_HALF + r;
+        const float4 v = make_float4(src[0], src[PAIR_HALF], src[2 * PAIR_HALF], src[3 * PAIR_HALF]);
+        float4 h, l;
+        h.x = to_tf32(v.x); h.y = to_tf32(v.y); h.z = to_tf32(v.z); h.w = to_tf32(v.w);
+        l.x = to_tf32(v.x - h.x); l.y = to_tf32(v.y - h.y); l.z = to_tf32(v.z - h.z); l.w = to_tf32(v.w - h.w);
+        const uint32_t off = swizzled_offset<Cfg::SWZ>(r, g);
+        *reinterpret_cast<float4*>(bhi + off) = h;
+        *reinterpret_cast<float4*>(blo + off) = l;
       }
       fence_proxy_async_smem();  // the generic-proxy writes, visible to the tensor core
       __syncwarp();
       if (lane == 0) {
         mbar_arrive_cluster(&full_bar[s], 0);
-        *(volatile uint32_t*)&converted_kb[cw] = kb + 1;
+        *(volatile uint32_t*)&converted_kb[cw] = kb + INSM_CONV_WARPS;  // this warp's next stage
       }
     }
   }
@@ -960,7 +958,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
   // TMA copies still in flight: those the converters never consumed.
   if (threadIdx.x == 32) mbar_wait(&drain_bar, 0, err, kErrWaitDrain);
   if (aborted && threadIdx.x == 0) {
-    uint32_t done = converted_kb[0];
+    uint32_t done = converted_kb[0];  // the first stage no converter finished
     for (uint32_t w = 1; w < INSM_CONV_WARPS; ++w) done = min(done, converted_kb[w]);
     for (uint32_t kb = done; kb < issued_kb; ++kb)
       if (!mbar_wait(&raw_full[kb % S], (kb / S) & 1u, err, kErrWaitDrain)) break;
