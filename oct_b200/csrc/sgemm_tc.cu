@@ -662,7 +662,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 //     [BK][128] (B is N-major) unswizzled into the stage's B_raw slot, counting
 //     the bytes on the CTA's own `raw_full` barrier; the TMA zero-fills every
 //     element past m, n or k, so ragged edges need no padding;
-//   * six converter warps per CTA, each owning whole stages in turn, split A
+//   * one converter warp per stage slot (each CTA), owning its slot's stages, split A
 //     in place (A_hi <- tf32(a), A_lo <- tf32(a - A_hi), elementwise: both
 //     slots share one layout) and transpose B from B_raw into the K-major
 //     swizzled B_hi / B_lo slots, make the writes visible to the tensor core
@@ -762,7 +762,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
     mbar_init(&drain_bar, 1);
     aborted = 0;
     issued_kb = 0;
-    for (uint32_t w = 0; w < INSM_CONV_WARPS; ++w) converted_kb[w] = w;  // each warp's next stage
+    for (uint32_t w = 0; w < INSM_CONV_WARPS; ++w) converted_kb[w] = w < S ? w : 0xFFFFFFFFu;  // next stage
     fence_mbar_init();
     fence_proxy_async_smem();
     prefetch_tensormap(&tm_a);
@@ -843,12 +843,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
     }
   } else {
     // ---------------- converters (each CTA): split A in place, transpose + split B.
-    // Converter warp w takes whole stages kb = w, w + 6, ...: several stages
-    // convert at once, and each warp's proxy fence covers a whole stage.
+    // Converter warp w owns stage slot w (one warp per slot, S <= 6): it takes
+    // stages kb = w, w + S, ..., so several stages convert at once, each warp's
+    // proxy fence covers a whole stage, and a warp only ever waits for the next
+    // phase of its own slot's barrier (a parity wait further ahead would pass
+    // at once).
     const uint32_t cw = warp - INSM_CONV_WARP0;
     constexpr uint32_t A_ITEMS = Cfg::A_BYTES / 16;          // float4 granules of A
     constexpr uint32_t B_ITEMS = PAIR_HALF * (BK / 4);       // granules of B^T: (row n, k group g)
-    for (uint32_t kb = cw; kb < num_kb; kb += INSM_CONV_WARPS) {
+    static_assert(S <= INSM_CONV_WARPS, "one converter warp per stage slot");
+    for (uint32_t kb = cw; cw < S && kb < num_kb; kb += S) {
       const uint32_t s = kb % S;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&raw_full[s], (kb / S) & 1u, err, kErrWaitFull));
       if (!ok || *(volatile uint32_t*)&aborted != 0u) {
@@ -886,7 +890,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive_cluster(&full_bar[s], 0);
-        *(volatile uint32_t*)&converted_kb[cw] = kb + INSM_CONV_WARPS;  // this warp's next stage
+        *(volatile uint32_t*)&converted_kb[cw] = kb + S;  // this warp's next stage
       }
     }
   }
