@@ -865,26 +865,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(INSM_THREADS, 1)
       uint8_t* bhi = st + 2 * Cfg::A_BYTES;
       uint8_t* blo = bhi + Cfg::B_BYTES;
       const float* braw = reinterpret_cast<const float*>(blo + Cfg::B_BYTES);  // [BK][128]
-#pragma unroll 4
-      for (uint32_t i = lane; i < A_ITEMS; i += 32) {
-        const float4 v = ahi[i];
-        float4 h, l;
-        h.x = to_tf32(v.x); h.y = to_tf32(v.y); h.z = to_tf32(v.z); h.w = to_tf32(v.w);
-        l.x = to_tf32(v.x - h.x); l.y = to_tf32(v.y - h.y); l.z = to_tf32(v.z - h.z); l.w = to_tf32(v.w - h.w);
-        ahi[i] = h;
-        alo[i] = l;
+      // Batches of 8 granules per lane: all loads of a batch are issued before any
+      // store (the compiler cannot tell the staging reads from the operand writes).
+      constexpr uint32_t BATCH = 8;
+      static_assert((A_ITEMS / 32) % BATCH == 0 && (B_ITEMS / 32) % BATCH == 0, "batches tile the stage");
+#pragma unroll 1
+      for (uint32_t i0 = 0; i0 < A_ITEMS; i0 += 32 * BATCH) {
+        float4 v[BATCH];
+#pragma unroll
+        for (uint32_t u = 0; u < BATCH; ++u) v[u] = ahi[i0 + lane + 32 * u];
+#pragma unroll
+        for (uint32_t u = 0; u < BATCH; ++u) {
+          float4 h, l;
+          h.x = to_tf32(v[u].x); h.y = to_tf32(v[u].y); h.z = to_tf32(v[u].z); h.w = to_tf32(v[u].w);
+          l.x = to_tf32(v[u].x - h.x); l.y = to_tf32(v[u].y - h.y);
+          l.z = to_tf32(v[u].z - h.z); l.w = to_tf32(v[u].w - h.w);
+          ahi[i0 + lane + 32 * u] = h;
+          alo[i0 + lane + 32 * u] = l;
+        }
       }
-#pragma unroll 4
-      for (uint32_t j = lane; j < B_ITEMS; j += 32) {
-        const uint32_t r = j & (PAIR_HALF - 1), g = j / PAIR_HALF;
-        const float* src = braw + (4u * g) * PAIR_HALF + r;
-        const float4 v = make_float4(src[0], src[PAIR_HALF], src[2 * PAIR_HALF], src[3 * PAIR_HALF]);
-        float4 h, l;
-        h.x = to_tf32(v.x); h.y = to_tf32(v.y); h.z = to_tf32(v.z); h.w = to_tf32(v.w);
-        l.x = to_tf32(v.x - h.x); l.y = to_tf32(v.y - h.y); l.z = to_tf32(v.z - h.z); l.w = to_tf32(v.w - h.w);
-        const uint32_t off = swizzled_offset<Cfg::SWZ>(r, g);
-        *reinterpret_cast<float4*>(bhi + off) = h;
-        *reinterpret_cast<float4*>(blo + off) = l;
+#pragma unroll 1
+      for (uint32_t j0 = 0; j0 < B_ITEMS; j0 += 32 * BATCH) {
+        float4 v[BATCH];
+#pragma unroll
+        for (uint32_t u = 0; u < BATCH; ++u) {
+          const uint32_t j = j0 + lane + 32 * u, r = j & (PAIR_HALF - 1), g = j / PAIR_HALF;
+          const float* src = braw + (4u * g) * PAIR_HALF + r;
+          v[u] = make_float4(src[0], src[PAIR_HALF], src[2 * PAIR_HALF], src[3 * PAIR_HALF]);
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < BATCH; ++u) {
+          const uint32_t j = j0 + lane + 32 * u;
+          float4 h, l;
+          h.x = to_tf32(v[u].x); h.y = to_tf32(v[u].y); h.z = to_tf32(v[u].z); h.w = to_tf32(v[u].w);
+          l.x = to_tf32(v[u].x - h.x); l.y = to_tf32(v[u].y - h.y);
+          l.z = to_tf32(v[u].z - h.z); l.w = to_tf32(v[u].w - h.w);
+          const uint32_t off = swizzled_offset<Cfg::SWZ>(j & (PAIR_HALF - 1), j / PAIR_HALF);
+          *reinterpret_cast<float4*>(bhi + off) = h;
+          *reinterpret_cast<float4*>(blo + off) = l;
+        }
       }
       fence_proxy_async_smem();  // the generic-proxy writes, visible to the tensor core
       __syncwarp();
