@@ -390,6 +390,354 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------ 256-channel heads, CTA pair
+// Gemma's attention: heads of 256 channels, optionally causal, K / V heads shared
+// by groups of query heads (MQA: one K / V head).  Q hi/lo of a 256-channel head
+// would fill all 512 TMEM columns, so a cluster of two CTAs takes one 128-query
+// tile and each CTA works on one 128-channel half of the head: CTA r holds Q
+// channels [128 r, 128 r + 128) in its TMEM, streams the same channels of K and
+// V^T, and computes a partial score block S_r = Q_r K_r^T (exactly as
+// flash_attn_kernel computes a 128-channel head).  The softmax warps of each CTA
+// send their partial block to the other CTA through distributed shared memory and
+// add the two: S_0 + S_1 in one CTA and S_1 + S_0 in the other are the same fp32
+// sums (addition commutes), so both CTAs form the same probabilities, and each
+// accumulates the output for its 128 channels.  The operands use the 128-channel
+// layouts of flash_attn_kernel with each 256-channel head taken as two half heads
+// (half head 2 h + r), which split_heads / split_transpose_heads produce.
+// Causal: query position q sees keys 0 .. q; a 128-query tile stops after its
+// diagonal key blocks, and the largest tiles start first.
+constexpr uint32_t FA2_SX_LD = FA_BKV + 4;  // exchange row stride (floats): conflict-free 16-byte stores
+constexpr uint32_t FA2_SMEM = FA_STAGES * FA_STAGE_BYTES + FA_BQ * FA2_SX_LD * 4 + 1024;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
+    flash_attn_pair_kernel(const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
+                           const __grid_constant__ CUtensorMap tm_vhi, const __grid_constant__ CUtensorMap tm_vlo,
+                           const float* __restrict__ qhi, const float* __restrict__ qlo, float* __restrict__ out,
+                           uint64_t ldo, uint32_t heads, uint32_t kv_heads, uint32_t seq, float scale,
+                           uint32_t causal, unsigned int* __restrict__ err, float* __restrict__ out_lo) {
+  constexpr uint32_t IDESC_S = umma_idesc_tf32(FA_BQ, FA_BKV);
+  constexpr uint32_t IDESC_O = umma_idesc_tf32(FA_BQ, FA_HD);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* sx = reinterpret_cast<float*>(smem + FA_STAGES * FA_STAGE_BYTES);  // [128][FA2_SX_LD], written by the peer
+  __shared__ __align__(8) uint64_t kv_full[FA_STAGES], kv_empty[FA_STAGES];
+  __shared__ __align__(8) uint64_t s_full, s_empty, p_full, o_full, o_empty, drain_bar;
+  __shared__ __align__(8) uint64_t alpha_full[2], l_ready, sx_full, sx_empty;
+  __shared__ float alpha_sh[2][FA_BQ];
+  __shared__ float inv_l_sh[FA_BQ];
+  __shared__ uint32_t tmem_slot;
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_cta_rank(), peer = rank ^ 1u;
+  const uint32_t tiles = seq / FA_BQ;
+  const uint32_t qtile = tiles - 1u - (blockIdx.x >> 1);  // largest causal tiles first
+  const uint32_t head = blockIdx.y, item = blockIdx.z;
+  const uint32_t nb = causal ? (qtile + 1u) * (FA_BQ / FA_BKV) : seq / FA_BKV;
+  const uint32_t kv_head = head / (heads / kv_heads);
+  const uint64_t qslab = (static_cast<uint64_t>(item) * heads + head) * 2 + rank;       // half head of Q
+  const uint64_t kvslab = (static_cast<uint64_t>(item) * kv_heads + kv_head) * 2 + rank;  // half head of K, V
+  const int key_row0 = static_cast<int>(kvslab * seq);
+  const int vt_row0 = static_cast<int>(kvslab * FA_HD);
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < FA_STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(&s_full, 1);
+    mbar_init(&s_empty, 4);
+    mbar_init(&p_full, 4);
+    mbar_init(&o_full, 1);
+    mbar_init(&o_empty, 4);
+    mbar_init(&drain_bar, 1);
+    mbar_init(&alpha_full[0], 4);
+    mbar_init(&alpha_full[1], 4);
+    mbar_init(&l_ready, 4);
+    mbar_init(&sx_full, FA_BQ);  // every softmax thread of the peer, after its stores
+    mbar_init(&sx_empty, 4);     // the peer's softmax warps, after reading what this CTA sent
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    prefetch_tensormap(&tm_khi);
+    prefetch_tensormap(&tm_klo);
+    prefetch_tensormap(&tm_vhi);
+    prefetch_tensormap(&tm_vlo);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (uint32_t j = 0; j < nb; ++j) {
+        const uint32_t st = j % FA_STAGES;
+        if (j >= FA_STAGES && !mbar_wait(&kv_empty[st], ((j / FA_STAGES) - 1) & 1u, err, kErrWaitEmpty)) break;
+        uint8_t* base = smem + st * FA_STAGE_BYTES;
+        mbar_arrive_expect_tx(&kv_full[st], FA_STAGE_BYTES);
+        const int krow = key_row0 + static_cast<int>(j * FA_BKV);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          tma_load_2d(base + a * 4096, &tm_khi, &kv_full[st], a * 32, krow);
+          tma_load_2d(base + FA_K_BYTES + a * 4096, &tm_klo, &kv_full[st], a * 32, krow);
+        }
+        tma_load_2d(base + 2 * FA_K_BYTES, &tm_vhi, &kv_full[st], static_cast<int>(j * FA_BKV), vt_row0);
+        tma_load_2d(base + 2 * FA_K_BYTES + FA_V_BYTES, &tm_vlo, &kv_full[st], static_cast<int>(j * FA_BKV),
+                    vt_row0);
+      }
+    }
+  } else if (warp == 1) {
+    q_ready_barrier();
+    tc_fence_after();
+    auto issue_pv = [&](uint32_t jj) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(&p_full, jj & 1u, err, kErrWaitAccum))) return false;
+      if (jj >= 1 && !__all_sync(0xffffffffu, mbar_wait(&o_empty, (jj - 1) & 1u, err, kErrWaitAccum))) return false;
+      tc_fence_after();
+      const uint32_t st = jj % FA_STAGES;
+      const uint32_t vbase = smem_addr(smem + st * FA_STAGE_BYTES + 2 * FA_K_BYTES);
+#pragma unroll
+      for (uint32_t kk = 0; kk < FA_BKV / 8; ++kk) {
+        const uint64_t dvh = umma_desc_kmajor(vbase + kk * 32, 128);
+        const uint64_t dvl = umma_desc_kmajor(vbase + FA_V_BYTES + kk * 32, 128);
+        if (elect_one()) {
+          umma_tf32_ts(tmem + COL_O, tmem + COL_PHI + kk * 8, dvl, IDESC_O, kk != 0 ? 1u : 0u);
+          umma_tf32_ts(tmem + COL_O, tmem + COL_PLO + kk * 8, dvh, IDESC_O, 1u);
+          umma_tf32_ts(tmem + COL_O, tmem + COL_PHI + kk * 8, dvh, IDESC_O, 1u);
+        }
+        __syncwarp();
+      }
+      if (elect_one()) {
+        umma_commit(&o_full);
+        umma_commit(&kv_empty[st]);
+      }
+      __syncwarp();
+      return true;
+    };
+    bool ok = true;
+    for (uint32_t j = 0; j < nb && ok; ++j) {
+      const uint32_t st = j % FA_STAGES;
+      if (!__all_sync(0xffffffffu, mbar_wait(&kv_full[st], (j / FA_STAGES) & 1u, err, kErrWaitFull))) {
+        ok = false;
+        break;
+      }
+      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(&s_empty, (j - 1) & 1u, err, kErrWaitAccum))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t kbase = smem_addr(smem + st * FA_STAGE_BYTES);
+#pragma unroll
+      for (uint32_t kk = 0; kk < FA_HD / 8; ++kk) {
+        const uint32_t koff = (kk >> 2) * 4096 + (kk & 3) * 32;
+        const uint64_t dkh = umma_desc_kmajor(kbase + koff, 128);
+        const uint64_t dkl = umma_desc_kmajor(kbase + FA_K_BYTES + koff, 128);
+        if (elect_one()) {
+          umma_tf32_ts(tmem + COL_SM, tmem + COL_QHI + kk * 8, dkh, IDESC_S, kk != 0 ? 1u : 0u);
+          umma_tf32_ts(tmem + COL_SC, tmem + COL_QHI + kk * 8, dkl, IDESC_S, kk != 0 ? 1u : 0u);
+          umma_tf32_ts(tmem + COL_SC, tmem + COL_QLO + kk * 8, dkh, IDESC_S, 1u);
+        }
+        __syncwarp();
+      }
+      if (elect_one()) umma_commit(&s_full);
+      __syncwarp();
+      if (j >= 1) ok = issue_pv(j - 1);
+    }
+    if (ok && nb > 0) ok = issue_pv(nb - 1);
+    if (elect_one()) umma_commit(&drain_bar);
+    __syncwarp();
+  } else {
+    const bool softmax = warp < 6;
+    const uint32_t quad = warp & 3u;
+    const uint32_t row = quad * 32 + lane;
+    const uint32_t lane_addr = (quad * 32u) << 16;
+    {
+      const uint64_t qrow = qslab * seq + static_cast<uint64_t>(qtile) * FA_BQ + row;
+      const float* src = (softmax ? qhi : qlo) + qrow * FA_HD;
+      const uint32_t col = softmax ? COL_QHI : COL_QLO;
+#pragma unroll 1
+      for (uint32_t c0 = 0; c0 < FA_HD; c0 += 32) {
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(src + c0 + i));
+          r[i] = __float_as_uint(v.x);
+          r[i + 1] = __float_as_uint(v.y);
+          r[i + 2] = __float_as_uint(v.z);
+          r[i + 3] = __float_as_uint(v.w);
+        }
+        tmem_st_32x32b_x32(tmem + lane_addr + col + c0, r);
+      }
+      tmem_st_wait();
+    }
+    tc_fence_before();
+    q_ready_barrier();
+
+    if (softmax) {
+      float m_run = -FLT_MAX;
+      double l_run = 0.0;
+      const uint32_t qpos = qtile * FA_BQ + row;
+      const uint32_t sx_peer = cluster_smem_addr(sx + row * FA2_SX_LD, peer);
+      const float* sx_mine = sx + row * FA2_SX_LD;
+      for (uint32_t j = 0; j < nb; ++j) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full, j & 1u, err, kErrWaitAccum))) break;
+        tc_fence_after();
+        float p[32];
+        {
+          uint32_t sm[32], sc[32];
+          tmem_ld_32x32b_x32(tmem + lane_addr + COL_SM, sm);
+          tmem_ld_32x32b_x32(tmem + lane_addr + COL_SC, sc);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) p[i] = __uint_as_float(sm[i]) + __uint_as_float(sc[i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty);
+        // exchange the partial scores with the other half of the head
+        if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(&sx_empty, (j - 1) & 1u, err, kErrWaitPeer))) break;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) st_cluster_v4(sx_peer + 4u * i, p[i], p[i + 1], p[i + 2], p[i + 3]);
+        mbar_arrive_cluster_thread(&sx_full, peer);
+        if (!__all_sync(0xffffffffu, mbar_wait_cluster(&sx_full, j & 1u, err, kErrWaitPeer))) break;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 q4 = *reinterpret_cast<const float4*>(sx_mine + i);
+          p[i] = (p[i] + q4.x) * scale;
+          p[i + 1] = (p[i + 1] + q4.y) * scale;
+          p[i + 2] = (p[i + 2] + q4.z) * scale;
+          p[i + 3] = (p[i + 3] + q4.w) * scale;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(&sx_empty, peer);
+        if (causal && (j + 1) * FA_BKV > qtile * FA_BQ) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (j * FA_BKV + static_cast<uint32_t>(i) > qpos) p[i] = -INFINITY;
+        }
+        float t[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t[i] = fmaxf(p[i], p[i + 16]);
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; ++i) t[i] = fmaxf(t[i], t[i + w]);
+        const float mx = t[0];
+        const float m_new = (mx > m_run + FA_TAU) ? mx : m_run;
+        const float alpha = (m_new == m_run) ? 1.0f : expf(m_run - m_new);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) p[i] = expf(p[i] - m_new);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t[i] = p[i] + p[i + 16];
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; ++i) t[i] += t[i + w];
+        l_run = l_run * static_cast<double>(alpha) + static_cast<double>(t[0]);
+        m_run = m_new;
+        if (j >= 1) {
+          alpha_sh[(j - 1) & 1u][row] = alpha;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&alpha_full[(j - 1) & 1u]);
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_full, (j - 1) & 1u, err, kErrWaitAccum))) break;
+          tc_fence_after();
+        }
+        {
+          uint32_t ph[32], pl[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float h = to_tf32(p[i]);
+            ph[i] = __float_as_uint(h);
+            pl[i] = __float_as_uint(to_tf32(p[i] - h));
+          }
+          tmem_st_32x32b_x32(tmem + lane_addr + COL_PHI, ph);
+          tmem_st_32x32b_x32(tmem + lane_addr + COL_PLO, pl);
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full);
+      }
+      inv_l_sh[row] = static_cast<float>(1.0 / l_run);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&l_ready);
+    } else {
+      float o_run[FA_HD];
+#pragma unroll
+      for (int i = 0; i < static_cast<int>(FA_HD); ++i) o_run[i] = 0.f;
+      bool ok = true;
+      for (uint32_t j = 1; j < nb; ++j) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&alpha_full[(j - 1) & 1u], ((j - 1) >> 1) & 1u, err, kErrWaitAccum) &&
+                                         mbar_wait(&o_full, (j - 1) & 1u, err, kErrWaitAccum));
+        if (!ok) break;
+        tc_fence_after();
+        const float alpha = alpha_sh[(j - 1) & 1u][row];
+        const bool rescale = __any_sync(0xffffffffu, alpha != 1.0f);
+#pragma unroll
+        for (uint32_t g = 0; g < FA_HD / 32; ++g) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem + lane_addr + COL_O + g * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o_run[g * 32 + i] += __uint_as_float(r[i]);
+          if (rescale) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o_run[g * 32 + i] *= alpha;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_empty);
+      }
+      if (ok && nb > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_full, (nb - 1) & 1u, err, kErrWaitAccum) &&
+                                         mbar_wait(&l_ready, 0, err, kErrWaitAccum));
+        if (ok) {
+          tc_fence_after();
+          const float inv = inv_l_sh[row];
+          const uint64_t o = (static_cast<uint64_t>(item) * seq + static_cast<uint64_t>(qtile) * FA_BQ + row) * ldo +
+                             (static_cast<uint64_t>(head) * 2 + rank) * FA_HD;
+          float* dst = out + o;
+          float* dst_lo = out_lo != nullptr ? out_lo + o : nullptr;
+#pragma unroll
+          for (uint32_t g = 0; g < FA_HD / 32; ++g) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem + lane_addr + COL_O + g * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const int c = static_cast<int>(g * 32) + i;
+              float4 v = make_float4((o_run[c] + __uint_as_float(r[i])) * inv,
+                                     (o_run[c + 1] + __uint_as_float(r[i + 1])) * inv,
+                                     (o_run[c + 2] + __uint_as_float(r[i + 2])) * inv,
+                                     (o_run[c + 3] + __uint_as_float(r[i + 3])) * inv);
+              if (dst_lo != nullptr) {
+                const float4 h = make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
+                *reinterpret_cast<float4*>(dst_lo + c) =
+                    make_float4(to_tf32(v.x - h.x), to_tf32(v.y - h.y), to_tf32(v.z - h.z), to_tf32(v.w - h.w));
+                v = h;
+              }
+              *reinterpret_cast<float4*>(dst + c) = v;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 32) mbar_wait(&drain_bar, 0, err, kErrWaitDrain);
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still write its exchange buffer or barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // V [items*S rows][ldv] (head h in columns h*128 ..) -> V^T hi / lo [(item*heads + h)*128 + c][S].
 // 32 x 32 tiles through shared memory: reads along channels, writes along positions.
 __global__ void split_transpose_heads_kernel(const float* __restrict__ v, uint64_t ldv, uint32_t heads, uint32_t seq,
@@ -454,6 +802,34 @@ bool make_attn_map(CUtensorMap* map, const float* base, uint64_t rows, uint64_t 
 }
 
 }  // namespace
+
+bool flash_attention256_supported(uint32_t head_dim, uint32_t seq, uint32_t heads, uint32_t kv_heads) {
+  return head_dim == 2 * FA_HD && seq >= FA_BQ && seq % FA_BQ == 0 && kv_heads > 0 && heads % kv_heads == 0;
+}
+
+cudaError_t flash_attention256_tf32x3(const AttnOperands& in, float* out, uint64_t ldo, uint32_t items, uint32_t heads,
+                                      uint32_t kv_heads, uint32_t seq, float scale, bool causal, unsigned int* err,
+                                      cudaStream_t stream, float* out_lo) {
+  if (!flash_attention256_supported(2 * FA_HD, seq, heads, kv_heads) || items == 0 || heads == 0)
+    return cudaErrorInvalidValue;
+  const uint64_t kv_slabs = static_cast<uint64_t>(items) * kv_heads * 2;
+  if (kv_slabs * seq > 0x7FFFFFFFull || static_cast<uint64_t>(items) * heads * 2 * seq > 0x7FFFFFFFull)
+    return cudaErrorInvalidValue;
+  CUtensorMap m_khi, m_klo, m_vhi, m_vlo;
+  if (!make_attn_map(&m_khi, in.khi, kv_slabs * seq, FA_HD, FA_BKV) ||
+      !make_attn_map(&m_klo, in.klo, kv_slabs * seq, FA_HD, FA_BKV) ||
+      !make_attn_map(&m_vhi, in.vthi, kv_slabs * FA_HD, seq, FA_HD) ||
+      !make_attn_map(&m_vlo, in.vtlo, kv_slabs * FA_HD, seq, FA_HD))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(flash_attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(FA2_SMEM));
+  if (e != cudaSuccess) return e;
+  const dim3 grid(2 * (seq / FA_BQ), heads, items);
+  flash_attn_pair_kernel<<<grid, FA_THREADS, FA2_SMEM, stream>>>(m_khi, m_klo, m_vhi, m_vlo, in.qhi, in.qlo, out, ldo,
+                                                                 heads, kv_heads, seq, scale, causal ? 1u : 0u, err,
+                                                                 out_lo);
+  return cudaGetLastError();
+}
 
 bool flash_attention_supported(uint32_t head_dim, uint32_t seq) {
   return head_dim == FA_HD && seq >= FA_BQ && seq % FA_BQ == 0;

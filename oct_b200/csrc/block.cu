@@ -568,15 +568,22 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
       return -3;
   }
   qkv_ = alloc(T * qkv_cols);
-  fused_attn_ = d.family == kDit && flash_attention_supported(d.head_dim, d.seq_len);
-  if (const char* mode = std::getenv("OCT_B200_DIT_ATTENTION"))
-    if (std::strcmp(mode, "materialized") == 0) fused_attn_ = false;
+  if (d.family == kDit) {
+    fused_attn_ = flash_attention_supported(d.head_dim, d.seq_len);
+    if (const char* mode = std::getenv("OCT_B200_DIT_ATTENTION"))
+      if (std::strcmp(mode, "materialized") == 0) fused_attn_ = false;
+  } else {
+    fused_attn_ = flash_attention256_supported(d.head_dim, d.seq_len, d.heads, d.kv_heads);
+    if (const char* mode = std::getenv("OCT_B200_GEMMA_ATTENTION"))
+      if (std::strcmp(mode, "materialized") == 0) fused_attn_ = false;
+  }
   if (fused_attn_) {
     // Q, K and V^T in the TF32 hi/lo per-head layouts of the fused kernel, all batch items
     const uint64_t e = T * attn_cols;
+    const uint64_t ekv = T * static_cast<uint64_t>(d.kv_heads) * d.head_dim;
     qsplit_ = alloc(2 * e);
-    ksplit_ = alloc(2 * e);
-    vtsplit_ = alloc(2 * e);
+    ksplit_ = alloc(2 * ekv);
+    vtsplit_ = alloc(2 * ekv);
     ok = ok && qsplit_ && ksplit_ && vtsplit_;
   } else {
     scores_ = alloc(static_cast<uint64_t>(d.max_batch) * d.heads * d.seq_len * d.seq_len);
@@ -839,7 +846,24 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
     rope_half_kernel<<<grid_for(rope_work, NT), NT, 0, stream_>>>(qkv_, qkv_cols, 0, d.heads + d.kv_heads,
                                                                  d.head_dim, rope_cos_, rope_sin_, d.seq_len, T);
     if (!ok()) return -4;
-    e = attention(batch, qkv_cols, attn_cols, attn_cols + d.kv_heads * d.head_dim, true);
+    if (fused_attn_) {
+      // Q, K and V^T as TF32 splits in half-head layouts, then one fused causal launch
+      const uint64_t se = static_cast<uint64_t>(T) * attn_cols;
+      const uint64_t skv = static_cast<uint64_t>(T) * d.kv_heads * d.head_dim;
+      const uint32_t halves = d.head_dim / 128;
+      e = split_heads(qkv_, qkv_cols, batch, d.heads * halves, d.seq_len, qsplit_, qsplit_ + se, stream_);
+      if (ok()) e = split_heads(qkv_ + attn_cols, qkv_cols, batch, d.kv_heads * halves, d.seq_len, ksplit_,
+                                ksplit_ + skv, stream_);
+      if (ok()) e = split_transpose_heads(qkv_ + attn_cols + static_cast<uint64_t>(d.kv_heads) * d.head_dim, qkv_cols,
+                                          batch, d.kv_heads * halves, d.seq_len, vtsplit_, vtsplit_ + skv, stream_);
+      if (!ok()) return -4;
+      const AttnOperands ops{qsplit_, qsplit_ + se, ksplit_, ksplit_ + skv, vtsplit_, vtsplit_ + skv};
+      e = flash_attention256_tf32x3(ops, attn_, attn_cols, batch, d.heads, d.kv_heads, d.seq_len,
+                                    1.0f / std::sqrt(static_cast<float>(d.head_dim)), true, err_, stream_,
+                                    sp ? attnlo_ : nullptr);
+    } else {
+      e = attention(batch, qkv_cols, attn_cols, attn_cols + d.kv_heads * d.head_dim, true);
+    }
     if (!ok()) return -4;
     if (tpf) {
       // partial O Wo rows -> their owners; owners: x1 = x + sum, h = RMSNorm(x1) -> every rank
@@ -857,7 +881,8 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
       if (ok()) e = tp_phase(1);
       if (!ok()) return -4;
     } else {
-      e = gemm(attn_, attn_cols, wo_, x1_, d.hidden, T, lead ? x : nullptr, d.hidden);  // x1 = x + O Wo
+      e = (sp && fused_attn_) ? gemm_ab(attn_, attnlo_, wo_, x1_, d.hidden, T, lead ? x : nullptr, d.hidden)
+                              : gemm(attn_, attn_cols, wo_, x1_, d.hidden, T, lead ? x : nullptr, d.hidden);  // x1 = x + O Wo
       if (ok()) e = all_reduce(x1_, static_cast<uint64_t>(T) * d.hidden);
       if (!ok()) return -4;
       norm_fused_kernel<<<grid_for(T, 1), NT, 0, stream_>>>(x1_, d.hidden, norm2_, d.eps, nullptr, nullptr, nullptr,

@@ -138,6 +138,15 @@ bool flash_attention_supported(uint32_t head_dim, uint32_t seq);
 cudaError_t flash_attention_tf32x3(const AttnOperands& in, float* out, uint64_t ldo, uint32_t items, uint32_t heads,
                                    uint32_t seq, float scale, unsigned int* err, cudaStream_t stream,
                                    float* out_lo = nullptr);
+// Heads of 256 channels (Gemma), causal or not, K / V heads shared by groups of
+// heads / kv_heads query heads: one CTA pair per 128-query tile, each CTA on one
+// 128-channel half.  Operands in the layouts above with every 256-channel head
+// taken as two half heads: q hi/lo from split_heads over 2 * heads half heads,
+// k hi/lo and vt hi/lo over 2 * kv_heads; out[(item*seq + position) * ldo + h*256 + c].
+bool flash_attention256_supported(uint32_t head_dim, uint32_t seq, uint32_t heads, uint32_t kv_heads);
+cudaError_t flash_attention256_tf32x3(const AttnOperands& in, float* out, uint64_t ldo, uint32_t items, uint32_t heads,
+                                      uint32_t kv_heads, uint32_t seq, float scale, bool causal, unsigned int* err,
+                                      cudaStream_t stream, float* out_lo = nullptr);
 // V columns of `heads` heads ([items*seq][ldv], head h at columns h*128..) ->
 // the vt hi/lo layout above.
 // Q or K columns of `heads` heads ([items*seq][ldx]) -> the q/k hi/lo layout above.

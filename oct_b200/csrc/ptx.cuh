@@ -193,6 +193,23 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, uint32_t rank
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(bar)), "r"(rank));
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
 }
+// Shared::cluster address of this CTA's shared-memory object `p` in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_smem_addr(const void* p, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(p)), "r"(rank));
+  return remote;
+}
+// 16-byte store into another CTA's shared memory (distributed shared memory).
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+// Per-thread arrive with cluster-scope release on the mbarrier at the same offset in CTA `rank`.
+__device__ __forceinline__ void mbar_arrive_cluster_thread(uint64_t* bar, uint32_t rank) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_smem_addr(bar, rank))
+               : "memory");
+}
+
 // Shared::cluster address of the even (leader) CTA's copy of a pair-local
 // shared-memory object: the pair's addresses differ only in the peer bit.
 __device__ __forceinline__ uint32_t leader_smem_addr(const void* p) { return smem_addr(p) & 0xFEFFFFFFu; }

@@ -27,6 +27,9 @@ CASES = {
     "gemma_baseline_dims": (OB.gemma_config(seq_len=256), 1),
     "dit_baseline_dims": (OB.dit_config(seq_len=256, grid_w=16), 1),
     "dit_seq1024": (OB.dit_config(seq_len=1024, hidden=512, heads=4, ffn=1024, grid_w=32), 2),
+    # 256-channel heads take the fused causal CTA-pair attention kernel: one and three query tiles
+    "gemma_head256_seq128": (OB.gemma_config(seq_len=128, hidden=512, heads=2, head_dim=256, ffn=1024), 2),
+    "gemma_head256_seq384": (OB.gemma_config(seq_len=384, hidden=512, heads=2, head_dim=256, ffn=1024), 2),
     # the benchmark configurations themselves
     "gemma_baseline_config": (OB.gemma_config(), 4),
     "dit_baseline_config": (OB.dit_config(), 2),
@@ -116,4 +119,30 @@ def test_dit_fused_and_materialized_attention_agree(runtime, monkeypatch):
     for mode, y in outs.items():
         nw, l2 = errors(y, ref)
         print(f"dit {mode}: normwise {nw:.3e}  relL2 {l2:.3e}")
+        assert nw <= NORMWISE_TOL and l2 <= L2_TOL, (mode, nw, l2)
+
+
+@pytest.mark.parametrize("name", ["gemma_head256_seq384", "gemma_baseline_dims"])
+def test_gemma_fused_and_materialized_attention_agree(runtime, monkeypatch, name):
+    """The Gemma block's fused causal attention (CTA pair per 128-query tile, 256-channel heads)
+    and its materialised path (scores in HBM, causal softmax kernel, two batched products) both
+    meet the oracle bar."""
+    cfg, batch = CASES[name]
+    w = OB.random_weights(cfg, seed=23)
+    rng = np.random.Generator(np.random.PCG64(24))
+    x = rng.standard_normal((batch * cfg.seq_len, cfg.hidden), dtype=np.float32)
+    outs = {}
+    for mode in ("fused", "materialized"):
+        monkeypatch.setenv("OCT_B200_GEMMA_ATTENTION", mode)
+        blk = make_block(runtime, cfg, batch)
+        try:
+            blk.set_weights(w)
+            outs[mode] = blk.forward(x, batch)
+        finally:
+            blk.close()
+        assert runtime.sync_status().ok
+    ref = OB.forward(cfg, w, x)
+    for mode, y in outs.items():
+        nw, l2 = errors(y, ref)
+        print(f"{name} {mode}: normwise {nw:.3e}  relL2 {l2:.3e}")
         assert nw <= NORMWISE_TOL and l2 <= L2_TOL, (mode, nw, l2)
