@@ -453,7 +453,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
     mbar_init(&alpha_full[0], 4);
     mbar_init(&alpha_full[1], 4);
     mbar_init(&l_ready, 4);
-    mbar_init(&sx_full, FA_BQ);  // every softmax thread of the peer, after its stores
+    mbar_init(&sx_full, 4);      // the peer's softmax warps, after their stores
     mbar_init(&sx_empty, 4);     // the peer's softmax warps, after reading what this CTA sent
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -600,7 +600,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
         if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait_cluster(&sx_empty, (j - 1) & 1u, err, kErrWaitPeer))) break;
 #pragma unroll
         for (int i = 0; i < 32; i += 4) st_cluster_v4(sx_peer + 4u * i, p[i], p[i + 1], p[i + 2], p[i + 3]);
-        mbar_arrive_cluster_thread(&sx_full, peer);
+        __syncwarp();  // every lane's stores come before the warp's release below
+        if (lane == 0) mbar_arrive_cluster(&sx_full, peer);
         if (!__all_sync(0xffffffffu, mbar_wait_cluster(&sx_full, j & 1u, err, kErrWaitPeer))) break;
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {

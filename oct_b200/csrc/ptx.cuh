@@ -204,11 +204,6 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, f
   asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");
 }
-// Per-thread arrive with cluster-scope release on the mbarrier at the same offset in CTA `rank`.
-__device__ __forceinline__ void mbar_arrive_cluster_thread(uint64_t* bar, uint32_t rank) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_smem_addr(bar, rank))
-               : "memory");
-}
 
 // Shared::cluster address of the even (leader) CTA's copy of a pair-local
 // shared-memory object: the pair's addresses differ only in the peer bit.
