@@ -597,12 +597,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty);
         // exchange the partial scores with the other half of the head
-        if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait_cluster(&sx_empty, (j - 1) & 1u, err, kErrWaitPeer))) break;
+        if (j >= 1 && !__all_sync(0xffffffffu, mbar_spin_cluster(&sx_empty, (j - 1) & 1u, err, kErrWaitPeer))) break;
 #pragma unroll
         for (int i = 0; i < 32; i += 4) st_cluster_v4(sx_peer + 4u * i, p[i], p[i + 1], p[i + 2], p[i + 3]);
         __syncwarp();  // every lane's stores come before the warp's release below
         if (lane == 0) mbar_arrive_cluster(&sx_full, peer);
-        if (!__all_sync(0xffffffffu, mbar_wait_cluster(&sx_full, j & 1u, err, kErrWaitPeer))) break;
+        if (!__all_sync(0xffffffffu, mbar_spin_cluster(&sx_full, j & 1u, err, kErrWaitPeer))) break;
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
           const float4 q4 = *reinterpret_cast<const float4*>(sx_mine + i);

@@ -119,6 +119,35 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   }
 }
 
+// As mbar_wait_cluster, polling with the non-suspending test_wait: for barriers
+// completed by another CTA's remote arrive, where a suspended try_wait may wake late.
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool mbar_spin_cluster(uint64_t* bar, uint32_t parity, unsigned int* err,
+                                                  unsigned int err_bit) {
+  if (mbar_test_wait_cluster(bar, parity)) return true;
+  const unsigned long long start = global_timer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_test_wait_cluster(bar, parity)) return true;
+    if ((++spins & 255u) == 0u) {
+      if (global_timer_ns() - start > kWaitBudgetNs) {
+        atomicOr(err, err_bit);
+        return false;
+      }
+    }
+  }
+}
+
 // Named barrier over `count` threads (a multiple of 32) of the CTA.
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
