@@ -406,8 +406,17 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 // (half head 2 h + r), which split_heads / split_transpose_heads produce.
 // Causal: query position q sees keys 0 .. q; a 128-query tile stops after its
 // diagonal key blocks, and the largest tiles start first.
+// Shared memory: a 2-slot ring of K blocks (hi, lo) and a 2-slot ring of V^T
+// blocks (hi, lo), so a K slot frees as soon as its scores are computed, and a
+// double-buffered exchange area that the other CTA writes.  The score exchange
+// is software-pipelined: a CTA sends its partial block j + 1 before it works on
+// block j, so the partial it needs has normally arrived by the time it looks.
 constexpr uint32_t FA2_SX_LD = FA_BKV + 4;  // exchange row stride (floats): conflict-free 16-byte stores
-constexpr uint32_t FA2_SMEM = FA_STAGES * FA_STAGE_BYTES + FA_BQ * FA2_SX_LD * 4 + 1024;
+constexpr uint32_t FA2_RING = 2;
+constexpr uint32_t FA2_K_STAGE = 2 * FA_K_BYTES;  // K hi, K lo of one key block
+constexpr uint32_t FA2_V_STAGE = 2 * FA_V_BYTES;  // V^T hi, V^T lo of one key block
+constexpr uint32_t FA2_SX_BYTES = FA_BQ * FA2_SX_LD * 4;
+constexpr uint32_t FA2_SMEM = FA2_RING * (FA2_K_STAGE + FA2_V_STAGE) + 2 * FA2_SX_BYTES + 1024;
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
     flash_attn_pair_kernel(const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
@@ -419,10 +428,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
   constexpr uint32_t IDESC_O = umma_idesc_tf32(FA_BQ, FA_HD);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* sx = reinterpret_cast<float*>(smem + FA_STAGES * FA_STAGE_BYTES);  // [128][FA2_SX_LD], written by the peer
-  __shared__ __align__(8) uint64_t kv_full[FA_STAGES], kv_empty[FA_STAGES];
+  uint8_t* kring = smem;
+  uint8_t* vring = smem + FA2_RING * FA2_K_STAGE;
+  float* sx = reinterpret_cast<float*>(vring + FA2_RING * FA2_V_STAGE);  // [2][128][FA2_SX_LD], written by the peer
+  __shared__ __align__(8) uint64_t k_full[FA2_RING], k_empty[FA2_RING], v_full[FA2_RING], v_empty[FA2_RING];
   __shared__ __align__(8) uint64_t s_full, s_empty, p_full, o_full, o_empty, drain_bar;
-  __shared__ __align__(8) uint64_t alpha_full[2], l_ready, sx_full, sx_empty;
+  __shared__ __align__(8) uint64_t alpha_full[2], l_ready, sx_full[2], sx_empty[2];
   __shared__ float alpha_sh[2][FA_BQ];
   __shared__ float inv_l_sh[FA_BQ];
   __shared__ uint32_t tmem_slot;
@@ -440,9 +451,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
   const int vt_row0 = static_cast<int>(kvslab * FA_HD);
 
   if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < FA_STAGES; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (uint32_t s = 0; s < FA2_RING; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     mbar_init(&s_full, 1);
     mbar_init(&s_empty, 4);
@@ -453,8 +466,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
     mbar_init(&alpha_full[0], 4);
     mbar_init(&alpha_full[1], 4);
     mbar_init(&l_ready, 4);
-    mbar_init(&sx_full, 4);      // the peer's softmax warps, after their stores
-    mbar_init(&sx_empty, 4);     // the peer's softmax warps, after reading what this CTA sent
+    for (uint32_t b = 0; b < 2; ++b) {
+      mbar_init(&sx_full[b], 4);   // the peer's softmax warps, after their stores into buffer b
+      mbar_init(&sx_empty[b], 4);  // the peer's softmax warps, after reading what this CTA sent into buffer b
+    }
     fence_mbar_init();
     fence_proxy_async_smem();
     prefetch_tensormap(&tm_khi);
@@ -474,30 +489,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       for (uint32_t j = 0; j < nb; ++j) {
-        const uint32_t st = j % FA_STAGES;
-        if (j >= FA_STAGES && !mbar_wait(&kv_empty[st], ((j / FA_STAGES) - 1) & 1u, err, kErrWaitEmpty)) break;
-        uint8_t* base = smem + st * FA_STAGE_BYTES;
-        mbar_arrive_expect_tx(&kv_full[st], FA_STAGE_BYTES);
+        const uint32_t st = j % FA2_RING, ph = ((j / FA2_RING) - 1) & 1u;
+        if (j >= FA2_RING && !mbar_wait(&k_empty[st], ph, err, kErrWaitEmpty)) break;
+        uint8_t* kb = kring + st * FA2_K_STAGE;
+        mbar_arrive_expect_tx(&k_full[st], FA2_K_STAGE);
         const int krow = key_row0 + static_cast<int>(j * FA_BKV);
 #pragma unroll
         for (int a = 0; a < 4; ++a) {
-          tma_load_2d(base + a * 4096, &tm_khi, &kv_full[st], a * 32, krow);
-          tma_load_2d(base + FA_K_BYTES + a * 4096, &tm_klo, &kv_full[st], a * 32, krow);
+          tma_load_2d(kb + a * 4096, &tm_khi, &k_full[st], a * 32, krow);
+          tma_load_2d(kb + FA_K_BYTES + a * 4096, &tm_klo, &k_full[st], a * 32, krow);
         }
-        tma_load_2d(base + 2 * FA_K_BYTES, &tm_vhi, &kv_full[st], static_cast<int>(j * FA_BKV), vt_row0);
-        tma_load_2d(base + 2 * FA_K_BYTES + FA_V_BYTES, &tm_vlo, &kv_full[st], static_cast<int>(j * FA_BKV),
-                    vt_row0);
+        if (j >= FA2_RING && !mbar_wait(&v_empty[st], ph, err, kErrWaitEmpty)) break;
+        uint8_t* vb = vring + st * FA2_V_STAGE;
+        mbar_arrive_expect_tx(&v_full[st], FA2_V_STAGE);
+        tma_load_2d(vb, &tm_vhi, &v_full[st], static_cast<int>(j * FA_BKV), vt_row0);
+        tma_load_2d(vb + FA_V_BYTES, &tm_vlo, &v_full[st], static_cast<int>(j * FA_BKV), vt_row0);
       }
     }
   } else if (warp == 1) {
     q_ready_barrier();
     tc_fence_after();
     auto issue_pv = [&](uint32_t jj) -> bool {
+      const uint32_t st = jj % FA2_RING;
       if (!__all_sync(0xffffffffu, mbar_wait(&p_full, jj & 1u, err, kErrWaitAccum))) return false;
       if (jj >= 1 && !__all_sync(0xffffffffu, mbar_wait(&o_empty, (jj - 1) & 1u, err, kErrWaitAccum))) return false;
+      if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (jj / FA2_RING) & 1u, err, kErrWaitFull))) return false;
       tc_fence_after();
-      const uint32_t st = jj % FA_STAGES;
-      const uint32_t vbase = smem_addr(smem + st * FA_STAGE_BYTES + 2 * FA_K_BYTES);
+      const uint32_t vbase = smem_addr(vring + st * FA2_V_STAGE);
 #pragma unroll
       for (uint32_t kk = 0; kk < FA_BKV / 8; ++kk) {
         const uint64_t dvh = umma_desc_kmajor(vbase + kk * 32, 128);
@@ -511,24 +529,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
       }
       if (elect_one()) {
         umma_commit(&o_full);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&v_empty[st]);
       }
       __syncwarp();
       return true;
     };
-    bool ok = true;
-    for (uint32_t j = 0; j < nb && ok; ++j) {
-      const uint32_t st = j % FA_STAGES;
-      if (!__all_sync(0xffffffffu, mbar_wait(&kv_full[st], (j / FA_STAGES) & 1u, err, kErrWaitFull))) {
-        ok = false;
-        break;
-      }
-      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(&s_empty, (j - 1) & 1u, err, kErrWaitAccum))) {
-        ok = false;
-        break;
-      }
+    // Q K^T of block jj (single TMEM score buffer: the softmax warps have loaded block jj - 1)
+    auto issue_s = [&](uint32_t jj) -> bool {
+      const uint32_t st = jj % FA2_RING;
+      if (!__all_sync(0xffffffffu, mbar_wait(&k_full[st], (jj / FA2_RING) & 1u, err, kErrWaitFull))) return false;
+      if (jj >= 1 && !__all_sync(0xffffffffu, mbar_wait(&s_empty, (jj - 1) & 1u, err, kErrWaitAccum))) return false;
       tc_fence_after();
-      const uint32_t kbase = smem_addr(smem + st * FA_STAGE_BYTES);
+      const uint32_t kbase = smem_addr(kring + st * FA2_K_STAGE);
 #pragma unroll
       for (uint32_t kk = 0; kk < FA_HD / 8; ++kk) {
         const uint32_t koff = (kk >> 2) * 4096 + (kk & 3) * 32;
@@ -541,11 +553,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
         }
         __syncwarp();
       }
-      if (elect_one()) umma_commit(&s_full);
+      if (elect_one()) {
+        umma_commit(&s_full);
+        umma_commit(&k_empty[st]);
+      }
       __syncwarp();
-      if (j >= 1) ok = issue_pv(j - 1);
+      return true;
+    };
+    // The scores run two blocks ahead of P V: the softmax warps fetch (and send)
+    // block j + 1 before they finish block j, so S(j + 2) can start before P(j) exists.
+    bool ok = nb > 0 && issue_s(0);
+    if (ok && nb > 1) ok = issue_s(1);
+    for (uint32_t j = 0; j < nb && ok; ++j) {
+      if (j + 2 < nb) ok = issue_s(j + 2);
+      if (ok) ok = issue_pv(j);
     }
-    if (ok && nb > 0) ok = issue_pv(nb - 1);
     if (elect_one()) umma_commit(&drain_bar);
     __syncwarp();
   } else {
@@ -579,40 +601,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
       float m_run = -FLT_MAX;
       double l_run = 0.0;
       const uint32_t qpos = qtile * FA_BQ + row;
-      const uint32_t sx_peer = cluster_smem_addr(sx + row * FA2_SX_LD, peer);
-      const float* sx_mine = sx + row * FA2_SX_LD;
-      for (uint32_t j = 0; j < nb; ++j) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full, j & 1u, err, kErrWaitAccum))) break;
+      // Load this CTA's partial score block jj from TMEM into `part`, free the TMEM
+      // scores for the next product, and send the partial into the peer's buffer jj % 2.
+      auto fetch_send = [&](uint32_t jj, float (&part)[32]) -> bool {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full, jj & 1u, err, kErrWaitAccum))) return false;
         tc_fence_after();
-        float p[32];
         {
           uint32_t sm[32], sc[32];
           tmem_ld_32x32b_x32(tmem + lane_addr + COL_SM, sm);
           tmem_ld_32x32b_x32(tmem + lane_addr + COL_SC, sc);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) p[i] = __uint_as_float(sm[i]) + __uint_as_float(sc[i]);
+          for (int i = 0; i < 32; ++i) part[i] = __uint_as_float(sm[i]) + __uint_as_float(sc[i]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty);
-        // exchange the partial scores with the other half of the head
-        if (j >= 1 && !__all_sync(0xffffffffu, mbar_spin_cluster(&sx_empty, (j - 1) & 1u, err, kErrWaitPeer))) break;
+        const uint32_t b = jj & 1u;
+        // the peer has read what this CTA sent into buffer b two blocks ago
+        if (jj >= 2 && !__all_sync(0xffffffffu, mbar_spin_cluster(&sx_empty[b], ((jj >> 1) - 1) & 1u, err,
+                                                                   kErrWaitPeer)))
+          return false;
+        const uint32_t dst = cluster_smem_addr(sx + (b * FA_BQ + row) * FA2_SX_LD, peer);
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) st_cluster_v4(sx_peer + 4u * i, p[i], p[i + 1], p[i + 2], p[i + 3]);
+        for (int i = 0; i < 32; i += 4) st_cluster_v4(dst + 4u * i, part[i], part[i + 1], part[i + 2], part[i + 3]);
         __syncwarp();  // every lane's stores come before the warp's release below
-        if (lane == 0) mbar_arrive_cluster(&sx_full, peer);
-        if (!__all_sync(0xffffffffu, mbar_spin_cluster(&sx_full, j & 1u, err, kErrWaitPeer))) break;
+        if (lane == 0) mbar_arrive_cluster(&sx_full[b], peer);
+        return true;
+      };
+      float pc[32], pn[32];
+      bool ok = nb > 0 && fetch_send(0, pc);
+      for (uint32_t j = 0; j < nb && ok; ++j) {
+        if (j + 1 < nb && !fetch_send(j + 1, pn)) break;
+        // the peer's partial of block j (sent one block ahead) completes the scores
+        const uint32_t b = j & 1u;
+        if (!__all_sync(0xffffffffu, mbar_spin_cluster(&sx_full[b], (j >> 1) & 1u, err, kErrWaitPeer))) break;
+        float p[32];
+        const float* mine = sx + (b * FA_BQ + row) * FA2_SX_LD;
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
-          const float4 q4 = *reinterpret_cast<const float4*>(sx_mine + i);
-          p[i] = (p[i] + q4.x) * scale;
-          p[i + 1] = (p[i + 1] + q4.y) * scale;
-          p[i + 2] = (p[i + 2] + q4.z) * scale;
-          p[i + 3] = (p[i + 3] + q4.w) * scale;
+          const float4 q4 = *reinterpret_cast<const float4*>(mine + i);
+          p[i] = (pc[i] + q4.x) * scale;
+          p[i + 1] = (pc[i + 1] + q4.y) * scale;
+          p[i + 2] = (pc[i + 2] + q4.z) * scale;
+          p[i + 3] = (pc[i + 3] + q4.w) * scale;
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(&sx_empty, peer);
+        if (lane == 0) mbar_arrive_cluster(&sx_empty[b], peer);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pc[i] = pn[i];
         if (causal && (j + 1) * FA_BKV > qtile * FA_BQ) {
 #pragma unroll
           for (int i = 0; i < 32; ++i)
@@ -665,6 +702,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&l_ready);
     } else {
+
       float o_run[FA_HD];
 #pragma unroll
       for (int i = 0; i < static_cast<int>(FA_HD); ++i) o_run[i] = 0.f;
