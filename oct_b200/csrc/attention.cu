@@ -416,8 +416,7 @@ constexpr uint32_t FA2_RING = 2;
 constexpr uint32_t FA2_K_STAGE = 2 * FA_K_BYTES;  // K hi, K lo of one key block
 constexpr uint32_t FA2_V_STAGE = 2 * FA_V_BYTES;  // V^T hi, V^T lo of one key block
 constexpr uint32_t FA2_SX_BYTES = FA_BQ * FA2_SX_LD * 4;
-constexpr uint32_t FA2_SMEM = FA2_RING * (FA2_K_STAGE + FA2_V_STAGE) + 4 * FA2_SX_BYTES + 1024;
-constexpr uint32_t FA2_WARP_ROWS_BYTES = 32 * FA2_SX_LD * 4;  // one softmax warp's 32 rows of a partial block
+constexpr uint32_t FA2_SMEM = FA2_RING * (FA2_K_STAGE + FA2_V_STAGE) + 2 * FA2_SX_BYTES + 1024;
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
     flash_attn_pair_kernel(const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
@@ -431,8 +430,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* kring = smem;
   uint8_t* vring = smem + FA2_RING * FA2_K_STAGE;
-  float* sx = reinterpret_cast<float*>(vring + FA2_RING * FA2_V_STAGE);  // [2][128][FA2_SX_LD], filled by the peer
-  float* sb = sx + 2 * FA_BQ * FA2_SX_LD;                                 // [2][128][FA2_SX_LD], sent to the peer
+  float* sx = reinterpret_cast<float*>(vring + FA2_RING * FA2_V_STAGE);  // [2][128][FA2_SX_LD], written by the peer
   __shared__ __align__(8) uint64_t k_full[FA2_RING], k_empty[FA2_RING], v_full[FA2_RING], v_empty[FA2_RING];
   __shared__ __align__(8) uint64_t s_full, s_empty, p_full, o_full, o_empty, drain_bar;
   __shared__ __align__(8) uint64_t alpha_full[2], l_ready, sx_full[2], sx_empty[2];
@@ -469,7 +467,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
     mbar_init(&alpha_full[1], 4);
     mbar_init(&l_ready, 4);
     for (uint32_t b = 0; b < 2; ++b) {
-      mbar_init(&sx_full[b], 1);   // this CTA's expected bytes; the peer's bulk copies complete them
+      mbar_init(&sx_full[b], 4);   // the peer's softmax warps, after their stores into buffer b
       mbar_init(&sx_empty[b], 4);  // the peer's softmax warps, after reading what this CTA sent into buffer b
     }
     fence_mbar_init();
@@ -620,26 +618,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty);
         const uint32_t b = jj & 1u;
-        // this CTA's send buffer b: the bulk copy of block jj - 2 has read it
-        if (jj >= 2) {
-          if (lane == 0) bulk_wait_read<1>();
-          __syncwarp();
-        }
-        float* srow = sb + (b * FA_BQ + row) * FA2_SX_LD;
-#pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(srow + i) = make_float4(part[i], part[i + 1], part[i + 2], part[i + 3]);
-        fence_proxy_async_smem();  // the stores, visible to the bulk copy
-        __syncwarp();
-        // the peer's buffer b: the peer has read what this CTA sent into it two blocks ago
+        // the peer has read what this CTA sent into buffer b two blocks ago
         if (jj >= 2 && !__all_sync(0xffffffffu, mbar_spin_cluster(&sx_empty[b], ((jj >> 1) - 1) & 1u, err,
                                                                    kErrWaitPeer)))
           return false;
-        if (lane == 0) {
-          const uint32_t off = (b * FA_BQ + quad * 32u) * FA2_SX_LD;
-          bulk_copy_to_cluster(cluster_smem_addr(sx + off, peer), sb + off, FA2_WARP_ROWS_BYTES,
-                               cluster_smem_addr(&sx_full[b], peer));
-        }
+        const uint32_t dst = cluster_smem_addr(sx + (b * FA_BQ + row) * FA2_SX_LD, peer);
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) st_cluster_v4(dst + 4u * i, part[i], part[i + 1], part[i + 2], part[i + 3]);
+        __syncwarp();  // every lane's stores come before the warp's release below
+        if (lane == 0) mbar_arrive_cluster(&sx_full[b], peer);
         return true;
       };
       float pc[32], pn[32];
@@ -648,7 +635,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
         if (j + 1 < nb && !fetch_send(j + 1, pn)) break;
         // the peer's partial of block j (sent one block ahead) completes the scores
         const uint32_t b = j & 1u;
-        if (warp == 2 && lane == 0) mbar_arrive_expect_tx(&sx_full[b], 4 * FA2_WARP_ROWS_BYTES);
         if (!__all_sync(0xffffffffu, mbar_spin_cluster(&sx_full[b], (j >> 1) & 1u, err, kErrWaitPeer))) break;
         float p[32];
         const float* mine = sx + (b * FA_BQ + row) * FA2_SX_LD;
@@ -714,10 +700,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
       }
       inv_l_sh[row] = static_cast<float>(1.0 / l_run);
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&l_ready);
-        bulk_wait_read<0>();  // the last bulk copies have read this CTA's send buffer
-      }
+      if (lane == 0) mbar_arrive(&l_ready);
     } else {
 
       float o_run[FA_HD];

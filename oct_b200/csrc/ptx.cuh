@@ -228,22 +228,11 @@ __device__ __forceinline__ uint32_t cluster_smem_addr(const void* p, uint32_t ra
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(p)), "r"(rank));
   return remote;
 }
-// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this
-// CTA's shared memory into another CTA's (shared::cluster addresses `dst`, `bar`);
-// the bytes complete on that CTA's mbarrier.  Tracked in the issuing thread's bulk groups.
-__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-      "r"(smem_addr(src)), "r"(bytes), "r"(bar)
-      : "memory");
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+// 16-byte store into another CTA's shared memory (distributed shared memory).
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
 }
-// Waits until at most N of this thread's most recent bulk groups still read their source.
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-
 
 // Shared::cluster address of the even (leader) CTA's copy of a pair-local
 // shared-memory object: the pair's addresses differ only in the peer bit.
