@@ -411,11 +411,14 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 // double-buffered exchange area that the other CTA writes.  The score exchange
 // is software-pipelined: a CTA sends its partial block j + 1 before it works on
 // block j, so the partial it needs has normally arrived by the time it looks.
-constexpr uint32_t FA2_SX_LD = FA_BKV + 4;  // exchange row stride (floats): conflict-free 16-byte stores
+// Exchange layout, group-major: [FA_BKV / 4 groups][128 rows][4 floats], so each 16-byte
+// remote store instruction of a warp writes 512 contiguous bytes, and the local 16-byte reads
+// of consecutive rows are conflict-free.
 constexpr uint32_t FA2_RING = 2;
 constexpr uint32_t FA2_K_STAGE = 2 * FA_K_BYTES;  // K hi, K lo of one key block
 constexpr uint32_t FA2_V_STAGE = 2 * FA_V_BYTES;  // V^T hi, V^T lo of one key block
-constexpr uint32_t FA2_SX_BYTES = FA_BQ * FA2_SX_LD * 4;
+constexpr uint32_t FA2_SX_FLOATS = FA_BQ * FA_BKV;
+constexpr uint32_t FA2_SX_BYTES = FA2_SX_FLOATS * 4;
 constexpr uint32_t FA2_SMEM = FA2_RING * (FA2_K_STAGE + FA2_V_STAGE) + 2 * FA2_SX_BYTES + 1024;
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
@@ -430,7 +433,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* kring = smem;
   uint8_t* vring = smem + FA2_RING * FA2_K_STAGE;
-  float* sx = reinterpret_cast<float*>(vring + FA2_RING * FA2_V_STAGE);  // [2][128][FA2_SX_LD], written by the peer
+  float* sx = reinterpret_cast<float*>(vring + FA2_RING * FA2_V_STAGE);  // [2][8][128][4], written by the peer
   __shared__ __align__(8) uint64_t k_full[FA2_RING], k_empty[FA2_RING], v_full[FA2_RING], v_empty[FA2_RING];
   __shared__ __align__(8) uint64_t s_full, s_empty, p_full, o_full, o_empty, drain_bar;
   __shared__ __align__(8) uint64_t alpha_full[2], l_ready, sx_full[2], sx_empty[2];
@@ -622,9 +625,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
         if (jj >= 2 && !__all_sync(0xffffffffu, mbar_spin_cluster(&sx_empty[b], ((jj >> 1) - 1) & 1u, err,
                                                                    kErrWaitPeer)))
           return false;
-        const uint32_t dst = cluster_smem_addr(sx + (b * FA_BQ + row) * FA2_SX_LD, peer);
+        const uint32_t dst = cluster_smem_addr(sx + b * FA2_SX_FLOATS + row * 4, peer);
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) st_cluster_v4(dst + 4u * i, part[i], part[i + 1], part[i + 2], part[i + 3]);
+        for (int i = 0; i < 32; i += 4)
+          st_cluster_v4(dst + 4u * (i / 4) * FA_BQ * 4, part[i], part[i + 1], part[i + 2], part[i + 3]);
         __syncwarp();  // every lane's stores come before the warp's release below
         if (lane == 0) mbar_arrive_cluster(&sx_full[b], peer);
         return true;
@@ -637,10 +641,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FA_THREADS, 1)
         const uint32_t b = j & 1u;
         if (!__all_sync(0xffffffffu, mbar_spin_cluster(&sx_full[b], (j >> 1) & 1u, err, kErrWaitPeer))) break;
         float p[32];
-        const float* mine = sx + (b * FA_BQ + row) * FA2_SX_LD;
+        const float* mine = sx + b * FA2_SX_FLOATS + row * 4;
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
-          const float4 q4 = *reinterpret_cast<const float4*>(mine + i);
+          const float4 q4 = *reinterpret_cast<const float4*>(mine + (i / 4) * FA_BQ * 4);
           p[i] = (pc[i] + q4.x) * scale;
           p[i + 1] = (pc[i + 1] + q4.y) * scale;
           p[i + 2] = (pc[i + 2] + q4.z) * scale;
