@@ -396,21 +396,23 @@ def smallm_measurements(rt, torch, stream, hbm_peak: float) -> list[dict]:
         a = torch.rand(m, k, device="cuda", generator=g) * 2 - 1
         b = torch.rand(k, n, device="cuda", generator=g) * 2 - 1
         c = torch.empty(m, n, device="cuda")
-        for _ in range(3):
-            rt.sgemm_device(a, b, c, m, n, k, R.SGEMM_AUTO, stream)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        iters = 20
-        e0.record(stream)
-        for _ in range(iters):
-            rt.sgemm_device(a, b, c, m, n, k, R.SGEMM_AUTO, stream)
-        e1.record(stream)
-        e1.synchronize()
-        ms = e0.elapsed_time(e1) / iters
-        nbytes = 4 * (k * n + m * k + m * n)
-        out.append({"kernel": "sgemm_smallm", "m": m, "n": n, "k": k, "ms": round(ms, 4),
-                    "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1), "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 /
-                                                                                       hbm_peak, 3),
-                    "bytes": nbytes, "l2": "B larger than L2, no flush"})
+        for variant, label in ((R.SGEMM_AUTO, "sgemm_smallm"), (R.SGEMM_SMALLM, "sgemm_smallm_cuda_cores"),
+                               (R.SGEMM_SMALLM_TC, "sgemm_smallm_tensor_cores")):
+            for _ in range(3):
+                rt.sgemm_device(a, b, c, m, n, k, variant, stream)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            iters = 20
+            e0.record(stream)
+            for _ in range(iters):
+                rt.sgemm_device(a, b, c, m, n, k, variant, stream)
+            e1.record(stream)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1) / iters
+            nbytes = 4 * (k * n + m * k + m * n)
+            out.append({"kernel": label, "m": m, "n": n, "k": k, "ms": round(ms, 4),
+                        "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                        "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 3),
+                        "bytes": nbytes, "l2": "B larger than L2, no flush"})
     return out
 
 

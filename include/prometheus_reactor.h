@@ -1461,6 +1461,9 @@ enum {
   OCT_B200_SGEMM_TC3XTF32 = 1u,   /* tcgen05/TMEM tensor cores, split-TF32 x3 */
   OCT_B200_SGEMM_FMA = 2u,        /* plain FP32 FMA on the CUDA cores (control) */
   OCT_B200_SGEMM_SMALLM = 3u,     /* m <= 16: HBM-bound CUDA-core kernel, split-K, ordered reduction */
+  OCT_B200_SGEMM_SMALLM_TC = 4u,  /* m <= 16: tcgen05 3xTF32 with the TF32 split inside the kernel (C^T = B^T A^T,
+                                     A and B read in place: 16-byte aligned, lda / ldb multiples of 4, else
+                                     runs as OCT_B200_SGEMM_SMALLM), split-K, ordered reduction */
   OCT_B200_SGEMM_TC_BK16 = 16u,   /* tensor cores, one CTA per 128x256 tile, 16-deep K stages */
   OCT_B200_SGEMM_TC_BK32 = 32u,   /* tensor cores, one CTA per 128x256 tile, 32-deep K stages */
   OCT_B200_SGEMM_TC_PAIR16 = 216u, /* tensor cores, CTA pair (cta_group::2) per 256x256 tile, 16-deep */

@@ -203,6 +203,17 @@ cudaError_t sgemm_smallm(const float* a, uint64_t lda, const float* b, uint64_t 
                          uint32_t m, uint32_t n, uint32_t k, void* scratch, cudaStream_t stream,
                          unsigned int* err = nullptr);
 
+// Small-M fp32 SGEMM (1 <= m <= 16) on the tcgen05 tensor cores with the TF32
+// split inside the kernel (sgemm_smallm_tc.cu): A and B read in place by TMA
+// (16-byte aligned, leading dimensions multiples of 4), split-K partials in
+// `scratch` (sgemm_smallm_tc_scratch_bytes, may be 0) added in split order.
+bool sgemm_smallm_tc_eligible(const float* a, uint64_t lda, const float* b, uint64_t ldb, uint32_t m, uint32_t n,
+                              uint32_t k);
+uint64_t sgemm_smallm_tc_scratch_bytes(uint32_t m, uint32_t n, uint32_t k);
+cudaError_t sgemm_smallm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
+                            uint32_t m, uint32_t n, uint32_t k, void* scratch, unsigned int* err,
+                            cudaStream_t stream);
+
 // ---------------------------------------------------------------- reductions
 // op: 1 = row sum, 2 = row max, 3 = stable softmax.  `nonfinite` (device
 // u64, preset to UINT64_MAX by the caller) receives the smallest flat index of

@@ -79,7 +79,7 @@ const oct::SgemmEvents* next_timing_events(Runtime* rt) {
 // Enqueues C = A * B for device pointers; chooses the kernel.
 bool known_variant(uint32_t v) {
   return v == OCT_B200_SGEMM_AUTO || v == OCT_B200_SGEMM_TC3XTF32 || v == OCT_B200_SGEMM_FMA ||
-         v == OCT_B200_SGEMM_SMALLM ||
+         v == OCT_B200_SGEMM_SMALLM || v == OCT_B200_SGEMM_SMALLM_TC ||
          v == OCT_B200_SGEMM_TC_BK16 || v == OCT_B200_SGEMM_TC_BK32 || v == OCT_B200_SGEMM_TC_PAIR16 ||
          v == OCT_B200_SGEMM_TC_PAIR32 || v == OCT_B200_SGEMM_TC_INSM16 || v == OCT_B200_SGEMM_TC_INSM32;
 }
@@ -104,10 +104,22 @@ int oct::rt::enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const floa
                            const oct::GemmBatch* batch, DevBuf* scratch) {
   variant = resolve_variant(variant, m, n, k);
   if (scratch == nullptr) scratch = &rt->scratch;
-  // the small-M kernel has no batched or B^T form: those take the FMA control
-  if (variant == OCT_B200_SGEMM_SMALLM && batch != nullptr && (batch->count > 1 || batch->b_trans))
+  // the small-M kernels have no batched or B^T form: those take the FMA control
+  if ((variant == OCT_B200_SGEMM_SMALLM || variant == OCT_B200_SGEMM_SMALLM_TC) && batch != nullptr &&
+      (batch->count > 1 || batch->b_trans))
     variant = OCT_B200_SGEMM_FMA;
   cudaError_t e;
+  if (variant == OCT_B200_SGEMM_SMALLM_TC) {
+    if (!oct::sgemm_smallm_supported(m)) return OCT_B200_DETAIL_UNSUPPORTED_SHAPE;
+    if (oct::sgemm_smallm_tc_eligible(a, lda, b, ldb, m, n, k)) {
+      const uint64_t need = oct::sgemm_smallm_tc_scratch_bytes(m, n, k);
+      if (need != 0 && scratch->ensure(need, stream) != cudaSuccess) return OCT_B200_DETAIL_OUT_OF_MEMORY;
+      e = oct::sgemm_smallm_tc(a, lda, b, ldb, c, ldc, m, n, k, need != 0 ? scratch->aligned() : nullptr,
+                               rt->err_word(), stream);
+      return e == cudaSuccess ? 0 : OCT_B200_DETAIL_CUDA_ERROR;
+    }
+    variant = OCT_B200_SGEMM_SMALLM;  // operands TMA cannot read in place
+  }
   if (variant == OCT_B200_SGEMM_SMALLM) {
     if (!oct::sgemm_smallm_supported(m)) return OCT_B200_DETAIL_UNSUPPORTED_SHAPE;
     const uint64_t need = oct::sgemm_smallm_scratch_bytes(m, n, k);

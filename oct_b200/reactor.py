@@ -70,6 +70,7 @@ SGEMM_AUTO, SGEMM_TC3XTF32, SGEMM_FMA, SGEMM_SMALLM = 0, 1, 2, 3
 SGEMM_TC_BK16, SGEMM_TC_BK32 = 16, 32  # explicit tensor-core stage depths, one CTA per tile
 SGEMM_TC_PAIR16, SGEMM_TC_PAIR32 = 216, 232  # CTA-pair (cta_group::2) 256x256 tiles
 SGEMM_TC_INSM16, SGEMM_TC_INSM32 = 316, 332  # CTA pair, TF32 split inside the kernel (no split pass)
+SGEMM_SMALLM_TC = 4  # m <= 16 on the tensor cores, TF32 split inside the kernel
 
 MAX_STAGES = 8
 

@@ -155,6 +155,28 @@ def test_small_m_kernel(runtime, oracle_mod, golden, shape):
         assert o.compare_against_oracle(o.cpu_sgemm_f32(ga, gb, 15, 256, 1536), c).pass_ == 1
 
 
+@pytest.mark.parametrize("shape", [(1, 256, 1536), (7, 256, 1536), (15, 256, 1536), (16, 256, 1536),
+                                   (1, 16384, 2048), (8, 16384, 2048), (16, 16384, 2048), (16, 8192, 4096),
+                                   (5, 1004, 776), (16, 12, 40000), (4, 2052, 4), (2, 300, 100), (9, 1001, 777)])
+def test_small_m_tensor_core_kernel(runtime, oracle_mod, golden, shape):
+    """The tensor-core small-M kernel (C^T = B^T A^T, TF32 split inside the kernel, split-K
+    with an ordered reduction): the small-M corpus shapes, Gemma per-token shapes and ragged
+    ones (n not a multiple of 128, k not a multiple of 32, one k step, a deep single column
+    tile); repeat calls are bit-identical.  Shapes whose operands TMA cannot read in place
+    (lda or ldb not a multiple of 4: 9 x 1001 x 777) run the CUDA-core kernel instead."""
+    o = oracle_mod
+    m, n, k = shape
+    a, b = o.uniform_matrix(m, k, m + n).ravel(), o.uniform_matrix(k, n, k).ravel()
+    c = device_sgemm(runtime, a, b, m, n, k, R.SGEMM_SMALLM_TC)
+    _check_against_fp64(o, c, a, b, m, n, k)
+    assert np.array_equal(c, device_sgemm(runtime, a, b, m, n, k, R.SGEMM_SMALLM_TC))
+    assert o.compare_against_oracle(o.cpu_sgemm_f32(a, b, m, n, k), c).pass_ == 1
+    if (m, n, k) == (15, 256, 1536):  # the corpus inputs and their golden answer
+        ga, gb = o.gemma_corpus_a(15 * 1536), o.gemma_corpus_b(1536 * 256)
+        c = device_sgemm(runtime, ga, gb, 15, 256, 1536, R.SGEMM_SMALLM_TC)
+        assert o.compare_against_oracle(o.cpu_sgemm_f32(ga, gb, 15, 256, 1536), c).pass_ == 1
+
+
 def test_small_m_kernel_rejects_larger_m(runtime):
     import torch
     x = torch.zeros((17, 8), device="cuda")
