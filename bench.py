@@ -122,6 +122,7 @@ class ClockSampler:
         self.gpu = gpu
         self.proc = None
         self.lines: list[str] = []
+        self.start = 0
 
     def __enter__(self):
         try:
@@ -130,6 +131,12 @@ class ClockSampler:
                  "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi takes a moment to start: begin the timed region only once it
+            # reports, and keep only the samples taken from then on
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0:
+                time.sleep(0.01)
+            self.start = len(self.lines)
         except Exception:
             self.proc = None
         return self
@@ -140,7 +147,11 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc is not None:
-            time.sleep(0.25)
+            # at least one sample after the region started (short regions end between samples)
+            t0 = time.time()
+            while len(self.lines) <= self.start and time.time() - t0 < 2.0:
+                time.sleep(0.01)
+            time.sleep(0.1)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -150,7 +161,7 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        for line in (self.lines[self.start:] or self.lines):
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 8:
                 continue
