@@ -158,11 +158,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     // its granules; a warp only waits for the next phase of its own slot's barrier.
     const uint32_t cw = warp - 2u;
     const uint32_t slot = cw / ST_CONV, half = cw % ST_CONV;
-    constexpr uint32_t B_ITEMS = ST_NT * (ST_BK / 4);  // (row n, k group) granules of B^T
-    constexpr uint32_t A_ITEMS = ST_A / 16;             // granules of A
-    constexpr uint32_t PER = (B_ITEMS + A_ITEMS) / ST_CONV;
-    constexpr uint32_t BATCH = 6;
-    static_assert(PER % (32 * BATCH) == 0, "batches tile a warp's share");
+    // Each lane owns whole rows of B^T (columns of B): rows lane + 32 t, t = 2 half, 2 half + 1,
+    // all 8 k groups of each; the second warp also splits A (4 granules a lane).
+    constexpr uint32_t GROUPS = ST_BK / 4;
+    static_assert(ST_CONV == 2 && ST_NT == 128 && ST_A / 16 % 32 == 0, "two warps share 4 x 32 rows and A");
     for (uint32_t kb = slot; kb < num_kb; kb += ST_S) {
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&raw_full[slot], (kb / ST_S) & 1u, err, kErrWaitFull));
       if (!ok || *(volatile uint32_t*)&aborted != 0u) {
@@ -176,35 +175,37 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
       float4* ahi = reinterpret_cast<float4*>(btlo + ST_BT);
       float4* alo = reinterpret_cast<float4*>(btlo + ST_BT + ST_A);
 #pragma unroll 1
-      for (uint32_t i0 = half * PER; i0 < (half + 1) * PER; i0 += 32 * BATCH) {
-        float4 v[BATCH];
+      for (uint32_t t = 2 * half; t < 2 * half + 2; ++t) {
+        const uint32_t r = lane + 32u * t, x = r & 7u;
+        const float* src = braw + r;
+        float4 v[GROUPS];
 #pragma unroll
-        for (uint32_t u = 0; u < BATCH; ++u) {
-          const uint32_t i = i0 + lane + 32 * u;
-          if (i < B_ITEMS) {
-            const uint32_t r = i & (ST_NT - 1), g = i / ST_NT;
-            const float* src = braw + (4u * g) * ST_NT + r;
-            v[u] = make_float4(src[0], src[ST_NT], src[2 * ST_NT], src[3 * ST_NT]);
-          } else {
-            v[u] = ahi[i - B_ITEMS];
-          }
+        for (uint32_t g = 0; g < GROUPS; ++g)
+          v[g] = make_float4(src[(4 * g) * ST_NT], src[(4 * g + 1) * ST_NT], src[(4 * g + 2) * ST_NT],
+                             src[(4 * g + 3) * ST_NT]);
+#pragma unroll
+        for (uint32_t g = 0; g < GROUPS; ++g) {
+          float4 h, l;
+          h.x = to_tf32(v[g].x); h.y = to_tf32(v[g].y); h.z = to_tf32(v[g].z); h.w = to_tf32(v[g].w);
+          l.x = to_tf32(v[g].x - h.x); l.y = to_tf32(v[g].y - h.y);
+          l.z = to_tf32(v[g].z - h.z); l.w = to_tf32(v[g].w - h.w);
+          const uint32_t off = r * 128u + ((g ^ x) << 4);  // 128-byte swizzle
+          *reinterpret_cast<float4*>(bthi + off) = h;
+          *reinterpret_cast<float4*>(btlo + off) = l;
         }
+      }
+      if (half == 1) {
+        float4 v[ST_A / 16 / 32];
 #pragma unroll
-        for (uint32_t u = 0; u < BATCH; ++u) {
-          const uint32_t i = i0 + lane + 32 * u;
+        for (uint32_t u = 0; u < ST_A / 16 / 32; ++u) v[u] = ahi[lane + 32 * u];
+#pragma unroll
+        for (uint32_t u = 0; u < ST_A / 16 / 32; ++u) {
           float4 h, l;
           h.x = to_tf32(v[u].x); h.y = to_tf32(v[u].y); h.z = to_tf32(v[u].z); h.w = to_tf32(v[u].w);
           l.x = to_tf32(v[u].x - h.x); l.y = to_tf32(v[u].y - h.y);
           l.z = to_tf32(v[u].z - h.z); l.w = to_tf32(v[u].w - h.w);
-          if (i < B_ITEMS) {
-            const uint32_t r = i & (ST_NT - 1), g = i / ST_NT;
-            const uint32_t off = r * 128u + ((g ^ (r & 7u)) << 4);  // 128-byte swizzle
-            *reinterpret_cast<float4*>(bthi + off) = h;
-            *reinterpret_cast<float4*>(btlo + off) = l;
-          } else {
-            ahi[i - B_ITEMS] = h;
-            alo[i - B_ITEMS] = l;
-          }
+          ahi[lane + 32 * u] = h;
+          alo[lane + 32 * u] = l;
         }
       }
       fence_proxy_async_smem();  // the generic-proxy writes, visible to the tensor core
