@@ -110,6 +110,18 @@ __device__ __forceinline__ void note_nonfinite(float v, uint64_t flat, uint64_t&
   if (!isfinite(v) && flat < first) first = flat;
 }
 
+// Per-float4 pieces of the row arithmetic, shared by every kernel so that they
+// evaluate (and contract) the same expressions.
+__device__ __forceinline__ float max4(float4 x) { return fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)); }
+__device__ __forceinline__ float4 exp4(float4 x, float mx) {
+  return make_float4(expf(x.x - mx), expf(x.y - mx), expf(x.z - mx), expf(x.w - mx));
+}
+__device__ __forceinline__ float hsum4(float4 x) { return (x.x + x.y) + (x.z + x.w); }
+__device__ __forceinline__ double sq4(float4 x) {
+  // four non-negative squares summed in fp32, accumulated in binary64
+  return static_cast<double>((x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w));
+}
+
 // Processes one row held in shared memory.  `lane` / TPR index the threads of
 // the row group; out_row points at this row's output (softmax / RMSNorm) or
 // at out[r] (sum / max).
@@ -139,7 +151,7 @@ __device__ __forceinline__ float process_row(float* srow, uint32_t w, uint32_t l
     float mx = -FLT_MAX;
     for (uint32_t i = lane; i < nv; i += TPR) {
       const float4 x = v4[i];
-      mx = fmaxf(mx, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
+      mx = fmaxf(mx, max4(x));
       if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
         note_nonfinite(x.x, row * w + 4 * i, first_bad); note_nonfinite(x.y, row * w + 4 * i + 1, first_bad);
         note_nonfinite(x.z, row * w + 4 * i + 2, first_bad); note_nonfinite(x.w, row * w + 4 * i + 3, first_bad);
@@ -152,7 +164,7 @@ __device__ __forceinline__ float process_row(float* srow, uint32_t w, uint32_t l
     float mx = -FLT_MAX;
     for (uint32_t i = lane; i < nv; i += TPR) {
       const float4 x = v4[i];
-      mx = fmaxf(mx, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
+      mx = fmaxf(mx, max4(x));
       if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
         note_nonfinite(x.x, row * w + 4 * i, first_bad); note_nonfinite(x.y, row * w + 4 * i + 1, first_bad);
         note_nonfinite(x.z, row * w + 4 * i + 2, first_bad); note_nonfinite(x.w, row * w + 4 * i + 3, first_bad);
@@ -163,9 +175,8 @@ __device__ __forceinline__ float process_row(float* srow, uint32_t w, uint32_t l
     // fp32 (a few ulp) and the row sum accumulates those partials in binary64.
     double s = 0.0;
     for (uint32_t i = lane; i < nv; i += TPR) {
-      float4 x = v4[i];
-      x.x = expf(x.x - mx); x.y = expf(x.y - mx); x.z = expf(x.z - mx); x.w = expf(x.w - mx);
-      s += static_cast<double>((x.x + x.y) + (x.z + x.w));
+      const float4 x = exp4(v4[i], mx);
+      s += static_cast<double>(hsum4(x));
       v4[i] = x;  // keep exp(x - max) for the normalising pass
     }
     s = group_sum_d<TPR>(s, dscratch);
@@ -180,8 +191,7 @@ __device__ __forceinline__ float process_row(float* srow, uint32_t w, uint32_t l
     double ss = 0.0;
     for (uint32_t i = lane; i < nv; i += TPR) {
       const float4 x = v4[i];
-      // four non-negative squares summed in fp32, accumulated in binary64
-      ss += static_cast<double>((x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w));
+      ss += sq4(x);
       if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
         note_nonfinite(x.x, row * w + 4 * i, first_bad); note_nonfinite(x.y, row * w + 4 * i + 1, first_bad);
         note_nonfinite(x.z, row * w + 4 * i + 2, first_bad); note_nonfinite(x.w, row * w + 4 * i + 3, first_bad);
@@ -390,6 +400,111 @@ __global__ void __launch_bounds__(THREADS) row_warp_kernel(const float* __restri
   }
 }
 
+// Narrow rows (w = 128 * NV, NV <= 4): one warp per row, each lane holding NV
+// float4 of it in registers.  A warp issues the loads of RPW rows at once
+// (NV * RPW = 8 float4 in flight per lane) straight from global memory; with no
+// shared-memory ring up to 8 CTAs (64 warps) fit on an SM, so at 32768 x 256
+// every row is requested in the first round of loads.  The arithmetic is
+// process_row's for TPR = 32, float4 by float4 in the same order.
+template <int OP, int NV>
+__global__ void __launch_bounds__(THREADS) row_reg_kernel(const float* __restrict__ in, uint64_t stride,
+                                                          float* __restrict__ out, float* __restrict__ inv_rms,
+                                                          const float* __restrict__ weight, float eps, uint32_t rows,
+                                                          unsigned long long* __restrict__ nonfinite) {
+  constexpr uint32_t RPW = 8 / NV;  // rows per warp
+  constexpr uint32_t W = 128 * NV;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t warp_id = blockIdx.x * static_cast<uint64_t>(THREADS / 32) + (threadIdx.x >> 5);
+  const uint64_t r0 = warp_id * RPW;
+  griddep_wait();  // as the ring kernels: the previous kernel completes first
+  if (r0 >= rows) return;
+  float4 v[RPW][NV];
+#pragma unroll
+  for (uint32_t j = 0; j < RPW; ++j)
+#pragma unroll
+    for (uint32_t t = 0; t < NV; ++t)
+      v[j][t] = (r0 + j < rows) ? __ldcs(reinterpret_cast<const float4*>(in + (r0 + j) * stride) + lane + 32 * t)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+  uint64_t first_bad = ~0ull;
+#pragma unroll
+  for (uint32_t j = 0; j < RPW; ++j) {
+    const uint64_t row = r0 + j;
+    if (row >= rows) break;
+    {
+#pragma unroll
+      for (uint32_t t = 0; t < NV; ++t) {
+        const float4 x = v[j][t];
+        const uint32_t i = lane + 32 * t;
+        if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
+          note_nonfinite(x.x, row * W + 4 * i, first_bad); note_nonfinite(x.y, row * W + 4 * i + 1, first_bad);
+          note_nonfinite(x.z, row * W + 4 * i + 2, first_bad); note_nonfinite(x.w, row * W + 4 * i + 3, first_bad);
+        }
+      }
+    }
+    if constexpr (OP == kSum) {
+      double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+#pragma unroll
+      for (uint32_t t = 0; t < NV; ++t) {
+        s0 += static_cast<double>(v[j][t].x); s1 += static_cast<double>(v[j][t].y);
+        s2 += static_cast<double>(v[j][t].z); s3 += static_cast<double>(v[j][t].w);
+      }
+      const double s = warp_sum_d((s0 + s1) + (s2 + s3));
+      if (lane == 0) out[row] = static_cast<float>(s);
+    } else if constexpr (OP == kMax) {
+      float mx = -FLT_MAX;
+#pragma unroll
+      for (uint32_t t = 0; t < NV; ++t) mx = fmaxf(mx, max4(v[j][t]));
+      mx = warp_max_f(mx);
+      if (lane == 0) out[row] = mx;
+    } else if constexpr (OP == kSoftmax) {
+      float mx = -FLT_MAX;
+#pragma unroll
+      for (uint32_t t = 0; t < NV; ++t) mx = fmaxf(mx, max4(v[j][t]));
+      mx = warp_max_f(mx);
+      double sum = 0.0;
+#pragma unroll
+      for (uint32_t t = 0; t < NV; ++t) {
+        v[j][t] = exp4(v[j][t], mx);
+        sum += static_cast<double>(hsum4(v[j][t]));
+      }
+      sum = warp_sum_d(sum);
+      const float inv = static_cast<float>(1.0 / sum);
+      float4* o4 = reinterpret_cast<float4*>(out + row * W);
+#pragma unroll
+      for (uint32_t t = 0; t < NV; ++t) {
+        const float4 e = v[j][t];
+        __stcs(o4 + lane + 32 * t, make_float4(e.x * inv, e.y * inv, e.z * inv, e.w * inv));
+      }
+    } else {  // kRms
+      double ss = 0.0;
+#pragma unroll
+      for (uint32_t t = 0; t < NV; ++t) ss += sq4(v[j][t]);
+      ss = warp_sum_d(ss);
+      const float inv = static_cast<float>(1.0 / sqrt(ss / static_cast<double>(W) + static_cast<double>(eps)));
+      float4* o4 = reinterpret_cast<float4*>(out + row * W);
+      const float4* w4 = reinterpret_cast<const float4*>(weight);
+#pragma unroll
+      for (uint32_t t = 0; t < NV; ++t) {
+        const float4 x = v[j][t];
+        const float4 g = __ldg(w4 + lane + 32 * t);
+        __stcs(o4 + lane + 32 * t, make_float4(x.x * inv * g.x, x.y * inv * g.y, x.z * inv * g.z, x.w * inv * g.w));
+      }
+      if (lane == 0 && inv_rms != nullptr) inv_rms[row] = inv;
+    }
+  }
+  if (first_bad != ~0ull) atomicMin(nonfinite, static_cast<unsigned long long>(first_bad));
+}
+
+template <int OP, int NV>
+cudaError_t launch_reg(const float* in, uint64_t stride, float* out, float* inv_rms, const float* weight, float eps,
+                       uint32_t rows, unsigned long long* nonfinite, cudaStream_t stream) {
+  constexpr uint32_t rows_per_cta = (THREADS / 32) * (8 / NV);
+  const uint64_t grid = (static_cast<uint64_t>(rows) + rows_per_cta - 1) / rows_per_cta;
+  if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
+  return launch_dependent(row_reg_kernel<OP, NV>, dim3(static_cast<uint32_t>(grid)), dim3(THREADS), 0, stream, in,
+                          stride, out, inv_rms, weight, eps, rows, nonfinite);
+}
+
 template <int OP>
 cudaError_t launch_warp(const float* in, uint64_t stride, float* out, float* inv_rms, const float* weight, float eps,
                         uint32_t rows, uint32_t w, unsigned long long* nonfinite, unsigned int* err,
@@ -521,6 +636,9 @@ cudaError_t dispatch(const float* in, uint64_t stride, float* out, float* inv_rm
   const bool rowwise_out = (OP == kSoftmax || OP == kRms);
   const bool aligned = (w % 4 == 0) && (stride % 4 == 0) && a16(in) && (!rowwise_out || a16(out)) &&
                        (weight == nullptr || a16(weight));
+  if (aligned && w == 128) return launch_reg<OP, 1>(in, stride, out, inv_rms, weight, eps, rows, nonfinite, stream);
+  if (aligned && w == 256) return launch_reg<OP, 2>(in, stride, out, inv_rms, weight, eps, rows, nonfinite, stream);
+  if (aligned && w == 512) return launch_reg<OP, 4>(in, stride, out, inv_rms, weight, eps, rows, nonfinite, stream);
   if (aligned && w <= 2048) return launch_warp<OP>(in, stride, out, inv_rms, weight, eps, rows, w, nonfinite, err, stream);
   if (aligned && w <= BULK_MAX_WIDTH)
     return launch_bulk<OP, THREADS>(in, stride, out, inv_rms, weight, eps, rows, w, nonfinite, err, stream);
