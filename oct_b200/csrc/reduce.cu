@@ -400,9 +400,9 @@ __global__ void __launch_bounds__(THREADS) row_warp_kernel(const float* __restri
   }
 }
 
-// Narrow rows (w = 128 * NV, NV <= 4): one warp per row, each lane holding NV
+// Rows of w = 128 * NV (NV <= 16): one warp per row, each lane holding NV
 // float4 of it in registers.  A warp issues the loads of RPW rows at once
-// (NV * RPW = 8 float4 in flight per lane) straight from global memory; with no
+// (NV * RPW >= 8 float4 in flight per lane) straight from global memory; with no
 // shared-memory ring up to 8 CTAs (64 warps) fit on an SM, so at 32768 x 256
 // every row is requested in the first round of loads.  The arithmetic is
 // process_row's for TPR = 32, float4 by float4 in the same order.
@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(THREADS) row_reg_kernel(const float* __restric
                                                           float* __restrict__ out, float* __restrict__ inv_rms,
                                                           const float* __restrict__ weight, float eps, uint32_t rows,
                                                           unsigned long long* __restrict__ nonfinite) {
-  constexpr uint32_t RPW = 8 / NV;  // rows per warp
+  constexpr uint32_t RPW = NV >= 8 ? 1 : 8 / NV;  // rows per warp
   constexpr uint32_t W = 128 * NV;
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t warp_id = blockIdx.x * static_cast<uint64_t>(THREADS / 32) + (threadIdx.x >> 5);
@@ -495,10 +495,126 @@ __global__ void __launch_bounds__(THREADS) row_reg_kernel(const float* __restric
   if (first_bad != ~0ull) atomicMin(nonfinite, static_cast<unsigned long long>(first_bad));
 }
 
+// Rows of 4096: two warps per row, each lane holding 16 float4 of its warp's half;
+// the two halves meet in shared memory.  Four rows per CTA.
+template <int OP>
+__global__ void __launch_bounds__(THREADS) row_reg2_kernel(const float* __restrict__ in, uint64_t stride,
+                                                           float* __restrict__ out, float* __restrict__ inv_rms,
+                                                           const float* __restrict__ weight, float eps, uint32_t rows,
+                                                           unsigned long long* __restrict__ nonfinite) {
+  constexpr uint32_t NV = 16, W = 4096, PAIRS = THREADS / 64;
+  __shared__ double dsh[PAIRS][2];
+  __shared__ float fsh[PAIRS][2];
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t pair = warp >> 1, half = warp & 1u;
+  const uint64_t row = blockIdx.x * static_cast<uint64_t>(PAIRS) + pair;
+  const bool live = row < rows;
+  griddep_wait();  // as the ring kernels: the previous kernel completes first
+  float4 v[NV];
+  const uint32_t q0 = half * 512u + lane;  // float4 index within the row: q0 + 32 t
+#pragma unroll
+  for (uint32_t t = 0; t < NV; ++t)
+    v[t] = live ? __ldcs(reinterpret_cast<const float4*>(in + row * stride) + q0 + 32 * t)
+                : make_float4(0.f, 0.f, 0.f, 0.f);
+  uint64_t first_bad = ~0ull;
+  if (live) {
+#pragma unroll
+    for (uint32_t t = 0; t < NV; ++t) {
+      const float4 x = v[t];
+      const uint64_t i = q0 + 32 * t;
+      if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
+        note_nonfinite(x.x, row * W + 4 * i, first_bad); note_nonfinite(x.y, row * W + 4 * i + 1, first_bad);
+        note_nonfinite(x.z, row * W + 4 * i + 2, first_bad); note_nonfinite(x.w, row * W + 4 * i + 3, first_bad);
+      }
+    }
+  }
+  // sum of the two halves' partials, the same in both warps of the pair
+  auto pair_sum = [&](double p) -> double {
+    p = warp_sum_d(p);
+    if (lane == 0) dsh[pair][half] = p;
+    __syncthreads();
+    const double t = dsh[pair][0] + dsh[pair][1];
+    __syncthreads();
+    return t;
+  };
+  auto pair_max = [&](float p) -> float {
+    p = warp_max_f(p);
+    if (lane == 0) fsh[pair][half] = p;
+    __syncthreads();
+    const float t = fmaxf(fsh[pair][0], fsh[pair][1]);
+    __syncthreads();
+    return t;
+  };
+  if constexpr (OP == kSum) {
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+#pragma unroll
+    for (uint32_t t = 0; t < NV; ++t) {
+      s0 += static_cast<double>(v[t].x); s1 += static_cast<double>(v[t].y);
+      s2 += static_cast<double>(v[t].z); s3 += static_cast<double>(v[t].w);
+    }
+    const double s = pair_sum((s0 + s1) + (s2 + s3));
+    if (live && half == 0 && lane == 0) out[row] = static_cast<float>(s);
+  } else if constexpr (OP == kMax) {
+    float mx = -FLT_MAX;
+#pragma unroll
+    for (uint32_t t = 0; t < NV; ++t) mx = fmaxf(mx, max4(v[t]));
+    mx = pair_max(mx);
+    if (live && half == 0 && lane == 0) out[row] = mx;
+  } else if constexpr (OP == kSoftmax) {
+    float mx = -FLT_MAX;
+#pragma unroll
+    for (uint32_t t = 0; t < NV; ++t) mx = fmaxf(mx, max4(v[t]));
+    mx = pair_max(mx);
+    double sum = 0.0;
+#pragma unroll
+    for (uint32_t t = 0; t < NV; ++t) {
+      v[t] = exp4(v[t], mx);
+      sum += static_cast<double>(hsum4(v[t]));
+    }
+    sum = pair_sum(sum);
+    const float inv = static_cast<float>(1.0 / sum);
+    if (live) {
+      float4* o4 = reinterpret_cast<float4*>(out + row * W);
+#pragma unroll
+      for (uint32_t t = 0; t < NV; ++t) {
+        const float4 e = v[t];
+        __stcs(o4 + q0 + 32 * t, make_float4(e.x * inv, e.y * inv, e.z * inv, e.w * inv));
+      }
+    }
+  } else {  // kRms
+    double ss = 0.0;
+#pragma unroll
+    for (uint32_t t = 0; t < NV; ++t) ss += sq4(v[t]);
+    ss = pair_sum(ss);
+    const float inv = static_cast<float>(1.0 / sqrt(ss / static_cast<double>(W) + static_cast<double>(eps)));
+    if (live) {
+      float4* o4 = reinterpret_cast<float4*>(out + row * W);
+      const float4* w4 = reinterpret_cast<const float4*>(weight);
+#pragma unroll
+      for (uint32_t t = 0; t < NV; ++t) {
+        const float4 x = v[t];
+        const float4 g = __ldg(w4 + q0 + 32 * t);
+        __stcs(o4 + q0 + 32 * t, make_float4(x.x * inv * g.x, x.y * inv * g.y, x.z * inv * g.z, x.w * inv * g.w));
+      }
+      if (half == 0 && lane == 0 && inv_rms != nullptr) inv_rms[row] = inv;
+    }
+  }
+  if (first_bad != ~0ull) atomicMin(nonfinite, static_cast<unsigned long long>(first_bad));
+}
+
+template <int OP>
+cudaError_t launch_reg2(const float* in, uint64_t stride, float* out, float* inv_rms, const float* weight, float eps,
+                        uint32_t rows, unsigned long long* nonfinite, cudaStream_t stream) {
+  const uint64_t grid = (static_cast<uint64_t>(rows) + THREADS / 64 - 1) / (THREADS / 64);
+  if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
+  return launch_dependent(row_reg2_kernel<OP>, dim3(static_cast<uint32_t>(grid)), dim3(THREADS), 0, stream, in,
+                          stride, out, inv_rms, weight, eps, rows, nonfinite);
+}
+
 template <int OP, int NV>
 cudaError_t launch_reg(const float* in, uint64_t stride, float* out, float* inv_rms, const float* weight, float eps,
                        uint32_t rows, unsigned long long* nonfinite, cudaStream_t stream) {
-  constexpr uint32_t rows_per_cta = (THREADS / 32) * (8 / NV);
+  constexpr uint32_t rows_per_cta = (THREADS / 32) * (NV >= 8 ? 1 : 8 / NV);
   const uint64_t grid = (static_cast<uint64_t>(rows) + rows_per_cta - 1) / rows_per_cta;
   if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
   return launch_dependent(row_reg_kernel<OP, NV>, dim3(static_cast<uint32_t>(grid)), dim3(THREADS), 0, stream, in,
@@ -639,6 +755,9 @@ cudaError_t dispatch(const float* in, uint64_t stride, float* out, float* inv_rm
   if (aligned && w == 128) return launch_reg<OP, 1>(in, stride, out, inv_rms, weight, eps, rows, nonfinite, stream);
   if (aligned && w == 256) return launch_reg<OP, 2>(in, stride, out, inv_rms, weight, eps, rows, nonfinite, stream);
   if (aligned && w == 512) return launch_reg<OP, 4>(in, stride, out, inv_rms, weight, eps, rows, nonfinite, stream);
+  if (aligned && w == 1024) return launch_reg<OP, 8>(in, stride, out, inv_rms, weight, eps, rows, nonfinite, stream);
+  if (aligned && w == 2048) return launch_reg<OP, 16>(in, stride, out, inv_rms, weight, eps, rows, nonfinite, stream);
+  if (aligned && w == 4096) return launch_reg2<OP>(in, stride, out, inv_rms, weight, eps, rows, nonfinite, stream);
   if (aligned && w <= 2048) return launch_warp<OP>(in, stride, out, inv_rms, weight, eps, rows, w, nonfinite, err, stream);
   if (aligned && w <= BULK_MAX_WIDTH)
     return launch_bulk<OP, THREADS>(in, stride, out, inv_rms, weight, eps, rows, w, nonfinite, err, stream);
