@@ -30,7 +30,7 @@ CASES = {
     # 256-channel heads take the fused causal CTA-pair attention kernel: one and three query tiles
     "gemma_head256_seq128": (OB.gemma_config(seq_len=128, hidden=512, heads=2, head_dim=256, ffn=1024), 2),
     "gemma_head256_seq384": (OB.gemma_config(seq_len=384, hidden=512, heads=2, head_dim=256, ffn=1024), 2),
-    # the benchmark configurations themselves
+    # the benchmark block configurations themselves (Gemma 4 x 1024 at d 2048, DiT 2 x 4096 at d 3072)
     "gemma_baseline_config": (OB.gemma_config(), 4),
     "dit_baseline_config": (OB.dit_config(), 2),
 }
