@@ -71,11 +71,13 @@ def test_baseline_shapes(runtime, oracle_mod, width, op):
         assert np.array_equal(y, ref)
 
 
-@pytest.mark.parametrize("rows,width", [(30001, 256), (40000, 128), (32768, 512)])
+@pytest.mark.parametrize("rows,width", [(30001, 256), (40000, 128), (32768, 512), (1001, 128), (999, 512), (5, 1024)])
 @pytest.mark.parametrize("op", [R.OP_SUM, R.OP_MAX, R.OP_SOFTMAX])
 def test_tall_short_rows(runtime, oracle_mod, rows, width, op):
     """Tall matrices of short rows whose row count leaves the last ring slot ragged, and
-    rows too many for every warp to hold all of its rows in the ring at once."""
+    rows too many for every warp to hold all of its rows in the ring at once; row counts
+    that leave the last warp of the register-resident kernels (8 / 4 / 2 / 1 rows per warp
+    at widths 128 / 256 / 512 / 1024) part-filled."""
     o = oracle_mod
     x = o.normal_matrix(rows, width, seed=rows + width)
     y, res = runtime.reduction(x, op)
