@@ -350,22 +350,6 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def sgemm_launches_per_product(m: int, n: int, k: int, variant: int) -> int:
-    """Kernels one device-pointer product launches: the FMA control and the in-kernel split
-    one; the split-pass variants split A and B and run the main kernel -- as one launch each,
-    or, for products of at least 2048 x 2048 x 512, in up to four row chunks of A and four
-    column chunks of B with one main launch per (A0, Bj) block and per later A chunk (the
-    library's overlapped split pass)."""
-    if variant in (2, 316, 332):
-        return 1
-    if m >= 2048 and n >= 2048 and k >= 512:
-        rows = -(-(-(-m // 4)) // 256) * 256
-        cols = -(-(-(-n // 4)) // 256) * 256
-        nr, nc = -(-m // rows), -(-n // cols)
-        return nr + nc + nc + (nr - 1)
-    return 3
-
-
 def reduction_measurements(rt, torch, hbm_peak: float) -> list[dict]:
     """Row reductions and RMSNorm at the benchmark shapes (32768 rows x 256 / 2048 / 4096)."""
     from oct_b200 import reactor as R
@@ -917,9 +901,7 @@ def run_ours(args) -> None:
                 "bound": "tensor",
                 "kernel": ("sgemm3x_insm_kernel" if args.variant in (316, 332) else
                            "sgemm3x_pair_kernel" if args.variant in (216, 232) else "sgemm3x_kernel")
-                          + " (tcgen05 kind::tf32, 3 products per k-step"
-                          + ("" if args.variant in (2, 316, 332) else
-                             "; the product's main launches, split pieces overlapped beside them") + ")",
+                          + " (tcgen05 kind::tf32, 3 products per k-step)",
                 "achieved": achieved,
                 "peak": tensor_peak,
                 "unit": "TFLOP/s",
@@ -936,7 +918,8 @@ def run_ours(args) -> None:
             },
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "gpu_launches": sgemm_launches_per_product(m, n, k, args.variant) * args.steps,
+            # FMA and the in-kernel split: one kernel per step; the others: 2 split passes + main
+            "gpu_launches": (1 if args.variant in (2, 316, 332) else 3) * args.steps,
             "clocks": clock_rec,
             "secondary": secondary,
         }

@@ -61,19 +61,9 @@ enum TcConfig : int {
 struct SgemmEvents {
   cudaEvent_t split_begin = nullptr, main_begin = nullptr, main_end = nullptr;
 };
-// Two streams and a set of events (owned by the caller, who serialises the
-// calls that share them) with which sgemm_tc overlaps the split pass of a large
-// single product with its main kernel: the split runs in pieces on `split`, the
-// main kernel as one launch per piece on the caller's stream and `gemm` in turn.
-constexpr uint32_t kSplitOverlapEvents = 12;
-struct SplitOverlap {
-  cudaStream_t split = nullptr, gemm = nullptr;
-  cudaEvent_t ev[kSplitOverlapEvents] = {};
-};
 cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
                      uint32_t m, uint32_t n, uint32_t k, void* scratch, unsigned int* err, int bk,
-                     cudaStream_t stream, const SgemmEvents* events = nullptr, const GemmBatch* batch = nullptr,
-                     const SplitOverlap* overlap = nullptr);
+                     cudaStream_t stream, const SgemmEvents* events = nullptr, const GemmBatch* batch = nullptr);
 // The in-SM split kernel reads A and B in place with TMA: single products whose
 // bases are 16-byte aligned and whose leading dimensions are multiples of 4.
 // It needs no scratch; C = R + A * B when `residual` is given.

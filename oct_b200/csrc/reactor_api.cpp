@@ -97,43 +97,12 @@ uint32_t resolve_variant(uint32_t variant, uint32_t m, uint32_t n, uint32_t k) {
 
 }  // namespace
 
-namespace {
-
-// The handle's split-overlap streams and events, created on first use; null if
-// they cannot be (the product then runs its split pass in one piece).
-const oct::SplitOverlap* split_overlap(Runtime* rt) {
-  if (rt->overlap_ready) return &rt->overlap;
-  bool ok = true;
-  for (cudaStream_t* st : {&rt->overlap.split, &rt->overlap.gemm})
-    if (*st == nullptr && cudaStreamCreateWithFlags(st, cudaStreamNonBlocking) != cudaSuccess) {
-      *st = nullptr;
-      ok = false;
-    }
-  for (cudaEvent_t& ev : rt->overlap.ev)
-    if (ev == nullptr && cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
-      ev = nullptr;
-      ok = false;
-    }
-  if (!ok) {
-    (void)cudaGetLastError();
-    return nullptr;
-  }
-  rt->overlap_ready = true;
-  return &rt->overlap;
-}
-
-}  // namespace
-
 // `scratch` (default: the handle's) holds the TF32 split operands; calls that
-// run concurrently on different streams need different scratch buffers.  Large
-// single (unbatched) products on the handle's own scratch overlap their split
-// pass with the main kernel on the handle's two side streams (the handle's lock
-// orders the calls).
+// run concurrently on different streams need different scratch buffers.
 int oct::rt::enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c,
                            uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, uint32_t variant, cudaStream_t stream,
                            const oct::GemmBatch* batch, DevBuf* scratch) {
   variant = resolve_variant(variant, m, n, k);
-  const bool own_scratch = scratch == nullptr || scratch == &rt->scratch;
   if (scratch == nullptr) scratch = &rt->scratch;
   // the small-M kernels have no batched or B^T form: those take the FMA control
   if ((variant == OCT_B200_SGEMM_SMALLM || variant == OCT_B200_SGEMM_SMALLM_TC) && batch != nullptr &&
@@ -174,7 +143,7 @@ int oct::rt::enqueue_sgemm(Runtime* rt, const float* a, uint64_t lda, const floa
     const oct::SgemmEvents* ev = nullptr;
     if (rt->timing && (ev = next_timing_events(rt)) == nullptr) return OCT_B200_DETAIL_CUDA_ERROR;
     e = oct::sgemm_tc(a, lda, b, ldb, c, ldc, m, n, k, insm ? nullptr : scratch->aligned(), rt->err_word(), bk,
-                      stream, ev, batch, own_scratch && batch == nullptr ? split_overlap(rt) : nullptr);
+                      stream, ev, batch);
   } else {
     return OCT_B200_DETAIL_BAD_VARIANT;
   }
@@ -234,17 +203,6 @@ Runtime* create_runtime(const PrometheusReactorConfig* cfg, int* status) {
 
 void destroy_runtime(Runtime* rt) {
   if (rt->stream != nullptr) cudaStreamSynchronize(rt->stream);
-  for (cudaStream_t* st : {&rt->overlap.split, &rt->overlap.gemm})
-    if (*st != nullptr) {
-      cudaStreamSynchronize(*st);
-      cudaStreamDestroy(*st);
-      *st = nullptr;
-    }
-  for (cudaEvent_t& ev : rt->overlap.ev)
-    if (ev != nullptr) {
-      cudaEventDestroy(ev);
-      ev = nullptr;
-    }
   for (auto& kv : rt->blocks) delete kv.second;
   rt->blocks.clear();
   for (auto& kv : rt->tp_sgemms) delete kv.second;
@@ -682,9 +640,8 @@ int sgemm_host_pipelined(Runtime* rt, const float* a, const float* b, float* c, 
     set_status(out_stage, out_detail_code, PROM_STAGE_INIT, OCT_B200_DETAIL_CUDA_ERROR);
     return PROM_ERROR;
   }
-  // ~16 row chunks of at least 256 rows (the tile-pair height): the last chunk's
-  // product and download are the part of the step that no upload hides
-  const uint32_t rows = std::max<uint32_t>(256u, ((m + 15u) / 16u + 255u) / 256u * 256u);
+  // ~8 row chunks of at least 256 rows (the tile-pair height)
+  const uint32_t rows = std::max<uint32_t>(256u, ((m + 7u) / 8u + 255u) / 256u * 256u);
   const uint32_t nchunks = (m + rows - 1) / rows;
   const uint32_t nev = 2 * nchunks + 1;
   while (rt->pipe_events.size() < nev) {

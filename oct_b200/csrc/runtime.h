@@ -123,10 +123,6 @@ struct Runtime {
   bool timing = false;
   std::vector<oct::SgemmEvents> timing_events;
   size_t timing_used = 0;
-  // Split pass overlapped with the main kernel (large tensor-core products on
-  // the handle's own scratch): created on first use.
-  oct::SplitOverlap overlap;
-  bool overlap_ready = false;
   // Pipelined host SGEMM: upload and download streams, chunk events.
   cudaStream_t copy_in = nullptr, copy_out = nullptr;
   std::vector<cudaEvent_t> pipe_events;

@@ -1295,95 +1295,9 @@ cudaError_t sgemm_tc_insm(const float* a, uint64_t lda, const float* b, uint64_t
   return e;
 }
 
-namespace {
-
-// Large single products with a SplitOverlap: A is split in (up to) four row
-// chunks and B in (up to) four column chunks on the split stream, in the order
-// A0, B0..B3, A1..A3, and the main kernel runs as one launch per block -- (A0,
-// Bj) for each j, then (Ai, all of B) -- alternating between the caller's stream
-// and the overlap's gemm stream, each launch waiting only for the pieces it
-// reads.  Only A0 and B0 are split before the first launch; the other pieces
-// run beside the main kernel (a split CTA fits on an SM next to a main-kernel
-// CTA), and a launch's last wave overlaps the next launch's first.  The chunk
-// edges are multiples of the tile pair (256 rows, 256 columns), so every output
-// tile is the tile of the single launch with the same K order: the same bits.
-bool split_overlap_eligible(uint32_t m, uint32_t n, uint32_t k) { return m >= 2048 && n >= 2048 && k >= 512; }
-
-cudaError_t sgemm_tc_overlapped(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
-                                uint32_t m, uint32_t n, uint32_t k, const SplitDims& d, float* ahi, float* alo,
-                                float* bhi, float* blo, unsigned int* err, int bk, cudaStream_t stream,
-                                const SgemmEvents* events, const SplitOverlap& ov) {
-  constexpr uint32_t kChunks = 4;
-  const uint32_t rows = round_up((m + kChunks - 1) / kChunks, PAIR_BM);
-  const uint32_t cols = round_up((n + kChunks - 1) / kChunks, BN);
-  const uint32_t nr = (m + rows - 1) / rows, nc = (n + cols - 1) / cols;
-  static_assert(2 * kChunks + 2 <= kSplitOverlapEvents, "one event per piece, plus start and join");
-  cudaEvent_t ev_start = ov.ev[0], ev_join = ov.ev[kSplitOverlapEvents - 1];
-  auto ev_b = [&](uint32_t j) { return ov.ev[1 + j]; };           // B0..Bj (and A0) split
-  auto ev_a = [&](uint32_t i) { return ov.ev[1 + kChunks + i]; };  // A1..Ai (and all of B) split
-  cudaError_t e = cudaSuccess;
-  auto ok = [&](cudaError_t x) {
-    if (e == cudaSuccess) e = x;
-    return e == cudaSuccess;
-  };
-  if (events != nullptr && events->split_begin != nullptr) ok(cudaEventRecord(events->split_begin, stream));
-  ok(cudaEventRecord(ev_start, stream));
-  ok(cudaStreamWaitEvent(ov.split, ev_start, 0));
-  ok(cudaStreamWaitEvent(ov.gemm, ev_start, 0));
-  if (e != cudaSuccess) return e;
-  auto split_a = [&](uint32_t i) {
-    const uint32_t r0 = i * rows, rc = std::min(rows, m - r0), rp = std::min(rows, d.mp - r0);
-    const uint64_t groups = static_cast<uint64_t>(rp) * (d.kp / 4);
-    const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((groups + 255) / 256, 148ull * 16));
-    split_rows_kernel<<<dim3(blocks, 1), 256, 0, ov.split>>>(a + static_cast<uint64_t>(r0) * lda, lda, rc, k,
-                                                               ahi + static_cast<uint64_t>(r0) * d.kp,
-                                                               alo + static_cast<uint64_t>(r0) * d.kp, rp, d.kp,
-                                                               EntryStride{});
-    return ok(cudaGetLastError());
-  };
-  auto split_b = [&](uint32_t j) {
-    const uint32_t c0 = j * cols, cn = std::min(cols, n - c0), cp = std::min(cols, d.np - c0);
-    split_transpose_kernel<<<dim3(cp / 32, d.kp / 32, 1), 256, 0, ov.split>>>(
-        b + c0, ldb, k, cn, bhi + static_cast<uint64_t>(c0) * d.kp, blo + static_cast<uint64_t>(c0) * d.kp, d.kp,
-        cp, EntryStride{});
-    return ok(cudaGetLastError());
-  };
-  uint32_t launches = 0;
-  auto run = [&](uint32_t r0, uint32_t c0, uint32_t span, cudaEvent_t ready) {
-    cudaStream_t st = (launches++ & 1u) ? ov.gemm : stream;
-    if (!ok(cudaStreamWaitEvent(st, ready, 0))) return false;
-    if (launches == 1 && events != nullptr && events->main_begin != nullptr &&
-        !ok(cudaEventRecord(events->main_begin, st)))
-      return false;
-    const uint32_t rc = std::min(rows, m - r0), rp = std::min(rows, d.mp - r0);
-    const uint32_t cn = std::min(span, n - c0), cp = std::min(span, d.np - c0);
-    const SplitDims db{rp, cp, d.kp};
-    return ok(launch_config(bk, ahi + static_cast<uint64_t>(r0) * d.kp, alo + static_cast<uint64_t>(r0) * d.kp,
-                            bhi + static_cast<uint64_t>(c0) * d.kp, blo + static_cast<uint64_t>(c0) * d.kp,
-                            c + static_cast<uint64_t>(r0) * ldc + c0, ldc, rc, cn, db, err, st, 1, EntryStride{}));
-  };
-  bool enqueued = split_a(0);
-  for (uint32_t j = 0; enqueued && j < nc; ++j) enqueued = split_b(j) && ok(cudaEventRecord(ev_b(j), ov.split));
-  for (uint32_t i = 1; enqueued && i < nr; ++i) enqueued = split_a(i) && ok(cudaEventRecord(ev_a(i), ov.split));
-  for (uint32_t j = 0; enqueued && j < nc; ++j) enqueued = run(0, j * cols, cols, ev_b(j));
-  for (uint32_t i = 1; enqueued && i < nr; ++i) enqueued = run(i * rows, 0, d.np, ev_a(i));
-  // join, failed or not: the caller's stream waits for all the work of both side streams
-  cudaError_t j1 = cudaEventRecord(ev_join, ov.gemm);
-  if (j1 == cudaSuccess) j1 = cudaStreamWaitEvent(stream, ev_join, 0);
-  cudaError_t j2 = cudaEventRecord(ev_join, ov.split);
-  if (j2 == cudaSuccess) j2 = cudaStreamWaitEvent(stream, ev_join, 0);
-  ok(j1);
-  ok(j2);
-  if (events != nullptr && events->main_end != nullptr) ok(cudaEventRecord(events->main_end, stream));
-  return e;
-}
-
-}  // namespace
-
 cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb, float* c, uint64_t ldc,
                      uint32_t m, uint32_t n, uint32_t k, void* scratch, unsigned int* err, int bk,
-                     cudaStream_t stream, const SgemmEvents* events, const GemmBatch* batch,
-                     const SplitOverlap* overlap) {
+                     cudaStream_t stream, const SgemmEvents* events, const GemmBatch* batch) {
   if (m == 0 || n == 0 || k == 0) return cudaSuccess;
   if (bk == kTcInsm16 || bk == kTcInsm32) {
     if (sgemm_insm_eligible(a, lda, b, ldb, m, n, k, batch))
@@ -1404,9 +1318,6 @@ cudaError_t sgemm_tc(const float* a, uint64_t lda, const float* b, uint64_t ldb,
   float* alo = ahi + a_elems;
   float* bhi = alo + a_elems;
   float* blo = bhi + b_elems;
-  if (overlap != nullptr && bt.count == 1 && !bt.b_trans && split_overlap_eligible(m, n, k))
-    return sgemm_tc_overlapped(a, lda, b, ldb, c, ldc, m, n, k, d, ahi, alo, bhi, blo, err, bk, stream, events,
-                               *overlap);
 
   if (events != nullptr && events->split_begin != nullptr) cudaEventRecord(events->split_begin, stream);
   const uint64_t groups = static_cast<uint64_t>(d.mp) * (d.kp / 4);

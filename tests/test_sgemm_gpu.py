@@ -277,36 +277,6 @@ def test_in_kernel_split_reads_ragged_operands_in_place(runtime, oracle_mod, sha
                         rows=slice(0, min(m, 64)))
 
 
-@pytest.mark.parametrize("variant", [R.SGEMM_AUTO, R.SGEMM_TC_BK32, R.SGEMM_TC_PAIR16, R.SGEMM_TC_PAIR32])
-@pytest.mark.parametrize("shape", [(2048, 2048, 512), (4097, 4095, 1023), (6000, 5000, 777)])
-def test_overlapped_split_pass_gives_the_same_bits(runtime, oracle_mod, shape, variant):
-    """A large single product splits A (row chunks) and B (column chunks) on a side stream
-    while the main kernel runs one launch per chunk on two streams; the strided-batch entry
-    with one entry splits both operands in one piece before one launch.  Chunk edges are
-    multiples of 256, so both give the same bits; the padding past k and n is never read and
-    the columns of C past n stay untouched."""
-    import torch
-    o = oracle_mod
-    m, n, k = shape
-    lda, ldb, ldc = k + 5, n + 3, n + 7
-    a = o.uniform_matrix(m, k, m + 7).reshape(m, k)
-    b = o.uniform_matrix(k, n, n + 9).reshape(k, n)
-    da = torch.full((m, lda), float("nan"), device="cuda")
-    db = torch.full((k, ldb), float("nan"), device="cuda")
-    da[:, :k] = torch.from_numpy(a).cuda()
-    db[:, :n] = torch.from_numpy(b).cuda()
-    d1 = torch.full((m, ldc), -3.0, device="cuda")
-    d2 = torch.full((m, ldc), -3.0, device="cuda")
-    runtime.sgemm_device(da, db, d1, m, n, k, variant, lda=lda, ldb=ldb, ldc=ldc)
-    runtime.sgemm_batched_device(da, lda, 0, db, ldb, 0, False, d2, ldc, 0, 1, m, n, k, variant)
-    assert runtime.sync_status().ok
-    c1, c2 = d1.cpu().numpy(), d2.cpu().numpy()
-    assert np.all(c1[:, n:] == -3.0)
-    assert np.array_equal(c1, c2)
-    _check_against_fp64(o, np.ascontiguousarray(c1[:, :n]).ravel(), a.ravel(), b.ravel(), m, n, k,
-                        rows=slice(m - 64, m))
-
-
 def test_variants_agree_with_batched_and_transposed_forms(runtime, oracle_mod):
     """Strided-batch and B^T (NT) forms equal per-entry products (attention's Q K^T and P V)."""
     import torch
