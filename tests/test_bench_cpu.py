@@ -91,12 +91,13 @@ def test_reference_arm_runs_on_rank_zero_only():
     assert out.stdout.strip() == ""
 
 
-def test_roofline_peak_is_the_burst_peak_scaled_by_the_clock_record():
+def test_roofline_peak_is_the_unscaled_burst_peak_with_the_clock_scaled_figure_beside_it():
     import bench
     pk = {"bf16_tflops": 1642.6, "bf16_tflops_sustained": 1377.5, "sm_max_mhz": 1965.0}
     peak, note = bench.tensor_roofline_peak(pk, "measured", {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0})
     assert abs(peak - 1642.6 / 6) < 1e-9 and "maximum clock" in note
     peak, note = bench.tensor_roofline_peak(pk, "measured", {"sm_mhz": 1572.0, "sm_max_mhz": 1965.0})
-    assert abs(peak - 1642.6 / 6 * 0.8) < 1e-9 and "scaled" in note
+    assert abs(peak - 1642.6 / 6) < 1e-9 and "not scaled" in note and "0.800" in note
+    assert abs(bench.clock_scaled_peak(pk, {"sm_mhz": 1572.0, "sm_max_mhz": 1965.0}) - 1642.6 / 6 * 0.8) < 1e-9
     peak, _ = bench.tensor_roofline_peak(pk, "measured", {"sm_mhz": None, "sm_max_mhz": None})
     assert abs(peak - 1642.6 / 6) < 1e-9
