@@ -742,15 +742,25 @@ int Block::set_weight(uint32_t slot, const float* src, uint64_t count, bool on_d
   return cudaStreamSynchronize(stream_) == cudaSuccess ? 0 : -4;
 }
 
+// Products of at least 2048 x 2048 run on the CTA-pair kernel with 32-deep
+// stages (faster under the power cap; same MMAs in the same order, so the same
+// bits); smaller ones, and those whose epilogue scatters rows to the tensor-
+// parallel peers (a single-CTA epilogue), on the single-CTA kernel.
+static int block_cfg(uint32_t m, uint32_t n, const RowScatter* scatter) {
+  const bool scatters = scatter != nullptr && scatter->dst != nullptr;
+  return (!scatters && m >= 2048 && n >= 2048) ? kTcPair32 : kTcSingle16;
+}
+
 cudaError_t Block::gemm(const float* a, uint64_t lda, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
                         const float* residual, uint64_t ldr, const RowScatter* scatter) {
   return sgemm_tc_presplit(a, lda, w.hi, w.lo, c, ldc, m, w.n, w.k, scratch_, err_, stream_, residual, ldr,
-                           kTcSingle16, scatter);
+                           block_cfg(m, w.n, scatter), scatter);
 }
 
 cudaError_t Block::gemm_ab(const float* ahi, const float* alo, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
                            const float* residual, uint64_t ldr) {
-  return sgemm_tc_presplit_ab(ahi, alo, w.hi, w.lo, c, ldc, m, w.n, w.k, err_, stream_, residual, ldr);
+  return sgemm_tc_presplit_ab(ahi, alo, w.hi, w.lo, c, ldc, m, w.n, w.k, err_, stream_, residual, ldr,
+                              block_cfg(m, w.n, nullptr));
 }
 
 cudaError_t Block::all_reduce(float* buf, uint64_t count) {
