@@ -1457,7 +1457,8 @@ PROM_REACTOR_API int prometheus_runtime_probe(void* handle, PrometheusCaps* out_
 
 /* SGEMM kernel variants. */
 enum {
-  OCT_B200_SGEMM_AUTO = 0u,       /* small-M kernel for m <= 16, else 3xTF32 tcgen05; FMA for tiny products */
+  OCT_B200_SGEMM_AUTO = 0u,       /* small-M kernel for m <= 16; FMA for tiny products; the CTA pair with 32-deep
+                                     stages (232) for m, n >= 2048; else 3xTF32 tcgen05 (1) */
   OCT_B200_SGEMM_TC3XTF32 = 1u,   /* tcgen05/TMEM tensor cores, split-TF32 x3 */
   OCT_B200_SGEMM_FMA = 2u,        /* plain FP32 FMA on the CUDA cores (control) */
   OCT_B200_SGEMM_SMALLM = 3u,     /* m <= 16: HBM-bound CUDA-core kernel, split-K, ordered reduction */
