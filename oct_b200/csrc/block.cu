@@ -502,6 +502,8 @@ cudaError_t Block::tp_phase(uint32_t slot) {
   return tp_signal_wait(flag_peers_, flags_, slot, dims_.tp_world, dims_.tp_rank, epoch_, err_, kPeerWaitNs, stream_);
 }
 
+static int block_cfg(uint32_t m, uint32_t n, const RowScatter* scatter);  // below, beside the products
+
 int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t stream) {
   dims_ = d;
   stream_ = stream;
@@ -560,7 +562,7 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
   }
   if (want_fused_tp) {
     const uint64_t rpr = (T + d.tp_world - 1) / d.tp_world;  // rows per rank at max_batch
-    rs_ = sym_alloc(rpr * d.tp_world * d.hidden);
+    rs_ = sym_alloc(rpr * d.tp_world * kMaxScatterRanges * d.hidden);
     ysym_ = sym_alloc(T * d.hidden);
     flags_ = reinterpret_cast<uint64_t*>(sym_alloc(2ull * kTpSlots * d.tp_world));
     if (rs_ == nullptr || ysym_ == nullptr || flags_ == nullptr ||
@@ -611,6 +613,23 @@ int Block::init(const BlockDims& d, const NcclUniqueIdBytes* id, cudaStream_t st
                   : std::max(sgemm_tc_scratch_bytes(d.seq_len, d.seq_len, d.head_dim, d.max_batch * d.heads),
                              static_cast<uint64_t>(2ull * sizeof(float) * d.max_batch * d.heads * vd.np * vd.kp));
   scratch_ = alloc(std::max(a_need, b_need) / sizeof(float) + 1);
+  // split-K partials: the largest need of the products at the full token count
+  // (shorter batches that would need more take fewer ranges)
+  {
+    const std::pair<uint32_t, uint32_t> nk[] = {{qkv_cols, d.hidden}, {d.hidden, attn_cols},
+                                                {2 * d.ffn, d.hidden}, {d.hidden, d.ffn}};
+    uint64_t cap = 0;
+    for (const auto& p : nk) {
+      const uint32_t n = p.first, kk = p.second;
+      if (block_cfg(static_cast<uint32_t>(T), n, nullptr) != kTcSingle16) continue;
+      const uint32_t r = sgemm_tc_pick_k_ranges(static_cast<uint32_t>(T), n, kk);
+      if (r > 1) cap = std::max(cap, static_cast<uint64_t>(sgemm_tc_k_ranges(kk, r)) * T * n);
+    }
+    if (cap > 0) {
+      splitk_ = alloc(cap);
+      splitk_cap_ = splitk_ != nullptr ? cap : 0;
+    }
+  }
   err_ = reinterpret_cast<unsigned int*>(alloc(4));
   ok = ok && hbuf_ && qkv_ && attn_ && x1_ && proj_ && gu_ && act_ && scratch_ && err_;
   if (!ok) return -3;
@@ -751,16 +770,47 @@ static int block_cfg(uint32_t m, uint32_t n, const RowScatter* scatter) {
   return (!scatters && m >= 2048 && n >= 2048) ? kTcPair32 : kTcSingle16;
 }
 
+// Single-CTA products under one wave of tiles (the tensor-parallel shards and
+// short batches) run split K: a scattering product in up to kMaxScatterRanges
+// ranges (its partials land in that many owner slots per rank), the others in
+// as many as the partial buffer holds.  The count is fixed per block and
+// product, from the block's largest token count, so a sequence's output does
+// not depend on the batch it runs in (a product that takes the CTA-pair kernel
+// at that count never splits; single and pair give the same bits); every rank
+// takes the same decision.
+uint32_t Block::k_ranges(uint32_t n, uint32_t k, bool scatter) const {
+  const uint32_t tmax = dims_.max_batch * dims_.seq_len;
+  if (!scatter && block_cfg(tmax, n, nullptr) != kTcSingle16) return 1;
+  const uint32_t r = sgemm_tc_pick_k_ranges(tmax, n, k);
+  if (r <= 1) return 1;
+  if (scatter) return std::min(r, kMaxScatterRanges);
+  const uint64_t need = static_cast<uint64_t>(sgemm_tc_k_ranges(k, r)) * tmax * n;
+  return need <= splitk_cap_ ? r : 1;
+}
+
 cudaError_t Block::gemm(const float* a, uint64_t lda, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
-                        const float* residual, uint64_t ldr, const RowScatter* scatter) {
-  return sgemm_tc_presplit(a, lda, w.hi, w.lo, c, ldc, m, w.n, w.k, scratch_, err_, stream_, residual, ldr,
-                           block_cfg(m, w.n, scatter), scatter);
+                        const float* residual, uint64_t ldr, const RowScatter* scatter, uint32_t* ranges) {
+  const int cfg = block_cfg(m, w.n, scatter);
+  const bool scatters = scatter != nullptr && scatter->dst != nullptr;
+  SplitK sk;
+  if (cfg == kTcSingle16) {
+    sk.ranges = k_ranges(w.n, w.k, scatters);
+    sk.partial = splitk_;
+  }
+  if (ranges != nullptr) *ranges = sgemm_tc_k_ranges(w.k, sk.ranges);
+  return sgemm_tc_presplit(a, lda, w.hi, w.lo, c, ldc, m, w.n, w.k, scratch_, err_, stream_, residual, ldr, cfg,
+                           scatter, &sk);
 }
 
 cudaError_t Block::gemm_ab(const float* ahi, const float* alo, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
                            const float* residual, uint64_t ldr) {
-  return sgemm_tc_presplit_ab(ahi, alo, w.hi, w.lo, c, ldc, m, w.n, w.k, err_, stream_, residual, ldr,
-                              block_cfg(m, w.n, nullptr));
+  const int cfg = block_cfg(m, w.n, nullptr);
+  SplitK sk;
+  if (cfg == kTcSingle16) {
+    sk.ranges = k_ranges(w.n, w.k, false);
+    sk.partial = splitk_;
+  }
+  return sgemm_tc_presplit_ab(ahi, alo, w.hi, w.lo, c, ldc, m, w.n, w.k, err_, stream_, residual, ldr, cfg, &sk);
 }
 
 cudaError_t Block::all_reduce(float* buf, uint64_t count) {
@@ -877,10 +927,12 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
     if (!ok()) return -4;
     if (tpf) {
       // partial O Wo rows -> their owners; owners: x1 = x + sum, h = RMSNorm(x1) -> every rank
-      e = gemm(attn_, attn_cols, wo_, rs_, d.hidden, T, nullptr, 0, &sc);
+      uint32_t ranges = 1;
+      e = gemm(attn_, attn_cols, wo_, rs_, d.hidden, T, nullptr, 0, &sc, &ranges);
       if (ok()) e = tp_phase(0);
       if (!ok()) return -4;
       TpReduce r = red;
+      r.nslots = d.tp_world * ranges;  // each rank's partials arrive in `ranges` slots
       r.res = x;
       r.ld_res = d.hidden;
       r.keep = x1_;
@@ -907,10 +959,12 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
     if (!ok()) return -4;
     if (tpf) {
       // partial act Wd rows -> owners; owners: y = x1 + sum -> every rank
-      e = gemm(act_, d.ffn, wd_, rs_, d.hidden, T, nullptr, 0, &sc);
+      uint32_t ranges = 1;
+      e = gemm(act_, d.ffn, wd_, rs_, d.hidden, T, nullptr, 0, &sc, &ranges);
       if (ok()) e = tp_phase(2);
       if (!ok()) return -4;
       TpReduce r = red;
+      r.nslots = d.tp_world * ranges;  // each rank's partials arrive in `ranges` slots
       r.res = x1_;
       r.ld_res = d.hidden;
       r.push = y_peers_;
@@ -984,10 +1038,12 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
   if (tpf) {
     // partial attn Wo rows -> owners; owners: x1 = x + gate_a * RMSNorm(sum),
     // h = RMSNorm(x1) * scale_m + shift_m -> every rank
-    e = gemm(attn_, attn_cols, wo_, rs_, d.hidden, T, nullptr, 0, &sc);
+    uint32_t ranges = 1;
+    e = gemm(attn_, attn_cols, wo_, rs_, d.hidden, T, nullptr, 0, &sc, &ranges);
     if (ok()) e = tp_phase(0);
     if (!ok()) return -4;
     TpReduce r = red;
+    r.nslots = d.tp_world * ranges;  // each rank's partials arrive in `ranges` slots
     r.mod_stride = ms;
     r.g1 = norm2_;
     r.gate1 = gate_a;
@@ -1023,10 +1079,12 @@ int Block::forward(const float* x, float* y, uint32_t batch, const float* timest
   if (!ok()) return -4;
   if (tpf) {
     // partial act W2 rows -> owners; owners: y = x1 + gate_m * RMSNorm(sum) -> every rank
-    e = gemm(act_, d.ffn, wd_, rs_, d.hidden, T, nullptr, 0, &sc);
+    uint32_t ranges = 1;
+    e = gemm(act_, d.ffn, wd_, rs_, d.hidden, T, nullptr, 0, &sc, &ranges);
     if (ok()) e = tp_phase(2);
     if (!ok()) return -4;
     TpReduce r = red;
+    r.nslots = d.tp_world * ranges;  // each rank's partials arrive in `ranges` slots
     r.mod_stride = ms;
     r.g1 = norm4_;
     r.gate1 = gate_m;

@@ -95,8 +95,13 @@ class Block {
   };
   float* alloc(uint64_t floats);
   int build_rope_tables();
+  // `ranges`: the K ranges the product ran in (a scattering product fills that
+  // many slots per rank at the owner)
   cudaError_t gemm(const float* a, uint64_t lda, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
-                   const float* residual = nullptr, uint64_t ldr = 0, const RowScatter* scatter = nullptr);
+                   const float* residual = nullptr, uint64_t ldr = 0, const RowScatter* scatter = nullptr,
+                   uint32_t* ranges = nullptr);
+  // split-K range count of this block's (n, k) product on the single-CTA kernel
+  uint32_t k_ranges(uint32_t n, uint32_t k, bool scatter) const;
   // C = R + A * W with A already split by its producer (hi, lo rows of length w.k)
   cudaError_t gemm_ab(const float* ahi, const float* alo, const SplitW& w, float* c, uint64_t ldc, uint32_t m,
                       const float* residual = nullptr, uint64_t ldr = 0);
@@ -129,6 +134,10 @@ class Block {
   bool fused_attn_ = false;
   float *qsplit_ = nullptr, *ksplit_ = nullptr, *vtsplit_ = nullptr;
   unsigned int* err_ = nullptr;
+  // split-K partial products of the products under one wave (splitk_cap_ floats)
+  float* splitk_ = nullptr;
+  uint64_t splitk_cap_ = 0;
+  static constexpr uint32_t kMaxScatterRanges = 4;  // K ranges of a scattering product (owner slots per rank)
   // Fused tensor parallel: the row-parallel products scatter their partial rows
   // into the owner rank's `rs_` slots; owners reduce and push finished rows into
   // every rank's `hbuf_` / `ysym_`.  Flags: [5 slots][world] u64 epochs.

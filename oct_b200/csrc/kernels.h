@@ -96,17 +96,34 @@ struct RowScatter {
   uint32_t bcast = 0;
   uint64_t col_offset = 0;
 };
+// Split K for products that fill less than one wave of SMs (single-CTA
+// configurations only): K in `ranges` ranges of whole 64-deep accumulation
+// chunks (sgemm_tc_k_ranges gives how many run), one CTA per (tile, range).
+// Without a row scatter the ranges' partial products go to `partial`
+// (ranges * m * n floats) and a second kernel sums them in range order into
+// C = R + sum; with one, range j goes to slot src_rank * ranges + j of the
+// owner rank, whose reduction sums the slots in order.
+struct SplitK {
+  uint32_t ranges = 1;
+  float* partial = nullptr;
+};
+uint32_t sgemm_tc_k_ranges(uint32_t k, uint32_t ranges);
+// The range count for an (m, n, k) product on the single-CTA kernel: 1 when
+// its 128 x 256 tiles fill a wave, else the count (<= 8, each range >= 128 of
+// K) whose CTAs fill the waves they start best.
+uint32_t sgemm_tc_pick_k_ranges(uint32_t m, uint32_t n, uint32_t k);
 cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, const float* blo, float* c,
                               uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* a_scratch, unsigned int* err,
                               cudaStream_t stream, const float* residual = nullptr, uint64_t ldr = 0,
-                              int cfg = kTcSingle16, const RowScatter* scatter = nullptr);
+                              int cfg = kTcSingle16, const RowScatter* scatter = nullptr,
+                              const SplitK* splitk = nullptr);
 
 // A and B both already split: A hi/lo rows of length Kp (split_dims), written by
 // the kernel that produced A; C = R + A * B as in sgemm_tc_presplit.
 cudaError_t sgemm_tc_presplit_ab(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
                                  uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, unsigned int* err,
                                  cudaStream_t stream, const float* residual = nullptr, uint64_t ldr = 0,
-                                 int cfg = kTcSingle16);
+                                 int cfg = kTcSingle16, const SplitK* splitk = nullptr);
 
 // A already split by its producer (hi/lo in the [count][Mp][Kp] layout of
 // split_dims, zero padded); B is split into b_scratch.  Strided batch as GemmBatch.

@@ -149,10 +149,10 @@ template <int BK>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     sgemm3x_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                    const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
-                   float* __restrict__ c, uint32_t m, uint32_t n, uint64_t ldc, uint32_t num_kb,
+                   float* __restrict__ c, uint32_t m, uint32_t n, uint64_t ldc, uint32_t kb_total,
                    uint32_t tiles_m, uint32_t tiles_n, uint32_t entry_rows_a, uint32_t entry_rows_b,
                    EntryStride stride_c, const float* __restrict__ residual, uint64_t ldr,
-                   unsigned int* __restrict__ err, const RowScatter scatter) {
+                   unsigned int* __restrict__ err, const RowScatter scatter, uint32_t kb_split) {
   using Cfg = TileCfg<BK>;
   constexpr uint32_t S = Cfg::STAGES;
   constexpr uint32_t KBC = KC / BK;  // k-blocks per accumulation chunk
@@ -169,13 +169,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __shared__ uint32_t issued_kb, consumed_kb, aborted;
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t num_chunks = (num_kb + KBC - 1) / KBC;
 
   // Batch entry, then grouped rasterisation inside it: GROUP_M tile rows
   // sweep all tile columns together.  Split buffers stack the batch entries
   // along rows (Mp and Np rows each), so a tile never straddles two entries.
+  // Split K (kb_split > 0): entry e is the K range [e * kb_split, ...) of one
+  // product (the host passes zero entry rows), written to its own slice of C
+  // (or, scattering, to its own slot of the owner rank).
   const uint32_t tiles_per_entry = tiles_m * tiles_n;
   const uint32_t entry = blockIdx.x / tiles_per_entry;
+  const uint32_t kb0 = kb_split != 0u ? entry * kb_split : 0u;
+  const uint32_t num_kb = kb_split != 0u ? min(kb_total - kb0, kb_split) : kb_total;
+  const uint32_t num_chunks = (num_kb + KBC - 1) / KBC;
   const uint32_t t = blockIdx.x % tiles_per_entry;
   const uint32_t per_group = GROUP_M * tiles_n;
   const uint32_t first_m = (t / per_group) * GROUP_M;
@@ -229,7 +234,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (__any_sync(0xffffffffu, *(volatile uint32_t*)&aborted != 0u)) break;
       uint8_t* st = smem + s * Cfg::STAGE_BYTES;
-      const int kx = static_cast<int>(kb * BK);
+      const int kx = static_cast<int>((kb0 + kb) * BK);
       if (elect_one()) {
         mbar_arrive_expect_tx(&full_bar[s], Cfg::STAGE_BYTES);
         tma_load_2d(st, &tm_ahi, &full_bar[s], kx, row_a);
@@ -363,8 +368,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t row = tile_m * BM + lr;
           if (row >= m) break;
           const uint32_t owner = row / scatter.rows_per_rank;
+          const uint32_t slot = scatter.src_rank + (kb_split != 0u ? entry : 0u);
           const uint64_t slot_row =
-              static_cast<uint64_t>(scatter.src_rank) * scatter.rows_per_rank + (row - owner * scatter.rows_per_rank);
+              static_cast<uint64_t>(slot) * scatter.rows_per_rank + (row - owner * scatter.rows_per_rank);
           float* drow = scatter.dst[owner] + slot_row * scatter.ld;
           const float* srow = stage_tile + lr * LDS;
 #pragma unroll
@@ -1012,11 +1018,23 @@ bool make_operand_map(CUtensorMap* map, const float* base, uint32_t rows, uint32
 }
 
 template <int BK>
+// ksplit > 1 (single products only): K in that many ranges of whole
+// accumulation chunks (splitk_ranges), one batch entry each; C then receives
+// the ranges' partial products in slices of stride m * ldc (no residual), or,
+// scattering, each range goes to its own slot of the owner rank.
 cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
                         uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
                         cudaStream_t stream, uint32_t batch, EntryStride stride_c, const float* residual = nullptr,
-                        uint64_t ldr = 0, const RowScatter* scatter = nullptr) {
+                        uint64_t ldr = 0, const RowScatter* scatter = nullptr, uint32_t ksplit = 1) {
   using Cfg = TileCfg<BK>;
+  uint32_t kb_split = 0;
+  if (ksplit > 1) {
+    if (batch != 1 || residual != nullptr || (scatter != nullptr && scatter->bcast > 0)) return cudaErrorInvalidValue;
+    const uint32_t kbc = KC / BK, chunks = (d.kp / BK + kbc - 1) / kbc;
+    kb_split = (chunks + ksplit - 1) / ksplit * kbc;
+    batch = (d.kp / BK + kb_split - 1) / kb_split;
+    stride_c = EntryStride{static_cast<uint64_t>(m) * ldc, 0, 0};
+  }
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
   const uint32_t rows_a = d.mp * batch, rows_b = d.np * batch;
   if (!make_operand_map(&m_ahi, ahi, rows_a, d.kp, BK, BM) || !make_operand_map(&m_alo, alo, rows_a, d.kp, BK, BM) ||
@@ -1029,13 +1047,15 @@ cudaError_t launch_main(const float* ahi, const float* alo, const float* bhi, co
   const uint32_t tiles_m = (m + BM - 1) / BM, tiles_n = (n + BN - 1) / BN;
   const uint64_t grid = static_cast<uint64_t>(tiles_m) * tiles_n * batch;
   if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
-  const RowScatter sc = scatter != nullptr ? *scatter : RowScatter{};
-  if (sc.dst != nullptr && (batch != 1 || (sc.rows_per_rank == 0 && sc.bcast == 0) || sc.ld % 4 != 0 ||
-                            ldc % 4 != 0 || sc.col_offset % 4 != 0 || (sc.bcast > 0 && sc.src_rank >= sc.bcast)))
+  RowScatter sc = scatter != nullptr ? *scatter : RowScatter{};
+  if (sc.dst != nullptr && ((batch != 1 && kb_split == 0) || (sc.rows_per_rank == 0 && sc.bcast == 0) ||
+                            sc.ld % 4 != 0 || ldc % 4 != 0 || sc.col_offset % 4 != 0 ||
+                            (sc.bcast > 0 && sc.src_rank >= sc.bcast)))
     return cudaErrorInvalidValue;
+  if (sc.dst != nullptr && kb_split != 0) sc.src_rank *= batch;  // range e lands in slot src_rank * ranges + e
   sgemm3x_kernel<BK><<<static_cast<uint32_t>(grid), NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(
-      m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, d.mp, d.np, stride_c, residual, ldr,
-      err, sc);
+      m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, kb_split ? 0u : d.mp,
+      kb_split ? 0u : d.np, stride_c, residual, ldr, err, sc, kb_split);
   return cudaGetLastError();
 }
 
@@ -1122,13 +1142,13 @@ cudaError_t launch_pair(const float* ahi, const float* alo, const float* bhi, co
 cudaError_t launch_config(int cfg, const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
                           uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
                           cudaStream_t stream, uint32_t batch, EntryStride stride_c, const float* residual = nullptr,
-                          uint64_t ldr = 0, const RowScatter* scatter = nullptr) {
-  // the CTA-pair kernels have no row-scatter epilogue
-  if (scatter != nullptr && scatter->dst != nullptr && cfg != kTcSingle16 && cfg != kTcSingle32)
+                          uint64_t ldr = 0, const RowScatter* scatter = nullptr, uint32_t ksplit = 1) {
+  // the CTA-pair kernels have no row-scatter epilogue and no split-K form
+  if (((scatter != nullptr && scatter->dst != nullptr) || ksplit > 1) && cfg != kTcSingle16 && cfg != kTcSingle32)
     return cudaErrorInvalidValue;
   switch (cfg) {
-    case kTcSingle16: return launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr, scatter);
-    case kTcSingle32: return launch_main<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr, scatter);
+    case kTcSingle16: return launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr, scatter, ksplit);
+    case kTcSingle32: return launch_main<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr, scatter, ksplit);
     case kTcPair16: return launch_pair<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
     case kTcPair32: return launch_pair<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
     default: return cudaErrorInvalidValue;
@@ -1172,10 +1192,82 @@ uint64_t sgemm_tc_a_scratch_bytes(uint32_t m, uint32_t k) {
   return 2ull * sizeof(float) * d.mp * d.kp;
 }
 
+namespace {
+
+// C = R + (P_0 + P_1 + ... ) over the K ranges' partial products P_j
+// (ranges * m * n floats, range-major), in range order; R optional.  Rows step
+// by blockIdx.y, columns by the x threads (coalesced; no index division).
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ p, uint32_t ranges, uint32_t m,
+                                                            uint32_t n, const float* __restrict__ residual,
+                                                            uint64_t ldr, float* __restrict__ c, uint64_t ldc) {
+  const uint64_t total = static_cast<uint64_t>(m) * n;
+  for (uint32_t row = blockIdx.y; row < m; row += gridDim.y) {
+    const float* pr = p + static_cast<uint64_t>(row) * n;
+    for (uint32_t col = blockIdx.x * 256u + threadIdx.x; col < n; col += gridDim.x * 256u) {
+      float s = pr[col];
+      for (uint32_t j = 1; j < ranges; ++j) s += pr[j * total + col];
+      if (residual != nullptr) s = residual[static_cast<uint64_t>(row) * ldr + col] + s;
+      c[static_cast<uint64_t>(row) * ldc + col] = s;
+    }
+  }
+}
+
+// The product on the prepared split operands, split K or not (see SplitK).
+cudaError_t run_split_k(int cfg, const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
+                        uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, const SplitDims& d, unsigned int* err,
+                        cudaStream_t stream, const float* residual, uint64_t ldr, const RowScatter* scatter,
+                        const SplitK* splitk) {
+  const uint32_t ranges = splitk != nullptr ? sgemm_tc_k_ranges(k, splitk->ranges) : 1u;
+  if (ranges <= 1)
+    return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, EntryStride{}, residual, ldr,
+                         scatter);
+  if (scatter != nullptr && scatter->dst != nullptr) {
+    if (residual != nullptr) return cudaErrorInvalidValue;
+    return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, EntryStride{}, nullptr, 0,
+                         scatter, splitk->ranges);
+  }
+  if (splitk->partial == nullptr) return cudaErrorInvalidValue;
+  cudaError_t e = launch_config(cfg, ahi, alo, bhi, blo, splitk->partial, n, m, n, d, err, stream, 1, EntryStride{},
+                                nullptr, 0, nullptr, splitk->ranges);
+  if (e != cudaSuccess) return e;
+  const uint32_t bx = std::min<uint32_t>((n + 255) / 256, 8u);
+  const uint32_t by = std::min<uint32_t>(m, std::max<uint32_t>(1u, 148u * 16u / bx));
+  splitk_reduce_kernel<<<dim3(bx, by), 256, 0, stream>>>(splitk->partial, ranges, m, n, residual, ldr, c, ldc);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+uint32_t sgemm_tc_k_ranges(uint32_t k, uint32_t ranges) {
+  if (ranges <= 1 || k == 0) return 1;
+  const uint32_t kp = round_up(k, KPAD), chunks = (kp + KC - 1) / KC;
+  const uint32_t per = (chunks + ranges - 1) / ranges;
+  return (chunks + per - 1) / per;
+}
+
+uint32_t sgemm_tc_pick_k_ranges(uint32_t m, uint32_t n, uint32_t k) {
+  constexpr uint32_t kSms = 148;
+  const uint64_t tiles = static_cast<uint64_t>((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  if (tiles == 0 || tiles >= kSms || k == 0) return 1;
+  const uint32_t chunks = (round_up(k, KPAD) + KC - 1) / KC;
+  uint32_t best = 1;
+  double best_score = -1.0;
+  for (uint32_t s = 1; s <= 8 && (s == 1 || chunks / s >= 2); ++s) {
+    const uint64_t ctas = tiles * sgemm_tc_k_ranges(k, s);
+    const double fill = static_cast<double>(ctas) / (static_cast<double>((ctas + kSms - 1) / kSms) * kSms);
+    const double score = fill - 0.03 * (s - 1);  // each range adds a prologue, an epilogue and partial traffic
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = s;
+    }
+  }
+  return best;
+}
+
 cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, const float* blo, float* c,
                               uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* a_scratch, unsigned int* err,
                               cudaStream_t stream, const float* residual, uint64_t ldr, int cfg,
-                              const RowScatter* scatter) {
+                              const RowScatter* scatter, const SplitK* splitk) {
   if (m == 0 || n == 0 || k == 0) return cudaSuccess;
   if ((reinterpret_cast<uintptr_t>(a_scratch) & 1023u) != 0) return cudaErrorInvalidValue;
   const SplitDims d = split_dims(m, n, k);
@@ -1186,17 +1278,18 @@ cudaError_t sgemm_tc_presplit(const float* a, uint64_t lda, const float* bhi, co
   split_rows_kernel<<<dim3(blocks, 1), 256, 0, stream>>>(a, lda, m, k, ahi, alo, d.mp, d.kp, EntryStride{});
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, EntryStride{}, residual, ldr, scatter);
+  return run_split_k(cfg, ahi, alo, bhi, blo, c, ldc, m, n, k, d, err, stream, residual, ldr, scatter, splitk);
 }
 
 // Both operands already split: A hi/lo in the [Mp][Kp] layout of split_dims
 // (written by its producer), B as from sgemm_tc_split_b.
 cudaError_t sgemm_tc_presplit_ab(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
                                  uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, unsigned int* err,
-                                 cudaStream_t stream, const float* residual, uint64_t ldr, int cfg) {
+                                 cudaStream_t stream, const float* residual, uint64_t ldr, int cfg,
+                                 const SplitK* splitk) {
   if (m == 0 || n == 0 || k == 0) return cudaSuccess;
   const SplitDims d = split_dims(m, n, k);
-  return launch_config(cfg, ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, 1, EntryStride{}, residual, ldr);
+  return run_split_k(cfg, ahi, alo, bhi, blo, c, ldc, m, n, k, d, err, stream, residual, ldr, nullptr, splitk);
 }
 
 // A operand already in the split layout (hi/lo, [count][Mp][Kp], zero padded),
