@@ -763,11 +763,10 @@ int Block::set_weight(uint32_t slot, const float* src, uint64_t count, bool on_d
 
 // Products of at least 2048 x 2048 run on the CTA-pair kernel with 32-deep
 // stages (faster under the power cap; same MMAs in the same order, so the same
-// bits); smaller ones, and those whose epilogue scatters rows to the tensor-
-// parallel peers (a single-CTA epilogue), on the single-CTA kernel.
-static int block_cfg(uint32_t m, uint32_t n, const RowScatter* scatter) {
-  const bool scatters = scatter != nullptr && scatter->dst != nullptr;
-  return (!scatters && m >= 2048 && n >= 2048) ? kTcPair32 : kTcSingle16;
+// bits), those whose epilogue scatters rows to the tensor-parallel owners
+// included; smaller ones on the single-CTA kernel.
+static int block_cfg(uint32_t m, uint32_t n, const RowScatter* /*scatter*/) {
+  return (m >= 2048 && n >= 2048) ? kTcPair32 : kTcSingle16;
 }
 
 // Single-CTA products under one wave of tiles (the tensor-parallel shards and
@@ -780,7 +779,7 @@ static int block_cfg(uint32_t m, uint32_t n, const RowScatter* scatter) {
 // takes the same decision.
 uint32_t Block::k_ranges(uint32_t n, uint32_t k, bool scatter) const {
   const uint32_t tmax = dims_.max_batch * dims_.seq_len;
-  if (!scatter && block_cfg(tmax, n, nullptr) != kTcSingle16) return 1;
+  if (block_cfg(tmax, n, nullptr) != kTcSingle16) return 1;
   const uint32_t r = sgemm_tc_pick_k_ranges(tmax, n, k);
   if (r <= 1) return 1;
   if (scatter) return std::min(r, kMaxScatterRanges);

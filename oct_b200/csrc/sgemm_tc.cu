@@ -463,7 +463,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                         float* __restrict__ c, uint32_t m, uint32_t n, uint64_t ldc, uint32_t num_kb,
                         uint32_t tiles_m, uint32_t tiles_n, uint32_t entry_rows_a, uint32_t entry_rows_b,
                         EntryStride stride_c, const float* __restrict__ residual, uint64_t ldr,
-                        unsigned int* __restrict__ err) {
+                        unsigned int* __restrict__ err, const RowScatter scatter) {
   using Cfg = PairCfg<BK>;
   constexpr uint32_t S = Cfg::STAGES;
   constexpr uint32_t KBC = KC / BK;
@@ -613,7 +613,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(&acc_empty[buf], 0);
     }
-    if (ok && num_kb > 0) {
+    if (scatter.dst != nullptr && num_kb > 0) {
+      // Row scatter (owner rows, as the single-CTA kernel's): this CTA's 128 x 256
+      // half tile is staged in its own operand ring -- idle once the last
+      // accumulator chunk arrived, since the leader's final commit covers every
+      // pair MMA, and every TMA copy was consumed by one -- then each warp stores
+      // whole rows as 512-byte coalesced segments.
+      constexpr uint32_t LDS = BN + 4;  // padded row stride (floats): conflict-free float4 stores
+      float* stage_tile = reinterpret_cast<float*>(smem);
+      if (ok) {
+        float* srow = stage_tile + (q * 32 + lane) * LDS + h * 128u;
+#pragma unroll
+        for (int j = 0; j < 128; j += 4)
+          *reinterpret_cast<float4*>(srow + j) = make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight epilogue warps of this CTA
+      if (*(volatile uint32_t*)&aborted == 0u) {
+        const uint32_t ew = warp - 2u;
+        for (uint32_t lr = ew; lr < PAIR_HALF; lr += 8u) {
+          const uint32_t row = tile_m * PAIR_BM + rank * PAIR_HALF + lr;
+          if (row >= m) break;
+          const uint32_t owner = row / scatter.rows_per_rank;
+          const uint64_t slot_row =
+              static_cast<uint64_t>(scatter.src_rank) * scatter.rows_per_rank + (row - owner * scatter.rows_per_rank);
+          float* drow = scatter.dst[owner] + slot_row * scatter.ld;
+          const float* srow = stage_tile + lr * LDS;
+#pragma unroll
+          for (uint32_t half = 0; half < 2; ++half) {
+            const uint32_t cl = half * 128u + lane * 4u;  // column within the tile
+            const uint32_t col = tile_n * BN + cl;
+            if (col + 4 <= n) {
+              *reinterpret_cast<float4*>(drow + col) = *reinterpret_cast<const float4*>(srow + cl);
+            } else {
+              for (uint32_t t = 0; t < 4; ++t)
+                if (col + t < n) drow[col + t] = srow[cl + t];
+            }
+          }
+        }
+      }
+    } else if (ok && num_kb > 0) {
       const uint32_t row = tile_m * PAIR_BM + rank * PAIR_HALF + q * 32 + lane;
       const uint32_t col0 = tile_n * BN + h * 128u;
       const bool vec_ok = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) &&
@@ -1117,9 +1155,14 @@ template <int BK>
 cudaError_t launch_pair(const float* ahi, const float* alo, const float* bhi, const float* blo, float* c,
                         uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
                         cudaStream_t stream, uint32_t batch, EntryStride stride_c, const float* residual = nullptr,
-                        uint64_t ldr = 0) {
+                        uint64_t ldr = 0, const RowScatter* scatter = nullptr) {
   using Cfg = PairCfg<BK>;
   if (d.mp % PAIR_BM != 0) return cudaErrorInvalidValue;
+  const RowScatter sc = scatter != nullptr ? *scatter : RowScatter{};
+  // the pair epilogue scatters owner rows only (no broadcast form)
+  if (sc.dst != nullptr && (batch != 1 || sc.rows_per_rank == 0 || sc.bcast != 0 || sc.ld % 4 != 0 ||
+                            residual != nullptr))
+    return cudaErrorInvalidValue;
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
   const uint32_t rows_a = d.mp * batch, rows_b = d.np * batch;
   if (!make_operand_map(&m_ahi, ahi, rows_a, d.kp, BK, PAIR_HALF) ||
@@ -1135,7 +1178,7 @@ cudaError_t launch_pair(const float* ahi, const float* alo, const float* bhi, co
   if (grid > 0x7FFFFFFFull) return cudaErrorInvalidValue;
   sgemm3x_pair_kernel<BK><<<static_cast<uint32_t>(grid), NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(
       m_ahi, m_alo, m_bhi, m_blo, c, m, n, ldc, d.kp / BK, tiles_m, tiles_n, d.mp, d.np, stride_c, residual, ldr,
-      err);
+      err, sc);
   return cudaGetLastError();
 }
 
@@ -1143,14 +1186,13 @@ cudaError_t launch_config(int cfg, const float* ahi, const float* alo, const flo
                           uint64_t ldc, uint32_t m, uint32_t n, const SplitDims& d, unsigned int* err,
                           cudaStream_t stream, uint32_t batch, EntryStride stride_c, const float* residual = nullptr,
                           uint64_t ldr = 0, const RowScatter* scatter = nullptr, uint32_t ksplit = 1) {
-  // the CTA-pair kernels have no row-scatter epilogue and no split-K form
-  if (((scatter != nullptr && scatter->dst != nullptr) || ksplit > 1) && cfg != kTcSingle16 && cfg != kTcSingle32)
-    return cudaErrorInvalidValue;
+  // the CTA-pair kernels have no split-K form (their row scatter is checked in launch_pair)
+  if (ksplit > 1 && cfg != kTcSingle16 && cfg != kTcSingle32) return cudaErrorInvalidValue;
   switch (cfg) {
     case kTcSingle16: return launch_main<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr, scatter, ksplit);
     case kTcSingle32: return launch_main<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr, scatter, ksplit);
-    case kTcPair16: return launch_pair<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
-    case kTcPair32: return launch_pair<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr);
+    case kTcPair16: return launch_pair<16>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr, scatter);
+    case kTcPair32: return launch_pair<32>(ahi, alo, bhi, blo, c, ldc, m, n, d, err, stream, batch, stride_c, residual, ldr, scatter);
     default: return cudaErrorInvalidValue;
   }
 }
