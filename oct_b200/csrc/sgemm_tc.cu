@@ -614,7 +614,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) mbar_arrive_cluster(&acc_empty[buf], 0);
     }
     if (scatter.dst != nullptr && num_kb > 0) {
-      // Row scatter (owner rows, as the single-CTA kernel's): this CTA's 128 x 256
+      // Row scatter (owner rows or broadcast, as the single-CTA kernel's): this CTA's 128 x 256
       // half tile is staged in its own operand ring -- idle once the last
       // accumulator chunk arrived, since the leader's final commit covers every
       // pair MMA, and every TMA copy was consumed by one -- then each warp stores
@@ -628,7 +628,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           *reinterpret_cast<float4*>(srow + j) = make_float4(run[j], run[j + 1], run[j + 2], run[j + 3]);
       }
       asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight epilogue warps of this CTA
-      if (*(volatile uint32_t*)&aborted == 0u) {
+      if (*(volatile uint32_t*)&aborted == 0u && scatter.bcast > 0u) {
+        // Broadcast (the column-parallel product's gather): each row to every rank,
+        // the peers first and this rank last, each warp starting at a different peer.
+        const uint32_t ew = warp - 2u;
+        for (uint32_t lr = ew; lr < PAIR_HALF; lr += 8u) {
+          const uint32_t row = tile_m * PAIR_BM + rank * PAIR_HALF + lr;
+          if (row >= m) break;
+          const float* srow = stage_tile + lr * LDS;
+          for (uint32_t i = 1; i <= scatter.bcast; ++i) {
+            const uint32_t rk = (scatter.src_rank + (i == scatter.bcast ? 0u : 1u + (i - 1u + ew) % (scatter.bcast - 1u))) %
+                                scatter.bcast;
+            float* drow = scatter.dst[rk] + static_cast<uint64_t>(row) * scatter.ld + scatter.col_offset;
+#pragma unroll
+            for (uint32_t half = 0; half < 2; ++half) {
+              const uint32_t cl = half * 128u + lane * 4u;
+              const uint32_t col = tile_n * BN + cl;
+              if (col + 4 <= n) {
+                *reinterpret_cast<float4*>(drow + col) = *reinterpret_cast<const float4*>(srow + cl);
+              } else {
+                for (uint32_t t = 0; t < 4; ++t)
+                  if (col + t < n) drow[col + t] = srow[cl + t];
+              }
+            }
+          }
+        }
+      } else if (*(volatile uint32_t*)&aborted == 0u) {
         const uint32_t ew = warp - 2u;
         for (uint32_t lr = ew; lr < PAIR_HALF; lr += 8u) {
           const uint32_t row = tile_m * PAIR_BM + rank * PAIR_HALF + lr;
@@ -1159,8 +1184,8 @@ cudaError_t launch_pair(const float* ahi, const float* alo, const float* bhi, co
   using Cfg = PairCfg<BK>;
   if (d.mp % PAIR_BM != 0) return cudaErrorInvalidValue;
   const RowScatter sc = scatter != nullptr ? *scatter : RowScatter{};
-  // the pair epilogue scatters owner rows only (no broadcast form)
-  if (sc.dst != nullptr && (batch != 1 || sc.rows_per_rank == 0 || sc.bcast != 0 || sc.ld % 4 != 0 ||
+  if (sc.dst != nullptr && (batch != 1 || (sc.rows_per_rank == 0 && sc.bcast == 0) || sc.ld % 4 != 0 ||
+                            ldc % 4 != 0 || sc.col_offset % 4 != 0 || (sc.bcast > 0 && sc.src_rank >= sc.bcast) ||
                             residual != nullptr))
     return cudaErrorInvalidValue;
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;

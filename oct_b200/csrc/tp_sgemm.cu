@@ -232,10 +232,13 @@ int TpSgemm::run(const float* a, uint64_t lda, const float* b, uint64_t ldb, flo
   float* out = out_[buf];
   cudaError_t e = sgemm_tc_split_b(b, ldb, k, nr, bhi, blo, stream);
   if (e != cudaSuccess) return -4;
+  // the rank's block on the CTA-pair kernel with 32-deep stages from 2048 x 2048 up
+  // (as the one-GPU product's AUTO; same bits as the single-CTA kernel)
+  const int cfg = (m >= 2048 && nr >= 2048) ? kTcPair32 : kTcSingle16;
   if (d.world == 1) {
     float* dst = c != nullptr ? c : out;
     const uint64_t ldd = c != nullptr ? ldc : n;
-    e = sgemm_tc_presplit(a, lda, bhi, blo, dst, ldd, m, n, k, ascratch, err_, stream);
+    e = sgemm_tc_presplit(a, lda, bhi, blo, dst, ldd, m, n, k, ascratch, err_, stream, nullptr, 0, cfg);
     if (e != cudaSuccess) return -4;
     if (c != nullptr && result != nullptr) {
       e = cudaMemcpy2DAsync(out, n * sizeof(float), c, ldc * sizeof(float), n * sizeof(float), m,
@@ -249,7 +252,7 @@ int TpSgemm::run(const float* a, uint64_t lda, const float* b, uint64_t ldb, flo
     sc.ld = n;
     sc.bcast = d.world;
     sc.col_offset = static_cast<uint64_t>(d.rank) * nr;
-    e = sgemm_tc_presplit(a, lda, bhi, blo, out, n, m, nr, k, ascratch, err_, stream, nullptr, 0, kTcSingle16, &sc);
+    e = sgemm_tc_presplit(a, lda, bhi, blo, out, n, m, nr, k, ascratch, err_, stream, nullptr, 0, cfg, &sc);
     if (e != cudaSuccess) return -4;
     e = tp_signal_wait(flag_peers_, flags_, 0, d.world, d.rank, epoch_, err_, kTpWaitNs, stream);
     if (e != cudaSuccess) return -4;
@@ -261,7 +264,7 @@ int TpSgemm::run(const float* a, uint64_t lda, const float* b, uint64_t ldb, flo
   } else {
     const uint64_t slab = static_cast<uint64_t>(m) * nr;
     float* mine = gather_ + d.rank * slab;
-    e = sgemm_tc_presplit(a, lda, bhi, blo, mine, nr, m, nr, k, ascratch, err_, stream);
+    e = sgemm_tc_presplit(a, lda, bhi, blo, mine, nr, m, nr, k, ascratch, err_, stream, nullptr, 0, cfg);
     if (e != cudaSuccess) return -4;
     if (nccl().all_gather(mine, gather_, slab, kNcclFloat32, comm_, stream) != 0) return -4;
     const uint64_t granules = slab * d.world / 4;
